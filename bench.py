@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark of the exact hard-reset LIF scan on B200 (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (the one the headline metric is quoted on):
+lif_tuned forward+backward, B*N = 16384 neurons per GPU (B = 64 x 256),
+T = 1024, x ~ N(0.05, 0.2^2) fp32, beta = 0.99, theta = 1, u_r = 0, u0 = 0,
+the default sigmoid surrogate (alpha = 4, detached reset), upstream gradient
+on the spikes ~ N(0, 1).  Inputs are drawn on the CPU from a seeded
+torch.Generator and copied to the device (synthetic data of the config's
+shape and distribution).  A step = one lif_tuned forward + backward
+(torch.autograd.backward(S, GS)) through the public API.
+
+Multi-GPU: one process per GPU (torchrun); every rank owns its own batch
+shard of 16384 neurons (weak scaling, no data-path collective); the step time
+is the max over ranks; value = all ranks' neuron-steps / that time.
+
+--impl reference times the reference's CPU path for the same workload: the
+CPU oracle (oracle/, a C restatement of lifscan/fast.py's serial forward and
+adjoint) on all host threads.  Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+T_STEPS = 1024
+N_PER_GPU = 16384
+BETA = 0.99
+MU, SD = 0.05, 0.2
+FWD_BYTES = 12   # read I, write U and S (fp32) per neuron-step
+BWD_BYTES = 20   # read I, U[t-1], S, GS, write Lam per neuron-step (GU is zero, not read)
+METRIC = "neuron-steps/s, lif_tuned fwd+bwd (B*N=16384/GPU, T=1024)"
+UNIT = "neuron-steps/s"
+FALLBACK_HBM_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    p.add_argument("--mode", default="scan", choices=("scan", "serial", "auto"),
+                   help="lif_tuned mode (default: the reference's default, scan)")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    return p.parse_args()
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_per_unit(kernel_key):
+    """DRAM bytes per neuron-step of a kernel from a committed ncu summary
+    (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            d = json.load(f)
+        return float(d[kernel_key]["dram_bytes_per_neuron_step"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML during the timed region."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index, period=0.01):
+        self.index, self.period = index, period
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # NVML missing: no clock record
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def record(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def cpu_oracle_rate(T, N, seconds, want_bwd=True):
+    """Reference CPU path (C restatement of lifscan/fast.py serial forward +
+    adjoint) on all host threads; repeats the full workload until `seconds`
+    have elapsed (at least once).  Returns (neuron-steps/s, threads, sample)."""
+    import numpy as np
+    from oracle import oracle as O
+    I, u0, GS = O.gen_inputs(T, N, MU, SD, seed=0, grad=True)
+    threads = O.num_threads()
+    O.serial_forward(I[:64], BETA, 1.0, 0.0, u0)  # warm the library
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        U, S = O.serial_forward(I, BETA, 1.0, 0.0, u0)
+        if want_bwd:
+            O.serial_backward(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0, True)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    del np
+    return done * T * N / el, threads, f"{done} x full workload (T={T}, N={N}) in {el:.1f} s"
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    T, N = T_STEPS, N_PER_GPU
+    I, u0, GS = O.gen_inputs(T, N, MU, SD, seed=0, grad=True)
+    for _ in range(max(args.warmup, 0)):
+        U, S = O.serial_forward(I, BETA, 1.0, 0.0, u0)
+        O.serial_backward(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0, True)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        U, S = O.serial_forward(I, BETA, 1.0, 0.0, u0)
+        O.serial_backward(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0, True)
+        ts.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(ts) / len(ts)
+    value = N * T / (ms / 1e3)
+    cores = O.num_threads()
+    sample = f"full workload per step (T={T}, N={N}), serial forward + adjoint"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "c2: lif_tuned fwd+bwd, B*N=16384, T=1024, beta=0.99, x~N(0.05,0.2^2)",
+                   "path": "CPU oracle port of lifscan/fast.py serial_forward_nograd + serial_backward"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200 import lifscan as L
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if ws == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    T, N = T_STEPS, N_PER_GPU
+    g = torch.Generator().manual_seed(1000 + rank)
+    I_h = (MU + SD * torch.randn(T, N, generator=g)).float()
+    GS_h = torch.randn(T, N, generator=g).float()
+    u0_h = torch.zeros(N)
+    I = I_h.to(dev)
+    GS = GS_h.to(dev)
+    u0 = u0_h.to(dev)
+    Iq = I.clone().requires_grad_(True)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        Iq.grad = None
+        S = L.lif_tuned(Iq, u0, beta=BETA, theta=1.0, u_r=0.0, alpha=4.0, mode=args.mode) if args.mode != "auto" \
+            else L.lif_auto(Iq, u0, beta=BETA)
+        torch.autograd.backward(S, GS)
+        return S
+
+    def timed(fn, steps, count_launches=False):
+        """Per-step CUDA events on the launching stream, L2 flushed between
+        steps outside the events; returns (mean ms, launches)."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        n0 = lib.lifb_kernel_launches()
+        for a, b in evs:
+            flush.fill_(1.0)
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        n1 = lib.lifb_kernel_launches()
+        barrier()
+        ms = [a.elapsed_time(b) for a, b in evs]
+        return sum(ms) / len(ms), n1 - n0
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+
+    with ClockSampler(local) as clk:
+        ms_local, launches = timed(step, args.steps)
+    ms = max_over_ranks(ms_local)
+    units = N * T * ws
+    value = units / (ms / 1e3)
+
+    # forward-only and per-call timings (roofline of the dominant call)
+    def fwd_call():
+        return L.scan_forward_auto(I, BETA, 1.0, 0.0, u0) if args.mode == "scan" else \
+            L.serial_forward_auto(I, BETA, 1.0, 0.0, u0)
+    U, S = fwd_call()
+
+    def bwd_call():
+        if args.mode == "scan":
+            return L.scan_backward_auto(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0)
+        return L.serial_backward_auto(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0)
+    for _ in range(3):
+        fwd_call()
+        bwd_call()
+    ms_fwd, n_fwd = timed(fwd_call, args.steps)
+    ms_bwd, n_bwd = timed(bwd_call, args.steps)
+    ms_fwd = max_over_ranks(ms_fwd)
+    ms_bwd = max_over_ranks(ms_bwd)
+    hbm, peak_kind = peaks()
+    per_call = {
+        "fwd": {"ms": ms_fwd, "bytes": FWD_BYTES * N * T, "launches": n_fwd // max(args.steps, 1)},
+        "bwd": {"ms": ms_bwd, "bytes": BWD_BYTES * N * T, "launches": n_bwd // max(args.steps, 1)},
+    }
+    for v in per_call.values():
+        v["gbs"] = v["bytes"] / (v["ms"] / 1e3) / 1e9
+        v["frac"] = v["gbs"] / hbm
+    dom = "fwd" if ms_fwd >= ms_bwd else "bwd"
+    kname = {"fwd": f"lifb forward ({args.mode})", "bwd": f"lifb backward ({args.mode})"}[dom]
+    tpu = traffic_per_unit(f"{args.mode}_{dom}")
+    roofline = {
+        "bound": "hbm", "kernel": kname, "launches_per_call": per_call[dom]["launches"],
+        "achieved": per_call[dom]["gbs"], "peak": hbm, "peak_source": peak_kind, "unit": "GB/s",
+        "frac": per_call[dom]["frac"],
+        "traffic": (tpu * N * T) if tpu is not None else None,
+        "algorithmic_bytes": per_call[dom]["bytes"],
+        "step_frac": (32 * N * T) / (ms_local / 1e3) / 1e9 / hbm,
+    }
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        I_p = I_h.pin_memory()
+        GS_p = GS_h.pin_memory()
+        S_p = torch.empty(T, N).pin_memory()
+        dI_p = torch.empty(T, N).pin_memory()
+        du0_p = torch.empty(N).pin_memory()
+        u0r = u0.clone().requires_grad_(True)
+
+        def e2e_step():
+            Id = I_p.to(dev, non_blocking=True).requires_grad_(True)
+            G = GS_p.to(dev, non_blocking=True)
+            u0r.grad = None
+            S_ = L.lif_tuned(Id, u0r, beta=BETA, mode=args.mode) if args.mode != "auto" else \
+                L.lif_auto(Id, u0r, beta=BETA)
+            torch.autograd.backward(S_, G)
+            S_p.copy_(S_.detach(), non_blocking=True)
+            dI_p.copy_(Id.grad, non_blocking=True)
+            du0_p.copy_(u0r.grad, non_blocking=True)
+        for _ in range(3):
+            e2e_step()
+        ms_e2e, _ = timed(e2e_step, max(args.steps // 2, 5))
+        ms_e2e = max_over_ranks(ms_e2e)
+        e2e = {"value": units / (ms_e2e / 1e3), "unit": UNIT, "ms_per_step": ms_e2e,
+               "h2d_bytes_per_step": 2 * N * T * 4, "d2h_bytes_per_step": 2 * N * T * 4 + N * 4}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        v, threads, sample = cpu_oracle_rate(T, N, args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch.Generator, config 2 shape)",
+            "config": {"workload": "c2: lif_tuned fwd+bwd, B*N=16384 per GPU, T=1024, beta=0.99, x~N(0.05,0.2^2)",
+                       "mode": args.mode, "global_neurons": N * ws, "seq_len": T,
+                       "parallelism": f"batch-sharded x{ws}, no collective",
+                       "l2": "flushed between steps (256 MiB write outside the events)"},
+            "fwd": {"ms": ms_fwd, "value": units / (ms_fwd / 1e3), "gbs": per_call["fwd"]["gbs"],
+                    "frac": per_call["fwd"]["frac"]},
+            "bwd": {"ms": ms_bwd, "value": units / (ms_bwd / 1e3), "gbs": per_call["bwd"]["gbs"],
+                    "frac": per_call["bwd"]["frac"]},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clk.record(),
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,122 @@
+"""ctypes binding of liblifb.so (include/lifscan_b200.h).
+
+The product path calls CUDA only through this C ABI.  There is no CPU or
+Python fallback: if the library is missing or a tensor is not on a CUDA
+device, the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+c_void_p = ctypes.c_void_p
+c_i64 = ctypes.c_int64
+c_int = ctypes.c_int
+c_float = ctypes.c_float
+c_size_t = ctypes.c_size_t
+
+ABI_VERSION = 1
+
+# Every symbol include/lifscan_b200.h declares, with its ctypes signature.
+SIGNATURES = {
+    "lifb_abi_version": ([], c_int),
+    "lifb_kernel_launches": ([], ctypes.c_uint64),
+    "lifb_status_string": ([c_int], ctypes.c_char_p),
+    "lifb_last_error": ([], ctypes.c_char_p),
+    "lifb_serial_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
+                         c_void_p], c_int),
+    "lifb_serial_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
+                         c_float, c_float, c_float, c_float, c_int, c_void_p], c_int),
+    "lifb_scan_fwd_v3_workspace_bytes": ([c_i64, c_i64, c_int, c_int], c_size_t),
+    "lifb_scan_fwd_v3": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
+                          c_int, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p], c_int),
+    "lifb_scan_fwd_v4_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
+    "lifb_scan_fwd_v4": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
+                          c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p], c_int),
+    "lifb_scan_bwd_workspace_bytes": ([c_i64, c_i64, c_int], c_size_t),
+    "lifb_scan_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
+                       c_float, c_float, c_float, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p], c_int),
+}
+
+
+class LifbError(RuntimeError):
+    """A nonzero status returned by liblifb."""
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def load(build_if_missing: bool = True):
+    """Load liblifb.so (building it first when it is missing or stale and nvcc
+    is available).  Raises if it cannot be loaded."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB
+        if build_if_missing:
+            try:
+                path = _build.build()
+            except (RuntimeError, OSError) as e:  # no nvcc: use the prebuilt library if present
+                if not os.path.exists(path):
+                    raise RuntimeError(f"liblifb.so is missing and cannot be built: {e}") from e
+        if not os.path.exists(path):
+            raise RuntimeError(f"liblifb.so not found at {path}; run python -m hard_resets_compose_b200.build")
+        L = ctypes.CDLL(path)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        v = L.lifb_abi_version()
+        if v != ABI_VERSION:
+            raise RuntimeError(f"liblifb ABI version {v} != expected {ABI_VERSION}")
+        _lib = L
+        return L
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        L = load(False)
+        msg = L.lifb_last_error().decode() or L.lifb_status_string(status).decode()
+        raise LifbError(f"{what} failed (status {status}: {L.lifb_status_string(status).decode()}): {msg}")
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+class Stats(ctypes.Structure):
+    """Mirror of lifb_stats."""
+    _fields_ = [
+        ("repair_iters", ctypes.c_int32),
+        ("max_cnt", ctypes.c_int32),
+        ("max_super_cnt", ctypes.c_int32),
+        ("status", ctypes.c_int32),
+        ("n_maps", ctypes.c_int64),
+        ("n_overflow", ctypes.c_int64),
+        ("sum_cnt", ctypes.c_int64),
+        ("n_super", ctypes.c_int64),
+        ("n_super_overflow", ctypes.c_int64),
+        ("sum_super_cnt", ctypes.c_int64),
+    ]
+
+
+STATS_BYTES = ctypes.sizeof(Stats)
+
+
+def read_stats(dev_buf: torch.Tensor) -> Stats:
+    host = dev_buf.cpu()  # synchronises the stream
+    return Stats.from_buffer_copy(bytes(host.numpy().tobytes()))

@@ -1,0 +1,268 @@
+// extern "C" entry points of liblifb (declared in include/lifscan_b200.h).
+// Argument checks, workspace carving and kernel dispatch; no allocation, no
+// synchronisation, no exceptions across the ABI.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <string>
+
+#include "lifb_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int check_launch(const char *what)
+{
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(LIFB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    g_last_error.clear();
+    return LIFB_OK;
+}
+
+constexpr size_t kAlign = 256;
+
+// Carves aligned sub-arrays from one workspace; with base == nullptr it only
+// measures.
+struct Carver {
+    char *base;
+    size_t off = 0;
+    explicit Carver(void *b) : base((char *)b) {}
+    template <class T>
+    T *take(int64_t count)
+    {
+        off = (off + kAlign - 1) / kAlign * kAlign;
+        T *p = base ? (T *)(base + off) : nullptr;
+        off += (size_t)count * sizeof(T);
+        return p;
+    }
+};
+
+void carve_fwd(Carver &c, lifb::FwdMaps &mp, int64_t M, int64_t N, int K)
+{
+    mp.Lo = c.take<float>(M * N);
+    mp.MA = c.take<float>(M * N);
+    mp.MB = c.take<float>(M * N);
+    mp.MX = c.take<float>(M * K * N);
+    mp.MC = c.take<float>(M * K * N);
+    mp.MN = c.take<int32_t>(M * N);
+    mp.OVF = c.take<int32_t>(M * N);
+    mp.Starts = c.take<float>(M * N);
+    mp.Ends = c.take<float>(M * N);
+}
+
+void carve_super(Carver &c, lifb::SuperMaps &sp, int64_t M2, int64_t N, int K2)
+{
+    sp.SA = c.take<float>(M2 * N);
+    sp.SB = c.take<float>(M2 * N);
+    sp.SX = c.take<float>(M2 * K2 * N);
+    sp.SC = c.take<float>(M2 * K2 * N);
+    sp.SN = c.take<int32_t>(M2 * N);
+    sp.SOVF = c.take<int32_t>(M2 * N);
+    sp.SStarts = c.take<float>(M2 * N);
+}
+
+int check_common(const void *I, const void *u0, const void *U, const void *S, int64_t T, int64_t N)
+{
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "negative shape T=%lld N=%lld", (long long)T, (long long)N);
+    if (T > 0 && N > 0 && (!I || !u0 || !U || !S)) return fail(LIFB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    return LIFB_OK;
+}
+
+int check_ws(void *ws, size_t have, size_t need)
+{
+    if (need == 0) return LIFB_OK;
+    if (!ws) return fail(LIFB_ERR_WORKSPACE, "workspace is NULL (need %zu bytes)", need);
+    if ((uintptr_t)ws % kAlign) return fail(LIFB_ERR_WORKSPACE, "workspace not %zu-byte aligned", kAlign);
+    if (have < need) return fail(LIFB_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", have, need);
+    return LIFB_OK;
+}
+
+constexpr int64_t kMaxGridY = 65535;
+
+}  // namespace
+
+namespace lifb {
+void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+}  // namespace lifb
+
+extern "C" {
+
+int lifb_abi_version(void) { return 1; }
+
+uint64_t lifb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+const char *lifb_status_string(int status)
+{
+    switch (status) {
+    case LIFB_OK: return "ok";
+    case LIFB_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case LIFB_ERR_CUDA: return "CUDA error";
+    case LIFB_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case LIFB_ERR_UNSUPPORTED: return "unsupported configuration";
+    default: return "unknown status";
+    }
+}
+
+const char *lifb_last_error(void) { return g_last_error.c_str(); }
+
+int lifb_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                    float theta, float u_r, void *stream)
+{
+    int st = check_common(I, u0, U, S, T, N);
+    if (st) return st;
+    if (T == 0 || N == 0) return LIFB_OK;
+    lifb::serial_fwd(I, u0, U, S, T, N, beta, theta, u_r, (cudaStream_t)stream);
+    return check_launch("lifb_serial_fwd");
+}
+
+int lifb_serial_bwd(const float *I, const float *u0, const float *U, const float *S, const float *GS,
+                    const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
+                    float alpha, int detach, void *stream)
+{
+    int st = check_common(I, u0, U, S, T, N);
+    if (st) return st;
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "null GS or Lam");
+    lifb::serial_bwd(I, u0, U, S, GS, GU, Lam, T, N, beta, theta, u_r, alpha, detach != 0, (cudaStream_t)stream);
+    return check_launch("lifb_serial_bwd");
+}
+
+size_t lifb_scan_fwd_v3_workspace_bytes(int64_t T, int64_t N, int C, int K)
+{
+    if (T <= 0 || N <= 0 || C <= 0 || K <= 0 || T % C) return 0;
+    Carver c(nullptr);
+    lifb::FwdMaps mp;
+    carve_fwd(c, mp, T / C, N, K);
+    return c.off;
+}
+
+static int check_scan_args(int64_t T, int C, int K, int64_t &M)
+{
+    if (C <= 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "chunk length C=%d must be positive", C);
+    if (T % C) return fail(LIFB_ERR_INVALID_ARGUMENT, "T=%lld is not a multiple of C=%d", (long long)T, C);
+    if (K < 1 || K > 64) return fail(LIFB_ERR_INVALID_ARGUMENT, "map capacity K=%d outside 1..64", K);
+    M = T / C;
+    if (M > kMaxGridY) return fail(LIFB_ERR_UNSUPPORTED, "T/C=%lld chunks exceeds %lld", (long long)M, (long long)kMaxGridY);
+    return LIFB_OK;
+}
+
+int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                     float theta, float u_r, int C, int K, int max_repair, void *workspace,
+                     size_t workspace_bytes, lifb_stats *stats_dev, void *stream)
+{
+    int st = check_common(I, u0, U, S, T, N);
+    if (st) return st;
+    int64_t M = 0;
+    if ((st = check_scan_args(T, C, K, M))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (stats_dev && cudaMemsetAsync(stats_dev, 0, sizeof(lifb_stats), s) != cudaSuccess)
+        return check_launch("lifb_scan_fwd_v3: stats reset");
+    if (T == 0 || N == 0) return LIFB_OK;
+    size_t need = lifb_scan_fwd_v3_workspace_bytes(T, N, C, K);
+    if ((st = check_ws(workspace, workspace_bytes, need))) return st;
+    Carver c(workspace);
+    lifb::FwdMaps mp;
+    carve_fwd(c, mp, M, N, K);
+    lifb::grid_envelope(I, u0, mp, T, N, C, beta, u_r, s);
+    lifb::grid_build(I, u0, mp, T, N, C, K, beta, theta, u_r, stats_dev, s);
+    lifb::grid_carry(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r, s);
+    lifb::grid_replay_repair(I, u0, mp, U, S, T, N, C, max_repair, beta, theta, u_r, stats_dev, s);
+    return check_launch("lifb_scan_fwd_v3");
+}
+
+size_t lifb_scan_fwd_v4_workspace_bytes(int64_t T, int64_t N, int C, int G, int K, int K2)
+{
+    if (T <= 0 || N <= 0 || C <= 0 || G <= 0 || K <= 0 || K2 <= 0 || T % ((int64_t)C * G)) return 0;
+    Carver c(nullptr);
+    lifb::FwdMaps mp;
+    lifb::SuperMaps sp;
+    carve_fwd(c, mp, T / C, N, K);
+    carve_super(c, sp, T / C / G, N, K2);
+    return c.off;
+}
+
+int lifb_scan_fwd_v4(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                     float theta, float u_r, int C, int G, int K, int K2, int max_repair, void *workspace,
+                     size_t workspace_bytes, lifb_stats *stats_dev, void *stream)
+{
+    int st = check_common(I, u0, U, S, T, N);
+    if (st) return st;
+    int64_t M = 0;
+    if ((st = check_scan_args(T, C, K, M))) return st;
+    if (G <= 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "group size G=%d must be positive", G);
+    if (M % G) return fail(LIFB_ERR_INVALID_ARGUMENT, "T=%lld must be divisible by C*G=%lld", (long long)T, (long long)C * G);
+    if (K2 < 1 || K2 > 64) return fail(LIFB_ERR_INVALID_ARGUMENT, "super capacity K2=%d outside 1..64", K2);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (stats_dev && cudaMemsetAsync(stats_dev, 0, sizeof(lifb_stats), s) != cudaSuccess)
+        return check_launch("lifb_scan_fwd_v4: stats reset");
+    if (T == 0 || N == 0) return LIFB_OK;
+    int64_t M2 = M / G;
+    size_t need = lifb_scan_fwd_v4_workspace_bytes(T, N, C, G, K, K2);
+    if ((st = check_ws(workspace, workspace_bytes, need))) return st;
+    Carver c(workspace);
+    lifb::FwdMaps mp;
+    lifb::SuperMaps sp;
+    carve_fwd(c, mp, M, N, K);
+    carve_super(c, sp, M2, N, K2);
+    lifb::grid_envelope(I, u0, mp, T, N, C, beta, u_r, s);
+    lifb::grid_build(I, u0, mp, T, N, C, K, beta, theta, u_r, stats_dev, s);
+    lifb::grid_compose(mp, sp, u0, T, N, C, G, K, K2, theta, u_r, stats_dev, s);
+    lifb::grid_carry(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2,
+                     beta, theta, u_r, s);
+    lifb::grid_carry_inner(I, mp, sp.SStarts, T, N, C, G, K, beta, theta, u_r, s);
+    lifb::grid_replay_repair(I, u0, mp, U, S, T, N, C, max_repair, beta, theta, u_r, stats_dev, s);
+    return check_launch("lifb_scan_fwd_v4");
+}
+
+size_t lifb_scan_bwd_workspace_bytes(int64_t T, int64_t N, int C)
+{
+    if (T <= 0 || N <= 0 || C <= 0 || T % C) return 0;
+    Carver c(nullptr);
+    int64_t M = T / C;
+    c.take<float>(M * N);
+    c.take<float>(M * N);
+    c.take<float>(M * N);
+    return c.off;
+}
+
+int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *S, const float *GS,
+                  const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
+                  float alpha, int detach, int C, void *workspace, size_t workspace_bytes, void *stream)
+{
+    int st = check_common(I, u0, U, S, T, N);
+    if (st) return st;
+    if (C <= 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "chunk length C=%d must be positive", C);
+    if (T % C) return fail(LIFB_ERR_INVALID_ARGUMENT, "T=%lld is not a multiple of C=%d", (long long)T, C);
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "null GS or Lam");
+    int64_t M = T / C;
+    if (M > kMaxGridY) return fail(LIFB_ERR_UNSUPPORTED, "T/C=%lld chunks exceeds %lld", (long long)M, (long long)kMaxGridY);
+    size_t need = lifb_scan_bwd_workspace_bytes(T, N, C);
+    if ((st = check_ws(workspace, workspace_bytes, need))) return st;
+    Carver c(workspace);
+    lifb::BwdScratch w;
+    w.P = c.take<float>(M * N);
+    w.Q = c.take<float>(M * N);
+    w.LamEnd = c.take<float>(M * N);
+    lifb::grid_scan_bwd(I, u0, U, S, GS, GU, Lam, w, T, N, C, beta, theta, u_r, alpha, detach != 0,
+                        (cudaStream_t)stream);
+    return check_launch("lifb_scan_bwd");
+}
+
+}  // extern "C"

@@ -1,0 +1,58 @@
+// Internal declarations shared by the CUDA translation units of liblifb.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/lifscan_b200.h"
+
+namespace lifb {
+
+// Adds n to the library's launch counter (lifb_kernel_launches).
+void count_launches(int n);
+
+// Chunk-level scratch of the forward scan, carved from the caller's workspace.
+// All arrays are [M, N] (MX/MC: [M, K, N]) with the neuron index fastest.
+struct FwdMaps {
+    float *Lo, *MA, *MB, *MX, *MC, *Starts, *Ends;
+    int32_t *MN, *OVF;
+};
+
+// Super-map scratch of the three-level forward (v4): [M2, N] / [M2, K2, N].
+struct SuperMaps {
+    float *SA, *SB, *SX, *SC, *SStarts;
+    int32_t *SN, *SOVF;
+};
+
+// serial.cu
+void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                float theta, float u_r, cudaStream_t s);
+void serial_bwd(const float *I, const float *u0, const float *U, const float *S, const float *GS,
+                const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
+                float alpha, bool detach, cudaStream_t s);
+
+// scan_fwd_grid.cu
+void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t T, int64_t N, int C, float beta,
+                   float u_r, cudaStream_t s);
+void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t T, int64_t N, int C, int K, float beta,
+                float theta, float u_r, lifb_stats *st, cudaStream_t s);
+void grid_carry(const float *I, const float *u0, const float *MA, const float *MB, const float *MX,
+                const float *MC, const int32_t *MN, const int32_t *OVF, float *Starts, int64_t N, int64_t M,
+                int64_t L, int K, float beta, float theta, float u_r, cudaStream_t s);
+void grid_compose(const FwdMaps &mp, const SuperMaps &sp, const float *u0, int64_t T, int64_t N, int C, int G,
+                  int K, int K2, float theta, float u_r, lifb_stats *st, cudaStream_t s);
+void grid_carry_inner(const float *I, const FwdMaps &mp, const float *SStarts, int64_t T, int64_t N, int C, int G,
+                      int K, float beta, float theta, float u_r, cudaStream_t s);
+void grid_replay_repair(const float *I, const float *u0, FwdMaps &mp, float *U, float *S, int64_t T, int64_t N,
+                        int C, int max_repair, float beta, float theta, float u_r, lifb_stats *st,
+                        cudaStream_t s);
+
+// scan_bwd.cu
+struct BwdScratch {
+    float *P, *Q, *LamEnd;
+};
+void grid_scan_bwd(const float *I, const float *u0, const float *U, const float *S, const float *GS,
+                   const float *GU, float *Lam, BwdScratch &w, int64_t T, int64_t N, int C, float beta,
+                   float theta, float u_r, float alpha, bool detach, cudaStream_t s);
+
+}  // namespace lifb

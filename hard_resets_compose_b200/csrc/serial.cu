@@ -1,0 +1,116 @@
+// Serial forward and adjoint: one recurrence per thread, neurons along the
+// lanes (coalesced rows of [T, N]), time tiles of D rows prefetched into
+// registers one tile ahead.
+//   k_serial_fwd  follows fwd_tiled_kernel with M = 1 (lifscan/triton_lif.py:353-379,
+//                 serial_forward_tiled :460-466) and fast.serial_forward_nograd
+//                 (lifscan/fast.py:69-81) bit for bit.
+//   k_serial_bwd  follows bwd_tiled_pf_kernel (lifscan/triton_lif.py:1087-1127)
+//                 and fast.serial_backward (lifscan/fast.py:227-239).
+#include "lifb_common.cuh"
+#include "lifb_internal.h"
+
+namespace lifb {
+
+constexpr int kSerBlock = 128;
+constexpr int kSerD = 16;
+
+template <int D>
+__global__ void __launch_bounds__(kSerBlock) k_serial_fwd(const float *__restrict__ I, const float *__restrict__ u0,
+                                                          float *__restrict__ U, float *__restrict__ S, int64_t T,
+                                                          int64_t N, float beta, float theta, float u_r)
+{
+    int64_t n = (int64_t)blockIdx.x * kSerBlock + threadIdx.x;
+    if (n >= N) return;
+    float u = u0[n];
+    const float *p = I + n;
+    int64_t Tf = (T / D) * D;
+    float cur[D], nxt[D];
+    if (Tf > 0) {
+#pragma unroll
+        for (int d = 0; d < D; d++) cur[d] = __ldg(p + (int64_t)d * N);
+    }
+    for (int64_t t0 = 0; t0 < Tf; t0 += D) {
+        bool more = t0 + D < Tf;
+        if (more) {
+#pragma unroll
+            for (int d = 0; d < D; d++) nxt[d] = __ldg(p + (t0 + D + d) * N);
+        }
+#pragma unroll
+        for (int d = 0; d < D; d++) {
+            bool s;
+            u = lif_step(u, cur[d], beta, theta, u_r, s);
+            int64_t o = (t0 + d) * N + n;
+            U[o] = u;
+            S[o] = s ? 1.0f : 0.0f;
+        }
+        if (more) {
+#pragma unroll
+            for (int d = 0; d < D; d++) cur[d] = nxt[d];
+        }
+    }
+    for (int64_t t = Tf; t < T; t++) {
+        bool s;
+        u = lif_step(u, __ldg(p + t * N), beta, theta, u_r, s);
+        U[t * N + n] = u;
+        S[t * N + n] = s ? 1.0f : 0.0f;
+    }
+}
+
+// Reverse sweep in tiles of D rows [t0, t0 + cnt), last tile first.
+template <int D>
+__global__ void __launch_bounds__(kSerBlock) k_serial_bwd(const float *__restrict__ I, const float *__restrict__ u0,
+                                                          const float *__restrict__ U, const float *__restrict__ S,
+                                                          const float *__restrict__ GS, const float *__restrict__ GU,
+                                                          float *__restrict__ Lam, int64_t T, int64_t N, float beta,
+                                                          float theta, float u_r, float alpha, bool detach)
+{
+    int64_t n = (int64_t)blockIdx.x * kSerBlock + threadIdx.x;
+    if (n >= N) return;
+    float lam = 0.0f;
+    float un0 = u0[n];
+    for (int64_t tend = T; tend > 0; tend -= D) {
+        int64_t t0 = tend - D > 0 ? tend - D : 0;
+        int cnt = (int)(tend - t0);
+        float x[D], s[D], up[D], gs[D], gu[D];
+#pragma unroll
+        for (int d = 0; d < D; d++) {
+            if (d < cnt) {
+                int64_t t = t0 + d;
+                int64_t o = t * N + n;
+                x[d] = __ldg(I + o);
+                s[d] = __ldg(S + o);
+                gs[d] = __ldg(GS + o);
+                gu[d] = GU ? __ldg(GU + o) : 0.0f;
+                up[d] = t > 0 ? __ldg(U + o - N) : un0;
+            }
+        }
+#pragma unroll
+        for (int dd = D - 1; dd >= 0; dd--) {
+            if (dd < cnt) {
+                float a, b;
+                lif_coef(up[dd], s[dd], x[dd], gs[dd], gu[dd], beta, theta, u_r, alpha, detach, a, b);
+                lam = b + a * lam;
+                Lam[(t0 + dd) * N + n] = lam;
+            }
+        }
+    }
+}
+
+void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                float theta, float u_r, cudaStream_t s)
+{
+    unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
+    count_launches(1);
+    k_serial_fwd<kSerD><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, u_r);
+}
+
+void serial_bwd(const float *I, const float *u0, const float *U, const float *S, const float *GS,
+                const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
+                float alpha, bool detach, cudaStream_t s)
+{
+    unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
+    count_launches(1);
+    k_serial_bwd<8><<<g, kSerBlock, 0, s>>>(I, u0, U, S, GS, GU, Lam, T, N, beta, theta, u_r, alpha, detach);
+}
+
+}  // namespace lifb

@@ -1,0 +1,402 @@
+"""Drop-in mirror of the reference's `lifscan.triton_lif` API on B200 kernels.
+
+    from hard_resets_compose_b200 import lifscan as L     # was: from lifscan import triton_lif as L
+    S = L.lif_tuned(I, u0, beta=0.9, mode="scan")
+
+Same names, argument order, defaults and return values as
+lifscan/triton_lif.py; every call runs hand-written sm_100a CUDA kernels
+through the C ABI of liblifb.so (include/lifscan_b200.h).  Triton tuning
+knobs (BN, nw, BNc, nwc, BNr, D, nwr, BNg, nwg, num_warps) are accepted and
+ignored: launch shapes are chosen by the library for B200.
+
+Conventions (lifscan/triton_lif.py:3): I is [T, N] fp32 on a CUDA device
+(made contiguous here), u0 is [N] fp32, beta/theta/u_r/alpha are Python
+floats used as fp32; outputs are new tensors like torch.empty_like(I); S is
+fp32 in {0, 1}.
+
+Deliberate difference (recorded in the design notes): the forward always
+repairs to convergence, so U and S are bit-identical to the serial fp32
+recurrence for every `repair` value; `repair` is accepted for signature
+compatibility and stats['repair_iters'] reports the rounds actually run.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream_of
+
+__all__ = [
+    "serial_forward", "serial_backward", "serial_forward_tiled", "serial_backward_tiled",
+    "serial_backward_tiled_pf", "serial_forward_auto", "serial_backward_auto",
+    "scan_forward", "scan_backward", "scan_forward_tiled", "scan_forward_v2", "scan_forward_v3",
+    "scan_forward_v4", "scan_backward_tiled", "scan_forward_auto", "scan_backward_auto",
+    "state_bounds", "surrogate_grad", "_pick_C", "LIFTuned", "lif_tuned", "LIFFunction", "lif",
+    "AUTO_FWD_MAX_N", "AUTO_FWD_MIN_T", "AUTO_BWD_MAX_N", "AUTO_BWD_MIN_T", "auto_modes",
+    "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg",
+]
+
+_CONVERGE = -1  # max_repair value meaning "repair until converged"
+
+
+# ----------------------------------------------------------------------------- checks
+def _cuda_f32(name, t, shape=None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (this implementation has no CPU path)")
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32, got {t.dtype}")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+    return t.contiguous()
+
+
+def _prep_fwd(I, u0):
+    if I.dim() != 2:
+        raise ValueError(f"I must be [T, N], got shape {tuple(I.shape)}")
+    I = _cuda_f32("I", I)
+    T, N = I.shape
+    u0 = _cuda_f32("u0", u0, (N,))
+    if u0.device != I.device:
+        raise ValueError("I and u0 are on different devices")
+    return I, u0, T, N
+
+
+def _prep_bwd(I, u0, U, S, GS, GU):
+    I, u0, T, N = _prep_fwd(I, u0)
+    U = _cuda_f32("U", U, (T, N))
+    S = _cuda_f32("S", S, (T, N))
+    GS = _cuda_f32("GS", GS, (T, N))
+    GU = None if GU is None else _cuda_f32("GU", GU, (T, N))
+    return I, u0, U, S, GS, GU, T, N
+
+
+def _f(x):
+    return float(x)
+
+
+# ----------------------------------------------------------------------------- serial
+def serial_forward(I, beta, theta, u_r, u0, BN=None):
+    """Serial hard-reset LIF forward (lifscan/triton_lif.py:246-251) -> (U, S)."""
+    I, u0, T, N = _prep_fwd(I, u0)
+    U = torch.empty_like(I)
+    S = torch.empty_like(I)
+    L = _lib.load()
+    with torch.cuda.device(I.device):
+        check(L.lifb_serial_fwd(ptr(I), ptr(u0), ptr(U), ptr(S), T, N, _f(beta), _f(theta), _f(u_r),
+                                stream_of(I)), "serial_forward")
+    return U, S
+
+
+def serial_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True, BN=None):
+    """Serial adjoint (lifscan/triton_lif.py:254-259) -> Lam = dL/dv = dL/dI.
+    GU may be None (zeros)."""
+    I, u0, U, S, GS, GU, T, N = _prep_bwd(I, u0, U, S, GS, GU)
+    Lam = torch.empty_like(I)
+    L = _lib.load()
+    with torch.cuda.device(I.device):
+        check(L.lifb_serial_bwd(ptr(I), ptr(u0), ptr(U), ptr(S), ptr(GS), ptr(GU), ptr(Lam), T, N, _f(beta),
+                                _f(theta), _f(u_r), _f(alpha), int(bool(detach)), stream_of(I)),
+              "serial_backward")
+    return Lam
+
+
+def serial_forward_tiled(I, beta, theta, u_r, u0, BN=32, D=4, num_warps=1):
+    """lifscan/triton_lif.py:460-466 (same results as serial_forward)."""
+    return serial_forward(I, beta, theta, u_r, u0)
+
+
+def serial_backward_tiled(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True, BN=32, D=4,
+                          num_warps=1):
+    """lifscan/triton_lif.py:469-476."""
+    return serial_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha, detach)
+
+
+def serial_backward_tiled_pf(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True, BN=32, D=4,
+                             num_warps=1):
+    """lifscan/triton_lif.py:1130-1135."""
+    return serial_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha, detach)
+
+
+def serial_fwd_cfg(N):
+    """Kept for signature compatibility (lifscan/triton_lif.py:1213-1218); the
+    B200 kernels choose their own tiles."""
+    return 32, 16, 1
+
+
+def serial_bwd_cfg(N):
+    """Kept for signature compatibility (lifscan/triton_lif.py:1184-1189)."""
+    return 32, 8, 1
+
+
+def serial_forward_auto(I, beta, theta, u_r, u0):
+    """lifscan/triton_lif.py:1221-1225."""
+    return serial_forward(I, beta, theta, u_r, u0)
+
+
+def serial_backward_auto(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True):
+    """lifscan/triton_lif.py:1199-1203."""
+    return serial_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha, detach)
+
+
+# ----------------------------------------------------------------------------- scan forward
+def _stats_buffer(dev, want):
+    return torch.zeros(_lib.STATS_BYTES, dtype=torch.uint8, device=dev) if want else None
+
+
+def _fill_stats(stats, buf, level):
+    st = _lib.read_stats(buf)
+    stats["repair_iters"] = int(st.repair_iters)
+    n = max(int(st.n_maps), 1)
+    stats["overflow_frac"] = float(st.n_overflow) / n
+    stats["mean_pieces"] = float(st.sum_cnt) / n + 1.0
+    if level == 3:
+        stats["max_pieces"] = int(st.max_cnt) + 1
+    else:
+        ns = max(int(st.n_super), 1)
+        stats["super_overflow_frac"] = float(st.n_super_overflow) / ns
+        stats["super_mean_pieces"] = float(st.sum_super_cnt) / ns + 1.0
+        stats["super_max_pieces"] = int(st.max_super_cnt) + 1
+
+
+def scan_forward_v3(I, beta, theta, u_r, u0, C=64, K=16, BN=32, nw=1, BNc=16, nwc=1, BNr=32, D=8, nwr=1,
+                    repair=0, stats=None):
+    """Two-level exact scan (lifscan/triton_lif.py:782-817) -> (U, S).
+
+    Envelope-pruned chunk maps of length C and capacity K, sequential carry,
+    replay, and device-side repair to convergence."""
+    I, u0, T, N = _prep_fwd(I, u0)
+    C, K = int(C), int(K)
+    if C <= 0 or T % C:
+        raise ValueError(f"T={T} must be a positive multiple of C={C}")
+    U = torch.empty_like(I)
+    S = torch.empty_like(I)
+    L = _lib.load()
+    with torch.cuda.device(I.device):
+        nb = L.lifb_scan_fwd_v3_workspace_bytes(T, N, C, K)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=I.device)
+        sb = _stats_buffer(I.device, stats is not None)
+        check(L.lifb_scan_fwd_v3(ptr(I), ptr(u0), ptr(U), ptr(S), T, N, _f(beta), _f(theta), _f(u_r), C, K,
+                                 _CONVERGE, ptr(ws), nb, ptr(sb), stream_of(I)), "scan_forward_v3")
+        if stats is not None:
+            _fill_stats(stats, sb, 3)
+    return U, S
+
+
+def scan_forward_v4(I, beta, theta, u_r, u0, C=64, G=16, K=16, K2=32, BN=32, nw=1, BNg=16, nwg=1, BNc=16,
+                    nwc=1, BNr=32, D=8, nwr=1, repair=0, stats=None):
+    """Three-level exact scan (lifscan/triton_lif.py:935-983) -> (U, S)."""
+    I, u0, T, N = _prep_fwd(I, u0)
+    C, G, K, K2 = int(C), int(G), int(K), int(K2)
+    if C <= 0 or G <= 0 or T % (C * G):
+        raise AssertionError("T must be divisible by C*G")
+    U = torch.empty_like(I)
+    S = torch.empty_like(I)
+    L = _lib.load()
+    with torch.cuda.device(I.device):
+        nb = L.lifb_scan_fwd_v4_workspace_bytes(T, N, C, G, K, K2)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=I.device)
+        sb = _stats_buffer(I.device, stats is not None)
+        check(L.lifb_scan_fwd_v4(ptr(I), ptr(u0), ptr(U), ptr(S), T, N, _f(beta), _f(theta), _f(u_r), C, G, K, K2,
+                                 _CONVERGE, ptr(ws), nb, ptr(sb), stream_of(I)), "scan_forward_v4")
+        if stats is not None:
+            _fill_stats(stats, sb, 4)
+    return U, S
+
+
+def scan_forward(I, beta, theta, u_r, u0, C=64, K=16, BN=None, repair=0, stats=None):
+    """Legacy entry (lifscan/triton_lif.py:262-295); runs the v3 algorithm,
+    whose envelope bound is tighter than the legacy global bound.  Outputs are
+    identical (both are exact); stats describe the v3 maps."""
+    return scan_forward_v3(I, beta, theta, u_r, u0, C=C, K=K, repair=repair, stats=stats)
+
+
+def scan_forward_tiled(I, beta, theta, u_r, u0, C=64, K=16, BN=128, BNr=32, D=4, nw=4, nwr=1, repair=0,
+                       stats=None):
+    """Legacy entry (lifscan/triton_lif.py:479-509); runs the v3 algorithm."""
+    return scan_forward_v3(I, beta, theta, u_r, u0, C=C, K=K, repair=repair, stats=stats)
+
+
+def scan_forward_v2(I, beta, theta, u_r, u0, C=64, K=16, BN=128, nw=4, STAGES=3, CSTAGES=1, BNr=32, D=4, nwr=1,
+                    repair=0, stats=None, Imin=None):
+    """Legacy entry (lifscan/triton_lif.py:609-642); runs the v3 algorithm."""
+    return scan_forward_v3(I, beta, theta, u_r, u0, C=C, K=K, repair=repair, stats=stats)
+
+
+def _pick_C(T, D=8):
+    """lifscan/triton_lif.py:647-651: largest C in (256, ..., 8) with T % C == 0,
+    C % D == 0 and C*C <= 4T."""
+    for C in (256, 128, 64, 32, 16, 8):
+        if T % C == 0 and C % D == 0 and C * C <= 4 * T:
+            return C
+    raise ValueError(f"T={T} needs a chunk length divisible by {D}")
+
+
+def scan_forward_auto(I, beta, theta, u_r, u0, K=16, repair=0):
+    """lifscan/triton_lif.py:1228-1232: v3 with C = _pick_C(T, 16)."""
+    T = I.shape[0]
+    return scan_forward_v3(I, beta, theta, u_r, u0, C=_pick_C(T, D=16), K=K, repair=repair)
+
+
+# ----------------------------------------------------------------------------- scan backward
+def scan_backward_tiled(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True, C=64, BNr=32, D=4,
+                        nwr=1):
+    """Tiled affine-scan backward (lifscan/triton_lif.py:512-526) -> Lam.
+    GU may be None (zeros)."""
+    I, u0, U, S, GS, GU, T, N = _prep_bwd(I, u0, U, S, GS, GU)
+    C = int(C)
+    if C <= 0 or T % C:
+        raise ValueError(f"T={T} must be a positive multiple of C={C}")
+    Lam = torch.empty_like(I)
+    L = _lib.load()
+    with torch.cuda.device(I.device):
+        nb = L.lifb_scan_bwd_workspace_bytes(T, N, C)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=I.device)
+        check(L.lifb_scan_bwd(ptr(I), ptr(u0), ptr(U), ptr(S), ptr(GS), ptr(GU), ptr(Lam), T, N, _f(beta),
+                              _f(theta), _f(u_r), _f(alpha), int(bool(detach)), C, ptr(ws), nb, stream_of(I)),
+              "scan_backward_tiled")
+    return Lam
+
+
+def scan_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True, C=64, BN=None):
+    """Legacy entry (lifscan/triton_lif.py:298-312)."""
+    return scan_backward_tiled(I, u0, U, S, GS, GU, beta, theta, u_r, alpha, detach, C=C)
+
+
+def scan_backward_auto(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0):
+    """lifscan/triton_lif.py:1235-1239: C = min(128, _pick_C(T, 2))."""
+    T = I.shape[0]
+    return scan_backward_tiled(I, u0, U, S, GS, GU, beta, theta, u_r, alpha, C=min(128, _pick_C(T, D=2)))
+
+
+# ----------------------------------------------------------------------------- helpers
+def state_bounds(I, beta, theta, u_r, u0):
+    """Loose global state bounds (lifscan/triton_lif.py:238-243); host helper,
+    not on the kernel path."""
+    Imin = I.min(0).values.clamp(max=0)
+    base = torch.minimum(u0, torch.full_like(u0, u_r)).clamp(max=0)
+    lo = base + (Imin / (1 - beta) if beta < 1 else I.clamp(max=0).sum(0))
+    hi = torch.maximum(u0, torch.full_like(u0, max(theta, u_r)))
+    return lo.contiguous(), hi.contiguous()
+
+
+def surrogate_grad(x, alpha):
+    """Derivative of sigmoid(alpha*x) (lifscan/fast.py:48-51)."""
+    sg = torch.sigmoid(alpha * x)
+    return alpha * sg * (1 - sg)
+
+
+# ----------------------------------------------------------------------------- autograd layers
+class LIFTuned(torch.autograd.Function):
+    """Hard-reset LIF, detached reset, sigmoid surrogate (lifscan/triton_lif.py:654-683).
+    mode in {"serial", "scan"}; returns spikes S [T, N]."""
+
+    @staticmethod
+    def forward(ctx, I, u0, beta, theta, u_r, alpha, mode, K, repair):
+        I = I.contiguous()
+        if mode == "serial":
+            U, S = serial_forward_auto(I, beta, theta, u_r, u0)
+        else:
+            U, S = scan_forward_auto(I, beta, theta, u_r, u0, K=K, repair=repair)
+        ctx.save_for_backward(I, u0, U, S)
+        ctx.cfg = (beta, theta, u_r, alpha, mode)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        I, u0, U, S = ctx.saved_tensors
+        beta, theta, u_r, alpha, mode = ctx.cfg
+        gS = gS.contiguous()
+        # GU is identically zero on this path: pass None instead of materialising zeros_like(gS).
+        if mode == "serial":
+            Lam = serial_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+        else:
+            Lam = scan_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+        return Lam, beta * Lam[0], None, None, None, None, None, None, None
+
+
+def lif_tuned(I, u0, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, mode="scan", K=16, repair=0):
+    """lifscan/triton_lif.py:686-687."""
+    return LIFTuned.apply(I, u0, beta, theta, u_r, alpha, mode, K, repair)
+
+
+class LIFFunction(torch.autograd.Function):
+    """Legacy layer (lifscan/triton_lif.py:315-339) with an explicit chunk length C."""
+
+    @staticmethod
+    def forward(ctx, I, u0, beta, theta, u_r, alpha, mode, C, K, repair):
+        I = I.contiguous()
+        if mode == "serial":
+            U, S = serial_forward(I, beta, theta, u_r, u0)
+        else:
+            U, S = scan_forward(I, beta, theta, u_r, u0, C=C, K=K, repair=repair)
+        ctx.save_for_backward(I, u0, U, S)
+        ctx.cfg = (beta, theta, u_r, alpha, mode, C)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        I, u0, U, S = ctx.saved_tensors
+        beta, theta, u_r, alpha, mode, C = ctx.cfg
+        gS = gS.contiguous()
+        if mode == "serial":
+            Lam = serial_backward(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+        else:
+            Lam = scan_backward(I, u0, U, S, gS, None, beta, theta, u_r, alpha, C=C)
+        return Lam, beta * Lam[0], None, None, None, None, None, None, None, None
+
+
+def lif(I, u0, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, mode="scan", C=64, K=16, repair=0):
+    """lifscan/triton_lif.py:342-343."""
+    return LIFFunction.apply(I, u0, beta, theta, u_r, alpha, mode, C, K, repair)
+
+
+# ----------------------------------------------------------------------------- auto dispatch
+# Scan only where the serial recurrence cannot fill the GPU (lifscan/triton_lif.py:986-1000).
+# The reference calibrated these on an RTX 5090; these values are B200's: the serial
+# kernels saturate HBM once ~5k independent recurrences are in flight, so time
+# parallelism pays only below that width (and only for long enough T).
+AUTO_FWD_MAX_N = 4096
+AUTO_FWD_MIN_T = 4096
+AUTO_BWD_MAX_N = 4096
+AUTO_BWD_MIN_T = 2048
+
+
+def auto_modes(N, T):
+    """lifscan/triton_lif.py:997-1000 -> (fwd_mode, bwd_mode)."""
+    fwd = "scan" if (N <= AUTO_FWD_MAX_N and T >= AUTO_FWD_MIN_T) else "serial"
+    bwd = "scan" if (N <= AUTO_BWD_MAX_N and T >= AUTO_BWD_MIN_T) else "serial"
+    return fwd, bwd
+
+
+class LIFAuto(torch.autograd.Function):
+    """lifscan/triton_lif.py:1003-1026."""
+
+    @staticmethod
+    def forward(ctx, I, u0, beta, theta, u_r, alpha, K, repair, fwd_mode, bwd_mode):
+        I = I.contiguous()
+        if fwd_mode == "scan":
+            U, S = scan_forward_auto(I, beta, theta, u_r, u0, K=K, repair=repair)
+        else:
+            U, S = serial_forward_auto(I, beta, theta, u_r, u0)
+        ctx.save_for_backward(I, u0, U, S)
+        ctx.cfg = (beta, theta, u_r, alpha, bwd_mode)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        I, u0, U, S = ctx.saved_tensors
+        beta, theta, u_r, alpha, bwd_mode = ctx.cfg
+        gS = gS.contiguous()
+        if bwd_mode == "scan":
+            Lam = scan_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+        else:
+            Lam = serial_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+        return Lam, beta * Lam[0], None, None, None, None, None, None, None, None
+
+
+def lif_auto(I, u0, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, K=16, repair=0):
+    """lifscan/triton_lif.py:1029-1031."""
+    fwd, bwd = auto_modes(I.shape[1], I.shape[0])
+    return LIFAuto.apply(I, u0, beta, theta, u_r, alpha, K, repair, fwd, bwd)

@@ -1,0 +1,138 @@
+/*
+ * lifscan_b200.h -- C ABI of the B200 (sm_100a) exact hard-reset LIF scan.
+ *
+ * The reference (cheshireyang/hard-resets-compose) exposes this path only as
+ * Python functions in lifscan/triton_lif.py; it has no native FFI.  Each entry
+ * point below is what a ctypes/cffi binding of that Python API binds: the same
+ * tensors as raw device pointers, the same scalars, the same sizes.  The
+ * reference function each one replaces is cited beside it.
+ *
+ * Conventions (identical to the reference, lifscan/triton_lif.py:3):
+ *   - I, U, S, GS, GU, Lam are [T, N] fp32, row-major, contiguous, neuron index
+ *     fastest (element (t, n) at t*N + n); N = batch x neurons.
+ *   - u0 is [N] fp32.  S holds 0.0f / 1.0f.
+ *   - All pointers are CUDA device pointers on the current device; the work is
+ *     enqueued on `stream` (a cudaStream_t passed as void*, NULL = legacy
+ *     default stream) and the call returns without synchronising.
+ *   - beta, theta, u_r, alpha are used as fp32 (the reference casts its Python
+ *     floats to fp32 once).
+ *   - Scratch memory is caller-provided: query *_workspace_bytes, pass a device
+ *     buffer of at least that size (256-byte aligned).  The library allocates
+ *     nothing on these paths.
+ *   - Forward outputs are bit-identical to the serial fp32 recurrence
+ *     v = fl(fl(beta*u) + x); s = v >= theta; u = s ? u_r : v
+ *     (lifscan/fast.py:69-81) for every input without NaN.
+ * Every function returns LIFB_OK (0) or a nonzero status; it never throws and
+ * never aborts.  lifb_last_error() returns a message for the calling thread.
+ */
+#ifndef LIFSCAN_B200_H
+#define LIFSCAN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LIFB_OK 0
+#define LIFB_ERR_INVALID_ARGUMENT 1 /* shape, capacity or parameter out of range */
+#define LIFB_ERR_CUDA 2             /* a CUDA runtime call or launch failed */
+#define LIFB_ERR_WORKSPACE 3        /* workspace NULL, too small or misaligned */
+#define LIFB_ERR_UNSUPPORTED 4      /* valid request this build cannot serve */
+
+/* Device-resident counters filled by the scan forward when a stats pointer is
+ * given; they give the reference's `stats` dict (triton_lif.py:812-816 for v3,
+ * :976-982 for v4):
+ *   repair_iters        = repair_iters
+ *   overflow_frac       = n_overflow / n_maps
+ *   mean_pieces         = sum_cnt / n_maps + 1
+ *   max_pieces          = max_cnt + 1
+ *   super_overflow_frac = n_super_overflow / n_super           (v4)
+ *   super_mean_pieces   = sum_super_cnt / n_super + 1          (v4)
+ *   super_max_pieces    = max_super_cnt + 1                    (v4)
+ * The struct lives in device memory; copy it to the host after the stream
+ * has finished.  The call zeroes it before counting. */
+typedef struct lifb_stats {
+    int32_t repair_iters;
+    int32_t max_cnt;
+    int32_t max_super_cnt;
+    int32_t status; /* 0, or a nonzero device-side status code */
+    int64_t n_maps;
+    int64_t n_overflow;
+    int64_t sum_cnt;
+    int64_t n_super;
+    int64_t n_super_overflow;
+    int64_t sum_super_cnt;
+} lifb_stats;
+
+/* ABI version of this header; bumped on any signature change. */
+int lifb_abi_version(void);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices, all threads).  Diagnostic: lets a caller count the library's own
+ * launches inside a timed region. */
+uint64_t lifb_kernel_launches(void);
+
+/* Human-readable text of a status code, and the last error message recorded
+ * on the calling host thread (empty string if none). */
+const char *lifb_status_string(int status);
+const char *lifb_last_error(void);
+
+/* Serial forward: one recurrence per neuron, time-tiled.
+ * Replaces serial_forward_auto (lifscan/triton_lif.py:1221-1225), which is
+ * serial_forward_tiled (:460-466) over fwd_tiled_kernel (:353-379), and
+ * serial_forward (:246-251). */
+int lifb_serial_fwd(const float *I, const float *u0, float *U, float *S,
+                    int64_t T, int64_t N, float beta, float theta, float u_r,
+                    void *stream);
+
+/* Serial adjoint: lam_t = a_t lam_{t+1} + b_t swept backwards, with the
+ * sigmoid surrogate (alpha) and the detached (detach != 0) or attached reset.
+ * GU may be NULL (all zeros, the lif_tuned path).
+ * Replaces serial_backward_auto (lifscan/triton_lif.py:1199-1203), i.e.
+ * bwd_tiled_pf_kernel (:1087-1127), and serial_backward (:254-259). */
+int lifb_serial_bwd(const float *I, const float *u0, const float *U, const float *S,
+                    const float *GS, const float *GU, float *Lam,
+                    int64_t T, int64_t N, float beta, float theta, float u_r,
+                    float alpha, int detach, void *stream);
+
+/* Two-level exact scan forward with envelope-pruned chunk maps.
+ * C = chunk length (T % C == 0), K = map capacity (1..64).
+ * max_repair < 0: repair until converged (always within T/C rounds), the
+ * default of the Python layer; max_repair >= 0 caps the rounds like the
+ * reference's `repair` argument.
+ * Replaces scan_forward_v3 (lifscan/triton_lif.py:782-817). */
+size_t lifb_scan_fwd_v3_workspace_bytes(int64_t T, int64_t N, int C, int K);
+int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S,
+                     int64_t T, int64_t N, float beta, float theta, float u_r,
+                     int C, int K, int max_repair,
+                     void *workspace, size_t workspace_bytes,
+                     lifb_stats *stats_dev, void *stream);
+
+/* Three-level exact scan forward: chunk maps (C, K) composed in groups of G
+ * into super maps of capacity K2 (1..64); T % (C*G) == 0.
+ * Replaces scan_forward_v4 (lifscan/triton_lif.py:935-983). */
+size_t lifb_scan_fwd_v4_workspace_bytes(int64_t T, int64_t N, int C, int G, int K, int K2);
+int lifb_scan_fwd_v4(const float *I, const float *u0, float *U, float *S,
+                     int64_t T, int64_t N, float beta, float theta, float u_r,
+                     int C, int G, int K, int K2, int max_repair,
+                     void *workspace, size_t workspace_bytes,
+                     lifb_stats *stats_dev, void *stream);
+
+/* Tiled affine-scan backward with the surrogate fused in; C = chunk length
+ * (T % C == 0).  GU may be NULL (zeros).
+ * Replaces scan_backward_tiled (lifscan/triton_lif.py:512-526) and, with the
+ * reference's choice of C, scan_backward_auto (:1235-1239). */
+size_t lifb_scan_bwd_workspace_bytes(int64_t T, int64_t N, int C);
+int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *S,
+                  const float *GS, const float *GU, float *Lam,
+                  int64_t T, int64_t N, float beta, float theta, float u_r,
+                  float alpha, int detach, int C,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIFSCAN_B200_H */

@@ -1,0 +1,174 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference.
+
+Run once in a container that has the reference checked out (read-only) at
+$LIFSCAN_REF (default /root/reference):
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own code:
+  * lifscan/fast.py (PyTorch CPU): serial_forward_nograd (fast.py:69-81) and
+    serial_backward (fast.py:227-239) -> the bit-exact forward anchor and the
+    gradient anchor;
+  * lifscan/triton_lif.py under TRITON_INTERPRET=1 (its Triton kernels run on
+    the CPU through the interpreter, with numpy fp32 arithmetic and no FMA
+    contraction): the v3 phases env_chunk/env_carry/build3/carry2
+    (triton_lif.py:698-779, 578-606), scan_forward_v3 (:782), the v4 phases
+    compose_group/carry_inner (:828-932), scan_forward_v4 (:935) and
+    scan_backward_tiled (:512), including their internal map arrays and stats.
+
+Inputs are drawn on the CPU with torch.Generator (tests/test_fast.py:7-9) and
+stored in the fixture too.  The GPU box never runs this script; the tests read
+only the .npz files it writes next to itself.
+"""
+import os
+import sys
+
+os.environ["TRITON_INTERPRET"] = "1"
+REF = os.environ.get("LIFSCAN_REF", "/root/reference")
+sys.path.insert(0, REF)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import triton  # noqa: E402
+
+from lifscan import fast  # noqa: E402
+from lifscan import triton_lif as L  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def gen(T, N, mu, sd, seed, u0_sd):
+    g = torch.Generator().manual_seed(seed)
+    I = (mu + sd * torch.randn(T, N, generator=g)).to(torch.float32).contiguous()
+    u0 = (u0_sd * torch.randn(N, generator=g)).to(torch.float32) if u0_sd else torch.zeros(N)
+    GS = torch.randn(T, N, generator=g).to(torch.float32)
+    return I, u0.contiguous(), GS
+
+
+def v3_internals(I, beta, theta, u_r, u0, C, K):
+    """The phases of scan_forward_v3 (triton_lif.py:782-803), run one by one."""
+    T, N = I.shape
+    M = T // C
+    BN, BNc, BNr, D = 32, 16, 32, 8
+    EC = torch.empty(M, N); EA = torch.empty(M, N); EB = torch.empty(M, N)
+    De = D if C % D == 0 else 1
+    L.env_chunk_kernel[(M, triton.cdiv(N, BNr))](I, EC, EA, EB, N, C, beta, u_r, BN=BNr, D=De)
+    Lo = torch.empty(M, N)
+    L.env_carry_kernel[(triton.cdiv(N, BNc),)](u0, EC, EA, EB, Lo, N, M, 1e-5, BN=BNc)
+    MA = torch.empty(M, N); MB = torch.empty(M, N)
+    MX = torch.empty(M, K, N); MC = torch.empty(M, K, N)
+    MN = torch.empty(M, N, dtype=torch.int32); OVF = torch.empty(M, N, dtype=torch.int32)
+    L.build3_kernel[(M, triton.cdiv(N, BN))](I, Lo, u0, MA, MB, MX, MC, MN, OVF, N, C, beta, theta, u_r,
+                                             K=K, BN=BN)
+    Starts = torch.empty(M, N)
+    L.carry2_kernel[(triton.cdiv(N, BNc),)](I, u0, MA, MB, MX, MC, MN, OVF, Starts, N, M, C,
+                                            beta, theta, u_r, K=K, BN=BNc, STAGES=1)
+    return dict(Lo=Lo, MA=MA, MB=MB, MX=MX, MC=MC, MN=MN, OVF=OVF, Starts=Starts)
+
+
+def v4_internals(I, beta, theta, u_r, u0, C, G, K, K2, base):
+    """compose_group + carry over supers + carry_inner (triton_lif.py:951-965)."""
+    T, N = I.shape
+    M = T // C
+    M2 = M // G
+    BNg, BNc = 16, 16
+    SA = torch.empty(M2, N); SB = torch.empty(M2, N)
+    SX = torch.empty(M2, K2, N); SC = torch.empty(M2, K2, N)
+    SN = torch.empty(M2, N, dtype=torch.int32); SOVF = torch.empty(M2, N, dtype=torch.int32)
+    L.compose_group_kernel[(M2, triton.cdiv(N, BNg))](base["MA"], base["MB"], base["MX"], base["MC"],
+                                                      base["MN"], base["OVF"], base["Lo"], u0,
+                                                      SA, SB, SX, SC, SN, SOVF, N, G, theta, u_r,
+                                                      K=K, K2=K2, BN=BNg)
+    SStarts = torch.empty(M2, N)
+    L.carry2_kernel[(triton.cdiv(N, BNc),)](I, u0, SA, SB, SX, SC, SN, SOVF, SStarts, N, M2, C * G,
+                                            beta, theta, u_r, K=K2, BN=BNc, STAGES=1)
+    Starts = torch.empty(M, N)
+    L.carry_inner_kernel[(M2, triton.cdiv(N, BNc))](I, SStarts, base["MA"], base["MB"], base["MX"],
+                                                    base["MC"], base["MN"], base["OVF"], Starts, N, G, C,
+                                                    beta, theta, u_r, K=K, BN=BNc)
+    return dict(SA=SA, SB=SB, SX=SX, SC=SC, SN=SN, SOVF=SOVF, SStarts=SStarts, Starts4=Starts)
+
+
+FWD_CASES = [
+    # name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, K
+    ("c1like", 512, 40, 0.1, 0.3, 0, 0.0, 0.9, 0.0, 64, 16),
+    ("c2like", 512, 33, 0.05, 0.2, 1, 0.0, 0.99, 0.0, 64, 16),
+    ("b05_neg", 256, 24, -0.1, 0.6, 2, 0.3, 0.5, -0.1, 32, 4),
+    ("b1_ovf", 256, 24, 0.4, 0.2, 3, 0.3, 1.0, -0.1, 64, 2),
+    ("b099_k64", 256, 17, 0.15, 0.4, 4, 0.3, 0.99, -0.1, 32, 64),
+]
+
+V4_CASES = [
+    # name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, G, K, K2
+    ("v4a", 1024, 20, 0.15, 0.4, 5, 0.3, 0.99, -0.1, 32, 8, 8, 16),
+    ("v4b", 512, 20, 0.1, 0.3, 6, 0.0, 0.9, 0.0, 16, 4, 4, 8),
+]
+
+BWD_CASES = [
+    # name, T, N, mu, sd, seed, u0_sd, beta, u_r, alpha, detach, C
+    ("bwd_det", 256, 24, 0.15, 0.4, 7, 0.2, 0.9, -0.1, 4.0, True, 32),
+    ("bwd_nodet", 256, 24, 0.15, 0.4, 8, 0.2, 0.9, -0.1, 4.0, False, 64),
+    ("bwd_c2like", 256, 33, 0.05, 0.2, 9, 0.0, 0.99, 0.0, 4.0, True, 64),
+]
+
+
+def npy(d):
+    return {k: v.numpy() if torch.is_tensor(v) else np.asarray(v) for k, v in d.items()}
+
+
+def main():
+    theta = 1.0
+    for (name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, K) in FWD_CASES:
+        I, u0, _ = gen(T, N, mu, sd, seed, u0_sd)
+        us, ss, vs = fast.serial_forward_nograd(I, beta, theta, u_r, u0)
+        inter = v3_internals(I, beta, theta, u_r, u0, C, K)
+        st0, st = {}, {}
+        U0, S0 = L.scan_forward_v3(I, beta, theta, u_r, u0, C=C, K=K, repair=0, stats=st0)
+        U, S = L.scan_forward_v3(I, beta, theta, u_r, u0, C=C, K=K, repair=10 ** 6, stats=st)
+        assert torch.equal(U, us) and torch.equal(S, ss), name
+        out = dict(I=I, u0=u0, U=us, S=ss, U_norepair=U0, S_norepair=S0,
+                   params=np.array([beta, theta, u_r, C, K], np.float64),
+                   stats_keys=np.array(sorted(st)), stats_vals=np.array([st[k] for k in sorted(st)], np.float64),
+                   stats0_vals=np.array([st0[k] for k in sorted(st0)], np.float64))
+        out.update(inter)
+        np.savez_compressed(os.path.join(HERE, f"fwd_{name}.npz"), **npy(out))
+        print(name, st, st0)
+
+    for (name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, G, K, K2) in V4_CASES:
+        I, u0, _ = gen(T, N, mu, sd, seed, u0_sd)
+        us, ss, _ = fast.serial_forward_nograd(I, beta, theta, u_r, u0)
+        base = v3_internals(I, beta, theta, u_r, u0, C, K)
+        inter = v4_internals(I, beta, theta, u_r, u0, C, G, K, K2, base)
+        st = {}
+        U, S = L.scan_forward_v4(I, beta, theta, u_r, u0, C=C, G=G, K=K, K2=K2, repair=10 ** 6, stats=st)
+        assert torch.equal(U, us) and torch.equal(S, ss), name
+        out = dict(I=I, u0=u0, U=us, S=ss, params=np.array([beta, theta, u_r, C, G, K, K2], np.float64),
+                   stats_keys=np.array(sorted(st)), stats_vals=np.array([st[k] for k in sorted(st)], np.float64))
+        out.update({k: base[k] for k in ("Lo", "MN", "OVF", "MA", "MB")})
+        out.update(inter)
+        np.savez_compressed(os.path.join(HERE, f"v4_{name}.npz"), **npy(out))
+        print(name, st)
+
+    for (name, T, N, mu, sd, seed, u0_sd, beta, u_r, alpha, detach, C) in BWD_CASES:
+        I, u0, GS = gen(T, N, mu, sd, seed, u0_sd)
+        GU = torch.randn(T, N, generator=torch.Generator().manual_seed(seed + 100)) if not detach \
+            else torch.zeros(T, N)
+        us, ss, vs = fast.serial_forward_nograd(I, beta, theta, u_r, u0)
+        lam_fast = fast.serial_backward(vs, ss, GS, GU, beta, theta, u_r, alpha, detach_reset=detach)
+        lam_tri = L.scan_backward_tiled(I, u0, us, ss, GS, GU, beta, theta, u_r, alpha, detach=detach,
+                                        C=C, BNr=16, D=4)
+        # fp64 autograd through the reference's differentiable serial loop (fast.py:52-66)
+        Id = I.double().requires_grad_(True)
+        u0d = u0.double().requires_grad_(True)
+        ud, sd_ = fast.serial_lif(Id, beta, theta, u_r, u0d, alpha=alpha, detach_reset=detach)
+        ((GS.double() * sd_).sum() + (GU.double() * ud).sum()).backward()
+        out = dict(I=I, u0=u0, U=us, S=ss, GS=GS, GU=GU, Lam_fast=lam_fast, Lam_triton=lam_tri,
+                   dI_fp64=Id.grad, du0_fp64=u0d.grad,
+                   params=np.array([beta, theta, u_r, alpha, float(detach), C], np.float64))
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **npy(out))
+        rel = ((lam_fast - lam_tri).norm() / lam_fast.norm()).item()
+        print(name, "fast vs triton-interp rel", rel)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,115 @@
+"""GPU backward and autograd parity through the C ABI.
+
+Gradients must match the reference's backward within relative error 1e-5
+(north star).  References: the oracle's restatement of
+lifscan/fast.py:227-239 (serial adjoint) and of the tiled scan
+(lifscan/triton_lif.py:512-526), the reference's own outputs stored in
+tests/golden/bwd_*.npz, and fp64 autograd through fast.serial_lif."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.helpers import assert_bit_equal, gen, rel, to_dev
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5  # relative (Frobenius) error bound on dI and du0
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def L():
+    from hard_resets_compose_b200 import lifscan
+    return lifscan
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "bwd_*.npz"))), ids=os.path.basename)
+def test_golden_reference_gradients(cuda, path):
+    z = np.load(path)
+    beta, theta, u_r, alpha, det, C = (float(v) for v in z["params"])
+    det = bool(det)
+    d = to_dev(cuda, z["I"], z["u0"], z["U"], z["S"], z["GS"], z["GU"])
+    GU = d[5] if not det else None
+    l1 = L().serial_backward(*d[:5], GU, beta, theta, u_r, alpha, det)
+    l2 = L().scan_backward_tiled(*d[:5], GU, beta, theta, u_r, alpha, det, C=int(C))
+    assert rel(_np(l1), z["Lam_fast"]) < TOL
+    assert rel(_np(l2), z["Lam_fast"]) < TOL
+    assert rel(_np(l2), z["Lam_triton"]) < TOL
+    assert rel(_np(l1), z["dI_fp64"]) < TOL
+
+
+@pytest.mark.parametrize("detach", (True, False))
+@pytest.mark.parametrize("N,T,C", ((100, 4096, 64), (1000, 2048, 128), (5000, 1024, 64), (37, 512, 8)))
+def test_backward_vs_oracle(cuda, detach, N, T, C):
+    I, u0, GS = gen(T, N, 0.15, 0.4, seed=1, u0_sd=0.2, grad=True)
+    U, S = O.serial_forward(I, 0.9, 1.0, -0.1, u0)
+    GU = np.random.default_rng(2).standard_normal(I.shape).astype(np.float32)
+    ref = O.serial_backward(I, u0, U, S, GS, GU, 0.9, 1.0, -0.1, 4.0, detach)
+    d = to_dev(cuda, I, u0, U, S, GS, GU)
+    l1 = L().serial_backward(*d, 0.9, 1.0, -0.1, 4.0, detach)
+    l2 = L().scan_backward_tiled(*d, 0.9, 1.0, -0.1, 4.0, detach, C=C)
+    assert rel(_np(l1), ref) < TOL
+    assert rel(_np(l2), ref) < TOL
+
+
+@pytest.mark.parametrize("mode", ("scan", "serial"))
+def test_lif_tuned_c2_forward_backward(cuda, mode):
+    """lif_tuned fwd+bwd, B*N = 16384, T = 1024,
+    x ~ N(0.05, 0.2^2), beta = 0.99, default surrogate, upstream grad N(0, 1)."""
+    T, N, beta = 1024, 16384, 0.99
+    I, u0, GS = gen(T, N, 0.05, 0.2, seed=0, grad=True)
+    Us, Ss = O.serial_forward(I, beta, 1.0, 0.0, u0)
+    dI_ref = O.serial_backward(I, u0, Us, Ss, GS, None, beta, 1.0, 0.0, 4.0, True)
+    Id, u0d, GSd = to_dev(cuda, I, u0, GS)
+    Id.requires_grad_(True)
+    u0d.requires_grad_(True)
+    S = L().lif_tuned(Id, u0d, beta=beta, mode=mode)
+    (S * GSd).sum().backward()
+    assert_bit_equal(_np(S), Ss, "S")
+    assert rel(_np(Id.grad), dI_ref) < TOL
+    assert rel(_np(u0d.grad), beta * dI_ref[0]) < TOL
+
+
+def test_lif_auto_and_legacy_layer(cuda):
+    T, N = 2048, 1000
+    I, u0, GS = gen(T, N, 0.15, 0.4, seed=3, grad=True)
+    Us, Ss = O.serial_forward(I, 0.9, 1.0, 0.0, u0)
+    dI_ref = O.serial_backward(I, u0, Us, Ss, GS, None, 0.9, 1.0, 0.0, 4.0, True)
+    for f in (lambda x, u: L().lif_auto(x, u, beta=0.9),
+              lambda x, u: L().lif(x, u, beta=0.9, mode="scan", C=64),
+              lambda x, u: L().lif(x, u, beta=0.9, mode="serial")):
+        Id, u0d, GSd = to_dev(cuda, I, u0, GS)
+        Id.requires_grad_(True)
+        S = f(Id, u0d)
+        (S * GSd).sum().backward()
+        assert_bit_equal(_np(S), Ss, "S")
+        assert rel(_np(Id.grad), dI_ref) < TOL
+
+
+def test_gradient_against_fp64_autograd(cuda):
+    """fp32 scan gradient vs an fp64 autograd pass through a plain serial
+    recurrence in torch (the reference's fast.serial_lif, restated)."""
+    T, N, beta, alpha = 512, 64, 0.9, 4.0
+    I, u0, GS = gen(T, N, 0.15, 0.4, seed=4, grad=True)
+    Ix = torch.from_numpy(I).double().requires_grad_(True)
+    u = torch.zeros(N, dtype=torch.float64)
+    ss = []
+    for t in range(T):
+        v = beta * u + Ix[t]
+        sg = torch.sigmoid(alpha * (v - 1.0))
+        # Heaviside forward, ds/dv = alpha*sg*(1-sg) backward (lifscan/fast.py:33-51)
+        s = (v >= 1.0).double() + (sg - sg.detach())
+        u = v * (1 - s.detach())  # detached reset to u_r = 0
+        ss.append(s)
+    (torch.from_numpy(GS).double() * torch.stack(ss)).sum().backward()
+    Id, u0d, GSd = to_dev(cuda, I, u0, GS)
+    Id.requires_grad_(True)
+    S = L().lif_tuned(Id, u0d, beta=beta, mode="scan")
+    (S * GSd).sum().backward()
+    assert rel(_np(Id.grad), Ix.grad.numpy()) < 1e-5

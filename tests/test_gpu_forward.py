@@ -1,0 +1,171 @@
+"""GPU forward parity through the C ABI: U and S bit-identical to the serial
+fp32 recurrence (the CPU oracle, itself pinned to lifscan/fast.py), and the
+scan's stats equal to the oracle's (hence the reference's).
+
+Grids follow the reference's GPU tests: tests/test_triton.py:10-26 (beta x
+drift x K, u_r = -0.1, u0 ~ N(0, 0.3^2)), tests/test_triton_tiled.py:6-20
+(ragged widths), experiments/test_v3.py:12-22 and experiments/test_v4.py:6-20.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.helpers import assert_bit_equal, gen, to_dev
+
+pytestmark = pytest.mark.gpu
+
+BETAS = (0.5, 0.9, 0.99, 1.0)
+DRIFTS = ((0.15, 0.4), (-0.1, 0.6), (0.4, 0.2))
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def L():
+    from hard_resets_compose_b200 import lifscan
+    return lifscan
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+@pytest.mark.parametrize("N,T", ((100, 4096), (1000, 2048), (5000, 1024), (1, 300), (33, 7)))
+def test_serial_forward_bit_exact(cuda, N, T):
+    I, u0 = gen(T, N, 0.15, 0.4, seed=1, u0_sd=0.2)
+    Us, Ss = O.serial_forward(I, 0.9, 1.0, -0.1, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    U, S = L().serial_forward(Id, 0.9, 1.0, -0.1, u0d)
+    assert_bit_equal(_np(U), Us, "U")
+    assert_bit_equal(_np(S), Ss, "S")
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "fwd_*.npz"))), ids=os.path.basename)
+def test_golden_reference_outputs_and_stats(cuda, path):
+    """Against the reference's own outputs (fast.py) and the stats of its v3
+    kernels (stored by tests/golden/make_golden.py)."""
+    z = np.load(path)
+    beta, theta, u_r, C, K = (float(v) for v in z["params"])
+    Id, u0d = to_dev(cuda, z["I"], z["u0"])
+    U, S = L().serial_forward(Id, beta, theta, u_r, u0d)
+    assert_bit_equal(_np(U), z["U"], "serial U")
+    assert_bit_equal(_np(S), z["S"], "serial S")
+    st = {}
+    U, S = L().scan_forward_v3(Id, beta, theta, u_r, u0d, C=int(C), K=int(K), stats=st)
+    assert_bit_equal(_np(U), z["U"], "v3 U")
+    assert_bit_equal(_np(S), z["S"], "v3 S")
+    ref = {str(k): float(v) for k, v in zip(z["stats_keys"], z["stats_vals"])}
+    assert st["repair_iters"] == int(ref["repair_iters"])
+    assert st["max_pieces"] == int(ref["max_pieces"])
+    assert abs(st["overflow_frac"] - ref["overflow_frac"]) < 1e-6
+    assert abs(st["mean_pieces"] - ref["mean_pieces"]) < 1e-5
+
+
+@pytest.mark.parametrize("beta", BETAS)
+@pytest.mark.parametrize("mu,sd", DRIFTS)
+@pytest.mark.parametrize("K", (4, 16, 64))
+def test_v3_bit_exact_and_stats(cuda, beta, mu, sd, K):
+    T, N = 4096, 1000
+    I, u0 = gen(T, N, mu, sd, seed=0, u0_sd=0.3)
+    Us, Ss = O.serial_forward(I, beta, 1.0, -0.1, u0)
+    _, _, ost = O.scan_forward_v3(I, beta, 1.0, -0.1, u0, C=64, K=K)
+    Id, u0d = to_dev(cuda, I, u0)
+    st = {}
+    U, S = L().scan_forward_v3(Id, beta, 1.0, -0.1, u0d, C=64, K=K, stats=st)
+    assert_bit_equal(_np(U), Us, "U")
+    assert_bit_equal(_np(S), Ss, "S")
+    assert st["repair_iters"] == ost["repair_iters"]
+    assert st["max_pieces"] == ost["max_pieces"]
+    assert abs(st["overflow_frac"] - ost["overflow_frac"]) < 1e-12
+    assert abs(st["mean_pieces"] - ost["mean_pieces"]) < 1e-9
+
+
+@pytest.mark.parametrize("beta", BETAS)
+@pytest.mark.parametrize("mu,sd", DRIFTS)
+@pytest.mark.parametrize("K,K2", ((16, 32), (8, 16)))
+def test_v4_bit_exact_and_stats(cuda, beta, mu, sd, K, K2):
+    T, N = 8192, 777
+    I, u0 = gen(T, N, mu, sd, seed=0, u0_sd=0.3)
+    Us, Ss = O.serial_forward(I, beta, 1.0, -0.1, u0)
+    _, _, ost = O.scan_forward_v4(I, beta, 1.0, -0.1, u0, C=64, G=16, K=K, K2=K2)
+    Id, u0d = to_dev(cuda, I, u0)
+    st = {}
+    U, S = L().scan_forward_v4(Id, beta, 1.0, -0.1, u0d, C=64, G=16, K=K, K2=K2, stats=st)
+    assert_bit_equal(_np(U), Us, "U")
+    assert_bit_equal(_np(S), Ss, "S")
+    for k in ("repair_iters", "super_max_pieces"):
+        assert st[k] == ost[k], k
+    for k in ("overflow_frac", "super_overflow_frac", "mean_pieces", "super_mean_pieces"):
+        assert abs(st[k] - ost[k]) < 1e-9, k
+
+
+@pytest.mark.parametrize("C,K", ((8, 1), (16, 2), (32, 4), (256, 8), (1024, 16)))
+def test_v3_chunk_shapes_and_overflow(cuda, C, K):
+    """Tiny capacities force the in-carry serial fallback; C = T is one chunk."""
+    T, N = 1024, 257
+    I, u0 = gen(T, N, 0.2, 0.5, seed=7, u0_sd=0.3)
+    Us, Ss = O.serial_forward(I, 0.95, 1.0, 0.0, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    st = {}
+    U, S = L().scan_forward_v3(Id, 0.95, 1.0, 0.0, u0d, C=C, K=K, stats=st)
+    assert_bit_equal(_np(U), Us, "U")
+    assert_bit_equal(_np(S), Ss, "S")
+    _, _, ost = O.scan_forward_v3(I, 0.95, 1.0, 0.0, u0, C=C, K=K)
+    assert st["overflow_frac"] == pytest.approx(ost["overflow_frac"], abs=1e-12)
+
+
+def test_c1_full_size_bit_exact(cuda):
+    """B*N = 4096, T = 1024, x ~ N(0.1, 0.3^2), beta = 0.9."""
+    I, u0 = gen(1024, 4096, 0.1, 0.3, seed=0)
+    Us, Ss = O.serial_forward(I, 0.9, 1.0, 0.0, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    for fn in (lambda: L().scan_forward_auto(Id, 0.9, 1.0, 0.0, u0d),
+               lambda: L().scan_forward_v3(Id, 0.9, 1.0, 0.0, u0d, C=64, K=16),
+               lambda: L().serial_forward_auto(Id, 0.9, 1.0, 0.0, u0d)):
+        U, S = fn()
+        assert_bit_equal(_np(U), Us, "U")
+        assert_bit_equal(_np(S), Ss, "S")
+
+
+def test_c2_full_size_bit_exact(cuda):
+    """BASELINE config 2 forward: B*N = 16384, T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99."""
+    I, u0 = gen(1024, 16384, 0.05, 0.2, seed=0)
+    Us, Ss = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    U, S = L().scan_forward_auto(Id, 0.99, 1.0, 0.0, u0d)
+    assert_bit_equal(_np(U), Us, "U")
+    assert_bit_equal(_np(S), Ss, "S")
+
+
+def test_long_sequence_v4_properties(cuda):
+    """Long-T three-level path at reduced T (T = 2^18, B*N = 1024): exact
+    against the oracle's serial recurrence."""
+    T, N = 1 << 18, 1024
+    I, u0 = gen(T, N, 0.02, 0.1, seed=0)
+    Us, Ss = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    U, S = L().scan_forward_v4(Id, 0.99, 1.0, 0.0, u0d, C=64, G=16, K=16, K2=32)
+    assert_bit_equal(_np(S), Ss, "S")
+    assert_bit_equal(_np(U), Us, "U")
+
+
+def test_empty_inputs(cuda):
+    I = torch.empty(0, 5, device=cuda)
+    U, S = L().serial_forward(I, 0.9, 1.0, 0.0, torch.zeros(5, device=cuda))
+    assert U.shape == (0, 5)
+    I = torch.empty(64, 0, device=cuda)
+    U, S = L().scan_forward_v3(I, 0.9, 1.0, 0.0, torch.zeros(0, device=cuda))
+    assert U.shape == (64, 0)
+
+
+def test_bad_arguments_raise(cuda):
+    I = torch.zeros(100, 4, device=cuda)
+    with pytest.raises(ValueError):
+        L().scan_forward_v3(I, 0.9, 1.0, 0.0, torch.zeros(4, device=cuda), C=64)
+    with pytest.raises(Exception):
+        L().scan_forward_v3(torch.zeros(128, 4, device=cuda), 0.9, 1.0, 0.0, torch.zeros(4, device=cuda), C=64,
+                            K=65)
+    with pytest.raises(ValueError):
+        L().serial_forward(I, 0.9, 1.0, 0.0, torch.zeros(5, device=cuda))

@@ -1,0 +1,127 @@
+"""Pin the CPU oracle to the reference (no GPU needed).
+
+tests/golden/*.npz were written by tests/golden/make_golden.py from the
+reference's own code: lifscan/fast.py (serial forward / backward) and the
+reference's Triton kernels run through the Triton interpreter (v3/v4 phases,
+maps, starts, stats and the tiled backward).  The oracle must reproduce the
+integer/bit-level quantities exactly and the gradients to 1e-6 relative.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.helpers import assert_bit_equal, rel
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+FWD = sorted(glob.glob(os.path.join(GOLD, "fwd_*.npz")))
+V4 = sorted(glob.glob(os.path.join(GOLD, "v4_*.npz")))
+BWD = sorted(glob.glob(os.path.join(GOLD, "bwd_*.npz")))
+
+
+def _valid(arr, cnt, K):
+    mask = np.arange(K)[None, :, None] < cnt[:, None, :]
+    return np.where(mask, arr, 0.0).astype(np.float32)
+
+
+def _stats(z):
+    return {str(k): float(v) for k, v in zip(z["stats_keys"], z["stats_vals"])}
+
+
+def test_fixtures_present():
+    assert len(FWD) >= 5 and len(V4) >= 2 and len(BWD) >= 3
+
+
+@pytest.mark.parametrize("path", FWD, ids=os.path.basename)
+def test_serial_forward_matches_fast_py(path):
+    z = np.load(path)
+    beta, theta, u_r = (float(v) for v in z["params"][:3])
+    U, S = O.serial_forward(z["I"], beta, theta, u_r, z["u0"])
+    assert_bit_equal(U, z["U"], "U")
+    assert_bit_equal(S, z["S"], "S")
+
+
+@pytest.mark.parametrize("path", FWD, ids=os.path.basename)
+def test_v3_phases_match_reference_kernels(path):
+    z = np.load(path)
+    beta, theta, u_r, C, K = z["params"]
+    C, K = int(C), int(K)
+    I, u0 = z["I"], z["u0"]
+    Lo = O.envelope(I, u0, C, float(beta), float(u_r))
+    assert_bit_equal(Lo, z["Lo"], "Lo (env_chunk + env_carry)")
+    d = O.build_maps(I, u0, Lo, C, K, float(beta), float(theta), float(u_r))
+    for k in ("MA", "MB", "MN", "OVF"):
+        assert_bit_equal(d[k], z[k], k)
+    assert_bit_equal(_valid(d["MX"], d["MN"], K), _valid(z["MX"], z["MN"], K), "MX (live slots)")
+    assert_bit_equal(_valid(d["MC"], d["MN"], K), _valid(z["MC"], z["MN"], K), "MC (live slots)")
+
+
+@pytest.mark.parametrize("path", FWD, ids=os.path.basename)
+def test_v3_outputs_and_stats(path):
+    z = np.load(path)
+    beta, theta, u_r, C, K = z["params"]
+    C, K = int(C), int(K)
+    U, S, st = O.scan_forward_v3(z["I"], float(beta), float(theta), float(u_r), z["u0"], C=C, K=K)
+    assert_bit_equal(U, z["U"], "U after repair")
+    assert_bit_equal(S, z["S"], "S after repair")
+    ref = _stats(z)
+    assert st["repair_iters"] == int(ref["repair_iters"])
+    assert st["max_pieces"] == int(ref["max_pieces"])
+    assert abs(st["overflow_frac"] - ref["overflow_frac"]) < 1e-6
+    assert abs(st["mean_pieces"] - ref["mean_pieces"]) < 1e-5
+    # without repair the replay from the carried starts must match the reference's too
+    U0, S0, _ = O.scan_forward_v3(z["I"], float(beta), float(theta), float(u_r), z["u0"], C=C, K=K, repair=0)
+    assert_bit_equal(U0, z["U_norepair"], "U without repair")
+    assert_bit_equal(S0, z["S_norepair"], "S without repair")
+
+
+@pytest.mark.parametrize("path", V4, ids=os.path.basename)
+def test_v4_phases_outputs_and_stats(path):
+    z = np.load(path)
+    beta, theta, u_r, C, G, K, K2 = z["params"]
+    C, G, K, K2 = int(C), int(G), int(K), int(K2)
+    U, S, st, d = O.scan_forward_v4(z["I"], float(beta), float(theta), float(u_r), z["u0"], C=C, G=G, K=K,
+                                    K2=K2, return_internals=True)
+    assert_bit_equal(U, z["U"], "U")
+    assert_bit_equal(S, z["S"], "S")
+    for k in ("SA", "SB", "SN", "SOVF", "SStarts"):
+        assert_bit_equal(d[k], z[k], k)
+    assert_bit_equal(_valid(d["SX"], d["SN"], K2), _valid(z["SX"], z["SN"], K2), "SX (live slots)")
+    assert_bit_equal(_valid(d["SC"], d["SN"], K2), _valid(z["SC"], z["SN"], K2), "SC (live slots)")
+    ref = _stats(z)
+    assert st["repair_iters"] == int(ref["repair_iters"])
+    assert st["super_max_pieces"] == int(ref["super_max_pieces"])
+    for k in ("overflow_frac", "super_overflow_frac"):
+        assert abs(st[k] - ref[k]) < 1e-6, k
+    for k in ("mean_pieces", "super_mean_pieces"):
+        assert abs(st[k] - ref[k]) < 1e-5, k
+
+
+@pytest.mark.parametrize("path", V4, ids=os.path.basename)
+def test_v4_carry_inner_matches_reference(path):
+    z = np.load(path)
+    beta, theta, u_r, C, G, K, K2 = z["params"]
+    C, G, K, K2 = int(C), int(G), int(K), int(K2)
+    # carry_inner's chunk starts are the replay starts before any repair round
+    U, S, st, d = O.scan_forward_v4(z["I"], float(beta), float(theta), float(u_r), z["u0"], C=C, G=G, K=K,
+                                    K2=K2, repair=0, return_internals=True)
+    assert_bit_equal(d["Starts"], z["Starts4"], "chunk starts from carry_inner")
+
+
+@pytest.mark.parametrize("path", BWD, ids=os.path.basename)
+def test_backward_matches_reference(path):
+    z = np.load(path)
+    beta, theta, u_r, alpha, det, C = z["params"]
+    det = bool(det)
+    args = (z["I"], z["u0"], z["U"], z["S"], z["GS"], z["GU"], float(beta), float(theta), float(u_r), float(alpha),
+            det)
+    lam_serial = O.serial_backward(*args)
+    lam_scan = O.scan_backward(*args, C=int(C))
+    assert rel(lam_serial, z["Lam_fast"]) < 1e-6
+    assert rel(lam_scan, z["Lam_triton"]) < 1e-6
+    assert rel(lam_scan, z["Lam_fast"]) < 1e-6
+    # and against fp64 autograd through the reference's differentiable serial loop
+    assert rel(lam_serial, z["dI_fp64"]) < 1e-5
+    assert rel(float(beta) * lam_serial[0], z["du0_fp64"]) < 1e-5
