@@ -38,7 +38,9 @@ N_PER_GPU = 16384
 BETA = 0.99
 MU, SD = 0.05, 0.2
 FWD_BYTES = 12   # read I, write U and S (fp32) per neuron-step
-BWD_BYTES = 20   # read I, U[t-1], S, GS, write Lam per neuron-step (GU is zero, not read)
+# lif_tuned's backward reads I, U[t-1], GS and writes Lam; GU is identically
+# zero and S is recomputed bit-exactly from U and I, so neither is read.
+BWD_BYTES = 16
 METRIC = "neuron-steps/s, lif_tuned fwd+bwd (B*N=16384/GPU, T=1024)"
 UNIT = "neuron-steps/s"
 FALLBACK_HBM_GBS = 6650.0
@@ -244,9 +246,11 @@ def main():
         torch.autograd.backward(S, GS)
         return S
 
-    def timed(fn, steps, count_launches=False):
+    def timed(fn, steps, launches_per_call=None):
         """Per-step CUDA events on the launching stream, L2 flushed between
-        steps outside the events; returns (mean ms, launches)."""
+        steps outside the events; returns (mean ms, kernel launches).  For a
+        graph replay the library's launch counter does not move, so the
+        launches recorded at capture time are used."""
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         barrier()
         torch.cuda.synchronize(dev)
@@ -260,16 +264,42 @@ def main():
         n1 = lib.lifb_kernel_launches()
         barrier()
         ms = [a.elapsed_time(b) for a, b in evs]
-        return sum(ms) / len(ms), n1 - n0
+        n = (n1 - n0) if launches_per_call is None else launches_per_call * steps
+        return sum(ms) / len(ms), n
+
+    def graphed(fn):
+        """Capture fn (warmed up on a side stream) in a CUDA graph; returns
+        (replay callable, kernel launches of this library per replay)."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        n0 = lib.lifb_kernel_launches()
+        with torch.cuda.graph(g):
+            fn()
+        n1 = lib.lifb_kernel_launches()
+        torch.cuda.synchronize(dev)
+        return g.replay, n1 - n0
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
-
-    with ClockSampler(local) as clk:
-        ms_local, launches = timed(step, args.steps)
-    ms = max_over_ranks(ms_local)
     units = N * T * ws
+
+    # eager: the autograd call as a training loop issues it, host overhead included
+    ms_eager, _ = timed(step, args.steps)
+    ms_eager = max_over_ranks(ms_eager)
+    # the same step captured once in a CUDA graph and replayed (device time)
+    replay_step, per_step_launches = graphed(step)
+    for _ in range(max(args.warmup, 3)):
+        replay_step()
+    with ClockSampler(local) as clk:
+        ms_local, launches = timed(replay_step, args.steps, per_step_launches)
+    ms = max_over_ranks(ms_local)
     value = units / (ms / 1e3)
 
     # forward-only and per-call timings (roofline of the dominant call)
@@ -278,21 +308,23 @@ def main():
             L.serial_forward_auto(I, BETA, 1.0, 0.0, u0)
     U, S = fwd_call()
 
-    def bwd_call():
+    def bwd_call():  # exactly lif_tuned's backward call (S recomputed, GU zero)
         if args.mode == "scan":
-            return L.scan_backward_auto(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0)
-        return L.serial_backward_auto(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0)
+            return L.scan_backward_auto(I, u0, U, None, GS, None, BETA, 1.0, 0.0, 4.0)
+        return L.serial_backward_auto(I, u0, U, None, GS, None, BETA, 1.0, 0.0, 4.0)
     for _ in range(3):
         fwd_call()
         bwd_call()
-    ms_fwd, n_fwd = timed(fwd_call, args.steps)
-    ms_bwd, n_bwd = timed(bwd_call, args.steps)
+    rf, n_fwd = graphed(fwd_call)
+    rb, n_bwd = graphed(bwd_call)
+    ms_fwd, _ = timed(rf, args.steps, n_fwd)
+    ms_bwd, _ = timed(rb, args.steps, n_bwd)
     ms_fwd = max_over_ranks(ms_fwd)
     ms_bwd = max_over_ranks(ms_bwd)
     hbm, peak_kind = peaks()
     per_call = {
-        "fwd": {"ms": ms_fwd, "bytes": FWD_BYTES * N * T, "launches": n_fwd // max(args.steps, 1)},
-        "bwd": {"ms": ms_bwd, "bytes": BWD_BYTES * N * T, "launches": n_bwd // max(args.steps, 1)},
+        "fwd": {"ms": ms_fwd, "bytes": FWD_BYTES * N * T, "launches": n_fwd},
+        "bwd": {"ms": ms_bwd, "bytes": BWD_BYTES * N * T, "launches": n_bwd},
     }
     for v in per_call.values():
         v["gbs"] = v["bytes"] / (v["ms"] / 1e3) / 1e9
@@ -306,7 +338,7 @@ def main():
         "frac": per_call[dom]["frac"],
         "traffic": (tpu * N * T) if tpu is not None else None,
         "algorithmic_bytes": per_call[dom]["bytes"],
-        "step_frac": (32 * N * T) / (ms_local / 1e3) / 1e9 / hbm,
+        "step_frac": ((FWD_BYTES + BWD_BYTES) * N * T) / (ms_local / 1e3) / 1e9 / hbm,
     }
 
     # end to end through the public API with host buffers
@@ -349,7 +381,10 @@ def main():
             "config": {"workload": "c2: lif_tuned fwd+bwd, B*N=16384 per GPU, T=1024, beta=0.99, x~N(0.05,0.2^2)",
                        "mode": args.mode, "global_neurons": N * ws, "seq_len": T,
                        "parallelism": f"batch-sharded x{ws}, no collective",
+                       "step": "lif_tuned forward + torch.autograd.backward, captured in a CUDA graph and replayed",
                        "l2": "flushed between steps (256 MiB write outside the events)"},
+            "eager": {"ms_per_step": ms_eager, "value": units / (ms_eager / 1e3),
+                      "note": "same step issued eagerly from Python each time (host overhead included)"},
             "fwd": {"ms": ms_fwd, "value": units / (ms_fwd / 1e3), "gbs": per_call["fwd"]["gbs"],
                     "frac": per_call["fwd"]["frac"]},
             "bwd": {"ms": ms_bwd, "value": units / (ms_bwd / 1e3), "gbs": per_call["bwd"]["gbs"],

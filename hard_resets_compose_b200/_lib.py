@@ -31,6 +31,7 @@ SIGNATURES = {
     "lifb_kernel_launches": ([], ctypes.c_uint64),
     "lifb_status_string": ([c_int], ctypes.c_char_p),
     "lifb_last_error": ([], ctypes.c_char_p),
+    "lifb_device_status": ([c_int], c_int),
     "lifb_serial_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
                          c_void_p], c_int),
     "lifb_serial_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,

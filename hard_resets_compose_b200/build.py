@@ -46,28 +46,33 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
+def build(force: bool = False, verbose: bool = False, defines=(), out: str = None) -> str:
+    """Compile liblifb.so.  `defines` are extra -D flags (the build-time
+    tunables of csrc/chunk_tma.cu); `out` builds to another path instead of
+    the in-tree library."""
+    target = out or LIB
+    if out is None and not force and not _stale():
         return LIB
-    os.makedirs(LIBDIR, exist_ok=True)
-    objdir = os.path.join(LIBDIR, "obj")
+    libdir = os.path.dirname(target)
+    os.makedirs(libdir, exist_ok=True)
+    objdir = os.path.join(libdir, "obj" if out is None else "obj_" + os.path.basename(target))
     os.makedirs(objdir, exist_ok=True)
     nvcc = _nvcc()
     objs = []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-c", src, "-o", obj]
+        cmd = [nvcc, *ARCH, *NVCC_FLAGS, *[f"-D{d}" for d in defines], "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)
         objs.append(obj)
-    tmp = LIB + ".tmp"
+    tmp = target + ".tmp"
     cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, target)
+    return target
 
 
 if __name__ == "__main__":

@@ -77,10 +77,12 @@ void carve_super(Carver &c, lifb::SuperMaps &sp, int64_t M2, int64_t N, int K2)
     sp.SStarts = c.take<float>(M2 * N);
 }
 
-int check_common(const void *I, const void *u0, const void *U, const void *S, int64_t T, int64_t N)
+int check_common(const void *I, const void *u0, const void *U, const void *S, int64_t T, int64_t N,
+                 bool s_optional = false)
 {
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "negative shape T=%lld N=%lld", (long long)T, (long long)N);
-    if (T > 0 && N > 0 && (!I || !u0 || !U || !S)) return fail(LIFB_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (T > 0 && N > 0 && (!I || !u0 || !U || (!S && !s_optional)))
+        return fail(LIFB_ERR_INVALID_ARGUMENT, "null tensor pointer");
     return LIFB_OK;
 }
 
@@ -121,6 +123,8 @@ const char *lifb_status_string(int status)
 
 const char *lifb_last_error(void) { return g_last_error.c_str(); }
 
+int lifb_device_status(int reset) { return lifb::read_device_status(reset != 0); }
+
 int lifb_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                     float theta, float u_r, void *stream)
 {
@@ -135,7 +139,7 @@ int lifb_serial_bwd(const float *I, const float *u0, const float *U, const float
                     const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
                     float alpha, int detach, void *stream)
 {
-    int st = check_common(I, u0, U, S, T, N);
+    int st = check_common(I, u0, U, S, T, N, true);
     if (st) return st;
     if (T == 0 || N == 0) return LIFB_OK;
     if (!GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "null GS or Lam");
@@ -176,11 +180,18 @@ int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S, int64_
     if (T == 0 || N == 0) return LIFB_OK;
     size_t need = lifb_scan_fwd_v3_workspace_bytes(T, N, C, K);
     if ((st = check_ws(workspace, workspace_bytes, need))) return st;
+    // Without stats the last chunk's map is never evaluated: build M-1 maps.
+    // One chunk and no stats: the start is u0 and the scan is its replay alone.
+    const int64_t Mb = stats_dev ? M : M - 1;
+    if (Mb == 0) {
+        lifb::serial_fwd(I, u0, U, S, T, N, beta, theta, u_r, s);
+        return check_launch("lifb_scan_fwd_v3");
+    }
     Carver c(workspace);
     lifb::FwdMaps mp;
     carve_fwd(c, mp, M, N, K);
-    lifb::grid_envelope(I, u0, mp, T, N, C, beta, u_r, s);
-    lifb::grid_build(I, u0, mp, T, N, C, K, beta, theta, u_r, stats_dev, s);
+    lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
+    lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
     lifb::grid_carry(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r, s);
     lifb::grid_replay_repair(I, u0, mp, U, S, T, N, C, max_repair, beta, theta, u_r, stats_dev, s);
     return check_launch("lifb_scan_fwd_v3");
@@ -215,14 +226,22 @@ int lifb_scan_fwd_v4(const float *I, const float *u0, float *U, float *S, int64_
     int64_t M2 = M / G;
     size_t need = lifb_scan_fwd_v4_workspace_bytes(T, N, C, G, K, K2);
     if ((st = check_ws(workspace, workspace_bytes, need))) return st;
+    // Without stats the last chunk map and the last super map are never
+    // evaluated, so they are not built.
+    const int64_t Mb = stats_dev ? M : M - 1;
+    const int64_t M2c = stats_dev ? M2 : M2 - 1;
+    if (Mb == 0) {
+        lifb::serial_fwd(I, u0, U, S, T, N, beta, theta, u_r, s);
+        return check_launch("lifb_scan_fwd_v4");
+    }
     Carver c(workspace);
     lifb::FwdMaps mp;
     lifb::SuperMaps sp;
     carve_fwd(c, mp, M, N, K);
     carve_super(c, sp, M2, N, K2);
-    lifb::grid_envelope(I, u0, mp, T, N, C, beta, u_r, s);
-    lifb::grid_build(I, u0, mp, T, N, C, K, beta, theta, u_r, stats_dev, s);
-    lifb::grid_compose(mp, sp, u0, T, N, C, G, K, K2, theta, u_r, stats_dev, s);
+    lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
+    lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
+    if (M2c > 0) lifb::grid_compose(mp, sp, u0, M2c, N, G, K, K2, theta, u_r, stats_dev, s);
     lifb::grid_carry(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2,
                      beta, theta, u_r, s);
     lifb::grid_carry_inner(I, mp, sp.SStarts, T, N, C, G, K, beta, theta, u_r, s);
@@ -245,7 +264,7 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
                   const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
                   float alpha, int detach, int C, void *workspace, size_t workspace_bytes, void *stream)
 {
-    int st = check_common(I, u0, U, S, T, N);
+    int st = check_common(I, u0, U, S, T, N, true);
     if (st) return st;
     if (C <= 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "chunk length C=%d must be positive", C);
     if (T % C) return fail(LIFB_ERR_INVALID_ARGUMENT, "T=%lld is not a multiple of C=%d", (long long)T, C);
@@ -253,6 +272,10 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
     if (!GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "null GS or Lam");
     int64_t M = T / C;
     if (M > kMaxGridY) return fail(LIFB_ERR_UNSUPPORTED, "T/C=%lld chunks exceeds %lld", (long long)M, (long long)kMaxGridY);
+    if (M == 1) {  // one chunk: lam = 0 at its end, the scan is its replay alone
+        lifb::serial_bwd(I, u0, U, S, GS, GU, Lam, T, N, beta, theta, u_r, alpha, detach != 0, (cudaStream_t)stream);
+        return check_launch("lifb_scan_bwd");
+    }
     size_t need = lifb_scan_bwd_workspace_bytes(T, N, C);
     if ((st = check_ws(workspace, workspace_bytes, need))) return st;
     Carver c(workspace);

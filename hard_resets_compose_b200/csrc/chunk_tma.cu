@@ -1,0 +1,540 @@
+// TMA-pipelined chunk kernels: the forward replay (which is also the serial
+// forward: one chunk of T rows starting from u0) and the reverse adjoint
+// sweep (the serial backward: one chunk ending at lam = 0), both streaming
+// HBM once.
+//
+// CTA = one warp owning NB = 32*NPL consecutive neurons (NPL = 4: a float4 of
+// four independent recurrences per lane; NPL = 1: one per lane, for more
+// warps on narrow N) and one chunk m of C rows (blockIdx.y).  Time tiles of
+// R rows x NB neurons stream into a ring of S shared-memory stages with 2-D
+// TMA loads (cp.async.bulk.tensor, no multicast) completing on one mbarrier
+// per stage; lane 0 refills a stage once the warp has consumed it.  Results
+// are written into a double-buffered shared-memory tile and leave with one
+// TMA bulk-tensor store per tile, so a step costs one shared load, the
+// recurrence and one shared store per output; no per-step address math or
+// predicates on full tiles.  The ragged last tile (C % R rows) and the tile
+// holding t = 0 of the adjoint take a checked path with direct stores.
+//
+//   k_fwd_tma  replay of chunk m from Starts[m] (or u0): U, S rows and Ends[m]
+//              = fwd_tiled_kernel (lifscan/triton_lif.py:353-379); with M = 1 it is
+//              serial_forward_tiled (:460-466), bit-identical to fast.py:69-81.
+//   k_bwd_tma  reverse sweep of lam_t = a_t lam_{t+1} + b_t over chunk m with the
+//              surrogate fused (_coef :42-50):
+//                kReplay:  from LamEnd[m] (or 0), writes Lam (= bwd_tiled_kernel
+//                          :382-418; with M = 1 bwd_tiled_pf_kernel :1087-1127)
+//                kCompose: chunk map lam_start = P*lam_end + Q (= bwd_chunk_tiled_kernel :421-457)
+//              With S == NULL the spike s_t is recomputed as [v_t >= theta] from the
+//              recomputed v_t (bit-identical to the forward's S), saving 4 B/step.
+//
+// The launchers fall back (return false) unless N % 4 == 0 and every tensor
+// is 16-byte aligned (TMA stride rule and vector accesses).
+#include "lifb_common.cuh"
+#include "lifb_internal.h"
+#include "tma.cuh"
+
+namespace lifb {
+
+template <int NPL>
+struct Vec {
+    float v[NPL];
+};
+
+template <int NPL>
+__device__ __forceinline__ Vec<NPL> ld_vec(const float *p)
+{
+    Vec<NPL> r;
+    if constexpr (NPL == 4) {
+        float4 t = *reinterpret_cast<const float4 *>(p);
+        r.v[0] = t.x; r.v[1] = t.y; r.v[2] = t.z; r.v[3] = t.w;
+    } else {
+        r.v[0] = *p;
+    }
+    return r;
+}
+
+template <int NPL>
+__device__ __forceinline__ void st_vec(float *p, const Vec<NPL> &a)
+{
+    if constexpr (NPL == 4) {
+        *reinterpret_cast<float4 *>(p) = make_float4(a.v[0], a.v[1], a.v[2], a.v[3]);
+    } else {
+        *p = a.v[0];
+    }
+}
+
+// ===================================================================== forward
+template <int NPL, int R, int S>
+__global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensorMap tI,
+                                                const __grid_constant__ CUtensorMap tU,
+                                                const __grid_constant__ CUtensorMap tS, const float *__restrict__ u0,
+                                                const float *__restrict__ Starts, float *__restrict__ U,
+                                                float *__restrict__ Sout, float *__restrict__ Ends, int64_t N,
+                                                int64_t C, float beta, float theta, float u_r, int *status)
+{
+    constexpr int NB = 32 * NPL;
+    constexpr int kTile = R * NB;  // floats per tile
+    constexpr uint32_t kStageBytes = kTile * 4;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    float *ring = reinterpret_cast<float *>(smem_raw);  // S input tiles
+    float *obuf = ring + S * kTile;                      // 2 x (U tile, S tile)
+    __shared__ __align__(8) uint64_t full[S];
+    const int lane = threadIdx.x;
+    const int64_t n0 = (int64_t)blockIdx.x * NB;
+    const int64_t m = blockIdx.y;
+    const int64_t row0 = m * C;
+    const int64_t nfull = C / R;
+    const int rem = (int)(C - nfull * R);
+    const int64_t ntiles = nfull + (rem ? 1 : 0);
+
+    if (lane == 0) {
+        prefetch_tmap(&tI);
+        prefetch_tmap(&tU);
+        prefetch_tmap(&tS);
+        for (int s = 0; s < S; s++) mbar_init(&full[s], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    if (lane == 0) {
+        for (int s = 0; s < S && s < ntiles; s++) {
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)(row0 + s * R), &full[s]);
+        }
+    }
+    const int64_t nl = n0 + NPL * lane;
+    const bool act = nl < N;
+    Vec<NPL> u;
+    if (act) {
+        u = ld_vec<NPL>((Starts ? Starts + m * N : u0) + nl);
+    } else {
+#pragma unroll
+        for (int i = 0; i < NPL; i++) u.v[i] = 0.f;
+    }
+    bool ok = true;
+
+    for (int64_t k = 0; k < nfull; k++) {
+        const int s = (int)(k % S);
+        if (!mbar_wait(&full[s], (uint32_t)((k / S) & 1))) { ok = false; break; }
+        const float *in = ring + s * kTile + NPL * lane;
+        Vec<NPL> x[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) x[r] = ld_vec<NPL>(in + r * NB);
+        float *ou = obuf + (int)(k & 1) * 2 * kTile;
+        float *os = ou + kTile;
+        if (k >= 2) {  // the store issued two tiles ago must have read this buffer
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            Vec<NPL> sp;
+#pragma unroll
+            for (int i = 0; i < NPL; i++) {
+                bool f;
+                u.v[i] = lif_step(u.v[i], x[r].v[i], beta, theta, u_r, f);
+                sp.v[i] = f ? 1.0f : 0.0f;
+            }
+            st_vec<NPL>(ou + r * NB + NPL * lane, u);
+            st_vec<NPL>(os + r * NB + NPL * lane, sp);
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(&tU, (int)n0, (int)(row0 + k * R), ou);
+            tma_store_2d(&tS, (int)n0, (int)(row0 + k * R), os);
+            bulk_commit();
+            if (k + S < ntiles) {
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)(row0 + (k + S) * R), &full[s]);
+            }
+        }
+    }
+    if (ok && rem) {  // ragged last tile: checked rows, direct stores
+        const int64_t k = nfull;
+        const int s = (int)(k % S);
+        if (!mbar_wait(&full[s], (uint32_t)((k / S) & 1))) {
+            ok = false;
+        } else {
+            const float *in = ring + s * kTile + NPL * lane;
+            for (int r = 0; r < rem; r++) {
+                const Vec<NPL> x = ld_vec<NPL>(in + r * NB);
+                Vec<NPL> sp;
+#pragma unroll
+                for (int i = 0; i < NPL; i++) {
+                    bool f;
+                    u.v[i] = lif_step(u.v[i], x.v[i], beta, theta, u_r, f);
+                    sp.v[i] = f ? 1.0f : 0.0f;
+                }
+                if (act) {
+                    const int64_t o = (row0 + k * R + r) * N + nl;
+                    st_vec<NPL>(U + o, u);
+                    st_vec<NPL>(Sout + o, sp);
+                }
+            }
+        }
+    }
+    if (!ok && status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
+    if (ok && Ends && act) st_vec<NPL>(Ends + m * N + nl, u);
+    if (lane == 0) bulk_wait_all();
+}
+
+// ==================================================================== backward
+enum BwdMode { kReplay = 0, kCompose = 1 };
+
+// Input tensors per stage, in ring order: I, U (one row earlier), [S], GS, [GU].
+template <bool READ_S, bool HAS_GU>
+struct BwdLayout {
+    static constexpr int kI = 0, kU = 1, kS = 2;
+    static constexpr int kGS = READ_S ? 3 : 2;
+    static constexpr int kGU = kGS + 1;
+    static constexpr int NT = 3 + (READ_S ? 1 : 0) + (HAS_GU ? 1 : 0);
+};
+
+// Adjoint coefficients lam_t = a*lam_{t+1} + c of NPL neurons at in-tile
+// offset `off` (no dependence on lam, so a whole tile is computed ahead).
+template <int NPL, bool READ_S, bool HAS_GU>
+__device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec<NPL> &a, Vec<NPL> &c, float beta,
+                                         float theta, float u_r, float alpha, bool detach)
+{
+    using Ly = BwdLayout<READ_S, HAS_GU>;
+    const Vec<NPL> x = ld_vec<NPL>(b + Ly::kI * kTile + off);
+    const Vec<NPL> up = ld_vec<NPL>(b + Ly::kU * kTile + off);
+    const Vec<NPL> gs = ld_vec<NPL>(b + Ly::kGS * kTile + off);
+    Vec<NPL> sv, gu;
+    if constexpr (READ_S) sv = ld_vec<NPL>(b + Ly::kS * kTile + off);
+    if constexpr (HAS_GU) gu = ld_vec<NPL>(b + Ly::kGU * kTile + off);
+#pragma unroll
+    for (int i = 0; i < NPL; i++) {
+        const float v = __fadd_rn(__fmul_rn(beta, up.v[i]), x.v[i]);  // the forward's v, bit for bit
+        float s;
+        if constexpr (READ_S) s = sv.v[i];
+        else s = v >= theta ? 1.0f : 0.0f;
+        const float e = __expf(-alpha * (v - theta));
+        const float sig = rcp_approx(1.0f + e);
+        const float sg = alpha * sig * (1.0f - sig);
+        float J = 1.0f - s;
+        if (!detach) J = J + (u_r - v) * sg;
+        a.v[i] = beta * J;
+        float cc = gs.v[i] * sg;
+        if constexpr (HAS_GU) cc = cc + J * gu.v[i];
+        c.v[i] = cc;
+    }
+}
+
+// One reverse step for NPL neurons at in-tile offset `off`.
+template <int NPL, bool READ_S, bool HAS_GU, int MODE>
+__device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, const Vec<NPL> *up_override,
+                                         Vec<NPL> &lam, Vec<NPL> &pp, float beta, float theta, float u_r,
+                                         float alpha, bool detach)
+{
+    using Ly = BwdLayout<READ_S, HAS_GU>;
+    const Vec<NPL> x = ld_vec<NPL>(b + Ly::kI * kTile + off);
+    const Vec<NPL> up = up_override ? *up_override : ld_vec<NPL>(b + Ly::kU * kTile + off);
+    const Vec<NPL> gs = ld_vec<NPL>(b + Ly::kGS * kTile + off);
+    Vec<NPL> sv, gu;
+    if constexpr (READ_S) sv = ld_vec<NPL>(b + Ly::kS * kTile + off);
+    if constexpr (HAS_GU) gu = ld_vec<NPL>(b + Ly::kGU * kTile + off);
+#pragma unroll
+    for (int i = 0; i < NPL; i++) {
+        const float v = __fadd_rn(__fmul_rn(beta, up.v[i]), x.v[i]);  // the forward's v, bit for bit
+        float s;
+        if constexpr (READ_S) s = sv.v[i];
+        else s = v >= theta ? 1.0f : 0.0f;
+        const float e = __expf(-alpha * (v - theta));
+        const float sig = rcp_approx(1.0f + e);
+        const float sg = alpha * sig * (1.0f - sig);
+        float J = 1.0f - s;
+        if (!detach) J = J + (u_r - v) * sg;
+        const float a = beta * J;
+        float c = gs.v[i] * sg;
+        if constexpr (HAS_GU) c = c + J * gu.v[i];
+        lam.v[i] = c + a * lam.v[i];
+        if (MODE == kCompose) pp.v[i] = a * pp.v[i];
+    }
+}
+
+template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE>
+__global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensorMap tI,
+                                                const __grid_constant__ CUtensorMap tU,
+                                                const __grid_constant__ CUtensorMap tS,
+                                                const __grid_constant__ CUtensorMap tGS,
+                                                const __grid_constant__ CUtensorMap tGU,
+                                                const __grid_constant__ CUtensorMap tLam,
+                                                const float *__restrict__ u0, const float *__restrict__ LamEnd,
+                                                float *__restrict__ Lam, float *__restrict__ P, float *__restrict__ Q,
+                                                int64_t N, int64_t C, float beta, float theta, float u_r, float alpha,
+                                                bool detach, int *status)
+{
+    using Ly = BwdLayout<READ_S, HAS_GU>;
+    constexpr int NB = 32 * NPL;
+    constexpr int NT = Ly::NT;
+    constexpr int kTile = R * NB;
+    constexpr uint32_t kStageBytes = NT * kTile * 4;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    float *ring = reinterpret_cast<float *>(smem_raw);
+    float *obuf = ring + (size_t)S * NT * kTile;  // 2 Lam tiles (kReplay)
+    __shared__ __align__(8) uint64_t full[S];
+    const int lane = threadIdx.x;
+    const int64_t n0 = (int64_t)blockIdx.x * NB;
+    const int64_t m = blockIdx.y;
+    const int64_t cstart = m * C, cend = (m + 1) * C;
+    const int64_t nfull = C / R;
+    const int rem = (int)(C - nfull * R);
+    const int64_t ntiles = nfull + (rem ? 1 : 0);
+
+    auto issue = [&](int s, int64_t k) {
+        const int row = (int)(cend - (k + 1) * R);  // may be negative: zero-filled
+        float *b = ring + (size_t)s * NT * kTile;
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        tma_load_2d(b + Ly::kI * kTile, &tI, (int)n0, row, &full[s]);
+        tma_load_2d(b + Ly::kU * kTile, &tU, (int)n0, row - 1, &full[s]);
+        if (READ_S) tma_load_2d(b + Ly::kS * kTile, &tS, (int)n0, row, &full[s]);
+        tma_load_2d(b + Ly::kGS * kTile, &tGS, (int)n0, row, &full[s]);
+        if (HAS_GU) tma_load_2d(b + Ly::kGU * kTile, &tGU, (int)n0, row, &full[s]);
+    };
+
+    if (lane == 0) {
+        prefetch_tmap(&tI);
+        prefetch_tmap(&tU);
+        prefetch_tmap(&tGS);
+        if (READ_S) prefetch_tmap(&tS);
+        if (HAS_GU) prefetch_tmap(&tGU);
+        if (MODE == kReplay) prefetch_tmap(&tLam);
+        for (int s = 0; s < S; s++) mbar_init(&full[s], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    if (lane == 0)
+        for (int s = 0; s < S && s < ntiles; s++) issue(s, s);
+
+    const int64_t nl = n0 + NPL * lane;
+    const bool act = nl < N;
+    Vec<NPL> uz, lam, pp;
+#pragma unroll
+    for (int i = 0; i < NPL; i++) { uz.v[i] = 0.f; lam.v[i] = 0.f; pp.v[i] = 1.f; }
+    if (act) {
+        uz = ld_vec<NPL>(u0 + nl);
+        if (MODE == kReplay && LamEnd) lam = ld_vec<NPL>(LamEnd + m * N + nl);
+    }
+    bool ok = true;
+
+    for (int64_t k = 0; k < ntiles; k++) {
+        const int s = (int)(k % S);
+        if (!mbar_wait(&full[s], (uint32_t)((k / S) & 1))) { ok = false; break; }
+        const float *b = ring + (size_t)s * NT * kTile;
+        const int64_t rbase = cend - (k + 1) * R;  // global row of in-tile row 0
+        const bool fast = k < nfull && rbase > 0;  // full tile, no row 0 inside
+        if (fast) {
+            float *ol = obuf + (int)(k & 1) * kTile;
+            Vec<NPL> av[R], cv[R];
+#pragma unroll
+            for (int rr = 0; rr < R; rr++)
+                bwd_coef<NPL, READ_S, HAS_GU>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta, theta, u_r, alpha,
+                                              detach);
+            if (MODE == kReplay && k >= 2) {
+                if (lane == 0) bulk_wait_read<1>();
+                __syncwarp();
+            }
+#pragma unroll
+            for (int rr = R - 1; rr >= 0; rr--) {
+#pragma unroll
+                for (int i = 0; i < NPL; i++) {
+                    lam.v[i] = cv[rr].v[i] + av[rr].v[i] * lam.v[i];
+                    if (MODE == kCompose) pp.v[i] = av[rr].v[i] * pp.v[i];
+                }
+                if (MODE == kReplay) st_vec<NPL>(ol + rr * NB + NPL * lane, lam);
+            }
+            if (MODE == kReplay) {
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tLam, (int)n0, (int)rbase, ol);
+                    bulk_commit();
+                }
+            }
+        } else {  // ragged tile or the tile holding t = 0: checked rows, direct stores
+            for (int rr = R - 1; rr >= 0; rr--) {
+                const int64_t t = rbase + rr;
+                if (t < cstart) break;
+                bwd_step<NPL, READ_S, HAS_GU, MODE>(b, kTile, rr * NB + NPL * lane, t == 0 ? &uz : nullptr, lam, pp,
+                                                    beta, theta, u_r, alpha, detach);
+                if (MODE == kReplay && act) st_vec<NPL>(Lam + t * N + nl, lam);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && k + S < ntiles) issue(s, k + S);
+    }
+    if (!ok && status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
+    if (ok && MODE == kCompose && act) {
+        st_vec<NPL>(P + m * N + nl, pp);
+        st_vec<NPL>(Q + m * N + nl, lam);
+    }
+    if (MODE == kReplay && lane == 0) bulk_wait_all();
+}
+
+// ================================================================= host side
+// Tile rows R and ring depth S per lane width (build-time tunables, chosen by
+// a sweep on B200: longer tiles amortise the per-tile barrier/TMA work for
+// one-neuron lanes; float4 lanes move 4x the bytes per tile already).
+#ifndef LIFB_FWD1_R
+#define LIFB_FWD1_R 32
+#endif
+#ifndef LIFB_FWD1_S
+#define LIFB_FWD1_S 4
+#endif
+#ifndef LIFB_FWD4_R
+#define LIFB_FWD4_R 16
+#endif
+#ifndef LIFB_FWD4_S
+#define LIFB_FWD4_S 6
+#endif
+#ifndef LIFB_BWD1_R
+#define LIFB_BWD1_R 16
+#endif
+#ifndef LIFB_BWD1_S
+#define LIFB_BWD1_S 4
+#endif
+#ifndef LIFB_BWD4_R
+#define LIFB_BWD4_R 8
+#endif
+#ifndef LIFB_BWD4_S
+#define LIFB_BWD4_S 6
+#endif
+// float4 lanes once there are at least this many 128-neuron CTAs per SM
+#ifndef LIFB_FWD_NPL4_MIN_CTAS_PER_SM
+#define LIFB_FWD_NPL4_MIN_CTAS_PER_SM 2
+#endif
+#ifndef LIFB_BWD_NPL4_MIN_CTAS_PER_SM
+#define LIFB_BWD_NPL4_MIN_CTAS_PER_SM 1000000
+#endif
+#ifndef LIFB_FORCE_NPL
+#define LIFB_FORCE_NPL 0
+#endif
+template <int NPL>
+struct FwdTile {
+    static constexpr int R = NPL == 4 ? LIFB_FWD4_R : LIFB_FWD1_R;
+    static constexpr int S = NPL == 4 ? LIFB_FWD4_S : LIFB_FWD1_S;
+};
+template <int NPL>
+struct BwdTile {
+    static constexpr int R = NPL == 4 ? LIFB_BWD4_R : LIFB_BWD1_R;
+    static constexpr int S = NPL == 4 ? LIFB_BWD4_S : LIFB_BWD1_S;
+};
+
+static bool tma_ok(const void *const *ptrs, int n, int64_t N)
+{
+    if (N % 4) return false;
+    for (int i = 0; i < n; i++)
+        if (ptrs[i] && ((uintptr_t)ptrs[i] & 15)) return false;
+    return true;
+}
+
+// float4 lanes when there are enough 128-neuron CTAs per SM; otherwise one
+// neuron per lane (4x more warps for narrow problems).
+static int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
+{
+    if (LIFB_FORCE_NPL == 1 || LIFB_FORCE_NPL == 4) return LIFB_FORCE_NPL;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return ((N + 127) / 128) * M >= (int64_t)min_ctas_per_sm * sms ? 4 : 1;
+}
+
+template <int NPL>
+static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, float *U, float *S, float *Ends,
+                       int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, int *status,
+                       cudaStream_t s)
+{
+    constexpr int NB = 32 * NPL;
+    constexpr int R = FwdTile<NPL>::R, ST = FwdTile<NPL>::S;
+    const size_t smem = (size_t)(ST + 4) * R * NB * 4;
+    auto kern = k_fwd_tma<NPL, R, ST>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
+    count_launches(1);
+    kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], u0, Starts, U, S, Ends, N, C, beta, theta, u_r, status);
+}
+
+bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
+                    int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s)
+{
+    const void *p[] = {I, u0, Starts, U, S, Ends};
+    if (!tma_ok(p, 6, N) || C <= 0 || T % C) return false;
+    const int64_t M = T / C;
+    if (M > 65535) return false;
+    const int npl = pick_npl(N, M, LIFB_FWD_NPL4_MIN_CTAS_PER_SM);
+    const int R = npl == 4 ? FwdTile<4>::R : FwdTile<1>::R;
+    CUtensorMap maps[3];
+    if (!make_tmap_2d(&maps[0], I, N, T, 32 * npl, R) || !make_tmap_2d(&maps[1], U, N, T, 32 * npl, R) ||
+        !make_tmap_2d(&maps[2], S, N, T, 32 * npl, R))
+        return false;
+    int *status = device_status_ptr();
+    if (npl == 4) launch_fwd<4>(maps, u0, Starts, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
+    else launch_fwd<1>(maps, u0, Starts, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
+    return true;
+}
+
+template <int NPL, bool READ_S, bool HAS_GU, int MODE>
+static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *LamEnd, float *Lam, float *P, float *Q,
+                       int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
+                       bool detach, int *status, cudaStream_t s)
+{
+    constexpr int NB = 32 * NPL;
+    constexpr int NT = BwdLayout<READ_S, HAS_GU>::NT;
+    constexpr int R = BwdTile<NPL>::R, ST = BwdTile<NPL>::S;
+    const size_t smem = ((size_t)ST * NT + (MODE == kReplay ? 2 : 0)) * R * NB * 4;
+    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
+    count_launches(1);
+    kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], u0, LamEnd, Lam, P, Q, N, C, beta,
+                             theta, u_r, alpha, detach, status);
+}
+
+template <int NPL, int MODE>
+static void launch_bwd_v(bool read_s, bool has_gu, const CUtensorMap *maps, const float *u0, const float *LamEnd,
+                         float *Lam, float *P, float *Q, int64_t N, int64_t M, int64_t C, float beta, float theta,
+                         float u_r, float alpha, bool detach, int *status, cudaStream_t s)
+{
+    if (read_s) {
+        if (has_gu) launch_bwd<NPL, true, true, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd<NPL, true, false, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+    } else {
+        if (has_gu) launch_bwd<NPL, false, true, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd<NPL, false, false, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+    }
+}
+
+bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const float *S, const float *GS,
+             const float *GU, const float *LamEnd, float *Lam, float *P, float *Q, int64_t T, int64_t N, int64_t C,
+             float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s)
+{
+    const void *p[] = {I, u0, U, S, GS, GU, LamEnd, Lam, P, Q};
+    if (!tma_ok(p, 10, N) || C <= 0 || T % C) return false;
+    const int64_t M = T / C;
+    if (M > 65535) return false;
+    const int npl = pick_npl(N, M, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
+    const int nb = 32 * npl;
+    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    // maps: I, U, S, GS, GU, Lam (unused slots repeat a valid map)
+    CUtensorMap maps[6];
+    if (!make_tmap_2d(&maps[0], I, N, T, nb, R) || !make_tmap_2d(&maps[1], U, N, T, nb, R) ||
+        !make_tmap_2d(&maps[3], GS, N, T, nb, R))
+        return false;
+    maps[2] = maps[0];
+    maps[4] = maps[0];
+    maps[5] = maps[0];
+    if (S && !make_tmap_2d(&maps[2], S, N, T, nb, R)) return false;
+    if (GU && !make_tmap_2d(&maps[4], GU, N, T, nb, R)) return false;
+    if (mode == kReplay && !make_tmap_2d(&maps[5], Lam, N, T, nb, R)) return false;
+    int *status = device_status_ptr();
+    const bool rs = S != nullptr, g = GU != nullptr;
+    if (mode == kReplay) {
+        if (npl == 4) launch_bwd_v<4, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd_v<1, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+    } else {
+        if (npl == 4) launch_bwd_v<4, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd_v<1, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+    }
+    return true;
+}
+
+}  // namespace lifb

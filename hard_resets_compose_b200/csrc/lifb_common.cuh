@@ -40,10 +40,13 @@ LIFB_DEV float mul_add_rn(float a, float b, float c) { return __fadd_rn(__fmul_r
 // sigma' = alpha*sig*(1-sig), sig = 1/(1+exp(-alpha*(v-theta))), J = 1-s
 // (+ (u_r - v)*sigma' when the reset is not detached).  v is recomputed from
 // the saved previous state with the forward's exact rounding.
+// s < 0 means "not stored": s = [v >= theta] is recomputed from v, which is
+// bit-identical to the forward's spike.
 LIFB_DEV void lif_coef(float up, float s, float x, float gs, float gu, float beta, float theta,
                        float u_r, float alpha, bool detach, float &a, float &b)
 {
     float v = __fadd_rn(__fmul_rn(beta, up), x);
+    if (s < 0.0f) s = v >= theta ? 1.0f : 0.0f;
     float e = __expf(-alpha * (v - theta));
     float sig = __frcp_rn(1.0f + e);
     float sg = alpha * sig * (1.0f - sig);

@@ -1,6 +1,7 @@
 // Internal declarations shared by the CUDA translation units of liblifb.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -24,6 +25,22 @@ struct SuperMaps {
     int32_t *SN, *SOVF;
 };
 
+// runtime.cu
+bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_x, int box_y);
+int *device_status_ptr();                 // status word of the current device
+int read_device_status(bool reset);       // synchronous read (current device)
+
+// chunk_tma.cu: TMA-pipelined chunk kernels; false when the TMA path does not
+// apply (N % 4 != 0, a misaligned tensor, more than 65535 chunks).
+// Forward replay of M = T/C chunks from Starts (NULL: one chunk from u0).
+bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
+                    int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s);
+// Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0),
+// mode 1 writes the chunk maps P, Q.
+bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const float *S, const float *GS,
+             const float *GU, const float *LamEnd, float *Lam, float *P, float *Q, int64_t T, int64_t N, int64_t C,
+             float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s);
+
 // serial.cu
 void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                 float theta, float u_r, cudaStream_t s);
@@ -32,14 +49,16 @@ void serial_bwd(const float *I, const float *u0, const float *U, const float *S,
                 float alpha, bool detach, cudaStream_t s);
 
 // scan_fwd_grid.cu
-void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t T, int64_t N, int C, float beta,
+// grid_envelope / grid_build / grid_compose work on the first M chunks (M2
+// supers) only; the last chunk's map is needed only for the stats.
+void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, float beta,
                    float u_r, cudaStream_t s);
-void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t T, int64_t N, int C, int K, float beta,
+void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, int K, float beta,
                 float theta, float u_r, lifb_stats *st, cudaStream_t s);
 void grid_carry(const float *I, const float *u0, const float *MA, const float *MB, const float *MX,
                 const float *MC, const int32_t *MN, const int32_t *OVF, float *Starts, int64_t N, int64_t M,
                 int64_t L, int K, float beta, float theta, float u_r, cudaStream_t s);
-void grid_compose(const FwdMaps &mp, const SuperMaps &sp, const float *u0, int64_t T, int64_t N, int C, int G,
+void grid_compose(const FwdMaps &mp, const SuperMaps &sp, const float *u0, int64_t M2, int64_t N, int G,
                   int K, int K2, float theta, float u_r, lifb_stats *st, cudaStream_t s);
 void grid_carry_inner(const float *I, const FwdMaps &mp, const float *SStarts, int64_t T, int64_t N, int C, int G,
                       int K, float beta, float theta, float u_r, cudaStream_t s);

@@ -1,0 +1,75 @@
+// Host runtime pieces shared by the kernels: TMA tensor-map encoding through
+// the driver entry point (no link-time libcuda dependency) and the per-device
+// status word that bounded device-side waits write into.
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "lifb_internal.h"
+
+namespace lifb {
+
+// One status word per device: 0 = ok, else the first device-side error code
+// (a bounded wait that expired).  Kernels receive its address as a parameter.
+__device__ int g_status_word = 0;
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+constexpr int kMaxDevices = 64;
+int *g_status_ptr[kMaxDevices] = {};
+std::mutex g_status_mu;
+}  // namespace
+
+static PFN_cuTensorMapEncodeTiled_v12000 encoder()
+{
+    std::call_once(g_encode_once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    });
+    return g_encode;
+}
+
+bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_x, int box_y)
+{
+    auto enc = encoder();
+    if (!enc || ((uintptr_t)base & 15) || (N * 4) % 16 || T >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
+        return false;
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)N * 4};
+    cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+int *device_status_ptr()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> g(g_status_mu);
+    if (!g_status_ptr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+        g_status_ptr[dev] = (int *)p;
+    }
+    return g_status_ptr[dev];
+}
+
+int read_device_status(bool reset)
+{
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_status_word, sizeof(int)) != cudaSuccess) return -1;
+    if (reset && v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_status_word, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace lifb

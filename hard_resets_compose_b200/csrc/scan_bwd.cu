@@ -21,7 +21,8 @@ __device__ __forceinline__ void coef_at(const float *__restrict__ I, const float
     int64_t o = t * N + n;
     float up = t > 0 ? __ldg(U + o - N) : __ldg(u0 + n);
     float gu = GU ? __ldg(GU + o) : 0.0f;
-    lif_coef(up, __ldg(S + o), __ldg(I + o), __ldg(GS + o), gu, beta, theta, u_r, alpha, detach, a, b);
+    float sv = S ? __ldg(S + o) : -1.0f;  // -1: recompute from v
+    lif_coef(up, sv, __ldg(I + o), __ldg(GS + o), gu, beta, theta, u_r, alpha, detach, a, b);
 }
 
 __global__ void __launch_bounds__(kBwBlock) k_bwd_chunk(const float *__restrict__ I, const float *__restrict__ u0,
@@ -88,12 +89,19 @@ void grid_scan_bwd(const float *I, const float *u0, const float *U, const float 
 {
     int64_t M = T / C;
     unsigned nb = (unsigned)((N + kBwBlock - 1) / kBwBlock);
-    count_launches(3);
-    k_bwd_chunk<<<dim3(nb, (unsigned)M), kBwBlock, 0, s>>>(I, u0, U, S, GS, GU, w.P, w.Q, N, C, beta, theta, u_r,
-                                                            alpha, detach);
+    if (!bwd_tma(1, I, u0, U, S, GS, GU, nullptr, nullptr, w.P, w.Q, T, N, C, beta, theta, u_r, alpha, detach, s)) {
+        count_launches(1);
+        k_bwd_chunk<<<dim3(nb, (unsigned)M), kBwBlock, 0, s>>>(I, u0, U, S, GS, GU, w.P, w.Q, N, C, beta, theta,
+                                                                u_r, alpha, detach);
+    }
+    count_launches(1);
     k_bwd_carry<<<nb, kBwBlock, 0, s>>>(w.P, w.Q, w.LamEnd, N, M);
-    k_bwd_replay<<<dim3(nb, (unsigned)M), kBwBlock, 0, s>>>(I, u0, U, S, GS, GU, w.LamEnd, Lam, N, C, beta, theta,
-                                                             u_r, alpha, detach);
+    if (!bwd_tma(0, I, u0, U, S, GS, GU, w.LamEnd, Lam, nullptr, nullptr, T, N, C, beta, theta, u_r, alpha, detach,
+                 s)) {
+        count_launches(1);
+        k_bwd_replay<<<dim3(nb, (unsigned)M), kBwBlock, 0, s>>>(I, u0, U, S, GS, GU, w.LamEnd, Lam, N, C, beta,
+                                                                 theta, u_r, alpha, detach);
+    }
 }
 
 }  // namespace lifb

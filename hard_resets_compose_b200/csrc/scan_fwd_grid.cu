@@ -176,6 +176,7 @@ __global__ void __launch_bounds__(kBlock) k_carry(const float *__restrict__ I, c
     for (int64_t m = 0; m < M; m++) {
         int64_t o = m * N + n;
         Starts[o] = u;
+        if (m + 1 == M) break;  // the last map's value is never used
         float nu;
         if (OVF[o]) {
             float w = u;
@@ -283,8 +284,8 @@ __global__ void __launch_bounds__(kBlock) k_carry_inner(const float *__restrict_
                                                         const float *__restrict__ MX, const float *__restrict__ MC,
                                                         const int32_t *__restrict__ MN,
                                                         const int32_t *__restrict__ OVF, float *__restrict__ Starts,
-                                                        int64_t N, int G, int C, int K, float beta, float theta,
-                                                        float u_r)
+                                                        int64_t N, int64_t Mtot, int G, int C, int K, float beta,
+                                                        float theta, float u_r)
 {
     int64_t n = (int64_t)blockIdx.x * kBlock + threadIdx.x;
     if (n >= N) return;
@@ -294,6 +295,7 @@ __global__ void __launch_bounds__(kBlock) k_carry_inner(const float *__restrict_
         int64_t m = s * G + jj;
         int64_t o = m * N + n;
         Starts[o] = u;
+        if (m + 1 >= Mtot) break;  // the last chunk's map is never used
         float nu;
         if (OVF[o]) {
             float w = u;
@@ -388,10 +390,9 @@ static void launch_compose(dim3 g, cudaStream_t s, const FwdMaps &mp, const Supe
 
 static inline unsigned nblk(int64_t N) { return (unsigned)((N + kBlock - 1) / kBlock); }
 
-void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t T, int64_t N, int C, float beta,
+void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, float beta,
                    float u_r, cudaStream_t s)
 {
-    int64_t M = T / C;
     // EC/EA/EB live in the Starts/Ends/MB slots, which are written later.
     float *EC = mp.Starts, *EA = mp.Ends, *EB = mp.MB;
     count_launches(2);
@@ -399,10 +400,9 @@ void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t T, int6
     k_env_carry<<<nblk(N), kBlock, 0, s>>>(u0, EC, EA, EB, mp.Lo, N, M, 1e-5f);
 }
 
-void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t T, int64_t N, int C, int K, float beta,
+void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, int K, float beta,
                 float theta, float u_r, lifb_stats *st, cudaStream_t s)
 {
-    int64_t M = T / C;
     dim3 g(nblk(N), (unsigned)M);
     int km = K <= 2 ? 2 : K <= 4 ? 4 : K <= 8 ? 8 : K <= 16 ? 16 : K <= 32 ? 32 : 64;
     switch (km) {
@@ -423,10 +423,9 @@ void grid_carry(const float *I, const float *u0, const float *MA, const float *M
     k_carry<<<nblk(N), kBlock, 0, s>>>(I, u0, MA, MB, MX, MC, MN, OVF, Starts, N, M, L, K, beta, theta, u_r);
 }
 
-void grid_compose(const FwdMaps &mp, const SuperMaps &sp, const float *u0, int64_t T, int64_t N, int C, int G,
+void grid_compose(const FwdMaps &mp, const SuperMaps &sp, const float *u0, int64_t M2, int64_t N, int G,
                   int K, int K2, float theta, float u_r, lifb_stats *st, cudaStream_t s)
 {
-    int64_t M2 = T / C / G;
     dim3 g(nblk(N), (unsigned)M2);
     int km = K2 <= 2 ? 2 : K2 <= 4 ? 4 : K2 <= 8 ? 8 : K2 <= 16 ? 16 : K2 <= 32 ? 32 : 64;
     switch (km) {
@@ -445,7 +444,8 @@ void grid_carry_inner(const float *I, const FwdMaps &mp, const float *SStarts, i
     int64_t M2 = T / C / G;
     count_launches(1);
     k_carry_inner<<<dim3(nblk(N), (unsigned)M2), kBlock, 0, s>>>(I, SStarts, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN,
-                                                                mp.OVF, mp.Starts, N, G, C, K, beta, theta, u_r);
+                                                                mp.OVF, mp.Starts, N, T / C, G, C, K, beta, theta,
+                                                                u_r);
 }
 
 void grid_replay_repair(const float *I, const float *u0, FwdMaps &mp, float *U, float *S, int64_t T, int64_t N,
@@ -453,8 +453,10 @@ void grid_replay_repair(const float *I, const float *u0, FwdMaps &mp, float *U, 
                         cudaStream_t s)
 {
     int64_t M = T / C;
-    count_launches(1);
-    k_replay<<<dim3(nblk(N), (unsigned)M), kBlock, 0, s>>>(I, mp.Starts, U, S, mp.Ends, N, C, beta, theta, u_r);
+    if (!fwd_replay_tma(I, u0, mp.Starts, U, S, mp.Ends, T, N, C, beta, theta, u_r, s)) {
+        count_launches(1);
+        k_replay<<<dim3(nblk(N), (unsigned)M), kBlock, 0, s>>>(I, mp.Starts, U, S, mp.Ends, N, C, beta, theta, u_r);
+    }
     int rounds = max_repair < 0 ? (int)(M + 1) : max_repair;
     if (rounds > 0) {
         count_launches(1);

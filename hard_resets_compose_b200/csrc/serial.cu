@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_bwd(const float *__restric
                 int64_t t = t0 + d;
                 int64_t o = t * N + n;
                 x[d] = __ldg(I + o);
-                s[d] = __ldg(S + o);
+                s[d] = S ? __ldg(S + o) : -1.0f;
                 gs[d] = __ldg(GS + o);
                 gu[d] = GU ? __ldg(GU + o) : 0.0f;
                 up[d] = t > 0 ? __ldg(U + o - N) : un0;
@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_bwd(const float *__restric
 void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                 float theta, float u_r, cudaStream_t s)
 {
+    if (fwd_replay_tma(I, u0, nullptr, U, S, nullptr, T, N, T, beta, theta, u_r, s)) return;
     unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
     count_launches(1);
     k_serial_fwd<kSerD><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, u_r);
@@ -108,6 +109,8 @@ void serial_bwd(const float *I, const float *u0, const float *U, const float *S,
                 const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
                 float alpha, bool detach, cudaStream_t s)
 {
+    if (bwd_tma(0, I, u0, U, S, GS, GU, nullptr, Lam, nullptr, nullptr, T, N, T, beta, theta, u_r, alpha, detach, s))
+        return;
     unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
     count_launches(1);
     k_serial_bwd<8><<<g, kSerBlock, 0, s>>>(I, u0, U, S, GS, GU, Lam, T, N, beta, theta, u_r, alpha, detach);

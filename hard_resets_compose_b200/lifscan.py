@@ -33,7 +33,7 @@ __all__ = [
     "scan_forward_v4", "scan_backward_tiled", "scan_forward_auto", "scan_backward_auto",
     "state_bounds", "surrogate_grad", "_pick_C", "LIFTuned", "lif_tuned", "LIFFunction", "lif",
     "AUTO_FWD_MAX_N", "AUTO_FWD_MIN_T", "AUTO_BWD_MAX_N", "AUTO_BWD_MIN_T", "auto_modes",
-    "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg",
+    "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg", "scan_chunk_fwd", "scan_chunk_bwd",
 ]
 
 _CONVERGE = -1  # max_repair value meaning "repair until converged"
@@ -66,7 +66,7 @@ def _prep_fwd(I, u0):
 def _prep_bwd(I, u0, U, S, GS, GU):
     I, u0, T, N = _prep_fwd(I, u0)
     U = _cuda_f32("U", U, (T, N))
-    S = _cuda_f32("S", S, (T, N))
+    S = None if S is None else _cuda_f32("S", S, (T, N))
     GS = _cuda_f32("GS", GS, (T, N))
     GU = None if GU is None else _cuda_f32("GU", GU, (T, N))
     return I, u0, U, S, GS, GU, T, N
@@ -91,7 +91,9 @@ def serial_forward(I, beta, theta, u_r, u0, BN=None):
 
 def serial_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True, BN=None):
     """Serial adjoint (lifscan/triton_lif.py:254-259) -> Lam = dL/dv = dL/dI.
-    GU may be None (zeros)."""
+    GU may be None (zeros).  S may be None when it is the forward's own
+    output: the spikes are then recomputed bit-exactly from U and I instead
+    of being read."""
     I, u0, U, S, GS, GU, T, N = _prep_bwd(I, u0, U, S, GS, GU)
     Lam = torch.empty_like(I)
     L = _lib.load()
@@ -233,17 +235,40 @@ def _pick_C(T, D=8):
     raise ValueError(f"T={T} needs a chunk length divisible by {D}")
 
 
+# Widths at which one recurrence per lane already keeps HBM busy on B200: the
+# serial chain costs ~18 SM cycles per step (forward) and ~6 (adjoint), so a
+# single pass is HBM-bound once N*12 B (forward) or N*20 B (adjoint) per step
+# outlasts that chain at the measured copy bandwidth.  Below these widths the
+# time-parallel scan is used with the reference's chunk length.
+SCAN_FWD_SERIAL_MIN_N = 6144
+SCAN_BWD_SERIAL_MIN_N = 2048
+
+
+def scan_chunk_fwd(T, N):
+    """Chunk length of lif_tuned's scan forward on B200: the whole sequence (one
+    chunk, i.e. the replay pass alone) when N is wide enough to saturate HBM,
+    else the reference's _pick_C(T, 16) (lifscan/triton_lif.py:1230)."""
+    return T if N >= SCAN_FWD_SERIAL_MIN_N else _pick_C(T, D=16)
+
+
+def scan_chunk_bwd(T, N):
+    """Chunk length of lif_tuned's scan backward on B200 (reference:
+    min(128, _pick_C(T, 2)), lifscan/triton_lif.py:1238)."""
+    return T if N >= SCAN_BWD_SERIAL_MIN_N else min(128, _pick_C(T, D=2))
+
+
 def scan_forward_auto(I, beta, theta, u_r, u0, K=16, repair=0):
-    """lifscan/triton_lif.py:1228-1232: v3 with C = _pick_C(T, 16)."""
-    T = I.shape[0]
-    return scan_forward_v3(I, beta, theta, u_r, u0, C=_pick_C(T, D=16), K=K, repair=repair)
+    """lifscan/triton_lif.py:1228-1232 with a B200 chunk choice (scan_chunk_fwd).
+    Outputs are identical for every chunk length (exact after repair)."""
+    T, N = I.shape
+    return scan_forward_v3(I, beta, theta, u_r, u0, C=scan_chunk_fwd(T, N), K=K, repair=repair)
 
 
 # ----------------------------------------------------------------------------- scan backward
 def scan_backward_tiled(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True, C=64, BNr=32, D=4,
                         nwr=1):
     """Tiled affine-scan backward (lifscan/triton_lif.py:512-526) -> Lam.
-    GU may be None (zeros)."""
+    GU may be None (zeros); S may be None as for serial_backward."""
     I, u0, U, S, GS, GU, T, N = _prep_bwd(I, u0, U, S, GS, GU)
     C = int(C)
     if C <= 0 or T % C:
@@ -265,9 +290,9 @@ def scan_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True,
 
 
 def scan_backward_auto(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0):
-    """lifscan/triton_lif.py:1235-1239: C = min(128, _pick_C(T, 2))."""
-    T = I.shape[0]
-    return scan_backward_tiled(I, u0, U, S, GS, GU, beta, theta, u_r, alpha, C=min(128, _pick_C(T, D=2)))
+    """lifscan/triton_lif.py:1235-1239 with a B200 chunk choice (scan_chunk_bwd)."""
+    T, N = I.shape
+    return scan_backward_tiled(I, u0, U, S, GS, GU, beta, theta, u_r, alpha, C=scan_chunk_bwd(T, N))
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -308,11 +333,13 @@ class LIFTuned(torch.autograd.Function):
         I, u0, U, S = ctx.saved_tensors
         beta, theta, u_r, alpha, mode = ctx.cfg
         gS = gS.contiguous()
-        # GU is identically zero on this path: pass None instead of materialising zeros_like(gS).
+        # GU is identically zero on this path: pass None instead of materialising
+        # zeros_like(gS); S is this layer's own forward output, so the kernels
+        # recompute it bit-exactly from U and I instead of reading it (S=None).
         if mode == "serial":
-            Lam = serial_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+            Lam = serial_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         else:
-            Lam = scan_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+            Lam = scan_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         return Lam, beta * Lam[0], None, None, None, None, None, None, None
 
 
@@ -341,9 +368,9 @@ class LIFFunction(torch.autograd.Function):
         beta, theta, u_r, alpha, mode, C = ctx.cfg
         gS = gS.contiguous()
         if mode == "serial":
-            Lam = serial_backward(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+            Lam = serial_backward(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         else:
-            Lam = scan_backward(I, u0, U, S, gS, None, beta, theta, u_r, alpha, C=C)
+            Lam = scan_backward(I, u0, U, None, gS, None, beta, theta, u_r, alpha, C=C)
         return Lam, beta * Lam[0], None, None, None, None, None, None, None, None
 
 
@@ -390,9 +417,9 @@ class LIFAuto(torch.autograd.Function):
         beta, theta, u_r, alpha, bwd_mode = ctx.cfg
         gS = gS.contiguous()
         if bwd_mode == "scan":
-            Lam = scan_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+            Lam = scan_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         else:
-            Lam = serial_backward_auto(I, u0, U, S, gS, None, beta, theta, u_r, alpha)
+            Lam = serial_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         return Lam, beta * Lam[0], None, None, None, None, None, None, None, None
 
 

@@ -74,6 +74,13 @@ int lifb_abi_version(void);
  * launches inside a timed region. */
 uint64_t lifb_kernel_launches(void);
 
+/* Device-side status of the current CUDA device: 0 when no kernel of this
+ * library has reported a problem, else the code of the first one (101 = a
+ * bounded wait for an asynchronous copy expired; the kernel stopped early and
+ * its outputs are incomplete).  Synchronous (reads device memory); reset != 0
+ * clears the word afterwards.  Returns -1 if the read itself failed. */
+int lifb_device_status(int reset);
+
 /* Human-readable text of a status code, and the last error message recorded
  * on the calling host thread (empty string if none). */
 const char *lifb_status_string(int status);
@@ -89,7 +96,10 @@ int lifb_serial_fwd(const float *I, const float *u0, float *U, float *S,
 
 /* Serial adjoint: lam_t = a_t lam_{t+1} + b_t swept backwards, with the
  * sigmoid surrogate (alpha) and the detached (detach != 0) or attached reset.
- * GU may be NULL (all zeros, the lif_tuned path).
+ * GU may be NULL (all zeros, the lif_tuned path).  S may be NULL when it is
+ * the forward's own output: s_t is then recomputed as [v_t >= theta] from
+ * v_t = fl(fl(beta*U[t-1]) + I[t]), which equals the stored spike bit for bit,
+ * and the kernel reads 16 instead of 20 bytes per neuron-step.
  * Replaces serial_backward_auto (lifscan/triton_lif.py:1199-1203), i.e.
  * bwd_tiled_pf_kernel (:1087-1127), and serial_backward (:254-259). */
 int lifb_serial_bwd(const float *I, const float *u0, const float *U, const float *S,
@@ -121,7 +131,7 @@ int lifb_scan_fwd_v4(const float *I, const float *u0, float *U, float *S,
                      lifb_stats *stats_dev, void *stream);
 
 /* Tiled affine-scan backward with the surrogate fused in; C = chunk length
- * (T % C == 0).  GU may be NULL (zeros).
+ * (T % C == 0).  GU may be NULL (zeros); S may be NULL as for lifb_serial_bwd.
  * Replaces scan_backward_tiled (lifscan/triton_lif.py:512-526) and, with the
  * reference's choice of C, scan_backward_auto (:1235-1239). */
 size_t lifb_scan_bwd_workspace_bytes(int64_t T, int64_t N, int C);
