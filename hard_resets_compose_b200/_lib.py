@@ -42,6 +42,8 @@ SIGNATURES = {
     "lifb_scan_fwd_v4_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
     "lifb_scan_fwd_v4": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
                           c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p], c_int),
+    "lifb_scan_fwd_v3_noalloc": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float,
+                                  c_float, c_int, c_int, c_int, c_void_p, c_void_p], c_int),
     "lifb_scan_bwd_workspace_bytes": ([c_i64, c_i64, c_int], c_size_t),
     "lifb_scan_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
                        c_float, c_float, c_float, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p], c_int),

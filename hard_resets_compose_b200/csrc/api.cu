@@ -101,6 +101,7 @@ constexpr int64_t kMaxGridY = 65535;
 
 namespace lifb {
 void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+void set_last_error(const char *msg) { g_last_error = msg ? msg : ""; }
 }  // namespace lifb
 
 extern "C" {

@@ -11,6 +11,8 @@ namespace lifb {
 
 // Adds n to the library's launch counter (lifb_kernel_launches).
 void count_launches(int n);
+// Sets the calling thread's lifb_last_error() text.
+void set_last_error(const char *msg);
 
 // Chunk-level scratch of the forward scan, carved from the caller's workspace.
 // All arrays are [M, N] (MX/MC: [M, K, N]) with the neuron index fastest.

@@ -141,6 +141,33 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
                   float alpha, int detach, int C,
                   void *workspace, size_t workspace_bytes, void *stream);
 
+/* No-allocation variant of lifb_scan_fwd_v3 (no counterpart in the
+ * reference, which only runs inside PyTorch and always allocates).
+ * For callers that cannot allocate device memory when they call in: a plain
+ * C or FFI host with no device allocator, an application whose device memory
+ * is already committed to another pool or capped, or a latency-critical loop
+ * that must never call cudaMalloc (which can block on the device).  The
+ * arguments are those of lifb_scan_fwd_v3 without the workspace: its scratch
+ * is a fixed array of LIFB_NOALLOC_SCRATCH_BYTES (64 MiB) inside the library,
+ * held by every GPU that loads the library until the process exits.  The call
+ * allocates nothing.
+ *   - Requests whose lifb_scan_fwd_v3_workspace_bytes(T, N, C, K) exceed the
+ *     maximum return LIFB_ERR_INVALID_ARGUMENT (the message gives the size)
+ *     without touching the GPU.  At C = 64, K = 16 that is T*N up to about
+ *     27 million neuron-steps.
+ *   - The first call on each device looks up the array's device address
+ *     (once per device, with that device current); make that first call
+ *     before any stream capture on the device.
+ *   - All calls on a device share the one array: calls that can overlap on
+ *     the GPU (other streams, or other host threads without ordering) race
+ *     on it and corrupt each other's results.  Issue them on one stream.
+ *   - Nothing needs clearing between calls: each call writes every scratch
+ *     word before reading it. */
+#define LIFB_NOALLOC_SCRATCH_BYTES (64ull << 20)
+int lifb_scan_fwd_v3_noalloc(const float *I, const float *u0, float *U, float *S,
+                             int64_t T, int64_t N, float beta, float theta, float u_r,
+                             int C, int K, int max_repair, lifb_stats *stats_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
