@@ -289,4 +289,28 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
     return check_launch("lifb_scan_bwd");
 }
 
+size_t lifb_lif_fwd_bwd_host_workspace_bytes(int64_t T, int64_t N, int64_t block_n)
+{
+    return lifb::host_pipe_workspace_bytes(T, N, block_n);
+}
+
+int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float *u0_host, float *S_host,
+                          float *dI_host, float *du0_host, int64_t T, int64_t N, float beta, float theta, float u_r,
+                          float alpha, int64_t block_n, void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "negative shape T=%lld N=%lld", (long long)T, (long long)N);
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!I_host || !GS_host || !u0_host || !S_host || !dI_host || !du0_host)
+        return fail(LIFB_ERR_INVALID_ARGUMENT, "null host pointer");
+    if (block_n <= 0 || block_n % 4) return fail(LIFB_ERR_INVALID_ARGUMENT, "block_n=%lld must be a positive multiple of 4", (long long)block_n);
+    int st;
+    size_t need = lifb::host_pipe_workspace_bytes(T, N, block_n);
+    if ((st = check_ws(workspace, workspace_bytes, need))) return st;
+    const char *err = nullptr;
+    st = lifb::host_pipe_run(I_host, GS_host, u0_host, S_host, dI_host, du0_host, T, N, beta, theta, u_r, alpha,
+                             block_n, workspace, (cudaStream_t)stream, &err);
+    if (st) return fail(st, "lifb_lif_fwd_bwd_host: %s", err ? err : "error");
+    return check_launch("lifb_lif_fwd_bwd_host");
+}
+
 }  // extern "C"

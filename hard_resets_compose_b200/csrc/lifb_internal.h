@@ -68,6 +68,12 @@ void grid_replay_repair(const float *I, const float *u0, FwdMaps &mp, float *U, 
                         int C, int max_repair, float beta, float theta, float u_r, lifb_stats *st,
                         cudaStream_t s);
 
+// host_pipeline.cu
+size_t host_pipe_workspace_bytes(int64_t T, int64_t N, int64_t block_n);
+int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float *S_h, float *dI_h, float *du0_h,
+                  int64_t T, int64_t N, float beta, float theta, float u_r, float alpha, int64_t block_n,
+                  void *workspace, cudaStream_t cs, const char **err);
+
 // scan_bwd.cu
 struct BwdScratch {
     float *P, *Q, *LamEnd;

@@ -21,6 +21,8 @@ compatibility and stats['repair_iters'] reports the rounds actually run.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -34,6 +36,7 @@ __all__ = [
     "state_bounds", "surrogate_grad", "_pick_C", "LIFTuned", "lif_tuned", "LIFFunction", "lif",
     "AUTO_FWD_MAX_N", "AUTO_FWD_MIN_T", "AUTO_BWD_MAX_N", "AUTO_BWD_MIN_T", "auto_modes",
     "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg", "scan_chunk_fwd", "scan_chunk_bwd",
+    "lif_tuned_host",
 ]
 
 _CONVERGE = -1  # max_repair value meaning "repair until converged"
@@ -427,3 +430,40 @@ def lif_auto(I, u0, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, K=16, repair=0):
     """lifscan/triton_lif.py:1029-1031."""
     fwd, bwd = auto_modes(I.shape[1], I.shape[0])
     return LIFAuto.apply(I, u0, beta, theta, u_r, alpha, K, repair, fwd, bwd)
+
+
+# ----------------------------------------------------------------------------- host-resident tensors
+def lif_tuned_host(I, GS, u0=None, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, block_n=None, device=None,
+                   out=None):
+    """lif_tuned forward + backward for host (CPU) tensors, pipelined over
+    neuron blocks so host->device copies, compute and device->host copies
+    overlap (lifb_lif_fwd_bwd_host).  Returns (S, dI, du0) as CPU tensors
+    (pinned); equivalent to S = lif_tuned(I, u0, ...);
+    torch.autograd.backward(S, GS) with dI = I.grad and du0 = u0.grad.
+    I and GS should be pinned for full overlap; `out` may pass preallocated
+    pinned (S, dI, du0)."""
+    if I.is_cuda or GS.is_cuda:
+        raise ValueError("lif_tuned_host takes host tensors; use lif_tuned for CUDA tensors")
+    if I.dtype != torch.float32 or GS.dtype != torch.float32:
+        raise TypeError("I and GS must be float32")
+    I = I.contiguous()
+    GS = GS.contiguous()
+    T, N = I.shape
+    if tuple(GS.shape) != (T, N):
+        raise ValueError("GS must have the shape of I")
+    u0 = torch.zeros(N, dtype=torch.float32) if u0 is None else u0.contiguous()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if block_n is None:  # about 8 blocks, 128-neuron aligned
+        block_n = max(128, ((N + 7) // 8 + 127) // 128 * 128)
+    if out is None:
+        out = (torch.empty(T, N).pin_memory(), torch.empty(T, N).pin_memory(), torch.empty(N).pin_memory())
+    S, dI, du0 = out
+    L = _lib.load()
+    with torch.cuda.device(dev):
+        nb = L.lifb_lif_fwd_bwd_host_workspace_bytes(T, N, block_n)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        check(L.lifb_lif_fwd_bwd_host(ptr(I), ptr(GS), ptr(u0), ptr(S), ptr(dI), ptr(du0), T, N, _f(beta),
+                                      _f(theta), _f(u_r), _f(alpha), int(block_n), ptr(ws), nb, st),
+              "lif_tuned_host")
+    return S, dI, du0

@@ -141,6 +141,25 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
                   float alpha, int detach, int C,
                   void *workspace, size_t workspace_bytes, void *stream);
 
+/* lif_tuned forward + backward for HOST-resident tensors (the layer of
+ * lifscan/triton_lif.py:654-683 with the detached sigmoid surrogate, called
+ * with tensors that live in host memory).  Inputs I_host, GS_host [T, N] and
+ * u0_host [N]; outputs S_host [T, N] (spikes), dI_host [T, N] (= Lam = dL/dI)
+ * and du0_host [N] (= beta * Lam[0]).  Host buffers should be pinned
+ * (cudaHostAlloc / page-locked) for the copies to overlap.  The neurons are
+ * processed in column blocks of block_n (a multiple of 4): while block b runs
+ * forward and adjoint on `stream`, block b+1 is copied in and block b-1 out on
+ * two library-owned copy streams, so the call is bound by the slower PCIe
+ * direction.  The workspace is device memory of at least
+ * lifb_lif_fwd_bwd_host_workspace_bytes(T, N, block_n) bytes (two staging
+ * slots).  Work is ordered after what is already queued on `stream`; the
+ * outputs are complete once `stream` has reached the end of this call. */
+size_t lifb_lif_fwd_bwd_host_workspace_bytes(int64_t T, int64_t N, int64_t block_n);
+int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float *u0_host,
+                          float *S_host, float *dI_host, float *du0_host,
+                          int64_t T, int64_t N, float beta, float theta, float u_r, float alpha,
+                          int64_t block_n, void *workspace, size_t workspace_bytes, void *stream);
+
 /* No-allocation variant of lifb_scan_fwd_v3 (no counterpart in the
  * reference, which only runs inside PyTorch and always allocates).
  * For callers that cannot allocate device memory when they call in: a plain

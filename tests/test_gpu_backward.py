@@ -113,3 +113,26 @@ def test_gradient_against_fp64_autograd(cuda):
     S = L().lif_tuned(Id, u0d, beta=beta, mode="scan")
     (S * GSd).sum().backward()
     assert rel(_np(Id.grad), Ix.grad.numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("N,block_n", ((16384, 2048), (1000, 256), (4096, 4096)))
+def test_lif_tuned_host_pipeline(cuda, N, block_n):
+    """Host-buffer forward+backward (lifb_lif_fwd_bwd_host): spikes bit-exact,
+    dI and du0 within 1e-5 of the oracle, for block counts that leave a
+    ragged last block, a single block, and two-slot reuse."""
+    T, beta = 1024, 0.99
+    I, u0, GS = gen(T, N, 0.05, 0.2, seed=5, u0_sd=0.3, grad=True)
+    Us, Ss = O.serial_forward(I, beta, 1.0, 0.0, u0)
+    dI_ref = O.serial_backward(I, u0, Us, Ss, GS, None, beta, 1.0, 0.0, 4.0, True)
+    It = torch.from_numpy(I).pin_memory()
+    Gt = torch.from_numpy(GS).pin_memory()
+    S, dI, du0 = L().lif_tuned_host(It, Gt, torch.from_numpy(u0), beta=beta, block_n=block_n)
+    torch.cuda.synchronize()
+    assert_bit_equal(S.numpy(), Ss, "S")
+    assert rel(dI.numpy(), dI_ref) < TOL
+    assert rel(du0.numpy(), beta * dI_ref[0]) < TOL
+    # a second call reuses the library's copy streams and the staging slots
+    S2, dI2, _ = L().lif_tuned_host(It, Gt, torch.from_numpy(u0), beta=beta, block_n=block_n)
+    torch.cuda.synchronize()
+    assert_bit_equal(S2.numpy(), Ss, "S (second call)")
+    assert np.array_equal(dI2.numpy(), dI.numpy())
