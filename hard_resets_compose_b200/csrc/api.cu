@@ -97,6 +97,29 @@ int check_ws(void *ws, size_t have, size_t need)
 
 constexpr int64_t kMaxGridY = 65535;
 
+// Chunks per replay segment for the fast v3 path: the largest power of two
+// dividing M that still leaves enough (segment, 32-neuron) warps to keep every
+// SM busy (about 8 per SM), so each warp replays one long segment.
+int64_t segment_chunks(int64_t M, int64_t N)
+{
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t warps_per_seg = (N + 31) / 32;
+    const int64_t want = (8 * (int64_t)sms + warps_per_seg - 1) / warps_per_seg;  // segments wanted
+    int64_t g = 1;
+    while ((M % (2 * g)) == 0 && M / (2 * g) >= want) g *= 2;
+    return g;
+}
+
+// Sequential carry: the TMA-staged kernel when it applies, else the plain one.
+void carry_any(const float *I, const float *u0, const float *MA, const float *MB, const float *MX, const float *MC,
+               const int32_t *MN, const int32_t *OVF, float *Starts, int64_t N, int64_t M, int64_t L, int K,
+               float beta, float theta, float u_r, cudaStream_t s)
+{
+    if (!lifb::carry_staged(I, u0, MA, MB, MX, MC, MN, OVF, Starts, N, M, L, K, beta, theta, u_r, s))
+        lifb::grid_carry(I, u0, MA, MB, MX, MC, MN, OVF, Starts, N, M, L, K, beta, theta, u_r, s);
+}
+
 }  // namespace
 
 namespace lifb {
@@ -193,7 +216,22 @@ int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S, int64_
     carve_fwd(c, mp, M, N, K);
     lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
     lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
-    lifb::grid_carry(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r, s);
+    if (!stats_dev && max_repair < 0) {
+        // Fast path: carry every chunk start, replay segments of G chunks from
+        // every G-th start, then fix the few segments whose start was not exact.
+        carry_any(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r, s);
+        const int64_t G = segment_chunks(M, N);
+        if (lifb::fwd_replay_tma(I, u0, mp.Starts, U, S, mp.Ends, T, N, (int64_t)C * G, beta, theta, u_r, s, G)) {
+            // Lo and MN are free once the maps are built and carried
+            lifb::fwd_fixup(I, mp.Starts, G, U, S, mp.Ends, mp.Lo, mp.MN, N, M / G, (int64_t)C * G, beta, theta, u_r,
+                            nullptr, s);
+            return check_launch("lifb_scan_fwd_v3");
+        }
+    } else {
+        lifb::grid_carry(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r,
+                         s);
+    }
+    // chunk-level replay and the reference's round-by-round repair (stats, caps on rounds)
     lifb::grid_replay_repair(I, u0, mp, U, S, T, N, C, max_repair, beta, theta, u_r, stats_dev, s);
     return check_launch("lifb_scan_fwd_v3");
 }
@@ -243,6 +281,17 @@ int lifb_scan_fwd_v4(const float *I, const float *u0, float *U, float *S, int64_
     lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
     lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
     if (M2c > 0) lifb::grid_compose(mp, sp, u0, M2c, N, G, K, K2, theta, u_r, stats_dev, s);
+    if (!stats_dev && max_repair < 0) {
+        // Fast path: carry the super maps, replay each super (C*G rows) from its
+        // carried start, then fix the few supers whose start was not exact.
+        carry_any(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2, beta,
+                  theta, u_r, s);
+        if (lifb::fwd_replay_tma(I, u0, sp.SStarts, U, S, mp.Ends, T, N, (int64_t)C * G, beta, theta, u_r, s, 1)) {
+            lifb::fwd_fixup(I, sp.SStarts, 1, U, S, mp.Ends, mp.Lo, mp.MN, N, M2, (int64_t)C * G, beta, theta, u_r,
+                            nullptr, s);
+            return check_launch("lifb_scan_fwd_v4");
+        }
+    }
     lifb::grid_carry(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2,
                      beta, theta, u_r, s);
     lifb::grid_carry_inner(I, mp, sp.SStarts, T, N, C, G, K, beta, theta, u_r, s);
@@ -284,6 +333,14 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
     w.P = c.take<float>(M * N);
     w.Q = c.take<float>(M * N);
     w.LamEnd = c.take<float>(M * N);
+    if (detach &&
+        lifb::bwd_tma(0, I, u0, U, S, GS, GU, nullptr, Lam, w.P, w.Q, T, N, C, beta, theta, u_r, alpha, true,
+                      (cudaStream_t)stream)) {
+        // Detached reset: every chunk replayed from lam_end = 0 is exact at and
+        // below its last spike; the fix-up recomputes only the rows above it.
+        lifb::bwd_fixup(I, u0, U, S, GS, GU, w.P, w.Q, Lam, N, M, C, beta, theta, alpha, (cudaStream_t)stream);
+        return check_launch("lifb_scan_bwd");
+    }
     lifb::grid_scan_bwd(I, u0, U, S, GS, GU, Lam, w, T, N, C, beta, theta, u_r, alpha, detach != 0,
                         (cudaStream_t)stream);
     return check_launch("lifb_scan_bwd");

@@ -63,13 +63,15 @@ __device__ __forceinline__ void st_vec(float *p, const Vec<NPL> &a)
 }
 
 // ===================================================================== forward
+// Chunk m starts from Starts[m * start_stride] (rows of N) or u0.
 template <int NPL, int R, int S>
 __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS, const float *__restrict__ u0,
-                                                const float *__restrict__ Starts, float *__restrict__ U,
-                                                float *__restrict__ Sout, float *__restrict__ Ends, int64_t N,
-                                                int64_t C, float beta, float theta, float u_r, int *status)
+                                                const float *__restrict__ Starts, int64_t start_stride,
+                                                float *__restrict__ U, float *__restrict__ Sout,
+                                                float *__restrict__ Ends, int64_t N, int64_t C, float beta,
+                                                float theta, float u_r, int *status)
 {
     constexpr int NB = 32 * NPL;
     constexpr int kTile = R * NB;  // floats per tile
@@ -104,7 +106,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
     const bool act = nl < N;
     Vec<NPL> u;
     if (act) {
-        u = ld_vec<NPL>((Starts ? Starts + m * N : u0) + nl);
+        u = ld_vec<NPL>((Starts ? Starts + m * start_stride * N : u0) + nl);
     } else {
 #pragma unroll
         for (int i = 0; i < NPL; i++) u.v[i] = 0.f;
@@ -248,7 +250,7 @@ __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, con
         float c = gs.v[i] * sg;
         if constexpr (HAS_GU) c = c + J * gu.v[i];
         lam.v[i] = c + a * lam.v[i];
-        if (MODE == kCompose) pp.v[i] = a * pp.v[i];
+        pp.v[i] = a * pp.v[i];
     }
 }
 
@@ -339,7 +341,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
                     lam.v[i] = cv[rr].v[i] + av[rr].v[i] * lam.v[i];
-                    if (MODE == kCompose) pp.v[i] = av[rr].v[i] * pp.v[i];
+                    pp.v[i] = av[rr].v[i] * pp.v[i];
                 }
                 if (MODE == kReplay) st_vec<NPL>(ol + rr * NB + NPL * lane, lam);
             }
@@ -364,7 +366,9 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
         if (lane == 0 && k + S < ntiles) issue(s, k + S);
     }
     if (!ok && status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
-    if (ok && MODE == kCompose && act) {
+    // kCompose always writes the chunk map; kReplay writes it when P is given
+    // (then P = prod a over the chunk and Q = lam at its first row).
+    if (ok && P && act) {
         st_vec<NPL>(P + m * N + nl, pp);
         st_vec<NPL>(Q + m * N + nl, lam);
     }
@@ -439,9 +443,9 @@ static int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
 }
 
 template <int NPL>
-static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, float *U, float *S, float *Ends,
-                       int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, int *status,
-                       cudaStream_t s)
+static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, int64_t start_stride, float *U,
+                       float *S, float *Ends, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r,
+                       int *status, cudaStream_t s)
 {
     constexpr int NB = 32 * NPL;
     constexpr int R = FwdTile<NPL>::R, ST = FwdTile<NPL>::S;
@@ -450,11 +454,13 @@ static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *St
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
-    kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], u0, Starts, U, S, Ends, N, C, beta, theta, u_r, status);
+    kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], u0, Starts, start_stride, U, S, Ends, N, C, beta, theta, u_r,
+                             status);
 }
 
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
-                    int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s)
+                    int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
+                    int64_t start_stride)
 {
     const void *p[] = {I, u0, Starts, U, S, Ends};
     if (!tma_ok(p, 6, N) || C <= 0 || T % C) return false;
@@ -467,8 +473,8 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
         !make_tmap_2d(&maps[2], S, N, T, 32 * npl, R))
         return false;
     int *status = device_status_ptr();
-    if (npl == 4) launch_fwd<4>(maps, u0, Starts, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
-    else launch_fwd<1>(maps, u0, Starts, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
+    if (npl == 4) launch_fwd<4>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
+    else launch_fwd<1>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
     return true;
 }
 

@@ -29,16 +29,21 @@ struct SuperMaps {
 
 // runtime.cu
 bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_x, int box_y);
+// 2-D map of a [T, N] array of 4-byte elements (fp32, or int32 when int32 is true).
+bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N, int64_t T, int box_x, int box_y);
 int *device_status_ptr();                 // status word of the current device
 int read_device_status(bool reset);       // synchronous read (current device)
 
 // chunk_tma.cu: TMA-pipelined chunk kernels; false when the TMA path does not
 // apply (N % 4 != 0, a misaligned tensor, more than 65535 chunks).
 // Forward replay of M = T/C chunks from Starts (NULL: one chunk from u0).
+// Chunk m starts from Starts[m * start_stride] (in rows of N).
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
-                    int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s);
-// Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0),
-// mode 1 writes the chunk maps P, Q.
+                    int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
+                    int64_t start_stride = 1);
+// Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0)
+// and, when P is given, also the chunk maps; mode 1 writes only P, Q.
+// P[m] = prod of a_t over chunk m, Q[m] = lam at the chunk's first row.
 bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const float *S, const float *GS,
              const float *GU, const float *LamEnd, float *Lam, float *P, float *Q, int64_t T, int64_t N, int64_t C,
              float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s);
@@ -73,6 +78,25 @@ size_t host_pipe_workspace_bytes(int64_t T, int64_t N, int64_t block_n);
 int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float *S_h, float *dI_h, float *du0_h,
                   int64_t T, int64_t N, float beta, float theta, float u_r, float alpha, int64_t block_n,
                   void *workspace, cudaStream_t cs, const char **err);
+
+// carry_tma.cu: sequential map carry with TMA-staged map windows; false when
+// it does not apply (N % 4 != 0, K > 64).  Writes Starts[m] for m < M.
+bool carry_staged(const float *I, const float *u0, const float *MA, const float *MB, const float *MX, const float *MC,
+                  const int32_t *MN, const int32_t *OVF, float *Starts, int64_t N, int64_t M, int64_t L, int K,
+                  float beta, float theta, float u_r, cudaStream_t s);
+
+// carry_tma.cu: envelope prefix with TMA-staged (c, a, b) windows.
+bool env_carry_staged(const float *u0, const float *EC, const float *EA, const float *EB, float *Lo, int64_t N,
+                      int64_t M, float margin, cudaStream_t s);
+
+// scan_fixup.cu
+// EndsNew [NS, N] float and Changed [NS, N] int32 are scratch.
+void fwd_fixup(const float *I, const float *Starts, int64_t start_stride, float *U, float *S, float *Ends,
+               float *EndsNew, int32_t *Changed, int64_t N, int64_t NS, int64_t L, float beta, float theta, float u_r,
+               int *longest_chain, cudaStream_t s);
+void bwd_fixup(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,
+               const float *P, const float *Q, float *Lam, int64_t N, int64_t M, int64_t C, float beta, float theta,
+               float alpha, cudaStream_t s);
 
 // scan_bwd.cu
 struct BwdScratch {

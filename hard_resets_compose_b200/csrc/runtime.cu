@@ -35,6 +35,11 @@ static PFN_cuTensorMapEncodeTiled_v12000 encoder()
 
 bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_x, int box_y)
 {
+    return make_tmap_2d_typed(m, base, false, N, T, box_x, box_y);
+}
+
+bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N, int64_t T, int box_x, int box_y)
+{
     auto enc = encoder();
     if (!enc || ((uintptr_t)base & 15) || (N * 4) % 16 || T >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
         return false;
@@ -42,7 +47,8 @@ bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int b
     cuuint64_t strides[1] = {(cuuint64_t)N * 4};
     cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+    CUresult r = enc(m, int32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base,
+                     dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;

@@ -395,9 +395,12 @@ void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t M, int6
 {
     // EC/EA/EB live in the Starts/Ends/MB slots, which are written later.
     float *EC = mp.Starts, *EA = mp.Ends, *EB = mp.MB;
-    count_launches(2);
+    count_launches(1);
     k_env_chunk<<<dim3(nblk(N), (unsigned)M), kBlock, 0, s>>>(I, EC, EA, EB, N, C, beta, u_r);
-    k_env_carry<<<nblk(N), kBlock, 0, s>>>(u0, EC, EA, EB, mp.Lo, N, M, 1e-5f);
+    if (!env_carry_staged(u0, EC, EA, EB, mp.Lo, N, M, 1e-5f, s)) {
+        count_launches(1);
+        k_env_carry<<<nblk(N), kBlock, 0, s>>>(u0, EC, EA, EB, mp.Lo, N, M, 1e-5f);
+    }
 }
 
 void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, int K, float beta,

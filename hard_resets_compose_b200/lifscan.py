@@ -238,26 +238,39 @@ def _pick_C(T, D=8):
     raise ValueError(f"T={T} needs a chunk length divisible by {D}")
 
 
-# Widths at which one recurrence per lane already keeps HBM busy on B200: the
-# serial chain costs ~18 SM cycles per step (forward) and ~6 (adjoint), so a
-# single pass is HBM-bound once N*12 B (forward) or N*20 B (adjoint) per step
-# outlasts that chain at the measured copy bandwidth.  Below these widths the
-# time-parallel scan is used with the reference's chunk length.
-SCAN_FWD_SERIAL_MIN_N = 6144
-SCAN_BWD_SERIAL_MIN_N = 2048
+# Chunk lengths of lif_tuned's scan mode on B200, chosen from measurements
+# (profiles/scan_paths_b200.md):
+#  * forward: the single streaming pass (one chunk, C = T: the scan's replay
+#    pass from u0) is faster than building maps at every width measured, from
+#    N = 1024 x T = 2^20 (19 ms vs 34 ms for the map scan) to N = 16384 x
+#    T = 1024, so the auto path uses it; scan_forward_v3/v4 called directly still
+#    build and carry maps with the caller's C and K.
+#  * adjoint: below N = 8192 the single pass is chain-bound, and long chunks
+#    replayed in parallel from lam_end = 0 plus the tail fix-up (the detached
+#    reset zeroes the carry at every spike) win: T = 2^20, N = 1024 in ~4 ms vs
+#    43 ms.  Chunks are long (about 8 warps per SM in flight) so tails are rare.
+SCAN_FWD_SERIAL_MIN_N = 0
+SCAN_BWD_SERIAL_MIN_N = 8192
+
+
+def _long_chunk(T, N, warps_per_sm=8, sms=148):
+    """Largest power-of-two divisor C of T that still gives about
+    warps_per_sm x sms (chunk, 32-neuron) warps."""
+    want = max(1, -(-warps_per_sm * sms * 32 // max(N, 1)))
+    C = T
+    while C % 2 == 0 and T // C < want:
+        C //= 2
+    return C
 
 
 def scan_chunk_fwd(T, N):
-    """Chunk length of lif_tuned's scan forward on B200: the whole sequence (one
-    chunk, i.e. the replay pass alone) when N is wide enough to saturate HBM,
-    else the reference's _pick_C(T, 16) (lifscan/triton_lif.py:1230)."""
+    """Chunk length of lif_tuned's scan forward on B200 (see above)."""
     return T if N >= SCAN_FWD_SERIAL_MIN_N else _pick_C(T, D=16)
 
 
 def scan_chunk_bwd(T, N):
-    """Chunk length of lif_tuned's scan backward on B200 (reference:
-    min(128, _pick_C(T, 2)), lifscan/triton_lif.py:1238)."""
-    return T if N >= SCAN_BWD_SERIAL_MIN_N else min(128, _pick_C(T, D=2))
+    """Chunk length of lif_tuned's scan backward on B200 (see above)."""
+    return T if N >= SCAN_BWD_SERIAL_MIN_N else _long_chunk(T, N)
 
 
 def scan_forward_auto(I, beta, theta, u_r, u0, K=16, repair=0):

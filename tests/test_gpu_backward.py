@@ -136,3 +136,18 @@ def test_lif_tuned_host_pipeline(cuda, N, block_n):
     torch.cuda.synchronize()
     assert_bit_equal(S2.numpy(), Ss, "S (second call)")
     assert np.array_equal(dI2.numpy(), dI.numpy())
+
+
+@pytest.mark.parametrize("beta", (0.5, 0.9, 0.99, 1.0))
+@pytest.mark.parametrize("N,T,C", ((1000, 4096, 64), (1024, 1 << 16, 1024), (777, 2048, 128), (64, 4096, 4096)))
+def test_scan_backward_fast_path(cuda, beta, N, T, C):
+    """Detached reset: chunks replayed from lam_end = 0 plus the tail fix-up,
+    with and without S supplied, against the oracle's serial adjoint."""
+    I, u0, GS = gen(T, N, 0.05, 0.2, seed=13, u0_sd=0.3, grad=True)
+    U, S = O.serial_forward(I, beta, 1.0, 0.0, u0)
+    ref = O.serial_backward(I, u0, U, S, GS, None, beta, 1.0, 0.0, 4.0, True)
+    d = to_dev(cuda, I, u0, U, S, GS)
+    l1 = L().scan_backward_tiled(d[0], d[1], d[2], d[3], d[4], None, beta, 1.0, 0.0, 4.0, True, C=C)
+    l2 = L().scan_backward_tiled(d[0], d[1], d[2], None, d[4], None, beta, 1.0, 0.0, 4.0, True, C=C)
+    assert rel(_np(l1), ref) < TOL
+    assert rel(_np(l2), ref) < TOL

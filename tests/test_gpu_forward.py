@@ -169,3 +169,45 @@ def test_bad_arguments_raise(cuda):
                             K=65)
     with pytest.raises(ValueError):
         L().serial_forward(I, 0.9, 1.0, 0.0, torch.zeros(5, device=cuda))
+
+
+@pytest.mark.parametrize("beta", BETAS)
+@pytest.mark.parametrize("mu,sd", DRIFTS)
+@pytest.mark.parametrize("N", (1000, 777))
+def test_v3_fast_path_bit_exact(cuda, beta, mu, sd, N):
+    """Without stats the v3 forward replays long segments from the carried
+    starts and fixes the inexact ones (N = 1000: TMA kernels; N = 777: the
+    N % 4 != 0 fallback)."""
+    T = 4096
+    I, u0 = gen(T, N, mu, sd, seed=11, u0_sd=0.3)
+    Us, Ss = O.serial_forward(I, beta, 1.0, -0.1, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    for K in (4, 16):
+        U, S = L().scan_forward_v3(Id, beta, 1.0, -0.1, u0d, C=64, K=K)
+        assert_bit_equal(_np(U), Us, f"U K={K}")
+        assert_bit_equal(_np(S), Ss, f"S K={K}")
+
+
+@pytest.mark.parametrize("beta", BETAS)
+@pytest.mark.parametrize("mu,sd", DRIFTS)
+def test_v4_fast_path_bit_exact(cuda, beta, mu, sd):
+    T, N = 8192, 1000
+    I, u0 = gen(T, N, mu, sd, seed=12, u0_sd=0.3)
+    Us, Ss = O.serial_forward(I, beta, 1.0, -0.1, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    for (C, G, K, K2) in ((64, 16, 16, 32), (32, 8, 4, 8)):
+        U, S = L().scan_forward_v4(Id, beta, 1.0, -0.1, u0d, C=C, G=G, K=K, K2=K2)
+        assert_bit_equal(_np(U), Us, f"U {C},{G},{K},{K2}")
+        assert_bit_equal(_np(S), Ss, f"S {C},{G},{K},{K2}")
+
+
+def test_long_sequence_v3_fast_path(cuda):
+    """Two-level path at long T (T = 2^17, B*N = 1024): the staged carry runs
+    2048 maps per neuron; config 4's input distribution."""
+    T, N = 1 << 17, 1024
+    I, u0 = gen(T, N, 0.02, 0.1, seed=0)
+    Us, Ss = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    U, S = L().scan_forward_v3(Id, 0.99, 1.0, 0.0, u0d, C=64, K=16)
+    assert_bit_equal(_np(S), Ss, "S")
+    assert_bit_equal(_np(U), Us, "U")
