@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--workload", default="c2", choices=("c2", "c3"),
+                   help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step")
     return p.parse_args()
 
 
@@ -148,6 +150,7 @@ def cpu_oracle_rate(T, N, seconds, want_bwd=True):
     have elapsed (at least once).  Returns (neuron-steps/s, threads, sample)."""
     import numpy as np
     from oracle import oracle as O
+    O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
     I, u0, GS = O.gen_inputs(T, N, MU, SD, seed=0, grad=True)
     threads = O.num_threads()
     O.serial_forward(I[:64], BETA, 1.0, 0.0, u0)  # warm the library
@@ -169,6 +172,7 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     from oracle import oracle as O
+    O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
     T, N = T_STEPS, N_PER_GPU
     I, u0, GS = O.gen_inputs(T, N, MU, SD, seed=0, grad=True)
     for _ in range(max(args.warmup, 0)):
@@ -196,11 +200,113 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_network(args, ws, rank, local):
+    """Config 3: one training step (forward, backward, Adam) of the 700-256-256-20
+    LIF network, B = 64 per GPU, T = 1024, beta = 0.9, Kaiming-uniform init,
+    leaky readout, cross-entropy over 20 random labels, synthetic Bernoulli
+    raster (rates U(0.5%, 4%)).  Data parallel: one bucketed all-reduce of the
+    weight gradients per step when N > 1."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn as nn
+
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200.shdnet import Net, synthetic_batch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+    T, B, H = 1024, 64, 256
+    torch.manual_seed(0)
+    net = Net(mode="scan", beta=0.9, H=H, init="kaiming", readout="leaky").to(dev)
+    x, y = synthetic_batch(T, B, seed=1000 + rank, device=dev)
+    opt = torch.optim.Adam(net.parameters(), lr=1e-3, capturable=True)
+    params = list(net.parameters())
+    stream = torch.cuda.current_stream(dev)
+
+    def fwd_bwd():
+        loss = nn.functional.cross_entropy(net(x)[0], y)
+        loss.backward()
+        return loss
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            opt.zero_grad(set_to_none=True)
+            fwd_bwd()
+            opt.step()
+    stream.wait_stream(side)
+    torch.cuda.synchronize(dev)
+    opt.zero_grad(set_to_none=True)
+    g_fb = torch.cuda.CUDAGraph()
+    n0 = lib.lifb_kernel_launches()
+    with torch.cuda.graph(g_fb):
+        fwd_bwd()
+    launches = lib.lifb_kernel_launches() - n0
+    g_opt = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_opt):
+        opt.step()
+    flat = torch.empty(sum(p.numel() for p in params), device=dev)
+
+    def step():
+        g_fb.replay()
+        if ws > 1:  # data parallel: average the weight gradients (about 1 MB)
+            torch.cat([p.grad.reshape(-1) for p in params], out=flat)
+            dist.all_reduce(flat)
+            flat.div_(ws)
+            o = 0
+            for p in params:
+                p.grad.copy_(flat[o:o + p.numel()].view_as(p.grad))
+                o += p.numel()
+        g_opt.replay()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        for a, b in evs:
+            a.record(stream)
+            step()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    if ws > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    units = 2 * B * H * T * ws  # LIF neuron-steps per step, both layers, all ranks
+    if rank == 0:
+        print(json.dumps({
+            "metric": "LIF neuron-steps/s, 700-256-256-20 training step (B=64/GPU, T=1024)",
+            "value": units / (ms / 1e3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic Bernoulli raster, rates U(0.5%, 4%), 20 labels",
+            "config": {"workload": "c3: network training step (forward, backward, Adam)", "beta": 0.9,
+                       "init": "kaiming-uniform", "readout": "leaky (non-spiking integrator, mean over T)",
+                       "lif_mode": "scan", "batch_per_gpu": B, "seq_len": T,
+                       "parallelism": f"data-parallel x{ws}, gradient all-reduce per step",
+                       "step": "forward+backward and Adam each captured in a CUDA graph"},
+            "gpu_launches": launches * args.steps, "clocks": clk.record()}), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     ws, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, ws, rank)
+        return
+    if args.workload == "c3":
+        run_network(args, ws, rank, local)
         return
 
     import torch
