@@ -50,6 +50,21 @@ SIGNATURES = {
     "lifb_scan_bwd_workspace_bytes": ([c_i64, c_i64, c_int], c_size_t),
     "lifb_scan_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
                        c_float, c_float, c_float, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_tshard_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
+    "lifb_tshard_envelope": ([c_void_p, c_i64, c_i64, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p,
+                              c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_tshard_slice_map": ([c_void_p, c_void_p, c_int, c_void_p, c_i64, c_i64, c_float, c_float, c_float, c_int,
+                               c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_tshard_apply": ([c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                           c_i64, c_i64, c_float, c_float, c_float, c_int, c_int, c_int, c_int, c_void_p, c_size_t,
+                           c_void_p], c_int),
+    "lifb_tshard_repair": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float,
+                            c_float, c_float, c_void_p], c_int),
+    "lifb_tshard_bwd_workspace_bytes": ([c_i64, c_i64, c_int], c_size_t),
+    "lifb_tshard_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float,
+                         c_float, c_float, c_int, c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_tshard_bwd_fix": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float,
+                             c_float, c_float, c_int, c_void_p, c_size_t, c_void_p], c_int),
 }
 
 

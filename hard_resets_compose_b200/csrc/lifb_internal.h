@@ -60,13 +60,18 @@ void serial_bwd(const float *I, const float *u0, const float *U, const float *S,
 // supers) only; the last chunk's map is needed only for the stats.
 void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, float beta,
                    float u_r, cudaStream_t s);
+// The prefix half of grid_envelope: Lo from chunk envelope maps already in
+// the Starts / Ends / MB slots of `mp` (EC / EA / EB).
+void grid_envelope_carry(const float *u0, FwdMaps &mp, int64_t M, int64_t N, cudaStream_t s);
 void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, int K, float beta,
                 float theta, float u_r, lifb_stats *st, cudaStream_t s);
 void grid_carry(const float *I, const float *u0, const float *MA, const float *MB, const float *MX,
                 const float *MC, const int32_t *MN, const int32_t *OVF, float *Starts, int64_t N, int64_t M,
                 int64_t L, int K, float beta, float theta, float u_r, cudaStream_t s);
+// Composes groups of G maps of `mp` (capacity K) into `sp` (capacity K2); the
+// pruning bound of group s is Lo[(s*G) * lo_stride].
 void grid_compose(const FwdMaps &mp, const SuperMaps &sp, const float *u0, int64_t M2, int64_t N, int G,
-                  int K, int K2, float theta, float u_r, lifb_stats *st, cudaStream_t s);
+                  int K, int K2, float theta, float u_r, lifb_stats *st, cudaStream_t s, int64_t lo_stride = 1);
 void grid_carry_inner(const float *I, const FwdMaps &mp, const float *SStarts, int64_t T, int64_t N, int C, int G,
                       int K, float beta, float theta, float u_r, cudaStream_t s);
 void grid_replay_repair(const float *I, const float *u0, FwdMaps &mp, float *U, float *S, int64_t T, int64_t N,
@@ -84,6 +89,22 @@ int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float 
 bool carry_staged(const float *I, const float *u0, const float *MA, const float *MB, const float *MX, const float *MC,
                   const int32_t *MN, const int32_t *OVF, float *Starts, int64_t N, int64_t M, int64_t L, int K,
                   float beta, float theta, float u_r, cudaStream_t s);
+
+// carry_tma.cu: envelope of a whole slice: the chunk envelope maps (c, a, b)
+// composed in order (min(c2, a2*c1 + b2), a2*a1, a2*b1 + b2).
+void env_compose(const float *EC, const float *EA, const float *EB, float *env, int64_t N, int64_t M, cudaStream_t s);
+// k_env_chunk over M chunks of C rows (EC/EA/EB [M, N]).
+void env_chunks(const float *I, float *EC, float *EA, float *EB, int64_t N, int64_t M, int C, float beta, float u_r,
+                cudaStream_t s);
+// scan_fixup.cu: replay-until-resynchronised of rows [0, T) from new entry
+// states (cross-slice repair); changed[n] = 1 and end[n] updated for neurons
+// whose rows never resynchronise.
+void entry_repair(const float *I, const float *entry, float *U, float *S, float *end, int32_t *changed, int64_t T,
+                  int64_t N, float beta, float theta, float u_r, cudaStream_t s);
+// Lam fix-up given the lam entering the slice from above (lam_top, per neuron).
+void bwd_fixup_top(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,
+                   const float *P, const float *Q, const float *lam_top, float *Lam, int64_t N, int64_t M, int64_t C,
+                   float beta, float theta, float alpha, cudaStream_t s);
 
 // carry_tma.cu: envelope prefix with TMA-staged (c, a, b) windows.
 bool env_carry_staged(const float *u0, const float *EC, const float *EA, const float *EB, float *Lo, int64_t N,

@@ -144,6 +144,35 @@ __global__ void __launch_bounds__(kFixBlock) k_fwd_fixup_seq(const float *__rest
     if (longest_chain && act && longest) atomicMax(longest_chain, longest);
 }
 
+// Cross-slice repair: rows [0, T) were replayed (and fixed) from an entry
+// state that may differ from the exact one; replay from the exact entry until
+// (u, s) rejoins the stored rows.  Neurons that never rejoin get a new end.
+__global__ void __launch_bounds__(kFixBlock) k_entry_repair(const float *__restrict__ I,
+                                                            const float *__restrict__ entry, float *__restrict__ U,
+                                                            float *__restrict__ S, float *__restrict__ end,
+                                                            int32_t *__restrict__ changed, int64_t T, int64_t N,
+                                                            float beta, float theta, float u_r)
+{
+    const int64_t n = (int64_t)blockIdx.x * kFixBlock + threadIdx.x;
+    const bool act = n < N;
+    float u = act ? entry[n] : 0.0f;
+    // the stored rows started from the state before row 0, which the caller
+    // compares: every active lane is assumed to differ
+    const bool synced = replay_until_sync<16>(I, U, S, N, n, act, 0, T, u, act, beta, theta, u_r);
+    if (act) {
+        changed[n] = synced ? 0 : 1;
+        if (!synced) end[n] = u;
+    }
+}
+
+void entry_repair(const float *I, const float *entry, float *U, float *S, float *end, int32_t *changed, int64_t T,
+                  int64_t N, float beta, float theta, float u_r, cudaStream_t s)
+{
+    count_launches(1);
+    k_entry_repair<<<(unsigned)((N + kFixBlock - 1) / kFixBlock), kFixBlock, 0, s>>>(I, entry, U, S, end, changed, T,
+                                                                                      N, beta, theta, u_r);
+}
+
 // Adjoint coefficients with the same arithmetic as k_bwd_tma (bwd_coef).
 __device__ __forceinline__ void coef_fix(float up, float s, float x, float gs, float gu, float beta, float theta,
                                          float alpha, float &a, float &c)
@@ -158,22 +187,31 @@ __device__ __forceinline__ void coef_fix(float up, float s, float x, float gs, f
     c = gs * sg + J * gu;
 }
 
+// lam_top (nullable): lam entering the last chunk from above (0 when NULL).
 __global__ void __launch_bounds__(kFixBlock) k_bwd_fixup(const float *__restrict__ I, const float *__restrict__ u0,
                                                          const float *__restrict__ U, const float *__restrict__ S,
                                                          const float *__restrict__ GS, const float *__restrict__ GU,
                                                          const float *__restrict__ P, const float *__restrict__ Q,
-                                                         float *__restrict__ Lam, int64_t N, int64_t M, int64_t C,
-                                                         float beta, float theta, float alpha)
+                                                         const float *__restrict__ lam_top, float *__restrict__ Lam,
+                                                         int64_t N, int64_t M, int64_t C, float beta, float theta,
+                                                         float alpha)
 {
     const int64_t n = (int64_t)blockIdx.x * kFixBlock + threadIdx.x;
     const int64_t m = blockIdx.y;
-    if (n >= N || m + 1 >= M) return;  // the last chunk ends at lam = 0: exact
-    // first chunk e > m whose first-row lam is exact: it holds a spike (P = 0)
-    // or it is the last chunk
-    int64_t e = m + 1;
-    while (e + 1 < M && P[e * N + n] != 0.0f) e++;
-    float lam = Q[e * N + n];
-    for (int64_t i = e - 1; i > m; i--) lam = Q[i * N + n] + P[i * N + n] * lam;
+    if (n >= N) return;
+    const float top = lam_top ? lam_top[n] : 0.0f;
+    float lam;
+    if (m + 1 >= M) {
+        lam = top;  // the last chunk: lam_end is the lam entering from above
+    } else {
+        // first chunk e > m whose first-row lam is exact: it holds a spike
+        // (P = 0), or it is the last chunk (exact from `top`)
+        int64_t e = m + 1;
+        while (e + 1 < M && P[e * N + n] != 0.0f) e++;
+        lam = Q[e * N + n];
+        if (e + 1 == M && top != 0.0f) lam = lam + P[e * N + n] * top;
+        for (int64_t i = e - 1; i > m; i--) lam = Q[i * N + n] + P[i * N + n] * lam;
+    }
     if (lam == 0.0f) return;  // the replay's lam_end = 0 was already right
     const float un0 = u0[n];
     constexpr int kB = 8;  // rows loaded ahead of the dependent chain
@@ -226,7 +264,16 @@ void bwd_fixup(const float *I, const float *u0, const float *U, const float *S, 
     if (M < 2) return;
     count_launches(1);
     dim3 g((unsigned)((N + kFixBlock - 1) / kFixBlock), (unsigned)(M - 1));
-    k_bwd_fixup<<<g, kFixBlock, 0, s>>>(I, u0, U, S, GS, GU, P, Q, Lam, N, M, C, beta, theta, alpha);
+    k_bwd_fixup<<<g, kFixBlock, 0, s>>>(I, u0, U, S, GS, GU, P, Q, nullptr, Lam, N, M, C, beta, theta, alpha);
+}
+
+void bwd_fixup_top(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,
+                   const float *P, const float *Q, const float *lam_top, float *Lam, int64_t N, int64_t M, int64_t C,
+                   float beta, float theta, float alpha, cudaStream_t s)
+{
+    count_launches(1);
+    dim3 g((unsigned)((N + kFixBlock - 1) / kFixBlock), (unsigned)M);
+    k_bwd_fixup<<<g, kFixBlock, 0, s>>>(I, u0, U, S, GS, GU, P, Q, lam_top, Lam, N, M, C, beta, theta, alpha);
 }
 
 }  // namespace lifb

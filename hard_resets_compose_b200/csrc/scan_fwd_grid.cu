@@ -202,14 +202,14 @@ __global__ void __launch_bounds__(kBlock) k_compose(const float *__restrict__ MA
                                                     float *__restrict__ SX, float *__restrict__ SC,
                                                     int32_t *__restrict__ SN, int32_t *__restrict__ SOVF,
                                                     int64_t N, int G, int K, int K2, float theta, float u_r,
-                                                    lifb_stats *st)
+                                                    lifb_stats *st, int64_t lo_stride)
 {
     int64_t n0 = (int64_t)blockIdx.x * kBlock + threadIdx.x;
     bool act = n0 < N;
     int64_t n = act ? n0 : N - 1;
     int64_t s = blockIdx.y;
     int64_t m0 = s * G;
-    float lo = Lo[m0 * N + n];
+    float lo = Lo[m0 * lo_stride * N + n];
     float hi = fmaxf(u0[n], fmaxf(theta, u_r));
     float A = MA[m0 * N + n], B = MB[m0 * N + n];
     int nH = MN[m0 * N + n];
@@ -381,11 +381,11 @@ static void launch_build(dim3 g, cudaStream_t s, const float *I, const float *Lo
 
 template <int KM2>
 static void launch_compose(dim3 g, cudaStream_t s, const FwdMaps &mp, const SuperMaps &sp, const float *u0,
-                           int64_t N, int G, int K, int K2, float theta, float u_r, lifb_stats *st)
+                           int64_t N, int G, int K, int K2, float theta, float u_r, lifb_stats *st, int64_t lo_stride)
 {
     count_launches(1);
     k_compose<KM2><<<g, kBlock, 0, s>>>(mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Lo, u0, sp.SA, sp.SB, sp.SX,
-                                        sp.SC, sp.SN, sp.SOVF, N, G, K, K2, theta, u_r, st);
+                                        sp.SC, sp.SN, sp.SOVF, N, G, K, K2, theta, u_r, st, lo_stride);
 }
 
 static inline unsigned nblk(int64_t N) { return (unsigned)((N + kBlock - 1) / kBlock); }
@@ -394,13 +394,53 @@ void grid_envelope(const float *I, const float *u0, FwdMaps &mp, int64_t M, int6
                    float u_r, cudaStream_t s)
 {
     // EC/EA/EB live in the Starts/Ends/MB slots, which are written later.
-    float *EC = mp.Starts, *EA = mp.Ends, *EB = mp.MB;
     count_launches(1);
-    k_env_chunk<<<dim3(nblk(N), (unsigned)M), kBlock, 0, s>>>(I, EC, EA, EB, N, C, beta, u_r);
+    k_env_chunk<<<dim3(nblk(N), (unsigned)M), kBlock, 0, s>>>(I, mp.Starts, mp.Ends, mp.MB, N, C, beta, u_r);
+    grid_envelope_carry(u0, mp, M, N, s);
+}
+
+void grid_envelope_carry(const float *u0, FwdMaps &mp, int64_t M, int64_t N, cudaStream_t s)
+{
+    const float *EC = mp.Starts, *EA = mp.Ends, *EB = mp.MB;
     if (!env_carry_staged(u0, EC, EA, EB, mp.Lo, N, M, 1e-5f, s)) {
         count_launches(1);
         k_env_carry<<<nblk(N), kBlock, 0, s>>>(u0, EC, EA, EB, mp.Lo, N, M, 1e-5f);
     }
+}
+
+// Composition of the chunk envelope maps of a slice (one thread per neuron):
+// g2 o g1 = (min(c2, a2*c1 + b2), a2*a1, a2*b1 + b2).  env = [c | a | b] rows.
+__global__ void __launch_bounds__(kBlock) k_env_compose(const float *__restrict__ EC, const float *__restrict__ EA,
+                                                        const float *__restrict__ EB, float *__restrict__ env,
+                                                        int64_t N, int64_t M)
+{
+    int64_t n = (int64_t)blockIdx.x * kBlock + threadIdx.x;
+    if (n >= N) return;
+    float c = kInf, a = 1.0f, b = 0.0f;
+#pragma unroll 8
+    for (int64_t m = 0; m < M; m++) {
+        const float c2 = EC[m * N + n], a2 = EA[m * N + n], b2 = EB[m * N + n];
+        const float cc = mul_add_rn(a2, c, b2);
+        c = c2 < cc ? c2 : cc;
+        b = mul_add_rn(a2, b, b2);
+        a = __fmul_rn(a2, a);
+    }
+    env[n] = c;
+    env[N + n] = a;
+    env[2 * N + n] = b;
+}
+
+void env_compose(const float *EC, const float *EA, const float *EB, float *env, int64_t N, int64_t M, cudaStream_t s)
+{
+    count_launches(1);
+    k_env_compose<<<nblk(N), kBlock, 0, s>>>(EC, EA, EB, env, N, M);
+}
+
+void env_chunks(const float *I, float *EC, float *EA, float *EB, int64_t N, int64_t M, int C, float beta, float u_r,
+                cudaStream_t s)
+{
+    count_launches(1);
+    k_env_chunk<<<dim3(nblk(N), (unsigned)M), kBlock, 0, s>>>(I, EC, EA, EB, N, C, beta, u_r);
 }
 
 void grid_build(const float *I, const float *u0, FwdMaps &mp, int64_t M, int64_t N, int C, int K, float beta,
@@ -427,17 +467,17 @@ void grid_carry(const float *I, const float *u0, const float *MA, const float *M
 }
 
 void grid_compose(const FwdMaps &mp, const SuperMaps &sp, const float *u0, int64_t M2, int64_t N, int G,
-                  int K, int K2, float theta, float u_r, lifb_stats *st, cudaStream_t s)
+                  int K, int K2, float theta, float u_r, lifb_stats *st, cudaStream_t s, int64_t lo_stride)
 {
     dim3 g(nblk(N), (unsigned)M2);
     int km = K2 <= 2 ? 2 : K2 <= 4 ? 4 : K2 <= 8 ? 8 : K2 <= 16 ? 16 : K2 <= 32 ? 32 : 64;
     switch (km) {
-    case 2: launch_compose<2>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st); break;
-    case 4: launch_compose<4>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st); break;
-    case 8: launch_compose<8>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st); break;
-    case 16: launch_compose<16>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st); break;
-    case 32: launch_compose<32>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st); break;
-    default: launch_compose<64>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st); break;
+    case 2: launch_compose<2>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st, lo_stride); break;
+    case 4: launch_compose<4>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st, lo_stride); break;
+    case 8: launch_compose<8>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st, lo_stride); break;
+    case 16: launch_compose<16>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st, lo_stride); break;
+    case 32: launch_compose<32>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st, lo_stride); break;
+    default: launch_compose<64>(g, s, mp, sp, u0, N, G, K, K2, theta, u_r, st, lo_stride); break;
     }
 }
 

@@ -187,6 +187,55 @@ int lifb_scan_fwd_v3_noalloc(const float *I, const float *u0, float *U, float *S
                              int64_t T, int64_t N, float beta, float theta, float u_r,
                              int C, int K, int max_repair, lifb_stats *stats_dev, void *stream);
 
+/* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
+ * The reference scans one sequence on one device (lifscan/triton_lif.py:
+ * 944-983, scan_forward_v4; :512-526, scan_backward_tiled).  These phases
+ * split [T_total, N] into P slices of T rows; the caller exchanges the small
+ * per-slice results (all-gather over ranks) between phases.  Every pointer is
+ * device memory of the calling GPU; `ws` comes from the *_workspace_bytes
+ * query with the same sizes.  I/U/S/GS/Lam are the slice's [T, N] rows.
+ *
+ * Forward: envelope -> all-gather envs [P][3][N] -> slice_map -> all-gather
+ * maps [P][4 + 2*K3][N] -> apply -> repeat { all-gather ends; repair from
+ * the previous slice's end } until no slice end changes.
+ * Backward: bwd -> all-gather lam_pq [P][2][N] -> lam_top = fold of the later
+ * slices' (q, p) -> bwd_fix.  Forward U/S are bit-identical to the serial
+ * recurrence over T_total rows; Lam equals its adjoint within rounding. */
+size_t lifb_tshard_workspace_bytes(int64_t T, int64_t N, int C, int G, int K, int K2);
+/* env[3][N] = the slice's envelope map (c, a, b): l -> min(c, a*l + b). */
+int lifb_tshard_envelope(const float *I, int64_t T, int64_t N, int C, int G, int K, int K2,
+                         float beta, float u_r, float *env, void *ws, size_t bytes, void *stream);
+/* map[4 + 2*K3][N] = the slice's composed map (A, B, count, overflow,
+ * breakpoints, constants), pruned with the entry bound folded from envs of
+ * slices 0..rank-1 (envs: [P][3][N], gathered).  Reuses the chunk envelopes
+ * that lifb_tshard_envelope left in ws, and leaves the slice's super maps
+ * there for lifb_tshard_apply. */
+int lifb_tshard_slice_map(const float *I, const float *envs, int rank, const float *u0, int64_t T,
+                          int64_t N, float beta, float theta, float u_r, int C, int G, int K, int K2,
+                          int K3, float *map, void *ws, size_t bytes, void *stream);
+/* entry[N] = u0 through maps of slices 0..rank-1; U, S, end[N] (U's last row)
+ * from that entry, with the super maps of the slice_map call on the same ws. */
+int lifb_tshard_apply(const float *I, const float *maps, int rank, int K3, const float *u0,
+                      float *entry, float *U, float *S, float *end, int64_t T, int64_t N, float beta,
+                      float theta, float u_r, int C, int G, int K, int K2, void *ws, size_t bytes,
+                      void *stream);
+/* Replays from a new entry[N] until the rows rejoin U/S; changed[n] = 1 and
+ * end[n] updated where they never rejoin. */
+int lifb_tshard_repair(const float *I, const float *entry, float *U, float *S, float *end,
+                       int32_t *changed, int64_t T, int64_t N, float beta, float theta, float u_r,
+                       void *stream);
+size_t lifb_tshard_bwd_workspace_bytes(int64_t T, int64_t N, int C);
+/* Detached-reset adjoint of the slice with lam = 0 entering from above;
+ * u_prev[N] = U of the row before the slice (u0 on the first slice).
+ * lam_pq[2][N] = (q, p): lam at row 0 = q + p * lam entering from above. */
+int lifb_tshard_bwd(const float *I, const float *u_prev, const float *U, const float *GS, float *Lam,
+                    float *lam_pq, int64_t T, int64_t N, float beta, float theta, float u_r,
+                    float alpha, int C, void *ws, size_t bytes, void *stream);
+/* Lam made exact for lam_top[N] entering from the next slice (after bwd, same ws). */
+int lifb_tshard_bwd_fix(const float *I, const float *u_prev, const float *U, const float *GS,
+                        const float *lam_top, float *Lam, int64_t T, int64_t N, float beta,
+                        float theta, float alpha, int C, void *ws, size_t bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
