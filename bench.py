@@ -44,6 +44,9 @@ BWD_BYTES = 16
 METRIC = "neuron-steps/s, lif_tuned fwd+bwd (B*N=16384/GPU, T=1024)"
 UNIT = "neuron-steps/s"
 FALLBACK_HBM_GBS = 6650.0
+C4_T, C4_N, C4_MU, C4_SD = 1 << 20, 1024, 0.02, 0.1
+C4_METRIC = "neuron-steps/s, fwd+bwd of one sequence (B*N=1024, T=2^20)"
+C4_WORKLOAD = "c4: T=2^20, B*N=1024, beta=0.99, x~N(0.02,0.1^2), forward + backward"
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -58,8 +61,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--workload", default="c2", choices=("c2", "c3"),
-                   help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step")
+    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4"),
+                   help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step; "
+                        "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs")
     return p.parse_args()
 
 
@@ -144,28 +148,26 @@ class ClockSampler:
                 "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
 
 
-def cpu_oracle_rate(T, N, seconds, want_bwd=True):
+def cpu_oracle_rate(T, N, seconds, want_bwd=True, mu=MU, sd=SD, beta=BETA):
     """Reference CPU path (C restatement of lifscan/fast.py serial forward +
     adjoint) on all host threads; repeats the full workload until `seconds`
     have elapsed (at least once).  Returns (neuron-steps/s, threads, sample)."""
-    import numpy as np
     from oracle import oracle as O
     O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
-    I, u0, GS = O.gen_inputs(T, N, MU, SD, seed=0, grad=True)
+    I, u0, GS = O.gen_inputs(T, N, mu, sd, seed=0, grad=True)
     threads = O.num_threads()
-    O.serial_forward(I[:64], BETA, 1.0, 0.0, u0)  # warm the library
+    O.serial_forward(I[:64], beta, 1.0, 0.0, u0)  # warm the library
     done = 0
     t0 = time.perf_counter()
     while True:
-        U, S = O.serial_forward(I, BETA, 1.0, 0.0, u0)
+        U, S = O.serial_forward(I, beta, 1.0, 0.0, u0)
         if want_bwd:
-            O.serial_backward(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0, True)
+            O.serial_backward(I, u0, U, S, GS, None, beta, 1.0, 0.0, 4.0, True)
         done += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    del np
-    return done * T * N / el, threads, f"{done} x full workload (T={T}, N={N}) in {el:.1f} s"
+    return done * T * N / el, threads, f"{done} x T={T}, N={N} (serial forward + adjoint) in {el:.1f} s"
 
 
 def run_reference(args, ws, rank):
@@ -173,31 +175,179 @@ def run_reference(args, ws, rank):
         return
     from oracle import oracle as O
     O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
-    T, N = T_STEPS, N_PER_GPU
-    I, u0, GS = O.gen_inputs(T, N, MU, SD, seed=0, grad=True)
+    if args.workload == "c4":
+        # bounded sample of config 4: the first 2^17 of its 2^20 rows, all 1024 neurons
+        T, N, mu, sd, beta = 1 << 17, C4_N, C4_MU, C4_SD, BETA
+        metric, scaling = C4_METRIC, "strong"
+        workload = C4_WORKLOAD
+        sample = f"first {T} of {C4_T} rows per step (N={N}), serial forward + adjoint"
+    else:
+        T, N, mu, sd, beta = T_STEPS, N_PER_GPU, MU, SD, BETA
+        metric, scaling = METRIC, "weak"
+        workload = "c2: lif_tuned fwd+bwd, B*N=16384, T=1024, beta=0.99, x~N(0.05,0.2^2)"
+        sample = f"full workload per step (T={T}, N={N}), serial forward + adjoint"
+    I, u0, GS = O.gen_inputs(T, N, mu, sd, seed=0, grad=True)
     for _ in range(max(args.warmup, 0)):
-        U, S = O.serial_forward(I, BETA, 1.0, 0.0, u0)
-        O.serial_backward(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0, True)
+        U, S = O.serial_forward(I, beta, 1.0, 0.0, u0)
+        O.serial_backward(I, u0, U, S, GS, None, beta, 1.0, 0.0, 4.0, True)
     ts = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        U, S = O.serial_forward(I, BETA, 1.0, 0.0, u0)
-        O.serial_backward(I, u0, U, S, GS, None, BETA, 1.0, 0.0, 4.0, True)
+        U, S = O.serial_forward(I, beta, 1.0, 0.0, u0)
+        O.serial_backward(I, u0, U, S, GS, None, beta, 1.0, 0.0, 4.0, True)
         ts.append(time.perf_counter() - t0)
     ms = 1e3 * sum(ts) / len(ts)
     value = N * T / (ms / 1e3)
     cores = O.num_threads()
-    sample = f"full workload per step (T={T}, N={N}), serial forward + adjoint"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": metric, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "c2: lif_tuned fwd+bwd, B*N=16384, T=1024, beta=0.99, x~N(0.05,0.2^2)",
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload,
                    "path": "CPU oracle port of lifscan/fast.py serial_forward_nograd + serial_backward"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_long(args, ws, rank, local):
+    """Config 4: one sequence of T = 2^20 rows, B*N = 1024 neurons,
+    x ~ N(0.02, 0.1^2), beta = 0.99, forward + backward (spikes out, upstream
+    gradient N(0, 1) on the spikes).  One GPU: lif_tuned (mode "scan", the
+    library's long-sequence policy).  N GPUs: lif_tshard, rank r owning rows
+    [r*T/N, (r+1)*T/N) (strong scaling: the total work is fixed), with the
+    all-gathers of the time-sharded protocol over NCCL."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200 import lifscan as L
+    from hard_resets_compose_b200 import tshard
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+    N, T = C4_N, C4_T // ws
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    I = (C4_MU + C4_SD * torch.randn(T, N, generator=g, device=dev)).float()
+    GS = torch.randn(T, N, generator=g, device=dev).float()
+    u0 = torch.zeros(N, device=dev)
+    Iq = I.clone().requires_grad_(True)
+    stream = torch.cuda.current_stream(dev)
+    comm = tshard.TorchComm() if ws > 1 else None
+    ops = tshard.CudaSliceOps(T, N, dev, BETA, 1.0, 0.0) if ws > 1 else None
+
+    def lif(x, u):
+        if ws > 1:
+            return tshard.lif_tshard(x, u, beta=BETA, ops=ops, comm=comm)
+        return L.lif_tuned(x, u, beta=BETA, mode="scan")
+
+    def step(x=Iq, G=GS, mid=None):
+        x.grad = None
+        S = lif(x, u0)
+        if mid is not None:
+            mid.record(stream)
+        torch.autograd.backward(S, G)
+        return S
+
+    def max_over_ranks(v):
+        if ws == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    steps = args.steps
+    evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    n0 = lib.lifb_kernel_launches()
+    with ClockSampler(local) as clk:
+        for a, m, b in evs:
+            a.record(stream)
+            step(mid=m)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+    launches = lib.lifb_kernel_launches() - n0
+    barrier()
+    ms = max_over_ranks(sum(a.elapsed_time(b) for a, _, b in evs) / steps)
+    ms_f = max_over_ranks(sum(a.elapsed_time(m) for a, m, _ in evs) / steps)
+    ms_b = max_over_ranks(sum(m.elapsed_time(b) for _, m, b in evs) / steps)
+    units = C4_T * N
+    value = units / (ms / 1e3)
+    hbm, peak_kind = peaks()
+    # algorithmic bytes of this rank's rows: forward 12 B, backward 16 B per neuron-step
+    fwd_gbs = FWD_BYTES * T * N / (ms_f / 1e3) / 1e9
+    bwd_gbs = BWD_BYTES * T * N / (ms_b / 1e3) / 1e9
+    dom = ("fwd", ms_f, fwd_gbs, FWD_BYTES) if ms_f >= ms_b else ("bwd", ms_b, bwd_gbs, BWD_BYTES)
+    roofline = {"bound": "hbm", "kernel": f"{dom[0]} phase of the step (all its launches)", "achieved": dom[2],
+                "peak": hbm, "peak_source": peak_kind, "unit": "GB/s", "frac": dom[2] / hbm, "traffic": None,
+                "algorithmic_bytes": dom[3] * T * N,
+                "step_frac": (FWD_BYTES + BWD_BYTES) * T * N / (ms / 1e3) / 1e9 / hbm}
+
+    e2e = None
+    if not args.no_e2e:
+        I_p = I.cpu().pin_memory()
+        G_p = GS.cpu().pin_memory()
+        S_p = torch.empty(T, N).pin_memory()
+        dI_p = torch.empty(T, N).pin_memory()
+
+        def e2e_step():
+            Id = I_p.to(dev, non_blocking=True).requires_grad_(True)
+            Gd = G_p.to(dev, non_blocking=True)
+            S_ = step(Id, Gd)
+            S_p.copy_(S_.detach(), non_blocking=True)
+            dI_p.copy_(Id.grad, non_blocking=True)
+        e2e_step()
+        n_e = max(min(steps, 3), 1)
+        ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_e)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        for a, b in ee:
+            a.record(stream)
+            e2e_step()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms_e = max_over_ranks(sum(a.elapsed_time(b) for a, b in ee) / n_e)
+        e2e = {"value": units / (ms_e / 1e3), "unit": UNIT, "ms_per_step": ms_e,
+               "h2d_bytes_per_step": 2 * T * N * 4 * ws, "d2h_bytes_per_step": 2 * T * N * 4 * ws,
+               "api": "pinned host slices -> .to(cuda) -> lif_tshard / lif_tuned + autograd.backward -> S, dI "
+                      "copied back (all ranks)"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        v, threads, sample = cpu_oracle_rate(1 << 17, N, args.cpu_seconds, mu=C4_MU, sd=C4_SD)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": sample + f" (the first 2^17 of the {C4_T} rows)"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": C4_METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded CUDA torch.Generator, config 4 shape)",
+            "config": {"workload": C4_WORKLOAD, "seq_len": C4_T, "neurons": N,
+                       "parallelism": f"time-sharded x{ws} (NCCL all-gathers)" if ws > 1 else "one GPU",
+                       "path": "lif_tshard (entry_mode='speculate')" if ws > 1 else "lif_tuned(mode='scan')",
+                       "forward_segments": list(L.spec_segment(T, N)),
+                       "l2": "inputs (4 GiB per tensor / N) larger than L2"},
+            "fwd": {"ms": ms_f, "gbs": fwd_gbs, "frac": fwd_gbs / hbm},
+            "bwd": {"ms": ms_b, "gbs": bwd_gbs, "frac": bwd_gbs / hbm},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clk.record()}), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_network(args, ws, rank, local):
@@ -307,6 +457,9 @@ def main():
         return
     if args.workload == "c3":
         run_network(args, ws, rank, local)
+        return
+    if args.workload == "c4":
+        run_long(args, ws, rank, local)
         return
 
     import torch

@@ -50,6 +50,9 @@ SIGNATURES = {
     "lifb_scan_bwd_workspace_bytes": ([c_i64, c_i64, c_int], c_size_t),
     "lifb_scan_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
                        c_float, c_float, c_float, c_float, c_int, c_int, c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_scan_fwd_spec_workspace_bytes": ([c_i64, c_i64, c_i64], c_size_t),
+    "lifb_scan_fwd_spec": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float, c_i64,
+                            c_i64, c_void_p, c_i64, c_void_p, c_size_t, c_void_p], c_int),
     "lifb_tshard_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
     "lifb_tshard_envelope": ([c_void_p, c_i64, c_i64, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p], c_int),

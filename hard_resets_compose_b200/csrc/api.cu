@@ -333,12 +333,13 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
     w.P = c.take<float>(M * N);
     w.Q = c.take<float>(M * N);
     w.LamEnd = c.take<float>(M * N);
+    int32_t *D = reinterpret_cast<int32_t *>(w.LamEnd);  // the fast path needs no LamEnd
     if (detach &&
         lifb::bwd_tma(0, I, u0, U, S, GS, GU, nullptr, Lam, w.P, w.Q, T, N, C, beta, theta, u_r, alpha, true,
-                      (cudaStream_t)stream)) {
+                      (cudaStream_t)stream, D)) {
         // Detached reset: every chunk replayed from lam_end = 0 is exact at and
-        // below its last spike; the fix-up recomputes only the rows above it.
-        lifb::bwd_fixup(I, u0, U, S, GS, GU, w.P, w.Q, Lam, N, M, C, beta, theta, alpha, (cudaStream_t)stream);
+        // below its last spike; the fix-up corrects only the rows above it.
+        lifb::bwd_fixup(I, u0, U, S, GS, GU, w.P, w.Q, D, Lam, N, M, C, beta, theta, alpha, (cudaStream_t)stream);
         return check_launch("lifb_scan_bwd");
     }
     lifb::grid_scan_bwd(I, u0, U, S, GS, GU, Lam, w, T, N, C, beta, theta, u_r, alpha, detach != 0,

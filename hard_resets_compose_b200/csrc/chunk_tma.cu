@@ -263,8 +263,8 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                                                 const __grid_constant__ CUtensorMap tLam,
                                                 const float *__restrict__ u0, const float *__restrict__ LamEnd,
                                                 float *__restrict__ Lam, float *__restrict__ P, float *__restrict__ Q,
-                                                int64_t N, int64_t C, float beta, float theta, float u_r, float alpha,
-                                                bool detach, int *status)
+                                                int32_t *__restrict__ D, int64_t N, int64_t C, float beta, float theta,
+                                                float u_r, float alpha, bool detach, int *status)
 {
     using Ly = BwdLayout<READ_S, HAS_GU>;
     constexpr int NB = 32 * NPL;
@@ -311,8 +311,11 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
     const int64_t nl = n0 + NPL * lane;
     const bool act = nl < N;
     Vec<NPL> uz, lam, pp;
+    // dn: rows, counted from the chunk's last row, whose running product of a
+    // is still nonzero (the rows a lam entering from above changes)
+    int dn[NPL];
 #pragma unroll
-    for (int i = 0; i < NPL; i++) { uz.v[i] = 0.f; lam.v[i] = 0.f; pp.v[i] = 1.f; }
+    for (int i = 0; i < NPL; i++) { uz.v[i] = 0.f; lam.v[i] = 0.f; pp.v[i] = 1.f; dn[i] = 0; }
     if (act) {
         uz = ld_vec<NPL>(u0 + nl);
         if (MODE == kReplay && LamEnd) lam = ld_vec<NPL>(LamEnd + m * N + nl);
@@ -336,6 +339,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
             }
+            const Vec<NPL> pp_in = pp;
 #pragma unroll
             for (int rr = R - 1; rr >= 0; rr--) {
 #pragma unroll
@@ -344,6 +348,19 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                     pp.v[i] = av[rr].v[i] * pp.v[i];
                 }
                 if (MODE == kReplay) st_vec<NPL>(ol + rr * NB + NPL * lane, lam);
+            }
+#pragma unroll
+            for (int i = 0; i < NPL; i++) {
+                if (pp.v[i] != 0.f) {
+                    dn[i] += R;
+                } else if (pp_in.v[i] != 0.f) {  // the product reached 0 in this tile: find the row
+                    float q = pp_in.v[i];
+                    for (int rr = R - 1; rr >= 0; rr--) {
+                        q = av[rr].v[i] * q;
+                        if (q == 0.f) break;
+                        dn[i]++;
+                    }
+                }
             }
             if (MODE == kReplay) {
                 fence_proxy_async_shared();
@@ -359,6 +376,8 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                 if (t < cstart) break;
                 bwd_step<NPL, READ_S, HAS_GU, MODE>(b, kTile, rr * NB + NPL * lane, t == 0 ? &uz : nullptr, lam, pp,
                                                     beta, theta, u_r, alpha, detach);
+#pragma unroll
+                for (int i = 0; i < NPL; i++) dn[i] += pp.v[i] != 0.f ? 1 : 0;
                 if (MODE == kReplay && act) st_vec<NPL>(Lam + t * N + nl, lam);
             }
         }
@@ -371,6 +390,10 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
     if (ok && P && act) {
         st_vec<NPL>(P + m * N + nl, pp);
         st_vec<NPL>(Q + m * N + nl, lam);
+        if (D) {
+#pragma unroll
+            for (int i = 0; i < NPL; i++) D[m * N + nl + i] = dn[i];
+        }
     }
     if (MODE == kReplay && lane == 0) bulk_wait_all();
 }
@@ -480,7 +503,7 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
 
 template <int NPL, bool READ_S, bool HAS_GU, int MODE>
 static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *LamEnd, float *Lam, float *P, float *Q,
-                       int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
+                       int32_t *D, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
                        bool detach, int *status, cudaStream_t s)
 {
     constexpr int NB = 32 * NPL;
@@ -491,27 +514,27 @@ static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *La
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
-    kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], u0, LamEnd, Lam, P, Q, N, C, beta,
-                             theta, u_r, alpha, detach, status);
+    kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], u0, LamEnd, Lam, P, Q, D, N, C,
+                             beta, theta, u_r, alpha, detach, status);
 }
 
 template <int NPL, int MODE>
 static void launch_bwd_v(bool read_s, bool has_gu, const CUtensorMap *maps, const float *u0, const float *LamEnd,
-                         float *Lam, float *P, float *Q, int64_t N, int64_t M, int64_t C, float beta, float theta,
-                         float u_r, float alpha, bool detach, int *status, cudaStream_t s)
+                         float *Lam, float *P, float *Q, int32_t *D, int64_t N, int64_t M, int64_t C, float beta,
+                         float theta, float u_r, float alpha, bool detach, int *status, cudaStream_t s)
 {
     if (read_s) {
-        if (has_gu) launch_bwd<NPL, true, true, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd<NPL, true, false, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        if (has_gu) launch_bwd<NPL, true, true, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd<NPL, true, false, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     } else {
-        if (has_gu) launch_bwd<NPL, false, true, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd<NPL, false, false, MODE>(maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        if (has_gu) launch_bwd<NPL, false, true, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd<NPL, false, false, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     }
 }
 
 bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const float *S, const float *GS,
              const float *GU, const float *LamEnd, float *Lam, float *P, float *Q, int64_t T, int64_t N, int64_t C,
-             float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s)
+             float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s, int32_t *D)
 {
     const void *p[] = {I, u0, U, S, GS, GU, LamEnd, Lam, P, Q};
     if (!tma_ok(p, 10, N) || C <= 0 || T % C) return false;
@@ -534,11 +557,11 @@ bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const fl
     int *status = device_status_ptr();
     const bool rs = S != nullptr, g = GU != nullptr;
     if (mode == kReplay) {
-        if (npl == 4) launch_bwd_v<4, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd_v<1, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        if (npl == 4) launch_bwd_v<4, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd_v<1, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     } else {
-        if (npl == 4) launch_bwd_v<4, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd_v<1, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        if (npl == 4) launch_bwd_v<4, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd_v<1, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     }
     return true;
 }

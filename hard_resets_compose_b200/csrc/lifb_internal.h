@@ -44,9 +44,12 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
 // Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0)
 // and, when P is given, also the chunk maps; mode 1 writes only P, Q.
 // P[m] = prod of a_t over chunk m, Q[m] = lam at the chunk's first row.
+// D (optional, with P): per chunk and neuron, the rows counted from the
+// chunk's last row whose running product of a is nonzero, i.e. the rows that
+// a lam entering the chunk from above changes.
 bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const float *S, const float *GS,
              const float *GU, const float *LamEnd, float *Lam, float *P, float *Q, int64_t T, int64_t N, int64_t C,
-             float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s);
+             float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s, int32_t *D = nullptr);
 
 // serial.cu
 void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
@@ -78,6 +81,16 @@ void grid_replay_repair(const float *I, const float *u0, FwdMaps &mp, float *U, 
                         int C, int max_repair, float beta, float theta, float u_r, lifb_stats *st,
                         cudaStream_t s);
 
+// Replay of T/L segments of L rows from Starts (TMA kernel, or the plain
+// kernel when the TMA path does not apply); writes U, S and Ends [T/L, N].
+void replay_any(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends, int64_t T,
+                int64_t N, int64_t L, float beta, float theta, float u_r, cudaStream_t s);
+
+// scan_spec.cu: Starts[s] of NS segments of L rows guessed by a W-row lead-in
+// from u_r (Starts[0] = u0; lead-ins that reach row 0 start from u0).
+void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts, int64_t N,
+                   int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r, cudaStream_t s);
+
 // host_pipeline.cu
 size_t host_pipe_workspace_bytes(int64_t T, int64_t N, int64_t block_n);
 int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float *S_h, float *dI_h, float *du0_h,
@@ -103,8 +116,8 @@ void entry_repair(const float *I, const float *entry, float *U, float *S, float 
                   int64_t N, float beta, float theta, float u_r, cudaStream_t s);
 // Lam fix-up given the lam entering the slice from above (lam_top, per neuron).
 void bwd_fixup_top(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,
-                   const float *P, const float *Q, const float *lam_top, float *Lam, int64_t N, int64_t M, int64_t C,
-                   float beta, float theta, float alpha, cudaStream_t s);
+                   const float *P, const float *Q, const int32_t *D, const float *lam_top, float *Lam, int64_t N,
+                   int64_t M, int64_t C, float beta, float theta, float alpha, cudaStream_t s);
 
 // carry_tma.cu: envelope prefix with TMA-staged (c, a, b) windows.
 bool env_carry_staged(const float *u0, const float *EC, const float *EA, const float *EB, float *Lo, int64_t N,
@@ -115,9 +128,12 @@ bool env_carry_staged(const float *u0, const float *EC, const float *EA, const f
 void fwd_fixup(const float *I, const float *Starts, int64_t start_stride, float *U, float *S, float *Ends,
                float *EndsNew, int32_t *Changed, int64_t N, int64_t NS, int64_t L, float beta, float theta, float u_r,
                int *longest_chain, cudaStream_t s);
+// With D (from bwd_tma) the rows above each chunk's last spike, where every
+// a is exactly beta (detached reset), are corrected in place by
+// lam_end * beta^k instead of being recomputed from I, U and GS.
 void bwd_fixup(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,
-               const float *P, const float *Q, float *Lam, int64_t N, int64_t M, int64_t C, float beta, float theta,
-               float alpha, cudaStream_t s);
+               const float *P, const float *Q, const int32_t *D, float *Lam, int64_t N, int64_t M, int64_t C,
+               float beta, float theta, float alpha, cudaStream_t s);
 
 // scan_bwd.cu
 struct BwdScratch {

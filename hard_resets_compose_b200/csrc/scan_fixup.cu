@@ -192,6 +192,7 @@ __global__ void __launch_bounds__(kFixBlock) k_bwd_fixup(const float *__restrict
                                                          const float *__restrict__ U, const float *__restrict__ S,
                                                          const float *__restrict__ GS, const float *__restrict__ GU,
                                                          const float *__restrict__ P, const float *__restrict__ Q,
+                                                         const int32_t *__restrict__ D,
                                                          const float *__restrict__ lam_top, float *__restrict__ Lam,
                                                          int64_t N, int64_t M, int64_t C, float beta, float theta,
                                                          float alpha)
@@ -213,6 +214,28 @@ __global__ void __launch_bounds__(kFixBlock) k_bwd_fixup(const float *__restrict
         for (int64_t i = e - 1; i > m; i--) lam = Q[i * N + n] + P[i * N + n] * lam;
     }
     if (lam == 0.0f) return;  // the replay's lam_end = 0 was already right
+    if (D) {
+        // rows above the chunk's last spike: a = beta exactly, so the replay's
+        // rows differ from the exact ones by lam_end * beta^k (k = 1 at the
+        // chunk's last row); rows at and below the spike are already exact
+        const int64_t d = D[m * N + n];
+        constexpr int kB = 16;
+        float f = lam;
+        for (int64_t k0 = 0; k0 < d && f != 0.0f; k0 += kB) {
+            float l[kB];
+#pragma unroll
+            for (int q = 0; q < kB; q++)
+                if (k0 + q < d) l[q] = Lam[((m + 1) * C - 1 - k0 - q) * N + n];
+#pragma unroll
+            for (int q = 0; q < kB; q++) {
+                if (k0 + q < d) {
+                    f = beta * f;
+                    Lam[((m + 1) * C - 1 - k0 - q) * N + n] = l[q] + f;
+                }
+            }
+        }
+        return;
+    }
     const float un0 = u0[n];
     constexpr int kB = 8;  // rows loaded ahead of the dependent chain
     bool running = true;
@@ -258,22 +281,22 @@ void fwd_fixup(const float *I, const float *Starts, int64_t start_stride, float 
 }
 
 void bwd_fixup(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,
-               const float *P, const float *Q, float *Lam, int64_t N, int64_t M, int64_t C, float beta, float theta,
-               float alpha, cudaStream_t s)
+               const float *P, const float *Q, const int32_t *D, float *Lam, int64_t N, int64_t M, int64_t C,
+               float beta, float theta, float alpha, cudaStream_t s)
 {
     if (M < 2) return;
     count_launches(1);
     dim3 g((unsigned)((N + kFixBlock - 1) / kFixBlock), (unsigned)(M - 1));
-    k_bwd_fixup<<<g, kFixBlock, 0, s>>>(I, u0, U, S, GS, GU, P, Q, nullptr, Lam, N, M, C, beta, theta, alpha);
+    k_bwd_fixup<<<g, kFixBlock, 0, s>>>(I, u0, U, S, GS, GU, P, Q, D, nullptr, Lam, N, M, C, beta, theta, alpha);
 }
 
 void bwd_fixup_top(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,
-                   const float *P, const float *Q, const float *lam_top, float *Lam, int64_t N, int64_t M, int64_t C,
-                   float beta, float theta, float alpha, cudaStream_t s)
+                   const float *P, const float *Q, const int32_t *D, const float *lam_top, float *Lam, int64_t N,
+                   int64_t M, int64_t C, float beta, float theta, float alpha, cudaStream_t s)
 {
     count_launches(1);
     dim3 g((unsigned)((N + kFixBlock - 1) / kFixBlock), (unsigned)M);
-    k_bwd_fixup<<<g, kFixBlock, 0, s>>>(I, u0, U, S, GS, GU, P, Q, lam_top, Lam, N, M, C, beta, theta, alpha);
+    k_bwd_fixup<<<g, kFixBlock, 0, s>>>(I, u0, U, S, GS, GU, P, Q, D, lam_top, Lam, N, M, C, beta, theta, alpha);
 }
 
 }  // namespace lifb

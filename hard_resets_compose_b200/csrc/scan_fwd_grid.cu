@@ -491,6 +491,15 @@ void grid_carry_inner(const float *I, const FwdMaps &mp, const float *SStarts, i
                                                                 u_r);
 }
 
+void replay_any(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends, int64_t T,
+                int64_t N, int64_t L, float beta, float theta, float u_r, cudaStream_t s)
+{
+    if (fwd_replay_tma(I, u0, Starts, U, S, Ends, T, N, L, beta, theta, u_r, s)) return;
+    count_launches(1);
+    k_replay<<<dim3(nblk(N), (unsigned)(T / L)), kBlock, 0, s>>>(I, Starts, U, S, Ends, N, (int)L, beta, theta,
+                                                                u_r);
+}
+
 void grid_replay_repair(const float *I, const float *u0, FwdMaps &mp, float *U, float *S, int64_t T, int64_t N,
                         int C, int max_repair, float beta, float theta, float u_r, lifb_stats *st,
                         cudaStream_t s)

@@ -1,0 +1,144 @@
+// Speculative segment forward for long sequences with few neurons.
+//
+// The serial recurrence over T rows for N neurons has N independent chains;
+// when N is small (config 4: N = 1024 on 148 SMs) one pass cannot fill the GPU
+// and runs at the latency of one dependent step per row.  Hard resets make a
+// trajectory forget its start: two trajectories of the same neuron driven by
+// the same input end up bit-identical once they spike in the same row (or
+// their difference rounds away), typically within a few hundred rows.  So:
+//
+//   k_leadin  the start of each segment of L rows, guessed by running the W rows
+//             before it from u_r ("just reset"); segment 0 starts from u0, and
+//             a lead-in that reaches row 0 starts from u0 too (then it is exact).
+//             With a halo (rows before row 0, e.g. the end of the previous
+//             time slice), segment 0 starts from u0 run through the halo.
+//   replay    every segment from its guessed start (k_fwd_tma: TMA-staged rows,
+//             TMA-store epilogue), all segments at once
+//   fix-up    per neuron, in time order, every segment whose guessed start
+//             differs bit for bit from the previous segment's exact end is
+//             replayed from that end until its rows rejoin (scan_fixup.cu)
+//
+// U and S equal the serial recurrence bit for bit whatever the guesses were;
+// the guesses decide only how much the fix-up replays.  The map scan of the
+// reference (lifscan/triton_lif.py:782-983) computes exact segment starts
+// instead; this path trades its map build for a W-row lead-in.
+#include "lifb_common.cuh"
+#include "lifb_internal.h"
+
+namespace lifb {
+
+constexpr int kLeadBlock = 128;
+constexpr int kLeadB = 16;  // rows loaded one batch ahead of the dependent chain
+
+// Starts[s] for segment s.  Segment 0 starts from u0, or, when a halo of
+// W_halo rows before row 0 is given, from u0 run through the halo.
+__global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__ I, const float *__restrict__ u0,
+                                                       const float *__restrict__ I_halo, int64_t W_halo,
+                                                       float *__restrict__ Starts, int64_t N, int64_t L, int64_t W,
+                                                       float beta, float theta, float u_r)
+{
+    const int64_t n = (int64_t)blockIdx.x * kLeadBlock + threadIdx.x;
+    const int64_t s = blockIdx.y;
+    if (n >= N) return;
+    const float *p;
+    int64_t len;
+    float u;
+    if (s == 0) {
+        u = u0[n];
+        if (!I_halo || W_halo <= 0) {
+            Starts[n] = u;
+            return;
+        }
+        p = I_halo + n;
+        len = W_halo;
+    } else {
+        const int64_t t1 = s * L;
+        int64_t t0 = t1 - W;
+        u = u_r;
+        if (t0 <= 0) {
+            t0 = 0;
+            u = u0[n];
+        }
+        p = I + t0 * N + n;
+        len = t1 - t0;
+    }
+    float cur[kLeadB], nxt[kLeadB];
+#pragma unroll
+    for (int q = 0; q < kLeadB; q++) cur[q] = q < len ? __ldg(p + q * N) : 0.0f;
+    for (int64_t b = 0; b < len; b += kLeadB) {
+        const int64_t nb = b + kLeadB;
+#pragma unroll
+        for (int q = 0; q < kLeadB; q++) nxt[q] = nb + q < len ? __ldg(p + (nb + q) * N) : 0.0f;
+#pragma unroll
+        for (int q = 0; q < kLeadB; q++)
+            if (b + q < len) u = lif_step_u(u, cur[q], beta, theta, u_r);
+#pragma unroll
+        for (int q = 0; q < kLeadB; q++) cur[q] = nxt[q];
+    }
+    Starts[s * N + n] = u;
+}
+
+void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts, int64_t N,
+                   int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r, cudaStream_t s)
+{
+    count_launches(1);
+    k_leadin<<<dim3((unsigned)((N + kLeadBlock - 1) / kLeadBlock), (unsigned)NS), kLeadBlock, 0, s>>>(
+        I, u0, I_halo, W_halo, Starts, N, L, W, beta, theta, u_r);
+}
+
+}  // namespace lifb
+
+namespace {
+constexpr size_t kAl = 256;
+size_t al(size_t x) { return (x + kAl - 1) / kAl * kAl; }
+}  // namespace
+
+extern "C" {
+
+size_t lifb_scan_fwd_spec_workspace_bytes(int64_t T, int64_t N, int64_t L)
+{
+    if (T <= 0 || N <= 0 || L <= 0 || T % L) return 0;
+    const size_t one = al((size_t)(T / L) * N * 4);
+    return 4 * one;
+}
+
+int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                       float theta, float u_r, int64_t L, int64_t W, const float *I_halo, int64_t W_halo,
+                       void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (T < 0 || N < 0 || L <= 0 || W < 0 || W_halo < 0 || (T > 0 && T % L)) {
+        lifb::set_last_error("lifb_scan_fwd_spec: T must be a multiple of the segment length L > 0, W >= 0");
+        return LIFB_ERR_INVALID_ARGUMENT;
+    }
+    if (T / L > 65535) {
+        lifb::set_last_error("lifb_scan_fwd_spec: more than 65535 segments");
+        return LIFB_ERR_UNSUPPORTED;
+    }
+    if (T == 0 || N == 0) return LIFB_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t NS = T / L;
+    if (NS == 1 && (!I_halo || W_halo == 0)) {
+        lifb::serial_fwd(I, u0, U, S, T, N, beta, theta, u_r, s);
+    } else {
+        if (!workspace || (uintptr_t)workspace % kAl || workspace_bytes < lifb_scan_fwd_spec_workspace_bytes(T, N, L)) {
+            lifb::set_last_error("lifb_scan_fwd_spec: workspace missing, misaligned or too small");
+            return LIFB_ERR_WORKSPACE;
+        }
+        char *b = (char *)workspace;
+        const size_t one = al((size_t)NS * N * 4);
+        float *Starts = (float *)b, *Ends = (float *)(b + one), *EndsNew = (float *)(b + 2 * one);
+        int32_t *Changed = (int32_t *)(b + 3 * one);
+        lifb::leadin_starts(I, u0, I_halo, W_halo, Starts, N, NS, L, W, beta, theta, u_r, s);
+        lifb::replay_any(I, u0, Starts, U, S, Ends, T, N, L, beta, theta, u_r, s);
+        lifb::fwd_fixup(I, Starts, 1, U, S, Ends, EndsNew, Changed, N, NS, L, beta, theta, u_r, nullptr, s);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        lifb::set_last_error("lifb_scan_fwd_spec: launch failed");
+        return LIFB_ERR_CUDA;
+    }
+    lifb::set_last_error("");
+    return LIFB_OK;
+}
+
+}  // extern "C"

@@ -256,7 +256,7 @@ int lifb_tshard_repair(const float *I, const float *entry, float *U, float *S, f
 size_t lifb_tshard_bwd_workspace_bytes(int64_t T, int64_t N, int C)
 {
     if (T <= 0 || N <= 0 || C <= 0 || T % C) return 0;
-    return 2 * al((size_t)(T / C) * N * 4);
+    return 3 * al((size_t)(T / C) * N * 4);
 }
 
 int lifb_tshard_bwd(const float *I, const float *u_prev, const float *U, const float *GS, float *Lam, float *lam_pq,
@@ -270,9 +270,11 @@ int lifb_tshard_bwd(const float *I, const float *u_prev, const float *U, const f
         return ts_fail(LIFB_ERR_WORKSPACE, "time-sharded adjoint: workspace missing, misaligned or too small");
     cudaStream_t s = (cudaStream_t)stream;
     const int64_t M = T / C;
-    float *P = (float *)ws, *Q = (float *)((char *)ws + al((size_t)M * N * 4));
+    const size_t one = al((size_t)M * N * 4);
+    float *P = (float *)ws, *Q = (float *)((char *)ws + one);
+    int32_t *D = (int32_t *)((char *)ws + 2 * one);
     if (!lifb::bwd_tma(0, I, u_prev, U, nullptr, GS, nullptr, nullptr, Lam, P, Q, T, N, C, beta, theta, u_r, alpha,
-                       true, s))
+                       true, s, D))
         return ts_fail(LIFB_ERR_UNSUPPORTED, "time-sharded adjoint: needs N % 4 == 0 and 16-byte aligned tensors");
     const unsigned nb = (unsigned)((N + lifb::kTsBlock - 1) / lifb::kTsBlock);
     lifb::count_launches(1);
@@ -289,8 +291,10 @@ int lifb_tshard_bwd_fix(const float *I, const float *u_prev, const float *U, con
     if (!ws || (uintptr_t)ws % kAl || bytes < lifb_tshard_bwd_workspace_bytes(T, N, C))
         return ts_fail(LIFB_ERR_WORKSPACE, "time-sharded adjoint: workspace missing, misaligned or too small");
     const int64_t M = T / C;
-    const float *P = (const float *)ws, *Q = (const float *)((const char *)ws + al((size_t)M * N * 4));
-    lifb::bwd_fixup_top(I, u_prev, U, nullptr, GS, nullptr, P, Q, lam_top, Lam, N, M, C, beta, theta, alpha,
+    const size_t one = al((size_t)M * N * 4);
+    const float *P = (const float *)ws, *Q = (const float *)((const char *)ws + one);
+    const int32_t *D = (const int32_t *)((const char *)ws + 2 * one);
+    lifb::bwd_fixup_top(I, u_prev, U, nullptr, GS, nullptr, P, Q, D, lam_top, Lam, N, M, C, beta, theta, alpha,
                         (cudaStream_t)stream);
     return ts_check("lifb_tshard_bwd_fix");
 }

@@ -36,7 +36,7 @@ __all__ = [
     "state_bounds", "surrogate_grad", "_pick_C", "LIFTuned", "lif_tuned", "LIFFunction", "lif",
     "AUTO_FWD_MAX_N", "AUTO_FWD_MIN_T", "AUTO_BWD_MAX_N", "AUTO_BWD_MIN_T", "auto_modes",
     "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg", "scan_chunk_fwd", "scan_chunk_bwd",
-    "lif_tuned_host",
+    "lif_tuned_host", "scan_forward_spec", "spec_segment",
 ]
 
 _CONVERGE = -1  # max_repair value meaning "repair until converged"
@@ -238,8 +238,8 @@ def _pick_C(T, D=8):
     raise ValueError(f"T={T} needs a chunk length divisible by {D}")
 
 
-# Chunk lengths of lif_tuned's scan mode on B200, chosen from measurements
-# (profiles/scan_paths_b200.md):
+# Chunk lengths of lif_tuned's scan mode on B200, chosen from CUDA-event
+# timings of every path on a B200:
 #  * forward: the single streaming pass (one chunk, C = T: the scan's replay
 #    pass from u0) is faster than building maps at every width measured, from
 #    N = 1024 x T = 2^20 (19 ms vs 34 ms for the map scan) to N = 16384 x
@@ -273,10 +273,69 @@ def scan_chunk_bwd(T, N):
     return T if N >= SCAN_BWD_SERIAL_MIN_N else _long_chunk(T, N)
 
 
+# Speculative segment forward (lifb_scan_fwd_spec): when N neurons alone
+# cannot fill the GPU (N < SPEC_FILL, about 8 warps per SM), the sequence is
+# cut into segments of SPEC_L rows (a power of two down to SPEC_MIN_L that
+# divides T into at least two) started from SPEC_LEAD-row lead-ins and fixed
+# up exactly.  Measured on B200 at N = 1024, x ~ N(0.02, 0.1^2), beta = 0.99:
+# T = 2^20 takes 2.7 ms against 19.3 ms for the single pass, T = 2^17 0.55 ms
+# against 2.4 ms; shorter segments or lead-ins below ~2048 rows lose time
+# in the fix-up, longer lead-ins re-read more rows.
+SPEC_FILL = 8 * 148 * 32
+SPEC_L = 16384
+SPEC_MIN_L = 4096
+SPEC_LEAD = 4096
+
+
+def spec_segment(T, N):
+    """(L, W) of lif_tuned's scan forward on B200: L = T is the single pass."""
+    if N >= SPEC_FILL:
+        return T, 0
+    L = SPEC_L
+    while L >= SPEC_MIN_L and (T % L or T // L < 2):
+        L //= 2
+    if L < SPEC_MIN_L:
+        return T, 0
+    return L, min(SPEC_LEAD, L)
+
+
+def scan_forward_spec(I, beta, theta, u_r, u0, L=None, W=None, halo=None):
+    """Speculative segment forward (lifb_scan_fwd_spec) -> (U, S), identical to
+    the serial recurrence; L = segment length (T % L == 0), W = lead-in rows
+    (defaults: spec_segment).  halo [W_halo, N]: rows before row 0; u0 is then
+    the (guessed) state before the halo and the result is exact for the state
+    the halo leads to."""
+    I, u0, T, N = _prep_fwd(I, u0)
+    if halo is not None:
+        halo = _cuda_f32("halo", halo)
+        if halo.dim() != 2 or halo.shape[1] != N:
+            raise ValueError(f"halo must be [W, {N}], got {tuple(halo.shape)}")
+    U = torch.empty_like(I)
+    S = torch.empty_like(I)
+    if T == 0 or N == 0:
+        return U, S
+    Ld, Wd = spec_segment(T, N)
+    L = Ld if L is None else int(L)
+    W = Wd if W is None else int(W)
+    if L <= 0 or T % L:
+        raise ValueError(f"T={T} is not a multiple of the segment length L={L}")
+    lib = _lib.load()
+    with torch.cuda.device(I.device):
+        nb = lib.lifb_scan_fwd_spec_workspace_bytes(T, N, L)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=I.device)
+        check(lib.lifb_scan_fwd_spec(ptr(I), ptr(u0), ptr(U), ptr(S), T, N, _f(beta), _f(theta), _f(u_r), L, W,
+                                     ptr(halo), 0 if halo is None else halo.shape[0], ptr(ws), nb, stream_of(I)),
+              "scan_forward_spec")
+    return U, S
+
+
 def scan_forward_auto(I, beta, theta, u_r, u0, K=16, repair=0):
-    """lifscan/triton_lif.py:1228-1232 with a B200 chunk choice (scan_chunk_fwd).
-    Outputs are identical for every chunk length (exact after repair)."""
+    """lifscan/triton_lif.py:1228-1232 with a B200 path choice: the single
+    streaming pass, or the speculative segment forward when N is too small to
+    fill the GPU (spec_segment).  Outputs are identical either way (exact)."""
     T, N = I.shape
+    if T > 0 and N > 0 and spec_segment(T, N)[0] < T:
+        return scan_forward_spec(I, beta, theta, u_r, u0)
     return scan_forward_v3(I, beta, theta, u_r, u0, C=scan_chunk_fwd(T, N), K=K, repair=repair)
 
 

@@ -5,7 +5,7 @@ lifscan/triton_lif.py:944-983; scan_backward_tiled, :512-526).  Here rank r
 of a process group owns rows [r*T, (r+1)*T) of a [P*T, N] sequence and the
 ranks exchange only small per-neuron summaries with all-gathers:
 
-forward
+forward (entry_mode "maps"; "speculate" replaces steps 1-3, see tshard_forward)
   1. envelope   each slice's envelope map l -> min(c, a*l + b)        3 floats
   2. slice map  each slice composed into one pruned piecewise map,
                 pruned with the entry bound folded from the envelopes   4 + 2*K3 floats
@@ -58,6 +58,22 @@ class TorchComm:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
 
+    def shift(self, t):
+        """t of rank r-1 on rank r (rank 0 receives None); every rank sends
+        its t to rank r+1."""
+        t = t.contiguous()
+        ops = []
+        if self.rank + 1 < self.world:
+            ops.append(dist.P2POp(dist.isend, t, self.rank + 1, group=self.group))
+        buf = None
+        if self.rank > 0:
+            buf = torch.empty_like(t)
+            ops.append(dist.P2POp(dist.irecv, buf, self.rank - 1, group=self.group))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        return buf
+
     def all_gather(self, t):
         t = t.contiguous()
         if t.is_cuda:
@@ -94,6 +110,10 @@ class LocalComm:
         out = torch.stack(sh.slots)
         sh.barrier.wait()  # every rank has its copy before the slots are reused
         return out
+
+    def shift(self, t):
+        g = self.all_gather(t)
+        return g[self.rank - 1].clone() if self.rank > 0 else None
 
 
 def run_local(world, fn):
@@ -173,6 +193,13 @@ class CudaSliceOps:
                                            self.G, self.K, self.K2, *self._ws(), stream_of(I)), "tshard apply")
         return entry, U, S, end
 
+    def spec_forward(self, I, entry, halo=None):
+        """U, S of the slice from a (guessed) entry state: the speculative
+        segment forward inside the slice (lifscan.scan_forward_spec); with a
+        halo, `entry` is the guess before the halo rows."""
+        from .lifscan import scan_forward_spec
+        return scan_forward_spec(I, self.beta, self.theta, self.u_r, entry, halo=halo)
+
     def repair(self, I, entry, U, S, end):
         changed = torch.empty(self.N, dtype=torch.int32, device=self.dev)
         with torch.cuda.device(self.dev):
@@ -197,18 +224,39 @@ class CudaSliceOps:
         return Lam
 
 
-def tshard_forward(I, u0, ops, comm, info=None):
+def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", halo_rows=4096):
     """Forward of this rank's slice I [T, N] (u0: the state before row 0 of
     the whole sequence, the same on every rank) -> (U, S, entry), where entry
-    is the exact state before this slice's first row.  `info` (a dict)
-    receives the number of repair rounds and the neurons repaired per round."""
+    is the exact state before this slice's first row.
+
+    entry_mode "maps": the entry of every slice comes from the gathered slice
+    maps (steps 1-3 of the module docstring), exact unless a map overflowed.
+    entry_mode "speculate": every slice after the first receives the last
+    `halo_rows` input rows of the slice before it (a point-to-point shift) and
+    guesses its entry by running them from u_r (as if its neuron had just
+    spiked); all slices then run at once.  Hard resets make the guess exact in
+    almost every neuron, and the repair replays the others from the exact
+    entry only until their rows rejoin (no map is built; the envelope and map
+    exchanges are skipped).
+    Both give the same bits.  `info` (a dict) receives the number of repair
+    rounds and the neurons repaired per round."""
     R, r = comm.world, comm.rank
     N = I.shape[1]
-    env = ops.envelope(I)
-    envs = comm.all_gather(env)
-    m = ops.slice_map(I, envs, r, u0)
-    maps = comm.all_gather(m)
-    entry, U, S, end = ops.apply(I, maps, r, u0)
+    if entry_mode == "maps":
+        env = ops.envelope(I)
+        envs = comm.all_gather(env)
+        m = ops.slice_map(I, envs, r, u0)
+        maps = comm.all_gather(m)
+        entry, U, S, end = ops.apply(I, maps, r, u0)
+    elif entry_mode == "speculate":
+        # the previous slice's last rows lead the guess (u_r before them) to
+        # the exact entry state in all but a few neurons
+        halo = comm.shift(I[-min(halo_rows, I.shape[0]):])
+        entry = u0.clone() if r == 0 else torch.full_like(u0, float(ops.u_r))
+        U, S = ops.spec_forward(I, entry, halo)
+        end = U[-1].clone()
+    else:
+        raise ValueError(f"unknown entry_mode {entry_mode!r}")
     # cross-slice repair: rank r's rows are exact once slices 0..r-1 are, so
     # R-1 rounds suffice; stop as soon as no slice end moved
     flag = torch.ones(1, dtype=end.dtype, device=end.device)
@@ -253,8 +301,8 @@ class LIFTimeSharded(torch.autograd.Function):
     surrogate, detached reset) over a sequence sharded along time."""
 
     @staticmethod
-    def forward(ctx, I, u0, beta, theta, u_r, alpha, ops, comm):
-        U, S, entry = tshard_forward(I.contiguous(), u0.contiguous(), ops, comm)
+    def forward(ctx, I, u0, beta, theta, u_r, alpha, ops, comm, entry_mode="speculate"):
+        U, S, entry = tshard_forward(I.contiguous(), u0.contiguous(), ops, comm, entry_mode=entry_mode)
         ctx.save_for_backward(I, U, entry)
         ctx.ops, ctx.comm, ctx.beta = ops, comm, float(beta)
         return S
@@ -263,16 +311,17 @@ class LIFTimeSharded(torch.autograd.Function):
     def backward(ctx, gS):
         I, U, entry = ctx.saved_tensors
         dI, du0 = tshard_backward(I, entry, U, gS.contiguous(), ctx.ops, ctx.comm, ctx.beta)
-        return dI, du0, None, None, None, None, None, None
+        return dI, du0, None, None, None, None, None, None, None
 
 
 def lif_tshard(I, u0, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, group=None, C=64, G=16, K=16, K2=32, K3=64,
-               ops=None, comm=None):
+               ops=None, comm=None, entry_mode="speculate"):
     """Spikes of this rank's time slice I [T, N] of a sequence split evenly
     over the ranks of `group` (rank order = time order).  Differentiable in I
-    and u0 like lif_tuned; one process per GPU."""
+    and u0 like lif_tuned; one process per GPU.  entry_mode: see
+    tshard_forward (C, G, K, K2, K3 shape the maps of entry_mode "maps")."""
     if not I.is_cuda and ops is None:
         raise RuntimeError("lif_tshard needs CUDA tensors (this implementation has no CPU path)")
     comm = comm or TorchComm(group)
     ops = ops or CudaSliceOps(I.shape[0], I.shape[1], I.device, beta, theta, u_r, alpha, C, G, K, K2, K3)
-    return LIFTimeSharded.apply(I, u0, beta, theta, u_r, alpha, ops, comm)
+    return LIFTimeSharded.apply(I, u0, beta, theta, u_r, alpha, ops, comm, entry_mode)

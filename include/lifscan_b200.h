@@ -187,6 +187,23 @@ int lifb_scan_fwd_v3_noalloc(const float *I, const float *u0, float *U, float *S
                              int64_t T, int64_t N, float beta, float theta, float u_r,
                              int C, int K, int max_repair, lifb_stats *stats_dev, void *stream);
 
+/* Speculative segment forward for long sequences (used by the B200 policy of
+ * scan_forward_auto, lifscan/triton_lif.py:1228-1232, when N is too small to
+ * fill the GPU with one pass): T/L segments of L rows (T % L == 0), each
+ * started from a guess made by running the W rows before it from u_r, all
+ * replayed at once, then every segment whose guessed start differs from the
+ * previous segment's exact end is replayed from that end until its rows
+ * rejoin.  U and S are bit-identical to the serial recurrence for every L and
+ * W; L = T is the serial pass.  Optional halo: I_halo [W_halo, N], the rows
+ * just before row 0 when u0 is only a guess of the state before the halo (a
+ * time slice after the first); segment 0 then starts from u0 run through the
+ * halo, and the outputs are exact for that start. */
+size_t lifb_scan_fwd_spec_workspace_bytes(int64_t T, int64_t N, int64_t L);
+int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S,
+                       int64_t T, int64_t N, float beta, float theta, float u_r,
+                       int64_t L, int64_t W, const float *I_halo, int64_t W_halo,
+                       void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:
  * 944-983, scan_forward_v4; :512-526, scan_backward_tiled).  These phases

@@ -211,3 +211,43 @@ def test_long_sequence_v3_fast_path(cuda):
     U, S = L().scan_forward_v3(Id, 0.99, 1.0, 0.0, u0d, C=64, K=16)
     assert_bit_equal(_np(S), Ss, "S")
     assert_bit_equal(_np(U), Us, "U")
+
+
+@pytest.mark.parametrize("beta,mu,sd", ((0.99, 0.02, 0.1), (0.9, 0.15, 0.4), (1.0, -0.01, 0.05), (0.5, 0.4, 0.2)))
+@pytest.mark.parametrize("N,T,Lseg,W", ((1024, 1 << 16, 4096, 1024), (1000, 1 << 15, 2048, 0), (64, 1 << 15, 1024, 4096),
+                                     (2048, 8192, 512, 256), (777, 1 << 14, 1024, 1024)))
+def test_spec_forward_bit_exact(cuda, beta, mu, sd, N, T, Lseg, W):
+    """Speculative segment forward: W-row lead-ins (W = 0: every guess is u_r,
+    W > L: lead-ins span several segments), N % 4 != 0 on the plain replay."""
+    I, u0 = gen(T, N, mu, sd, seed=21, u0_sd=0.3)
+    Us, Ss = O.serial_forward(I, beta, 1.0, -0.1, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    U, S = L().scan_forward_spec(Id, beta, 1.0, -0.1, u0d, L=Lseg, W=W)
+    assert_bit_equal(_np(U), Us, "U")
+    assert_bit_equal(_np(S), Ss, "S")
+
+
+def test_spec_forward_c4_reduced_auto(cuda):
+    """The auto policy at config 4's width and distribution (T = 2^18)."""
+    T, N = 1 << 18, 1024
+    I, u0 = gen(T, N, 0.02, 0.1, seed=0)
+    Us, Ss = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
+    Id, u0d = to_dev(cuda, I, u0)
+    assert L().spec_segment(T, N)[0] < T
+    U, S = L().scan_forward_auto(Id, 0.99, 1.0, 0.0, u0d)
+    assert_bit_equal(_np(S), Ss, "S")
+    assert_bit_equal(_np(U), Us, "U")
+
+
+@pytest.mark.parametrize("N,T,W", ((1024, 1 << 15, 4096), (1000, 8192, 512)))
+def test_spec_forward_halo(cuda, N, T, W):
+    """With a halo (the rows before row 0) and u0 the guess before it, the
+    result is the recurrence from the state the halo leads to."""
+    I, _ = gen(T + W, N, 0.02, 0.1, seed=5)
+    guess = np.zeros(N, np.float32)
+    Uh, _ = O.serial_forward(I[:W], 0.99, 1.0, 0.0, guess)
+    Us, Ss = O.serial_forward(I[W:], 0.99, 1.0, 0.0, Uh[-1].copy())
+    Id, gd = to_dev(cuda, I, guess)
+    U, S = L().scan_forward_spec(Id[W:], 0.99, 1.0, 0.0, gd, halo=Id[:W])
+    assert_bit_equal(_np(S), Ss, "S")
+    assert_bit_equal(_np(U), Us, "U")

@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _run(cuda, T_total, N, mu, sd, beta, world, u_r=0.0, u0_sd=0.0, K3=64, seed=0):
+def _run(cuda, T_total, N, mu, sd, beta, world, u_r=0.0, u0_sd=0.0, K3=64, seed=0, entry_mode="maps"):
     from hard_resets_compose_b200 import tshard
     I, u0, GS = gen(T_total, N, mu, sd, seed=seed, u0_sd=u0_sd, grad=True)
     Id = torch.from_numpy(I).to(cuda)
@@ -33,7 +33,7 @@ def _run(cuda, T_total, N, mu, sd, beta, world, u_r=0.0, u0_sd=0.0, K3=64, seed=
         r = comm.rank
         ops = tshard.CudaSliceOps(T, N, cuda, beta, 1.0, u_r, K3=K3)
         Ir = Id[r * T:(r + 1) * T]
-        U, S, entry = tshard.tshard_forward(Ir, u0d, ops, comm, info=infos[r])
+        U, S, entry = tshard.tshard_forward(Ir, u0d, ops, comm, info=infos[r], entry_mode=entry_mode)
         Lam, du0 = tshard.tshard_backward(Ir, entry, U, Gd[r * T:(r + 1) * T], ops, comm, beta)
         return U, S, Lam, du0
 
@@ -51,10 +51,11 @@ def _run(cuda, T_total, N, mu, sd, beta, world, u_r=0.0, u0_sd=0.0, K3=64, seed=
     return infos
 
 
+@pytest.mark.parametrize("entry_mode", ("maps", "speculate"))
 @pytest.mark.parametrize("world", (2, 4, 8))
 @pytest.mark.parametrize("beta,mu,sd", ((0.99, 0.02, 0.1), (0.9, 0.15, 0.4), (1.0, -0.01, 0.05), (0.5, 0.4, 0.2)))
-def test_tshard_threads_bit_exact(cuda, world, beta, mu, sd):
-    infos = _run(cuda, 1 << 15, 1024, mu, sd, beta, world, u0_sd=0.3)
+def test_tshard_threads_bit_exact(cuda, world, beta, mu, sd, entry_mode):
+    infos = _run(cuda, 1 << 15, 1024, mu, sd, beta, world, u0_sd=0.3, entry_mode=entry_mode)
     assert infos[0]["repair_rounds"] <= world - 1
 
 
@@ -64,9 +65,11 @@ def test_tshard_overflowing_slice_maps(cuda):
     _run(cuda, 1 << 15, 1024, 0.15, 0.4, 0.9, 4, u_r=-0.1, u0_sd=0.3, K3=1)
 
 
-def test_tshard_c4_reduced(cuda):
-    """Config 4's distribution and width at T = 2^18 over 4 slices."""
-    infos = _run(cuda, 1 << 18, 1024, 0.02, 0.1, 0.99, 4)
+@pytest.mark.parametrize("entry_mode", ("maps", "speculate"))
+def test_tshard_c4_reduced(cuda, entry_mode):
+    """Config 4's distribution and width at T = 2^18 over 4 slices (slices of
+    2^16 rows: the speculative mode runs segments with lead-ins inside them)."""
+    infos = _run(cuda, 1 << 18, 1024, 0.02, 0.1, 0.99, 4, entry_mode=entry_mode)
     assert infos[0]["repair_rounds"] <= 3
 
 

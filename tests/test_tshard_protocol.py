@@ -33,13 +33,16 @@ def _free_port():
 
 
 def _slice_run(comm, case, mode, info):
+    """mode: "maps" (oracle slice maps), "corrupt" (maps that guess 0.5) or
+    "speculate" (no maps, every later slice starts from u_r)."""
     from hard_resets_compose_b200 import tshard
     T_total, N, mu, sd, beta = CASES[case]
     I, u0, GS = gen(T_total, N, mu, sd, seed=3, u0_sd=0.3, grad=True)
     a, b = tshard.slice_rows(T_total, comm.world, comm.rank)
-    ops = OracleSliceOps(b - a, N, beta, 1.0, 0.0, C=64, K=8, K3=32, mode=mode)
+    ops = OracleSliceOps(b - a, N, beta, 1.0, 0.0, C=64, K=8, K3=32, mode="corrupt" if mode == "corrupt" else "maps")
     It, u0t, Gt = (torch.from_numpy(np.ascontiguousarray(x)) for x in (I[a:b], u0, GS[a:b]))
-    U, S, entry = tshard.tshard_forward(It, u0t, ops, comm, info=info)
+    U, S, entry = tshard.tshard_forward(It, u0t, ops, comm, info=info,
+                                        entry_mode="speculate" if mode == "speculate" else "maps")
     Lam, du0 = tshard.tshard_backward(It, entry, U, Gt, ops, comm, beta)
     return U.numpy(), S.numpy(), Lam.numpy(), du0.numpy()
 
@@ -60,7 +63,7 @@ def _check(case, world, results):
         assert not r[3].any()
 
 
-@pytest.mark.parametrize("mode", ("maps", "corrupt"))
+@pytest.mark.parametrize("mode", ("maps", "corrupt", "speculate"))
 @pytest.mark.parametrize("case", sorted(CASES))
 @pytest.mark.parametrize("world", (2, 3, 4))
 def test_protocol_threads(case, mode, world):
@@ -88,7 +91,8 @@ def _gloo_worker(rank, world, port, case, mode, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,case,mode", ((2, "spiking", "maps"), (4, "c4like", "maps"), (4, "rare", "corrupt")))
+@pytest.mark.parametrize("world,case,mode", ((2, "spiking", "maps"), (4, "c4like", "maps"), (4, "rare", "corrupt"),
+                                             (4, "c4like", "speculate")))
 def test_protocol_gloo(tmp_path, world, case, mode):
     mp.spawn(_gloo_worker, args=(world, _free_port(), case, mode, str(tmp_path)), nprocs=world, join=True)
     res = []
