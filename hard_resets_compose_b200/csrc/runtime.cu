@@ -38,8 +38,20 @@ bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int b
     return make_tmap_2d_typed(m, base, false, N, T, box_x, box_y);
 }
 
+// The encoder is a driver-API call and needs the device's primary context
+// current on the calling thread.  A thread whose first CUDA work is this call
+// (autograd's backward worker, say, when every allocation it makes is served
+// from the caching allocator) has none bound yet: bind it once per device.
+static void bind_primary_context()
+{
+    thread_local int bound = -1;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev != bound && cudaSetDevice(dev) == cudaSuccess) bound = dev;
+}
+
 bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N, int64_t T, int box_x, int box_y)
 {
+    bind_primary_context();
     auto enc = encoder();
     if (!enc || ((uintptr_t)base & 15) || (N * 4) % 16 || T >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
         return false;

@@ -45,16 +45,28 @@ __device__ __forceinline__ bool replay_until_sync(const float *__restrict__ I, f
 {
     const unsigned full = 0xffffffffu;
     bool synced = !active;
+    if (!__any_sync(full, active)) return synced;
+    // rows of batch b are loaded while batch b - kB is replayed
+    float x[kB], uo[kB], so[kB];
+#pragma unroll
+    for (int q = 0; q < kB; q++) {
+        if (act && q < L) {
+            const int64_t o = (r0 + q) * N + n;
+            x[q] = __ldg(I + o);
+            uo[q] = U[o];
+            so[q] = S[o];
+        }
+    }
     for (int64_t b = 0; b < L; b += kB) {
         if (!__any_sync(full, active)) break;
-        float x[kB], uo[kB], so[kB];
+        float xn[kB], un_[kB], sn[kB];
 #pragma unroll
         for (int q = 0; q < kB; q++) {
-            if (act && b + q < L) {
-                const int64_t o = (r0 + b + q) * N + n;
-                x[q] = __ldg(I + o);
-                uo[q] = U[o];
-                so[q] = S[o];
+            if (act && b + kB + q < L) {
+                const int64_t o = (r0 + b + kB + q) * N + n;
+                xn[q] = __ldg(I + o);
+                un_[q] = U[o];
+                sn[q] = S[o];
             }
         }
 #pragma unroll
@@ -73,6 +85,12 @@ __device__ __forceinline__ bool replay_until_sync(const float *__restrict__ I, f
                     S[o] = fs;
                 }
             }
+        }
+#pragma unroll
+        for (int q = 0; q < kB; q++) {
+            x[q] = xn[q];
+            uo[q] = un_[q];
+            so[q] = sn[q];
         }
     }
     return synced;
@@ -118,6 +136,15 @@ __global__ void __launch_bounds__(kFixBlock) k_fwd_fixup_seq(const float *__rest
 {
     const int64_t n = (int64_t)blockIdx.x * kFixBlock + threadIdx.x;
     const bool act = n < N;
+    // nothing to carry unless some lane has a segment whose fix did not
+    // resynchronise: check all flags first (independent loads)
+    bool any_ch = false;
+    for (int64_t s0 = 1; s0 < NS && !__any_sync(0xffffffffu, any_ch); s0 += 16) {
+#pragma unroll
+        for (int q = 0; q < 16; q++)
+            if (act && s0 + q < NS) any_ch |= Changed[(s0 + q) * N + n] != 0;
+    }
+    if (!__any_sync(0xffffffffu, any_ch)) return;
     bool carry = false;  // the previous segment's end differs from the replay's
     float end = 0.0f;
     int run = 0, longest = 0;

@@ -28,7 +28,11 @@
 namespace lifb {
 
 constexpr int kLeadBlock = 128;
-constexpr int kLeadB = 16;  // rows loaded one batch ahead of the dependent chain
+// Rows per batch; the next batch is loaded while this one is stepped, so 2 x
+// kLeadB loads per thread are in flight.  A batch of 64 steps (~1300 cycles
+// of dependent arithmetic) covers the load latency; 16 left it exposed
+// (a 4096-row lead-in took ~250 us).
+constexpr int kLeadB = 64;
 
 // Starts[s] for segment s.  Segment 0 starts from u0, or, when a halo of
 // W_halo rows before row 0 is given, from u0 run through the halo.

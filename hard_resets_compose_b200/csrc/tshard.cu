@@ -14,6 +14,8 @@
 //              enters the slice from the next one (folded from the gathered maps)
 // The map algebra is the v4 three-level scan (lifscan/triton_lif.py:828-983)
 // applied one level further, across GPUs.
+#include <cstdio>
+
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
 
@@ -274,8 +276,15 @@ int lifb_tshard_bwd(const float *I, const float *u_prev, const float *U, const f
     float *P = (float *)ws, *Q = (float *)((char *)ws + one);
     int32_t *D = (int32_t *)((char *)ws + 2 * one);
     if (!lifb::bwd_tma(0, I, u_prev, U, nullptr, GS, nullptr, nullptr, Lam, P, Q, T, N, C, beta, theta, u_r, alpha,
-                       true, s, D))
-        return ts_fail(LIFB_ERR_UNSUPPORTED, "time-sharded adjoint: needs N % 4 == 0 and 16-byte aligned tensors");
+                       true, s, D)) {
+        char msg[256];
+        snprintf(msg, sizeof msg,
+                 "time-sharded adjoint: needs N %% 4 == 0 and 16-byte aligned tensors (N=%lld; address mod 16: "
+                 "I %u, u_prev %u, U %u, GS %u, Lam %u)",
+                 (long long)N, (unsigned)((uintptr_t)I & 15), (unsigned)((uintptr_t)u_prev & 15),
+                 (unsigned)((uintptr_t)U & 15), (unsigned)((uintptr_t)GS & 15), (unsigned)((uintptr_t)Lam & 15));
+        return ts_fail(LIFB_ERR_UNSUPPORTED, msg);
+    }
     const unsigned nb = (unsigned)((N + lifb::kTsBlock - 1) / lifb::kTsBlock);
     lifb::count_launches(1);
     lifb::k_slice_adjoint<<<nb, lifb::kTsBlock, 0, s>>>(P, Q, lam_pq, N, M);

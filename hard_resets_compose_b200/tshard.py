@@ -261,13 +261,17 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", halo_row
     # R-1 rounds suffice; stop as soon as no slice end moved
     flag = torch.ones(1, dtype=end.dtype, device=end.device)
     rounds, repaired = 0, []
-    for _ in range(R - 1):
+    for it in range(R - 1):
         g = comm.all_gather(torch.cat([end, flag]))
-        flags = g[:, N].tolist()
-        if not any(f != 0.0 for f in flags[:R - 1]):
-            break
+        if it == 0:
+            need = r > 0  # every slice end is new: no flags to read (no host sync)
+        else:
+            flags = g[:, N].tolist()
+            if not any(f != 0.0 for f in flags[:R - 1]):
+                break
+            need = r > 0 and flags[r - 1] != 0.0
         rounds += 1
-        if r > 0 and flags[r - 1] != 0.0:
+        if need:
             entry.copy_(g[r - 1, :N])
             changed = ops.repair(I, entry, U, S, end)
             cnt = changed.sum()

@@ -151,3 +151,37 @@ def test_scan_backward_fast_path(cuda, beta, N, T, C):
     l2 = L().scan_backward_tiled(d[0], d[1], d[2], None, d[4], None, beta, 1.0, 0.0, 4.0, True, C=C)
     assert rel(_np(l1), ref) < TOL
     assert rel(_np(l2), ref) < TOL
+
+
+def test_calls_from_a_fresh_thread(cuda):
+    """A host thread whose first CUDA work is a library call (autograd's
+    backward worker, when the caching allocator serves every allocation):
+    the TMA descriptors must still encode, forward and backward."""
+    import threading
+    T, N = 4096, 1024
+    I, u0, GS = gen(T, N, 0.05, 0.2, seed=17, grad=True)
+    U, S = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
+    ref = O.serial_backward(I, u0, U, S, GS, None, 0.99, 1.0, 0.0, 4.0, True)
+    d = to_dev(cuda, I, u0, U, GS)
+    # warm the caching allocator with blocks of the sizes the calls allocate
+    for _ in range(2):
+        L().serial_forward(d[0], 0.99, 1.0, 0.0, d[1])
+        L().scan_backward_tiled(d[0], d[1], d[2], None, d[3], None, 0.99, 1.0, 0.0, 4.0, True, C=1024)
+    torch.cuda.synchronize()
+    out = {}
+
+    def body():
+        try:
+            out["fwd"] = L().serial_forward(d[0], 0.99, 1.0, 0.0, d[1])
+            out["bwd"] = L().scan_backward_tiled(d[0], d[1], d[2], None, d[3], None, 0.99, 1.0, 0.0, 4.0, True,
+                                                 C=1024)
+        except Exception as e:  # noqa: BLE001 - reported below
+            out["err"] = e
+
+    th = threading.Thread(target=body)
+    th.start()
+    th.join()
+    assert "err" not in out, out.get("err")
+    torch.cuda.synchronize()
+    assert_bit_equal(_np(out["fwd"][0]), U, "U")
+    assert rel(_np(out["bwd"]), ref) < TOL
