@@ -88,8 +88,12 @@ void replay_any(const float *I, const float *u0, const float *Starts, float *U, 
 
 // scan_spec.cu: Starts[s] of NS segments of L rows guessed by a W-row lead-in
 // from u_r (Starts[0] = u0; lead-ins that reach row 0 start from u0).
-void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts, int64_t N,
-                   int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r, cudaStream_t s);
+// end_guess (optional): the same lead-in over the last W rows (a guess of the
+// state after row T-1).  u0 NULL: lead-ins that reach row 0 start from u_r
+// and Starts[0] is left to the caller.
+void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts,
+                   float *end_guess, int64_t N, int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r,
+                   cudaStream_t s);
 
 // host_pipeline.cu
 size_t host_pipe_workspace_bytes(int64_t T, int64_t N, int64_t block_n);

@@ -22,6 +22,8 @@
 // the guesses decide only how much the fix-up replays.  The map scan of the
 // reference (lifscan/triton_lif.py:782-983) computes exact segment starts
 // instead; this path trades its map build for a W-row lead-in.
+#include <cstdio>
+
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
 
@@ -34,12 +36,17 @@ constexpr int kLeadBlock = 128;
 // (a 4096-row lead-in took ~250 us).
 constexpr int kLeadB = 64;
 
-// Starts[s] for segment s.  Segment 0 starts from u0, or, when a halo of
-// W_halo rows before row 0 is given, from u0 run through the halo.
+// blockIdx.y = s.  s < NS: Starts[s] for segment s.  Segment 0 starts from
+// u0 (when given), or, with a halo of W_halo rows before row 0, from u0 (u_r
+// when NULL) run through the halo.  Segment s >= 1 starts from a lead-in over
+// rows [s*L - W, s*L) from u_r; one that reaches row 0 starts there from u0
+// (u_r when NULL).  s == NS (when end_guess is given): the same lead-in over
+// the last W rows, a guess of the state after row T-1 for whatever follows.
 __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__ I, const float *__restrict__ u0,
                                                        const float *__restrict__ I_halo, int64_t W_halo,
-                                                       float *__restrict__ Starts, int64_t N, int64_t L, int64_t W,
-                                                       float beta, float theta, float u_r)
+                                                       float *__restrict__ Starts, float *__restrict__ end_guess,
+                                                       int64_t N, int64_t NS, int64_t L, int64_t W, float beta,
+                                                       float theta, float u_r)
 {
     const int64_t n = (int64_t)blockIdx.x * kLeadBlock + threadIdx.x;
     const int64_t s = blockIdx.y;
@@ -48,20 +55,20 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
     int64_t len;
     float u;
     if (s == 0) {
-        u = u0[n];
+        u = u0 ? u0[n] : u_r;
         if (!I_halo || W_halo <= 0) {
-            Starts[n] = u;
+            if (u0) Starts[n] = u;
             return;
         }
         p = I_halo + n;
         len = W_halo;
     } else {
-        const int64_t t1 = s * L;
+        const int64_t t1 = s * L;  // s == NS: t1 = T
         int64_t t0 = t1 - W;
         u = u_r;
         if (t0 <= 0) {
             t0 = 0;
-            u = u0[n];
+            u = u0 ? u0[n] : u_r;
         }
         p = I + t0 * N + n;
         len = t1 - t0;
@@ -79,15 +86,24 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
 #pragma unroll
         for (int q = 0; q < kLeadB; q++) cur[q] = nxt[q];
     }
-    Starts[s * N + n] = u;
+    if (s < NS) Starts[s * N + n] = u;
+    else end_guess[n] = u;
 }
 
-void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts, int64_t N,
-                   int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r, cudaStream_t s)
+void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts,
+                   float *end_guess, int64_t N, int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r,
+                   cudaStream_t s)
 {
     count_launches(1);
-    k_leadin<<<dim3((unsigned)((N + kLeadBlock - 1) / kLeadBlock), (unsigned)NS), kLeadBlock, 0, s>>>(
-        I, u0, I_halo, W_halo, Starts, N, L, W, beta, theta, u_r);
+    const unsigned ny = (unsigned)(NS + (end_guess ? 1 : 0));
+    k_leadin<<<dim3((unsigned)((N + kLeadBlock - 1) / kLeadBlock), ny), kLeadBlock, 0, s>>>(
+        I, u0, I_halo, W_halo, Starts, end_guess, N, NS, L, W, beta, theta, u_r);
+}
+
+__global__ void k_copy_row(const float *__restrict__ src, float *__restrict__ dst, int64_t N)
+{
+    const int64_t n = (int64_t)blockIdx.x * kLeadBlock + threadIdx.x;
+    if (n < N) dst[n] = src[n];
 }
 
 }  // namespace lifb
@@ -106,43 +122,112 @@ size_t lifb_scan_fwd_spec_workspace_bytes(int64_t T, int64_t N, int64_t L)
     return 4 * one;
 }
 
+static int spec_check(const char *who, int64_t T, int64_t N, int64_t L, int64_t W, int64_t W_halo)
+{
+    char msg[160];
+    if (T < 0 || N < 0 || L <= 0 || W < 0 || W_halo < 0 || (T > 0 && T % L)) {
+        snprintf(msg, sizeof msg, "%s: T must be a multiple of the segment length L > 0, W >= 0", who);
+        lifb::set_last_error(msg);
+        return LIFB_ERR_INVALID_ARGUMENT;
+    }
+    if (T / L > 65535) {
+        snprintf(msg, sizeof msg, "%s: more than 65535 segments", who);
+        lifb::set_last_error(msg);
+        return LIFB_ERR_UNSUPPORTED;
+    }
+    return LIFB_OK;
+}
+
+static int spec_ws(const char *who, int64_t T, int64_t N, int64_t L, void *workspace, size_t workspace_bytes)
+{
+    if (!workspace || (uintptr_t)workspace % kAl || workspace_bytes < lifb_scan_fwd_spec_workspace_bytes(T, N, L)) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "%s: workspace missing, misaligned or too small", who);
+        lifb::set_last_error(msg);
+        return LIFB_ERR_WORKSPACE;
+    }
+    return LIFB_OK;
+}
+
+static int spec_done(const char *who)
+{
+    if (cudaGetLastError() != cudaSuccess) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "%s: launch failed", who);
+        lifb::set_last_error(msg);
+        return LIFB_ERR_CUDA;
+    }
+    lifb::set_last_error("");
+    return LIFB_OK;
+}
+
+struct SpecScratch {
+    float *Starts, *Ends, *EndsNew;
+    int32_t *Changed;
+};
+
+static SpecScratch spec_carve(void *workspace, int64_t NS, int64_t N)
+{
+    char *b = (char *)workspace;
+    const size_t one = al((size_t)NS * N * 4);
+    return {(float *)b, (float *)(b + one), (float *)(b + 2 * one), (int32_t *)(b + 3 * one)};
+}
+
 int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                        float theta, float u_r, int64_t L, int64_t W, const float *I_halo, int64_t W_halo,
                        void *workspace, size_t workspace_bytes, void *stream)
 {
-    if (T < 0 || N < 0 || L <= 0 || W < 0 || W_halo < 0 || (T > 0 && T % L)) {
-        lifb::set_last_error("lifb_scan_fwd_spec: T must be a multiple of the segment length L > 0, W >= 0");
-        return LIFB_ERR_INVALID_ARGUMENT;
-    }
-    if (T / L > 65535) {
-        lifb::set_last_error("lifb_scan_fwd_spec: more than 65535 segments");
-        return LIFB_ERR_UNSUPPORTED;
-    }
+    int st = spec_check("lifb_scan_fwd_spec", T, N, L, W, W_halo);
+    if (st) return st;
     if (T == 0 || N == 0) return LIFB_OK;
     cudaStream_t s = (cudaStream_t)stream;
     const int64_t NS = T / L;
     if (NS == 1 && (!I_halo || W_halo == 0)) {
         lifb::serial_fwd(I, u0, U, S, T, N, beta, theta, u_r, s);
     } else {
-        if (!workspace || (uintptr_t)workspace % kAl || workspace_bytes < lifb_scan_fwd_spec_workspace_bytes(T, N, L)) {
-            lifb::set_last_error("lifb_scan_fwd_spec: workspace missing, misaligned or too small");
-            return LIFB_ERR_WORKSPACE;
-        }
-        char *b = (char *)workspace;
-        const size_t one = al((size_t)NS * N * 4);
-        float *Starts = (float *)b, *Ends = (float *)(b + one), *EndsNew = (float *)(b + 2 * one);
-        int32_t *Changed = (int32_t *)(b + 3 * one);
-        lifb::leadin_starts(I, u0, I_halo, W_halo, Starts, N, NS, L, W, beta, theta, u_r, s);
-        lifb::replay_any(I, u0, Starts, U, S, Ends, T, N, L, beta, theta, u_r, s);
-        lifb::fwd_fixup(I, Starts, 1, U, S, Ends, EndsNew, Changed, N, NS, L, beta, theta, u_r, nullptr, s);
+        if ((st = spec_ws("lifb_scan_fwd_spec", T, N, L, workspace, workspace_bytes))) return st;
+        SpecScratch w = spec_carve(workspace, NS, N);
+        lifb::leadin_starts(I, u0, I_halo, W_halo, w.Starts, nullptr, N, NS, L, W, beta, theta, u_r, s);
+        lifb::replay_any(I, u0, w.Starts, U, S, w.Ends, T, N, L, beta, theta, u_r, s);
+        lifb::fwd_fixup(I, w.Starts, 1, U, S, w.Ends, w.EndsNew, w.Changed, N, NS, L, beta, theta, u_r, nullptr, s);
     }
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        lifb::set_last_error("lifb_scan_fwd_spec: launch failed");
-        return LIFB_ERR_CUDA;
+    return spec_done("lifb_scan_fwd_spec");
+}
+
+int lifb_scan_fwd_spec_begin(const float *I, int64_t T, int64_t N, float beta, float theta, float u_r, int64_t L,
+                             int64_t W, float *end_guess, void *workspace, size_t workspace_bytes, void *stream)
+{
+    int st = spec_check("lifb_scan_fwd_spec_begin", T, N, L, W, 0);
+    if (st) return st;
+    if (T == 0 || N == 0) return LIFB_OK;
+    if ((st = spec_ws("lifb_scan_fwd_spec_begin", T, N, L, workspace, workspace_bytes))) return st;
+    SpecScratch w = spec_carve(workspace, T / L, N);
+    lifb::leadin_starts(I, nullptr, nullptr, 0, w.Starts, end_guess, N, T / L, L, W, beta, theta, u_r,
+                        (cudaStream_t)stream);
+    return spec_done("lifb_scan_fwd_spec_begin");
+}
+
+int lifb_scan_fwd_spec_finish(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                              float theta, float u_r, int64_t L, void *workspace, size_t workspace_bytes,
+                              void *stream)
+{
+    int st = spec_check("lifb_scan_fwd_spec_finish", T, N, L, 0, 0);
+    if (st) return st;
+    if (T == 0 || N == 0) return LIFB_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t NS = T / L;
+    if (NS == 1) {
+        lifb::serial_fwd(I, u0, U, S, T, N, beta, theta, u_r, s);
+        return spec_done("lifb_scan_fwd_spec_finish");
     }
-    lifb::set_last_error("");
-    return LIFB_OK;
+    if ((st = spec_ws("lifb_scan_fwd_spec_finish", T, N, L, workspace, workspace_bytes))) return st;
+    SpecScratch w = spec_carve(workspace, NS, N);
+    lifb::count_launches(1);
+    lifb::k_copy_row<<<(unsigned)((N + lifb::kLeadBlock - 1) / lifb::kLeadBlock), lifb::kLeadBlock, 0, s>>>(
+        u0, w.Starts, N);
+    lifb::replay_any(I, u0, w.Starts, U, S, w.Ends, T, N, L, beta, theta, u_r, s);
+    lifb::fwd_fixup(I, w.Starts, 1, U, S, w.Ends, w.EndsNew, w.Changed, N, NS, L, beta, theta, u_r, nullptr, s);
+    return spec_done("lifb_scan_fwd_spec_finish");
 }
 
 }  // extern "C"

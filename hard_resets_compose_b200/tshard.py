@@ -193,12 +193,37 @@ class CudaSliceOps:
                                            self.G, self.K, self.K2, *self._ws(), stream_of(I)), "tshard apply")
         return entry, U, S, end
 
-    def spec_forward(self, I, entry, halo=None):
-        """U, S of the slice from a (guessed) entry state: the speculative
-        segment forward inside the slice (lifscan.scan_forward_spec); with a
-        halo, `entry` is the guess before the halo rows."""
-        from .lifscan import scan_forward_spec
-        return scan_forward_spec(I, self.beta, self.theta, self.u_r, entry, halo=halo)
+    def _spec_ws(self):
+        if getattr(self, "_sws", None) is None:
+            from .lifscan import SPEC_LEAD, spec_segment
+            L, W = spec_segment(self.T, self.N)
+            self._sL, self._sW = L, (W if W > 0 else min(SPEC_LEAD, self.T))
+            nb = self.L.lifb_scan_fwd_spec_workspace_bytes(self.T, self.N, L)
+            self._sws = torch.empty(max(nb, 1), dtype=torch.uint8, device=self.dev)
+        return self._sws
+
+    def spec_begin(self, I):
+        """Lead-ins of the slice's segments (lifb_scan_fwd_spec_begin) and the
+        guess of its final state: its last rows run from u_r."""
+        ws = self._spec_ws()
+        g = torch.empty(self.N, device=self.dev)
+        with torch.cuda.device(self.dev):
+            check(self.L.lifb_scan_fwd_spec_begin(ptr(I), self.T, self.N, self.beta, self.theta, self.u_r, self._sL,
+                                                  self._sW, ptr(g), ptr(ws), ws.numel(), stream_of(I)),
+                  "tshard speculative lead-ins")
+        return g
+
+    def spec_finish(self, I, entry):
+        """U, S of the slice from `entry` (lifb_scan_fwd_spec_finish, after
+        spec_begin): exact for that entry."""
+        ws = self._spec_ws()
+        U = torch.empty_like(I)
+        S = torch.empty_like(I)
+        with torch.cuda.device(self.dev):
+            check(self.L.lifb_scan_fwd_spec_finish(ptr(I), ptr(entry), ptr(U), ptr(S), self.T, self.N, self.beta,
+                                                   self.theta, self.u_r, self._sL, ptr(ws), ws.numel(),
+                                                   stream_of(I)), "tshard speculative forward")
+        return U, S
 
     def repair(self, I, entry, U, S, end):
         changed = torch.empty(self.N, dtype=torch.int32, device=self.dev)
@@ -224,22 +249,31 @@ class CudaSliceOps:
         return Lam
 
 
-def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", halo_rows=4096):
+def _mark(timeline, name, ref):
+    """Appends (name, CUDA event recorded now on ref's stream) when timing."""
+    if timeline is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(torch.cuda.current_stream(ref.device))
+        timeline.append((name, e))
+
+
+def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", timeline=None):
     """Forward of this rank's slice I [T, N] (u0: the state before row 0 of
     the whole sequence, the same on every rank) -> (U, S, entry), where entry
     is the exact state before this slice's first row.
 
     entry_mode "maps": the entry of every slice comes from the gathered slice
     maps (steps 1-3 of the module docstring), exact unless a map overflowed.
-    entry_mode "speculate": every slice after the first receives the last
-    `halo_rows` input rows of the slice before it (a point-to-point shift) and
-    guesses its entry by running them from u_r (as if its neuron had just
-    spiked); all slices then run at once.  Hard resets make the guess exact in
-    almost every neuron, and the repair replays the others from the exact
-    entry only until their rows rejoin (no map is built; the envelope and map
-    exchanges are skipped).
+    entry_mode "speculate": every slice runs its last few thousand rows from
+    u_r (as if its neuron had just spiked) alongside the lead-ins of its own
+    segments, and hands the result to the next slice (a point-to-point shift
+    of N floats) as that slice's entry guess; all slices then run at once.
+    Hard resets make the guess exact in almost every neuron, and the repair
+    replays the others from the exact entry only until their rows rejoin (no
+    map is built; the envelope and map exchanges are skipped).
     Both give the same bits.  `info` (a dict) receives the number of repair
-    rounds and the neurons repaired per round."""
+    rounds and the neurons repaired per round; `timeline` (a list, CUDA only)
+    receives (phase, CUDA event) pairs marking the end of each phase."""
     R, r = comm.world, comm.rank
     N = I.shape[1]
     if entry_mode == "maps":
@@ -251,10 +285,15 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", halo_row
     elif entry_mode == "speculate":
         # the previous slice's last rows lead the guess (u_r before them) to
         # the exact entry state in all but a few neurons
-        halo = comm.shift(I[-min(halo_rows, I.shape[0]):])
-        entry = u0.clone() if r == 0 else torch.full_like(u0, float(ops.u_r))
-        U, S = ops.spec_forward(I, entry, halo)
+        _mark(timeline, "start", I)
+        guess = ops.spec_begin(I)  # also a guess of this slice's final state
+        _mark(timeline, "lead_in", I)
+        entry = comm.shift(guess)  # the previous slice's guess is this one's entry
+        entry = u0.clone() if r == 0 else entry
+        _mark(timeline, "shift", I)
+        U, S = ops.spec_finish(I, entry)
         end = U[-1].clone()
+        _mark(timeline, "slice", I)
     else:
         raise ValueError(f"unknown entry_mode {entry_mode!r}")
     # cross-slice repair: rank r's rows are exact once slices 0..r-1 are, so
@@ -263,6 +302,7 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", halo_row
     rounds, repaired = 0, []
     for it in range(R - 1):
         g = comm.all_gather(torch.cat([end, flag]))
+        _mark(timeline, f"gather{it}", I)
         if it == 0:
             need = r > 0  # every slice end is new: no flags to read (no host sync)
         else:
@@ -277,6 +317,7 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", halo_row
             cnt = changed.sum()
             flag = (cnt > 0).to(end.dtype).reshape(1)
             repaired.append(cnt)
+            _mark(timeline, f"repair{it}", I)
         else:
             flag = torch.zeros(1, dtype=end.dtype, device=end.device)
     if info is not None:
@@ -285,17 +326,22 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", halo_row
     return U, S, entry
 
 
-def tshard_backward(I, entry, U, GS, ops, comm, beta):
+def tshard_backward(I, entry, U, GS, ops, comm, beta, timeline=None):
     """Adjoint of this rank's slice (entry: the state before its first row,
     from tshard_forward) -> (Lam, du0); du0 = beta * Lam[0] on rank 0, zeros
     on the others (their u0 does not enter their rows)."""
     R, r = comm.world, comm.rank
+    _mark(timeline, "bwd_start", I)
     Lam, pq = ops.bwd(I, entry, U, GS)
+    _mark(timeline, "adjoint", I)
     g = comm.all_gather(pq)
+    _mark(timeline, "gather_pq", I)
     top = torch.zeros_like(entry)
     for q in range(R - 1, r, -1):
         top = g[q, 0] + g[q, 1] * top
+    _mark(timeline, "fold", I)
     Lam = ops.bwd_fix(I, entry, U, GS, top, Lam)
+    _mark(timeline, "fix", I)
     du0 = Lam[0] * beta if r == 0 else torch.zeros_like(entry)
     return Lam, du0
 

@@ -203,6 +203,19 @@ int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S,
                        int64_t T, int64_t N, float beta, float theta, float u_r,
                        int64_t L, int64_t W, const float *I_halo, int64_t W_halo,
                        void *workspace, size_t workspace_bytes, void *stream);
+/* The same forward in two calls, for a time slice whose start state comes
+ * from elsewhere (the previous GPU): _begin runs the lead-ins of segments
+ * 1..T/L-1 (those reaching row 0 start from u_r) and, when end_guess [N] is
+ * given, the lead-in over the last W rows, a guess of the slice's final state
+ * to hand to the next slice; _finish replays every segment, segment 0 from
+ * u0, and fixes them up (same workspace, same L).  _finish alone is exact for
+ * u0 whatever _begin guessed. */
+int lifb_scan_fwd_spec_begin(const float *I, int64_t T, int64_t N, float beta, float theta,
+                             float u_r, int64_t L, int64_t W, float *end_guess,
+                             void *workspace, size_t workspace_bytes, void *stream);
+int lifb_scan_fwd_spec_finish(const float *I, const float *u0, float *U, float *S, int64_t T,
+                              int64_t N, float beta, float theta, float u_r, int64_t L,
+                              void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:

@@ -251,3 +251,28 @@ def test_spec_forward_halo(cuda, N, T, W):
     U, S = L().scan_forward_spec(Id[W:], 0.99, 1.0, 0.0, gd, halo=Id[:W])
     assert_bit_equal(_np(S), Ss, "S")
     assert_bit_equal(_np(U), Us, "U")
+
+
+def test_spec_begin_finish(cuda):
+    """The two-call form: _finish alone is exact for its u0; the end guess is
+    the last W rows run from u_r."""
+    from hard_resets_compose_b200 import _lib
+    T, N, Lseg, W = 1 << 16, 1024, 16384, 4096
+    I, u0 = gen(T, N, 0.02, 0.1, seed=9, u0_sd=0.3)
+    Us, Ss = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
+    Ug, _ = O.serial_forward(I[-W:], 0.99, 1.0, 0.0, np.zeros(N, np.float32))
+    Id, u0d = to_dev(cuda, I, u0)
+    lib = _lib.load()
+    nb = lib.lifb_scan_fwd_spec_workspace_bytes(T, N, Lseg)
+    ws = torch.empty(nb, dtype=torch.uint8, device=cuda)
+    g = torch.empty(N, device=cuda)
+    U = torch.empty_like(Id)
+    S = torch.empty_like(Id)
+    st = _lib.stream_of(Id)
+    _lib.check(lib.lifb_scan_fwd_spec_begin(_lib.ptr(Id), T, N, 0.99, 1.0, 0.0, Lseg, W, _lib.ptr(g), _lib.ptr(ws), nb,
+                                            st), "begin")
+    _lib.check(lib.lifb_scan_fwd_spec_finish(_lib.ptr(Id), _lib.ptr(u0d), _lib.ptr(U), _lib.ptr(S), T, N, 0.99, 1.0,
+                                             0.0, Lseg, _lib.ptr(ws), nb, st), "finish")
+    assert_bit_equal(_np(U), Us, "U")
+    assert_bit_equal(_np(S), Ss, "S")
+    assert_bit_equal(_np(g), Ug[-1], "end guess")
