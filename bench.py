@@ -61,9 +61,12 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4"),
+    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5"),
                    help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step; "
-                        "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs")
+                        "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs; c5: sweep of B*N, T, beta")
+    p.add_argument("--c5-n", default="14,15,16,17,18,19,20,21,22",
+                   help="c5: log2 of the total B*N values (split over the GPUs)")
+    p.add_argument("--c5-t", default="256,1024,4096", help="c5: sequence lengths")
     return p.parse_args()
 
 
@@ -211,6 +214,123 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_sweep(args, ws, rank, local):
+    """Config 5: forward and forward+backward over B*N in 2^14..2^22 (total,
+    batch-sharded over the GPUs), T in {256, 1024, 4096}, beta in {0.9, 0.99},
+    x ~ N(0.1, 0.3^2).  Each point times the library calls lif_tuned makes
+    (scan_forward_auto; scan_backward_auto with S recomputed and no GU) with
+    CUDA events, L2 flushed before every timed call; points whose tensors do
+    not fit this GPU (5 [T, N] fp32 tensors for fwd+bwd) are reported as
+    skipped.  One JSON line: every point, and the headline = the largest
+    point's fwd+bwd throughput."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200 import lifscan as L
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load()
+    hbm, peak_kind = peaks()
+    free_bytes = torch.cuda.mem_get_info(dev)[1]
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    evict = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def flush_l2():
+        flush.fill_(1.0)
+        torch.sum(evict, dim=0, out=sink)
+
+    def max_over_ranks(v):
+        if ws == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, reps):
+        fn()
+        ms = []
+        for _ in range(reps):
+            flush_l2()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+        return statistics.median(ms)
+
+    points = []
+    reps = max(args.steps, 3)
+    with ClockSampler(local) as clk:
+        for lg in (int(v) for v in args.c5_n.split(",")):
+            for T in (int(v) for v in args.c5_t.split(",")):
+                for beta in (0.9, 0.99):
+                    n_tot = 1 << lg
+                    N = n_tot // ws
+                    need = 5 * T * N * 4 + (1 << 30)
+                    pt = {"N": n_tot, "T": T, "beta": beta}
+                    fits = float(need <= 0.9 * free_bytes)
+                    if ws > 1:
+                        t = torch.tensor([fits], device=dev)
+                        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+                        fits = float(t.item())
+                    if not fits:
+                        pt["skipped"] = f"needs {need / 2**30:.0f} GiB per GPU for fwd+bwd"
+                        points.append(pt)
+                        continue
+                    g = torch.Generator(device=dev).manual_seed(5000 + lg * 7 + T + rank)
+                    I = torch.empty(T, N, device=dev).normal_(0.1, 0.3, generator=g)
+                    GS = torch.empty(T, N, device=dev).normal_(0.0, 1.0, generator=g)
+                    u0 = torch.zeros(N, device=dev)
+                    out = {}
+
+                    def fwd():
+                        out.clear()
+                        out["fwd"] = L.scan_forward_auto(I, beta, 1.0, 0.0, u0)
+
+                    def fwd_bwd():  # at most I, GS, U, S and Lam live
+                        out.clear()
+                        U_, _ = L.scan_forward_auto(I, beta, 1.0, 0.0, u0)
+                        out["lam"] = L.scan_backward_auto(I, u0, U_, None, GS, None, beta, 1.0, 0.0, 4.0)
+
+                    ms_f = max_over_ranks(timed(fwd, reps))
+                    ms_fb = max_over_ranks(timed(fwd_bwd, reps))
+                    units = T * n_tot
+                    gbs_f = FWD_BYTES * T * N / (ms_f / 1e3) / 1e9
+                    gbs_fb = (FWD_BYTES + BWD_BYTES) * T * N / (ms_fb / 1e3) / 1e9
+                    pt.update(fwd_ms=ms_f, fwd_value=units / (ms_f / 1e3), fwd_frac=gbs_f / hbm,
+                              fwd_bwd_ms=ms_fb, fwd_bwd_value=units / (ms_fb / 1e3), fwd_bwd_frac=gbs_fb / hbm,
+                              forward_segments=list(L.spec_segment(T, N)), bwd_chunk=L.scan_chunk_bwd(T, N))
+                    points.append(pt)
+                    del I, GS, u0, out
+                    torch.cuda.empty_cache()
+    done = [p for p in points if "skipped" not in p]
+    head = max(done, key=lambda p: (p["N"] * p["T"], p["beta"])) if done else None
+    if rank == 0:
+        print(json.dumps({
+            "metric": "neuron-steps/s, lif_tuned fwd+bwd over the config-5 sweep (largest point)",
+            "value": head["fwd_bwd_value"] if head else None, "unit": UNIT, "n_gpus": ws, "steps": reps,
+            "warmup": 1, "ms_per_step": head["fwd_bwd_ms"] if head else None, "higher_is_better": True,
+            "scaling": "weak" if ws > 1 else "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded CUDA torch.Generator, x ~ N(0.1, 0.3^2), upstream gradient N(0, 1))",
+            "config": {"workload": "c5: sweep B*N x T x beta, fwd and fwd+bwd", "parallelism":
+                       f"batch-sharded x{ws}, no collective" if ws > 1 else "one GPU",
+                       "l2": "flushed before every timed call (256 MiB written, 256 MiB read)",
+                       "peak": hbm, "peak_source": peak_kind},
+            "points": points, "clocks": clk.record()}), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def run_long(args, ws, rank, local):
     """Config 4: one sequence of T = 2^20 rows, B*N = 1024 neurons,
     x ~ N(0.02, 0.1^2), beta = 0.99, forward + backward (spikes out, upstream
@@ -287,6 +407,24 @@ def run_long(args, ws, rank, local):
     units = C4_T * N
     value = units / (ms / 1e3)
     hbm, peak_kind = peaks()
+    phases = None
+    if ws > 1:
+        # one more step through the protocol functions with CUDA-event marks at
+        # the end of each phase (untimed above); per phase the max over ranks
+        tl = []
+        U_, _, entry_ = tshard.tshard_forward(I, u0, ops, comm, timeline=tl)
+        tshard.tshard_backward(I, entry_, U_, GS, ops, comm, BETA, timeline=tl)
+        torch.cuda.synchronize(dev)
+        mine = [(tl[i][0], tl[i - 1][1].elapsed_time(tl[i][1])) for i in range(1, len(tl))]
+        every = [None] * ws
+        dist.all_gather_object(every, mine)
+        per_phase = {}
+        for lst in every:
+            for name, v in lst:
+                per_phase[name] = round(max(per_phase.get(name, 0.0), v), 4)
+        phases = {"note": "one extra step through tshard_forward/backward, CUDA events at the end of each "
+                          "phase; per phase the max over ranks (rank 0 has no repair phase)",
+                  "ms": per_phase, "step_ms_max": round(max(sum(v for _, v in lst) for lst in every), 4)}
     # algorithmic bytes of this rank's rows: forward 12 B, backward 16 B per neuron-step
     fwd_gbs = FWD_BYTES * T * N / (ms_f / 1e3) / 1e9
     bwd_gbs = BWD_BYTES * T * N / (ms_b / 1e3) / 1e9
@@ -344,7 +482,7 @@ def run_long(args, ws, rank, local):
             "fwd": {"ms": ms_f, "gbs": fwd_gbs, "frac": fwd_gbs / hbm},
             "bwd": {"ms": ms_b, "gbs": bwd_gbs, "frac": bwd_gbs / hbm},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clk.record()}), flush=True)
+            "phases": phases, "clocks": clk.record()}), flush=True)
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -460,6 +598,9 @@ def main():
         return
     if args.workload == "c4":
         run_long(args, ws, rank, local)
+        return
+    if args.workload == "c5":
+        run_sweep(args, ws, rank, local)
         return
 
     import torch

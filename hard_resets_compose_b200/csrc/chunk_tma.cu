@@ -349,16 +349,18 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                 }
                 if (MODE == kReplay) st_vec<NPL>(ol + rr * NB + NPL * lane, lam);
             }
+            if (D) {
 #pragma unroll
-            for (int i = 0; i < NPL; i++) {
-                if (pp.v[i] != 0.f) {
-                    dn[i] += R;
-                } else if (pp_in.v[i] != 0.f) {  // the product reached 0 in this tile: find the row
-                    float q = pp_in.v[i];
-                    for (int rr = R - 1; rr >= 0; rr--) {
-                        q = av[rr].v[i] * q;
-                        if (q == 0.f) break;
-                        dn[i]++;
+                for (int i = 0; i < NPL; i++) {
+                    if (pp.v[i] != 0.f) {
+                        dn[i] += R;
+                    } else if (pp_in.v[i] != 0.f) {  // the product reached 0 in this tile: find the row
+                        float q = pp_in.v[i];
+                        for (int rr = R - 1; rr >= 0; rr--) {
+                            q = av[rr].v[i] * q;
+                            if (q == 0.f) break;
+                            dn[i]++;
+                        }
                     }
                 }
             }
