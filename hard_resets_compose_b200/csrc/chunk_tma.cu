@@ -191,11 +191,42 @@ struct BwdLayout {
     static constexpr int NT = 3 + (READ_S ? 1 : 0) + (HAS_GU ? 1 : 0);
 };
 
-// Adjoint coefficients lam_t = a*lam_{t+1} + c of NPL neurons at in-tile
-// offset `off` (no dependence on lam, so a whole tile is computed ahead).
+// log2(e): e^x = 2^(x log2 e), so the surrogate's exponential is one ex2.
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Adjoint coefficients of one neuron-step: lam_t = a*lam_{t+1} + c with the
+// forward's v = fl(fl(beta*u_{t-1}) + x_t) (bit for bit), s = S or [v >= theta],
+// the sigmoid surrogate sg = alpha*sig*(1 - sig), sig = 1/(1 + e),
+// e = exp(-alpha (v - theta)) = 2^(k2 (theta - v)) with k2 = alpha*log2(e), and
+// J = 1 - s (+ (u_r - v) sg for the attached reset), a = beta*J, c = gs*sg + J*gu.
+template <bool READ_S, bool HAS_GU>
+__device__ __forceinline__ void adj_coef(float up, float x, float sread, float gs, float gu, float beta, float theta,
+                                         float u_r, float alpha, float k2, bool detach, float &a, float &c)
+{
+    const float v = __fadd_rn(__fmul_rn(beta, up), x);
+    const float e = ex2_approx(k2 * (theta - v));
+    const float sig = rcp_approx(1.0f + e);
+    const float sg = alpha * sig * (1.0f - sig);
+    float cc = gs * sg;
+    if (!READ_S && detach) {  // s in {0, 1}: a = beta*(1 - s) and J*gu as selects
+        const bool spk = v >= theta;
+        a = spk ? 0.0f : beta;
+        if constexpr (HAS_GU) cc = spk ? cc : cc + gu;
+    } else {
+        const float s = READ_S ? sread : (v >= theta ? 1.0f : 0.0f);
+        float J = 1.0f - s;
+        if (!detach) J = J + (u_r - v) * sg;
+        a = beta * J;
+        if constexpr (HAS_GU) cc = cc + J * gu;
+    }
+    c = cc;
+}
+
+// Coefficients of NPL neurons at in-tile offset `off` (no dependence on lam,
+// so a whole tile is computed ahead of the chain).
 template <int NPL, bool READ_S, bool HAS_GU>
 __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec<NPL> &a, Vec<NPL> &c, float beta,
-                                         float theta, float u_r, float alpha, bool detach)
+                                         float theta, float u_r, float alpha, float k2, bool detach)
 {
     using Ly = BwdLayout<READ_S, HAS_GU>;
     const Vec<NPL> x = ld_vec<NPL>(b + Ly::kI * kTile + off);
@@ -205,28 +236,17 @@ __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec
     if constexpr (READ_S) sv = ld_vec<NPL>(b + Ly::kS * kTile + off);
     if constexpr (HAS_GU) gu = ld_vec<NPL>(b + Ly::kGU * kTile + off);
 #pragma unroll
-    for (int i = 0; i < NPL; i++) {
-        const float v = __fadd_rn(__fmul_rn(beta, up.v[i]), x.v[i]);  // the forward's v, bit for bit
-        float s;
-        if constexpr (READ_S) s = sv.v[i];
-        else s = v >= theta ? 1.0f : 0.0f;
-        const float e = __expf(-alpha * (v - theta));
-        const float sig = rcp_approx(1.0f + e);
-        const float sg = alpha * sig * (1.0f - sig);
-        float J = 1.0f - s;
-        if (!detach) J = J + (u_r - v) * sg;
-        a.v[i] = beta * J;
-        float cc = gs.v[i] * sg;
-        if constexpr (HAS_GU) cc = cc + J * gu.v[i];
-        c.v[i] = cc;
-    }
+    for (int i = 0; i < NPL; i++)
+        adj_coef<READ_S, HAS_GU>(up.v[i], x.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
+                                 theta, u_r, alpha, k2, detach, a.v[i], c.v[i]);
 }
 
-// One reverse step for NPL neurons at in-tile offset `off`.
-template <int NPL, bool READ_S, bool HAS_GU, int MODE>
+// One reverse step for NPL neurons at in-tile offset `off`; pp (the running
+// product of a) only when the chunk map is tracked.
+template <int NPL, bool READ_S, bool HAS_GU, bool TRACK>
 __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, const Vec<NPL> *up_override,
                                          Vec<NPL> &lam, Vec<NPL> &pp, float beta, float theta, float u_r,
-                                         float alpha, bool detach)
+                                         float alpha, float k2, bool detach)
 {
     using Ly = BwdLayout<READ_S, HAS_GU>;
     const Vec<NPL> x = ld_vec<NPL>(b + Ly::kI * kTile + off);
@@ -237,24 +257,15 @@ __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, con
     if constexpr (HAS_GU) gu = ld_vec<NPL>(b + Ly::kGU * kTile + off);
 #pragma unroll
     for (int i = 0; i < NPL; i++) {
-        const float v = __fadd_rn(__fmul_rn(beta, up.v[i]), x.v[i]);  // the forward's v, bit for bit
-        float s;
-        if constexpr (READ_S) s = sv.v[i];
-        else s = v >= theta ? 1.0f : 0.0f;
-        const float e = __expf(-alpha * (v - theta));
-        const float sig = rcp_approx(1.0f + e);
-        const float sg = alpha * sig * (1.0f - sig);
-        float J = 1.0f - s;
-        if (!detach) J = J + (u_r - v) * sg;
-        const float a = beta * J;
-        float c = gs.v[i] * sg;
-        if constexpr (HAS_GU) c = c + J * gu.v[i];
+        float a, c;
+        adj_coef<READ_S, HAS_GU>(up.v[i], x.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
+                                 theta, u_r, alpha, k2, detach, a, c);
         lam.v[i] = c + a * lam.v[i];
-        pp.v[i] = a * pp.v[i];
+        if constexpr (TRACK) pp.v[i] = a * pp.v[i];
     }
 }
 
-template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE>
+template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK>
 __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS,
@@ -321,6 +332,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
         if (MODE == kReplay && LamEnd) lam = ld_vec<NPL>(LamEnd + m * N + nl);
     }
     bool ok = true;
+    const float k2 = alpha * kLog2e;
 
     for (int64_t k = 0; k < ntiles; k++) {
         const int s = (int)(k % S);
@@ -334,7 +346,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
 #pragma unroll
             for (int rr = 0; rr < R; rr++)
                 bwd_coef<NPL, READ_S, HAS_GU>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta, theta, u_r, alpha,
-                                              detach);
+                                              k2, detach);
             if (MODE == kReplay && k >= 2) {
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
@@ -345,11 +357,11 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
                     lam.v[i] = cv[rr].v[i] + av[rr].v[i] * lam.v[i];
-                    pp.v[i] = av[rr].v[i] * pp.v[i];
+                    if constexpr (TRACK) pp.v[i] = av[rr].v[i] * pp.v[i];
                 }
                 if (MODE == kReplay) st_vec<NPL>(ol + rr * NB + NPL * lane, lam);
             }
-            if (D) {
+            if (TRACK && D) {
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
                     if (pp.v[i] != 0.f) {
@@ -376,10 +388,12 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             for (int rr = R - 1; rr >= 0; rr--) {
                 const int64_t t = rbase + rr;
                 if (t < cstart) break;
-                bwd_step<NPL, READ_S, HAS_GU, MODE>(b, kTile, rr * NB + NPL * lane, t == 0 ? &uz : nullptr, lam, pp,
-                                                    beta, theta, u_r, alpha, detach);
+                bwd_step<NPL, READ_S, HAS_GU, TRACK>(b, kTile, rr * NB + NPL * lane, t == 0 ? &uz : nullptr, lam,
+                                                     pp, beta, theta, u_r, alpha, k2, detach);
+                if constexpr (TRACK) {
 #pragma unroll
-                for (int i = 0; i < NPL; i++) dn[i] += pp.v[i] != 0.f ? 1 : 0;
+                    for (int i = 0; i < NPL; i++) dn[i] += pp.v[i] != 0.f ? 1 : 0;
+                }
                 if (MODE == kReplay && act) st_vec<NPL>(Lam + t * N + nl, lam);
             }
         }
@@ -389,7 +403,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
     if (!ok && status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
     // kCompose always writes the chunk map; kReplay writes it when P is given
     // (then P = prod a over the chunk and Q = lam at its first row).
-    if (ok && P && act) {
+    if (TRACK && ok && P && act) {
         st_vec<NPL>(P + m * N + nl, pp);
         st_vec<NPL>(Q + m * N + nl, lam);
         if (D) {
@@ -503,7 +517,7 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
     return true;
 }
 
-template <int NPL, bool READ_S, bool HAS_GU, int MODE>
+template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK>
 static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *LamEnd, float *Lam, float *P, float *Q,
                        int32_t *D, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
                        bool detach, int *status, cudaStream_t s)
@@ -512,7 +526,7 @@ static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *La
     constexpr int NT = BwdLayout<READ_S, HAS_GU>::NT;
     constexpr int R = BwdTile<NPL>::R, ST = BwdTile<NPL>::S;
     const size_t smem = ((size_t)ST * NT + (MODE == kReplay ? 2 : 0)) * R * NB * 4;
-    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE>;
+    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
@@ -520,17 +534,17 @@ static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *La
                              beta, theta, u_r, alpha, detach, status);
 }
 
-template <int NPL, int MODE>
+template <int NPL, int MODE, bool TRACK>
 static void launch_bwd_v(bool read_s, bool has_gu, const CUtensorMap *maps, const float *u0, const float *LamEnd,
                          float *Lam, float *P, float *Q, int32_t *D, int64_t N, int64_t M, int64_t C, float beta,
                          float theta, float u_r, float alpha, bool detach, int *status, cudaStream_t s)
 {
     if (read_s) {
-        if (has_gu) launch_bwd<NPL, true, true, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd<NPL, true, false, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        if (has_gu) launch_bwd<NPL, true, true, MODE, TRACK>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd<NPL, true, false, MODE, TRACK>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     } else {
-        if (has_gu) launch_bwd<NPL, false, true, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd<NPL, false, false, MODE>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        if (has_gu) launch_bwd<NPL, false, true, MODE, TRACK>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd<NPL, false, false, MODE, TRACK>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     }
 }
 
@@ -558,12 +572,15 @@ bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const fl
     if (mode == kReplay && !make_tmap_2d(&maps[5], Lam, N, T, nb, R)) return false;
     int *status = device_status_ptr();
     const bool rs = S != nullptr, g = GU != nullptr;
-    if (mode == kReplay) {
-        if (npl == 4) launch_bwd_v<4, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd_v<1, kReplay>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+    if (mode == kReplay && P) {
+        if (npl == 4) launch_bwd_v<4, kReplay, true>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd_v<1, kReplay, true>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+    } else if (mode == kReplay) {
+        if (npl == 4) launch_bwd_v<4, kReplay, false>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd_v<1, kReplay, false>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     } else {
-        if (npl == 4) launch_bwd_v<4, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
-        else launch_bwd_v<1, kCompose>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        if (npl == 4) launch_bwd_v<4, kCompose, true>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
+        else launch_bwd_v<1, kCompose, true>(rs, g, maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     }
     return true;
 }

@@ -206,7 +206,7 @@ __device__ __forceinline__ void coef_fix(float up, float s, float x, float gs, f
 {
     const float v = __fadd_rn(__fmul_rn(beta, up), x);
     if (s < 0.0f) s = v >= theta ? 1.0f : 0.0f;
-    const float e = __expf(-alpha * (v - theta));
+    const float e = ex2_approx(alpha * 1.4426950408889634f * (theta - v));  // exp(-alpha (v - theta))
     const float sig = rcp_approx(1.0f + e);
     const float sg = alpha * sig * (1.0f - sig);
     const float J = 1.0f - s;

@@ -100,6 +100,14 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 
 // Approximate reciprocal (hardware MUFU, ~1 ulp); used where the result
 // enters a gradient checked to 1e-5 relative.
+// 2^x (PTX ex2.approx, flush-to-zero).
+__device__ __forceinline__ float ex2_approx(float x)
+{
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 __device__ __forceinline__ float rcp_approx(float x)
 {
     float r;

@@ -1,0 +1,78 @@
+"""Differentiable hard-reset LIF with gradients w.r.t. the neuron parameters
+(beta, theta, u_r), for fitting neuron models to long recordings: the GPU
+half of the reference's lifscan/fit.py:15-61 (`LIFParamFn`, `lif_param`).
+
+Forward and backward run this package's kernels (serial, scan or auto
+dispatch, as the reference); the parameter gradients are read off the same
+adjoint lam_t = dL/dv_t by one fused pass (lifb_param_grad_partials):
+    dL/dbeta  = sum_t lam_t u_{t-1}
+    dL/dtheta = -sum_t gS_t sigma'(v_t - theta)      (detached reset)
+    dL/du_r   = sum_t s_t beta lam_{t+1}
+The reference's CPU prototype backend (`LIFParamFnCPU`, built on fast.py) is
+not part of this package: there is no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from . import lifscan as L
+from ._lib import check, ptr, stream_of
+
+__all__ = ["LIFParamFn", "lif_param", "param_grads"]
+
+
+def param_grads(I, u0, U, GS, Lam, beta, theta, alpha=4.0):
+    """(dL/dbeta, dL/dtheta, dL/du_r) as 0-d fp32 tensors from a detached-reset
+    adjoint Lam of the forward (I, u0) -> U with upstream gradient GS on S."""
+    I, u0, T, N = L._prep_fwd(I, u0)
+    U = L._cuda_f32("U", U, (T, N))
+    GS = L._cuda_f32("GS", GS, (T, N))
+    Lam = L._cuda_f32("Lam", Lam, (T, N))
+    lib = _lib.load()
+    M = max(lib.lifb_param_grad_chunks(T, N), 1)
+    part = torch.zeros(3, M, N, dtype=torch.float64, device=I.device)
+    with torch.cuda.device(I.device):
+        check(lib.lifb_param_grad_partials(ptr(I), ptr(u0), ptr(U), ptr(GS), ptr(Lam), ptr(part), T, N, float(beta),
+                                           float(theta), float(alpha), M, stream_of(I)), "param_grads")
+    g = part.sum(dim=(1, 2)).to(torch.float32)
+    return g[0], g[1], g[2]
+
+
+class LIFParamFn(torch.autograd.Function):
+    """lifscan/fit.py:15-47: spikes out; gradients for I, u0, beta, theta, u_r."""
+
+    @staticmethod
+    def forward(ctx, I, u0, beta, theta, u_r, alpha, fwd_mode, bwd_mode, K):
+        b, th, ur = float(beta), float(theta), float(u_r)
+        I = I.contiguous()
+        if fwd_mode == "scan":
+            U, S = L.scan_forward_auto(I, b, th, ur, u0, K=K)
+        else:
+            U, S = L.serial_forward_auto(I, b, th, ur, u0)
+        ctx.save_for_backward(I, u0, U)
+        ctx.cfg = (b, th, ur, alpha, bwd_mode)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        I, u0, U = ctx.saved_tensors
+        b, th, ur, alpha, bwd_mode = ctx.cfg
+        gS = gS.contiguous()
+        # S is this layer's own output (recomputed bit for bit) and GU is zero
+        if bwd_mode == "scan":
+            lam = L.scan_backward_auto(I, u0, U, None, gS, None, b, th, ur, alpha)
+        else:
+            lam = L.serial_backward_auto(I, u0, U, None, gS, None, b, th, ur, alpha)
+        g_beta, g_theta, g_ur = param_grads(I, u0, U, gS, lam, b, th, alpha)
+        return lam, b * lam[0], g_beta, g_theta, g_ur, None, None, None, None
+
+
+def lif_param(I, u0, beta, theta, u_r, alpha=4.0, mode="auto", K=16):
+    """lifscan/fit.py:50-56."""
+    T, N = I.shape
+    if mode == "auto":
+        fwd, bwd = L.auto_modes(N, T)
+    else:
+        fwd = bwd = mode
+    return LIFParamFn.apply(I, u0, beta, theta, u_r, alpha, fwd, bwd, K)

@@ -217,6 +217,19 @@ int lifb_scan_fwd_spec_finish(const float *I, const float *u0, float *U, float *
                               int64_t N, float beta, float theta, float u_r, int64_t L,
                               void *workspace, size_t workspace_bytes, void *stream);
 
+/* Parameter gradients of the fitting layer (lifscan/fit.py:15-61, LIFParamFn):
+ * from the adjoint Lam of a detached-reset backward, per chunk of rows and
+ * neuron, the fp64 partial sums of
+ *   dL/dbeta = sum_t Lam_t u_{t-1},  dL/dtheta = -sum_t GS_t sigma'(v_t - theta),
+ *   dL/du_r  = sum_t s_t beta Lam_{t+1}
+ * into partials [3][M][N] (the caller sums each [M][N] block); s_t and v_t
+ * are recomputed from U and I bit for bit.  M = lifb_param_grad_chunks(T, N)
+ * (or any 1..65535).  Reads I, U, GS, Lam once (16 B per neuron-step). */
+int lifb_param_grad_chunks(int64_t T, int64_t N);
+int lifb_param_grad_partials(const float *I, const float *u0, const float *U, const float *GS,
+                             const float *Lam, double *partials, int64_t T, int64_t N,
+                             float beta, float theta, float alpha, int M, void *stream);
+
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:
  * 944-983, scan_forward_v4; :512-526, scan_backward_tiled).  These phases
