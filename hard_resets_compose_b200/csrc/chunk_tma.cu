@@ -63,7 +63,12 @@ __device__ __forceinline__ void st_vec(float *p, const Vec<NPL> &a)
 }
 
 // ===================================================================== forward
-// Chunk m starts from Starts[m * start_stride] (rows of N) or u0.
+// Chunk m starts from Starts[m * start_stride] (rows of N) or u0.  With
+// lead > 0 (a multiple of R, with C a multiple of R) chunk m >= 1 instead
+// runs the `lead` rows before it first, without stores, from u_r (from u0
+// when they reach row 0, where the start is then exact), streamed through the
+// same TMA ring, and records that guessed start in LeadStarts[m]; chunk 0
+// starts from Starts[0] or u0 as before.
 template <int NPL, int R, int S>
 __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
@@ -71,7 +76,8 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
                                                 const float *__restrict__ Starts, int64_t start_stride,
                                                 float *__restrict__ U, float *__restrict__ Sout,
                                                 float *__restrict__ Ends, int64_t N, int64_t C, float beta,
-                                                float theta, float u_r, int *status)
+                                                float theta, float u_r, int64_t lead, float *__restrict__ LeadStarts,
+                                                int *status)
 {
     constexpr int NB = 32 * NPL;
     constexpr int kTile = R * NB;  // floats per tile
@@ -87,6 +93,12 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
     const int64_t nfull = C / R;
     const int rem = (int)(C - nfull * R);
     const int64_t ntiles = nfull + (rem ? 1 : 0);
+    // lead-in tiles before the chunk's own: rows [lrow0, row0)
+    const bool leading = lead > 0 && m > 0;
+    const int64_t lrow0 = leading ? (row0 > lead ? row0 - lead : 0) : row0;
+    const int64_t nlead = (row0 - lrow0) / R;
+    const int64_t ntot = nlead + ntiles;
+    auto tile_row = [&](int64_t k) { return k < nlead ? lrow0 + k * R : row0 + (k - nlead) * R; };
 
     if (lane == 0) {
         prefetch_tmap(&tI);
@@ -97,32 +109,63 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
     }
     __syncwarp();
     if (lane == 0) {
-        for (int s = 0; s < S && s < ntiles; s++) {
+        for (int s = 0; s < S && s < ntot; s++) {
             mbar_arrive_expect_tx(&full[s], kStageBytes);
-            tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)(row0 + s * R), &full[s]);
+            tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)tile_row(s), &full[s]);
         }
     }
     const int64_t nl = n0 + NPL * lane;
     const bool act = nl < N;
     Vec<NPL> u;
     if (act) {
-        u = ld_vec<NPL>((Starts ? Starts + m * start_stride * N : u0) + nl);
+        if (leading) {
+            if (lrow0 == 0) {
+                u = ld_vec<NPL>(u0 + nl);
+            } else {
+#pragma unroll
+                for (int i = 0; i < NPL; i++) u.v[i] = u_r;
+            }
+        } else {
+            u = ld_vec<NPL>((Starts ? Starts + m * start_stride * N : u0) + nl);
+        }
     } else {
 #pragma unroll
         for (int i = 0; i < NPL; i++) u.v[i] = 0.f;
     }
     bool ok = true;
 
-    for (int64_t k = 0; k < nfull; k++) {
+    for (int64_t k = 0; k < nlead; k++) {  // lead-in: states only
         const int s = (int)(k % S);
         if (!mbar_wait(&full[s], (uint32_t)((k / S) & 1))) { ok = false; break; }
         const float *in = ring + s * kTile + NPL * lane;
         Vec<NPL> x[R];
 #pragma unroll
         for (int r = 0; r < R; r++) x[r] = ld_vec<NPL>(in + r * NB);
-        float *ou = obuf + (int)(k & 1) * 2 * kTile;
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int i = 0; i < NPL; i++) u.v[i] = lif_step_u(u.v[i], x[r].v[i], beta, theta, u_r);
+        // the stage's rows are consumed (every lane used them): refill it
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0 && k + S < ntot) {
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)tile_row(k + S), &full[s]);
+        }
+    }
+    if (leading && ok && LeadStarts && act) st_vec<NPL>(LeadStarts + m * N + nl, u);
+
+    for (int64_t kk = 0; kk < nfull && ok; kk++) {
+        const int64_t k = nlead + kk;  // ring index
+        const int s = (int)(k % S);
+        if (!mbar_wait(&full[s], (uint32_t)((k / S) & 1))) { ok = false; break; }
+        const float *in = ring + s * kTile + NPL * lane;
+        Vec<NPL> x[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) x[r] = ld_vec<NPL>(in + r * NB);
+        float *ou = obuf + (int)(kk & 1) * 2 * kTile;
         float *os = ou + kTile;
-        if (k >= 2) {  // the store issued two tiles ago must have read this buffer
+        if (kk >= 2) {  // the store issued two tiles ago must have read this buffer
             if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
         }
@@ -141,17 +184,17 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) {
-            tma_store_2d(&tU, (int)n0, (int)(row0 + k * R), ou);
-            tma_store_2d(&tS, (int)n0, (int)(row0 + k * R), os);
+            tma_store_2d(&tU, (int)n0, (int)(row0 + kk * R), ou);
+            tma_store_2d(&tS, (int)n0, (int)(row0 + kk * R), os);
             bulk_commit();
-            if (k + S < ntiles) {
+            if (k + S < ntot) {
                 mbar_arrive_expect_tx(&full[s], kStageBytes);
-                tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)(row0 + (k + S) * R), &full[s]);
+                tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)tile_row(k + S), &full[s]);
             }
         }
     }
     if (ok && rem) {  // ragged last tile: checked rows, direct stores
-        const int64_t k = nfull;
+        const int64_t k = nlead + nfull;
         const int s = (int)(k % S);
         if (!mbar_wait(&full[s], (uint32_t)((k / S) & 1))) {
             ok = false;
@@ -167,7 +210,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
                     sp.v[i] = f ? 1.0f : 0.0f;
                 }
                 if (act) {
-                    const int64_t o = (row0 + k * R + r) * N + nl;
+                    const int64_t o = (row0 + nfull * R + r) * N + nl;
                     st_vec<NPL>(U + o, u);
                     st_vec<NPL>(Sout + o, sp);
                 }
@@ -484,7 +527,7 @@ static int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
 template <int NPL>
 static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, int64_t start_stride, float *U,
                        float *S, float *Ends, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r,
-                       int *status, cudaStream_t s)
+                       int64_t lead, float *LeadStarts, int *status, cudaStream_t s)
 {
     constexpr int NB = 32 * NPL;
     constexpr int R = FwdTile<NPL>::R, ST = FwdTile<NPL>::S;
@@ -494,26 +537,34 @@ static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *St
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
     kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], u0, Starts, start_stride, U, S, Ends, N, C, beta, theta, u_r,
-                             status);
+                             lead, LeadStarts, status);
 }
 
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
-                    int64_t start_stride)
+                    int64_t start_stride, int64_t lead, float *LeadStarts)
 {
-    const void *p[] = {I, u0, Starts, U, S, Ends};
-    if (!tma_ok(p, 6, N) || C <= 0 || T % C) return false;
+    const void *p[] = {I, u0, Starts, U, S, Ends, LeadStarts};
+    if (!tma_ok(p, 7, N) || C <= 0 || T % C) return false;
     const int64_t M = T / C;
     if (M > 65535) return false;
     const int npl = pick_npl(N, M, LIFB_FWD_NPL4_MIN_CTAS_PER_SM);
     const int R = npl == 4 ? FwdTile<4>::R : FwdTile<1>::R;
+    if (lead > 0) {  // lead-in tiles: whole tiles inside whole chunks
+        if (C % R) return false;
+        lead = (lead + R - 1) / R * R;
+    }
     CUtensorMap maps[3];
     if (!make_tmap_2d(&maps[0], I, N, T, 32 * npl, R) || !make_tmap_2d(&maps[1], U, N, T, 32 * npl, R) ||
         !make_tmap_2d(&maps[2], S, N, T, 32 * npl, R))
         return false;
     int *status = device_status_ptr();
-    if (npl == 4) launch_fwd<4>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
-    else launch_fwd<1>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, status, s);
+    if (npl == 4)
+        launch_fwd<4>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, status,
+                      s);
+    else
+        launch_fwd<1>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, status,
+                      s);
     return true;
 }
 

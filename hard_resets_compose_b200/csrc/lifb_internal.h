@@ -38,9 +38,13 @@ int read_device_status(bool reset);       // synchronous read (current device)
 // apply (N % 4 != 0, a misaligned tensor, more than 65535 chunks).
 // Forward replay of M = T/C chunks from Starts (NULL: one chunk from u0).
 // Chunk m starts from Starts[m * start_stride] (in rows of N).
+// lead > 0: chunk m >= 1 starts from a lead-in over the `lead` rows before it
+// (from u_r, or from u0 when they reach row 0), streamed through the same
+// ring, and records that start in LeadStarts[m] (Starts is then ignored for
+// m >= 1); requires C % R == 0 (false otherwise), lead is rounded up to R.
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
-                    int64_t start_stride = 1);
+                    int64_t start_stride = 1, int64_t lead = 0, float *LeadStarts = nullptr);
 // Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0)
 // and, when P is given, also the chunk maps; mode 1 writes only P, Q.
 // P[m] = prod of a_t over chunk m, Q[m] = lam at the chunk's first row.

@@ -7,11 +7,13 @@
 // the same input end up bit-identical once they spike in the same row (or
 // their difference rounds away), typically within a few hundred rows.  So:
 //
-//   k_leadin  the start of each segment of L rows, guessed by running the W rows
+//   lead-in   the start of each segment of L rows, guessed by running the W rows
 //             before it from u_r ("just reset"); segment 0 starts from u0, and
 //             a lead-in that reaches row 0 starts from u0 too (then it is exact).
-//             With a halo (rows before row 0, e.g. the end of the previous
-//             time slice), segment 0 starts from u0 run through the halo.
+//             Normally inside the replay kernel (k_fwd_tma streams the lead-in
+//             rows through its TMA ring before the segment's own); k_leadin
+//             below does it as a separate pass for a halo (rows before row 0,
+//             e.g. the end of the previous time slice) and the two-call form.
 //   replay    every segment from its guessed start (k_fwd_tma: TMA-staged rows,
 //             TMA-store epilogue), all segments at once
 //   fix-up    per neuron, in time order, every segment whose guessed start
@@ -187,8 +189,15 @@ int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S, int6
     } else {
         if ((st = spec_ws("lifb_scan_fwd_spec", T, N, L, workspace, workspace_bytes))) return st;
         SpecScratch w = spec_carve(workspace, NS, N);
-        lifb::leadin_starts(I, u0, I_halo, W_halo, w.Starts, nullptr, N, NS, L, W, beta, theta, u_r, s);
-        lifb::replay_any(I, u0, w.Starts, U, S, w.Ends, T, N, L, beta, theta, u_r, s);
+        // one launch when it applies: each segment's CTA streams its lead-in
+        // rows through the replay's own TMA ring and records its start
+        const bool fused = !(I_halo && W_halo > 0) && W > 0 &&
+                           lifb::fwd_replay_tma(I, u0, nullptr, U, S, w.Ends, T, N, L, beta, theta, u_r, s, 1, W,
+                                                w.Starts);
+        if (!fused) {
+            lifb::leadin_starts(I, u0, I_halo, W_halo, w.Starts, nullptr, N, NS, L, W, beta, theta, u_r, s);
+            lifb::replay_any(I, u0, w.Starts, U, S, w.Ends, T, N, L, beta, theta, u_r, s);
+        }
         lifb::fwd_fixup(I, w.Starts, 1, U, S, w.Ends, w.EndsNew, w.Changed, N, NS, L, beta, theta, u_r, nullptr, s);
     }
     return spec_done("lifb_scan_fwd_spec");
