@@ -37,10 +37,13 @@ T_STEPS = 1024
 N_PER_GPU = 16384
 BETA = 0.99
 MU, SD = 0.05, 0.2
-FWD_BYTES = 12   # read I, write U and S (fp32) per neuron-step
-# lif_tuned's backward reads I, U[t-1], GS and writes Lam; GU is identically
-# zero and S is recomputed bit-exactly from U and I, so neither is read.
+FWD_BYTES = 12   # read I, write U (or V) and S (fp32) per neuron-step
+# lif_tuned's backward reads I, U[t-1], GS and writes Lam (GU is identically
+# zero and S is recomputed bit-exactly from U and I); when its forward is the
+# single pass it saves V (the pre-reset potential) instead of U and the
+# backward reads V and GS only.
 BWD_BYTES = 16
+BWD_BYTES_V = 12
 METRIC = "neuron-steps/s, lif_tuned fwd+bwd (B*N=16384/GPU, T=1024)"
 UNIT = "neuron-steps/s"
 FALLBACK_HBM_GBS = 6650.0
@@ -711,13 +714,21 @@ def main():
     ms = max_over_ranks(ms_local)
     value = units / (ms / 1e3)
 
-    # forward-only and per-call timings (roofline of the dominant call)
+    # forward-only and per-call timings (roofline of the dominant call): the
+    # calls lif_tuned itself makes for this shape and mode
+    vpath = L._single_pass(T, N, args.mode) and args.mode != "auto"
+    bwd_bytes = BWD_BYTES_V if vpath else BWD_BYTES
+
     def fwd_call():
+        if vpath:
+            return L.serial_forward_v(I, BETA, 1.0, 0.0, u0)
         return L.scan_forward_auto(I, BETA, 1.0, 0.0, u0) if args.mode == "scan" else \
             L.serial_forward_auto(I, BETA, 1.0, 0.0, u0)
     U, S = fwd_call()
 
     def bwd_call():  # exactly lif_tuned's backward call (S recomputed, GU zero)
+        if vpath:
+            return L.lif_backward_v(U, GS, BETA, 1.0, 4.0, C=T if args.mode == "serial" else L.scan_chunk_bwd(T, N))
         if args.mode == "scan":
             return L.scan_backward_auto(I, u0, U, None, GS, None, BETA, 1.0, 0.0, 4.0)
         return L.serial_backward_auto(I, u0, U, None, GS, None, BETA, 1.0, 0.0, 4.0)
@@ -733,21 +744,22 @@ def main():
     hbm, peak_kind = peaks()
     per_call = {
         "fwd": {"ms": ms_fwd, "bytes": FWD_BYTES * N * T, "launches": n_fwd},
-        "bwd": {"ms": ms_bwd, "bytes": BWD_BYTES * N * T, "launches": n_bwd},
+        "bwd": {"ms": ms_bwd, "bytes": bwd_bytes * N * T, "launches": n_bwd},
     }
     for v in per_call.values():
         v["gbs"] = v["bytes"] / (v["ms"] / 1e3) / 1e9
         v["frac"] = v["gbs"] / hbm
     dom = "fwd" if ms_fwd >= ms_bwd else "bwd"
     kname = {"fwd": f"lifb forward ({args.mode})", "bwd": f"lifb backward ({args.mode})"}[dom]
-    tpu = traffic_per_unit(f"{args.mode}_{dom}")
+    tpu = traffic_per_unit(f"{args.mode}_{dom}" + ("_v" if vpath else ""))
     roofline = {
         "bound": "hbm", "kernel": kname, "launches_per_call": per_call[dom]["launches"],
         "achieved": per_call[dom]["gbs"], "peak": hbm, "peak_source": peak_kind, "unit": "GB/s",
         "frac": per_call[dom]["frac"],
         "traffic": (tpu * N * T) if tpu is not None else None,
         "algorithmic_bytes": per_call[dom]["bytes"],
-        "step_frac": ((FWD_BYTES + BWD_BYTES) * N * T) / (ms_local / 1e3) / 1e9 / hbm,
+        "step_frac": ((FWD_BYTES + bwd_bytes) * N * T) / (ms_local / 1e3) / 1e9 / hbm,
+        "step_bytes_per_neuron_step": FWD_BYTES + bwd_bytes,
     }
 
     # end to end through the public API with host buffers: lif_tuned_host

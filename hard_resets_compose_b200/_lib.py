@@ -60,6 +60,11 @@ SIGNATURES = {
     "lifb_param_grad_chunks": ([c_i64, c_i64], c_int),
     "lifb_param_grad_partials": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float,
                                   c_float, c_float, c_int, c_void_p], c_int),
+    "lifb_serial_fwd_v": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
+                           c_void_p], c_int),
+    "lifb_lif_bwd_v_workspace_bytes": ([c_i64, c_i64, c_int], c_size_t),
+    "lifb_lif_bwd_v": ([c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float, c_int, c_void_p,
+                        c_size_t, c_void_p], c_int),
     "lifb_tshard_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
     "lifb_tshard_envelope": ([c_void_p, c_i64, c_i64, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p], c_int),

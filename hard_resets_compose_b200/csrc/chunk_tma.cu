@@ -28,6 +28,8 @@
 //
 // The launchers fall back (return false) unless N % 4 == 0 and every tensor
 // is 16-byte aligned (TMA stride rule and vector accesses).
+#include <type_traits>
+
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
 #include "tma.cuh"
@@ -68,8 +70,9 @@ __device__ __forceinline__ void st_vec(float *p, const Vec<NPL> &a)
 // runs the `lead` rows before it first, without stores, from u_r (from u0
 // when they reach row 0, where the start is then exact), streamed through the
 // same TMA ring, and records that guessed start in LeadStarts[m]; chunk 0
-// starts from Starts[0] or u0 as before.
-template <int NPL, int R, int S>
+// starts from Starts[0] or u0 as before.  VOUT: the U output receives the
+// pre-reset potential v_t instead of u_t (Ends still hold u).
+template <int NPL, int R, int S, bool VOUT>
 __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS, const float *__restrict__ u0,
@@ -171,14 +174,16 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
         }
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            Vec<NPL> sp;
+            Vec<NPL> sp, vv;
 #pragma unroll
             for (int i = 0; i < NPL; i++) {
-                bool f;
-                u.v[i] = lif_step(u.v[i], x[r].v[i], beta, theta, u_r, f);
+                const float v = __fadd_rn(__fmul_rn(beta, u.v[i]), x[r].v[i]);
+                const bool f = v >= theta;
+                u.v[i] = f ? u_r : v;
                 sp.v[i] = f ? 1.0f : 0.0f;
+                vv.v[i] = v;
             }
-            st_vec<NPL>(ou + r * NB + NPL * lane, u);
+            st_vec<NPL>(ou + r * NB + NPL * lane, VOUT ? vv : u);
             st_vec<NPL>(os + r * NB + NPL * lane, sp);
         }
         fence_proxy_async_shared();
@@ -202,16 +207,18 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
             const float *in = ring + s * kTile + NPL * lane;
             for (int r = 0; r < rem; r++) {
                 const Vec<NPL> x = ld_vec<NPL>(in + r * NB);
-                Vec<NPL> sp;
+                Vec<NPL> sp, vv;
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
-                    bool f;
-                    u.v[i] = lif_step(u.v[i], x.v[i], beta, theta, u_r, f);
+                    const float v = __fadd_rn(__fmul_rn(beta, u.v[i]), x.v[i]);
+                    const bool f = v >= theta;
+                    u.v[i] = f ? u_r : v;
                     sp.v[i] = f ? 1.0f : 0.0f;
+                    vv.v[i] = v;
                 }
                 if (act) {
                     const int64_t o = (row0 + nfull * R + r) * N + nl;
-                    st_vec<NPL>(U + o, u);
+                    st_vec<NPL>(U + o, VOUT ? vv : u);
                     st_vec<NPL>(Sout + o, sp);
                 }
             }
@@ -225,13 +232,15 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
 // ==================================================================== backward
 enum BwdMode { kReplay = 0, kCompose = 1 };
 
-// Input tensors per stage, in ring order: I, U (one row earlier), [S], GS, [GU].
-template <bool READ_S, bool HAS_GU>
+// Input tensors per stage, in ring order: I, U (one row earlier), [S], GS, [GU];
+// FROM_V (the forward saved v_t = fl(fl(beta*u_{t-1}) + x_t) in place of U):
+// V (slot kI), GS.
+template <bool READ_S, bool HAS_GU, bool FROM_V = false>
 struct BwdLayout {
     static constexpr int kI = 0, kU = 1, kS = 2;
-    static constexpr int kGS = READ_S ? 3 : 2;
+    static constexpr int kGS = FROM_V ? 1 : (READ_S ? 3 : 2);
     static constexpr int kGU = kGS + 1;
-    static constexpr int NT = 3 + (READ_S ? 1 : 0) + (HAS_GU ? 1 : 0);
+    static constexpr int NT = FROM_V ? 2 : 3 + (READ_S ? 1 : 0) + (HAS_GU ? 1 : 0);
 };
 
 // log2(e): e^x = 2^(x log2 e), so the surrogate's exponential is one ex2.
@@ -242,16 +251,19 @@ constexpr float kLog2e = 1.4426950408889634f;
 // the sigmoid surrogate sg = alpha*sig*(1 - sig), sig = 1/(1 + e),
 // e = exp(-alpha (v - theta)) = 2^(k2 (theta - v)) with k2 = alpha*log2(e), and
 // J = 1 - s (+ (u_r - v) sg for the attached reset), a = beta*J, c = gs*sg + J*gu.
-template <bool READ_S, bool HAS_GU>
-__device__ __forceinline__ void adj_coef(float up, float x, float sread, float gs, float gu, float beta, float theta,
-                                         float u_r, float alpha, float k2, bool detach, float &a, float &c)
+// k2 = alpha*log2(e), k2t = k2*theta: the exponent k2*(theta - v) is one FMA.
+// sig*(1 - sig) = sig - sig^2 (one FMA).  DET: the detached reset, known at
+// compile time (the V path has no other).
+template <bool READ_S, bool HAS_GU, bool DET = false>
+__device__ __forceinline__ void adj_coef_v(float v, float sread, float gs, float gu, float beta, float theta,
+                                           float u_r, float alpha, float k2, float k2t, bool detach, float &a,
+                                           float &c)
 {
-    const float v = __fadd_rn(__fmul_rn(beta, up), x);
-    const float e = ex2_approx(k2 * (theta - v));
+    const float e = ex2_approx(fmaf(-k2, v, k2t));
     const float sig = rcp_approx(1.0f + e);
-    const float sg = alpha * sig * (1.0f - sig);
+    const float sg = alpha * fmaf(-sig, sig, sig);
     float cc = gs * sg;
-    if (!READ_S && detach) {  // s in {0, 1}: a = beta*(1 - s) and J*gu as selects
+    if (!READ_S && (DET || detach)) {  // s in {0, 1}: a = beta*(1 - s) and J*gu as selects
         const bool spk = v >= theta;
         a = spk ? 0.0f : beta;
         if constexpr (HAS_GU) cc = spk ? cc : cc + gu;
@@ -265,35 +277,46 @@ __device__ __forceinline__ void adj_coef(float up, float x, float sread, float g
     c = cc;
 }
 
+// The forward's v, bit for bit, from U[t-1] and I[t]; or read (FROM_V).
+template <int NPL, bool FROM_V, typename Ly>
+__device__ __forceinline__ Vec<NPL> bwd_v(const float *b, int kTile, int off, const Vec<NPL> *up_override, float beta)
+{
+    Vec<NPL> v = ld_vec<NPL>(b + Ly::kI * kTile + off);
+    if constexpr (!FROM_V) {
+        const Vec<NPL> up = up_override ? *up_override : ld_vec<NPL>(b + Ly::kU * kTile + off);
+#pragma unroll
+        for (int i = 0; i < NPL; i++) v.v[i] = __fadd_rn(__fmul_rn(beta, up.v[i]), v.v[i]);
+    }
+    return v;
+}
+
 // Coefficients of NPL neurons at in-tile offset `off` (no dependence on lam,
 // so a whole tile is computed ahead of the chain).
-template <int NPL, bool READ_S, bool HAS_GU>
+template <int NPL, bool READ_S, bool HAS_GU, bool FROM_V>
 __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec<NPL> &a, Vec<NPL> &c, float beta,
-                                         float theta, float u_r, float alpha, float k2, bool detach)
+                                         float theta, float u_r, float alpha, float k2, float k2t, bool detach)
 {
-    using Ly = BwdLayout<READ_S, HAS_GU>;
-    const Vec<NPL> x = ld_vec<NPL>(b + Ly::kI * kTile + off);
-    const Vec<NPL> up = ld_vec<NPL>(b + Ly::kU * kTile + off);
+    using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
+    const Vec<NPL> v = bwd_v<NPL, FROM_V, Ly>(b, kTile, off, nullptr, beta);
     const Vec<NPL> gs = ld_vec<NPL>(b + Ly::kGS * kTile + off);
     Vec<NPL> sv, gu;
     if constexpr (READ_S) sv = ld_vec<NPL>(b + Ly::kS * kTile + off);
     if constexpr (HAS_GU) gu = ld_vec<NPL>(b + Ly::kGU * kTile + off);
 #pragma unroll
     for (int i = 0; i < NPL; i++)
-        adj_coef<READ_S, HAS_GU>(up.v[i], x.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
-                                 theta, u_r, alpha, k2, detach, a.v[i], c.v[i]);
+        adj_coef_v<READ_S, HAS_GU, FROM_V>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
+                                           theta, u_r, alpha, k2, k2t, detach, a.v[i], c.v[i]);
 }
 
 // One reverse step for NPL neurons at in-tile offset `off`; pp (the running
 // product of a) only when the chunk map is tracked.
-template <int NPL, bool READ_S, bool HAS_GU, bool TRACK>
+template <int NPL, bool READ_S, bool HAS_GU, bool TRACK, bool FROM_V>
 __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, const Vec<NPL> *up_override,
                                          Vec<NPL> &lam, Vec<NPL> &pp, float beta, float theta, float u_r,
-                                         float alpha, float k2, bool detach)
+                                         float alpha, float k2, float k2t, bool detach)
 {
-    using Ly = BwdLayout<READ_S, HAS_GU>;
-    const Vec<NPL> x = ld_vec<NPL>(b + Ly::kI * kTile + off);
-    const Vec<NPL> up = up_override ? *up_override : ld_vec<NPL>(b + Ly::kU * kTile + off);
+    using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
+    const Vec<NPL> v = bwd_v<NPL, FROM_V, Ly>(b, kTile, off, up_override, beta);
     const Vec<NPL> gs = ld_vec<NPL>(b + Ly::kGS * kTile + off);
     Vec<NPL> sv, gu;
     if constexpr (READ_S) sv = ld_vec<NPL>(b + Ly::kS * kTile + off);
@@ -301,14 +324,14 @@ __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, con
 #pragma unroll
     for (int i = 0; i < NPL; i++) {
         float a, c;
-        adj_coef<READ_S, HAS_GU>(up.v[i], x.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
-                                 theta, u_r, alpha, k2, detach, a, c);
+        adj_coef_v<READ_S, HAS_GU, FROM_V>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
+                                           theta, u_r, alpha, k2, k2t, detach, a, c);
         lam.v[i] = c + a * lam.v[i];
         if constexpr (TRACK) pp.v[i] = a * pp.v[i];
     }
 }
 
-template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK>
+template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V>
 __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS,
@@ -320,7 +343,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                                                 int32_t *__restrict__ D, int64_t N, int64_t C, float beta, float theta,
                                                 float u_r, float alpha, bool detach, int *status)
 {
-    using Ly = BwdLayout<READ_S, HAS_GU>;
+    using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
     constexpr int NB = 32 * NPL;
     constexpr int NT = Ly::NT;
     constexpr int kTile = R * NB;
@@ -342,7 +365,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
         float *b = ring + (size_t)s * NT * kTile;
         mbar_arrive_expect_tx(&full[s], kStageBytes);
         tma_load_2d(b + Ly::kI * kTile, &tI, (int)n0, row, &full[s]);
-        tma_load_2d(b + Ly::kU * kTile, &tU, (int)n0, row - 1, &full[s]);
+        if (!FROM_V) tma_load_2d(b + Ly::kU * kTile, &tU, (int)n0, row - 1, &full[s]);
         if (READ_S) tma_load_2d(b + Ly::kS * kTile, &tS, (int)n0, row, &full[s]);
         tma_load_2d(b + Ly::kGS * kTile, &tGS, (int)n0, row, &full[s]);
         if (HAS_GU) tma_load_2d(b + Ly::kGU * kTile, &tGU, (int)n0, row, &full[s]);
@@ -371,11 +394,11 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
 #pragma unroll
     for (int i = 0; i < NPL; i++) { uz.v[i] = 0.f; lam.v[i] = 0.f; pp.v[i] = 1.f; dn[i] = 0; }
     if (act) {
-        uz = ld_vec<NPL>(u0 + nl);
+        if (!FROM_V) uz = ld_vec<NPL>(u0 + nl);
         if (MODE == kReplay && LamEnd) lam = ld_vec<NPL>(LamEnd + m * N + nl);
     }
     bool ok = true;
-    const float k2 = alpha * kLog2e;
+    const float k2 = alpha * kLog2e, k2t = k2 * theta;
 
     for (int64_t k = 0; k < ntiles; k++) {
         const int s = (int)(k % S);
@@ -388,8 +411,8 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             Vec<NPL> av[R], cv[R];
 #pragma unroll
             for (int rr = 0; rr < R; rr++)
-                bwd_coef<NPL, READ_S, HAS_GU>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta, theta, u_r, alpha,
-                                              k2, detach);
+                bwd_coef<NPL, READ_S, HAS_GU, FROM_V>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta, theta,
+                                                      u_r, alpha, k2, k2t, detach);
             if (MODE == kReplay && k >= 2) {
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
@@ -431,8 +454,9 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             for (int rr = R - 1; rr >= 0; rr--) {
                 const int64_t t = rbase + rr;
                 if (t < cstart) break;
-                bwd_step<NPL, READ_S, HAS_GU, TRACK>(b, kTile, rr * NB + NPL * lane, t == 0 ? &uz : nullptr, lam,
-                                                     pp, beta, theta, u_r, alpha, k2, detach);
+                bwd_step<NPL, READ_S, HAS_GU, TRACK, FROM_V>(b, kTile, rr * NB + NPL * lane,
+                                                             (!FROM_V && t == 0) ? &uz : nullptr, lam, pp, beta,
+                                                             theta, u_r, alpha, k2, k2t, detach);
                 if constexpr (TRACK) {
 #pragma unroll
                     for (int i = 0; i < NPL; i++) dn[i] += pp.v[i] != 0.f ? 1 : 0;
@@ -524,7 +548,7 @@ static int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
     return ((N + 127) / 128) * M >= (int64_t)min_ctas_per_sm * sms ? 4 : 1;
 }
 
-template <int NPL>
+template <int NPL, bool VOUT>
 static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, int64_t start_stride, float *U,
                        float *S, float *Ends, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r,
                        int64_t lead, float *LeadStarts, int *status, cudaStream_t s)
@@ -532,7 +556,7 @@ static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *St
     constexpr int NB = 32 * NPL;
     constexpr int R = FwdTile<NPL>::R, ST = FwdTile<NPL>::S;
     const size_t smem = (size_t)(ST + 4) * R * NB * 4;
-    auto kern = k_fwd_tma<NPL, R, ST>;
+    auto kern = k_fwd_tma<NPL, R, ST, VOUT>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
@@ -542,7 +566,7 @@ static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *St
 
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
-                    int64_t start_stride, int64_t lead, float *LeadStarts)
+                    int64_t start_stride, int64_t lead, float *LeadStarts, bool vout)
 {
     const void *p[] = {I, u0, Starts, U, S, Ends, LeadStarts};
     if (!tma_ok(p, 7, N) || C <= 0 || T % C) return false;
@@ -559,25 +583,30 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
         !make_tmap_2d(&maps[2], S, N, T, 32 * npl, R))
         return false;
     int *status = device_status_ptr();
-    if (npl == 4)
-        launch_fwd<4>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, status,
-                      s);
-    else
-        launch_fwd<1>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, status,
-                      s);
+    auto go = [&](auto npl_c, auto vout_c) {
+        launch_fwd<decltype(npl_c)::value, decltype(vout_c)::value>(maps, u0, Starts, start_stride, U, S, Ends, N, M,
+                                                                     C, beta, theta, u_r, lead, LeadStarts, status,
+                                                                     s);
+    };
+    using I1 = std::integral_constant<int, 1>;
+    using I4 = std::integral_constant<int, 4>;
+    using BT = std::true_type;
+    using BF = std::false_type;
+    if (npl == 4) vout ? go(I4{}, BT{}) : go(I4{}, BF{});
+    else vout ? go(I1{}, BT{}) : go(I1{}, BF{});
     return true;
 }
 
-template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK>
+template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V = false>
 static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *LamEnd, float *Lam, float *P, float *Q,
                        int32_t *D, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
                        bool detach, int *status, cudaStream_t s)
 {
     constexpr int NB = 32 * NPL;
-    constexpr int NT = BwdLayout<READ_S, HAS_GU>::NT;
+    constexpr int NT = BwdLayout<READ_S, HAS_GU, FROM_V>::NT;
     constexpr int R = BwdTile<NPL>::R, ST = BwdTile<NPL>::S;
     const size_t smem = ((size_t)ST * NT + (MODE == kReplay ? 2 : 0)) * R * NB * 4;
-    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK>;
+    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
@@ -597,6 +626,34 @@ static void launch_bwd_v(bool read_s, bool has_gu, const CUtensorMap *maps, cons
         if (has_gu) launch_bwd<NPL, false, true, MODE, TRACK>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
         else launch_bwd<NPL, false, false, MODE, TRACK>(maps, u0, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, u_r, alpha, detach, status, s);
     }
+}
+
+// Adjoint from V (the forward's pre-reset potentials), GS: detached reset,
+// S recomputed as [v >= theta], no GU.  Same outputs as bwd_tma mode 0.
+bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, int32_t *D, int64_t T, int64_t N,
+               int64_t C, float beta, float theta, float alpha, cudaStream_t s)
+{
+    const void *p[] = {V, GS, Lam, P, Q, D};
+    if (!tma_ok(p, 6, N) || C <= 0 || T % C) return false;
+    const int64_t M = T / C;
+    if (M > 65535) return false;
+    const int npl = pick_npl(N, M, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
+    const int nb = 32 * npl;
+    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    CUtensorMap maps[6];
+    if (!make_tmap_2d(&maps[0], V, N, T, nb, R) || !make_tmap_2d(&maps[3], GS, N, T, nb, R) ||
+        !make_tmap_2d(&maps[5], Lam, N, T, nb, R))
+        return false;
+    maps[1] = maps[2] = maps[4] = maps[0];
+    int *status = device_status_ptr();
+    if (P) {
+        if (npl == 4) launch_bwd<4, false, false, kReplay, true, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+        else launch_bwd<1, false, false, kReplay, true, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+    } else {
+        if (npl == 4) launch_bwd<4, false, false, kReplay, false, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+        else launch_bwd<1, false, false, kReplay, false, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+    }
+    return true;
 }
 
 bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const float *S, const float *GS,

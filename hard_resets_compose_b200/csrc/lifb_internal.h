@@ -44,7 +44,7 @@ int read_device_status(bool reset);       // synchronous read (current device)
 // m >= 1); requires C % R == 0 (false otherwise), lead is rounded up to R.
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
-                    int64_t start_stride = 1, int64_t lead = 0, float *LeadStarts = nullptr);
+                    int64_t start_stride = 1, int64_t lead = 0, float *LeadStarts = nullptr, bool vout = false);
 // Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0)
 // and, when P is given, also the chunk maps; mode 1 writes only P, Q.
 // P[m] = prod of a_t over chunk m, Q[m] = lam at the chunk's first row.
@@ -55,12 +55,24 @@ bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const fl
              const float *GU, const float *LamEnd, float *Lam, float *P, float *Q, int64_t T, int64_t N, int64_t C,
              float beta, float theta, float u_r, float alpha, bool detach, cudaStream_t s, int32_t *D = nullptr);
 
+// chunk_tma.cu: the adjoint from V (the forward's pre-reset potentials v_t)
+// and GS only: detached reset, s recomputed as [v >= theta], no GU.  P, Q, D
+// as bwd_tma when P is given; false when the TMA path does not apply.
+bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, int32_t *D, int64_t T, int64_t N,
+               int64_t C, float beta, float theta, float alpha, cudaStream_t s);
+
 // serial.cu
 void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                 float theta, float u_r, cudaStream_t s);
 void serial_bwd(const float *I, const float *u0, const float *U, const float *S, const float *GS,
                 const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
                 float alpha, bool detach, cudaStream_t s);
+// The same forward writing V (pre-reset potentials v_t) in place of U, and
+// the adjoint from V and GS (detached reset, s = [v >= theta], no GU).
+void serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N, float beta,
+                  float theta, float u_r, cudaStream_t s);
+void serial_bwd_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta, float theta,
+                  float alpha, cudaStream_t s);
 
 // scan_fwd_grid.cu
 // grid_envelope / grid_build / grid_compose work on the first M chunks (M2

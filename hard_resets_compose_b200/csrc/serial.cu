@@ -14,7 +14,8 @@ namespace lifb {
 constexpr int kSerBlock = 128;
 constexpr int kSerD = 16;
 
-template <int D>
+// VOUT: U receives the pre-reset potential v_t instead of u_t.
+template <int D, bool VOUT>
 __global__ void __launch_bounds__(kSerBlock) k_serial_fwd(const float *__restrict__ I, const float *__restrict__ u0,
                                                           float *__restrict__ U, float *__restrict__ S, int64_t T,
                                                           int64_t N, float beta, float theta, float u_r)
@@ -37,10 +38,11 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_fwd(const float *__restric
         }
 #pragma unroll
         for (int d = 0; d < D; d++) {
-            bool s;
-            u = lif_step(u, cur[d], beta, theta, u_r, s);
+            const float v = __fadd_rn(__fmul_rn(beta, u), cur[d]);
+            const bool s = v >= theta;
+            u = s ? u_r : v;
             int64_t o = (t0 + d) * N + n;
-            U[o] = u;
+            U[o] = VOUT ? v : u;
             S[o] = s ? 1.0f : 0.0f;
         }
         if (more) {
@@ -49,10 +51,45 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_fwd(const float *__restric
         }
     }
     for (int64_t t = Tf; t < T; t++) {
-        bool s;
-        u = lif_step(u, __ldg(p + t * N), beta, theta, u_r, s);
-        U[t * N + n] = u;
+        const float v = __fadd_rn(__fmul_rn(beta, u), __ldg(p + t * N));
+        const bool s = v >= theta;
+        u = s ? u_r : v;
+        U[t * N + n] = VOUT ? v : u;
         S[t * N + n] = s ? 1.0f : 0.0f;
+    }
+}
+
+// Reverse sweep from V (pre-reset potentials) and GS: detached reset, s = [v >= theta], no GU.
+template <int D>
+__global__ void __launch_bounds__(kSerBlock) k_serial_bwd_v(const float *__restrict__ V, const float *__restrict__ GS,
+                                                            float *__restrict__ Lam, int64_t T, int64_t N, float beta,
+                                                            float theta, float alpha)
+{
+    int64_t n = (int64_t)blockIdx.x * kSerBlock + threadIdx.x;
+    if (n >= N) return;
+    float lam = 0.0f;
+    for (int64_t tend = T; tend > 0; tend -= D) {
+        int64_t t0 = tend - D > 0 ? tend - D : 0;
+        int cnt = (int)(tend - t0);
+        float v[D], gs[D];
+#pragma unroll
+        for (int d = 0; d < D; d++) {
+            if (d < cnt) {
+                const int64_t o = (t0 + d) * N + n;
+                v[d] = __ldg(V + o);
+                gs[d] = __ldg(GS + o);
+            }
+        }
+#pragma unroll
+        for (int dd = D - 1; dd >= 0; dd--) {
+            if (dd < cnt) {
+                const float s = v[dd] >= theta ? 1.0f : 0.0f;
+                const float sig = __frcp_rn(1.0f + __expf(-alpha * (v[dd] - theta)));
+                const float sg = alpha * sig * (1.0f - sig);
+                lam = gs[dd] * sg + beta * (1.0f - s) * lam;
+                Lam[(t0 + dd) * N + n] = lam;
+            }
+        }
     }
 }
 
@@ -102,7 +139,25 @@ void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, 
     if (fwd_replay_tma(I, u0, nullptr, U, S, nullptr, T, N, T, beta, theta, u_r, s)) return;
     unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
     count_launches(1);
-    k_serial_fwd<kSerD><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, u_r);
+    k_serial_fwd<kSerD, false><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, u_r);
+}
+
+void serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N, float beta,
+                  float theta, float u_r, cudaStream_t s)
+{
+    if (fwd_replay_tma(I, u0, nullptr, V, S, nullptr, T, N, T, beta, theta, u_r, s, 1, 0, nullptr, true)) return;
+    unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
+    count_launches(1);
+    k_serial_fwd<kSerD, true><<<g, kSerBlock, 0, s>>>(I, u0, V, S, T, N, beta, theta, u_r);
+}
+
+void serial_bwd_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta, float theta,
+                  float alpha, cudaStream_t s)
+{
+    if (bwd_tma_v(V, GS, Lam, nullptr, nullptr, nullptr, T, N, T, beta, theta, alpha, s)) return;
+    unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
+    count_launches(1);
+    k_serial_bwd_v<8><<<g, kSerBlock, 0, s>>>(V, GS, Lam, T, N, beta, theta, alpha);
 }
 
 void serial_bwd(const float *I, const float *u0, const float *U, const float *S, const float *GS,

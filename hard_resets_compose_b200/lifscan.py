@@ -36,7 +36,7 @@ __all__ = [
     "state_bounds", "surrogate_grad", "_pick_C", "LIFTuned", "lif_tuned", "LIFFunction", "lif",
     "AUTO_FWD_MAX_N", "AUTO_FWD_MIN_T", "AUTO_BWD_MAX_N", "AUTO_BWD_MIN_T", "auto_modes",
     "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg", "scan_chunk_fwd", "scan_chunk_bwd",
-    "lif_tuned_host", "scan_forward_spec", "spec_segment",
+    "lif_tuned_host", "scan_forward_spec", "spec_segment", "serial_forward_v", "lif_backward_v",
 ]
 
 _CONVERGE = -1  # max_repair value meaning "repair until converged"
@@ -387,6 +387,45 @@ def surrogate_grad(x, alpha):
     return alpha * sg * (1 - sg)
 
 
+# ----------------------------------------------------------------------------- V-saving layer path
+def serial_forward_v(I, beta, theta, u_r, u0):
+    """Serial forward that returns (V, S), V[t] = v_t = fl(fl(beta*u_{t-1}) + x_t),
+    the potential before the reset (lifb_serial_fwd_v); S as serial_forward."""
+    I, u0, T, N = _prep_fwd(I, u0)
+    V = torch.empty_like(I)
+    S = torch.empty_like(I)
+    lib = _lib.load()
+    with torch.cuda.device(I.device):
+        check(lib.lifb_serial_fwd_v(ptr(I), ptr(u0), ptr(V), ptr(S), T, N, _f(beta), _f(theta), _f(u_r),
+                                    stream_of(I)), "serial_forward_v")
+    return V, S
+
+
+def lif_backward_v(V, GS, beta, theta, alpha=4.0, C=None):
+    """Detached-reset adjoint of lif_tuned from V and GS alone (lifb_lif_bwd_v)
+    -> Lam = dL/dI; du0 = beta * Lam[0].  C = chunk length (default T)."""
+    if V.dim() != 2:
+        raise ValueError(f"V must be [T, N], got shape {tuple(V.shape)}")
+    V = _cuda_f32("V", V)
+    T, N = V.shape
+    GS = _cuda_f32("GS", GS, (T, N))
+    C = T if C is None else int(C)
+    Lam = torch.empty_like(V)
+    lib = _lib.load()
+    with torch.cuda.device(V.device):
+        nb = lib.lifb_lif_bwd_v_workspace_bytes(T, N, C) if C < T else 0
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=V.device)
+        check(lib.lifb_lif_bwd_v(ptr(V), ptr(GS), ptr(Lam), T, N, _f(beta), _f(theta), _f(alpha), C, ptr(ws), nb,
+                                 stream_of(V)), "lif_backward_v")
+    return Lam
+
+
+def _single_pass(T, N, mode):
+    """True when lif_tuned's forward is the single streaming pass (where it
+    saves V instead of U)."""
+    return T > 0 and N > 0 and (mode == "serial" or spec_segment(T, N)[0] == T)
+
+
 # ----------------------------------------------------------------------------- autograd layers
 class LIFTuned(torch.autograd.Function):
     """Hard-reset LIF, detached reset, sigmoid surrogate (lifscan/triton_lif.py:654-683).
@@ -395,19 +434,32 @@ class LIFTuned(torch.autograd.Function):
     @staticmethod
     def forward(ctx, I, u0, beta, theta, u_r, alpha, mode, K, repair):
         I = I.contiguous()
+        T, N = I.shape
+        ctx.cfg = (beta, theta, u_r, alpha, mode)
+        ctx.vpath = _single_pass(T, N, mode)
+        if ctx.vpath:
+            # the adjoint needs only v_t: save V (same bytes as U) and read
+            # V and GS in the backward instead of I, U and GS
+            V, S = serial_forward_v(I, beta, theta, u_r, u0)
+            ctx.save_for_backward(V)
+            return S
         if mode == "serial":
             U, S = serial_forward_auto(I, beta, theta, u_r, u0)
         else:
             U, S = scan_forward_auto(I, beta, theta, u_r, u0, K=K, repair=repair)
         ctx.save_for_backward(I, u0, U, S)
-        ctx.cfg = (beta, theta, u_r, alpha, mode)
         return S
 
     @staticmethod
     def backward(ctx, gS):
-        I, u0, U, S = ctx.saved_tensors
         beta, theta, u_r, alpha, mode = ctx.cfg
         gS = gS.contiguous()
+        if ctx.vpath:
+            (V,) = ctx.saved_tensors
+            T, N = V.shape
+            Lam = lif_backward_v(V, gS, beta, theta, alpha, C=T if mode == "serial" else scan_chunk_bwd(T, N))
+            return Lam, beta * Lam[0], None, None, None, None, None, None, None
+        I, u0, U, S = ctx.saved_tensors
         # GU is identically zero on this path: pass None instead of materialising
         # zeros_like(gS); S is this layer's own forward output, so the kernels
         # recompute it bit-exactly from U and I instead of reading it (S=None).

@@ -141,6 +141,21 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
                   float alpha, int detach, int C,
                   void *workspace, size_t workspace_bytes, void *stream);
 
+/* lif_tuned's layer with V saved instead of U (lifscan/triton_lif.py:654-683):
+ * lifb_serial_fwd_v is lifb_serial_fwd writing V[t] = v_t = fl(fl(beta*u_{t-1})
+ * + x_t) (the potential before the reset) in place of U; S is the same.
+ * lifb_lif_bwd_v is the detached-reset adjoint from V and GS alone
+ * (s_t = [v_t >= theta] recomputed, GU = 0): Lam = dL/dI, du0 = beta*Lam[0],
+ * reading 8 bytes per neuron-step instead of 12.  C = T: one sweep (no
+ * workspace); C < T: T/C chunks at once plus the fix-up
+ * (lifb_lif_bwd_v_workspace_bytes). */
+int lifb_serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N,
+                      float beta, float theta, float u_r, void *stream);
+size_t lifb_lif_bwd_v_workspace_bytes(int64_t T, int64_t N, int C);
+int lifb_lif_bwd_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta,
+                   float theta, float alpha, int C, void *workspace, size_t workspace_bytes,
+                   void *stream);
+
 /* lif_tuned forward + backward for HOST-resident tensors (the layer of
  * lifscan/triton_lif.py:654-683 with the detached sigmoid surrogate, called
  * with tensors that live in host memory).  Inputs I_host, GS_host [T, N] and

@@ -185,3 +185,38 @@ def test_calls_from_a_fresh_thread(cuda):
     torch.cuda.synchronize()
     assert_bit_equal(_np(out["fwd"][0]), U, "U")
     assert rel(_np(out["bwd"]), ref) < TOL
+
+
+@pytest.mark.parametrize("N,T,C", ((16384, 1024, 1024), (1000, 4096, 512), (777, 2048, 2048), (777, 2048, 256),
+                                   (64, 1 << 15, 4096)))
+def test_v_path(cuda, N, T, C):
+    """lif_tuned's V-saving path: V is the forward's pre-reset potential bit
+    for bit, S unchanged, and the adjoint from V and GS alone (one sweep or
+    chunks + fix-up; N = 777 takes the plain-kernel fallback) matches the
+    oracle's serial adjoint."""
+    beta = 0.99
+    I, u0, GS = gen(T, N, 0.05, 0.2, seed=23, u0_sd=0.3, grad=True)
+    Us, Ss, Vs = O.serial_forward(I, beta, 1.0, 0.0, u0, want_v=True)
+    ref = O.serial_backward(I, u0, Us, Ss, GS, None, beta, 1.0, 0.0, 4.0, True)
+    Id, u0d, GSd = to_dev(cuda, I, u0, GS)
+    V, S = L().serial_forward_v(Id, beta, 1.0, 0.0, u0d)
+    assert_bit_equal(_np(V), Vs, "V")
+    assert_bit_equal(_np(S), Ss, "S")
+    lam = L().lif_backward_v(V, GSd, beta, 1.0, 4.0, C=C)
+    assert rel(_np(lam), ref) < TOL
+
+
+@pytest.mark.parametrize("mode", ("scan", "serial"))
+def test_lif_tuned_v_path_selected(cuda, mode):
+    """At config 2's shape lif_tuned's forward is the single pass and saves V."""
+    T, N = 1024, 16384
+    I, u0, GS = gen(T, N, 0.05, 0.2, seed=4, grad=True)
+    Us, Ss = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
+    dI_ref = O.serial_backward(I, u0, Us, Ss, GS, None, 0.99, 1.0, 0.0, 4.0, True)
+    Id, u0d, GSd = to_dev(cuda, I, u0, GS)
+    Id.requires_grad_(True)
+    S = L().lif_tuned(Id, u0d, beta=0.99, mode=mode)
+    assert S.grad_fn is not None and len(S.grad_fn.saved_tensors) == 1  # V only
+    torch.autograd.backward(S, GSd)
+    assert_bit_equal(_np(S), Ss, "S")
+    assert rel(_np(Id.grad), dI_ref) < TOL
