@@ -58,6 +58,22 @@ class TorchComm:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
 
+    def shift(self, t):
+        """t of rank r-1 on rank r (rank 0 receives None); every rank sends
+        its t to rank r+1."""
+        t = t.contiguous()
+        ops = []
+        if self.rank + 1 < self.world:
+            ops.append(dist.P2POp(dist.isend, t, self.rank + 1, group=self.group))
+        buf = None
+        if self.rank > 0:
+            buf = torch.empty_like(t)
+            ops.append(dist.P2POp(dist.irecv, buf, self.rank - 1, group=self.group))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        return buf
+
     def all_gather(self, t):
         t = t.contiguous()
         if t.is_cuda:
@@ -94,6 +110,10 @@ class LocalComm:
         out = torch.stack(sh.slots)
         sh.barrier.wait()  # every rank has its copy before the slots are reused
         return out
+
+    def shift(self, t):
+        g = self.all_gather(t)
+        return g[self.rank - 1].clone() if self.rank > 0 else None
 
 
 def run_local(world, fn):
@@ -136,15 +156,17 @@ class CudaSliceOps:
         self.beta, self.theta, self.u_r, self.alpha = float(beta), float(theta), float(u_r), float(alpha)
         self.C, self.G, self.K, self.K2, self.K3, self.Cb = C, G, K, K2, K3, C_bwd
         L = self.L = _lib.load()
-        nb = L.lifb_tshard_workspace_bytes(T, N, C, G, K, K2)
+        self._nb = L.lifb_tshard_workspace_bytes(T, N, C, G, K, K2)
         nbb = L.lifb_tshard_bwd_workspace_bytes(T, N, C_bwd)
-        if nb == 0 or nbb == 0:
+        if self._nb == 0 or nbb == 0:
             raise ValueError("time-sharded scan: invalid slice shape")
-        self.ws = torch.empty(nb, dtype=torch.uint8, device=self.dev)
+        self.ws = None  # scratch of entry mode "maps", allocated on first use
         self.wsb = torch.empty(nbb, dtype=torch.uint8, device=self.dev)
         self.map_rows = 4 + 2 * K3
 
     def _ws(self):
+        if self.ws is None:
+            self.ws = torch.empty(self._nb, dtype=torch.uint8, device=self.dev)
         return ptr(self.ws), self.ws.numel()
 
     def envelope(self, I):
@@ -173,11 +195,37 @@ class CudaSliceOps:
                                            self.G, self.K, self.K2, *self._ws(), stream_of(I)), "tshard apply")
         return entry, U, S, end
 
-    def spec_forward(self, I, entry):
-        """U, S of the slice from a (guessed) entry state: the speculative
-        segment forward (lifscan.scan_forward_spec), exact for that entry."""
-        from .lifscan import scan_forward_spec
-        return scan_forward_spec(I, self.beta, self.theta, self.u_r, entry)
+    def _spec_ws(self):
+        if getattr(self, "_sws", None) is None:
+            from .lifscan import SPEC_LEAD, spec_segment
+            L, W = spec_segment(self.T, self.N)
+            self._sL, self._sW = L, (W if W > 0 else min(SPEC_LEAD, self.T))
+            nb = self.L.lifb_scan_fwd_spec_workspace_bytes(self.T, self.N, L)
+            self._sws = torch.empty(max(nb, 1), dtype=torch.uint8, device=self.dev)
+        return self._sws
+
+    def spec_begin(self, I):
+        """Lead-ins of the slice's segments (lifb_scan_fwd_spec_begin) and the
+        guess of its final state: its last rows run from u_r."""
+        ws = self._spec_ws()
+        g = torch.empty(self.N, device=self.dev)
+        with torch.cuda.device(self.dev):
+            check(self.L.lifb_scan_fwd_spec_begin(ptr(I), self.T, self.N, self.beta, self.theta, self.u_r, self._sL,
+                                                  self._sW, ptr(g), ptr(ws), ws.numel(), stream_of(I)),
+                  "tshard speculative lead-ins")
+        return g
+
+    def spec_finish(self, I, entry):
+        """U, S of the slice from `entry` (lifb_scan_fwd_spec_finish, after
+        spec_begin): exact for that entry."""
+        ws = self._spec_ws()
+        U = torch.empty_like(I)
+        S = torch.empty_like(I)
+        with torch.cuda.device(self.dev):
+            check(self.L.lifb_scan_fwd_spec_finish(ptr(I), ptr(entry), ptr(U), ptr(S), self.T, self.N, self.beta,
+                                                   self.theta, self.u_r, self._sL, ptr(ws), ws.numel(),
+                                                   stream_of(I)), "tshard speculative forward")
+        return U, S
 
     def repair(self, I, entry, U, S, end):
         changed = torch.empty(self.N, dtype=torch.int32, device=self.dev)
@@ -218,13 +266,14 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", timeline
 
     entry_mode "maps": the entry of every slice comes from the gathered slice
     maps (steps 1-3 of the module docstring), exact unless a map overflowed.
-    entry_mode "speculate": every slice after the first starts from u_r (as if
-    its neuron had just spiked) and runs at once with its own segments led in
-    (lifscan.scan_forward_spec); hard resets make a trajectory forget its
-    start within a few hundred rows, so every slice's end state is exact in
-    almost every neuron, and the first repair round replays each slice's first
-    rows from the exact entry only until they rejoin (no map is built; the
-    envelope and map exchanges are skipped).
+    entry_mode "speculate": every slice runs the lead-ins of its segments and,
+    in the same launch, its last few thousand rows from u_r (as if its neuron
+    had just spiked), and hands that guess of its final state to the next
+    slice (a point-to-point shift of N floats) as that slice's entry; all
+    slices then replay at once.  Hard resets make the guess exact in almost
+    every neuron, and the repair replays the others from the exact entry only
+    until their rows rejoin (no map is built; the envelope and map exchanges
+    are skipped).
     Both give the same bits.  `info` (a dict) receives the number of repair
     rounds and the neurons repaired per round; `timeline` (a list, CUDA only)
     receives (phase, CUDA event) pairs marking the end of each phase."""
@@ -240,8 +289,12 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", timeline
         # the previous slice's last rows lead the guess (u_r before them) to
         # the exact entry state in all but a few neurons
         _mark(timeline, "start", I)
-        entry = u0.clone() if r == 0 else torch.full_like(u0, float(ops.u_r))
-        U, S = ops.spec_forward(I, entry)
+        guess = ops.spec_begin(I)  # lead-ins, and a guess of this slice's final state
+        _mark(timeline, "lead_in", I)
+        entry = comm.shift(guess)  # the previous slice's guess is this one's entry
+        entry = u0.clone() if r == 0 else entry
+        _mark(timeline, "shift", I)
+        U, S = ops.spec_finish(I, entry)
         end = U[-1].clone()
         _mark(timeline, "slice", I)
     else:

@@ -10,7 +10,8 @@ Each phase keeps the contract of its lifb_tshard_* counterpart:
              (lifscan/triton_lif.py:828-899), pruned with the entry bound; in
              mode "corrupt" a constant map (a deliberately wrong guess)
   apply      entry = u0 through the earlier maps, then the serial recurrence
-  spec_forward  the serial recurrence from the (guessed) entry
+  spec_begin the guess of the slice's final state: its last rows run from u_r
+  spec_finish the serial recurrence from the (guessed) entry
   repair     the serial recurrence from the new entry; changed = end moved
   bwd        the serial adjoint with lam = 0 above the slice, and (q, p)
   bwd_fix    the serial adjoint with lam_top entering from above
@@ -84,7 +85,13 @@ class OracleSliceOps:
         U, S = O.serial_forward(I.numpy(), float(self.beta), float(self.theta), float(self.u_r), u)
         return (torch.from_numpy(u), torch.from_numpy(U), torch.from_numpy(S), torch.from_numpy(U[-1].copy()))
 
-    def spec_forward(self, I, entry):
+    def spec_begin(self, I, lead=256):
+        x = I.numpy()[-min(lead, self.T):]
+        Ug, _ = O.serial_forward(x, float(self.beta), float(self.theta), float(self.u_r),
+                                 np.full(self.N, self.u_r, np.float32))
+        return torch.from_numpy(Ug[-1].copy())
+
+    def spec_finish(self, I, entry):
         U, S = O.serial_forward(I.numpy(), float(self.beta), float(self.theta), float(self.u_r), entry.numpy())
         return torch.from_numpy(U), torch.from_numpy(S)
 
