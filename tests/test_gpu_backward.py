@@ -220,3 +220,17 @@ def test_lif_tuned_v_path_selected(cuda, mode):
     torch.autograd.backward(S, GSd)
     assert_bit_equal(_np(S), Ss, "S")
     assert rel(_np(Id.grad), dI_ref) < TOL
+
+
+@pytest.mark.parametrize("beta,mu,sd", ((0.99, 0.05, 0.2), (1.0, -0.01, 0.05), (0.5, 0.4, 0.2)))
+@pytest.mark.parametrize("N,T", ((4096, 1024), (1024, 1000), (2048, 4096), (512, 64), (1024, 200)))
+def test_v_path_one_chunk_regimes(cuda, beta, mu, sd, N, T):
+    """One-chunk adjoint from V across regimes: ragged tiles (T = 1000, 200),
+    long spike-free stretches (beta = 1, negative drift), frequent spikes, and
+    short sequences."""
+    I, u0, GS = gen(T, N, mu, sd, seed=29, u0_sd=0.3, grad=True)
+    Us, Ss, Vs = O.serial_forward(I, beta, 1.0, 0.0, u0, want_v=True)
+    ref = O.serial_backward(I, u0, Us, Ss, GS, None, beta, 1.0, 0.0, 4.0, True)
+    Vd, GSd = to_dev(cuda, Vs, GS)
+    lam = L().lif_backward_v(Vd, GSd, beta, 1.0, 4.0, C=T)
+    assert rel(_np(lam), ref) < TOL
