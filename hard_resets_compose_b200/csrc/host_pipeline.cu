@@ -3,13 +3,14 @@
 //
 // Neuron columns of [T, N] are independent recurrences, so the problem splits
 // into column blocks of `block_n` neurons.  Block b moves through three
-// streams: an input stream copies its columns of I, GS (and u0) host->device
-// (cudaMemcpy2DAsync, pitched), the caller's stream runs the forward and the
-// adjoint on it (the kernels of chunk_tma.cu / serial.cu), and an output
-// stream copies its columns of S, dI and du0 device->host.  Two staging slots
-// in the caller's device workspace let the H2D of block b+1, the compute of
-// block b and the D2H of block b-1 overlap, so the call is bound by the
-// slower PCIe direction instead of the sum of both.
+// streams: an input stream copies its columns of u0 and I, then of GS,
+// host->device (cudaMemcpy2DAsync, pitched); the caller's stream runs the
+// forward as soon as I has arrived (saving V, the pre-reset potentials, as
+// lif_tuned does) and the adjoint from V and GS once GS has; an output stream
+// copies S back as soon as the forward is done, then dI and du0.  Three
+// staging slots in the caller's device workspace keep both PCIe directions
+// busy at once (B200: ~55 GB/s each way alone, ~95 GB/s both ways together),
+// so the call is bound by their joint rate instead of the sum of both.
 #include <mutex>
 
 #include "lifb_common.cuh"
@@ -20,11 +21,11 @@ namespace lifb {
 namespace {
 
 constexpr int kMaxDev = 64;
-constexpr int kSlots = 2;
+constexpr int kSlots = 3;
 
 struct HostPipe {
     cudaStream_t in = nullptr, out = nullptr;
-    cudaEvent_t ev_in[kSlots], ev_done[kSlots], ev_free[kSlots], ev_start, ev_last;
+    cudaEvent_t ev_in[kSlots], ev_gs[kSlots], ev_fwd[kSlots], ev_done[kSlots], ev_free[kSlots], ev_start, ev_last;
     bool ready = false;
 };
 HostPipe g_pipe[kMaxDev];
@@ -42,6 +43,8 @@ HostPipe *pipe_for_current_device()
         if (cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
         for (int i = 0; i < kSlots; i++) {
             if (cudaEventCreateWithFlags(&p.ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&p.ev_gs[i], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&p.ev_fwd[i], cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&p.ev_done[i], cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&p.ev_free[i], cudaEventDisableTiming) != cudaSuccess)
                 return nullptr;
@@ -62,7 +65,7 @@ __global__ void k_scale_row(const float *__restrict__ row, float beta, float *__
 }
 
 struct Slot {
-    float *I, *GS, *U, *S, *Lam, *u0, *du0;
+    float *I, *GS, *V, *S, *Lam, *u0, *du0;
 };
 
 }  // namespace
@@ -93,7 +96,7 @@ int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float 
     for (int i = 0; i < kSlots; i++) {
         slot[i].I = (float *)w; w += big;
         slot[i].GS = (float *)w; w += big;
-        slot[i].U = (float *)w; w += big;
+        slot[i].V = (float *)w; w += big;
         slot[i].S = (float *)w; w += big;
         slot[i].Lam = (float *)w; w += big;
         slot[i].u0 = (float *)w; w += small;
@@ -114,20 +117,24 @@ int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float 
         Slot &s = slot[k];
         // input: wait until the slot's previous outputs have left the device
         if (b >= kSlots) cudaStreamWaitEvent(p->in, p->ev_free[k], 0);
-        cudaMemcpy2DAsync(s.I, dp, I_h + n0, hp, dp, (size_t)T, cudaMemcpyHostToDevice, p->in);
-        cudaMemcpy2DAsync(s.GS, dp, GS_h + n0, hp, dp, (size_t)T, cudaMemcpyHostToDevice, p->in);
         cudaMemcpyAsync(s.u0, u0_h + n0, dp, cudaMemcpyHostToDevice, p->in);
+        cudaMemcpy2DAsync(s.I, dp, I_h + n0, hp, dp, (size_t)T, cudaMemcpyHostToDevice, p->in);
         cudaEventRecord(p->ev_in[k], p->in);
-        // compute on the caller's stream
+        cudaMemcpy2DAsync(s.GS, dp, GS_h + n0, hp, dp, (size_t)T, cudaMemcpyHostToDevice, p->in);
+        cudaEventRecord(p->ev_gs[k], p->in);
+        // compute on the caller's stream: the forward needs I only
         cudaStreamWaitEvent(cs, p->ev_in[k], 0);
-        serial_fwd(s.I, s.u0, s.U, s.S, T, nb, beta, theta, u_r, cs);
-        serial_bwd(s.I, s.u0, s.U, nullptr, s.GS, nullptr, s.Lam, T, nb, beta, theta, u_r, alpha, true, cs);
+        serial_fwd_v(s.I, s.u0, s.V, s.S, T, nb, beta, theta, u_r, cs);
+        cudaEventRecord(p->ev_fwd[k], cs);
+        cudaStreamWaitEvent(cs, p->ev_gs[k], 0);
+        serial_bwd_v(s.V, s.GS, s.Lam, T, nb, beta, theta, alpha, cs);
         count_launches(1);
         k_scale_row<<<(unsigned)((nb + 255) / 256), 256, 0, cs>>>(s.Lam, beta, s.du0, nb);
         cudaEventRecord(p->ev_done[k], cs);
-        // output
-        cudaStreamWaitEvent(p->out, p->ev_done[k], 0);
+        // output: S as soon as the forward is done, then dI and du0
+        cudaStreamWaitEvent(p->out, p->ev_fwd[k], 0);
         cudaMemcpy2DAsync(S_h + n0, hp, s.S, dp, dp, (size_t)T, cudaMemcpyDeviceToHost, p->out);
+        cudaStreamWaitEvent(p->out, p->ev_done[k], 0);
         cudaMemcpy2DAsync(dI_h + n0, hp, s.Lam, dp, dp, (size_t)T, cudaMemcpyDeviceToHost, p->out);
         cudaMemcpyAsync(du0_h + n0, s.du0, dp, cudaMemcpyDeviceToHost, p->out);
         cudaEventRecord(p->ev_free[k], p->out);

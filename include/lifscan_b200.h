@@ -163,12 +163,14 @@ int lifb_lif_bwd_v(const float *V, const float *GS, float *Lam, int64_t T, int64
  * and du0_host [N] (= beta * Lam[0]).  Host buffers should be pinned
  * (cudaHostAlloc / page-locked) for the copies to overlap.  The neurons are
  * processed in column blocks of block_n (a multiple of 4): while block b runs
- * forward and adjoint on `stream`, block b+1 is copied in and block b-1 out on
- * two library-owned copy streams, so the call is bound by the slower PCIe
- * direction.  The workspace is device memory of at least
- * lifb_lif_fwd_bwd_host_workspace_bytes(T, N, block_n) bytes (two staging
- * slots).  Work is ordered after what is already queued on `stream`; the
- * outputs are complete once `stream` has reached the end of this call. */
+ * forward and adjoint on `stream` (the forward as soon as its I has arrived,
+ * the adjoint once GS has), later blocks are copied in and earlier ones out on
+ * two library-owned copy streams (S of a block leaves as soon as its forward
+ * is done), so both PCIe directions stay busy at once.  The workspace is
+ * device memory of at least lifb_lif_fwd_bwd_host_workspace_bytes(T, N,
+ * block_n) bytes (three staging slots).  Work is ordered after what is already
+ * queued on `stream`; the outputs are complete once `stream` has reached the
+ * end of this call. */
 size_t lifb_lif_fwd_bwd_host_workspace_bytes(int64_t T, int64_t N, int64_t block_n);
 int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float *u0_host,
                           float *S_host, float *dI_host, float *du0_host,

@@ -115,11 +115,11 @@ def test_gradient_against_fp64_autograd(cuda):
     assert rel(_np(Id.grad), Ix.grad.numpy()) < 1e-5
 
 
-@pytest.mark.parametrize("N,block_n", ((16384, 2048), (1000, 256), (4096, 4096)))
+@pytest.mark.parametrize("N,block_n", ((16384, 2048), (1000, 256), (4096, 4096), (16384, 1024), (777, 128)))
 def test_lif_tuned_host_pipeline(cuda, N, block_n):
     """Host-buffer forward+backward (lifb_lif_fwd_bwd_host): spikes bit-exact,
     dI and du0 within 1e-5 of the oracle, for block counts that leave a
-    ragged last block, a single block, and two-slot reuse."""
+    ragged last block, a single block, and reuse of the staging slots."""
     T, beta = 1024, 0.99
     I, u0, GS = gen(T, N, 0.05, 0.2, seed=5, u0_sd=0.3, grad=True)
     Us, Ss = O.serial_forward(I, beta, 1.0, 0.0, u0)
