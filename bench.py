@@ -296,23 +296,32 @@ def run_sweep(args, ws, rank, local):
                     u0 = torch.zeros(N, device=dev)
                     out = {}
 
+                    vpath = L._single_pass(T, N, "scan")  # what lif_tuned(mode="scan") runs here
+
                     def fwd():
                         out.clear()
-                        out["fwd"] = L.scan_forward_auto(I, beta, 1.0, 0.0, u0)
+                        out["fwd"] = L.serial_forward_v(I, beta, 1.0, 0.0, u0) if vpath else \
+                            L.scan_forward_auto(I, beta, 1.0, 0.0, u0)
 
-                    def fwd_bwd():  # at most I, GS, U, S and Lam live
+                    def fwd_bwd():  # at most I, GS, U (or V), S and Lam live
                         out.clear()
-                        U_, _ = L.scan_forward_auto(I, beta, 1.0, 0.0, u0)
-                        out["lam"] = L.scan_backward_auto(I, u0, U_, None, GS, None, beta, 1.0, 0.0, 4.0)
+                        if vpath:
+                            V_, _ = L.serial_forward_v(I, beta, 1.0, 0.0, u0)
+                            out["lam"] = L.lif_backward_v(V_, GS, beta, 1.0, 4.0, C=L.scan_chunk_bwd(T, N))
+                        else:
+                            U_, _ = L.scan_forward_auto(I, beta, 1.0, 0.0, u0)
+                            out["lam"] = L.scan_backward_auto(I, u0, U_, None, GS, None, beta, 1.0, 0.0, 4.0)
 
                     ms_f = max_over_ranks(timed(fwd, reps))
                     ms_fb = max_over_ranks(timed(fwd_bwd, reps))
                     units = T * n_tot
+                    step_bytes = FWD_BYTES + (BWD_BYTES_V if vpath else BWD_BYTES)
                     gbs_f = FWD_BYTES * T * N / (ms_f / 1e3) / 1e9
-                    gbs_fb = (FWD_BYTES + BWD_BYTES) * T * N / (ms_fb / 1e3) / 1e9
+                    gbs_fb = step_bytes * T * N / (ms_fb / 1e3) / 1e9
                     pt.update(fwd_ms=ms_f, fwd_value=units / (ms_f / 1e3), fwd_frac=gbs_f / hbm,
                               fwd_bwd_ms=ms_fb, fwd_bwd_value=units / (ms_fb / 1e3), fwd_bwd_frac=gbs_fb / hbm,
-                              forward_segments=list(L.spec_segment(T, N)), bwd_chunk=L.scan_chunk_bwd(T, N))
+                              forward_segments=list(L.spec_segment(T, N)), bwd_chunk=L.scan_chunk_bwd(T, N),
+                              saved="V" if vpath else "U", fwd_bwd_bytes_per_neuron_step=step_bytes)
                     points.append(pt)
                     del I, GS, u0, out
                     torch.cuda.empty_cache()

@@ -108,11 +108,17 @@ int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float 
     cudaStreamWaitEvent(p->in, p->ev_start, 0);
     cudaStreamWaitEvent(p->out, p->ev_start, 0);
     const size_t hp = (size_t)N * 4;  // host pitch
-    const int64_t nblocks = (N + nb_max - 1) / nb_max;
-    for (int64_t b = 0; b < nblocks; b++) {
+    // The first block's input and the last block's output cross PCIe with
+    // nothing to overlap: make those two blocks half as wide (4-neuron aligned).
+    const int64_t half = nb_max >= 8 ? (nb_max / 2) / 4 * 4 : nb_max;
+    const bool split_ends = N > 2 * nb_max;
+    int64_t n0 = 0;
+    for (int64_t b = 0; n0 < N; b++) {
         const int k = (int)(b % kSlots);
-        const int64_t n0 = b * nb_max;
-        const int64_t nb = (N - n0) < nb_max ? (N - n0) : nb_max;
+        int64_t nb = nb_max;
+        if (split_ends && (b == 0 || N - n0 <= half)) nb = half;
+        if (nb > N - n0) nb = N - n0;
+        if (split_ends && N - n0 - nb > 0 && N - n0 - nb < half) nb = N - n0 - half;  // leave a half block last
         const size_t dp = (size_t)nb * 4;  // device pitch (block is contiguous [T, nb])
         Slot &s = slot[k];
         // input: wait until the slot's previous outputs have left the device
@@ -138,6 +144,7 @@ int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float 
         cudaMemcpy2DAsync(dI_h + n0, hp, s.Lam, dp, dp, (size_t)T, cudaMemcpyDeviceToHost, p->out);
         cudaMemcpyAsync(du0_h + n0, s.du0, dp, cudaMemcpyDeviceToHost, p->out);
         cudaEventRecord(p->ev_free[k], p->out);
+        n0 += nb;
     }
     // the caller's stream completes only after the last output copy
     cudaEventRecord(p->ev_last, p->out);
