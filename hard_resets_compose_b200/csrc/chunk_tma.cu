@@ -72,7 +72,7 @@ __device__ __forceinline__ void st_vec(float *p, const Vec<NPL> &a)
 // same TMA ring, and records that guessed start in LeadStarts[m]; chunk 0
 // starts from Starts[0] or u0 as before.  VOUT: the U output receives the
 // pre-reset potential v_t instead of u_t (Ends still hold u).
-template <int NPL, int R, int S, bool VOUT>
+template <int NPL, int R, int S, bool VOUT, bool SOFT>
 __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS, const float *__restrict__ u0,
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
 #pragma unroll
         for (int r = 0; r < R; r++)
 #pragma unroll
-            for (int i = 0; i < NPL; i++) u.v[i] = lif_step_u(u.v[i], x[r].v[i], beta, theta, u_r);
+            for (int i = 0; i < NPL; i++) u.v[i] = step_r_u<SOFT>(u.v[i], x[r].v[i], beta, theta, u_r);
         // the stage's rows are consumed (every lane used them): refill it
         fence_proxy_async_shared();
         __syncwarp();
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
             for (int i = 0; i < NPL; i++) {
                 const float v = __fadd_rn(__fmul_rn(beta, u.v[i]), x[r].v[i]);
                 const bool f = v >= theta;
-                u.v[i] = f ? u_r : v;
+                u.v[i] = f ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
                 sp.v[i] = f ? 1.0f : 0.0f;
                 vv.v[i] = v;
             }
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
                 for (int i = 0; i < NPL; i++) {
                     const float v = __fadd_rn(__fmul_rn(beta, u.v[i]), x.v[i]);
                     const bool f = v >= theta;
-                    u.v[i] = f ? u_r : v;
+                    u.v[i] = f ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
                     sp.v[i] = f ? 1.0f : 0.0f;
                     vv.v[i] = v;
                 }
@@ -254,7 +254,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 // k2 = alpha*log2(e), k2t = k2*theta: the exponent k2*(theta - v) is one FMA.
 // sig*(1 - sig) = sig - sig^2 (one FMA).  DET: the detached reset, known at
 // compile time (the V path has no other).
-template <bool READ_S, bool HAS_GU, bool DET = false>
+template <bool READ_S, bool HAS_GU, bool DET = false, bool SOFT = false>
 __device__ __forceinline__ void adj_coef_v(float v, float sread, float gs, float gu, float beta, float theta,
                                            float u_r, float alpha, float k2, float k2t, bool detach, float &a,
                                            float &c)
@@ -263,7 +263,9 @@ __device__ __forceinline__ void adj_coef_v(float v, float sread, float gs, float
     const float sig = rcp_approx(1.0f + e);
     const float sg = alpha * fmaf(-sig, sig, sig);
     float cc = gs * sg;
-    if (!READ_S && (DET || detach)) {  // s in {0, 1}: a = beta*(1 - s) and J*gu as selects
+    if (SOFT) {  // detached soft reset: du_t/dv_t = 1, so a = beta at every step
+        a = beta;
+    } else if (!READ_S && (DET || detach)) {  // s in {0, 1}: a = beta*(1 - s) and J*gu as selects
         const bool spk = v >= theta;
         a = spk ? 0.0f : beta;
         if constexpr (HAS_GU) cc = spk ? cc : cc + gu;
@@ -292,7 +294,7 @@ __device__ __forceinline__ Vec<NPL> bwd_v(const float *b, int kTile, int off, co
 
 // Coefficients of NPL neurons at in-tile offset `off` (no dependence on lam,
 // so a whole tile is computed ahead of the chain).
-template <int NPL, bool READ_S, bool HAS_GU, bool FROM_V>
+template <int NPL, bool READ_S, bool HAS_GU, bool FROM_V, bool SOFT = false>
 __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec<NPL> &a, Vec<NPL> &c, float beta,
                                          float theta, float u_r, float alpha, float k2, float k2t, bool detach)
 {
@@ -304,13 +306,13 @@ __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec
     if constexpr (HAS_GU) gu = ld_vec<NPL>(b + Ly::kGU * kTile + off);
 #pragma unroll
     for (int i = 0; i < NPL; i++)
-        adj_coef_v<READ_S, HAS_GU, FROM_V>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
-                                           theta, u_r, alpha, k2, k2t, detach, a.v[i], c.v[i]);
+        adj_coef_v<READ_S, HAS_GU, FROM_V, SOFT>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f,
+                                                 beta, theta, u_r, alpha, k2, k2t, detach, a.v[i], c.v[i]);
 }
 
 // One reverse step for NPL neurons at in-tile offset `off`; pp (the running
 // product of a) only when the chunk map is tracked.
-template <int NPL, bool READ_S, bool HAS_GU, bool TRACK, bool FROM_V>
+template <int NPL, bool READ_S, bool HAS_GU, bool TRACK, bool FROM_V, bool SOFT = false>
 __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, const Vec<NPL> *up_override,
                                          Vec<NPL> &lam, Vec<NPL> &pp, float beta, float theta, float u_r,
                                          float alpha, float k2, float k2t, bool detach)
@@ -324,14 +326,14 @@ __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, con
 #pragma unroll
     for (int i = 0; i < NPL; i++) {
         float a, c;
-        adj_coef_v<READ_S, HAS_GU, FROM_V>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f, beta,
-                                           theta, u_r, alpha, k2, k2t, detach, a, c);
+        adj_coef_v<READ_S, HAS_GU, FROM_V, SOFT>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f,
+                                                 beta, theta, u_r, alpha, k2, k2t, detach, a, c);
         lam.v[i] = c + a * lam.v[i];
         if constexpr (TRACK) pp.v[i] = a * pp.v[i];
     }
 }
 
-template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V>
+template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V, bool SOFT = false>
 __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS,
@@ -411,8 +413,8 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             Vec<NPL> av[R], cv[R];
 #pragma unroll
             for (int rr = 0; rr < R; rr++)
-                bwd_coef<NPL, READ_S, HAS_GU, FROM_V>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta, theta,
-                                                      u_r, alpha, k2, k2t, detach);
+                bwd_coef<NPL, READ_S, HAS_GU, FROM_V, SOFT>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
+                                                            theta, u_r, alpha, k2, k2t, detach);
             if (MODE == kReplay && k >= 2) {
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
@@ -454,7 +456,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             for (int rr = R - 1; rr >= 0; rr--) {
                 const int64_t t = rbase + rr;
                 if (t < cstart) break;
-                bwd_step<NPL, READ_S, HAS_GU, TRACK, FROM_V>(b, kTile, rr * NB + NPL * lane,
+                bwd_step<NPL, READ_S, HAS_GU, TRACK, FROM_V, SOFT>(b, kTile, rr * NB + NPL * lane,
                                                              (!FROM_V && t == 0) ? &uz : nullptr, lam, pp, beta,
                                                              theta, u_r, alpha, k2, k2t, detach);
                 if constexpr (TRACK) {
@@ -548,7 +550,7 @@ static int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
     return ((N + 127) / 128) * M >= (int64_t)min_ctas_per_sm * sms ? 4 : 1;
 }
 
-template <int NPL, bool VOUT>
+template <int NPL, bool VOUT, bool SOFT>
 static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, int64_t start_stride, float *U,
                        float *S, float *Ends, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r,
                        int64_t lead, float *LeadStarts, int *status, cudaStream_t s)
@@ -556,7 +558,7 @@ static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *St
     constexpr int NB = 32 * NPL;
     constexpr int R = FwdTile<NPL>::R, ST = FwdTile<NPL>::S;
     const size_t smem = (size_t)(ST + 4) * R * NB * 4;
-    auto kern = k_fwd_tma<NPL, R, ST, VOUT>;
+    auto kern = k_fwd_tma<NPL, R, ST, VOUT, SOFT>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
@@ -566,7 +568,7 @@ static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *St
 
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
-                    int64_t start_stride, int64_t lead, float *LeadStarts, bool vout)
+                    int64_t start_stride, int64_t lead, float *LeadStarts, bool vout, bool soft)
 {
     const void *p[] = {I, u0, Starts, U, S, Ends, LeadStarts};
     if (!tma_ok(p, 7, N) || C <= 0 || T % C) return false;
@@ -583,21 +585,21 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
         !make_tmap_2d(&maps[2], S, N, T, 32 * npl, R))
         return false;
     int *status = device_status_ptr();
-    auto go = [&](auto npl_c, auto vout_c) {
-        launch_fwd<decltype(npl_c)::value, decltype(vout_c)::value>(maps, u0, Starts, start_stride, U, S, Ends, N, M,
-                                                                     C, beta, theta, u_r, lead, LeadStarts, status,
-                                                                     s);
+    auto go = [&](auto npl_c, auto vout_c, auto soft_c) {
+        launch_fwd<decltype(npl_c)::value, decltype(vout_c)::value, decltype(soft_c)::value>(
+            maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, status, s);
     };
     using I1 = std::integral_constant<int, 1>;
     using I4 = std::integral_constant<int, 4>;
     using BT = std::true_type;
     using BF = std::false_type;
-    if (npl == 4) vout ? go(I4{}, BT{}) : go(I4{}, BF{});
-    else vout ? go(I1{}, BT{}) : go(I1{}, BF{});
+    auto go2 = [&](auto npl_c, auto vout_c) { soft ? go(npl_c, vout_c, BT{}) : go(npl_c, vout_c, BF{}); };
+    if (npl == 4) vout ? go2(I4{}, BT{}) : go2(I4{}, BF{});
+    else vout ? go2(I1{}, BT{}) : go2(I1{}, BF{});
     return true;
 }
 
-template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V = false>
+template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V = false, bool SOFT = false>
 static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *LamEnd, float *Lam, float *P, float *Q,
                        int32_t *D, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
                        bool detach, int *status, cudaStream_t s)
@@ -606,7 +608,7 @@ static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *La
     constexpr int NT = BwdLayout<READ_S, HAS_GU, FROM_V>::NT;
     constexpr int R = BwdTile<NPL>::R, ST = BwdTile<NPL>::S;
     const size_t smem = ((size_t)ST * NT + (MODE == kReplay ? 2 : 0)) * R * NB * 4;
-    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V>;
+    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V, SOFT>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
@@ -652,6 +654,37 @@ bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, 
     } else {
         if (npl == 4) launch_bwd<4, false, false, kReplay, false, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
         else launch_bwd<1, false, false, kReplay, false, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+    }
+    return true;
+}
+
+// Soft-reset adjoint over one chunk of T rows: lam_t = gs_t sigma'(v_t) +
+// beta lam_{t+1}, v_t from U[t-1] and I[t] (from_v: V given).
+bool bwd_tma_soft(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
+                  int64_t N, float beta, float theta, float alpha, bool from_v, cudaStream_t s)
+{
+    const void *p[] = {IV, u0, U, GS, Lam};
+    if (!tma_ok(p, 5, N) || T <= 0) return false;
+    const int npl = pick_npl(N, 1, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
+    const int nb = 32 * npl;
+    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    CUtensorMap maps[6];
+    if (!make_tmap_2d(&maps[0], IV, N, T, nb, R) || !make_tmap_2d(&maps[3], GS, N, T, nb, R) ||
+        !make_tmap_2d(&maps[5], Lam, N, T, nb, R))
+        return false;
+    if (from_v) {
+        maps[1] = maps[0];
+    } else if (!make_tmap_2d(&maps[1], U, N, T, nb, R)) {
+        return false;
+    }
+    maps[2] = maps[4] = maps[0];
+    int *status = device_status_ptr();
+    if (from_v) {
+        if (npl == 4) launch_bwd<4, false, false, kReplay, false, true, true>(maps, nullptr, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
+        else launch_bwd<1, false, false, kReplay, false, true, true>(maps, nullptr, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
+    } else {
+        if (npl == 4) launch_bwd<4, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
+        else launch_bwd<1, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
     }
     return true;
 }

@@ -32,6 +32,33 @@ LIFB_DEV float lif_step_u(float u, float x, float beta, float theta, float u_r)
     return v >= theta ? u_r : v;
 }
 
+// The same step with the reset chosen at compile time: the hard reset above,
+// or the soft (subtractive) reset u' = s ? fl(v - theta) : v of the soft-reset
+// model (lifscan/triton_lif.py:1037-1049 soft_fwd_kernel, lifscan/triton_soft.py:107-111).
+template <bool SOFT>
+LIFB_DEV float step_r(float u, float x, float beta, float theta, float u_r, bool &s)
+{
+    const float v = __fadd_rn(__fmul_rn(beta, u), x);
+    s = v >= theta;
+    return s ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
+}
+
+template <bool SOFT>
+LIFB_DEV float step_r_u(float u, float x, float beta, float theta, float u_r)
+{
+    bool s;
+    return step_r<SOFT>(u, x, beta, theta, u_r, s);
+}
+
+// Runtime choice (host-chosen flag, uniform across the grid): the fix-up and
+// lead-in kernels, whose cost is not the step.
+LIFB_DEV float step_any(float u, float x, float beta, float theta, float u_r, bool soft, bool &s)
+{
+    const float v = __fadd_rn(__fmul_rn(beta, u), x);
+    s = v >= theta;
+    return s ? (soft ? __fsub_rn(v, theta) : u_r) : v;
+}
+
 // fl(fl(a*b) + c), never contracted to an FMA.
 LIFB_DEV float mul_add_rn(float a, float b, float c) { return __fadd_rn(__fmul_rn(a, b), c); }
 

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
                                                        const float *__restrict__ I_halo, int64_t W_halo,
                                                        float *__restrict__ Starts, float *__restrict__ end_guess,
                                                        int64_t N, int64_t NS, int64_t L, int64_t W, float beta,
-                                                       float theta, float u_r)
+                                                       float theta, float u_r, bool soft)
 {
     const int64_t n = (int64_t)blockIdx.x * kLeadBlock + threadIdx.x;
     const int64_t s = blockIdx.y;
@@ -84,7 +84,10 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
         for (int q = 0; q < kLeadB; q++) nxt[q] = nb + q < len ? __ldg(p + (nb + q) * N) : 0.0f;
 #pragma unroll
         for (int q = 0; q < kLeadB; q++)
-            if (b + q < len) u = lif_step_u(u, cur[q], beta, theta, u_r);
+            if (b + q < len) {
+                bool f;
+                u = step_any(u, cur[q], beta, theta, u_r, soft, f);
+            }
 #pragma unroll
         for (int q = 0; q < kLeadB; q++) cur[q] = nxt[q];
     }
@@ -94,12 +97,12 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
 
 void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts,
                    float *end_guess, int64_t N, int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r,
-                   cudaStream_t s)
+                   cudaStream_t s, bool soft)
 {
     count_launches(1);
     const unsigned ny = (unsigned)(NS + (end_guess ? 1 : 0));
     k_leadin<<<dim3((unsigned)((N + kLeadBlock - 1) / kLeadBlock), ny), kLeadBlock, 0, s>>>(
-        I, u0, I_halo, W_halo, Starts, end_guess, N, NS, L, W, beta, theta, u_r);
+        I, u0, I_halo, W_halo, Starts, end_guess, N, NS, L, W, beta, theta, u_r, soft);
 }
 
 __global__ void k_copy_row(const float *__restrict__ src, float *__restrict__ dst, int64_t N)

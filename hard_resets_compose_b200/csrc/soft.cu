@@ -1,0 +1,110 @@
+// The soft-reset LIF (subtractive reset u <- v - theta): the model class the
+// reference keeps beside the hard reset for its fitting experiments
+// (lifscan/triton_lif.py:1035-1082, 1139-1198; lifscan/triton_soft.py).
+//
+//   lifb_soft_serial_fwd   soft_serial_forward(_tiled): one pass, bit-identical to
+//                          the reference's fp32 soft recurrence (the TMA replay
+//                          kernel with the reset chosen at compile time)
+//   lifb_soft_scan_fwd     soft_scan_forward: exact.  The reference composes
+//                          interval maps (Theorem 7 of its paper); here the same
+//                          speculative segments as the hard reset (lead-ins,
+//                          segment replay, resynchronising fix-up).  A soft reset
+//                          forgets its start only as fast as beta^t rounds the
+//                          difference away (~1500-3000 rows at beta = 0.99, never
+//                          at beta = 1), so wrong guesses cost longer fix-ups;
+//                          the result is exact either way.
+//   lifb_soft_serial_bwd   soft_serial_backward(_auto): the detached-reset adjoint
+//                          lam_t = gs_t sigma'(v_t) + beta lam_{t+1} from U and I
+//   lifb_soft_adjoint_v    soft_adjoint_fft: the same recurrence from V; the
+//                          reference convolves in float64 by FFT, here it is the
+//                          fp32 reverse sweep (within the 1e-5 gradient bar)
+#include <cstdio>
+
+#include "lifb_common.cuh"
+#include "lifb_internal.h"
+
+namespace {
+int fail(int st, const char *msg)
+{
+    lifb::set_last_error(msg);
+    return st;
+}
+
+int done(const char *who)
+{
+    if (cudaGetLastError() != cudaSuccess) {
+        char msg[128];
+        snprintf(msg, sizeof msg, "%s: launch failed", who);
+        return fail(LIFB_ERR_CUDA, msg);
+    }
+    lifb::set_last_error("");
+    return LIFB_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int lifb_soft_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                         float theta, void *stream)
+{
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_fwd: negative size");
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!I || !u0 || !U || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_fwd: null pointer");
+    lifb::serial_fwd_soft(I, u0, U, S, T, N, beta, theta, (cudaStream_t)stream);
+    return done("lifb_soft_serial_fwd");
+}
+
+int lifb_soft_scan_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                       float theta, int64_t L, int64_t W, void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (T < 0 || N < 0 || L <= 0 || W < 0 || (T > 0 && T % L))
+        return fail(LIFB_ERR_INVALID_ARGUMENT,
+                    "lifb_soft_scan_fwd: T must be a multiple of the segment length L > 0, W >= 0");
+    if (T / L > 65535) return fail(LIFB_ERR_UNSUPPORTED, "lifb_soft_scan_fwd: more than 65535 segments");
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!I || !u0 || !U || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_scan_fwd: null pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t NS = T / L;
+    if (NS == 1) {
+        lifb::serial_fwd_soft(I, u0, U, S, T, N, beta, theta, s);
+        return done("lifb_soft_scan_fwd");
+    }
+    const size_t one = ((size_t)NS * N * 4 + 255) / 256 * 256;
+    if (!workspace || (uintptr_t)workspace % 256 || workspace_bytes < 4 * one)
+        return fail(LIFB_ERR_WORKSPACE, "lifb_soft_scan_fwd: workspace missing, misaligned or too small "
+                                        "(lifb_scan_fwd_spec_workspace_bytes)");
+    char *b = (char *)workspace;
+    float *Starts = (float *)b, *Ends = (float *)(b + one), *EndsNew = (float *)(b + 2 * one);
+    int32_t *Changed = (int32_t *)(b + 3 * one);
+    // segments led in and replayed in one launch, then the exact fix-up
+    if (W > 0 &&
+        lifb::fwd_replay_tma(I, u0, nullptr, U, S, Ends, T, N, L, beta, theta, 0.0f, s, 1, W, Starts, false, true)) {
+        lifb::fwd_fixup(I, Starts, 1, U, S, Ends, EndsNew, Changed, N, NS, L, beta, theta, 0.0f, nullptr, s, true);
+    } else {
+        // no lead-in, or the TMA path does not apply: the serial pass (exact, no fix-up needed)
+        lifb::serial_fwd_soft(I, u0, U, S, T, N, beta, theta, s);
+    }
+    return done("lifb_soft_scan_fwd");
+}
+
+int lifb_soft_serial_bwd(const float *I, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
+                         int64_t N, float beta, float theta, float alpha, void *stream)
+{
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_bwd: negative size");
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!I || !u0 || !U || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_bwd: null pointer");
+    lifb::serial_bwd_soft(I, u0, U, GS, Lam, T, N, beta, theta, alpha, false, (cudaStream_t)stream);
+    return done("lifb_soft_serial_bwd");
+}
+
+int lifb_soft_adjoint_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta, float theta,
+                        float alpha, void *stream)
+{
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_adjoint_v: negative size");
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!V || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_adjoint_v: null pointer");
+    lifb::serial_bwd_soft(V, nullptr, nullptr, GS, Lam, T, N, beta, theta, alpha, true, (cudaStream_t)stream);
+    return done("lifb_soft_adjoint_v");
+}
+
+}  // extern "C"

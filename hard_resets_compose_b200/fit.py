@@ -19,7 +19,7 @@ from . import _lib
 from . import lifscan as L
 from ._lib import check, ptr, stream_of
 
-__all__ = ["LIFParamFn", "lif_param", "param_grads"]
+__all__ = ["LIFParamFn", "lif_param", "param_grads", "LIFSoftFn", "lif_soft", "LIFSoftScanFn", "lif_soft_scan"]
 
 
 def param_grads(I, u0, U, GS, Lam, beta, theta, alpha=4.0):
@@ -76,3 +76,69 @@ def lif_param(I, u0, beta, theta, u_r, alpha=4.0, mode="auto", K=16):
     else:
         fwd = bwd = mode
     return LIFParamFn.apply(I, u0, beta, theta, u_r, alpha, fwd, bwd, K)
+
+
+def _soft_beta_grad(I, u0, U, gS, lam, beta, theta, alpha):
+    """dL/dbeta = sum_t lam_t u_{t-1} (lifscan/fit.py:116, :149), the fused
+    reduction of param_grads (its other two sums belong to the hard reset)."""
+    g_beta, _, _ = param_grads(I, u0, U, gS, lam, beta, theta, alpha)
+    return g_beta
+
+
+class LIFSoftFn(torch.autograd.Function):
+    """lifscan/fit.py:93-117: soft-reset LIF, serial kernels; gradients for I, u0, beta."""
+
+    @staticmethod
+    def forward(ctx, I, u0, beta, theta, alpha):
+        b, th = float(beta), float(theta)
+        I = I.contiguous()
+        U, S = L.soft_serial_forward(I, b, th, u0)
+        ctx.save_for_backward(I, u0, U)
+        ctx.cfg = (b, th, alpha)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        I, u0, U = ctx.saved_tensors
+        b, th, alpha = ctx.cfg
+        gS = gS.contiguous()
+        lam = L.soft_serial_backward_auto(I, u0, U, gS, b, th, alpha)
+        return lam, b * lam[0], _soft_beta_grad(I, u0, U, gS, lam, b, th, alpha), None, None
+
+
+def lif_soft(I, u0, beta, theta=1.0, alpha=4.0):
+    """lifscan/fit.py:120-121."""
+    return LIFSoftFn.apply(I, u0, beta, theta, alpha)
+
+
+class LIFSoftScanFn(torch.autograd.Function):
+    """lifscan/fit.py:124-150: soft-reset LIF with the exact soft scan (or serial)
+    forward; gradients for I, u0, beta.  mode in {"serial", "scan"}."""
+
+    @staticmethod
+    def forward(ctx, I, u0, beta, theta, alpha, mode, C, K):
+        from . import soft as TS
+        b, th = float(beta), float(theta)
+        I = I.contiguous()
+        if mode == "scan":
+            U, S = TS.soft_scan_forward(I, b, th, u0, C=C, K=K)
+        else:
+            U, S = L.soft_serial_forward(I, b, th, u0)
+        ctx.save_for_backward(I, u0, U)
+        ctx.cfg = (b, th, alpha)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        I, u0, U = ctx.saved_tensors
+        b, th, alpha = ctx.cfg
+        gS = gS.contiguous()
+        # both modes: the same adjoint (the reference's scan mode forms V and
+        # convolves by FFT, its serial mode sweeps; one sweep from U and I here)
+        lam = L.soft_serial_backward_auto(I, u0, U, gS, b, th, alpha)
+        return lam, b * lam[0], _soft_beta_grad(I, u0, U, gS, lam, b, th, alpha), None, None, None, None, None
+
+
+def lif_soft_scan(I, u0, beta, theta=1.0, alpha=4.0, mode="scan", C=128, K=32):
+    """lifscan/fit.py:153-154."""
+    return LIFSoftScanFn.apply(I, u0, beta, theta, alpha, mode, C, K)

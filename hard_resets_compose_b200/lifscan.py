@@ -37,6 +37,8 @@ __all__ = [
     "AUTO_FWD_MAX_N", "AUTO_FWD_MIN_T", "AUTO_BWD_MAX_N", "AUTO_BWD_MIN_T", "auto_modes",
     "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg", "scan_chunk_fwd", "scan_chunk_bwd",
     "lif_tuned_host", "scan_forward_spec", "spec_segment", "serial_forward_v", "lif_backward_v",
+    "soft_serial_forward", "soft_serial_backward", "soft_serial_backward_pf", "soft_serial_backward_auto",
+    "soft_bwd_cfg",
 ]
 
 _CONVERGE = -1  # max_repair value meaning "repair until converged"
@@ -385,6 +387,55 @@ def surrogate_grad(x, alpha):
     """Derivative of sigmoid(alpha*x) (lifscan/fast.py:48-51)."""
     sg = torch.sigmoid(alpha * x)
     return alpha * sg * (1 - sg)
+
+
+# ----------------------------------------------------------------------------- soft reset (serial)
+def soft_serial_forward(I, beta, theta, u0, BN=32):
+    """Soft-reset serial forward (lifscan/triton_lif.py:1072-1076) -> (U, S):
+    u <- v - theta on a spike instead of u_r."""
+    I, u0, T, N = _prep_fwd(I, u0)
+    U = torch.empty_like(I)
+    S = torch.empty_like(I)
+    lib = _lib.load()
+    with torch.cuda.device(I.device):
+        check(lib.lifb_soft_serial_fwd(ptr(I), ptr(u0), ptr(U), ptr(S), T, N, _f(beta), _f(theta), stream_of(I)),
+              "soft_serial_forward")
+    return U, S
+
+
+def soft_serial_backward(I, u0, U, GS, beta, theta, alpha=4.0, BN=32):
+    """Soft-reset detached adjoint (lifscan/triton_lif.py:1079-1083) -> Lam."""
+    I, u0, T, N = _prep_fwd(I, u0)
+    U = _cuda_f32("U", U, (T, N))
+    GS = _cuda_f32("GS", GS, (T, N))
+    Lam = torch.empty_like(I)
+    lib = _lib.load()
+    with torch.cuda.device(I.device):
+        check(lib.lifb_soft_serial_bwd(ptr(I), ptr(u0), ptr(U), ptr(GS), ptr(Lam), T, N, _f(beta), _f(theta),
+                                       _f(alpha), stream_of(I)), "soft_serial_backward")
+    return Lam
+
+
+def soft_serial_backward_pf(I, u0, U, GS, beta, theta, alpha=4.0, BN=32, D=4, num_warps=1):
+    """lifscan/triton_lif.py:1176-1180 (same results as soft_serial_backward)."""
+    return soft_serial_backward(I, u0, U, GS, beta, theta, alpha)
+
+
+def soft_bwd_cfg(N):
+    """lifscan/triton_lif.py:1192-1196 (Triton launch shape; kept for signature
+    compatibility, ignored by this implementation)."""
+    if N <= 8:
+        return 16, 8, 1
+    if N <= 64:
+        return 16, 4, 1
+    if N <= 16384:
+        return 64, 16, 1
+    return 128, 4, 1
+
+
+def soft_serial_backward_auto(I, u0, U, GS, beta, theta, alpha=4.0):
+    """lifscan/triton_lif.py:1206-1210."""
+    return soft_serial_backward(I, u0, U, GS, beta, theta, alpha)
 
 
 # ----------------------------------------------------------------------------- V-saving layer path

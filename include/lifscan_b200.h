@@ -247,6 +247,30 @@ int lifb_param_grad_partials(const float *I, const float *u0, const float *U, co
                              const float *Lam, double *partials, int64_t T, int64_t N,
                              float beta, float theta, float alpha, int M, void *stream);
 
+/* ---- Soft-reset LIF (subtractive reset u <- v - theta) ----------------------
+ * The reference's second model class (lifscan/triton_lif.py:1035-1082 and
+ * 1139-1198, lifscan/triton_soft.py): v = fl(fl(beta*u) + x); s = v >= theta;
+ * u' = s ? fl(v - theta) : v.  Forward outputs are bit-identical to the
+ * reference's fp32 soft recurrence.
+ *   lifb_soft_serial_fwd  soft_serial_forward / soft_serial_forward_tiled
+ *   lifb_soft_scan_fwd    soft_scan_forward, exact: T/L segments with W-row
+ *                         lead-ins and the fix-up (workspace:
+ *                         lifb_scan_fwd_spec_workspace_bytes(T, N, L))
+ *   lifb_soft_serial_bwd  soft_serial_backward(_auto): the detached-reset
+ *                         adjoint lam_t = GS_t sigma'(v_t) + beta lam_{t+1}
+ *                         from U, I and u0 (Lam = dL/dI, du0 = beta*Lam[0])
+ *   lifb_soft_adjoint_v   soft_adjoint_fft: the same adjoint from V (the
+ *                         pre-reset potentials), fp32 (the reference: float64 FFT) */
+int lifb_soft_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N,
+                         float beta, float theta, void *stream);
+int lifb_soft_scan_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N,
+                       float beta, float theta, int64_t L, int64_t W, void *workspace,
+                       size_t workspace_bytes, void *stream);
+int lifb_soft_serial_bwd(const float *I, const float *u0, const float *U, const float *GS, float *Lam,
+                         int64_t T, int64_t N, float beta, float theta, float alpha, void *stream);
+int lifb_soft_adjoint_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta,
+                        float theta, float alpha, void *stream);
+
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:
  * 944-983, scan_forward_v4; :512-526, scan_backward_tiled).  These phases

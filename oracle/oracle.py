@@ -66,6 +66,9 @@ def lib():
         L.oracle_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float]
         L.oracle_serial_fwd_cols.argtypes = [f32p, f32p, f32p, f32p, i64, i64, i64, i64,
                                              c_float, c_float, c_float]
+        L.oracle_soft_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float]
+        L.oracle_soft_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float,
+                                             c_int]
         L.oracle_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, f32p, i64, i64,
                                         c_float, c_float, c_float, c_float, c_int]
         L.oracle_envelope.argtypes = [f32p, f32p, f32p, i64, i64, c_int, c_float, c_float, c_float]
@@ -138,6 +141,27 @@ def serial_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=Tru
     Lam = np.empty_like(I)
     lib().oracle_serial_bwd(_p(I), _p(u0), _p(U), _p(S), _p(GS), _p(GU), _p(Lam), T, N,
                             beta, theta, u_r, alpha, int(bool(detach)))
+    return Lam
+
+
+def soft_serial_forward(I, beta, theta, u0, want_v=False):
+    """Soft-reset recurrence (lifscan/triton_lif.py:1037-1049) -> (U, S[, V])."""
+    I, u0 = _f(I), _f(u0)
+    T, N = I.shape
+    U = np.empty_like(I)
+    S = np.empty_like(I)
+    V = np.empty_like(I) if want_v else None
+    lib().oracle_soft_serial_fwd(_p(I), _p(u0), _p(U), _p(S), _p(V), T, N, beta, theta)
+    return (U, S, V) if want_v else (U, S)
+
+
+def soft_serial_backward(I, u0, U, GS, beta, theta, alpha=4.0, double=False):
+    """Soft-reset detached adjoint (lifscan/triton_lif.py:1052-1069), fp32 in the
+    kernel's order, or in double (double=True)."""
+    I, u0, U, GS = map(_f, (I, u0, U, GS))
+    T, N = I.shape
+    Lam = np.empty_like(I)
+    lib().oracle_soft_serial_bwd(_p(I), _p(u0), _p(U), _p(GS), _p(Lam), T, N, beta, theta, alpha, int(double))
     return Lam
 
 

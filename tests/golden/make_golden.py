@@ -14,7 +14,11 @@ It imports the reference's own code:
     contraction): the v3 phases env_chunk/env_carry/build3/carry2
     (triton_lif.py:698-779, 578-606), scan_forward_v3 (:782), the v4 phases
     compose_group/carry_inner (:828-932), scan_forward_v4 (:935) and
-    scan_backward_tiled (:512), including their internal map arrays and stats.
+    scan_backward_tiled (:512), including their internal map arrays and stats;
+  * the soft-reset model: triton_lif.soft_serial_forward / soft_serial_backward
+    (:1035-1082) and triton_soft.soft_scan_forward (interval maps, interpreted)
+    and soft_adjoint_fft (float64 FFT) -> tests/golden/soft_*.npz
+    (`--soft-only` regenerates just these).
 
 Inputs are drawn on the CPU with torch.Generator (tests/test_fast.py:7-9) and
 stored in the fixture too.  The GPU box never runs this script; the tests read
@@ -116,8 +120,44 @@ def npy(d):
     return {k: v.numpy() if torch.is_tensor(v) else np.asarray(v) for k, v in d.items()}
 
 
+# soft reset: name, T, N, mu, sd, seed, u0_sd, beta, alpha, C, K
+SOFT_CASES = [
+    ("soft_b095", 512, 33, 0.15, 0.4, 5, 0.3, 0.95, 4.0, 32, 16),
+    ("soft_b099", 1024, 16, 0.4, 0.3, 6, 0.3, 0.99, 4.0, 32, 32),
+    ("soft_neg", 512, 24, -0.1, 0.6, 7, 0.3, 0.9, 2.0, 16, 16),
+]
+
+
+def soft_cases():
+    """The soft-reset model (lifscan/triton_lif.py:1035-1082, lifscan/triton_soft.py):
+    serial forward and exact interval-map scan (Triton interpreter), the fp32 serial
+    adjoint (Triton interpreter) and the float64 FFT adjoint (PyTorch CPU)."""
+    from lifscan import triton_soft as TS
+    theta = 1.0
+    for (name, T, N, mu, sd, seed, u0_sd, beta, alpha, C, K) in SOFT_CASES:
+        I, u0, GS = gen(T, N, mu, sd, seed, u0_sd)
+        U, S = L.soft_serial_forward(I, beta, theta, u0)
+        st = {}
+        U2, S2 = TS.soft_scan_forward(I, beta, theta, u0, C=C, K=K, repair=10 ** 6, stats=st)
+        assert torch.equal(U2, U) and torch.equal(S2, S), name
+        lam_serial = L.soft_serial_backward(I, u0, U, GS, beta, theta, alpha)
+        uprev = torch.cat([u0[None], U[:-1]], 0)
+        V = beta * uprev + I  # as LIFSoftScanFn forms it (lifscan/fit.py:138-139)
+        lam_fft = TS.soft_adjoint_fft(V, GS, beta, theta, alpha)
+        out = dict(I=I, u0=u0, GS=GS, U=U, S=S, V=V, Lam_serial=lam_serial, Lam_fft=lam_fft,
+                   params=np.array([beta, theta, alpha, C, K], np.float64),
+                   stats_keys=np.array(sorted(st)), stats_vals=np.array([st[k] for k in sorted(st)], np.float64))
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **npy(out))
+        rel = ((lam_serial - lam_fft).norm() / lam_fft.norm()).item()
+        print(name, st, "serial vs fft rel", rel)
+
+
 def main():
     theta = 1.0
+    if "--soft-only" in sys.argv:
+        soft_cases()
+        return
+    soft_cases()
     for (name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, K) in FWD_CASES:
         I, u0, _ = gen(T, N, mu, sd, seed, u0_sd)
         us, ss, vs = fast.serial_forward_nograd(I, beta, theta, u_r, u0)

@@ -125,3 +125,20 @@ def test_backward_matches_reference(path):
     # and against fp64 autograd through the reference's differentiable serial loop
     assert rel(lam_serial, z["dI_fp64"]) < 1e-5
     assert rel(float(beta) * lam_serial[0], z["du0_fp64"]) < 1e-5
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "soft_*.npz"))), ids=os.path.basename)
+def test_oracle_soft_reset_matches_reference(path):
+    """Soft-reset model: the oracle's recurrence equals the reference's serial
+    forward (and its exact interval-map scan) bit for bit; its adjoint matches
+    the reference's fp32 serial adjoint and, in double, its float64 FFT adjoint."""
+    z = np.load(path)
+    beta, theta, alpha = (float(v) for v in z["params"][:3])
+    U, S, V = O.soft_serial_forward(z["I"], beta, theta, z["u0"], want_v=True)
+    assert_bit_equal(U, z["U"], "U")
+    assert_bit_equal(S, z["S"], "S")
+    assert_bit_equal(V, z["V"], "V")
+    lam = O.soft_serial_backward(z["I"], z["u0"], U, z["GS"], beta, theta, alpha)
+    lam_d = O.soft_serial_backward(z["I"], z["u0"], U, z["GS"], beta, theta, alpha, double=True)
+    assert rel(lam, z["Lam_serial"]) < 1e-6
+    assert rel(lam_d, z["Lam_fft"]) < 1e-6
