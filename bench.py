@@ -64,9 +64,10 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5"),
+    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5", "soft"),
                    help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step; "
-                        "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs; c5: sweep of B*N, T, beta")
+                        "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs; c5: sweep of B*N, T, beta; "
+                        "soft: the soft-reset fitting layer (lif_soft) at config 2's shape and a long soft scan")
     p.add_argument("--c5-n", default="14,15,16,17,18,19,20,21,22",
                    help="c5: log2 of the total B*N values (split over the GPUs)")
     p.add_argument("--c5-t", default="256,1024,4096", help="c5: sequence lengths")
@@ -343,6 +344,96 @@ def run_sweep(args, ws, rank, local):
         dist.destroy_process_group()
 
 
+def run_soft(args, ws, rank, local):
+    """The soft-reset model (subtractive reset; lifscan/fit.py:93-121 lif_soft,
+    lifscan/triton_soft.py soft_scan_forward): the fitting layer's forward +
+    backward (spikes out, gradients for I, u0 and beta) at config 2's shape
+    (B*N = 16384 per GPU, T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99),
+    issued eagerly; and the exact soft scan forward at T = 2^18, N = 1024 (x ~
+    N(0.02, 0.1^2)) beside the serial soft pass it replaces."""
+    import torch
+
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200 import fit
+    from hard_resets_compose_b200 import lifscan as L
+    from hard_resets_compose_b200 import soft as TS
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = _lib.load()
+    T, N = T_STEPS, N_PER_GPU
+    g = torch.Generator(device=dev).manual_seed(7000 + rank)
+    I = torch.empty(T, N, device=dev).normal_(MU, SD, generator=g)
+    GS = torch.empty(T, N, device=dev).normal_(0.0, 1.0, generator=g)
+    u0 = torch.zeros(N, device=dev)
+    Iq = I.clone().requires_grad_(True)
+    b = torch.tensor(BETA, device=dev, requires_grad=True)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    evict = torch.ones(L2_FLUSH_BYTES // 4, device=dev)
+    sink = torch.empty((), device=dev)
+
+    def step():
+        Iq.grad = None
+        b.grad = None
+        S = fit.lif_soft(Iq, u0, b, 1.0, 4.0)
+        torch.autograd.backward(S, GS)
+
+    def timed(fn, steps):
+        ms = []
+        for _ in range(steps):
+            flush.fill_(1.0)
+            torch.sum(evict, dim=0, out=sink)
+            a = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            e.record(stream)
+            e.synchronize()
+            ms.append(a.elapsed_time(e))
+        return statistics.median(ms)
+
+    # eager: the layer reads beta (a CUDA tensor) on the host, like the
+    # reference's (lifscan/fit.py:98), which rules out graph capture
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    n0 = lib.lifb_kernel_launches()
+    with ClockSampler(local) as clk:
+        ms = timed(step, args.steps)
+    launches = (lib.lifb_kernel_launches() - n0) // max(args.steps, 1)
+    U, S = L.soft_serial_forward(I, BETA, 1.0, u0)
+    ms_f = timed(lambda: L.soft_serial_forward(I, BETA, 1.0, u0), args.steps)
+    ms_b = timed(lambda: L.soft_serial_backward(I, u0, U, GS, BETA, 1.0, 4.0), args.steps)
+    hbm, peak_kind = peaks()
+    # the layer: forward 12 B, adjoint 16 B (I, U[t-1], GS in; Lam out), dbeta pass 16 B
+    layer_bytes = 12 + 16 + 16
+    Tl, Nl = 1 << 18, 1024
+    gl = torch.Generator(device=dev).manual_seed(7100 + rank)
+    Il = torch.empty(Tl, Nl, device=dev).normal_(0.02, 0.1, generator=gl)
+    u0l = torch.zeros(Nl, device=dev)
+    ms_serial_long = timed(lambda: L.soft_serial_forward(Il, BETA, 1.0, u0l), 3)
+    ms_scan_long = timed(lambda: TS.soft_scan_forward(Il, BETA, 1.0, u0l), 3)
+    units = T * N
+    if rank == 0:
+        print(json.dumps({
+            "metric": "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)",
+            "value": units / (ms / 1e3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded CUDA torch.Generator, config 2 shape)",
+            "config": {"workload": "soft: lif_soft (gradients for I, u0, beta), beta=0.99, x~N(0.05,0.2^2)",
+                       "step": "forward + torch.autograd.backward, issued eagerly (host overhead included)",
+                       "l2": "flushed before every timed call (256 MiB written, 256 MiB read)"},
+            "fwd": {"ms": ms_f, "gbs": 12 * units / (ms_f / 1e3) / 1e9, "frac": 12 * units / (ms_f / 1e3) / 1e9 / hbm},
+            "bwd": {"ms": ms_b, "gbs": 16 * units / (ms_b / 1e3) / 1e9, "frac": 16 * units / (ms_b / 1e3) / 1e9 / hbm},
+            "roofline": {"bound": "hbm", "kernel": "whole layer step (forward, adjoint, dbeta reduction)",
+                         "achieved": layer_bytes * units / (ms / 1e3) / 1e9, "peak": hbm, "peak_source": peak_kind,
+                         "unit": "GB/s", "frac": layer_bytes * units / (ms / 1e3) / 1e9 / hbm, "traffic": None},
+            "long_soft_scan": {"T": Tl, "N": Nl, "serial_ms": ms_serial_long, "scan_ms": ms_scan_long,
+                               "scan_value": Tl * Nl / (ms_scan_long / 1e3)},
+            "gpu_launches": launches * args.steps, "clocks": clk.record()}), flush=True)
+
+
 def run_long(args, ws, rank, local):
     """Config 4: one sequence of T = 2^20 rows, B*N = 1024 neurons,
     x ~ N(0.02, 0.1^2), beta = 0.99, forward + backward (spikes out, upstream
@@ -615,6 +706,9 @@ def main():
         return
     if args.workload == "c5":
         run_sweep(args, ws, rank, local)
+        return
+    if args.workload == "soft":
+        run_soft(args, ws, rank, local)
         return
 
     import torch
