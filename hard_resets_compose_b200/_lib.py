@@ -72,6 +72,15 @@ SIGNATURES = {
     "lifb_soft_serial_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float,
                              c_float, c_void_p], c_int),
     "lifb_soft_adjoint_v": ([c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float, c_void_p], c_int),
+    "lifb_aff_serial_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
+                             c_float, c_void_p], c_int),
+    "lifb_aff_scan_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float, c_float,
+                           c_i64, c_i64, c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_aff_adjoint": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
+                          c_float, c_void_p], c_int),
+    "lifb_aff_param_grad_partials": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
+                                      c_float, c_float, c_float, c_int, c_void_p], c_int),
+    "lifb_reverse_linear_scan": ([c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_void_p], c_int),
     "lifb_tshard_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
     "lifb_tshard_envelope": ([c_void_p, c_i64, c_i64, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p], c_int),

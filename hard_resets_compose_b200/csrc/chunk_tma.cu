@@ -71,8 +71,10 @@ __device__ __forceinline__ void st_vec(float *p, const Vec<NPL> &a)
 // when they reach row 0, where the start is then exact), streamed through the
 // same TMA ring, and records that guessed start in LeadStarts[m]; chunk 0
 // starts from Starts[0] or u0 as before.  VOUT: the U output receives the
-// pre-reset potential v_t instead of u_t (Ends still hold u).
-template <int NPL, int R, int S, bool VOUT, bool SOFT>
+// pre-reset potential v_t instead of u_t (Ends still hold u).  AFF: the affine
+// reset u = fl(fl(gamma*v) + delta) instead of u_r (gamma = 1, delta = -theta:
+// the soft reset).
+template <int NPL, int R, int S, bool VOUT, bool AFF>
 __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS, const float *__restrict__ u0,
@@ -80,7 +82,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
                                                 float *__restrict__ U, float *__restrict__ Sout,
                                                 float *__restrict__ Ends, int64_t N, int64_t C, float beta,
                                                 float theta, float u_r, int64_t lead, float *__restrict__ LeadStarts,
-                                                int *status)
+                                                float gamma, float delta, int *status)
 {
     constexpr int NB = 32 * NPL;
     constexpr int kTile = R * NB;  // floats per tile
@@ -147,7 +149,8 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
 #pragma unroll
         for (int r = 0; r < R; r++)
 #pragma unroll
-            for (int i = 0; i < NPL; i++) u.v[i] = step_r_u<SOFT>(u.v[i], x[r].v[i], beta, theta, u_r);
+            for (int i = 0; i < NPL; i++)
+                u.v[i] = step_r_u<AFF>(u.v[i], x[r].v[i], beta, theta, u_r, gamma, delta);
         // the stage's rows are consumed (every lane used them): refill it
         fence_proxy_async_shared();
         __syncwarp();
@@ -179,7 +182,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
             for (int i = 0; i < NPL; i++) {
                 const float v = __fadd_rn(__fmul_rn(beta, u.v[i]), x[r].v[i]);
                 const bool f = v >= theta;
-                u.v[i] = f ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
+                u.v[i] = f ? (AFF ? __fadd_rn(__fmul_rn(gamma, v), delta) : u_r) : v;
                 sp.v[i] = f ? 1.0f : 0.0f;
                 vv.v[i] = v;
             }
@@ -212,7 +215,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
                 for (int i = 0; i < NPL; i++) {
                     const float v = __fadd_rn(__fmul_rn(beta, u.v[i]), x.v[i]);
                     const bool f = v >= theta;
-                    u.v[i] = f ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
+                    u.v[i] = f ? (AFF ? __fadd_rn(__fmul_rn(gamma, v), delta) : u_r) : v;
                     sp.v[i] = f ? 1.0f : 0.0f;
                     vv.v[i] = v;
                 }
@@ -254,17 +257,17 @@ constexpr float kLog2e = 1.4426950408889634f;
 // k2 = alpha*log2(e), k2t = k2*theta: the exponent k2*(theta - v) is one FMA.
 // sig*(1 - sig) = sig - sig^2 (one FMA).  DET: the detached reset, known at
 // compile time (the V path has no other).
-template <bool READ_S, bool HAS_GU, bool DET = false, bool SOFT = false>
+template <bool READ_S, bool HAS_GU, bool DET = false, bool AFF = false>
 __device__ __forceinline__ void adj_coef_v(float v, float sread, float gs, float gu, float beta, float theta,
                                            float u_r, float alpha, float k2, float k2t, bool detach, float &a,
-                                           float &c)
+                                           float &c, float bgamma = 0.0f)
 {
     const float e = ex2_approx(fmaf(-k2, v, k2t));
     const float sig = rcp_approx(1.0f + e);
     const float sg = alpha * fmaf(-sig, sig, sig);
     float cc = gs * sg;
-    if (SOFT) {  // detached soft reset: du_t/dv_t = 1, so a = beta at every step
-        a = beta;
+    if (AFF) {  // detached affine reset: du_t/dv_t = gamma at a spike, 1 elsewhere (bgamma = beta*gamma)
+        a = v >= theta ? bgamma : beta;
     } else if (!READ_S && (DET || detach)) {  // s in {0, 1}: a = beta*(1 - s) and J*gu as selects
         const bool spk = v >= theta;
         a = spk ? 0.0f : beta;
@@ -294,9 +297,10 @@ __device__ __forceinline__ Vec<NPL> bwd_v(const float *b, int kTile, int off, co
 
 // Coefficients of NPL neurons at in-tile offset `off` (no dependence on lam,
 // so a whole tile is computed ahead of the chain).
-template <int NPL, bool READ_S, bool HAS_GU, bool FROM_V, bool SOFT = false>
+template <int NPL, bool READ_S, bool HAS_GU, bool FROM_V, bool AFF = false>
 __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec<NPL> &a, Vec<NPL> &c, float beta,
-                                         float theta, float u_r, float alpha, float k2, float k2t, bool detach)
+                                         float theta, float u_r, float alpha, float k2, float k2t, bool detach,
+                                         float bgamma = 0.0f)
 {
     using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
     const Vec<NPL> v = bwd_v<NPL, FROM_V, Ly>(b, kTile, off, nullptr, beta);
@@ -306,16 +310,16 @@ __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec
     if constexpr (HAS_GU) gu = ld_vec<NPL>(b + Ly::kGU * kTile + off);
 #pragma unroll
     for (int i = 0; i < NPL; i++)
-        adj_coef_v<READ_S, HAS_GU, FROM_V, SOFT>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f,
-                                                 beta, theta, u_r, alpha, k2, k2t, detach, a.v[i], c.v[i]);
+        adj_coef_v<READ_S, HAS_GU, FROM_V, AFF>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f,
+                                                beta, theta, u_r, alpha, k2, k2t, detach, a.v[i], c.v[i], bgamma);
 }
 
 // One reverse step for NPL neurons at in-tile offset `off`; pp (the running
 // product of a) only when the chunk map is tracked.
-template <int NPL, bool READ_S, bool HAS_GU, bool TRACK, bool FROM_V, bool SOFT = false>
+template <int NPL, bool READ_S, bool HAS_GU, bool TRACK, bool FROM_V, bool AFF = false>
 __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, const Vec<NPL> *up_override,
                                          Vec<NPL> &lam, Vec<NPL> &pp, float beta, float theta, float u_r,
-                                         float alpha, float k2, float k2t, bool detach)
+                                         float alpha, float k2, float k2t, bool detach, float bgamma = 0.0f)
 {
     using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
     const Vec<NPL> v = bwd_v<NPL, FROM_V, Ly>(b, kTile, off, up_override, beta);
@@ -326,14 +330,14 @@ __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, con
 #pragma unroll
     for (int i = 0; i < NPL; i++) {
         float a, c;
-        adj_coef_v<READ_S, HAS_GU, FROM_V, SOFT>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f,
-                                                 beta, theta, u_r, alpha, k2, k2t, detach, a, c);
+        adj_coef_v<READ_S, HAS_GU, FROM_V, AFF>(v.v[i], READ_S ? sv.v[i] : 0.0f, gs.v[i], HAS_GU ? gu.v[i] : 0.0f,
+                                                beta, theta, u_r, alpha, k2, k2t, detach, a, c, bgamma);
         lam.v[i] = c + a * lam.v[i];
         if constexpr (TRACK) pp.v[i] = a * pp.v[i];
     }
 }
 
-template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V, bool SOFT = false>
+template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V, bool AFF = false>
 __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS,
@@ -343,7 +347,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                                                 const float *__restrict__ u0, const float *__restrict__ LamEnd,
                                                 float *__restrict__ Lam, float *__restrict__ P, float *__restrict__ Q,
                                                 int32_t *__restrict__ D, int64_t N, int64_t C, float beta, float theta,
-                                                float u_r, float alpha, bool detach, int *status)
+                                                float u_r, float alpha, bool detach, float gamma, int *status)
 {
     using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
     constexpr int NB = 32 * NPL;
@@ -400,7 +404,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
         if (MODE == kReplay && LamEnd) lam = ld_vec<NPL>(LamEnd + m * N + nl);
     }
     bool ok = true;
-    const float k2 = alpha * kLog2e, k2t = k2 * theta;
+    const float k2 = alpha * kLog2e, k2t = k2 * theta, bgamma = beta * gamma;
 
     for (int64_t k = 0; k < ntiles; k++) {
         const int s = (int)(k % S);
@@ -413,8 +417,8 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             Vec<NPL> av[R], cv[R];
 #pragma unroll
             for (int rr = 0; rr < R; rr++)
-                bwd_coef<NPL, READ_S, HAS_GU, FROM_V, SOFT>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
-                                                            theta, u_r, alpha, k2, k2t, detach);
+                bwd_coef<NPL, READ_S, HAS_GU, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
+                                                           theta, u_r, alpha, k2, k2t, detach, bgamma);
             if (MODE == kReplay && k >= 2) {
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
@@ -456,9 +460,9 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             for (int rr = R - 1; rr >= 0; rr--) {
                 const int64_t t = rbase + rr;
                 if (t < cstart) break;
-                bwd_step<NPL, READ_S, HAS_GU, TRACK, FROM_V, SOFT>(b, kTile, rr * NB + NPL * lane,
-                                                             (!FROM_V && t == 0) ? &uz : nullptr, lam, pp, beta,
-                                                             theta, u_r, alpha, k2, k2t, detach);
+                bwd_step<NPL, READ_S, HAS_GU, TRACK, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane,
+                                                            (!FROM_V && t == 0) ? &uz : nullptr, lam, pp, beta,
+                                                            theta, u_r, alpha, k2, k2t, detach, bgamma);
                 if constexpr (TRACK) {
 #pragma unroll
                     for (int i = 0; i < NPL; i++) dn[i] += pp.v[i] != 0.f ? 1 : 0;
@@ -550,26 +554,28 @@ static int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
     return ((N + 127) / 128) * M >= (int64_t)min_ctas_per_sm * sms ? 4 : 1;
 }
 
-template <int NPL, bool VOUT, bool SOFT>
+template <int NPL, bool VOUT, bool AFF>
 static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, int64_t start_stride, float *U,
                        float *S, float *Ends, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r,
-                       int64_t lead, float *LeadStarts, int *status, cudaStream_t s)
+                       int64_t lead, float *LeadStarts, float gamma, float delta, int *status, cudaStream_t s)
 {
     constexpr int NB = 32 * NPL;
     constexpr int R = FwdTile<NPL>::R, ST = FwdTile<NPL>::S;
     const size_t smem = (size_t)(ST + 4) * R * NB * 4;
-    auto kern = k_fwd_tma<NPL, R, ST, VOUT, SOFT>;
+    auto kern = k_fwd_tma<NPL, R, ST, VOUT, AFF>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
     kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], u0, Starts, start_stride, U, S, Ends, N, C, beta, theta, u_r,
-                             lead, LeadStarts, status);
+                             lead, LeadStarts, gamma, delta, status);
 }
 
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
-                    int64_t start_stride, int64_t lead, float *LeadStarts, bool vout, bool soft)
+                    int64_t start_stride, int64_t lead, float *LeadStarts, bool vout, Reset rs)
 {
+    const bool aff = rs.aff;
+    const float gamma = rs.gamma, delta = rs.delta;
     const void *p[] = {I, u0, Starts, U, S, Ends, LeadStarts};
     if (!tma_ok(p, 7, N) || C <= 0 || T % C) return false;
     const int64_t M = T / C;
@@ -585,35 +591,36 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
         !make_tmap_2d(&maps[2], S, N, T, 32 * npl, R))
         return false;
     int *status = device_status_ptr();
-    auto go = [&](auto npl_c, auto vout_c, auto soft_c) {
-        launch_fwd<decltype(npl_c)::value, decltype(vout_c)::value, decltype(soft_c)::value>(
-            maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, status, s);
+    auto go = [&](auto npl_c, auto vout_c, auto aff_c) {
+        launch_fwd<decltype(npl_c)::value, decltype(vout_c)::value, decltype(aff_c)::value>(
+            maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, gamma, delta,
+            status, s);
     };
     using I1 = std::integral_constant<int, 1>;
     using I4 = std::integral_constant<int, 4>;
     using BT = std::true_type;
     using BF = std::false_type;
-    auto go2 = [&](auto npl_c, auto vout_c) { soft ? go(npl_c, vout_c, BT{}) : go(npl_c, vout_c, BF{}); };
+    auto go2 = [&](auto npl_c, auto vout_c) { aff ? go(npl_c, vout_c, BT{}) : go(npl_c, vout_c, BF{}); };
     if (npl == 4) vout ? go2(I4{}, BT{}) : go2(I4{}, BF{});
     else vout ? go2(I1{}, BT{}) : go2(I1{}, BF{});
     return true;
 }
 
-template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V = false, bool SOFT = false>
+template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V = false, bool AFF = false>
 static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *LamEnd, float *Lam, float *P, float *Q,
                        int32_t *D, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
-                       bool detach, int *status, cudaStream_t s)
+                       bool detach, int *status, cudaStream_t s, float gamma = 0.0f)
 {
     constexpr int NB = 32 * NPL;
     constexpr int NT = BwdLayout<READ_S, HAS_GU, FROM_V>::NT;
     constexpr int R = BwdTile<NPL>::R, ST = BwdTile<NPL>::S;
     const size_t smem = ((size_t)ST * NT + (MODE == kReplay ? 2 : 0)) * R * NB * 4;
-    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V, SOFT>;
+    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V, AFF>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
     kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], u0, LamEnd, Lam, P, Q, D, N, C,
-                             beta, theta, u_r, alpha, detach, status);
+                             beta, theta, u_r, alpha, detach, gamma, status);
 }
 
 template <int NPL, int MODE, bool TRACK>
@@ -658,10 +665,11 @@ bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, 
     return true;
 }
 
-// Soft-reset adjoint over one chunk of T rows: lam_t = gs_t sigma'(v_t) +
-// beta lam_{t+1}, v_t from U[t-1] and I[t] (from_v: V given).
-bool bwd_tma_soft(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
-                  int64_t N, float beta, float theta, float alpha, bool from_v, cudaStream_t s)
+// Affine-reset adjoint over one chunk of T rows (detached reset): lam_t =
+// gs_t sigma'(v_t) + a_t lam_{t+1}, a_t = beta*gamma at a spike, beta elsewhere
+// (gamma = 1: the soft reset); v_t from U[t-1] and I[t] (from_v: V given).
+bool bwd_tma_aff(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T, int64_t N,
+                 float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s)
 {
     const void *p[] = {IV, u0, U, GS, Lam};
     if (!tma_ok(p, 5, N) || T <= 0) return false;
@@ -680,11 +688,11 @@ bool bwd_tma_soft(const float *IV, const float *u0, const float *U, const float 
     maps[2] = maps[4] = maps[0];
     int *status = device_status_ptr();
     if (from_v) {
-        if (npl == 4) launch_bwd<4, false, false, kReplay, false, true, true>(maps, nullptr, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
-        else launch_bwd<1, false, false, kReplay, false, true, true>(maps, nullptr, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
+        if (npl == 4) launch_bwd<4, false, false, kReplay, false, true, true>(maps, nullptr, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s, gamma);
+        else launch_bwd<1, false, false, kReplay, false, true, true>(maps, nullptr, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s, gamma);
     } else {
-        if (npl == 4) launch_bwd<4, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
-        else launch_bwd<1, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s);
+        if (npl == 4) launch_bwd<4, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s, gamma);
+        else launch_bwd<1, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s, gamma);
     }
     return true;
 }

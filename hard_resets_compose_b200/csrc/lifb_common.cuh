@@ -33,30 +33,33 @@ LIFB_DEV float lif_step_u(float u, float x, float beta, float theta, float u_r)
 }
 
 // The same step with the reset chosen at compile time: the hard reset above,
-// or the soft (subtractive) reset u' = s ? fl(v - theta) : v of the soft-reset
-// model (lifscan/triton_lif.py:1037-1049 soft_fwd_kernel, lifscan/triton_soft.py:107-111).
-template <bool SOFT>
-LIFB_DEV float step_r(float u, float x, float beta, float theta, float u_r, bool &s)
+// or the affine reset u' = s ? fl(fl(gamma*v) + delta) : v of the affine-reset
+// model (lifscan/triton_affine.py:20-24 _aff_step).  It contains the soft
+// (subtractive) reset (lifscan/triton_lif.py:1037-1049): gamma = 1, delta =
+// -theta gives fl(v - theta) bit for bit.
+template <bool AFF>
+LIFB_DEV float step_r(float u, float x, float beta, float theta, float u_r, float gamma, float delta, bool &s)
 {
     const float v = __fadd_rn(__fmul_rn(beta, u), x);
     s = v >= theta;
-    return s ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
+    return s ? (AFF ? __fadd_rn(__fmul_rn(gamma, v), delta) : u_r) : v;
 }
 
-template <bool SOFT>
-LIFB_DEV float step_r_u(float u, float x, float beta, float theta, float u_r)
+template <bool AFF>
+LIFB_DEV float step_r_u(float u, float x, float beta, float theta, float u_r, float gamma, float delta)
 {
     bool s;
-    return step_r<SOFT>(u, x, beta, theta, u_r, s);
+    return step_r<AFF>(u, x, beta, theta, u_r, gamma, delta, s);
 }
 
 // Runtime choice (host-chosen flag, uniform across the grid): the fix-up and
 // lead-in kernels, whose cost is not the step.
-LIFB_DEV float step_any(float u, float x, float beta, float theta, float u_r, bool soft, bool &s)
+LIFB_DEV float step_any(float u, float x, float beta, float theta, float u_r, bool aff, float gamma, float delta,
+                        bool &s)
 {
     const float v = __fadd_rn(__fmul_rn(beta, u), x);
     s = v >= theta;
-    return s ? (soft ? __fsub_rn(v, theta) : u_r) : v;
+    return s ? (aff ? __fadd_rn(__fmul_rn(gamma, v), delta) : u_r) : v;
 }
 
 // fl(fl(a*b) + c), never contracted to an FMA.

@@ -27,6 +27,22 @@ struct SuperMaps {
     int32_t *SN, *SOVF;
 };
 
+// The reset rule of one scan, uniform across the grid: hard (u' = u_r) unless
+// aff, else the affine reset u' = fl(fl(gamma*v) + delta) (gamma = 1, delta =
+// -theta: the soft reset u' = v - theta, bit for bit).
+struct Reset {
+    bool aff = false;
+    float gamma = 0.0f, delta = 0.0f;
+};
+inline Reset affine_reset(float gamma, float delta)
+{
+    Reset r;
+    r.aff = true;
+    r.gamma = gamma;
+    r.delta = delta;
+    return r;
+}
+
 // runtime.cu
 bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_x, int box_y);
 // 2-D map of a [T, N] array of 4-byte elements (fp32, or int32 when int32 is true).
@@ -45,7 +61,7 @@ int read_device_status(bool reset);       // synchronous read (current device)
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
                     int64_t start_stride = 1, int64_t lead = 0, float *LeadStarts = nullptr, bool vout = false,
-                    bool soft = false);
+                    Reset rs = {});
 // Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0)
 // and, when P is given, also the chunk maps; mode 1 writes only P, Q.
 // P[m] = prod of a_t over chunk m, Q[m] = lam at the chunk's first row.
@@ -62,11 +78,11 @@ bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const fl
 bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, int32_t *D, int64_t T, int64_t N,
                int64_t C, float beta, float theta, float alpha, cudaStream_t s);
 
-// chunk_tma.cu: the soft-reset adjoint (a = beta at every step) over one chunk
-// of T rows, v from U and I (u0 for row 0) or from V (from_v); false when the
-// TMA path does not apply.
-bool bwd_tma_soft(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
-                  int64_t N, float beta, float theta, float alpha, bool from_v, cudaStream_t s);
+// chunk_tma.cu: the affine-reset adjoint (detached reset: a = beta*gamma at a
+// spike, beta elsewhere) over one chunk of T rows, v from U and I (u0 for row
+// 0) or from V (from_v); false when the TMA path does not apply.
+bool bwd_tma_aff(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T, int64_t N,
+                 float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s);
 
 // serial.cu
 void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
@@ -80,11 +96,20 @@ void serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T
                   float theta, float u_r, cudaStream_t s);
 void serial_bwd_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta, float theta,
                   float alpha, cudaStream_t s);
-// Soft-reset (u' = v - theta) serial forward and adjoint (from U and I, or from V).
-void serial_fwd_soft(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
-                     float theta, cudaStream_t s);
-void serial_bwd_soft(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
-                     int64_t N, float beta, float theta, float alpha, bool from_v, cudaStream_t s);
+// Affine-reset (u' = gamma*v + delta) serial forward (U, or V when vout) and
+// adjoint (from U and I, or from V).
+void serial_fwd_aff(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                    float theta, float gamma, float delta, bool vout, cudaStream_t s);
+void serial_bwd_aff(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
+                    int64_t N, float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s);
+
+// aff.cu: the exact speculative forward of the affine reset over segments of
+// L rows with W-row lead-ins (serial pass when T == L, W == 0 or the TMA path
+// does not apply); workspace as lifb_scan_fwd_spec.  False: workspace missing,
+// misaligned or too small (nothing launched).
+bool aff_scan_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta, float theta,
+                  float gamma, float delta, int64_t L, int64_t W, void *workspace, size_t workspace_bytes,
+                  cudaStream_t s);
 
 // scan_fwd_grid.cu
 // grid_envelope / grid_build / grid_compose work on the first M chunks (M2
@@ -121,7 +146,7 @@ void replay_any(const float *I, const float *u0, const float *Starts, float *U, 
 // and Starts[0] is left to the caller.
 void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts,
                    float *end_guess, int64_t N, int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r,
-                   cudaStream_t s, bool soft = false);
+                   cudaStream_t s, Reset rs = {});
 
 // host_pipeline.cu
 size_t host_pipe_workspace_bytes(int64_t T, int64_t N, int64_t block_n);
@@ -157,10 +182,10 @@ bool env_carry_staged(const float *u0, const float *EC, const float *EA, const f
 
 // scan_fixup.cu
 // EndsNew [NS, N] float and Changed [NS, N] int32 are scratch.
-// soft: the soft (subtractive) reset u' = v - theta instead of u_r.
+// rs: the reset rule (default: hard reset to u_r).
 void fwd_fixup(const float *I, const float *Starts, int64_t start_stride, float *U, float *S, float *Ends,
                float *EndsNew, int32_t *Changed, int64_t N, int64_t NS, int64_t L, float beta, float theta, float u_r,
-               int *longest_chain, cudaStream_t s, bool soft = false);
+               int *longest_chain, cudaStream_t s, Reset rs = {});
 // With D (from bwd_tma) the rows above each chunk's last spike, where every
 // a is exactly beta (detached reset), are corrected in place by
 // lam_end * beta^k instead of being recomputed from I, U and GS.

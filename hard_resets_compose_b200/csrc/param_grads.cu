@@ -8,6 +8,12 @@
 // surrogate and three products as [T, N] tensors (fit.py:36-47); here every
 // (chunk of rows, neuron) thread reads I, U, GS and Lam once (16 B per
 // neuron-step) and accumulates in fp64; the caller sums the [3, M, N] partials.
+//
+// The affine reset u = s ? gamma v + delta : v (LIFAffineFn.backward,
+// lifscan/triton_affine.py:230-238) adds one row: with dL/du_t = beta lam_{t+1},
+//   dL/ddelta = sum_t s_t beta lam_{t+1}   (the du_r row above)
+//   dL/dgamma = sum_t s_t v_t beta lam_{t+1}
+// and dL/dbeta = sum_t lam_t u_{t-1} as before (U holds the post-reset u).
 #include <cstdio>
 
 #include "lifb_common.cuh"
@@ -18,6 +24,7 @@ namespace lifb {
 
 constexpr int kPgBlock = 128;
 
+template <bool AFF>
 __global__ void __launch_bounds__(kPgBlock) k_param_partials(const float *__restrict__ I, const float *__restrict__ u0,
                                                              const float *__restrict__ U, const float *__restrict__ GS,
                                                              const float *__restrict__ Lam, double *__restrict__ part,
@@ -29,7 +36,7 @@ __global__ void __launch_bounds__(kPgBlock) k_param_partials(const float *__rest
     if (n >= N) return;
     const int64_t t0 = m * C, t1 = (t0 + C < T) ? t0 + C : T;
     const float k2 = alpha * 1.4426950408889634f;  // exp(x) = 2^(x log2 e)
-    double db = 0.0, dt = 0.0, dr = 0.0;
+    double db = 0.0, dt = 0.0, dr = 0.0, dg = 0.0;
     constexpr int kB = 8;
     for (int64_t b = t0; b < t1; b += kB) {
         float up[kB], x[kB], gs[kB], lm[kB], ln[kB];
@@ -53,13 +60,18 @@ __global__ void __launch_bounds__(kPgBlock) k_param_partials(const float *__rest
                 const float sg = alpha * sig * (1.0f - sig);
                 db += (double)lm[q] * (double)up[q];
                 dt -= (double)gs[q] * (double)sg;
-                if (v >= theta) dr += (double)beta * (double)ln[q];
+                if (v >= theta) {
+                    const double bl = (double)beta * (double)ln[q];
+                    dr += bl;
+                    if (AFF) dg += (double)v * bl;
+                }
             }
         }
     }
     part[(0 * M + m) * N + n] = db;
     part[(1 * M + m) * N + n] = dt;
     part[(2 * M + m) * N + n] = dr;
+    if (AFF) part[(3 * M + m) * N + n] = dg;
 }
 
 }  // namespace lifb
@@ -78,30 +90,55 @@ int lifb_param_grad_chunks(int64_t T, int64_t N)
     return (int)M;
 }
 
-int lifb_param_grad_partials(const float *I, const float *u0, const float *U, const float *GS, const float *Lam,
-                             double *partials, int64_t T, int64_t N, float beta, float theta, float alpha, int M,
-                             void *stream)
+static int param_partials(const char *who, bool aff, const float *I, const float *u0, const float *U,
+                          const float *GS, const float *Lam, double *partials, int64_t T, int64_t N, float beta,
+                          float theta, float alpha, int M, void *stream)
 {
+    char msg[160];
     if (T < 0 || N < 0 || M <= 0 || M > 65535) {
-        lifb::set_last_error("lifb_param_grad_partials: bad sizes (need T, N >= 0 and 1 <= M <= 65535)");
+        snprintf(msg, sizeof msg, "%s: bad sizes (need T, N >= 0 and 1 <= M <= 65535)", who);
+        lifb::set_last_error(msg);
         return LIFB_ERR_INVALID_ARGUMENT;
     }
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !GS || !Lam || !partials) {
-        lifb::set_last_error("lifb_param_grad_partials: null pointer");
+        snprintf(msg, sizeof msg, "%s: null pointer", who);
+        lifb::set_last_error(msg);
         return LIFB_ERR_INVALID_ARGUMENT;
     }
     const int64_t C = (T + M - 1) / M;  // chunks past row T-1 write zeros
     lifb::count_launches(1);
     dim3 g((unsigned)((N + lifb::kPgBlock - 1) / lifb::kPgBlock), (unsigned)M);
-    lifb::k_param_partials<<<g, lifb::kPgBlock, 0, (cudaStream_t)stream>>>(I, u0, U, GS, Lam, partials, T, N, C,
-                                                                           beta, theta, alpha);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (aff)
+        lifb::k_param_partials<true><<<g, lifb::kPgBlock, 0, s>>>(I, u0, U, GS, Lam, partials, T, N, C, beta, theta,
+                                                                  alpha);
+    else
+        lifb::k_param_partials<false><<<g, lifb::kPgBlock, 0, s>>>(I, u0, U, GS, Lam, partials, T, N, C, beta, theta,
+                                                                   alpha);
     if (cudaGetLastError() != cudaSuccess) {
-        lifb::set_last_error("lifb_param_grad_partials: launch failed");
+        snprintf(msg, sizeof msg, "%s: launch failed", who);
+        lifb::set_last_error(msg);
         return LIFB_ERR_CUDA;
     }
     lifb::set_last_error("");
     return LIFB_OK;
+}
+
+int lifb_param_grad_partials(const float *I, const float *u0, const float *U, const float *GS, const float *Lam,
+                             double *partials, int64_t T, int64_t N, float beta, float theta, float alpha, int M,
+                             void *stream)
+{
+    return param_partials("lifb_param_grad_partials", false, I, u0, U, GS, Lam, partials, T, N, beta, theta, alpha,
+                          M, stream);
+}
+
+int lifb_aff_param_grad_partials(const float *I, const float *u0, const float *U, const float *GS, const float *Lam,
+                                 double *partials, int64_t T, int64_t N, float beta, float theta, float alpha, int M,
+                                 void *stream)
+{
+    return param_partials("lifb_aff_param_grad_partials", true, I, u0, U, GS, Lam, partials, T, N, beta, theta,
+                          alpha, M, stream);
 }
 
 }  // extern "C"

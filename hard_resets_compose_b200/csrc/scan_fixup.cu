@@ -41,7 +41,7 @@ template <int kB>
 __device__ __forceinline__ bool replay_until_sync(const float *__restrict__ I, float *__restrict__ U,
                                                   float *__restrict__ S, int64_t N, int64_t n, bool act, int64_t r0,
                                                   int64_t L, float &u, bool active, float beta, float theta,
-                                                  float u_r, bool soft = false)
+                                                  float u_r, Reset rs = {})
 {
     const unsigned full = 0xffffffffu;
     bool synced = !active;
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool replay_until_sync(const float *__restrict__ I, f
         for (int q = 0; q < kB; q++) {
             if (active && b + q < L) {
                 bool f;
-                const float un = step_any(u, x[q], beta, theta, u_r, soft, f);
+                const float un = step_any(u, x[q], beta, theta, u_r, rs.aff, rs.gamma, rs.delta, f);
                 const float fs = f ? 1.0f : 0.0f;
                 u = un;
                 if (same_bits(un, uo[q]) && fs == so[q]) {
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kFixBlock) k_fwd_fixup_par(const float *__rest
                                                              float *__restrict__ U, float *__restrict__ S,
                                                              const float *__restrict__ Ends, float *__restrict__ EndsNew,
                                                              int32_t *__restrict__ Changed, int64_t N, int64_t L,
-                                                             float beta, float theta, float u_r, bool soft)
+                                                             float beta, float theta, float u_r, Reset rs)
 {
     const int64_t n = (int64_t)blockIdx.x * kFixBlock + threadIdx.x;
     const int64_t sg = (int64_t)blockIdx.y + 1;
@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kFixBlock) k_fwd_fixup_par(const float *__rest
         return;
     }
     float u = prev;
-    const bool synced = replay_until_sync<16>(I, U, S, N, n, act, sg * L, L, u, need, beta, theta, u_r, soft);
+    const bool synced = replay_until_sync<16>(I, U, S, N, n, act, sg * L, L, u, need, beta, theta, u_r, rs);
     if (act) {
         Changed[sg * N + n] = synced ? 0 : 1;
         if (!synced) EndsNew[sg * N + n] = u;
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kFixBlock) k_fwd_fixup_seq(const float *__rest
                                                              const float *__restrict__ EndsNew,
                                                              const int32_t *__restrict__ Changed, int64_t N,
                                                              int64_t NS, int64_t L, float beta, float theta, float u_r,
-                                                             int *__restrict__ longest_chain, bool soft)
+                                                             int *__restrict__ longest_chain, Reset rs)
 {
     const int64_t n = (int64_t)blockIdx.x * kFixBlock + threadIdx.x;
     const bool act = n < N;
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kFixBlock) k_fwd_fixup_seq(const float *__rest
             // redo segment sg from the previous segment's new end
             float u = end;
             const bool synced = replay_until_sync<16>(I, U, S, N, n, act, sg * L, L, u, carry, beta, theta, u_r,
-                                                      soft);
+                                                      rs);
             if (carry && !synced) {  // synced lanes rejoined the stored rows: (ch, e) stand
                 ch = true;
                 e = u;
@@ -297,15 +297,15 @@ __global__ void __launch_bounds__(kFixBlock) k_bwd_fixup(const float *__restrict
 
 void fwd_fixup(const float *I, const float *Starts, int64_t start_stride, float *U, float *S, float *Ends,
                float *EndsNew, int32_t *Changed, int64_t N, int64_t NS, int64_t L, float beta, float theta, float u_r,
-               int *longest_chain, cudaStream_t s, bool soft)
+               int *longest_chain, cudaStream_t s, Reset rs)
 {
     if (NS < 2) return;
     const unsigned nb = (unsigned)((N + kFixBlock - 1) / kFixBlock);
     count_launches(2);
     k_fwd_fixup_par<<<dim3(nb, (unsigned)(NS - 1)), kFixBlock, 0, s>>>(I, Starts, start_stride, U, S, Ends, EndsNew,
-                                                                       Changed, N, L, beta, theta, u_r, soft);
+                                                                       Changed, N, L, beta, theta, u_r, rs);
     k_fwd_fixup_seq<<<nb, kFixBlock, 0, s>>>(I, U, S, Ends, EndsNew, Changed, N, NS, L, beta, theta, u_r,
-                                             longest_chain, soft);
+                                             longest_chain, rs);
 }
 
 void bwd_fixup(const float *I, const float *u0, const float *U, const float *S, const float *GS, const float *GU,

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
                                                        const float *__restrict__ I_halo, int64_t W_halo,
                                                        float *__restrict__ Starts, float *__restrict__ end_guess,
                                                        int64_t N, int64_t NS, int64_t L, int64_t W, float beta,
-                                                       float theta, float u_r, bool soft)
+                                                       float theta, float u_r, Reset rs)
 {
     const int64_t n = (int64_t)blockIdx.x * kLeadBlock + threadIdx.x;
     const int64_t s = blockIdx.y;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
         for (int q = 0; q < kLeadB; q++)
             if (b + q < len) {
                 bool f;
-                u = step_any(u, cur[q], beta, theta, u_r, soft, f);
+                u = step_any(u, cur[q], beta, theta, u_r, rs.aff, rs.gamma, rs.delta, f);
             }
 #pragma unroll
         for (int q = 0; q < kLeadB; q++) cur[q] = nxt[q];
@@ -97,12 +97,12 @@ __global__ void __launch_bounds__(kLeadBlock) k_leadin(const float *__restrict__
 
 void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts,
                    float *end_guess, int64_t N, int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r,
-                   cudaStream_t s, bool soft)
+                   cudaStream_t s, Reset rs)
 {
     count_launches(1);
     const unsigned ny = (unsigned)(NS + (end_guess ? 1 : 0));
     k_leadin<<<dim3((unsigned)((N + kLeadBlock - 1) / kLeadBlock), ny), kLeadBlock, 0, s>>>(
-        I, u0, I_halo, W_halo, Starts, end_guess, N, NS, L, W, beta, theta, u_r, soft);
+        I, u0, I_halo, W_halo, Starts, end_guess, N, NS, L, W, beta, theta, u_r, rs);
 }
 
 __global__ void k_copy_row(const float *__restrict__ src, float *__restrict__ dst, int64_t N)

@@ -14,12 +14,14 @@ namespace lifb {
 constexpr int kSerBlock = 128;
 constexpr int kSerD = 16;
 
-// VOUT: U receives the pre-reset potential v_t instead of u_t.  SOFT: the
-// soft (subtractive) reset u = v - theta.
-template <int D, bool VOUT, bool SOFT = false>
+// VOUT: U receives the pre-reset potential v_t instead of u_t.  AFF: the
+// affine reset u = fl(fl(gamma*v) + delta) (gamma = 1, delta = -theta: the
+// soft reset).
+template <int D, bool VOUT, bool AFF = false>
 __global__ void __launch_bounds__(kSerBlock) k_serial_fwd(const float *__restrict__ I, const float *__restrict__ u0,
                                                           float *__restrict__ U, float *__restrict__ S, int64_t T,
-                                                          int64_t N, float beta, float theta, float u_r)
+                                                          int64_t N, float beta, float theta, float u_r,
+                                                          float gamma = 0.0f, float delta = 0.0f)
 {
     int64_t n = (int64_t)blockIdx.x * kSerBlock + threadIdx.x;
     if (n >= N) return;
@@ -41,7 +43,7 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_fwd(const float *__restric
         for (int d = 0; d < D; d++) {
             const float v = __fadd_rn(__fmul_rn(beta, u), cur[d]);
             const bool s = v >= theta;
-            u = s ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
+            u = s ? (AFF ? __fadd_rn(__fmul_rn(gamma, v), delta) : u_r) : v;
             int64_t o = (t0 + d) * N + n;
             U[o] = VOUT ? v : u;
             S[o] = s ? 1.0f : 0.0f;
@@ -54,7 +56,7 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_fwd(const float *__restric
     for (int64_t t = Tf; t < T; t++) {
         const float v = __fadd_rn(__fmul_rn(beta, u), __ldg(p + t * N));
         const bool s = v >= theta;
-        u = s ? (SOFT ? __fsub_rn(v, theta) : u_r) : v;
+        u = s ? (AFF ? __fadd_rn(__fmul_rn(gamma, v), delta) : u_r) : v;
         U[t * N + n] = VOUT ? v : u;
         S[t * N + n] = s ? 1.0f : 0.0f;
     }
@@ -143,20 +145,22 @@ void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, 
     k_serial_fwd<kSerD, false><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, u_r);
 }
 
-// Soft-reset adjoint, one thread per neuron: lam_t = gs_t sigma'(v_t) + beta lam_{t+1} with v_t from
-// V (when V is given) or from U[t-1] and I[t] (u0 for row 0).
+// Affine-reset adjoint (detached reset), one thread per neuron: lam_t =
+// gs_t sigma'(v_t) + a_t lam_{t+1}, a_t = beta*gamma at a spike and beta
+// elsewhere, with v_t from V (from_v) or from U[t-1] and I[t] (u0 for row 0).
 template <int D>
-__global__ void __launch_bounds__(kSerBlock) k_serial_bwd_soft(const float *__restrict__ IV,
-                                                               const float *__restrict__ u0,
-                                                               const float *__restrict__ U,
-                                                               const float *__restrict__ GS, float *__restrict__ Lam,
-                                                               int64_t T, int64_t N, float beta, float theta,
-                                                               float alpha, bool from_v)
+__global__ void __launch_bounds__(kSerBlock) k_serial_bwd_aff(const float *__restrict__ IV,
+                                                              const float *__restrict__ u0,
+                                                              const float *__restrict__ U,
+                                                              const float *__restrict__ GS, float *__restrict__ Lam,
+                                                              int64_t T, int64_t N, float beta, float theta,
+                                                              float alpha, float gamma, bool from_v)
 {
     int64_t n = (int64_t)blockIdx.x * kSerBlock + threadIdx.x;
     if (n >= N) return;
     float lam = 0.0f;
     const float un0 = from_v ? 0.0f : u0[n];
+    const float bg = beta * gamma;
     for (int64_t tend = T; tend > 0; tend -= D) {
         int64_t t0 = tend - D > 0 ? tend - D : 0;
         int cnt = (int)(tend - t0);
@@ -174,30 +178,34 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_bwd_soft(const float *__re
         for (int dd = D - 1; dd >= 0; dd--) {
             if (dd < cnt) {
                 const float sig = __frcp_rn(1.0f + __expf(-alpha * (v[dd] - theta)));
-                lam = gs[dd] * (alpha * sig * (1.0f - sig)) + beta * lam;
+                lam = gs[dd] * (alpha * sig * (1.0f - sig)) + (v[dd] >= theta ? bg : beta) * lam;
                 Lam[(t0 + dd) * N + n] = lam;
             }
         }
     }
 }
 
-void serial_fwd_soft(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
-                     float theta, cudaStream_t s)
+void serial_fwd_aff(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
+                    float theta, float gamma, float delta, bool vout, cudaStream_t s)
 {
-    if (fwd_replay_tma(I, u0, nullptr, U, S, nullptr, T, N, T, beta, theta, 0.0f, s, 1, 0, nullptr, false, true))
+    if (fwd_replay_tma(I, u0, nullptr, U, S, nullptr, T, N, T, beta, theta, 0.0f, s, 1, 0, nullptr, vout,
+                       affine_reset(gamma, delta)))
         return;
     unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
     count_launches(1);
-    k_serial_fwd<kSerD, false, true><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, 0.0f);
+    if (vout)
+        k_serial_fwd<kSerD, true, true><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, 0.0f, gamma, delta);
+    else
+        k_serial_fwd<kSerD, false, true><<<g, kSerBlock, 0, s>>>(I, u0, U, S, T, N, beta, theta, 0.0f, gamma, delta);
 }
 
-void serial_bwd_soft(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
-                     int64_t N, float beta, float theta, float alpha, bool from_v, cudaStream_t s)
+void serial_bwd_aff(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
+                    int64_t N, float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s)
 {
-    if (bwd_tma_soft(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, from_v, s)) return;
+    if (bwd_tma_aff(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, gamma, from_v, s)) return;
     unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
     count_launches(1);
-    k_serial_bwd_soft<8><<<g, kSerBlock, 0, s>>>(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, from_v);
+    k_serial_bwd_aff<8><<<g, kSerBlock, 0, s>>>(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, gamma, from_v);
 }
 
 void serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N, float beta,

@@ -18,6 +18,10 @@
 //   lifb_soft_adjoint_v    soft_adjoint_fft: the same recurrence from V; the
 //                          reference convolves in float64 by FFT, here it is the
 //                          fp32 reverse sweep (within the 1e-5 gradient bar)
+//
+// The soft reset is the affine reset u <- gamma*v + delta at gamma = 1, delta =
+// -theta (fl(1*v) = v, so fl(v + (-theta)) = fl(v - theta) bit for bit): every
+// entry point here runs the affine kernels of aff.cu with those constants.
 #include <cstdio>
 
 #include "lifb_common.cuh"
@@ -50,7 +54,7 @@ int lifb_soft_serial_fwd(const float *I, const float *u0, float *U, float *S, in
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_fwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_fwd: null pointer");
-    lifb::serial_fwd_soft(I, u0, U, S, T, N, beta, theta, (cudaStream_t)stream);
+    lifb::serial_fwd_aff(I, u0, U, S, T, N, beta, theta, 1.0f, -theta, false, (cudaStream_t)stream);
     return done("lifb_soft_serial_fwd");
 }
 
@@ -63,27 +67,10 @@ int lifb_soft_scan_fwd(const float *I, const float *u0, float *U, float *S, int6
     if (T / L > 65535) return fail(LIFB_ERR_UNSUPPORTED, "lifb_soft_scan_fwd: more than 65535 segments");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_scan_fwd: null pointer");
-    cudaStream_t s = (cudaStream_t)stream;
-    const int64_t NS = T / L;
-    if (NS == 1) {
-        lifb::serial_fwd_soft(I, u0, U, S, T, N, beta, theta, s);
-        return done("lifb_soft_scan_fwd");
-    }
-    const size_t one = ((size_t)NS * N * 4 + 255) / 256 * 256;
-    if (!workspace || (uintptr_t)workspace % 256 || workspace_bytes < 4 * one)
+    if (!lifb::aff_scan_fwd(I, u0, U, S, T, N, beta, theta, 1.0f, -theta, L, W, workspace, workspace_bytes,
+                            (cudaStream_t)stream))
         return fail(LIFB_ERR_WORKSPACE, "lifb_soft_scan_fwd: workspace missing, misaligned or too small "
                                         "(lifb_scan_fwd_spec_workspace_bytes)");
-    char *b = (char *)workspace;
-    float *Starts = (float *)b, *Ends = (float *)(b + one), *EndsNew = (float *)(b + 2 * one);
-    int32_t *Changed = (int32_t *)(b + 3 * one);
-    // segments led in and replayed in one launch, then the exact fix-up
-    if (W > 0 &&
-        lifb::fwd_replay_tma(I, u0, nullptr, U, S, Ends, T, N, L, beta, theta, 0.0f, s, 1, W, Starts, false, true)) {
-        lifb::fwd_fixup(I, Starts, 1, U, S, Ends, EndsNew, Changed, N, NS, L, beta, theta, 0.0f, nullptr, s, true);
-    } else {
-        // no lead-in, or the TMA path does not apply: the serial pass (exact, no fix-up needed)
-        lifb::serial_fwd_soft(I, u0, U, S, T, N, beta, theta, s);
-    }
     return done("lifb_soft_scan_fwd");
 }
 
@@ -93,7 +80,7 @@ int lifb_soft_serial_bwd(const float *I, const float *u0, const float *U, const 
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_bwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_bwd: null pointer");
-    lifb::serial_bwd_soft(I, u0, U, GS, Lam, T, N, beta, theta, alpha, false, (cudaStream_t)stream);
+    lifb::serial_bwd_aff(I, u0, U, GS, Lam, T, N, beta, theta, alpha, 1.0f, false, (cudaStream_t)stream);
     return done("lifb_soft_serial_bwd");
 }
 
@@ -103,7 +90,7 @@ int lifb_soft_adjoint_v(const float *V, const float *GS, float *Lam, int64_t T, 
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_adjoint_v: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!V || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_adjoint_v: null pointer");
-    lifb::serial_bwd_soft(V, nullptr, nullptr, GS, Lam, T, N, beta, theta, alpha, true, (cudaStream_t)stream);
+    lifb::serial_bwd_aff(V, nullptr, nullptr, GS, Lam, T, N, beta, theta, alpha, 1.0f, true, (cudaStream_t)stream);
     return done("lifb_soft_adjoint_v");
 }
 

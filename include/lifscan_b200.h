@@ -271,6 +271,39 @@ int lifb_soft_serial_bwd(const float *I, const float *u0, const float *U, const 
 int lifb_soft_adjoint_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta,
                         float theta, float alpha, void *stream);
 
+/* ---- Affine-reset LIF (u <- gamma*v + delta on a spike, 0 <= gamma <= 1) ----
+ * lifscan/triton_affine.py: v = fl(fl(beta*u) + x); s = v >= theta;
+ * u' = s ? fl(fl(gamma*v) + delta) : v (gamma = 0, delta = u_r: the hard
+ * reset; gamma = 1, delta = -theta: the soft reset, bit for bit).
+ *   lifb_aff_serial_fwd   aff_serial_forward (triton_affine.py:158-162)
+ *   lifb_aff_scan_fwd     aff_scan_forward (:165-199), exact: T/L segments with
+ *                         W-row lead-ins and the fix-up (workspace:
+ *                         lifb_scan_fwd_spec_workspace_bytes(T, N, L)); gamma
+ *                         outside [0, 1] is LIFB_ERR_INVALID_ARGUMENT
+ *   lifb_aff_adjoint      LIFAffineFn.backward's adjoint (:230-238): lam_t =
+ *                         GS_t sigma'(v_t) + a_t lam_{t+1}, a_t = beta*gamma at
+ *                         a spike, beta elsewhere, lam_T = 0; s, v recomputed
+ *                         from U, I and u0 (Lam = dL/dI, du0 = beta*Lam[0])
+ *   lifb_aff_param_grad_partials  as lifb_param_grad_partials with a fourth
+ *                         block: partials[4][M][N] = (dbeta, dtheta, ddelta,
+ *                         dgamma), ddelta = sum s beta lam_{t+1}, dgamma = sum
+ *                         s v beta lam_{t+1}
+ *   lifb_reverse_linear_scan  reverse_affine_scan (:202-211) for [T][N] a, b:
+ *                         out_t = a_t out_{t+1} + b_t, out_T = 0 (fp32 in order) */
+int lifb_aff_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N,
+                        float beta, float theta, float gamma, float delta, void *stream);
+int lifb_aff_scan_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N,
+                      float beta, float theta, float gamma, float delta, int64_t L, int64_t W,
+                      void *workspace, size_t workspace_bytes, void *stream);
+int lifb_aff_adjoint(const float *I, const float *u0, const float *U, const float *GS, float *Lam,
+                     int64_t T, int64_t N, float beta, float theta, float alpha, float gamma,
+                     void *stream);
+int lifb_aff_param_grad_partials(const float *I, const float *u0, const float *U, const float *GS,
+                                 const float *Lam, double *partials, int64_t T, int64_t N,
+                                 float beta, float theta, float alpha, int M, void *stream);
+int lifb_reverse_linear_scan(const float *A, const float *B, float *Out, int64_t T, int64_t N,
+                             void *stream);
+
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:
  * 944-983, scan_forward_v4; :512-526, scan_backward_tiled).  These phases

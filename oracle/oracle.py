@@ -31,6 +31,7 @@ _lib = None
 
 f32p = ctypes.POINTER(ctypes.c_float)
 i32p = ctypes.POINTER(ctypes.c_int32)
+f64p = ctypes.POINTER(ctypes.c_double)
 i64 = ctypes.c_int64
 c_float = ctypes.c_float
 c_int = ctypes.c_int
@@ -69,6 +70,10 @@ def lib():
         L.oracle_soft_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float]
         L.oracle_soft_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float,
                                              c_int]
+        L.oracle_aff_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float,
+                                            c_float]
+        L.oracle_aff_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, f64p, i64, i64, c_float, c_float,
+                                            c_float, c_float, c_int]
         L.oracle_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, f32p, i64, i64,
                                         c_float, c_float, c_float, c_float, c_int]
         L.oracle_envelope.argtypes = [f32p, f32p, f32p, i64, i64, c_int, c_float, c_float, c_float]
@@ -163,6 +168,29 @@ def soft_serial_backward(I, u0, U, GS, beta, theta, alpha=4.0, double=False):
     Lam = np.empty_like(I)
     lib().oracle_soft_serial_bwd(_p(I), _p(u0), _p(U), _p(GS), _p(Lam), T, N, beta, theta, alpha, int(double))
     return Lam
+
+
+def aff_serial_forward(I, beta, theta, gamma, delta, u0, want_v=False):
+    """Affine-reset recurrence (lifscan/triton_affine.py:19-23, 158-162) -> (U, S[, V])."""
+    I, u0 = _f(I), _f(u0)
+    T, N = I.shape
+    U = np.empty_like(I)
+    S = np.empty_like(I)
+    V = np.empty_like(I) if want_v else None
+    lib().oracle_aff_serial_fwd(_p(I), _p(u0), _p(U), _p(S), _p(V), T, N, beta, theta, gamma, delta)
+    return (U, S, V) if want_v else (U, S)
+
+
+def aff_serial_backward(I, u0, U, GS, beta, theta, gamma, alpha=4.0, double=False):
+    """Affine-reset detached adjoint and (dbeta, dgamma, ddelta)
+    (lifscan/triton_affine.py:229-238) -> (Lam, pg), fp32 in order or in
+    double (double=True)."""
+    I, u0, U, GS = map(_f, (I, u0, U, GS))
+    T, N = I.shape
+    Lam = np.empty_like(I)
+    pg = np.zeros(3, np.float64)
+    lib().oracle_aff_serial_bwd(_p(I), _p(u0), _p(U), _p(GS), _p(Lam), pg.ctypes.data_as(f64p), T, N, beta, theta, alpha, gamma, int(double))
+    return Lam, pg
 
 
 def envelope(I, u0, C, beta, u_r, margin=1e-5):

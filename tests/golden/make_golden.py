@@ -18,7 +18,11 @@ It imports the reference's own code:
   * the soft-reset model: triton_lif.soft_serial_forward / soft_serial_backward
     (:1035-1082) and triton_soft.soft_scan_forward (interval maps, interpreted)
     and soft_adjoint_fft (float64 FFT) -> tests/golden/soft_*.npz
-    (`--soft-only` regenerates just these).
+    (`--soft-only` regenerates just these);
+  * the affine-reset model: triton_affine.aff_serial_forward /
+    aff_scan_forward (interpreted) and LIFAffineFn's gradients (PyTorch CPU)
+    over the (gamma, delta) x beta grid of tests/test_affine.py ->
+    tests/golden/affine_grid.npz (`--affine-only`).
 
 Inputs are drawn on the CPU with torch.Generator (tests/test_fast.py:7-9) and
 stored in the fixture too.  The GPU box never runs this script; the tests read
@@ -152,12 +156,54 @@ def soft_cases():
         print(name, st, "serial vs fft rel", rel)
 
 
+# affine reset: the (gamma, delta) x beta grid of tests/test_affine.py:7-9 at
+# reduced size (T, N), C = 32, K = 16
+AFF_GRID = ((0.0, 0.0), (0.0, -0.2), (0.3, -0.1), (0.7, -0.5), (1.0, -1.0), (0.5, 0.2))
+AFF_BETAS = (0.9, 0.97)
+AFF_T, AFF_N, AFF_C, AFF_K = 256, 16, 32, 16
+
+
+def affine_cases():
+    """The affine-reset model (lifscan/triton_affine.py): serial forward and the
+    exact piecewise-affine map scan (Triton interpreter), and LIFAffineFn's
+    gradients for I, u0, beta, gamma, delta (PyTorch CPU, its own backward)."""
+    from lifscan import triton_affine as A
+    theta, alpha = 1.0, 4.0
+    out = {}
+    for gi, (gamma, delta) in enumerate(AFF_GRID):
+        for bi, beta in enumerate(AFF_BETAS):
+            key = f"g{gi}b{bi}"
+            I, u0, GS = gen(AFF_T, AFF_N, 0.15, 0.4, 20 + 2 * gi + bi, 0.2)
+            U, S = A.aff_serial_forward(I, beta, theta, gamma, delta, u0)
+            st = {}
+            U2, S2 = A.aff_scan_forward(I, beta, theta, gamma, delta, u0, C=AFF_C, K=AFF_K, repair=10 ** 6,
+                                        stats=st)
+            assert torch.equal(U2, U) and torch.equal(S2, S), key
+            Ig = I.clone().requires_grad_(True)
+            ug = u0.clone().requires_grad_(True)
+            ps = [torch.tensor(v, dtype=torch.float32, requires_grad=True) for v in (beta, gamma, delta)]
+            Sg = A.lif_affine(Ig, ug, ps[0], ps[1], ps[2], theta=theta, alpha=alpha, mode="serial")
+            assert torch.equal(Sg.detach(), S), key
+            (GS * Sg).sum().backward()
+            out.update({f"{key}_I": I, f"{key}_u0": u0, f"{key}_GS": GS, f"{key}_U": U, f"{key}_S": S,
+                        f"{key}_dI": Ig.grad, f"{key}_du0": ug.grad,
+                        f"{key}_dp": torch.stack([p.grad for p in ps]),
+                        f"{key}_params": np.array([beta, theta, gamma, delta, alpha], np.float64),
+                        f"{key}_stats": np.array([st["repair_iters"], st["overflow_frac"], st["mean_pieces"]])})
+            print(key, gamma, delta, beta, st, "spikes", float(S.mean()))
+    np.savez_compressed(os.path.join(HERE, "affine_grid.npz"), **npy(out))
+
+
 def main():
     theta = 1.0
     if "--soft-only" in sys.argv:
         soft_cases()
         return
+    if "--affine-only" in sys.argv:
+        affine_cases()
+        return
     soft_cases()
+    affine_cases()
     for (name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, K) in FWD_CASES:
         I, u0, _ = gen(T, N, mu, sd, seed, u0_sd)
         us, ss, vs = fast.serial_forward_nograd(I, beta, theta, u_r, u0)

@@ -142,3 +142,47 @@ def test_oracle_soft_reset_matches_reference(path):
     lam_d = O.soft_serial_backward(z["I"], z["u0"], U, z["GS"], beta, theta, alpha, double=True)
     assert rel(lam, z["Lam_serial"]) < 1e-6
     assert rel(lam_d, z["Lam_fft"]) < 1e-6
+
+
+AFF = os.path.join(GOLD, "affine_grid.npz")
+AFF_KEYS = [f"g{g}b{b}" for g in range(6) for b in range(2)]
+
+
+@pytest.mark.parametrize("key", AFF_KEYS)
+def test_oracle_affine_reset_matches_reference(key):
+    """Affine-reset model over the (gamma, delta) x beta grid of the
+    reference's tests/test_affine.py: the oracle's recurrence equals the
+    reference's serial forward (and its exact piecewise-affine map scan) bit
+    for bit; its adjoint and (dbeta, dgamma, ddelta) match LIFAffineFn's own
+    backward (Hillis-Steele scan in fp32, so within rounding)."""
+    z = np.load(AFF)
+    beta, theta, gamma, delta, alpha = (float(v) for v in z[f"{key}_params"])
+    I, u0, GS = z[f"{key}_I"], z[f"{key}_u0"], z[f"{key}_GS"]
+    U, S = O.aff_serial_forward(I, beta, theta, gamma, delta, u0)
+    assert_bit_equal(U, z[f"{key}_U"], "U")
+    assert_bit_equal(S, z[f"{key}_S"], "S")
+    lam, pg = O.aff_serial_backward(I, u0, U, GS, beta, theta, gamma, alpha)
+    lam_d, pg_d = O.aff_serial_backward(I, u0, U, GS, beta, theta, gamma, alpha, double=True)
+    assert rel(lam, z[f"{key}_dI"]) < 1e-6
+    assert rel(lam_d, z[f"{key}_dI"]) < 1e-6
+    assert rel(beta * lam[0], z[f"{key}_du0"]) < 1e-6
+    dp = z[f"{key}_dp"].astype(np.float64)
+    for i in range(3):
+        assert abs(pg[i] - dp[i]) <= 1e-5 * (abs(dp[i]) + 1e-3), (i, pg, dp)
+        assert abs(pg_d[i] - dp[i]) <= 1e-5 * (abs(dp[i]) + 1e-3), (i, pg_d, dp)
+
+
+def test_oracle_affine_contains_hard_and_soft():
+    """gamma = 0, delta = u_r is the hard reset and gamma = 1, delta = -theta
+    the soft reset, bit for bit (lifscan/triton_affine.py:1-4)."""
+    rng = np.random.default_rng(3)
+    I = (0.15 + 0.4 * rng.standard_normal((700, 13))).astype(np.float32)
+    u0 = (0.3 * rng.standard_normal(13)).astype(np.float32)
+    Ua, Sa = O.aff_serial_forward(I, 0.95, 1.0, 0.0, -0.2, u0)
+    Uh, Sh = O.serial_forward(I, 0.95, 1.0, -0.2, u0)
+    assert_bit_equal(Ua, Uh, "U hard")
+    assert_bit_equal(Sa, Sh, "S hard")
+    Ua, Sa = O.aff_serial_forward(I, 0.95, 1.0, 1.0, -1.0, u0)
+    Us, Ss = O.soft_serial_forward(I, 0.95, 1.0, u0)
+    assert_bit_equal(Ua, Us, "U soft")
+    assert_bit_equal(Sa, Ss, "S soft")
