@@ -64,10 +64,11 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5", "soft"),
+    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5", "soft", "affine"),
                    help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step; "
                         "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs; c5: sweep of B*N, T, beta; "
-                        "soft: the soft-reset fitting layer (lif_soft) at config 2's shape and a long soft scan")
+                        "soft: the soft-reset fitting layer (lif_soft) at config 2's shape and a long soft scan; "
+                        "affine: the affine-reset layer (lif_affine) at config 2's shape and a long affine scan")
     p.add_argument("--c5-n", default="14,15,16,17,18,19,20,21,22",
                    help="c5: log2 of the total B*N values (split over the GPUs)")
     p.add_argument("--c5-t", default="256,1024,4096", help="c5: sequence lengths")
@@ -344,16 +345,25 @@ def run_sweep(args, ws, rank, local):
         dist.destroy_process_group()
 
 
-def run_soft(args, ws, rank, local):
-    """The soft-reset model (subtractive reset; lifscan/fit.py:93-121 lif_soft,
-    lifscan/triton_soft.py soft_scan_forward): the fitting layer's forward +
-    backward (spikes out, gradients for I, u0 and beta) at config 2's shape
-    (B*N = 16384 per GPU, T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99),
-    issued eagerly; and the exact soft scan forward at T = 2^18, N = 1024 (x ~
-    N(0.02, 0.1^2)) beside the serial soft pass it replaces."""
+# affine workload: the reset u <- gamma*v + delta at one of the reference's
+# test points (lifscan tests/test_affine.py:7)
+AFF_GAMMA, AFF_DELTA = 0.3, -0.1
+
+
+def run_reset_family(args, ws, rank, local, family):
+    """The soft-reset model (family "soft": subtractive reset; lifscan/fit.py:
+    93-121 lif_soft, lifscan/triton_soft.py soft_scan_forward) or the
+    affine-reset model (family "affine": u <- gamma*v + delta, gamma = 0.3,
+    delta = -0.1; lifscan/triton_affine.py lif_affine, aff_scan_forward): the
+    fitting layer's forward + backward (spikes out; gradients for I, u0 and
+    beta, and for gamma and delta) at config 2's shape (B*N = 16384 per GPU,
+    T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99), issued eagerly; and the exact
+    scan forward at T = 2^18, N = 1024 (x ~ N(0.02, 0.1^2)) beside the serial
+    pass it replaces."""
     import torch
 
     from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200 import affine as A
     from hard_resets_compose_b200 import fit
     from hard_resets_compose_b200 import lifscan as L
     from hard_resets_compose_b200 import soft as TS
@@ -368,15 +378,21 @@ def run_soft(args, ws, rank, local):
     u0 = torch.zeros(N, device=dev)
     Iq = I.clone().requires_grad_(True)
     b = torch.tensor(BETA, device=dev, requires_grad=True)
+    gm = torch.tensor(AFF_GAMMA, device=dev, requires_grad=True)
+    dl = torch.tensor(AFF_DELTA, device=dev, requires_grad=True)
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
     evict = torch.ones(L2_FLUSH_BYTES // 4, device=dev)
     sink = torch.empty((), device=dev)
+    soft = family == "soft"
 
     def step():
         Iq.grad = None
-        b.grad = None
-        S = fit.lif_soft(Iq, u0, b, 1.0, 4.0)
+        b.grad = gm.grad = dl.grad = None
+        if soft:
+            S = fit.lif_soft(Iq, u0, b, 1.0, 4.0)
+        else:
+            S = A.lif_affine(Iq, u0, b, gm, dl, theta=1.0, alpha=4.0, mode="serial")
         torch.autograd.backward(S, GS)
 
     def timed(fn, steps):
@@ -394,7 +410,8 @@ def run_soft(args, ws, rank, local):
         return statistics.median(ms)
 
     # eager: the layer reads beta (a CUDA tensor) on the host, like the
-    # reference's (lifscan/fit.py:98), which rules out graph capture
+    # reference's (lifscan/fit.py:98, triton_affine.py:219), which rules out
+    # graph capture
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
@@ -402,35 +419,61 @@ def run_soft(args, ws, rank, local):
     with ClockSampler(local) as clk:
         ms = timed(step, args.steps)
     launches = (lib.lifb_kernel_launches() - n0) // max(args.steps, 1)
-    U, S = L.soft_serial_forward(I, BETA, 1.0, u0)
-    ms_f = timed(lambda: L.soft_serial_forward(I, BETA, 1.0, u0), args.steps)
-    ms_b = timed(lambda: L.soft_serial_backward(I, u0, U, GS, BETA, 1.0, 4.0), args.steps)
+    if soft:
+        fwd = lambda: L.soft_serial_forward(I, BETA, 1.0, u0)  # noqa: E731
+        U, S = fwd()
+        bwd = lambda: L.soft_serial_backward(I, u0, U, GS, BETA, 1.0, 4.0)  # noqa: E731
+        serial_long = lambda x, z: L.soft_serial_forward(x, BETA, 1.0, z)  # noqa: E731
+        scan_long = lambda x, z: TS.soft_scan_forward(x, BETA, 1.0, z)  # noqa: E731
+    else:
+        # the layer's single-pass path: forward writes V and S, the adjoint
+        # reads V and gS and sums the parameter gradients in the same sweep
+        fwd = lambda: A.aff_serial_forward_v(I, BETA, 1.0, AFF_GAMMA, AFF_DELTA, u0)  # noqa: E731
+        V, S = fwd()
+        bwd = lambda: A.aff_adjoint_v(V, u0, GS, BETA, 1.0, AFF_GAMMA, AFF_DELTA, 4.0)  # noqa: E731
+        serial_long = lambda x, z: A.aff_serial_forward(x, BETA, 1.0, AFF_GAMMA, AFF_DELTA, z)  # noqa: E731
+        scan_long = lambda x, z: A.aff_scan_forward(x, BETA, 1.0, AFF_GAMMA, AFF_DELTA, z)  # noqa: E731
+    ms_f = timed(fwd, args.steps)
+    ms_b = timed(bwd, args.steps)
     hbm, peak_kind = peaks()
-    # the layer: forward 12 B, adjoint 16 B (I, U[t-1], GS in; Lam out), dbeta pass 16 B
-    layer_bytes = 12 + 16 + 16
+    # soft layer: forward 12 B, adjoint 16 B (I, U[t-1], GS in; Lam out),
+    # dbeta pass 16 B (I, U[t-1], GS, Lam in).  Affine layer: forward 12 B
+    # (I in; V, S out), adjoint with the parameter sums 12 B (V, GS in; Lam out)
+    fwd_bytes, bwd_bytes = (12, 16) if soft else (12, 12)
+    layer_bytes = 12 + 16 + 16 if soft else 12 + 12
     Tl, Nl = 1 << 18, 1024
     gl = torch.Generator(device=dev).manual_seed(7100 + rank)
     Il = torch.empty(Tl, Nl, device=dev).normal_(0.02, 0.1, generator=gl)
     u0l = torch.zeros(Nl, device=dev)
-    ms_serial_long = timed(lambda: L.soft_serial_forward(Il, BETA, 1.0, u0l), 3)
-    ms_scan_long = timed(lambda: TS.soft_scan_forward(Il, BETA, 1.0, u0l), 3)
+    ms_serial_long = timed(lambda: serial_long(Il, u0l), 3)
+    ms_scan_long = timed(lambda: scan_long(Il, u0l), 3)
     units = T * N
+    if soft:
+        metric = "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)"
+        workload = "soft: lif_soft (gradients for I, u0, beta), beta=0.99, x~N(0.05,0.2^2)"
+    else:
+        metric = "neuron-steps/s, affine-reset layer lif_affine fwd+bwd (B*N=16384/GPU, T=1024)"
+        workload = (f"affine: lif_affine mode=serial (gradients for I, u0, beta, gamma, delta), beta=0.99, "
+                    f"gamma={AFF_GAMMA}, delta={AFF_DELTA}, x~N(0.05,0.2^2)")
     if rank == 0:
         print(json.dumps({
-            "metric": "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)",
+            "metric": metric,
             "value": units / (ms / 1e3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded CUDA torch.Generator, config 2 shape)",
-            "config": {"workload": "soft: lif_soft (gradients for I, u0, beta), beta=0.99, x~N(0.05,0.2^2)",
+            "config": {"workload": workload,
                        "step": "forward + torch.autograd.backward, issued eagerly (host overhead included)",
                        "l2": "flushed before every timed call (256 MiB written, 256 MiB read)"},
-            "fwd": {"ms": ms_f, "gbs": 12 * units / (ms_f / 1e3) / 1e9, "frac": 12 * units / (ms_f / 1e3) / 1e9 / hbm},
-            "bwd": {"ms": ms_b, "gbs": 16 * units / (ms_b / 1e3) / 1e9, "frac": 16 * units / (ms_b / 1e3) / 1e9 / hbm},
-            "roofline": {"bound": "hbm", "kernel": "whole layer step (forward, adjoint, dbeta reduction)",
+            "fwd": {"ms": ms_f, "bytes_per_unit": fwd_bytes, "gbs": fwd_bytes * units / (ms_f / 1e3) / 1e9,
+                    "frac": fwd_bytes * units / (ms_f / 1e3) / 1e9 / hbm},
+            "bwd": {"ms": ms_b, "bytes_per_unit": bwd_bytes, "gbs": bwd_bytes * units / (ms_b / 1e3) / 1e9,
+                    "frac": bwd_bytes * units / (ms_b / 1e3) / 1e9 / hbm},
+            "kernels_ms": ms_f + ms_b,
+            "roofline": {"bound": "hbm", "kernel": "whole layer step (forward, adjoint, parameter reduction)",
                          "achieved": layer_bytes * units / (ms / 1e3) / 1e9, "peak": hbm, "peak_source": peak_kind,
                          "unit": "GB/s", "frac": layer_bytes * units / (ms / 1e3) / 1e9 / hbm, "traffic": None},
-            "long_soft_scan": {"T": Tl, "N": Nl, "serial_ms": ms_serial_long, "scan_ms": ms_scan_long,
-                               "scan_value": Tl * Nl / (ms_scan_long / 1e3)},
+            "long_scan": {"T": Tl, "N": Nl, "serial_ms": ms_serial_long, "scan_ms": ms_scan_long,
+                          "scan_value": Tl * Nl / (ms_scan_long / 1e3)},
             "gpu_launches": launches * args.steps, "clocks": clk.record()}), flush=True)
 
 
@@ -707,8 +750,8 @@ def main():
     if args.workload == "c5":
         run_sweep(args, ws, rank, local)
         return
-    if args.workload == "soft":
-        run_soft(args, ws, rank, local)
+    if args.workload in ("soft", "affine"):
+        run_reset_family(args, ws, rank, local, args.workload)
         return
 
     import torch

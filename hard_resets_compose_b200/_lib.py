@@ -81,6 +81,10 @@ SIGNATURES = {
     "lifb_aff_param_grad_partials": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
                                       c_float, c_float, c_float, c_int, c_void_p], c_int),
     "lifb_reverse_linear_scan": ([c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_void_p], c_int),
+    "lifb_aff_serial_fwd_v": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
+                               c_float, c_void_p], c_int),
+    "lifb_aff_adjoint_v": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float,
+                            c_float, c_float, c_float, c_void_p], c_int),
     "lifb_tshard_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
     "lifb_tshard_envelope": ([c_void_p, c_i64, c_i64, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p], c_int),

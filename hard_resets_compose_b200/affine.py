@@ -17,10 +17,15 @@ Deliberate differences:
     ("segments", "lead_in") with repair_iters = 0.  C, K, BN, BNc, BNr are
     accepted; T % C == 0 and 0 <= gamma <= 1 are checked as the reference
     asserts them.
-  * LIFAffineFn's adjoint is one fp32 reverse sweep per neuron
-    (lifb_aff_adjoint) instead of reverse_affine_scan's Hillis-Steele passes
-    over [T, N]; the parameter gradients come from one fused pass
-    (lifb_aff_param_grad_partials, fp64 partial sums).
+  * LIFAffineFn's adjoint is one fp32 reverse sweep per neuron instead of
+    reverse_affine_scan's Hillis-Steele passes over [T, N].  When the forward
+    is one streaming pass (mode "serial", or "scan" at lengths where the scan
+    is that pass) the layer saves V (the potentials before the reset) instead
+    of I and U, and the adjoint sweep reads V and gS once and accumulates the
+    beta, gamma and delta sums in fp64 as it goes (lifb_aff_adjoint_v: 12 B
+    per neuron-step for the whole backward); otherwise it saves I, u0, U and
+    runs the adjoint and one fused parameter pass
+    (lifb_aff_param_grad_partials).
   * reverse_affine_scan runs lifb_reverse_linear_scan (fp32, in order) for
     [T] and [T, ...] inputs.
 """
@@ -32,8 +37,8 @@ from . import _lib
 from . import lifscan as L
 from ._lib import check, ptr, stream_of
 
-__all__ = ["aff_serial_forward", "aff_scan_forward", "reverse_affine_scan", "aff_param_grads", "LIFAffineFn",
-           "lif_affine", "AFF_LEAD"]
+__all__ = ["aff_serial_forward", "aff_scan_forward", "reverse_affine_scan", "aff_adjoint", "aff_param_grads",
+           "aff_serial_forward_v", "aff_adjoint_v", "LIFAffineFn", "lif_affine", "AFF_LEAD"]
 
 # Lead-in rows of the speculative affine forward.  gamma < 1 contracts the
 # state difference at every spike (gamma = 0 forgets the start at the first
@@ -138,32 +143,89 @@ def aff_param_grads(I, u0, U, gS, Lam, beta, theta, alpha=4.0):
     return g[0], g[3], g[2]
 
 
+def aff_serial_forward_v(I, beta, theta, gamma, delta, u0):
+    """The serial affine forward returning (V, S): V[t] = v_t =
+    fl(fl(beta*u_{t-1}) + x_t), the potential before the reset
+    (lifb_aff_serial_fwd_v)."""
+    I, u0, T, N = L._prep_fwd(I, u0)
+    V = torch.empty_like(I)
+    S = torch.empty_like(I)
+    lib = _lib.load()
+    with torch.cuda.device(I.device):
+        check(lib.lifb_aff_serial_fwd_v(ptr(I), ptr(u0), ptr(V), ptr(S), T, N, float(beta), float(theta),
+                                        float(gamma), float(delta), stream_of(I)), "aff_serial_forward_v")
+    return V, S
+
+
+def aff_adjoint_v(V, u0, gS, beta, theta, gamma, delta, alpha=4.0, param_grads=True):
+    """lam = dL/dv from V (aff_serial_forward_v's output) and gS, and with
+    param_grads the 0-d fp32 (dL/dbeta, dL/dgamma, dL/ddelta) of the same
+    sweep -> (Lam, (d_beta, d_gamma, d_delta) or None)."""
+    if V.dim() != 2:
+        raise ValueError(f"V must be [T, N], got shape {tuple(V.shape)}")
+    V = L._cuda_f32("V", V)
+    T, N = V.shape
+    u0 = L._cuda_f32("u0", u0, (N,))
+    gS = L._cuda_f32("gS", gS, (T, N))
+    Lam = torch.empty_like(V)
+    sums = torch.zeros(3, N, dtype=torch.float64, device=V.device) if param_grads else None
+    lib = _lib.load()
+    with torch.cuda.device(V.device):
+        check(lib.lifb_aff_adjoint_v(ptr(V), ptr(u0), ptr(gS), ptr(Lam), ptr(sums) if param_grads else None, T, N,
+                                     float(beta), float(theta), float(alpha), float(gamma), float(delta),
+                                     stream_of(V)), "aff_adjoint_v")
+    if not param_grads:
+        return Lam, None
+    g = sums.sum(dim=1).to(torch.float32)
+    return Lam, (g[0], g[1], g[2])
+
+
 class LIFAffineFn(torch.autograd.Function):
     """lifscan/triton_affine.py:214-242: affine-reset LIF; grads w.r.t. I, u0,
     beta, gamma, delta (detached reset, sigmoid surrogate)."""
 
     @staticmethod
     def forward(ctx, I, u0, beta, gamma, delta, theta, alpha, mode, C, K):
-        b, g, dl, th = float(beta), float(gamma), float(delta), float(theta)
+        b, g, dl, th = L._host_scalars(beta, gamma, delta, theta)
         I = I.contiguous()
+        T, N = I.shape
+        ctx.cfg = (b, g, dl, th, alpha)
+        if mode == "scan":
+            if int(C) <= 0 or T % int(C):
+                raise AssertionError(f"T={T} must be a multiple of C={C}")
+            _check_gamma(g)
+        ctx.vpath = L._single_pass(T, N, mode)
+        if ctx.vpath:
+            # one streaming pass: save V (same bytes as U) and let the adjoint
+            # read V and gS only, with the parameter sums in the same sweep
+            V, S = aff_serial_forward_v(I, b, th, g, dl, u0)
+            ctx.save_for_backward(V, u0)
+            return S
         if mode == "scan":
             U, S = aff_scan_forward(I, b, th, g, dl, u0, C=C, K=K)
         else:
             U, S = aff_serial_forward(I, b, th, g, dl, u0)
         ctx.save_for_backward(I, u0, U)
-        ctx.cfg = (b, g, dl, th, alpha)
         return S
 
     @staticmethod
     def backward(ctx, gS):
-        I, u0, U = ctx.saved_tensors
         b, g, dl, th, alpha = ctx.cfg
         gS = gS.contiguous()
+        need = ctx.needs_input_grad
+        want_params = need[2] or need[3] or need[4]
+        d_beta = d_gamma = d_delta = None
+        if ctx.vpath:
+            V, u0 = ctx.saved_tensors
+            lam, pg = aff_adjoint_v(V, u0, gS, b, th, g, dl, alpha, param_grads=want_params)
+            if want_params:
+                d_beta, d_gamma, d_delta = pg
+            return (lam, b * lam[0], d_beta if need[2] else None, d_gamma if need[3] else None,
+                    d_delta if need[4] else None, None, None, None, None, None)
+        I, u0, U = ctx.saved_tensors
         # S is this layer's own output: the kernels recompute it from U and I
         lam = aff_adjoint(I, u0, U, gS, b, th, g, alpha)
-        need = ctx.needs_input_grad
-        d_beta = d_gamma = d_delta = None
-        if need[2] or need[3] or need[4]:
+        if want_params:
             d_beta, d_gamma, d_delta = aff_param_grads(I, u0, U, gS, lam, b, th, alpha)
         # parameters passed as Python numbers get no gradient
         return (lam, b * lam[0], d_beta if need[2] else None, d_gamma if need[3] else None,

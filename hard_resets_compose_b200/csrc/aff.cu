@@ -21,6 +21,13 @@
 //                          scan over [T, N] (reverse_affine_scan, :202-211); here
 //                          one reverse sweep per neuron through the TMA adjoint
 //                          kernel, s recomputed from U and I.
+//   lifb_aff_serial_fwd_v  the serial forward writing V (pre-reset potentials)
+//                          in place of U: the layer's single-pass forward
+//   lifb_aff_adjoint_v     the adjoint from V and u0 with the parameter sums of
+//                          LIFAffineFn.backward fused into the same sweep (one
+//                          read of V and GS, one write of Lam: 12 B per
+//                          neuron-step instead of 16 for the adjoint plus 16
+//                          for a separate parameter pass)
 //   lifb_reverse_linear_scan  reverse_affine_scan itself for any (a, b) [T, N]:
 //                          out_t = a_t out_{t+1} + b_t, out_T = 0, fp32 in order.
 #include <cstdio>
@@ -148,6 +155,28 @@ int lifb_aff_adjoint(const float *I, const float *u0, const float *U, const floa
     if (!I || !u0 || !U || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_adjoint: null pointer");
     lifb::serial_bwd_aff(I, u0, U, GS, Lam, T, N, beta, theta, alpha, gamma, false, (cudaStream_t)stream);
     return done("lifb_aff_adjoint");
+}
+
+int lifb_aff_serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N, float beta,
+                          float theta, float gamma, float delta, void *stream)
+{
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_serial_fwd_v: negative size");
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!I || !u0 || !V || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_serial_fwd_v: null pointer");
+    lifb::serial_fwd_aff(I, u0, V, S, T, N, beta, theta, gamma, delta, true, (cudaStream_t)stream);
+    return done("lifb_aff_serial_fwd_v");
+}
+
+int lifb_aff_adjoint_v(const float *V, const float *u0, const float *GS, float *Lam, double *param_sums, int64_t T,
+                       int64_t N, float beta, float theta, float alpha, float gamma, float delta, void *stream)
+{
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_adjoint_v: negative size");
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!V || !GS || !Lam || (param_sums && !u0))
+        return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_adjoint_v: null pointer (param_sums needs u0)");
+    lifb::serial_bwd_aff(V, u0, nullptr, GS, Lam, T, N, beta, theta, alpha, gamma, true, (cudaStream_t)stream, delta,
+                         param_sums);
+    return done("lifb_aff_adjoint_v");
 }
 
 int lifb_reverse_linear_scan(const float *A, const float *B, float *Out, int64_t T, int64_t N, void *stream)

@@ -337,7 +337,8 @@ __device__ __forceinline__ void bwd_step(const float *b, int kTile, int off, con
     }
 }
 
-template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V, bool AFF = false>
+template <int NPL, int R, int S, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V, bool AFF = false,
+          bool PG = false>
 __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensorMap tI,
                                                 const __grid_constant__ CUtensorMap tU,
                                                 const __grid_constant__ CUtensorMap tS,
@@ -347,8 +348,10 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                                                 const float *__restrict__ u0, const float *__restrict__ LamEnd,
                                                 float *__restrict__ Lam, float *__restrict__ P, float *__restrict__ Q,
                                                 int32_t *__restrict__ D, int64_t N, int64_t C, float beta, float theta,
-                                                float u_r, float alpha, bool detach, float gamma, int *status)
+                                                float u_r, float alpha, bool detach, float gamma, float delta,
+                                                double *__restrict__ PGout, int *status)
 {
+    static_assert(!PG || (FROM_V && AFF && MODE == kReplay && !TRACK), "parameter sums: affine V path only");
     using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
     constexpr int NB = 32 * NPL;
     constexpr int NT = Ly::NT;
@@ -405,6 +408,26 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
     }
     bool ok = true;
     const float k2 = alpha * kLog2e, k2t = k2 * theta, bgamma = beta * gamma;
+    // PG: fp64 sums of dL/dbeta = sum_t lam_{t+1} u_t (+ lam_0 u0),
+    // dL/dgamma = sum_t s_t v_t beta lam_{t+1}, dL/ddelta = sum_t s_t beta lam_{t+1},
+    // taken at row t before lam is stepped (lam then holds lam_{t+1})
+    double pb[NPL], pgm[NPL], pdl[NPL];
+#pragma unroll
+    for (int i = 0; i < NPL; i++) { pb[i] = 0.0; pgm[i] = 0.0; pdl[i] = 0.0; }
+    auto pg_row = [&](const Vec<NPL> &v) {
+#pragma unroll
+        for (int i = 0; i < NPL; i++) {
+            const bool spk = v.v[i] >= theta;
+            const float u = spk ? __fadd_rn(__fmul_rn(gamma, v.v[i]), delta) : v.v[i];
+            const double ln = (double)lam.v[i];
+            pb[i] = fma(ln, (double)u, pb[i]);
+            if (spk) {
+                const double bl = (double)beta * ln;
+                pdl[i] += bl;
+                pgm[i] = fma((double)v.v[i], bl, pgm[i]);
+            }
+        }
+    };
 
     for (int64_t k = 0; k < ntiles; k++) {
         const int s = (int)(k % S);
@@ -426,6 +449,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             const Vec<NPL> pp_in = pp;
 #pragma unroll
             for (int rr = R - 1; rr >= 0; rr--) {
+                if constexpr (PG) pg_row(ld_vec<NPL>(b + Ly::kI * kTile + rr * NB + NPL * lane));
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
                     lam.v[i] = cv[rr].v[i] + av[rr].v[i] * lam.v[i];
@@ -460,6 +484,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             for (int rr = R - 1; rr >= 0; rr--) {
                 const int64_t t = rbase + rr;
                 if (t < cstart) break;
+                if constexpr (PG) pg_row(ld_vec<NPL>(b + Ly::kI * kTile + rr * NB + NPL * lane));
                 bwd_step<NPL, READ_S, HAS_GU, TRACK, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane,
                                                             (!FROM_V && t == 0) ? &uz : nullptr, lam, pp, beta,
                                                             theta, u_r, alpha, k2, k2t, detach, bgamma);
@@ -482,6 +507,19 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
         if (D) {
 #pragma unroll
             for (int i = 0; i < NPL; i++) D[m * N + nl + i] = dn[i];
+        }
+    }
+    if constexpr (PG) {
+        // one chunk holding row 0: lam is lam_0 and u_{-1} = u0
+        if (ok && act) {
+            const Vec<NPL> z = ld_vec<NPL>(u0 + nl);
+#pragma unroll
+            for (int i = 0; i < NPL; i++) {
+                pb[i] = fma((double)lam.v[i], (double)z.v[i], pb[i]);
+                PGout[nl + i] = pb[i];
+                PGout[N + nl + i] = pgm[i];
+                PGout[2 * N + nl + i] = pdl[i];
+            }
         }
     }
     if (MODE == kReplay && lane == 0) bulk_wait_all();
@@ -606,21 +644,23 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
     return true;
 }
 
-template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V = false, bool AFF = false>
+template <int NPL, bool READ_S, bool HAS_GU, int MODE, bool TRACK, bool FROM_V = false, bool AFF = false,
+          bool PG = false>
 static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *LamEnd, float *Lam, float *P, float *Q,
                        int32_t *D, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r, float alpha,
-                       bool detach, int *status, cudaStream_t s, float gamma = 0.0f)
+                       bool detach, int *status, cudaStream_t s, float gamma = 0.0f, float delta = 0.0f,
+                       double *PGout = nullptr)
 {
     constexpr int NB = 32 * NPL;
     constexpr int NT = BwdLayout<READ_S, HAS_GU, FROM_V>::NT;
     constexpr int R = BwdTile<NPL>::R, ST = BwdTile<NPL>::S;
     const size_t smem = ((size_t)ST * NT + (MODE == kReplay ? 2 : 0)) * R * NB * 4;
-    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V, AFF>;
+    auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V, AFF, PG>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
     count_launches(1);
     kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], u0, LamEnd, Lam, P, Q, D, N, C,
-                             beta, theta, u_r, alpha, detach, gamma, status);
+                             beta, theta, u_r, alpha, detach, gamma, delta, PGout, status);
 }
 
 template <int NPL, int MODE, bool TRACK>
@@ -694,6 +734,34 @@ bool bwd_tma_aff(const float *IV, const float *u0, const float *U, const float *
         if (npl == 4) launch_bwd<4, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s, gamma);
         else launch_bwd<1, false, false, kReplay, false, false, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr, N, 1, T, beta, theta, 0.f, alpha, true, status, s, gamma);
     }
+    return true;
+}
+
+// Affine-reset adjoint from V over one chunk of T rows with the parameter
+// sums fused in: PGout[3][N] (fp64) receives per neuron (dbeta, dgamma,
+// ddelta); u0 [N] supplies the u_{-1} of the dbeta sum.
+bool bwd_tma_aff_pg(const float *V, const float *u0, const float *GS, float *Lam, double *PGout, int64_t T, int64_t N,
+                    float beta, float theta, float alpha, float gamma, float delta, cudaStream_t s)
+{
+    const void *p[] = {V, u0, GS, Lam};
+    if (!tma_ok(p, 4, N) || T <= 0 || (uintptr_t)PGout % 8) return false;
+    const int npl = pick_npl(N, 1, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
+    const int nb = 32 * npl;
+    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    CUtensorMap maps[6];
+    if (!make_tmap_2d(&maps[0], V, N, T, nb, R) || !make_tmap_2d(&maps[3], GS, N, T, nb, R) ||
+        !make_tmap_2d(&maps[5], Lam, N, T, nb, R))
+        return false;
+    maps[1] = maps[2] = maps[4] = maps[0];
+    int *status = device_status_ptr();
+    if (npl == 4)
+        launch_bwd<4, false, false, kReplay, false, true, true, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr,
+                                                                      N, 1, T, beta, theta, 0.f, alpha, true, status, s,
+                                                                      gamma, delta, PGout);
+    else
+        launch_bwd<1, false, false, kReplay, false, true, true, true>(maps, u0, nullptr, Lam, nullptr, nullptr, nullptr,
+                                                                      N, 1, T, beta, theta, 0.f, alpha, true, status, s,
+                                                                      gamma, delta, PGout);
     return true;
 }
 

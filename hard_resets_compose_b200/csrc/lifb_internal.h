@@ -83,6 +83,10 @@ bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, 
 // 0) or from V (from_v); false when the TMA path does not apply.
 bool bwd_tma_aff(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T, int64_t N,
                  float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s);
+// The same from V with the parameter sums fused in: PGout [3][N] fp64 =
+// (dbeta, dgamma, ddelta) per neuron, u0 for the u_{-1} term of dbeta.
+bool bwd_tma_aff_pg(const float *V, const float *u0, const float *GS, float *Lam, double *PGout, int64_t T, int64_t N,
+                    float beta, float theta, float alpha, float gamma, float delta, cudaStream_t s);
 
 // serial.cu
 void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
@@ -97,11 +101,13 @@ void serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T
 void serial_bwd_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta, float theta,
                   float alpha, cudaStream_t s);
 // Affine-reset (u' = gamma*v + delta) serial forward (U, or V when vout) and
-// adjoint (from U and I, or from V).
+// adjoint (from U and I, or from V); PGout (optional, [3][N] fp64, needs u0):
+// the per-neuron parameter sums (dbeta, dgamma, ddelta) of the same sweep.
 void serial_fwd_aff(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                     float theta, float gamma, float delta, bool vout, cudaStream_t s);
 void serial_bwd_aff(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
-                    int64_t N, float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s);
+                    int64_t N, float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s,
+                    float delta = 0.0f, double *PGout = nullptr);
 
 // aff.cu: the exact speculative forward of the affine reset over segments of
 // L rows with W-row lead-ins (serial pass when T == L, W == 0 or the TMA path

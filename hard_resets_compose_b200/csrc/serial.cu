@@ -148,19 +148,24 @@ void serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, 
 // Affine-reset adjoint (detached reset), one thread per neuron: lam_t =
 // gs_t sigma'(v_t) + a_t lam_{t+1}, a_t = beta*gamma at a spike and beta
 // elsewhere, with v_t from V (from_v) or from U[t-1] and I[t] (u0 for row 0).
+// PGout (optional, [3][N] fp64): the parameter sums (dbeta, dgamma, ddelta) =
+// (sum lam_{t+1} u_t + lam_0 u0, sum s_t v_t beta lam_{t+1}, sum s_t beta lam_{t+1})
+// with u_t = s_t ? fl(fl(gamma v_t) + delta) : v_t; then u0 must be given.
 template <int D>
 __global__ void __launch_bounds__(kSerBlock) k_serial_bwd_aff(const float *__restrict__ IV,
                                                               const float *__restrict__ u0,
                                                               const float *__restrict__ U,
                                                               const float *__restrict__ GS, float *__restrict__ Lam,
                                                               int64_t T, int64_t N, float beta, float theta,
-                                                              float alpha, float gamma, bool from_v)
+                                                              float alpha, float gamma, bool from_v, float delta,
+                                                              double *__restrict__ PGout)
 {
     int64_t n = (int64_t)blockIdx.x * kSerBlock + threadIdx.x;
     if (n >= N) return;
     float lam = 0.0f;
     const float un0 = from_v ? 0.0f : u0[n];
     const float bg = beta * gamma;
+    double pb = 0.0, pgm = 0.0, pdl = 0.0;
     for (int64_t tend = T; tend > 0; tend -= D) {
         int64_t t0 = tend - D > 0 ? tend - D : 0;
         int cnt = (int)(tend - t0);
@@ -178,10 +183,26 @@ __global__ void __launch_bounds__(kSerBlock) k_serial_bwd_aff(const float *__res
         for (int dd = D - 1; dd >= 0; dd--) {
             if (dd < cnt) {
                 const float sig = __frcp_rn(1.0f + __expf(-alpha * (v[dd] - theta)));
-                lam = gs[dd] * (alpha * sig * (1.0f - sig)) + (v[dd] >= theta ? bg : beta) * lam;
+                const bool spk = v[dd] >= theta;
+                if (PGout) {  // lam is lam_{t+1} here
+                    const float u = spk ? __fadd_rn(__fmul_rn(gamma, v[dd]), delta) : v[dd];
+                    pb = fma((double)lam, (double)u, pb);
+                    if (spk) {
+                        const double bl = (double)beta * (double)lam;
+                        pdl += bl;
+                        pgm = fma((double)v[dd], bl, pgm);
+                    }
+                }
+                lam = gs[dd] * (alpha * sig * (1.0f - sig)) + (spk ? bg : beta) * lam;
                 Lam[(t0 + dd) * N + n] = lam;
             }
         }
+    }
+    if (PGout) {
+        pb = fma((double)lam, (double)u0[n], pb);
+        PGout[n] = pb;
+        PGout[N + n] = pgm;
+        PGout[2 * N + n] = pdl;
     }
 }
 
@@ -200,12 +221,18 @@ void serial_fwd_aff(const float *I, const float *u0, float *U, float *S, int64_t
 }
 
 void serial_bwd_aff(const float *IV, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
-                    int64_t N, float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s)
+                    int64_t N, float beta, float theta, float alpha, float gamma, bool from_v, cudaStream_t s,
+                    float delta, double *PGout)
 {
-    if (bwd_tma_aff(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, gamma, from_v, s)) return;
+    if (PGout && from_v) {
+        if (bwd_tma_aff_pg(IV, u0, GS, Lam, PGout, T, N, beta, theta, alpha, gamma, delta, s)) return;
+    } else if (!PGout && bwd_tma_aff(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, gamma, from_v, s)) {
+        return;
+    }
     unsigned g = (unsigned)((N + kSerBlock - 1) / kSerBlock);
     count_launches(1);
-    k_serial_bwd_aff<8><<<g, kSerBlock, 0, s>>>(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, gamma, from_v);
+    k_serial_bwd_aff<8><<<g, kSerBlock, 0, s>>>(IV, u0, U, GS, Lam, T, N, beta, theta, alpha, gamma, from_v, delta,
+                                                PGout);
 }
 
 void serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N, float beta,

@@ -44,7 +44,7 @@ class LIFParamFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, I, u0, beta, theta, u_r, alpha, fwd_mode, bwd_mode, K):
-        b, th, ur = float(beta), float(theta), float(u_r)
+        b, th, ur = L._host_scalars(beta, theta, u_r)
         I = I.contiguous()
         if fwd_mode == "scan":
             U, S = L.scan_forward_auto(I, b, th, ur, u0, K=K)
@@ -90,7 +90,7 @@ class LIFSoftFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, I, u0, beta, theta, alpha):
-        b, th = float(beta), float(theta)
+        b, th = L._host_scalars(beta, theta)
         I = I.contiguous()
         U, S = L.soft_serial_forward(I, b, th, u0)
         ctx.save_for_backward(I, u0, U)
@@ -118,7 +118,7 @@ class LIFSoftScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, I, u0, beta, theta, alpha, mode, C, K):
         from . import soft as TS
-        b, th = float(beta), float(theta)
+        b, th = L._host_scalars(beta, theta)
         I = I.contiguous()
         if mode == "scan":
             U, S = TS.soft_scan_forward(I, b, th, u0, C=C, K=K)

@@ -77,6 +77,14 @@ def _prep_bwd(I, u0, U, S, GS, GU):
     return I, u0, U, S, GS, GU, T, N
 
 
+def _host_scalars(*xs):
+    """The kernels take neuron parameters by value: read every tensor among xs
+    to the host in one copy (one device sync instead of one per parameter)."""
+    ts = [x for x in xs if torch.is_tensor(x)]
+    vals = iter(torch.stack([t.detach().reshape(()).to(torch.float32) for t in ts]).tolist() if ts else [])
+    return tuple(next(vals) if torch.is_tensor(x) else float(x) for x in xs)
+
+
 def _f(x):
     return float(x)
 

@@ -303,6 +303,19 @@ int lifb_aff_param_grad_partials(const float *I, const float *u0, const float *U
                                  float beta, float theta, float alpha, int M, void *stream);
 int lifb_reverse_linear_scan(const float *A, const float *B, float *Out, int64_t T, int64_t N,
                              void *stream);
+/* The affine layer's single-pass path (the layer saves V instead of U):
+ *   lifb_aff_serial_fwd_v  the serial forward writing V[t] = v_t (the
+ *                          potential before the reset) in place of U
+ *   lifb_aff_adjoint_v     lifb_aff_adjoint from V (s_t = [v_t >= theta],
+ *                          u_t = s_t ? gamma v_t + delta : v_t bit for bit);
+ *                          param_sums (optional, [3][N] double, needs u0)
+ *                          receives per neuron (dbeta, dgamma, ddelta) of
+ *                          the same sweep, dbeta including lam_0 * u0 */
+int lifb_aff_serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N,
+                          float beta, float theta, float gamma, float delta, void *stream);
+int lifb_aff_adjoint_v(const float *V, const float *u0, const float *GS, float *Lam, double *param_sums,
+                       int64_t T, int64_t N, float beta, float theta, float alpha, float gamma,
+                       float delta, void *stream);
 
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:

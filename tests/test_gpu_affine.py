@@ -167,3 +167,25 @@ def test_affine_argument_errors(cuda):
         A.aff_scan_forward(I, 0.9, 1.0, 0.5, 0.0, u0, C=100)
     U, S = A.aff_scan_forward(I[:0], 0.9, 1.0, 0.5, 0.0, u0)
     assert U.shape == (0, 8) and S.shape == (0, 8)
+
+
+@pytest.mark.parametrize("T,N", ((1024, 16384), (3000, 333), (16384, 8)))
+def test_affine_vpath(cuda, T, N):
+    """The layer's single-pass path: V (the potentials before the reset) bit for
+    bit, and the adjoint from V with the beta, gamma, delta sums fused into the
+    same sweep (TMA kernel for N % 4 == 0, plain kernel otherwise)."""
+    from hard_resets_compose_b200 import affine as A
+    beta, theta, gamma, delta, alpha = 0.97, 1.0, 0.6, -0.25, 4.0
+    I, u0, GS = gen(T, N, 0.08, 0.35, seed=13, u0_sd=0.2, grad=True)
+    Us, Ss, Vs = O.aff_serial_forward(I, beta, theta, gamma, delta, u0, want_v=True)
+    lam, pg = O.aff_serial_backward(I, u0, Us, GS, beta, theta, gamma, alpha)
+    Id, u0d, GSd = to_dev(cuda, I, u0, GS)
+    V, S = A.aff_serial_forward_v(Id, beta, theta, gamma, delta, u0d)
+    assert_bit_equal(_np(V), Vs, "V")
+    assert_bit_equal(_np(S), Ss, "S")
+    Lam, got = A.aff_adjoint_v(V, u0d, GSd, beta, theta, gamma, delta, alpha)
+    assert rel(_np(Lam), lam) < TOL
+    for i in range(3):
+        assert _param_close(float(got[i]), pg[i]), (i, float(got[i]), pg[i])
+    Lam2, none = A.aff_adjoint_v(V, u0d, GSd, beta, theta, gamma, delta, alpha, param_grads=False)
+    assert none is None and torch.equal(Lam2, Lam)
