@@ -64,11 +64,12 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5", "soft", "affine"),
+    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5", "soft", "affine", "alif"),
                    help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step; "
                         "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs; c5: sweep of B*N, T, beta; "
                         "soft: the soft-reset fitting layer (lif_soft) at config 2's shape and a long soft scan; "
-                        "affine: the affine-reset layer (lif_affine) at config 2's shape and a long affine scan")
+                        "affine: the affine-reset layer (lif_affine) at config 2's shape and a long affine scan; "
+                        "alif: the ALIF layer (alif) at config 2's shape and a long ALIF scan")
     p.add_argument("--c5-n", default="14,15,16,17,18,19,20,21,22",
                    help="c5: log2 of the total B*N values (split over the GPUs)")
     p.add_argument("--c5-t", default="256,1024,4096", help="c5: sequence lengths")
@@ -348,15 +349,19 @@ def run_sweep(args, ws, rank, local):
 # affine workload: the reset u <- gamma*v + delta at one of the reference's
 # test points (lifscan tests/test_affine.py:7)
 AFF_GAMMA, AFF_DELTA = 0.3, -0.1
+# alif workload: the "lsnn" neuron class of lifscan tests/test_alif.py:10
+ALIF_RHO, ALIF_Q = 0.995, 0.9
 
 
 def run_reset_family(args, ws, rank, local, family):
     """The soft-reset model (family "soft": subtractive reset; lifscan/fit.py:
-    93-121 lif_soft, lifscan/triton_soft.py soft_scan_forward) or the
+    93-121 lif_soft, lifscan/triton_soft.py soft_scan_forward), the
     affine-reset model (family "affine": u <- gamma*v + delta, gamma = 0.3,
-    delta = -0.1; lifscan/triton_affine.py lif_affine, aff_scan_forward): the
-    fitting layer's forward + backward (spikes out; gradients for I, u0 and
-    beta, and for gamma and delta) at config 2's shape (B*N = 16384 per GPU,
+    delta = -0.1; lifscan/triton_affine.py lif_affine, aff_scan_forward) or the
+    ALIF model (family "alif": rho = 0.995, q = 0.9; lifscan/triton_alif.py
+    alif, alif_scan_forward): the layer's forward + backward (spikes out;
+    gradients for I, u0 and beta, and for gamma and delta, or for w0, rho, q
+    and theta0) at config 2's shape (B*N = 16384 per GPU,
     T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99), issued eagerly; and the exact
     scan forward at T = 2^18, N = 1024 (x ~ N(0.02, 0.1^2)) beside the serial
     pass it replaces."""
@@ -364,6 +369,7 @@ def run_reset_family(args, ws, rank, local, family):
 
     from hard_resets_compose_b200 import _lib
     from hard_resets_compose_b200 import affine as A
+    from hard_resets_compose_b200 import alif as AL
     from hard_resets_compose_b200 import fit
     from hard_resets_compose_b200 import lifscan as L
     from hard_resets_compose_b200 import soft as TS
@@ -380,6 +386,10 @@ def run_reset_family(args, ws, rank, local, family):
     b = torch.tensor(BETA, device=dev, requires_grad=True)
     gm = torch.tensor(AFF_GAMMA, device=dev, requires_grad=True)
     dl = torch.tensor(AFF_DELTA, device=dev, requires_grad=True)
+    rh = torch.tensor(ALIF_RHO, device=dev, requires_grad=True)
+    qq = torch.tensor(ALIF_Q, device=dev, requires_grad=True)
+    th = torch.tensor(1.0, device=dev, requires_grad=True)
+    w0 = torch.zeros(N, device=dev)
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
     evict = torch.ones(L2_FLUSH_BYTES // 4, device=dev)
@@ -388,9 +398,11 @@ def run_reset_family(args, ws, rank, local, family):
 
     def step():
         Iq.grad = None
-        b.grad = gm.grad = dl.grad = None
+        b.grad = gm.grad = dl.grad = rh.grad = qq.grad = th.grad = None
         if soft:
             S = fit.lif_soft(Iq, u0, b, 1.0, 4.0)
+        elif family == "alif":
+            S, _, _ = AL.alif(Iq, u0, w0, b, rh, qq, th, fwd="serial", bwd="serial")
         else:
             S = A.lif_affine(Iq, u0, b, gm, dl, theta=1.0, alpha=4.0, mode="serial")
         torch.autograd.backward(S, GS)
@@ -425,6 +437,14 @@ def run_reset_family(args, ws, rank, local, family):
         bwd = lambda: L.soft_serial_backward(I, u0, U, GS, BETA, 1.0, 4.0)  # noqa: E731
         serial_long = lambda x, z: L.soft_serial_forward(x, BETA, 1.0, z)  # noqa: E731
         scan_long = lambda x, z: TS.soft_scan_forward(x, BETA, 1.0, z)  # noqa: E731
+    elif family == "alif":
+        fwd = lambda: AL.alif_serial_forward(I, BETA, ALIF_RHO, ALIF_Q, 1.0, 0.0, u0, w0)  # noqa: E731
+        U, W, S = fwd()
+        bwd = lambda: AL._alif_bwd(I, u0, w0, U, W, None, GS, BETA, ALIF_RHO, ALIF_Q, 1.0, 4.0,  # noqa: E731
+                                   False, True)
+        serial_long = lambda x, z: AL.alif_serial_forward(x, BETA, ALIF_RHO, ALIF_Q, 1.0, 0.0, z, z)  # noqa: E731
+        scan_long = lambda x, z: AL.alif_scan_forward(x, BETA, ALIF_RHO, ALIF_Q, 1.0, 0.0, z, z, None,  # noqa: E731
+                                                      0.1, C=128)
     else:
         # the layer's single-pass path: forward writes V and S, the adjoint
         # reads V and gS and sums the parameter gradients in the same sweep
@@ -439,8 +459,10 @@ def run_reset_family(args, ws, rank, local, family):
     # soft layer: forward 12 B, adjoint 16 B (I, U[t-1], GS in; Lam out),
     # dbeta pass 16 B (I, U[t-1], GS, Lam in).  Affine layer: forward 12 B
     # (I in; V, S out), adjoint with the parameter sums 12 B (V, GS in; Lam out)
-    fwd_bytes, bwd_bytes = (12, 16) if soft else (12, 12)
-    layer_bytes = 12 + 16 + 16 if soft else 12 + 12
+    # ALIF layer: forward 16 B (I in; U, W, S out), adjoint with the
+    # parameter sums 20 B (I, U[t-1], W[t-1], GS in; LV out)
+    fwd_bytes, bwd_bytes = {"soft": (12, 16), "affine": (12, 12), "alif": (16, 20)}[family]
+    layer_bytes = 12 + 16 + 16 if soft else fwd_bytes + bwd_bytes
     Tl, Nl = 1 << 18, 1024
     gl = torch.Generator(device=dev).manual_seed(7100 + rank)
     Il = torch.empty(Tl, Nl, device=dev).normal_(0.02, 0.1, generator=gl)
@@ -451,6 +473,10 @@ def run_reset_family(args, ws, rank, local, family):
     if soft:
         metric = "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)"
         workload = "soft: lif_soft (gradients for I, u0, beta), beta=0.99, x~N(0.05,0.2^2)"
+    elif family == "alif":
+        metric = "neuron-steps/s, ALIF layer alif fwd+bwd (B*N=16384/GPU, T=1024)"
+        workload = (f"alif: alif fwd=serial (gradients for I, u0, w0, beta, rho, q, theta0), beta=0.99, "
+                    f"rho={ALIF_RHO}, q={ALIF_Q}, theta0=1, x~N(0.05,0.2^2)")
     else:
         metric = "neuron-steps/s, affine-reset layer lif_affine fwd+bwd (B*N=16384/GPU, T=1024)"
         workload = (f"affine: lif_affine mode=serial (gradients for I, u0, beta, gamma, delta), beta=0.99, "
@@ -750,7 +776,7 @@ def main():
     if args.workload == "c5":
         run_sweep(args, ws, rank, local)
         return
-    if args.workload in ("soft", "affine"):
+    if args.workload in ("soft", "affine", "alif"):
         run_reset_family(args, ws, rank, local, args.workload)
         return
 

@@ -85,6 +85,18 @@ SIGNATURES = {
                                c_float, c_void_p], c_int),
     "lifb_aff_adjoint_v": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float,
                             c_float, c_float, c_float, c_void_p], c_int),
+    "lifb_alif_serial_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float,
+                              c_float, c_float, c_float, c_float, c_void_p], c_int),
+    "lifb_alif_scan_fwd_workspace_bytes": ([c_i64, c_i64, c_i64], c_size_t),
+    "lifb_alif_scan_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float,
+                            c_float, c_float, c_float, c_float, c_i64, c_i64, c_void_p, c_i64, c_void_p, c_size_t,
+                            c_void_p], c_int),
+    "lifb_alif_warm_predict": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64,
+                                c_i64, c_float, c_float, c_float, c_float, c_float, c_float, c_float, c_void_p],
+                               c_int),
+    "lifb_alif_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                       c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float, c_float, c_float, c_void_p],
+                      c_int),
     "lifb_tshard_workspace_bytes": ([c_i64, c_i64, c_int, c_int, c_int, c_int], c_size_t),
     "lifb_tshard_envelope": ([c_void_p, c_i64, c_i64, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p], c_int),

@@ -33,36 +33,9 @@
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
 #include "tma.cuh"
+#include "vec.cuh"
 
 namespace lifb {
-
-template <int NPL>
-struct Vec {
-    float v[NPL];
-};
-
-template <int NPL>
-__device__ __forceinline__ Vec<NPL> ld_vec(const float *p)
-{
-    Vec<NPL> r;
-    if constexpr (NPL == 4) {
-        float4 t = *reinterpret_cast<const float4 *>(p);
-        r.v[0] = t.x; r.v[1] = t.y; r.v[2] = t.z; r.v[3] = t.w;
-    } else {
-        r.v[0] = *p;
-    }
-    return r;
-}
-
-template <int NPL>
-__device__ __forceinline__ void st_vec(float *p, const Vec<NPL> &a)
-{
-    if constexpr (NPL == 4) {
-        *reinterpret_cast<float4 *>(p) = make_float4(a.v[0], a.v[1], a.v[2], a.v[3]);
-    } else {
-        *p = a.v[0];
-    }
-}
 
 // ===================================================================== forward
 // Chunk m starts from Starts[m * start_stride] (rows of N) or u0.  With
@@ -408,24 +381,32 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
     }
     bool ok = true;
     const float k2 = alpha * kLog2e, k2t = k2 * theta, bgamma = beta * gamma;
-    // PG: fp64 sums of dL/dbeta = sum_t lam_{t+1} u_t (+ lam_0 u0),
-    // dL/dgamma = sum_t s_t v_t beta lam_{t+1}, dL/ddelta = sum_t s_t beta lam_{t+1},
-    // taken at row t before lam is stepped (lam then holds lam_{t+1})
+    // PG: sums of dL/dbeta = sum_t lam_{t+1} u_t (+ lam_0 u0), dL/dgamma =
+    // sum_t s_t v_t beta lam_{t+1}, dL/ddelta = sum_t s_t beta lam_{t+1}, taken
+    // at row t before lam is stepped (lam then holds lam_{t+1}); each tile's
+    // rows are summed in fp32 (tb, tg, td) and folded into fp64 totals
     double pb[NPL], pgm[NPL], pdl[NPL];
+    float tb[NPL], tg[NPL], td[NPL];
 #pragma unroll
-    for (int i = 0; i < NPL; i++) { pb[i] = 0.0; pgm[i] = 0.0; pdl[i] = 0.0; }
+    for (int i = 0; i < NPL; i++) { pb[i] = 0.0; pgm[i] = 0.0; pdl[i] = 0.0; tb[i] = tg[i] = td[i] = 0.0f; }
     auto pg_row = [&](const Vec<NPL> &v) {
 #pragma unroll
         for (int i = 0; i < NPL; i++) {
             const bool spk = v.v[i] >= theta;
             const float u = spk ? __fadd_rn(__fmul_rn(gamma, v.v[i]), delta) : v.v[i];
-            const double ln = (double)lam.v[i];
-            pb[i] = fma(ln, (double)u, pb[i]);
-            if (spk) {
-                const double bl = (double)beta * ln;
-                pdl[i] += bl;
-                pgm[i] = fma((double)v.v[i], bl, pgm[i]);
-            }
+            tb[i] = fmaf(lam.v[i], u, tb[i]);
+            const float bl = spk ? beta * lam.v[i] : 0.0f;
+            td[i] += bl;
+            tg[i] = fmaf(v.v[i], bl, tg[i]);
+        }
+    };
+    auto pg_fold = [&]() {
+#pragma unroll
+        for (int i = 0; i < NPL; i++) {
+            pb[i] += (double)tb[i];
+            pgm[i] += (double)tg[i];
+            pdl[i] += (double)td[i];
+            tb[i] = tg[i] = td[i] = 0.0f;
         }
     };
 
@@ -457,6 +438,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                 }
                 if (MODE == kReplay) st_vec<NPL>(ol + rr * NB + NPL * lane, lam);
             }
+            if constexpr (PG) pg_fold();
             if (TRACK && D) {
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
@@ -494,6 +476,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                 }
                 if (MODE == kReplay && act) st_vec<NPL>(Lam + t * N + nl, lam);
             }
+            if constexpr (PG) pg_fold();
         }
         __syncwarp();
         if (lane == 0 && k + S < ntiles) issue(s, k + S);
@@ -574,7 +557,7 @@ struct BwdTile {
     static constexpr int S = NPL == 4 ? LIFB_BWD4_S : LIFB_BWD1_S;
 };
 
-static bool tma_ok(const void *const *ptrs, int n, int64_t N)
+bool tma_ok(const void *const *ptrs, int n, int64_t N)
 {
     if (N % 4) return false;
     for (int i = 0; i < n; i++)
@@ -584,7 +567,7 @@ static bool tma_ok(const void *const *ptrs, int n, int64_t N)
 
 // float4 lanes when there are enough 128-neuron CTAs per SM; otherwise one
 // neuron per lane (4x more warps for narrow problems).
-static int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
+int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
 {
     if (LIFB_FORCE_NPL == 1 || LIFB_FORCE_NPL == 4) return LIFB_FORCE_NPL;
     int dev = 0, sms = 148;

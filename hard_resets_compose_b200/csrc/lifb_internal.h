@@ -50,6 +50,13 @@ bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N,
 int *device_status_ptr();                 // status word of the current device
 int read_device_status(bool reset);       // synchronous read (current device)
 
+// chunk_tma.cu: true when N % 4 == 0 and every non-null pointer is 16-byte
+// aligned (the TMA kernels' requirement).
+bool tma_ok(const void *const *ptrs, int n, int64_t N);
+// 4 neurons per lane when there are at least min_ctas_per_sm 128-neuron CTAs
+// (times M chunks) per SM, else 1.
+int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm);
+
 // chunk_tma.cu: TMA-pipelined chunk kernels; false when the TMA path does not
 // apply (N % 4 != 0, a misaligned tensor, more than 65535 chunks).
 // Forward replay of M = T/C chunks from Starts (NULL: one chunk from u0).

@@ -317,6 +317,48 @@ int lifb_aff_adjoint_v(const float *V, const float *u0, const float *GS, float *
                        int64_t T, int64_t N, float beta, float theta, float alpha, float gamma,
                        float delta, void *stream);
 
+/* ---- Adaptive-threshold LIF (ALIF) ------------------------------------------
+ * lifscan/triton_alif.py: state (u, w);
+ *   v = fl(fl(beta*u) + x); s = v >= fl(theta0 + w);
+ *   u' = s ? u_r : v;       w' = s ? fl(fl(rho*w) + q) : fl(rho*w).
+ * U, W, S are [T][N] (the state after each row); u0, w0 are [N].
+ *   lifb_alif_serial_fwd   alif_serial_forward (triton_alif.py:263-273), one pass
+ *   lifb_alif_scan_fwd     alif_scan_forward (:301-363), exact: T/L segments,
+ *                          each started from a Wlead-row lead-in from (u_r, w
+ *                          guess) with the guess Wpred[row / Cpred] ([T/Cpred][N],
+ *                          optional: 0 without), replayed at once, then a fix-up
+ *                          until every segment's (u, w, s) rows match the serial
+ *                          recurrence (workspace: lifb_alif_scan_fwd_workspace_bytes)
+ *   lifb_alif_warm_predict alif_warm_predict (:74-92, 276-285): WP[m] ([T/C][N])
+ *                          = w after the Wn chunks of C rows before chunk m, run
+ *                          from (u_init, w_init), or from (UI, WI)[m - Wn] when
+ *                          given, or from (u0, w0) when they reach row 0
+ *   lifb_alif_bwd          the detached-reset adjoint (:359-364, 443-487) in one
+ *                          reverse sweep: LV[t] = dL/dv_t, LW[t] = dL/dw_t
+ *                          (optional), with d_t = GS_t + q lw_t, lv_t = (1 - s_t)
+ *                          beta lv_{t+1} + sg_t d_t, lw_{t-1} = rho lw_t - sg_t d_t,
+ *                          sg_t = alpha sig (1 - sig) at v_t - theta0 - w_{t-1};
+ *                          S optional (NULL: recomputed from U, W, I bit for bit);
+ *                          lw_m1 [N] (optional) = dL/dw0; param_sums [4][N] double
+ *                          (optional) = per-neuron (dbeta, drho, dq, dtheta0) of
+ *                          ALIFFn.backward (:542-554) */
+int lifb_alif_serial_fwd(const float *I, const float *u0, const float *w0, float *U, float *W, float *S,
+                         int64_t T, int64_t N, float beta, float rho, float q, float theta0, float u_r,
+                         void *stream);
+size_t lifb_alif_scan_fwd_workspace_bytes(int64_t T, int64_t N, int64_t L);
+int lifb_alif_scan_fwd(const float *I, const float *u0, const float *w0, float *U, float *W, float *S,
+                       int64_t T, int64_t N, float beta, float rho, float q, float theta0, float u_r,
+                       int64_t L, int64_t Wlead, const float *Wpred, int64_t Cpred, void *workspace,
+                       size_t workspace_bytes, void *stream);
+int lifb_alif_warm_predict(const float *I, const float *u0, const float *w0, float *WP, const float *UI,
+                           const float *WI, int64_t T, int64_t N, int64_t C, int64_t Wn, float u_init,
+                           float w_init, float beta, float rho, float q, float theta0, float u_r,
+                           void *stream);
+int lifb_alif_bwd(const float *I, const float *u0, const float *w0, const float *U, const float *W,
+                  const float *S, const float *GS, float *LV, float *LW, float *lw_m1, double *param_sums,
+                  int64_t T, int64_t N, float beta, float rho, float q, float theta0, float alpha,
+                  void *stream);
+
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:
  * 944-983, scan_forward_v4; :512-526, scan_backward_tiled).  These phases

@@ -70,6 +70,10 @@ def lib():
         L.oracle_soft_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float]
         L.oracle_soft_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float,
                                              c_int]
+        L.oracle_alif_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float,
+                                             c_float, c_float, c_float]
+        L.oracle_alif_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f64p,
+                                             i64, i64, c_float, c_float, c_float, c_float, c_float, c_int]
         L.oracle_aff_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float,
                                             c_float]
         L.oracle_aff_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, f64p, i64, i64, c_float, c_float,
@@ -191,6 +195,55 @@ def aff_serial_backward(I, u0, U, GS, beta, theta, gamma, alpha=4.0, double=Fals
     pg = np.zeros(3, np.float64)
     lib().oracle_aff_serial_bwd(_p(I), _p(u0), _p(U), _p(GS), _p(Lam), pg.ctypes.data_as(f64p), T, N, beta, theta, alpha, gamma, int(double))
     return Lam, pg
+
+
+def alif_serial_forward(I, beta, rho, q, theta0, u_r, u0, w0):
+    """ALIF recurrence (lifscan/triton_alif.py:25-42, 263-273) -> (U, W, S)."""
+    I, u0, w0 = _f(I), _f(u0), _f(w0)
+    T, N = I.shape
+    U = np.empty_like(I)
+    W = np.empty_like(I)
+    S = np.empty_like(I)
+    lib().oracle_alif_serial_fwd(_p(I), _p(u0), _p(w0), _p(U), _p(W), _p(S), T, N, beta, rho, q, theta0, u_r)
+    return U, W, S
+
+
+def alif_serial_backward(I, u0, w0, U, W, S, GS, beta, rho, q, theta0, alpha=4.0, double=False):
+    """ALIF detached adjoint (lifscan/triton_alif.py:366-431, PASS 4) and the
+    ALIFFn parameter gradients (:542-554) -> (LV, LW, lw_m1, pg) with pg =
+    (dbeta, drho, dq, dtheta0); fp32 in the kernel's order, or in double."""
+    I, u0, w0, U, W, S, GS = map(_f, (I, u0, w0, U, W, S, GS))
+    T, N = I.shape
+    LV = np.empty_like(I)
+    LW = np.empty_like(I)
+    lwm1 = np.empty(N, np.float32)
+    pg = np.zeros(4, np.float64)
+    lib().oracle_alif_serial_bwd(_p(I), _p(u0), _p(w0), _p(U), _p(W), _p(S), _p(GS), _p(LV), _p(LW), _p(lwm1),
+                                 pg.ctypes.data_as(f64p), T, N, beta, rho, q, theta0, alpha, int(double))
+    return LV, LW, lwm1, pg
+
+
+def alif_warm_predict(I, beta, rho, q, theta0, u_r, u0, w0, C, Wn=4, u_init=0.0, w_init=0.0, UI=None, WI=None):
+    """lifscan/triton_alif.py:74-92: WP[m] = w after the Wn chunks before chunk
+    m, from (u_init, w_init) or (UI, WI)[m - Wn], or (u0, w0) from row 0."""
+    I, u0, w0 = _f(I), _f(u0), _f(w0)
+    T, N = I.shape
+    M = T // C
+    WP = np.empty((M, N), np.float32)
+    for m in range(M):
+        s0 = max(m - Wn, 0)
+        if s0 == 0:
+            u, w = u0, w0
+        elif UI is not None:
+            u, w = _f(UI)[s0], _f(WI)[s0]
+        else:
+            u = np.full(N, u_init, np.float32)
+            w = np.full(N, w_init, np.float32)
+        if m * C > s0 * C:
+            Us, Ws, _ = alif_serial_forward(I[s0 * C:m * C], beta, rho, q, theta0, u_r, u, w)
+            w = Ws[-1]
+        WP[m] = w
+    return WP
 
 
 def envelope(I, u0, C, beta, u_r, margin=1e-5):

@@ -22,7 +22,12 @@ It imports the reference's own code:
   * the affine-reset model: triton_affine.aff_serial_forward /
     aff_scan_forward (interpreted) and LIFAffineFn's gradients (PyTorch CPU)
     over the (gamma, delta) x beta grid of tests/test_affine.py ->
-    tests/golden/affine_grid.npz (`--affine-only`).
+    tests/golden/affine_grid.npz (`--affine-only`);
+  * the ALIF model: triton_alif.alif_serial_forward (plain and tiled),
+    alif_scan_forward with warm-up predictions, alif_warm_predict and
+    alif_backward (serial and scan; interpreted), and ALIFFn's gradients, over
+    the neuron classes of tests/test_alif.py -> tests/golden/alif_grid.npz
+    (`--alif-only`).
 
 Inputs are drawn on the CPU with torch.Generator (tests/test_fast.py:7-9) and
 stored in the fixture too.  The GPU box never runs this script; the tests read
@@ -194,8 +199,69 @@ def affine_cases():
     np.savez_compressed(os.path.join(HERE, "affine_grid.npz"), **npy(out))
 
 
+# ALIF: the neuron classes of tests/test_alif.py:10 (name, beta, rho, q) x free
+# membrane drive m (:11) at reduced size (T, N), chunks of C = 32 rows
+ALIF_CASES = (("lsnn", 0.95, 0.995, 0.9), ("glif2", 0.99, 0.96, 0.2), ("appD-a", 0.9, 0.95, 0.5))
+ALIF_M = (0.5, 2.0)
+ALIF_T, ALIF_N, ALIF_C = 512, 8, 32
+
+
+def alif_cases():
+    """The ALIF model (lifscan/triton_alif.py): serial forward (plain and
+    time-tiled), the exact box scan with warm-up predictions (repair to
+    convergence), alif_warm_predict, the serial and two-level scan adjoints
+    (Triton interpreter), and ALIFFn's gradients for I, u0, w0, beta, rho, q,
+    theta0 (its own backward, PyTorch CPU + interpreter)."""
+    import math
+    from lifscan import triton_alif as A
+    theta0, u_r, alpha = 1.0, 0.0, 4.0
+    out = {}
+    for ci, (name, beta, rho, q) in enumerate(ALIF_CASES):
+        for mi, mfree in enumerate(ALIF_M):
+            key = f"a{ci}m{mi}"
+            g = torch.Generator().manual_seed(40 + 2 * ci + mi)
+            I = ((1 - beta) * mfree + 0.5 * math.sqrt(1 - beta * beta)
+                 * torch.randn(ALIF_T, ALIF_N, generator=g)).contiguous()
+            u0 = torch.zeros(ALIF_N)
+            w0 = (0.1 * torch.rand(ALIF_N, generator=g)).contiguous()
+            GS = torch.randn(ALIF_T, ALIF_N, generator=g)
+            U, W, S = A.alif_serial_forward(I, beta, rho, q, theta0, u_r, u0, w0)
+            Ut, Wt, St = A.alif_serial_forward(I, beta, rho, q, theta0, u_r, u0, w0, D=8)
+            assert torch.equal(Ut, U) and torch.equal(Wt, W) and torch.equal(St, S), key
+            WP = A.alif_warm_predict(I, beta, rho, q, theta0, u_r, u0, w0, ALIF_C, Wn=4)
+            st = {}
+            U2, W2, S2 = A.alif_scan_forward(I, beta, rho, q, theta0, u_r, u0, w0, WP.contiguous(), 0.1 * q,
+                                             C=ALIF_C, K1=16, K2=32, repair=10 ** 6, stats=st)
+            assert torch.equal(U2, U) and torch.equal(W2, W) and torch.equal(S2, S), key
+            LV, LW = A.alif_backward(I, U, W, S, GS, beta, rho, q, theta0, u0, w0, alpha=alpha, mode="serial")
+            LVs, LWs = A.alif_backward(I, U, W, S, GS, beta, rho, q, theta0, u0, w0, alpha=alpha, mode="scan",
+                                       C=ALIF_C)
+            # the reference's two-level scan adjoint agrees with its serial sweep
+            assert ((LVs - LV).norm() / LV.norm()).item() < 1e-5, key
+            assert ((LWs - LW).norm() / LW.norm()).item() < 1e-5, key
+            Ig = I.clone().requires_grad_(True)
+            ug = u0.clone().requires_grad_(True)
+            wg = w0.clone().requires_grad_(True)
+            ps = [torch.tensor(v, dtype=torch.float32, requires_grad=True) for v in (beta, rho, q, theta0)]
+            Sg, _, _ = A.alif(Ig, ug, wg, ps[0], ps[1], ps[2], ps[3], u_r=u_r, alpha=alpha, fwd="serial",
+                              bwd="serial")
+            assert torch.equal(Sg.detach(), S), key
+            (GS * Sg).sum().backward()
+            out.update({f"{key}_I": I, f"{key}_u0": u0, f"{key}_w0": w0, f"{key}_GS": GS, f"{key}_U": U,
+                        f"{key}_W": W, f"{key}_S": S, f"{key}_WP": WP, f"{key}_LV": LV, f"{key}_LW": LW,
+                        f"{key}_dI": Ig.grad, f"{key}_du0": ug.grad,
+                        f"{key}_dw0": wg.grad, f"{key}_dp": torch.stack([p.grad for p in ps]),
+                        f"{key}_params": np.array([beta, rho, q, theta0, u_r, alpha], np.float64),
+                        f"{key}_stats": np.array([st["repair_iters"], st["miss_frac"], st["mean_pieces"]])})
+            print(key, name, mfree, st, "spikes", float(S.mean()), flush=True)
+    np.savez_compressed(os.path.join(HERE, "alif_grid.npz"), **npy(out))
+
+
 def main():
     theta = 1.0
+    if "--alif-only" in sys.argv:
+        alif_cases()
+        return
     if "--soft-only" in sys.argv:
         soft_cases()
         return
@@ -204,6 +270,7 @@ def main():
         return
     soft_cases()
     affine_cases()
+    alif_cases()
     for (name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, K) in FWD_CASES:
         I, u0, _ = gen(T, N, mu, sd, seed, u0_sd)
         us, ss, vs = fast.serial_forward_nograd(I, beta, theta, u_r, u0)

@@ -186,3 +186,35 @@ def test_oracle_affine_contains_hard_and_soft():
     Us, Ss = O.soft_serial_forward(I, 0.95, 1.0, u0)
     assert_bit_equal(Ua, Us, "U soft")
     assert_bit_equal(Sa, Ss, "S soft")
+
+
+ALIF = os.path.join(GOLD, "alif_grid.npz")
+ALIF_KEYS = [f"a{c}m{m}" for c in range(3) for m in range(2)]
+
+
+@pytest.mark.parametrize("key", ALIF_KEYS)
+def test_oracle_alif_matches_reference(key):
+    """ALIF over the neuron classes of the reference's tests/test_alif.py: the
+    oracle's recurrence equals the reference's serial forward (and its exact
+    box scan) bit for bit, its warm-up prediction equals alif_warm_predict,
+    its adjoint pair matches the reference's serial sweep (which the
+    generating script checked against its two-level scan), and its parameter
+    sums match ALIFFn's own backward."""
+    z = np.load(ALIF)
+    beta, rho, q, theta0, u_r, alpha = (float(v) for v in z[f"{key}_params"])
+    I, u0, w0, GS = (z[f"{key}_{k}"] for k in ("I", "u0", "w0", "GS"))
+    U, W, S = O.alif_serial_forward(I, beta, rho, q, theta0, u_r, u0, w0)
+    assert_bit_equal(U, z[f"{key}_U"], "U")
+    assert_bit_equal(W, z[f"{key}_W"], "W")
+    assert_bit_equal(S, z[f"{key}_S"], "S")
+    WP = O.alif_warm_predict(I, beta, rho, q, theta0, u_r, u0, w0, 32, Wn=4)
+    assert_bit_equal(WP, z[f"{key}_WP"], "WP")
+    LV, LW, lwm1, pg = O.alif_serial_backward(I, u0, w0, U, W, S, GS, beta, rho, q, theta0, alpha)
+    assert rel(LV, z[f"{key}_LV"]) < 1e-6
+    assert rel(LW, z[f"{key}_LW"]) < 1e-6
+    assert rel(LV, z[f"{key}_dI"]) < 1e-6
+    assert rel(beta * LV[0], z[f"{key}_du0"]) < 1e-6
+    assert rel(lwm1, z[f"{key}_dw0"]) < 1e-5
+    dp = z[f"{key}_dp"].astype(np.float64)
+    for i in range(4):
+        assert abs(pg[i] - dp[i]) <= 1e-5 * (abs(dp[i]) + 1e-3), (i, pg, dp)
