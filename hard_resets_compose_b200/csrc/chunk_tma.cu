@@ -546,16 +546,36 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
 #ifndef LIFB_FORCE_NPL
 #define LIFB_FORCE_NPL 0
 #endif
-template <int NPL>
+// Single-chunk forward with one neuron per lane (the streaming pass over a
+// whole sequence): a deeper ring, measured 32.8 us against 34.8 us for the
+// V-saving forward at T = 1024, N = 16384.
+#ifndef LIFB_FWD1_DEEP_S
+#define LIFB_FWD1_DEEP_S 8
+#endif
+// Adjoint from V (two input arrays, V and GS) with one neuron per lane:
+// taller tiles keep twice the rows in flight; measured 36.9 us against 45.1 us
+// at T = 1024, N = 16384 (the three-array layouts are slower with them).
+#ifndef LIFB_BWDV1_R
+#define LIFB_BWDV1_R 32
+#endif
+#ifndef LIFB_BWDV1_S
+#define LIFB_BWDV1_S 4
+#endif
+template <int NPL, bool DEEP = false>
 struct FwdTile {
     static constexpr int R = NPL == 4 ? LIFB_FWD4_R : LIFB_FWD1_R;
-    static constexpr int S = NPL == 4 ? LIFB_FWD4_S : LIFB_FWD1_S;
+    static constexpr int S = NPL == 4 ? LIFB_FWD4_S : (DEEP ? LIFB_FWD1_DEEP_S : LIFB_FWD1_S);
 };
-template <int NPL>
+template <int NPL, bool FROM_V = false>
 struct BwdTile {
-    static constexpr int R = NPL == 4 ? LIFB_BWD4_R : LIFB_BWD1_R;
-    static constexpr int S = NPL == 4 ? LIFB_BWD4_S : LIFB_BWD1_S;
+    static constexpr int R = NPL == 4 ? LIFB_BWD4_R : (FROM_V ? LIFB_BWDV1_R : LIFB_BWD1_R);
+    static constexpr int S = NPL == 4 ? LIFB_BWD4_S : (FROM_V ? LIFB_BWDV1_S : LIFB_BWD1_S);
 };
+static int bwd_rows(int npl, bool from_v)
+{
+    if (npl == 4) return from_v ? BwdTile<4, true>::R : BwdTile<4>::R;
+    return from_v ? BwdTile<1, true>::R : BwdTile<1>::R;
+}
 
 bool tma_ok(const void *const *ptrs, int n, int64_t N)
 {
@@ -575,13 +595,13 @@ int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
     return ((N + 127) / 128) * M >= (int64_t)min_ctas_per_sm * sms ? 4 : 1;
 }
 
-template <int NPL, bool VOUT, bool AFF>
+template <int NPL, bool VOUT, bool AFF, bool DEEP>
 static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, int64_t start_stride, float *U,
                        float *S, float *Ends, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r,
                        int64_t lead, float *LeadStarts, float gamma, float delta, int *status, cudaStream_t s)
 {
     constexpr int NB = 32 * NPL;
-    constexpr int R = FwdTile<NPL>::R, ST = FwdTile<NPL>::S;
+    constexpr int R = FwdTile<NPL, DEEP>::R, ST = FwdTile<NPL, DEEP>::S;
     const size_t smem = (size_t)(ST + 4) * R * NB * 4;
     auto kern = k_fwd_tma<NPL, R, ST, VOUT, AFF>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -612,10 +632,17 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
         !make_tmap_2d(&maps[2], S, N, T, 32 * npl, R))
         return false;
     int *status = device_status_ptr();
+    // one chunk, one neuron per lane: the deeper ring
+    const bool deep = npl == 1 && M == 1 && lead == 0;
     auto go = [&](auto npl_c, auto vout_c, auto aff_c) {
-        launch_fwd<decltype(npl_c)::value, decltype(vout_c)::value, decltype(aff_c)::value>(
-            maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r, lead, LeadStarts, gamma, delta,
-            status, s);
+        constexpr int kNpl = decltype(npl_c)::value;
+        constexpr bool kV = decltype(vout_c)::value, kA = decltype(aff_c)::value;
+        if (kNpl == 1 && deep)
+            launch_fwd<kNpl, kV, kA, true>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r,
+                                           lead, LeadStarts, gamma, delta, status, s);
+        else
+            launch_fwd<kNpl, kV, kA, false>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r,
+                                            lead, LeadStarts, gamma, delta, status, s);
     };
     using I1 = std::integral_constant<int, 1>;
     using I4 = std::integral_constant<int, 4>;
@@ -636,7 +663,7 @@ static void launch_bwd(const CUtensorMap *maps, const float *u0, const float *La
 {
     constexpr int NB = 32 * NPL;
     constexpr int NT = BwdLayout<READ_S, HAS_GU, FROM_V>::NT;
-    constexpr int R = BwdTile<NPL>::R, ST = BwdTile<NPL>::S;
+    constexpr int R = BwdTile<NPL, FROM_V>::R, ST = BwdTile<NPL, FROM_V>::S;
     const size_t smem = ((size_t)ST * NT + (MODE == kReplay ? 2 : 0)) * R * NB * 4;
     auto kern = k_bwd_tma<NPL, R, ST, READ_S, HAS_GU, MODE, TRACK, FROM_V, AFF, PG>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -671,7 +698,7 @@ bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, 
     if (M > 65535) return false;
     const int npl = pick_npl(N, M, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
     const int nb = 32 * npl;
-    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    const int R = bwd_rows(npl, true);
     CUtensorMap maps[6];
     if (!make_tmap_2d(&maps[0], V, N, T, nb, R) || !make_tmap_2d(&maps[3], GS, N, T, nb, R) ||
         !make_tmap_2d(&maps[5], Lam, N, T, nb, R))
@@ -698,7 +725,7 @@ bool bwd_tma_aff(const float *IV, const float *u0, const float *U, const float *
     if (!tma_ok(p, 5, N) || T <= 0) return false;
     const int npl = pick_npl(N, 1, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
     const int nb = 32 * npl;
-    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    const int R = bwd_rows(npl, from_v);
     CUtensorMap maps[6];
     if (!make_tmap_2d(&maps[0], IV, N, T, nb, R) || !make_tmap_2d(&maps[3], GS, N, T, nb, R) ||
         !make_tmap_2d(&maps[5], Lam, N, T, nb, R))
@@ -730,7 +757,7 @@ bool bwd_tma_aff_pg(const float *V, const float *u0, const float *GS, float *Lam
     if (!tma_ok(p, 4, N) || T <= 0 || (uintptr_t)PGout % 8) return false;
     const int npl = pick_npl(N, 1, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
     const int nb = 32 * npl;
-    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    const int R = bwd_rows(npl, true);
     CUtensorMap maps[6];
     if (!make_tmap_2d(&maps[0], V, N, T, nb, R) || !make_tmap_2d(&maps[3], GS, N, T, nb, R) ||
         !make_tmap_2d(&maps[5], Lam, N, T, nb, R))
@@ -758,7 +785,7 @@ bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const fl
     if (M > 65535) return false;
     const int npl = pick_npl(N, M, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
     const int nb = 32 * npl;
-    const int R = npl == 4 ? BwdTile<4>::R : BwdTile<1>::R;
+    const int R = bwd_rows(npl, false);
     // maps: I, U, S, GS, GU, Lam (unused slots repeat a valid map)
     CUtensorMap maps[6];
     if (!make_tmap_2d(&maps[0], I, N, T, nb, R) || !make_tmap_2d(&maps[1], U, N, T, nb, R) ||
