@@ -17,9 +17,12 @@ Deliberate differences:
     result; dw, K1, K2 and the Triton launch knobs are accepted and ignored.
     `stats` reports "segments" and "lead_in" with repair_iters = 0; `phases`
     receives the whole call's GPU time under "scan".
-  * alif_backward computes the adjoint pair (LV, LW) in one fp32 reverse
-    sweep per neuron for every mode; "scan" keeps the reference's argument
-    checks (T % C == 0, C % D == 0).
+  * alif_backward's "scan" composes the chunk maps of the (lv, lw) pair
+    (upper-triangular 2x2 per step), carries them and replays every chunk,
+    over chunks of the B200 policy's length (lifscan.scan_chunk_bwd, at least
+    ALIF_MIN_CHUNK rows: one chunk when N fills the GPU); it keeps the
+    reference's argument checks
+    (T % C == 0, C % D == 0).  The serial modes run one reverse sweep.
   * ALIFFn does not save S (its own output, recomputed bit for bit from U, W
     and I) and sums its parameter gradients in fp64 inside the same reverse
     sweep (lifb_alif_bwd with param_sums), without writing LW.
@@ -148,29 +151,53 @@ def alif_scan_forward(I, beta, rho, q, theta0, u_r, u0, w0, Wpred, dw, C=128, K1
     return U, W, S
 
 
-def _alif_bwd(I, u0, w0, U, W, S, GS, beta, rho, q, theta0, alpha, want_lw, want_params):
+# Shortest chunk of the two-level ALIF adjoint: the carry runs over the T/C
+# chunks one after another, so very short chunks move the time into it
+# (measured T = 4096, N = 8: 1-row chunks 1.72 ms against 0.38 ms for the one
+# sweep).
+ALIF_MIN_CHUNK = 256
+
+
+def _alif_chunk(T, N):
+    """Chunk length of the two-level ALIF adjoint: lifscan's adjoint policy
+    (scan_chunk_bwd), doubled while it divides T until ALIF_MIN_CHUNK rows."""
+    C = L.scan_chunk_bwd(T, N)
+    while C < ALIF_MIN_CHUNK and C < T and T % (2 * C) == 0:
+        C *= 2
+    return C
+
+
+def _alif_bwd(I, u0, w0, U, W, S, GS, beta, rho, q, theta0, alpha, want_lw, want_params, chunked=False):
+    """(LV, LW or None, dL/dw0 or None, param sums [4, M, N] fp64 or None);
+    chunked: over T/C chunks of the B200 policy's length (lifb_alif_bwd_scan)."""
     I, u0, w0, T, N = _prep(I, u0, w0)
     U = L._cuda_f32("U", U, (T, N))
     W = L._cuda_f32("W", W, (T, N))
     if S is not None:
         S = L._cuda_f32("S", S, (T, N))
     GS = L._cuda_f32("GS", GS, (T, N))
+    C = _alif_chunk(T, N) if chunked and T > 0 else max(T, 1)
+    M = T // C if T else 1
     LV = torch.empty_like(I)
     LW = torch.empty_like(I) if want_lw else None
     lwm1 = torch.empty(N, device=I.device) if want_params else None
-    sums = torch.zeros(4, N, dtype=torch.float64, device=I.device) if want_params else None
+    sums = torch.zeros(4, M, N, dtype=torch.float64, device=I.device) if want_params else None
     lib = _lib.load()
     o = lambda t: ptr(t) if t is not None else None  # noqa: E731
     with torch.cuda.device(I.device):
-        check(lib.lifb_alif_bwd(ptr(I), ptr(u0), ptr(w0), ptr(U), ptr(W), o(S), ptr(GS), ptr(LV), o(LW), o(lwm1),
-                                o(sums), T, N, float(beta), float(rho), float(q), float(theta0), float(alpha),
-                                stream_of(I)), "alif_backward")
+        nb = lib.lifb_alif_bwd_scan_workspace_bytes(T, N, C) if M > 1 else 0
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=I.device)
+        check(lib.lifb_alif_bwd_scan(ptr(I), ptr(u0), ptr(w0), ptr(U), ptr(W), o(S), ptr(GS), ptr(LV), o(LW),
+                                     o(lwm1), o(sums), T, N, float(beta), float(rho), float(q), float(theta0),
+                                     float(alpha), C, ptr(ws), nb, stream_of(I)), "alif_backward")
     return LV, LW, lwm1, sums
 
 
 def alif_backward(I, U, W, S, GS, beta, rho, q, theta0, u0, w0, alpha=4.0, mode="scan", C=64, BN=32, D=4, nw=1):
     """lifscan/triton_alif.py:490-521 -> (LV, LW): LV[t] = dL/dv_t (= dL/dI_t),
-    LW[t] = dL/dw_t, for a loss with dL/dS = GS (detached reset)."""
+    LW[t] = dL/dw_t, for a loss with dL/dS = GS (detached reset).  "scan"
+    runs the two-level form over chunks of the B200 policy's length (the
+    reference's C and D are checked, not used); the serial modes one sweep."""
     if mode not in ("scan", "serial", "serial_pf", "serial_tuned"):
         raise ValueError(f"unknown mode {mode!r}")
     if mode == "scan":
@@ -178,7 +205,8 @@ def alif_backward(I, U, W, S, GS, beta, rho, q, theta0, u0, w0, alpha=4.0, mode=
         C, D = int(C), int(D)
         if C <= 0 or D <= 0 or T % C or C % D:
             raise AssertionError(f"T={T} must be a multiple of C={C}, and C of D={D}")
-    LV, LW, _, _ = _alif_bwd(I, u0, w0, U, W, S, GS, beta, rho, q, theta0, alpha, True, False)
+    LV, LW, _, _ = _alif_bwd(I, u0, w0, U, W, S, GS, beta, rho, q, theta0, alpha, True, False,
+                             chunked=mode == "scan")
     return LV, LW
 
 
@@ -197,6 +225,7 @@ class ALIFFn(torch.autograd.Function):
             U, W, S = alif_scan_forward(I, b, r, qq, th, u_r, u0, w0, Wpred, dw, C=C)
         ctx.save_for_backward(I, u0, w0, U, W)
         ctx.c = (b, r, qq, th, alpha)
+        ctx.bwd = bwd
         ctx.mark_non_differentiable(U, W)
         return S, U, W
 
@@ -207,8 +236,9 @@ class ALIFFn(torch.autograd.Function):
         need = ctx.needs_input_grad
         want = any(need[1:7])
         # S is this layer's own output: the sweep recomputes it from U, W, I
-        LV, _, lwm1, sums = _alif_bwd(I, u0, w0, U, W, None, gS.contiguous(), b, r, qq, th, alpha, False, want)
-        g = sums.sum(dim=1).to(torch.float32) if want else None
+        LV, _, lwm1, sums = _alif_bwd(I, u0, w0, U, W, None, gS.contiguous(), b, r, qq, th, alpha, False, want,
+                                      chunked=ctx.bwd == "scan")
+        g = sums.sum(dim=(1, 2)).to(torch.float32) if want else None
         pick = lambda i, v: v if need[i] else None  # noqa: E731
         return (LV, pick(1, b * LV[0]), pick(2, lwm1), pick(3, g[0] if want else None),
                 pick(4, g[1] if want else None), pick(5, g[2] if want else None), pick(6, g[3] if want else None),

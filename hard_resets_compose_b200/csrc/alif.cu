@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(kAlifBlock) k_alif_bwd(
     const float *__restrict__ I, const float *__restrict__ u0, const float *__restrict__ w0,
     const float *__restrict__ U, const float *__restrict__ W, const float *__restrict__ S,
     const float *__restrict__ GS, float *__restrict__ LV, float *__restrict__ LW, float *__restrict__ lwm1,
-    double *__restrict__ PG, int64_t T, int64_t N, AlifP p, float alpha)
+    double *__restrict__ PG, int64_t pg_stride, int64_t T, int64_t N, AlifP p, float alpha)
 {
     const int64_t n = (int64_t)blockIdx.x * kAlifBlock + threadIdx.x;
     if (n >= N) return;
@@ -578,45 +578,56 @@ __global__ void __launch_bounds__(kAlifBlock) k_alif_bwd(
     if (lwm1) lwm1[n] = lw;
     if (PG) {
         PG[n] = db;
-        PG[N + n] = dr;
-        PG[2 * N + n] = dq;
-        PG[3 * N + n] = -dt;
+        PG[pg_stride + n] = dr;
+        PG[2 * pg_stride + n] = dq;
+        PG[3 * pg_stride + n] = -dt;
     }
 }
 
 // ------------------------------------------------------------------ backward (TMA)
 constexpr int kAlifBwdR = 16, kAlifBwdS = 4;  // rows per tile, ring stages (one neuron per lane)
+constexpr int kAlifReplay = 0, kAlifCompose = 1;
 
-// The same reverse sweep with I[t], U[t-1], W[t-1], GS[t] (and S[t]) streamed
-// through a TMA ring of R-row tiles from the last row up, and LV (and LW)
-// written back by TMA stores.  Tiles wholly above row 0 take the fast path;
-// the tile holding row 0 (where u_{-1}, w_{-1} = u0, w0) and a ragged first
-// tile take checked rows with direct stores.
-template <int R, int S, bool READ_S, bool PGF, bool WRITE_LW>
+// The reverse sweep over chunk m = blockIdx.y (rows [m*C, (m+1)*C)) with
+// I[t], U[t-1], W[t-1], GS[t] (and S[t]) streamed through a TMA ring of R-row
+// tiles from the chunk's last row up.  One step is affine in (lv, lw):
+//     lv' = c lv + sg q lw + sg g,   lw' = (rho - sg q) lw - sg g,   c = (1 - s) beta
+// kAlifReplay: starts from (LVE, LWE)[m] (NULL: 0), writes LV (and LW) by TMA
+// stores, and per (chunk, neuron) the parameter sums PG[4][M][N] and, for
+// chunk 0, dL/dw0.  kAlifCompose: writes the chunk's map (m11, m12, m22, b1,
+// b2) into Map[j * mst + m * N + n], j = 0..4: (lv, lw) at the chunk's first row = [[m11, m12],
+// [0, m22]] (lv, lw entering) + (b1, b2).  Full tiles above row 0 take the
+// fast path; the tile holding row 0 (u_{-1}, w_{-1} = u0, w0) and a ragged
+// first tile take checked rows with direct stores.
+template <int R, int S, int MODE, bool READ_S, bool PGF, bool WRITE_LW>
 __global__ void __launch_bounds__(32) k_alif_bwd_tma(
     const __grid_constant__ CUtensorMap tI, const __grid_constant__ CUtensorMap tU,
     const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tGS,
     const __grid_constant__ CUtensorMap tS, const __grid_constant__ CUtensorMap tLV,
     const __grid_constant__ CUtensorMap tLW, const float *__restrict__ u0, const float *__restrict__ w0,
-    float *__restrict__ LV, float *__restrict__ LW, float *__restrict__ lwm1, double *__restrict__ PG, int64_t N,
-    int64_t T, AlifP p, float alpha, int *status)
+    float *__restrict__ LV, float *__restrict__ LW, float *__restrict__ lwm1, double *__restrict__ PG,
+    const float *__restrict__ LVE, const float *__restrict__ LWE, float *__restrict__ Map, int64_t mst, int64_t N,
+    int64_t C, AlifP p, float alpha, int *status)
 {
     constexpr int NB = 32;
     constexpr int NT = READ_S ? 5 : 4;  // I, U, W, GS (, S)
     constexpr int kTile = R * NB;
     constexpr uint32_t kStageBytes = NT * kTile * 4;
     constexpr int NO = WRITE_LW ? 2 : 1;  // LV (, LW) output tiles
+    constexpr bool kOut = MODE == kAlifReplay;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     float *ring = reinterpret_cast<float *>(smem_raw);
-    float *obuf = ring + (size_t)S * NT * kTile;  // 2 x NO tiles
+    float *obuf = ring + (size_t)S * NT * kTile;  // 2 x NO tiles (replay)
     __shared__ __align__(8) uint64_t full[S];
     const int lane = threadIdx.x;
     const int64_t n0 = (int64_t)blockIdx.x * NB;
-    const int64_t nfull = T / R;
-    const int64_t ntiles = nfull + (T % R ? 1 : 0);
+    const int64_t m = blockIdx.y, M = gridDim.y;
+    const int64_t cstart = m * C, cend = cstart + C;
+    const int64_t nfull = C / R;
+    const int64_t ntiles = nfull + (C % R ? 1 : 0);
 
     auto issue = [&](int s, int64_t k) {
-        const int row = (int)(T - (k + 1) * R);  // may be negative: zero-filled
+        const int row = (int)(cend - (k + 1) * R);  // may be negative: zero-filled
         float *b = ring + (size_t)s * NT * kTile;
         mbar_arrive_expect_tx(&full[s], kStageBytes);
         tma_load_2d(b, &tI, (int)n0, row, &full[s]);
@@ -631,8 +642,8 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
         prefetch_tmap(&tW);
         prefetch_tmap(&tGS);
         if (READ_S) prefetch_tmap(&tS);
-        prefetch_tmap(&tLV);
-        if (WRITE_LW) prefetch_tmap(&tLW);
+        if (kOut) prefetch_tmap(&tLV);
+        if (kOut && WRITE_LW) prefetch_tmap(&tLW);
         for (int s = 0; s < S; s++) mbar_init(&full[s], 1);
         fence_barrier_init();
     }
@@ -645,6 +656,11 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
     const float u00 = act ? u0[n] : 0.0f, w00 = act ? w0[n] : 0.0f;
     const float k2 = alpha * 1.4426950408889634f;  // exp(x) = 2^(x log2 e)
     float lv = 0.0f, lw = 0.0f;
+    if (kOut && act && LVE) {
+        lv = LVE[m * N + n];
+        lw = LWE[m * N + n];
+    }
+    float m11 = 1.0f, m12 = 0.0f, m22 = 1.0f;  // kAlifCompose: the chunk map's matrix
     // parameter sums: each tile's rows in fp32 (tb, tr, tq, tt), folded into
     // the fp64 totals once per tile
     double db = 0.0, dr = 0.0, dq = 0.0, dt = 0.0;
@@ -664,8 +680,15 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
         const float a = (v - p.theta0) - wp;
         const float sig = rcp_approx(1.0f + ex2_approx(-k2 * a));
         const float sg = alpha * sig * (1.0f - sig);
+        const float c = (1.0f - s) * p.beta;
+        if (MODE == kAlifCompose) {
+            const float sgq = sg * p.q;
+            m12 = c * m12 + sgq * m22;
+            m11 = c * m11;
+            m22 = (p.rho - sgq) * m22;
+        }
         const float d = gs + p.q * lw;
-        lv = (1.0f - s) * p.beta * lv + sg * d;
+        lv = c * lv + sg * d;
         out_lv = lv;
         out_lw = lw;
         if (PGF) {
@@ -681,12 +704,12 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
         const int s = (int)(k % S);
         if (!mbar_wait(&full[s], (uint32_t)((k / S) & 1))) { ok = false; break; }
         const float *b = ring + (size_t)s * NT * kTile + lane;
-        const int64_t rbase = T - (k + 1) * R;  // global row of in-tile row 0
+        const int64_t rbase = cend - (k + 1) * R;  // global row of in-tile row 0
         const bool fast = k < nfull && rbase > 0;
         if (fast) {
             float *ov = obuf + (int)(k & 1) * NO * kTile;
             float *ow = ov + kTile;
-            if (k >= 2) {  // the stores issued two tiles ago must have read this buffer
+            if (kOut && k >= 2) {  // the stores issued two tiles ago must have read this buffer
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
             }
@@ -695,26 +718,30 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
                 const int o = rr * NB;
                 float a, c;
                 step(b[o], b[kTile + o], b[2 * kTile + o], b[3 * kTile + o], READ_S ? b[4 * kTile + o] : 0.0f, a, c);
-                ov[o + lane] = a;
-                if (WRITE_LW) ow[o + lane] = c;
+                if (kOut) {
+                    ov[o + lane] = a;
+                    if (WRITE_LW) ow[o + lane] = c;
+                }
             }
-            fence_proxy_async_shared();
-            __syncwarp();
-            if (lane == 0) {
-                tma_store_2d(&tLV, (int)n0, (int)rbase, ov);
-                if (WRITE_LW) tma_store_2d(&tLW, (int)n0, (int)rbase, ow);
-                bulk_commit();
+            if (kOut) {
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tLV, (int)n0, (int)rbase, ov);
+                    if (WRITE_LW) tma_store_2d(&tLW, (int)n0, (int)rbase, ow);
+                    bulk_commit();
+                }
             }
         } else {
             for (int rr = R - 1; rr >= 0; rr--) {
                 const int64_t t = rbase + rr;
-                if (t < 0) break;
+                if (t < cstart) break;
                 const int o = rr * NB;
                 const float up = t == 0 ? u00 : b[kTile + o];
                 const float wp = t == 0 ? w00 : b[2 * kTile + o];
                 float a, c;
                 step(b[o], up, wp, b[3 * kTile + o], READ_S ? b[4 * kTile + o] : 0.0f, a, c);
-                if (act) {
+                if (kOut && act) {
                     LV[t * N + n] = a;
                     if (WRITE_LW) LW[t * N + n] = c;
                 }
@@ -728,38 +755,78 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
     }
     if (!ok && status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
     if (ok && act) {
-        if (lwm1) lwm1[n] = lw;
-        if (PGF) {
-            PG[n] = db;
-            PG[N + n] = dr;
-            PG[2 * N + n] = dq;
-            PG[3 * N + n] = -dt;
+        if (MODE == kAlifCompose) {
+            const int64_t o = m * N + n;
+            Map[o] = m11;
+            Map[mst + o] = m12;
+            Map[2 * mst + o] = m22;
+            Map[3 * mst + o] = lv;
+            Map[4 * mst + o] = lw;
+        } else {
+            if (lwm1 && m == 0) lwm1[n] = lw;
+            if (PGF) {
+                const int64_t o = m * N + n, st = M * N;
+                PG[o] = db;
+                PG[st + o] = dr;
+                PG[2 * st + o] = dq;
+                PG[3 * st + o] = -dt;
+            }
         }
     }
-    if (lane == 0) bulk_wait_all();
+    if (kOut && lane == 0) bulk_wait_all();
 }
 
-template <bool READ_S, bool PGF, bool WRITE_LW>
+// Entering (lv, lw) of every chunk from the chunk maps, last chunk first
+// (entering 0): chunk m-1 enters with chunk m's map applied to chunk m's entry.
+__global__ void __launch_bounds__(kAlifBlock) k_alif_bwd_carry(const float *__restrict__ Map, int64_t st,
+                                                               float *__restrict__ LVE, float *__restrict__ LWE,
+                                                               int64_t N, int64_t M)
+{
+    const int64_t n = (int64_t)blockIdx.x * kAlifBlock + threadIdx.x;
+    if (n >= N) return;
+    float e1 = 0.0f, e2 = 0.0f;
+    LVE[(M - 1) * N + n] = 0.0f;
+    LWE[(M - 1) * N + n] = 0.0f;
+    for (int64_t m = M - 1; m >= 1; m--) {
+        const int64_t o = m * N + n;
+        const float a11 = Map[o], a12 = Map[st + o], a22 = Map[2 * st + o], b1 = Map[3 * st + o],
+                    b2 = Map[4 * st + o];
+        const float n1 = a11 * e1 + a12 * e2 + b1;
+        const float n2 = a22 * e2 + b2;
+        e1 = n1;
+        e2 = n2;
+        LVE[(m - 1) * N + n] = e1;
+        LWE[(m - 1) * N + n] = e2;
+    }
+}
+
+template <int MODE, bool READ_S, bool PGF, bool WRITE_LW>
 static void launch_alif_bwd(const CUtensorMap *maps, const float *u0, const float *w0, float *LV, float *LW,
-                            float *lwm1, double *PG, int64_t N, int64_t T, const AlifP &p, float alpha, int *status,
-                            cudaStream_t s)
+                            float *lwm1, double *PG, const float *LVE, const float *LWE, float *Map, int64_t mst,
+                            int64_t N, int64_t M, int64_t C, const AlifP &p, float alpha, int *status, cudaStream_t s)
 {
     constexpr int R = kAlifBwdR, ST = kAlifBwdS, NT = READ_S ? 5 : 4, NO = WRITE_LW ? 2 : 1;
-    const size_t smem = ((size_t)ST * NT + 2 * NO) * R * 32 * 4;
-    auto kern = k_alif_bwd_tma<R, ST, READ_S, PGF, WRITE_LW>;
+    const size_t smem = ((size_t)ST * NT + (MODE == kAlifReplay ? 2 * NO : 0)) * R * 32 * 4;
+    auto kern = k_alif_bwd_tma<R, ST, MODE, READ_S, PGF, WRITE_LW>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     count_launches(1);
-    kern<<<(unsigned)((N + 31) / 32), 32, smem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6],
-                                                      u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status);
+    kern<<<dim3((unsigned)((N + 31) / 32), (unsigned)M), 32, smem, s>>>(
+        maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], u0, w0, LV, LW, lwm1, PG, LVE, LWE, Map, mst, N,
+        C, p, alpha, status);
 }
 
-// False when the TMA path does not apply (nothing launched).
+// The adjoint over M = T/C chunks (M = 1: one sweep).  M > 1 needs the
+// chunk maps Map (5 arrays of [M][N], mst floats apart) and LVE, LWE [M][N].
+// PG is [4][M][N].  False when the TMA path does not apply (nothing launched).
 static bool alif_bwd_tma(const float *I, const float *u0, const float *w0, const float *U, const float *W,
                          const float *S, const float *GS, float *LV, float *LW, float *lwm1, double *PG, int64_t T,
-                         int64_t N, const AlifP &p, float alpha, cudaStream_t s)
+                         int64_t N, int64_t C, float *Map, int64_t mst, float *LVE, float *LWE, const AlifP &p,
+                         float alpha, cudaStream_t s)
 {
     const void *ptrs[] = {I, U, W, S, GS, LV, LW};
-    if (!tma_ok(ptrs, 7, N) || T <= 0 || T > (1LL << 31) - 64 || ((uintptr_t)PG & 7)) return false;
+    if (!tma_ok(ptrs, 7, N) || T <= 0 || T > (1LL << 31) - 64 || ((uintptr_t)PG & 7) || C <= 0 || T % C) return false;
+    const int64_t M = T / C;
+    if (M > 65535) return false;
     constexpr int R = kAlifBwdR;
     CUtensorMap maps[7];
     if (!make_tmap_2d(&maps[0], I, N, T, 32, R) || !make_tmap_2d(&maps[1], U, N, T, 32, R) ||
@@ -772,16 +839,28 @@ static bool alif_bwd_tma(const float *I, const float *u0, const float *w0, const
     if (LW && !make_tmap_2d(&maps[6], LW, N, T, 32, R)) return false;
     int *status = device_status_ptr();
     const bool rs = S != nullptr, pg = PG != nullptr, wl = LW != nullptr;
+    const float *le = nullptr, *we = nullptr;
+    if (M > 1) {
+        if (rs) launch_alif_bwd<kAlifCompose, true, false, false>(maps, u0, w0, LV, LW, lwm1, PG, nullptr, nullptr, Map, mst, N, M, C, p, alpha, status, s);
+        else launch_alif_bwd<kAlifCompose, false, false, false>(maps, u0, w0, LV, LW, lwm1, PG, nullptr, nullptr, Map, mst, N, M, C, p, alpha, status, s);
+        count_launches(1);
+        k_alif_bwd_carry<<<(unsigned)((N + kAlifBlock - 1) / kAlifBlock), kAlifBlock, 0, s>>>(Map, mst, LVE, LWE, N, M);
+        le = LVE;
+        we = LWE;
+    }
     // the combinations the library uses: (S, LW) for alif_backward, neither
     // with the parameter sums for the layer; the rest for completeness
-    if (rs && wl && !pg) launch_alif_bwd<true, false, true>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
-    else if (!rs && wl && !pg) launch_alif_bwd<false, false, true>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
-    else if (!rs && !wl && pg) launch_alif_bwd<false, true, false>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
-    else if (rs && wl && pg) launch_alif_bwd<true, true, true>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
-    else if (!rs && wl && pg) launch_alif_bwd<false, true, true>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
-    else if (rs && !wl && pg) launch_alif_bwd<true, true, false>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
-    else if (rs && !wl && !pg) launch_alif_bwd<true, false, false>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
-    else launch_alif_bwd<false, false, false>(maps, u0, w0, LV, LW, lwm1, PG, N, T, p, alpha, status, s);
+#define LIFB_ALIF_GO(RS, PGF, WL) \
+    launch_alif_bwd<kAlifReplay, RS, PGF, WL>(maps, u0, w0, LV, LW, lwm1, PG, le, we, Map, mst, N, M, C, p, alpha, status, s)
+    if (rs && wl && !pg) LIFB_ALIF_GO(true, false, true);
+    else if (!rs && wl && !pg) LIFB_ALIF_GO(false, false, true);
+    else if (!rs && !wl && pg) LIFB_ALIF_GO(false, true, false);
+    else if (rs && wl && pg) LIFB_ALIF_GO(true, true, true);
+    else if (!rs && wl && pg) LIFB_ALIF_GO(false, true, true);
+    else if (rs && !wl && pg) LIFB_ALIF_GO(true, true, false);
+    else if (rs && !wl && !pg) LIFB_ALIF_GO(true, false, false);
+    else LIFB_ALIF_GO(false, false, false);
+#undef LIFB_ALIF_GO
     return true;
 }
 
@@ -883,6 +962,51 @@ int lifb_alif_warm_predict(const float *I, const float *u0, const float *w0, flo
     return done("lifb_alif_warm_predict");
 }
 
+size_t lifb_alif_bwd_scan_workspace_bytes(int64_t T, int64_t N, int64_t C)
+{
+    if (T <= 0 || N <= 0 || C <= 0 || T % C || T / C < 2) return 0;
+    return 7 * al256((size_t)(T / C) * N * 4);
+}
+
+int lifb_alif_bwd_scan(const float *I, const float *u0, const float *w0, const float *U, const float *W,
+                       const float *S, const float *GS, float *LV, float *LW, float *lw_m1, double *param_sums,
+                       int64_t T, int64_t N, float beta, float rho, float q, float theta0, float alpha, int64_t C,
+                       void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (T < 0 || N < 0 || C <= 0 || (T > 0 && T % C))
+        return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_bwd_scan: T must be a multiple of the chunk length C > 0");
+    if (T / C > 65535) return fail(LIFB_ERR_UNSUPPORTED, "lifb_alif_bwd_scan: more than 65535 chunks");
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!I || !u0 || !w0 || !U || !W || !GS || !LV)
+        return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_bwd_scan: null pointer");
+    const int64_t M = T / C;
+    float *Map = nullptr, *LVE = nullptr, *LWE = nullptr;
+    int64_t mst = 0;
+    if (M > 1) {
+        const size_t one = al256((size_t)M * N * 4);
+        if (!workspace || (uintptr_t)workspace % 256 || workspace_bytes < 7 * one)
+            return fail(LIFB_ERR_WORKSPACE, "lifb_alif_bwd_scan: workspace missing, misaligned or too small "
+                                            "(lifb_alif_bwd_scan_workspace_bytes)");
+        char *b = (char *)workspace;
+        Map = (float *)b;  // 5 arrays of [M][N], `one` bytes apart
+        mst = (int64_t)(one / 4);
+        LVE = (float *)(b + 5 * one);
+        LWE = (float *)(b + 6 * one);
+    }
+    const lifb::AlifP p{beta, rho, q, theta0, 0.0f};
+    cudaStream_t s = (cudaStream_t)stream;
+    if (lifb::alif_bwd_tma(I, u0, w0, U, W, S, GS, LV, LW, lw_m1, param_sums, T, N, C, Map, mst, LVE, LWE, p, alpha,
+                           s))
+        return done("lifb_alif_bwd_scan");
+    // the plain sweep over the whole sequence: its sums go to chunk 0's slots
+    if (param_sums && M > 1 && cudaMemsetAsync(param_sums, 0, (size_t)4 * M * N * sizeof(double), s) != cudaSuccess)
+        return fail(LIFB_ERR_CUDA, "lifb_alif_bwd_scan: memset failed");
+    lifb::count_launches(1);
+    lifb::k_alif_bwd<8><<<(unsigned)((N + lifb::kAlifBlock - 1) / lifb::kAlifBlock), lifb::kAlifBlock, 0, s>>>(
+        I, u0, w0, U, W, S, GS, LV, LW, lw_m1, param_sums, M * N, T, N, p, alpha);
+    return done("lifb_alif_bwd_scan");
+}
+
 int lifb_alif_bwd(const float *I, const float *u0, const float *w0, const float *U, const float *W, const float *S,
                   const float *GS, float *LV, float *LW, float *lw_m1, double *param_sums, int64_t T, int64_t N,
                   float beta, float rho, float q, float theta0, float alpha, void *stream)
@@ -890,14 +1014,8 @@ int lifb_alif_bwd(const float *I, const float *u0, const float *w0, const float 
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_bwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !w0 || !U || !W || !GS || !LV) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_bwd: null pointer");
-    const lifb::AlifP p{beta, rho, q, theta0, 0.0f};
-    cudaStream_t s = (cudaStream_t)stream;
-    if (!lifb::alif_bwd_tma(I, u0, w0, U, W, S, GS, LV, LW, lw_m1, param_sums, T, N, p, alpha, s)) {
-        lifb::count_launches(1);
-        lifb::k_alif_bwd<8><<<(unsigned)((N + lifb::kAlifBlock - 1) / lifb::kAlifBlock), lifb::kAlifBlock, 0, s>>>(
-            I, u0, w0, U, W, S, GS, LV, LW, lw_m1, param_sums, T, N, p, alpha);
-    }
-    return done("lifb_alif_bwd");
+    return lifb_alif_bwd_scan(I, u0, w0, U, W, S, GS, LV, LW, lw_m1, param_sums, T, N, beta, rho, q, theta0, alpha,
+                              T, nullptr, 0, stream);
 }
 
 }  // extern "C"

@@ -358,6 +358,19 @@ int lifb_alif_bwd(const float *I, const float *u0, const float *w0, const float 
                   const float *S, const float *GS, float *LV, float *LW, float *lw_m1, double *param_sums,
                   int64_t T, int64_t N, float beta, float rho, float q, float theta0, float alpha,
                   void *stream);
+/* The same adjoint over T/C chunks of C rows (alif_backward's "scan", :505-521):
+ * each step is affine in (lv, lw) with the upper-triangular matrix
+ * [[(1 - s) beta, sg q], [0, rho - sg q]], so every chunk's map (5 numbers per
+ * neuron) is composed in parallel, a carry gives every chunk its entering
+ * (lv, lw), and every chunk is replayed from it.  param_sums is [4][T/C][N]
+ * (per chunk and neuron; the caller sums).  C = T is lifb_alif_bwd.  Workspace:
+ * lifb_alif_bwd_scan_workspace_bytes(T, N, C) (0 when T/C < 2). */
+size_t lifb_alif_bwd_scan_workspace_bytes(int64_t T, int64_t N, int64_t C);
+int lifb_alif_bwd_scan(const float *I, const float *u0, const float *w0, const float *U, const float *W,
+                       const float *S, const float *GS, float *LV, float *LW, float *lw_m1,
+                       double *param_sums, int64_t T, int64_t N, float beta, float rho, float q,
+                       float theta0, float alpha, int64_t C, void *workspace, size_t workspace_bytes,
+                       void *stream);
 
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:

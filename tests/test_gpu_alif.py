@@ -138,7 +138,7 @@ def test_alif_forward_hard_cases(cuda, T, N, beta, rho, q):
         assert_bit_equal(_np(U), Us, "U")
 
 
-@pytest.mark.parametrize("T,N", ((4096, 8), (1024, 16384), (3000, 333)))
+@pytest.mark.parametrize("T,N", ((4096, 8), (1024, 16384), (3000, 333), (1 << 15, 512), (1 << 14, 100)))
 @pytest.mark.parametrize("cls", CLASSES, ids=lambda c: c[0])
 def test_alif_backward(cuda, T, N, cls):
     """The adjoint pair (reading S, and with S recomputed) and the fused
@@ -159,7 +159,18 @@ def test_alif_backward(cuda, T, N, cls):
     LVp, _, lw1, sums = A._alif_bwd(Id, u0d, w0d, Ud, Wd, None, GSd, beta, rho, q, 1.0, 4.0, False, True)
     assert torch.equal(LVp, LVg)
     assert rel(_np(lw1), lwm1) < TOL
-    got = sums.sum(dim=1).cpu().numpy()
+    got = sums.sum(dim=(1, 2)).cpu().numpy()
+    for i in range(4):
+        assert _param_close(float(got[i]), pg[i], sc[i]), (i, got[i], pg[i])
+    # the two-level form over chunks (composed maps, carry, replay)
+    LVs, LWs = A.alif_backward(Id, Ud, Wd, Sd, GSd, beta, rho, q, 1.0, u0d, w0d, mode="scan", C=T // 8, D=1)
+    assert rel(_np(LVs), LV) < TOL
+    assert rel(_np(LWs), LW) < TOL
+    LVc, _, lwc, sc_sums = A._alif_bwd(Id, u0d, w0d, Ud, Wd, None, GSd, beta, rho, q, 1.0, 4.0, False, True,
+                                       chunked=True)
+    assert rel(_np(LVc), LV) < TOL
+    assert rel(_np(lwc), lwm1) < TOL
+    got = sc_sums.sum(dim=(1, 2)).cpu().numpy()
     for i in range(4):
         assert _param_close(float(got[i]), pg[i], sc[i]), (i, got[i], pg[i])
 
