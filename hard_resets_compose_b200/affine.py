@@ -68,11 +68,13 @@ def aff_serial_forward(I, beta, theta, gamma, delta, u0, BN=32):
 def aff_scan_forward(I, beta, theta, gamma, delta, u0, C=128, K=32, BN=16, BNc=16, BNr=32, repair=0, stats=None):
     """lifscan/triton_affine.py:165-199 -> (U, S), bit-identical to
     aff_serial_forward."""
-    I, u0, T, N = L._prep_fwd(I, u0)
+    # the reference's asserts (triton_affine.py:167) come before any device work
+    T = I.shape[0] if I.dim() == 2 else -1
     C = int(C)
-    if C <= 0 or T % C:
+    if T >= 0 and (C <= 0 or T % C):
         raise AssertionError(f"T={T} must be a multiple of C={C}")
     _check_gamma(gamma)
+    I, u0, T, N = L._prep_fwd(I, u0)
     U = torch.empty_like(I)
     S = torch.empty_like(I)
     Lseg, _ = L.spec_segment(T, N)

@@ -117,10 +117,12 @@ def alif_scan_forward(I, beta, rho, q, theta0, u_r, u0, w0, Wpred, dw, C=128, K1
                       BNr=32, D=4, repair=0, stats=None, phases=None):
     """lifscan/triton_alif.py:301-363 -> (U, W, S), bit-identical to
     alif_serial_forward.  Wpred [T//C, N] (or None) seeds the lead-ins."""
-    I, u0, w0, T, N = _prep(I, u0, w0)
+    # the reference's assert (triton_alif.py:308) comes before any device work
+    T = I.shape[0] if I.dim() == 2 else -1
     C, D = int(C), int(D)
-    if C <= 0 or D <= 0 or T % C or C % D:
+    if T >= 0 and (C <= 0 or D <= 0 or T % C or C % D):
         raise AssertionError(f"T={T} must be a multiple of C={C}, and C of D={D}")
+    I, u0, w0, T, N = _prep(I, u0, w0)
     if Wpred is not None:
         Wpred = L._cuda_f32("Wpred", Wpred, (T // C, N))
     U = torch.empty_like(I)
