@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Workload (the one the headline metric is quoted on):
+Workload (config 2, the one the headline metric is quoted on):
 lif_tuned forward+backward, B*N = 16384 neurons per GPU (B = 64 x 256),
 T = 1024, x ~ N(0.05, 0.2^2) fp32, beta = 0.99, theta = 1, u_r = 0, u0 = 0,
 the default sigmoid surrogate (alpha = 4, detached reset), upstream gradient

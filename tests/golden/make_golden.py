@@ -1,7 +1,7 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
 Run once in a container that has the reference checked out (read-only) at
-$LIFSCAN_REF (default /root/reference):
+$LIFSCAN_REF (default: a directory named `reference` beside this repository):
 
     python tests/golden/make_golden.py
 
@@ -37,7 +37,8 @@ import os
 import sys
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = os.environ.get("LIFSCAN_REF", "/root/reference")
+REF = os.environ.get("LIFSCAN_REF", os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "..",
+                                                   "reference"))
 sys.path.insert(0, REF)
 
 import numpy as np  # noqa: E402

@@ -60,7 +60,7 @@ def test_backward_vs_oracle(cuda, detach, N, T, C):
 
 @pytest.mark.parametrize("mode", ("scan", "serial"))
 def test_lif_tuned_c2_forward_backward(cuda, mode):
-    """lif_tuned fwd+bwd, B*N = 16384, T = 1024,
+    """Config 2: lif_tuned fwd+bwd, B*N = 16384, T = 1024,
     x ~ N(0.05, 0.2^2), beta = 0.99, default surrogate, upstream grad N(0, 1)."""
     T, N, beta = 1024, 16384, 0.99
     I, u0, GS = gen(T, N, 0.05, 0.2, seed=0, grad=True)

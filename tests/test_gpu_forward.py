@@ -117,7 +117,7 @@ def test_v3_chunk_shapes_and_overflow(cuda, C, K):
 
 
 def test_c1_full_size_bit_exact(cuda):
-    """B*N = 4096, T = 1024, x ~ N(0.1, 0.3^2), beta = 0.9."""
+    """Config 1: B*N = 4096, T = 1024, x ~ N(0.1, 0.3^2), beta = 0.9."""
     I, u0 = gen(1024, 4096, 0.1, 0.3, seed=0)
     Us, Ss = O.serial_forward(I, 0.9, 1.0, 0.0, u0)
     Id, u0d = to_dev(cuda, I, u0)
@@ -130,7 +130,7 @@ def test_c1_full_size_bit_exact(cuda):
 
 
 def test_c2_full_size_bit_exact(cuda):
-    """BASELINE config 2 forward: B*N = 16384, T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99."""
+    """Config 2 forward: B*N = 16384, T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99."""
     I, u0 = gen(1024, 16384, 0.05, 0.2, seed=0)
     Us, Ss = O.serial_forward(I, 0.99, 1.0, 0.0, u0)
     Id, u0d = to_dev(cuda, I, u0)
