@@ -432,9 +432,11 @@ def run_reset_family(args, ws, rank, local, family):
         ms = timed(step, args.steps)
     launches = (lib.lifb_kernel_launches() - n0) // max(args.steps, 1)
     if soft:
-        fwd = lambda: L.soft_serial_forward(I, BETA, 1.0, u0)  # noqa: E731
-        U, S = fwd()
-        bwd = lambda: L.soft_serial_backward(I, u0, U, GS, BETA, 1.0, 4.0)  # noqa: E731
+        # the layer's single-pass path: the soft reset as the affine reset
+        # (gamma = 1, delta = -theta), V saved, dbeta summed in the adjoint sweep
+        fwd = lambda: A.aff_serial_forward_v(I, BETA, 1.0, 1.0, -1.0, u0)  # noqa: E731
+        V, S = fwd()
+        bwd = lambda: A.aff_adjoint_v(V, u0, GS, BETA, 1.0, 1.0, -1.0, 4.0)  # noqa: E731
         serial_long = lambda x, z: L.soft_serial_forward(x, BETA, 1.0, z)  # noqa: E731
         scan_long = lambda x, z: TS.soft_scan_forward(x, BETA, 1.0, z)  # noqa: E731
     elif family == "alif":
@@ -456,13 +458,12 @@ def run_reset_family(args, ws, rank, local, family):
     ms_f = timed(fwd, args.steps)
     ms_b = timed(bwd, args.steps)
     hbm, peak_kind = peaks()
-    # soft layer: forward 12 B, adjoint 16 B (I, U[t-1], GS in; Lam out),
-    # dbeta pass 16 B (I, U[t-1], GS, Lam in).  Affine layer: forward 12 B
-    # (I in; V, S out), adjoint with the parameter sums 12 B (V, GS in; Lam out)
-    # ALIF layer: forward 16 B (I in; U, W, S out), adjoint with the
-    # parameter sums 20 B (I, U[t-1], W[t-1], GS in; LV out)
-    fwd_bytes, bwd_bytes = {"soft": (12, 16), "affine": (12, 12), "alif": (16, 20)}[family]
-    layer_bytes = 12 + 16 + 16 if soft else fwd_bytes + bwd_bytes
+    # soft and affine layers: forward 12 B (I in; V, S out), adjoint with the
+    # parameter sums 12 B (V, GS in; Lam out).  ALIF layer: forward 16 B (I in;
+    # U, W, S out), adjoint with the parameter sums 20 B (I, U[t-1], W[t-1],
+    # GS in; LV out)
+    fwd_bytes, bwd_bytes = {"soft": (12, 12), "affine": (12, 12), "alif": (16, 20)}[family]
+    layer_bytes = fwd_bytes + bwd_bytes
     Tl, Nl = 1 << 18, 1024
     gl = torch.Generator(device=dev).manual_seed(7100 + rank)
     Il = torch.empty(Tl, Nl, device=dev).normal_(0.02, 0.1, generator=gl)

@@ -85,25 +85,42 @@ def _soft_beta_grad(I, u0, U, gS, lam, beta, theta, alpha):
     return g_beta
 
 
+def _soft_forward_v(ctx, I, u0, b, th):
+    """The soft layers' single-pass forward: the soft reset is the affine reset
+    with gamma = 1, delta = -theta (bit for bit), so the layer saves V and its
+    backward is the affine V-path sweep, which also sums dL/dbeta."""
+    from . import affine as A
+    V, S = A.aff_serial_forward_v(I, b, th, 1.0, -th, u0)
+    ctx.save_for_backward(V, u0)
+    return S
+
+
+def _soft_backward_v(ctx, gS, b, th, alpha, need_beta):
+    """(dI, du0, dbeta or None) from V: lam_t = gS_t sigma'(v_t) + beta
+    lam_{t+1} and dbeta = sum lam_t u_{t-1} in the same sweep."""
+    from . import affine as A
+    V, u0 = ctx.saved_tensors
+    lam, pg = A.aff_adjoint_v(V, u0, gS.contiguous(), b, th, 1.0, -th, alpha, param_grads=need_beta)
+    return lam, b * lam[0], pg[0] if need_beta else None
+
+
 class LIFSoftFn(torch.autograd.Function):
-    """lifscan/fit.py:93-117: soft-reset LIF, serial kernels; gradients for I, u0, beta."""
+    """lifscan/fit.py:93-117: soft-reset LIF, serial kernels; gradients for I, u0,
+    beta.  The layer saves V (the potentials before the reset) and its backward
+    reads V and gS once, dbeta included (12 + 12 B per neuron-step)."""
 
     @staticmethod
     def forward(ctx, I, u0, beta, theta, alpha):
         b, th = L._host_scalars(beta, theta)
         I = I.contiguous()
-        U, S = L.soft_serial_forward(I, b, th, u0)
-        ctx.save_for_backward(I, u0, U)
         ctx.cfg = (b, th, alpha)
-        return S
+        return _soft_forward_v(ctx, I, u0, b, th)
 
     @staticmethod
     def backward(ctx, gS):
-        I, u0, U = ctx.saved_tensors
         b, th, alpha = ctx.cfg
-        gS = gS.contiguous()
-        lam = L.soft_serial_backward_auto(I, u0, U, gS, b, th, alpha)
-        return lam, b * lam[0], _soft_beta_grad(I, u0, U, gS, lam, b, th, alpha), None, None
+        dI, du0, db = _soft_backward_v(ctx, gS, b, th, alpha, ctx.needs_input_grad[2])
+        return dI, du0, db, None, None
 
 
 def lif_soft(I, u0, beta, theta=1.0, alpha=4.0):
@@ -120,18 +137,25 @@ class LIFSoftScanFn(torch.autograd.Function):
         from . import soft as TS
         b, th = L._host_scalars(beta, theta)
         I = I.contiguous()
+        ctx.cfg = (b, th, alpha)
+        T, N = I.shape
+        ctx.vpath = L._single_pass(T, N, mode)
+        if ctx.vpath:  # one streaming pass: save V (see LIFSoftFn)
+            return _soft_forward_v(ctx, I, u0, b, th)
         if mode == "scan":
             U, S = TS.soft_scan_forward(I, b, th, u0, C=C, K=K)
         else:
             U, S = L.soft_serial_forward(I, b, th, u0)
         ctx.save_for_backward(I, u0, U)
-        ctx.cfg = (b, th, alpha)
         return S
 
     @staticmethod
     def backward(ctx, gS):
-        I, u0, U = ctx.saved_tensors
         b, th, alpha = ctx.cfg
+        if ctx.vpath:
+            dI, du0, db = _soft_backward_v(ctx, gS, b, th, alpha, ctx.needs_input_grad[2])
+            return dI, du0, db, None, None, None, None, None
+        I, u0, U = ctx.saved_tensors
         gS = gS.contiguous()
         # both modes: the same adjoint (the reference's scan mode forms V and
         # convolves by FFT, its serial mode sweeps; one sweep from U and I here)
