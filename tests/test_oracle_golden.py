@@ -218,3 +218,36 @@ def test_oracle_alif_matches_reference(key):
     dp = z[f"{key}_dp"].astype(np.float64)
     for i in range(4):
         assert abs(pg[i] - dp[i]) <= 1e-5 * (abs(dp[i]) + 1e-3), (i, pg, dp)
+
+
+def test_oracle_alif_reduces_to_hard_reset():
+    """q = 0 and w0 = 0 keep the adaptation at 0 (fl(rho*0) = 0), so ALIF is the
+    hard reset with theta = theta0 bit for bit; and with q = 0, lw never enters
+    lv's recurrence (d = gs), so lv is the hard reset's adjoint."""
+    rng = np.random.default_rng(4)
+    I = (0.12 + 0.4 * rng.standard_normal((600, 11))).astype(np.float32)
+    u0 = (0.3 * rng.standard_normal(11)).astype(np.float32)
+    w0 = np.zeros(11, np.float32)
+    GS = rng.standard_normal((600, 11)).astype(np.float32)
+    U, W, S = O.alif_serial_forward(I, 0.93, 0.97, 0.0, 1.0, -0.1, u0, w0)
+    Uh, Sh = O.serial_forward(I, 0.93, 1.0, -0.1, u0)
+    assert_bit_equal(U, Uh, "U")
+    assert_bit_equal(S, Sh, "S")
+    assert not W.any()
+    LV, _, _, _ = O.alif_serial_backward(I, u0, w0, U, W, S, GS, 0.93, 0.97, 0.0, 1.0, 4.0)
+    Lh = O.serial_backward(I, u0, Uh, Sh, GS, None, 0.93, 1.0, -0.1, 4.0, True)
+    assert rel(LV, Lh) < 1e-6
+
+
+def test_oracle_alif_warm_predict_from_row0_is_exact():
+    """A warm-up that reaches row 0 starts from (u0, w0), so the prediction is
+    the true entry adaptation (lifscan/triton_alif.py:78-79)."""
+    rng = np.random.default_rng(5)
+    T, N, C = 512, 6, 32
+    I = (0.1 + 0.3 * rng.standard_normal((T, N))).astype(np.float32)
+    u0 = np.zeros(N, np.float32)
+    w0 = (0.1 * rng.random(N)).astype(np.float32)
+    _, W, _ = O.alif_serial_forward(I, 0.95, 0.995, 0.9, 1.0, 0.0, u0, w0)
+    WP = O.alif_warm_predict(I, 0.95, 0.995, 0.9, 1.0, 0.0, u0, w0, C, Wn=T // C)
+    want = np.concatenate([w0[None], W[C - 1:-1:C]], 0)
+    assert_bit_equal(WP, want, "WP")
