@@ -170,7 +170,8 @@ def aff_adjoint_v(V, u0, gS, beta, theta, gamma, delta, alpha=4.0, param_grads=T
     u0 = L._cuda_f32("u0", u0, (N,))
     gS = L._cuda_f32("gS", gS, (T, N))
     Lam = torch.empty_like(V)
-    sums = torch.zeros(3, N, dtype=torch.float64, device=V.device) if param_grads else None
+    # every entry is written by the sweep (no clearing launch needed)
+    sums = torch.empty(3, N, dtype=torch.float64, device=V.device) if param_grads else None
     lib = _lib.load()
     with torch.cuda.device(V.device):
         check(lib.lifb_aff_adjoint_v(ptr(V), ptr(u0), ptr(gS), ptr(Lam), ptr(sums) if param_grads else None, T, N,

@@ -673,14 +673,18 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
         dt += (double)tt;
         tb = tr = tq = tt = 0.0f;
     };
-    // one reverse step at row t from the stage's values; returns (lv_t, lw_t)
-    auto step = [&](float x, float up, float wp, float gs, float sread, float &out_lv, float &out_lw) {
+    // the coefficients of row t, which do not depend on (lv, lw): the spike s,
+    // the surrogate sg and c = (1 - s) beta
+    auto coef = [&](float x, float up, float wp, float sread, float &s, float &sg, float &c) {
         const float v = __fadd_rn(__fmul_rn(p.beta, up), x);
-        const float s = READ_S ? sread : (v >= __fadd_rn(p.theta0, wp) ? 1.0f : 0.0f);
+        s = READ_S ? sread : (v >= __fadd_rn(p.theta0, wp) ? 1.0f : 0.0f);
         const float a = (v - p.theta0) - wp;
         const float sig = rcp_approx(1.0f + ex2_approx(-k2 * a));
-        const float sg = alpha * sig * (1.0f - sig);
-        const float c = (1.0f - s) * p.beta;
+        sg = alpha * sig * (1.0f - sig);
+        c = (1.0f - s) * p.beta;
+    };
+    // one reverse step at row t from its coefficients; returns (lv_t, lw_t)
+    auto chain = [&](float s, float sg, float c, float up, float wp, float gs, float &out_lv, float &out_lw) {
         if (MODE == kAlifCompose) {
             const float sgq = sg * p.q;
             m12 = c * m12 + sgq * m22;
@@ -709,6 +713,18 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
         if (fast) {
             float *ov = obuf + (int)(k & 1) * NO * kTile;
             float *ow = ov + kTile;
+            // the whole tile's coefficients first: their exponentials and
+            // reciprocals overlap instead of each sitting in the (lv, lw) chain
+            // behind the previous row's stores
+            float sv[R], sgv[R], cv[R], upv[R], wpv[R], gsv[R];
+#pragma unroll
+            for (int rr = 0; rr < R; rr++) {
+                const int o = rr * NB;
+                upv[rr] = b[kTile + o];
+                wpv[rr] = b[2 * kTile + o];
+                gsv[rr] = b[3 * kTile + o];
+                coef(b[o], upv[rr], wpv[rr], READ_S ? b[4 * kTile + o] : 0.0f, sv[rr], sgv[rr], cv[rr]);
+            }
             if (kOut && k >= 2) {  // the stores issued two tiles ago must have read this buffer
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
@@ -717,7 +733,7 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
             for (int rr = R - 1; rr >= 0; rr--) {
                 const int o = rr * NB;
                 float a, c;
-                step(b[o], b[kTile + o], b[2 * kTile + o], b[3 * kTile + o], READ_S ? b[4 * kTile + o] : 0.0f, a, c);
+                chain(sv[rr], sgv[rr], cv[rr], upv[rr], wpv[rr], gsv[rr], a, c);
                 if (kOut) {
                     ov[o + lane] = a;
                     if (WRITE_LW) ow[o + lane] = c;
@@ -739,8 +755,9 @@ __global__ void __launch_bounds__(32) k_alif_bwd_tma(
                 const int o = rr * NB;
                 const float up = t == 0 ? u00 : b[kTile + o];
                 const float wp = t == 0 ? w00 : b[2 * kTile + o];
-                float a, c;
-                step(b[o], up, wp, b[3 * kTile + o], READ_S ? b[4 * kTile + o] : 0.0f, a, c);
+                float a, c, sp, sg, cf;
+                coef(b[o], up, wp, READ_S ? b[4 * kTile + o] : 0.0f, sp, sg, cf);
+                chain(sp, sg, cf, up, wp, b[3 * kTile + o], a, c);
                 if (kOut && act) {
                     LV[t * N + n] = a;
                     if (WRITE_LW) LW[t * N + n] = c;

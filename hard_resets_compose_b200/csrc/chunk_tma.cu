@@ -269,14 +269,16 @@ __device__ __forceinline__ Vec<NPL> bwd_v(const float *b, int kTile, int off, co
 }
 
 // Coefficients of NPL neurons at in-tile offset `off` (no dependence on lam,
-// so a whole tile is computed ahead of the chain).
+// so a whole tile is computed ahead of the chain); vout, when given, receives
+// the forward's v of the row.
 template <int NPL, bool READ_S, bool HAS_GU, bool FROM_V, bool AFF = false>
 __device__ __forceinline__ void bwd_coef(const float *b, int kTile, int off, Vec<NPL> &a, Vec<NPL> &c, float beta,
                                          float theta, float u_r, float alpha, float k2, float k2t, bool detach,
-                                         float bgamma = 0.0f)
+                                         float bgamma = 0.0f, Vec<NPL> *vout = nullptr)
 {
     using Ly = BwdLayout<READ_S, HAS_GU, FROM_V>;
     const Vec<NPL> v = bwd_v<NPL, FROM_V, Ly>(b, kTile, off, nullptr, beta);
+    if (vout) *vout = v;
     const Vec<NPL> gs = ld_vec<NPL>(b + Ly::kGS * kTile + off);
     Vec<NPL> sv, gu;
     if constexpr (READ_S) sv = ld_vec<NPL>(b + Ly::kS * kTile + off);
@@ -382,9 +384,10 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
     bool ok = true;
     const float k2 = alpha * kLog2e, k2t = k2 * theta, bgamma = beta * gamma;
     // PG: sums of dL/dbeta = sum_t lam_{t+1} u_t (+ lam_0 u0), dL/dgamma =
-    // sum_t s_t v_t beta lam_{t+1}, dL/ddelta = sum_t s_t beta lam_{t+1}, taken
+    // beta sum_t s_t v_t lam_{t+1}, dL/ddelta = beta sum_t s_t lam_{t+1}, taken
     // at row t before lam is stepped (lam then holds lam_{t+1}); each tile's
-    // rows are summed in fp32 (tb, tg, td) and folded into fp64 totals
+    // rows are summed in fp32 (tb, tg, td) and folded into fp64 totals, where
+    // the factor beta of the last two is applied
     double pb[NPL], pgm[NPL], pdl[NPL];
     float tb[NPL], tg[NPL], td[NPL];
 #pragma unroll
@@ -395,17 +398,17 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             const bool spk = v.v[i] >= theta;
             const float u = spk ? __fadd_rn(__fmul_rn(gamma, v.v[i]), delta) : v.v[i];
             tb[i] = fmaf(lam.v[i], u, tb[i]);
-            const float bl = spk ? beta * lam.v[i] : 0.0f;
-            td[i] += bl;
-            tg[i] = fmaf(v.v[i], bl, tg[i]);
+            const float ls = spk ? lam.v[i] : 0.0f;
+            td[i] += ls;
+            tg[i] = fmaf(v.v[i], ls, tg[i]);
         }
     };
     auto pg_fold = [&]() {
 #pragma unroll
         for (int i = 0; i < NPL; i++) {
             pb[i] += (double)tb[i];
-            pgm[i] += (double)tg[i];
-            pdl[i] += (double)td[i];
+            pgm[i] = fma((double)beta, (double)tg[i], pgm[i]);
+            pdl[i] = fma((double)beta, (double)td[i], pdl[i]);
             tb[i] = tg[i] = td[i] = 0.0f;
         }
     };
@@ -419,26 +422,64 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
         if (fast) {
             float *ol = obuf + (int)(k & 1) * kTile;
             Vec<NPL> av[R], cv[R];
+            // PG: the post-reset potential u of every row and the rows that
+            // spiked (bit rr), found with the coefficients, so that the chain
+            // adds one FMA (the dbeta sum) per row
+            Vec<NPL> uv[PG ? R : 1];
+            uint32_t smask[NPL];
 #pragma unroll
-            for (int rr = 0; rr < R; rr++)
-                bwd_coef<NPL, READ_S, HAS_GU, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
-                                                           theta, u_r, alpha, k2, k2t, detach, bgamma);
+            for (int i = 0; i < NPL; i++) smask[i] = 0u;
+            static_assert(!PG || R <= 32, "spike mask holds 32 rows");
+#pragma unroll
+            for (int rr = 0; rr < R; rr++) {
+                if constexpr (PG) {
+                    Vec<NPL> vv;
+                    bwd_coef<NPL, READ_S, HAS_GU, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
+                                                               theta, u_r, alpha, k2, k2t, detach, bgamma, &vv);
+#pragma unroll
+                    for (int i = 0; i < NPL; i++) {
+                        const bool spk = vv.v[i] >= theta;
+                        uv[rr].v[i] = spk ? __fadd_rn(__fmul_rn(gamma, vv.v[i]), delta) : vv.v[i];
+                        smask[i] |= spk ? (1u << rr) : 0u;
+                    }
+                } else {
+                    bwd_coef<NPL, READ_S, HAS_GU, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
+                                                               theta, u_r, alpha, k2, k2t, detach, bgamma);
+                }
+            }
             if (MODE == kReplay && k >= 2) {
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
             }
             const Vec<NPL> pp_in = pp;
+            [[maybe_unused]] const Vec<NPL> lam_in = lam;
 #pragma unroll
             for (int rr = R - 1; rr >= 0; rr--) {
-                if constexpr (PG) pg_row(ld_vec<NPL>(b + Ly::kI * kTile + rr * NB + NPL * lane));
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
+                    if constexpr (PG) tb[i] = fmaf(lam.v[i], uv[rr].v[i], tb[i]);
                     lam.v[i] = cv[rr].v[i] + av[rr].v[i] * lam.v[i];
                     if constexpr (TRACK) pp.v[i] = av[rr].v[i] * pp.v[i];
                 }
                 if (MODE == kReplay) st_vec<NPL>(ol + rr * NB + NPL * lane, lam);
             }
-            if constexpr (PG) pg_fold();
+            if constexpr (PG) {
+                // the spiking rows only (a few per tile): lam_{t+1} is the
+                // tile's next row in ol (this lane's own stores), or the lam
+                // that entered the tile for its top row
+#pragma unroll
+                for (int i = 0; i < NPL; i++) {
+                    uint32_t msk = smask[i];
+                    while (msk) {
+                        const int rr = __ffs(msk) - 1;
+                        msk &= msk - 1u;
+                        const float ln = rr == R - 1 ? lam_in.v[i] : ol[(rr + 1) * NB + NPL * lane + i];
+                        td[i] += ln;
+                        tg[i] = fmaf(b[Ly::kI * kTile + rr * NB + NPL * lane + i], ln, tg[i]);
+                    }
+                }
+                pg_fold();
+            }
             if (TRACK && D) {
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
