@@ -105,15 +105,19 @@ def traffic_per_unit(kernel_key):
 
 
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML during the timed region."""
+    """Samples SM clock and throttle reasons through NVML during the timed
+    region: once on entry, every `period` seconds from a thread, and once on
+    exit, so that even a region of a few milliseconds has samples from its
+    start and its end."""
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
                0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
 
-    def __init__(self, index, period=0.01):
+    def __init__(self, index, period=0.005):
         self.index, self.period = index, period
         self.samples, self.reasons, self.max_mhz = [], set(), None
         self._stop = threading.Event()
+        self._lock = threading.Lock()
         self._t = None
         self.ok = False
         try:
@@ -126,21 +130,26 @@ class ClockSampler:
         except Exception:  # NVML missing: no clock record
             self.ok = False
 
-    def _run(self):
+    def _sample(self):
         nv = self.nv
-        while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if r & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
-            time.sleep(self.period)
+        try:
+            mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:  # a failed query leaves no sample
+            return
+        with self._lock:
+            self.samples.append(mhz)
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.wait(self.period):
+            self._sample()
 
     def __enter__(self):
         if self.ok:
+            self._sample()
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
@@ -149,6 +158,8 @@ class ClockSampler:
         self._stop.set()
         if self._t:
             self._t.join()
+        if self.ok:
+            self._sample()
 
     def record(self):
         if not self.ok or not self.samples:
