@@ -422,10 +422,11 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
         if (fast) {
             float *ol = obuf + (int)(k & 1) * kTile;
             Vec<NPL> av[R], cv[R];
-            // PG: the post-reset potential u of every row and the rows that
-            // spiked (bit rr), found with the coefficients, so that the chain
-            // adds one FMA (the dbeta sum) per row
-            Vec<NPL> uv[PG ? R : 1];
+            // PG: v of every row kept in registers and the rows that spiked
+            // (bit rr), found with the coefficients.  The chain adds one FMA
+            // per row, lam_{t+1} v_t; the spiking rows, where u_t differs from
+            // v_t, add lam_{t+1} (u_t - v_t) to the dbeta sum afterwards
+            Vec<NPL> vk[PG ? R : 1];
             uint32_t smask[NPL];
 #pragma unroll
             for (int i = 0; i < NPL; i++) smask[i] = 0u;
@@ -433,15 +434,10 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
 #pragma unroll
             for (int rr = 0; rr < R; rr++) {
                 if constexpr (PG) {
-                    Vec<NPL> vv;
                     bwd_coef<NPL, READ_S, HAS_GU, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
-                                                               theta, u_r, alpha, k2, k2t, detach, bgamma, &vv);
+                                                               theta, u_r, alpha, k2, k2t, detach, bgamma, &vk[rr]);
 #pragma unroll
-                    for (int i = 0; i < NPL; i++) {
-                        const bool spk = vv.v[i] >= theta;
-                        uv[rr].v[i] = spk ? __fadd_rn(__fmul_rn(gamma, vv.v[i]), delta) : vv.v[i];
-                        smask[i] |= spk ? (1u << rr) : 0u;
-                    }
+                    for (int i = 0; i < NPL; i++) smask[i] |= vk[rr].v[i] >= theta ? (1u << rr) : 0u;
                 } else {
                     bwd_coef<NPL, READ_S, HAS_GU, FROM_V, AFF>(b, kTile, rr * NB + NPL * lane, av[rr], cv[rr], beta,
                                                                theta, u_r, alpha, k2, k2t, detach, bgamma);
@@ -457,7 +453,7 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
             for (int rr = R - 1; rr >= 0; rr--) {
 #pragma unroll
                 for (int i = 0; i < NPL; i++) {
-                    if constexpr (PG) tb[i] = fmaf(lam.v[i], uv[rr].v[i], tb[i]);
+                    if constexpr (PG) tb[i] = fmaf(lam.v[i], vk[rr].v[i], tb[i]);
                     lam.v[i] = cv[rr].v[i] + av[rr].v[i] * lam.v[i];
                     if constexpr (TRACK) pp.v[i] = av[rr].v[i] * pp.v[i];
                 }
@@ -474,8 +470,11 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
                         const int rr = __ffs(msk) - 1;
                         msk &= msk - 1u;
                         const float ln = rr == R - 1 ? lam_in.v[i] : ol[(rr + 1) * NB + NPL * lane + i];
+                        const float v = b[Ly::kI * kTile + rr * NB + NPL * lane + i];
+                        const float u = __fadd_rn(__fmul_rn(gamma, v), delta);
+                        tb[i] = fmaf(ln, __fsub_rn(u, v), tb[i]);
                         td[i] += ln;
-                        tg[i] = fmaf(b[Ly::kI * kTile + rr * NB + NPL * lane + i], ln, tg[i]);
+                        tg[i] = fmaf(v, ln, tg[i]);
                     }
                 }
                 pg_fold();
