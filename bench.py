@@ -375,7 +375,8 @@ def run_reset_family(args, ws, rank, local, family):
     and theta0) at config 2's shape (B*N = 16384 per GPU,
     T = 1024, x ~ N(0.05, 0.2^2), beta = 0.99), issued eagerly; and the exact
     scan forward at T = 2^18, N = 1024 (x ~ N(0.02, 0.1^2)) beside the serial
-    pass it replaces."""
+    pass it replaces (for ALIF also the two-level adjoint with the parameter
+    sums at that length, beside the one reverse sweep)."""
     import torch
 
     from hard_resets_compose_b200 import _lib
@@ -499,6 +500,21 @@ def run_reset_family(args, ws, rank, local, family):
     u0l = torch.zeros(Nl, device=dev)
     ms_serial_long = timed(lambda: serial_long(Il, u0l), 3)
     ms_scan_long = timed(lambda: scan_long(Il, u0l), 3)
+    long_adj = None
+    if family == "alif":
+        # the two-level adjoint with the parameter sums over the long sequence
+        # (chunk maps composed, carried and replayed), beside the one sweep
+        Ul, Wl, _ = AL.alif_serial_forward(Il, BETA, ALIF_RHO, ALIF_Q, 1.0, 0.0, u0l, u0l)
+        GSl = torch.empty(Tl, Nl, device=dev).normal_(0.0, 1.0, generator=gl)
+
+        def adj(chunked):
+            return lambda: AL._alif_bwd(Il, u0l, u0l, Ul, Wl, None, GSl, BETA, ALIF_RHO, ALIF_Q, 1.0, 4.0,
+                                        False, True, chunked=chunked)
+        ms_adj_scan = timed_queued(adj(True), 3)
+        ms_adj_sweep = timed_queued(adj(False), 3)
+        long_adj = {"T": Tl, "N": Nl, "two_level_ms": ms_adj_scan, "one_sweep_ms": ms_adj_sweep,
+                    "two_level_value": Tl * Nl / (ms_adj_scan / 1e3)}
+        del Ul, Wl, GSl
     units = T * N
     if soft:
         metric = "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)"
@@ -530,6 +546,7 @@ def run_reset_family(args, ws, rank, local, family):
                          "unit": "GB/s", "frac": layer_bytes * units / (ms / 1e3) / 1e9 / hbm, "traffic": None},
             "long_scan": {"T": Tl, "N": Nl, "serial_ms": ms_serial_long, "scan_ms": ms_scan_long,
                           "scan_value": Tl * Nl / (ms_scan_long / 1e3)},
+            **({"long_adjoint": long_adj} if long_adj else {}),
             "gpu_launches": launches * args.steps, "clocks": clk.record()}), flush=True)
 
 
