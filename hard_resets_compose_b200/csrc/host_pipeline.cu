@@ -25,13 +25,30 @@ constexpr int kSlots = 3;
 
 struct HostPipe {
     cudaStream_t in = nullptr, out = nullptr;
-    cudaEvent_t ev_in[kSlots], ev_gs[kSlots], ev_fwd[kSlots], ev_done[kSlots], ev_free[kSlots], ev_start, ev_last;
+    cudaEvent_t ev_in[kSlots] = {}, ev_gs[kSlots] = {}, ev_fwd[kSlots] = {}, ev_done[kSlots] = {},
+                ev_free[kSlots] = {}, ev_start = nullptr, ev_last = nullptr;
     bool ready = false;
 };
 HostPipe g_pipe[kMaxDev];
 std::mutex g_pipe_mu;
 
-// Streams and events of the current device, created once (no memory is allocated).
+// Destroys whatever handles of q were created (a set that failed half-way).
+void destroy_pipe(HostPipe &q)
+{
+    if (q.in) cudaStreamDestroy(q.in);
+    if (q.out) cudaStreamDestroy(q.out);
+    cudaEvent_t *sets[] = {q.ev_in, q.ev_gs, q.ev_fwd, q.ev_done, q.ev_free};
+    for (cudaEvent_t *set : sets)
+        for (int i = 0; i < kSlots; i++)
+            if (set[i]) cudaEventDestroy(set[i]);
+    if (q.ev_start) cudaEventDestroy(q.ev_start);
+    if (q.ev_last) cudaEventDestroy(q.ev_last);
+    q = HostPipe{};
+}
+
+// Streams and events of the current device, created once (no memory is
+// allocated); a set that cannot be created completely is released again and
+// the next call tries anew.
 HostPipe *pipe_for_current_device()
 {
     int dev = 0;
@@ -39,20 +56,23 @@ HostPipe *pipe_for_current_device()
     std::lock_guard<std::mutex> g(g_pipe_mu);
     HostPipe &p = g_pipe[dev];
     if (!p.ready) {
-        if (cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
-        if (cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
-        for (int i = 0; i < kSlots; i++) {
-            if (cudaEventCreateWithFlags(&p.ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&p.ev_gs[i], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&p.ev_fwd[i], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&p.ev_done[i], cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&p.ev_free[i], cudaEventDisableTiming) != cudaSuccess)
-                return nullptr;
-        }
-        if (cudaEventCreateWithFlags(&p.ev_last, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&p.ev_start, cudaEventDisableTiming) != cudaSuccess)
+        HostPipe q;
+        bool ok = cudaStreamCreateWithFlags(&q.in, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&q.out, cudaStreamNonBlocking) == cudaSuccess;
+        for (int i = 0; ok && i < kSlots; i++)
+            ok = cudaEventCreateWithFlags(&q.ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&q.ev_gs[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&q.ev_fwd[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&q.ev_done[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&q.ev_free[i], cudaEventDisableTiming) == cudaSuccess;
+        ok = ok && cudaEventCreateWithFlags(&q.ev_last, cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&q.ev_start, cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            destroy_pipe(q);
             return nullptr;
-        p.ready = true;
+        }
+        q.ready = true;
+        p = q;
     }
     return &p;
 }
