@@ -190,41 +190,146 @@ def cpu_oracle_rate(T, N, seconds, want_bwd=True, mu=MU, sd=SD, beta=BETA):
     return done * T * N / el, threads, f"{done} x T={T}, N={N} (serial forward + adjoint) in {el:.1f} s"
 
 
+SOFT_METRIC = "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)"
+AFF_METRIC = "neuron-steps/s, affine-reset layer lif_affine fwd+bwd (B*N=16384/GPU, T=1024)"
+ALIF_METRIC = "neuron-steps/s, ALIF layer alif fwd+bwd (B*N=16384/GPU, T=1024)"
+C3_METRIC = "LIF neuron-steps/s, 700-256-256-20 training step (B=64/GPU, T=1024)"
+C5_METRIC = "neuron-steps/s, lif_tuned fwd+bwd over the config-5 sweep (largest point)"
+
+
+def _reference_network_step(O):
+    """One training step of the config-3 network (700-256-256-20, B = 64,
+    T = 1024, beta = 0.9, Kaiming-uniform Linear layers, leaky readout,
+    cross-entropy, Adam) on the CPU: torch's CPU Linear layers around the
+    oracle's serial LIF forward and adjoint (the C port of lifscan/fast.py).
+    Returns (step function, LIF neuron-steps per step)."""
+    import math
+
+    import numpy as np
+    import torch
+    import torch.nn as nn
+
+    from hard_resets_compose_b200.shdnet import synthetic_batch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+
+    class OracleLIF(torch.autograd.Function):
+        """Hard-reset LIF over [T, M] (spikes out); with theta = inf the
+        leaky integrator (potential out, gradient on the potential)."""
+
+        @staticmethod
+        def forward(ctx, I, beta, theta):
+            x = I.detach().contiguous().numpy()
+            u0 = np.zeros(x.shape[1], np.float32)
+            U, S = O.serial_forward(x, beta, theta, 0.0, u0)
+            ctx.st = (x, u0, U, S, beta, theta)
+            return torch.from_numpy(S if math.isfinite(theta) else U)
+
+        @staticmethod
+        def backward(ctx, g):
+            x, u0, U, S, beta, theta = ctx.st
+            gn = g.detach().contiguous().numpy()
+            if math.isfinite(theta):
+                lam = O.serial_backward(x, u0, U, S, gn, None, beta, theta, 0.0, 4.0, True)
+            else:
+                lam = O.serial_backward(x, u0, U, S, np.zeros_like(gn), gn, beta, theta, 0.0, 4.0, True)
+            return torch.from_numpy(lam), None, None
+
+    T, B, H, beta = 1024, 64, 256, 0.9
+    torch.manual_seed(0)
+    l1, l2, out = nn.Linear(700, H), nn.Linear(H, H), nn.Linear(H, 20)
+    params = list(l1.parameters()) + list(l2.parameters()) + list(out.parameters())
+    opt = torch.optim.Adam(params, lr=1e-3)
+    x, y = synthetic_batch(T, B, seed=1000, device="cpu")
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        s1 = OracleLIF.apply(l1(x).reshape(T, -1), beta, 1.0).reshape(T, B, H)
+        s2 = OracleLIF.apply(l2(s1).reshape(T, -1), beta, 1.0).reshape(T, B, H)
+        z = out(s2)
+        yv = OracleLIF.apply(z.reshape(T, -1), beta, math.inf).reshape(T, B, 20).mean(0)
+        nn.functional.cross_entropy(yv, y).backward()
+        opt.step()
+
+    return step, 2 * B * H * T
+
+
 def run_reference(args, ws, rank):
+    """The reference's CPU path for the chosen workload, on all host threads:
+    the oracle (a C port of lifscan/fast.py and of the reset families' serial
+    recurrences and adjoints) on a bounded sample of the workload, under the
+    same metric as this workload's b200 line."""
     if rank != 0:
         return
     from oracle import oracle as O
     O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
-    if args.workload == "c4":
-        # bounded sample of config 4: the first 2^17 of its 2^20 rows, all 1024 neurons
-        T, N, mu, sd, beta = 1 << 17, C4_N, C4_MU, C4_SD, BETA
-        metric, scaling = C4_METRIC, "strong"
-        workload = C4_WORKLOAD
-        sample = f"first {T} of {C4_T} rows per step (N={N}), serial forward + adjoint"
+    wl = args.workload
+    scaling = "weak"
+    if wl == "c3":
+        one_step, units = _reference_network_step(O)
+        metric = C3_METRIC
+        workload = "c3: 700-256-256-20 training step, B=64, T=1024, beta=0.9, leaky readout, Adam"
+        sample = "the full training step (torch CPU Linear layers, oracle LIF forward and adjoint)"
+        path = "torch CPU Linear layers + CPU oracle port of lifscan/fast.py's serial LIF and adjoint"
     else:
-        T, N, mu, sd, beta = T_STEPS, N_PER_GPU, MU, SD, BETA
-        metric, scaling = METRIC, "weak"
-        workload = "c2: lif_tuned fwd+bwd, B*N=16384, T=1024, beta=0.99, x~N(0.05,0.2^2)"
-        sample = f"full workload per step (T={T}, N={N}), serial forward + adjoint"
-    I, u0, GS = O.gen_inputs(T, N, mu, sd, seed=0, grad=True)
+        if wl == "c4":
+            # bounded sample of config 4: the first 2^17 of its 2^20 rows, all 1024 neurons
+            T, N, mu, sd, beta = 1 << 17, C4_N, C4_MU, C4_SD, BETA
+            metric, scaling, workload = C4_METRIC, "strong", C4_WORKLOAD
+            sample = f"first {T} of {C4_T} rows per step (N={N}), serial forward + adjoint"
+        elif wl == "c5":
+            # bounded sample of the sweep's largest point (B*N = 2^22, T = 4096, beta = 0.99)
+            T, N, mu, sd, beta = 4096, N_PER_GPU, 0.1, 0.3, 0.99
+            metric = C5_METRIC
+            workload = "c5: largest point B*N=2^22, T=4096, beta=0.99, x~N(0.1,0.3^2), fwd+bwd"
+            sample = f"first {N} of {1 << 22} neurons per step (T={T}), serial forward + adjoint"
+        else:
+            T, N, mu, sd, beta = T_STEPS, N_PER_GPU, MU, SD, BETA
+            metric = {"soft": SOFT_METRIC, "affine": AFF_METRIC, "alif": ALIF_METRIC}.get(wl, METRIC)
+            workload = {"soft": "soft: lif_soft fwd+bwd with dbeta, beta=0.99, x~N(0.05,0.2^2)",
+                        "affine": f"affine: lif_affine fwd+bwd with dbeta, dgamma, ddelta, beta=0.99, "
+                                  f"gamma={AFF_GAMMA}, delta={AFF_DELTA}, x~N(0.05,0.2^2)",
+                        "alif": f"alif: alif fwd+bwd with dbeta, drho, dq, dtheta0, beta=0.99, rho={ALIF_RHO}, "
+                                f"q={ALIF_Q}, theta0=1, x~N(0.05,0.2^2)"}.get(
+                wl, "c2: lif_tuned fwd+bwd, B*N=16384, T=1024, beta=0.99, x~N(0.05,0.2^2)")
+            sample = f"full workload per step (T={T}, N={N}), serial forward + adjoint"
+        I, u0, GS = O.gen_inputs(T, N, mu, sd, seed=0, grad=True)
+        if wl in ("soft", "affine"):
+            # the soft reset is the affine reset at gamma = 1, delta = -theta
+            g, d = (1.0, -1.0) if wl == "soft" else (AFF_GAMMA, AFF_DELTA)
+            path = "CPU oracle port of the affine-reset serial recurrence and adjoint with the parameter sums"
+
+            def one_step():
+                U, _ = O.aff_serial_forward(I, beta, 1.0, g, d, u0)
+                O.aff_serial_backward(I, u0, U, GS, beta, 1.0, g, 4.0)
+        elif wl == "alif":
+            path = "CPU oracle port of the ALIF serial recurrence and adjoint with the parameter sums"
+
+            def one_step():
+                U, W, S = O.alif_serial_forward(I, beta, ALIF_RHO, ALIF_Q, 1.0, 0.0, u0, u0)
+                O.alif_serial_backward(I, u0, u0, U, W, S, GS, beta, ALIF_RHO, ALIF_Q, 1.0, 4.0)
+        else:
+            path = "CPU oracle port of lifscan/fast.py serial_forward_nograd + serial_backward"
+
+            def one_step():
+                U, S = O.serial_forward(I, beta, 1.0, 0.0, u0)
+                O.serial_backward(I, u0, U, S, GS, None, beta, 1.0, 0.0, 4.0, True)
+        units = N * T
     for _ in range(max(args.warmup, 0)):
-        U, S = O.serial_forward(I, beta, 1.0, 0.0, u0)
-        O.serial_backward(I, u0, U, S, GS, None, beta, 1.0, 0.0, 4.0, True)
+        one_step()
     ts = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        U, S = O.serial_forward(I, beta, 1.0, 0.0, u0)
-        O.serial_backward(I, u0, U, S, GS, None, beta, 1.0, 0.0, 4.0, True)
+        one_step()
         ts.append(time.perf_counter() - t0)
     ms = 1e3 * sum(ts) / len(ts)
-    value = N * T / (ms / 1e3)
+    value = units / (ms / 1e3)
     cores = O.num_threads()
     line = {
         "impl": "reference", "metric": metric, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload,
-                   "path": "CPU oracle port of lifscan/fast.py serial_forward_nograd + serial_backward"},
+        "config": {"workload": workload, "path": path},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -343,7 +448,7 @@ def run_sweep(args, ws, rank, local):
     head = max(done, key=lambda p: (p["N"] * p["T"], p["beta"])) if done else None
     if rank == 0:
         print(json.dumps({
-            "metric": "neuron-steps/s, lif_tuned fwd+bwd over the config-5 sweep (largest point)",
+            "metric": C5_METRIC,
             "value": head["fwd_bwd_value"] if head else None, "unit": UNIT, "n_gpus": ws, "steps": reps,
             "warmup": 1, "ms_per_step": head["fwd_bwd_ms"] if head else None, "higher_is_better": True,
             "scaling": "weak" if ws > 1 else "strong", "vs_baseline": None, "dtype": "f32",
@@ -517,14 +622,14 @@ def run_reset_family(args, ws, rank, local, family):
         del Ul, Wl, GSl
     units = T * N
     if soft:
-        metric = "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)"
+        metric = SOFT_METRIC
         workload = "soft: lif_soft (gradients for I, u0, beta), beta=0.99, x~N(0.05,0.2^2)"
     elif family == "alif":
-        metric = "neuron-steps/s, ALIF layer alif fwd+bwd (B*N=16384/GPU, T=1024)"
+        metric = ALIF_METRIC
         workload = (f"alif: alif fwd=serial (gradients for I, u0, w0, beta, rho, q, theta0), beta=0.99, "
                     f"rho={ALIF_RHO}, q={ALIF_Q}, theta0=1, x~N(0.05,0.2^2)")
     else:
-        metric = "neuron-steps/s, affine-reset layer lif_affine fwd+bwd (B*N=16384/GPU, T=1024)"
+        metric = AFF_METRIC
         workload = (f"affine: lif_affine mode=serial (gradients for I, u0, beta, gamma, delta), beta=0.99, "
                     f"gamma={AFF_GAMMA}, delta={AFF_DELTA}, x~N(0.05,0.2^2)")
     if rank == 0:
@@ -794,7 +899,7 @@ def run_network(args, ws, rank, local):
     units = 2 * B * H * T * ws  # LIF neuron-steps per step, both layers, all ranks
     if rank == 0:
         print(json.dumps({
-            "metric": "LIF neuron-steps/s, 700-256-256-20 training step (B=64/GPU, T=1024)",
+            "metric": C3_METRIC,
             "value": units / (ms / 1e3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic Bernoulli raster, rates U(0.5%, 4%), 20 labels",
