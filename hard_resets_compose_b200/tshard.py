@@ -341,7 +341,7 @@ def tshard_backward(I, entry, U, GS, ops, comm, beta, timeline=None):
     _mark(timeline, "gather_pq", I)
     top = torch.zeros_like(entry)
     for q in range(R - 1, r, -1):
-        top = g[q, 0] + g[q, 1] * top
+        top = torch.addcmul(g[q, 0], g[q, 1], top)  # q + p * lam_above, one launch
     _mark(timeline, "fold", I)
     Lam = ops.bwd_fix(I, entry, U, GS, top, Lam)
     _mark(timeline, "fix", I)
