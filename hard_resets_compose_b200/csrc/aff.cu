@@ -122,6 +122,7 @@ extern "C" {
 int lifb_aff_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                         float theta, float gamma, float delta, void *stream)
 {
+    LIFB_RANGE("lifb_aff_serial_fwd");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_serial_fwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_serial_fwd: null pointer");
@@ -133,6 +134,7 @@ int lifb_aff_scan_fwd(const float *I, const float *u0, float *U, float *S, int64
                       float theta, float gamma, float delta, int64_t L, int64_t W, void *workspace,
                       size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_aff_scan_fwd");
     if (T < 0 || N < 0 || L <= 0 || W < 0 || (T > 0 && T % L))
         return fail(LIFB_ERR_INVALID_ARGUMENT,
                     "lifb_aff_scan_fwd: T must be a multiple of the segment length L > 0, W >= 0");
@@ -150,6 +152,7 @@ int lifb_aff_scan_fwd(const float *I, const float *u0, float *U, float *S, int64
 int lifb_aff_adjoint(const float *I, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
                      int64_t N, float beta, float theta, float alpha, float gamma, void *stream)
 {
+    LIFB_RANGE("lifb_aff_adjoint");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_adjoint: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_adjoint: null pointer");
@@ -160,6 +163,7 @@ int lifb_aff_adjoint(const float *I, const float *u0, const float *U, const floa
 int lifb_aff_serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N, float beta,
                           float theta, float gamma, float delta, void *stream)
 {
+    LIFB_RANGE("lifb_aff_serial_fwd_v");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_serial_fwd_v: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !V || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_serial_fwd_v: null pointer");
@@ -170,6 +174,7 @@ int lifb_aff_serial_fwd_v(const float *I, const float *u0, float *V, float *S, i
 int lifb_aff_adjoint_v(const float *V, const float *u0, const float *GS, float *Lam, double *param_sums, int64_t T,
                        int64_t N, float beta, float theta, float alpha, float gamma, float delta, void *stream)
 {
+    LIFB_RANGE("lifb_aff_adjoint_v");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_aff_adjoint_v: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!V || !GS || !Lam || (param_sums && !u0))
@@ -181,6 +186,7 @@ int lifb_aff_adjoint_v(const float *V, const float *u0, const float *GS, float *
 
 int lifb_reverse_linear_scan(const float *A, const float *B, float *Out, int64_t T, int64_t N, void *stream)
 {
+    LIFB_RANGE("lifb_reverse_linear_scan");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_reverse_linear_scan: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!A || !B || !Out) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_reverse_linear_scan: null pointer");

@@ -909,6 +909,7 @@ extern "C" {
 int lifb_alif_serial_fwd(const float *I, const float *u0, const float *w0, float *U, float *W, float *S, int64_t T,
                          int64_t N, float beta, float rho, float q, float theta0, float u_r, void *stream)
 {
+    LIFB_RANGE("lifb_alif_serial_fwd");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_serial_fwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !w0 || !U || !W || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_serial_fwd: null pointer");
@@ -926,6 +927,7 @@ int lifb_alif_scan_fwd(const float *I, const float *u0, const float *w0, float *
                        int64_t N, float beta, float rho, float q, float theta0, float u_r, int64_t L, int64_t Wlead,
                        const float *Wpred, int64_t Cpred, void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_alif_scan_fwd");
     if (T < 0 || N < 0 || L <= 0 || Wlead < 0 || (T > 0 && T % L))
         return fail(LIFB_ERR_INVALID_ARGUMENT,
                     "lifb_alif_scan_fwd: T must be a multiple of the segment length L > 0, W >= 0");
@@ -966,6 +968,7 @@ int lifb_alif_warm_predict(const float *I, const float *u0, const float *w0, flo
                            const float *WI, int64_t T, int64_t N, int64_t C, int64_t Wn, float u_init, float w_init,
                            float beta, float rho, float q, float theta0, float u_r, void *stream)
 {
+    LIFB_RANGE("lifb_alif_warm_predict");
     if (T < 0 || N < 0 || C <= 0 || Wn < 0 || T % C)
         return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_warm_predict: T must be a multiple of C > 0, Wn >= 0");
     if (T / C > 65535) return fail(LIFB_ERR_UNSUPPORTED, "lifb_alif_warm_predict: more than 65535 chunks");
@@ -990,6 +993,7 @@ int lifb_alif_bwd_scan(const float *I, const float *u0, const float *w0, const f
                        int64_t T, int64_t N, float beta, float rho, float q, float theta0, float alpha, int64_t C,
                        void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_alif_bwd_scan");
     if (T < 0 || N < 0 || C <= 0 || (T > 0 && T % C))
         return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_bwd_scan: T must be a multiple of the chunk length C > 0");
     if (T / C > 65535) return fail(LIFB_ERR_UNSUPPORTED, "lifb_alif_bwd_scan: more than 65535 chunks");
@@ -1028,6 +1032,7 @@ int lifb_alif_bwd(const float *I, const float *u0, const float *w0, const float 
                   const float *GS, float *LV, float *LW, float *lw_m1, double *param_sums, int64_t T, int64_t N,
                   float beta, float rho, float q, float theta0, float alpha, void *stream)
 {
+    LIFB_RANGE("lifb_alif_bwd");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_bwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !w0 || !U || !W || !GS || !LV) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_alif_bwd: null pointer");

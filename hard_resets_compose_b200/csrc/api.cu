@@ -152,6 +152,7 @@ int lifb_device_status(int reset) { return lifb::read_device_status(reset != 0);
 int lifb_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                     float theta, float u_r, void *stream)
 {
+    LIFB_RANGE("lifb_serial_fwd");
     int st = check_common(I, u0, U, S, T, N);
     if (st) return st;
     if (T == 0 || N == 0) return LIFB_OK;
@@ -163,6 +164,7 @@ int lifb_serial_bwd(const float *I, const float *u0, const float *U, const float
                     const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
                     float alpha, int detach, void *stream)
 {
+    LIFB_RANGE("lifb_serial_bwd");
     int st = check_common(I, u0, U, S, T, N, true);
     if (st) return st;
     if (T == 0 || N == 0) return LIFB_OK;
@@ -194,6 +196,7 @@ int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S, int64_
                      float theta, float u_r, int C, int K, int max_repair, void *workspace,
                      size_t workspace_bytes, lifb_stats *stats_dev, void *stream)
 {
+    LIFB_RANGE("lifb_scan_fwd_v3");
     int st = check_common(I, u0, U, S, T, N);
     if (st) return st;
     int64_t M = 0;
@@ -214,12 +217,22 @@ int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S, int64_
     Carver c(workspace);
     lifb::FwdMaps mp;
     carve_fwd(c, mp, M, N, K);
-    lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
-    lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
+    {
+        LIFB_RANGE("envelope");
+        lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
+    }
+    {
+        LIFB_RANGE("chunk maps");
+        lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
+    }
     if (!stats_dev && max_repair < 0) {
         // Fast path: carry every chunk start, replay segments of G chunks from
         // every G-th start, then fix the few segments whose start was not exact.
-        carry_any(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r, s);
+        {
+            LIFB_RANGE("carry");
+            carry_any(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r, s);
+        }
+        LIFB_RANGE("replay and fix-up");
         const int64_t G = segment_chunks(M, N);
         if (lifb::fwd_replay_tma(I, u0, mp.Starts, U, S, mp.Ends, T, N, (int64_t)C * G, beta, theta, u_r, s, G)) {
             // Lo and MN are free once the maps are built and carried
@@ -228,10 +241,12 @@ int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S, int64_
             return check_launch("lifb_scan_fwd_v3");
         }
     } else {
+        LIFB_RANGE("carry");
         lifb::grid_carry(I, u0, mp.MA, mp.MB, mp.MX, mp.MC, mp.MN, mp.OVF, mp.Starts, N, M, C, K, beta, theta, u_r,
                          s);
     }
     // chunk-level replay and the reference's round-by-round repair (stats, caps on rounds)
+    LIFB_RANGE("replay and repair");
     lifb::grid_replay_repair(I, u0, mp, U, S, T, N, C, max_repair, beta, theta, u_r, stats_dev, s);
     return check_launch("lifb_scan_fwd_v3");
 }
@@ -251,6 +266,7 @@ int lifb_scan_fwd_v4(const float *I, const float *u0, float *U, float *S, int64_
                      float theta, float u_r, int C, int G, int K, int K2, int max_repair, void *workspace,
                      size_t workspace_bytes, lifb_stats *stats_dev, void *stream)
 {
+    LIFB_RANGE("lifb_scan_fwd_v4");
     int st = check_common(I, u0, U, S, T, N);
     if (st) return st;
     int64_t M = 0;
@@ -278,23 +294,40 @@ int lifb_scan_fwd_v4(const float *I, const float *u0, float *U, float *S, int64_
     lifb::SuperMaps sp;
     carve_fwd(c, mp, M, N, K);
     carve_super(c, sp, M2, N, K2);
-    lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
-    lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
-    if (M2c > 0) lifb::grid_compose(mp, sp, u0, M2c, N, G, K, K2, theta, u_r, stats_dev, s);
+    {
+        LIFB_RANGE("envelope");
+        lifb::grid_envelope(I, u0, mp, Mb, N, C, beta, u_r, s);
+    }
+    {
+        LIFB_RANGE("chunk maps");
+        lifb::grid_build(I, u0, mp, Mb, N, C, K, beta, theta, u_r, stats_dev, s);
+    }
+    if (M2c > 0) {
+        LIFB_RANGE("super maps");
+        lifb::grid_compose(mp, sp, u0, M2c, N, G, K, K2, theta, u_r, stats_dev, s);
+    }
     if (!stats_dev && max_repair < 0) {
         // Fast path: carry the super maps, replay each super (C*G rows) from its
         // carried start, then fix the few supers whose start was not exact.
-        carry_any(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2, beta,
-                  theta, u_r, s);
+        {
+            LIFB_RANGE("carry");
+            carry_any(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2,
+                      beta, theta, u_r, s);
+        }
+        LIFB_RANGE("replay and fix-up");
         if (lifb::fwd_replay_tma(I, u0, sp.SStarts, U, S, mp.Ends, T, N, (int64_t)C * G, beta, theta, u_r, s, 1)) {
             lifb::fwd_fixup(I, sp.SStarts, 1, U, S, mp.Ends, mp.Lo, mp.MN, N, M2, (int64_t)C * G, beta, theta, u_r,
                             nullptr, s);
             return check_launch("lifb_scan_fwd_v4");
         }
     }
-    lifb::grid_carry(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2,
-                     beta, theta, u_r, s);
-    lifb::grid_carry_inner(I, mp, sp.SStarts, T, N, C, G, K, beta, theta, u_r, s);
+    {
+        LIFB_RANGE("carry");
+        lifb::grid_carry(I, u0, sp.SA, sp.SB, sp.SX, sp.SC, sp.SN, sp.SOVF, sp.SStarts, N, M2, (int64_t)C * G, K2,
+                         beta, theta, u_r, s);
+        lifb::grid_carry_inner(I, mp, sp.SStarts, T, N, C, G, K, beta, theta, u_r, s);
+    }
+    LIFB_RANGE("replay and repair");
     lifb::grid_replay_repair(I, u0, mp, U, S, T, N, C, max_repair, beta, theta, u_r, stats_dev, s);
     return check_launch("lifb_scan_fwd_v4");
 }
@@ -314,6 +347,7 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
                   const float *GU, float *Lam, int64_t T, int64_t N, float beta, float theta, float u_r,
                   float alpha, int detach, int C, void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_scan_bwd");
     int st = check_common(I, u0, U, S, T, N, true);
     if (st) return st;
     if (C <= 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "chunk length C=%d must be positive", C);
@@ -334,14 +368,20 @@ int lifb_scan_bwd(const float *I, const float *u0, const float *U, const float *
     w.Q = c.take<float>(M * N);
     w.LamEnd = c.take<float>(M * N);
     int32_t *D = reinterpret_cast<int32_t *>(w.LamEnd);  // the fast path needs no LamEnd
-    if (detach &&
-        lifb::bwd_tma(0, I, u0, U, S, GS, GU, nullptr, Lam, w.P, w.Q, T, N, C, beta, theta, u_r, alpha, true,
-                      (cudaStream_t)stream, D)) {
+    bool replayed = false;
+    if (detach) {
+        LIFB_RANGE("chunks from lam_end = 0");
+        replayed = lifb::bwd_tma(0, I, u0, U, S, GS, GU, nullptr, Lam, w.P, w.Q, T, N, C, beta, theta, u_r, alpha,
+                                 true, (cudaStream_t)stream, D);
+    }
+    if (replayed) {
         // Detached reset: every chunk replayed from lam_end = 0 is exact at and
         // below its last spike; the fix-up corrects only the rows above it.
+        LIFB_RANGE("fix-up above the last spikes");
         lifb::bwd_fixup(I, u0, U, S, GS, GU, w.P, w.Q, D, Lam, N, M, C, beta, theta, alpha, (cudaStream_t)stream);
         return check_launch("lifb_scan_bwd");
     }
+    LIFB_RANGE("compose, carry, replay");
     lifb::grid_scan_bwd(I, u0, U, S, GS, GU, Lam, w, T, N, C, beta, theta, u_r, alpha, detach != 0,
                         (cudaStream_t)stream);
     return check_launch("lifb_scan_bwd");
@@ -356,6 +396,7 @@ int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float
                           float *dI_host, float *du0_host, int64_t T, int64_t N, float beta, float theta, float u_r,
                           float alpha, int64_t block_n, void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_lif_fwd_bwd_host");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "negative shape T=%lld N=%lld", (long long)T, (long long)N);
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I_host || !GS_host || !u0_host || !S_host || !dI_host || !du0_host)

@@ -34,6 +34,7 @@ extern "C" {
 int lifb_serial_fwd_v(const float *I, const float *u0, float *V, float *S, int64_t T, int64_t N, float beta,
                       float theta, float u_r, void *stream)
 {
+    LIFB_RANGE("lifb_serial_fwd_v");
     if (T < 0 || N < 0) {
         lifb::set_last_error("lifb_serial_fwd_v: negative size");
         return LIFB_ERR_INVALID_ARGUMENT;
@@ -56,6 +57,7 @@ size_t lifb_lif_bwd_v_workspace_bytes(int64_t T, int64_t N, int C)
 int lifb_lif_bwd_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta, float theta,
                    float alpha, int C, void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_lif_bwd_v");
     if (T < 0 || N < 0 || C <= 0 || (T > 0 && T % C)) {
         lifb::set_last_error("lifb_lif_bwd_v: T must be a multiple of the chunk length C > 0");
         return LIFB_ERR_INVALID_ARGUMENT;

@@ -3,11 +3,27 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include "../../include/lifscan_b200.h"
 
 namespace lifb {
+
+// An NVTX range over a library call or one of its phases, so that profilers
+// which read NVTX attribute each kernel to the call and phase that launched
+// it.  NVTX is header-only here; without an attached tool a range costs one
+// predictable branch.
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+#define LIFB_RANGE_CAT2(a, b) a##b
+#define LIFB_RANGE_CAT(a, b) LIFB_RANGE_CAT2(a, b)
+// Opens a range named `name` until the end of the enclosing scope.
+#define LIFB_RANGE(name) ::lifb::NvtxRange LIFB_RANGE_CAT(lifb_range_, __LINE__)(name)
 
 // Adds n to the library's launch counter (lifb_kernel_launches).
 void count_launches(int n);

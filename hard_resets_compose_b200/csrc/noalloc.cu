@@ -37,6 +37,7 @@ extern "C" int lifb_scan_fwd_v3_noalloc(const float *I, const float *u0, float *
                                         int64_t N, float beta, float theta, float u_r, int C, int K,
                                         int max_repair, lifb_stats *stats_dev, void *stream)
 {
+    LIFB_RANGE("lifb_scan_fwd_v3_noalloc");
     // Size check first: nothing touches the GPU when the request cannot fit.
     const size_t need = lifb_scan_fwd_v3_workspace_bytes(T, N, C, K);
     if (need > (size_t)LIFB_NOALLOC_SCRATCH_BYTES) {

@@ -80,6 +80,7 @@ extern "C" {
 
 int lifb_param_grad_chunks(int64_t T, int64_t N)
 {
+    LIFB_RANGE("lifb_param_grad_chunks");
     if (T <= 0 || N <= 0) return 0;
     // enough (chunk, neuron) threads for ~8 warps per SM, chunks of >= 64 rows
     const int64_t want = (8 * 148 * 32 + N - 1) / N;
@@ -129,6 +130,7 @@ int lifb_param_grad_partials(const float *I, const float *u0, const float *U, co
                              double *partials, int64_t T, int64_t N, float beta, float theta, float alpha, int M,
                              void *stream)
 {
+    LIFB_RANGE("lifb_param_grad_partials");
     return param_partials("lifb_param_grad_partials", false, I, u0, U, GS, Lam, partials, T, N, beta, theta, alpha,
                           M, stream);
 }
@@ -137,6 +139,7 @@ int lifb_aff_param_grad_partials(const float *I, const float *u0, const float *U
                                  double *partials, int64_t T, int64_t N, float beta, float theta, float alpha, int M,
                                  void *stream)
 {
+    LIFB_RANGE("lifb_aff_param_grad_partials");
     return param_partials("lifb_aff_param_grad_partials", true, I, u0, U, GS, Lam, partials, T, N, beta, theta,
                           alpha, M, stream);
 }

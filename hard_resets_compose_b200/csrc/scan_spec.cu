@@ -182,6 +182,7 @@ int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S, int6
                        float theta, float u_r, int64_t L, int64_t W, const float *I_halo, int64_t W_halo,
                        void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_scan_fwd_spec");
     int st = spec_check("lifb_scan_fwd_spec", T, N, L, W, W_halo);
     if (st) return st;
     if (T == 0 || N == 0) return LIFB_OK;
@@ -209,6 +210,7 @@ int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S, int6
 int lifb_scan_fwd_spec_begin(const float *I, int64_t T, int64_t N, float beta, float theta, float u_r, int64_t L,
                              int64_t W, float *end_guess, void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_scan_fwd_spec_begin");
     int st = spec_check("lifb_scan_fwd_spec_begin", T, N, L, W, 0);
     if (st) return st;
     if (T == 0 || N == 0) return LIFB_OK;
@@ -223,6 +225,7 @@ int lifb_scan_fwd_spec_finish(const float *I, const float *u0, float *U, float *
                               float theta, float u_r, int64_t L, void *workspace, size_t workspace_bytes,
                               void *stream)
 {
+    LIFB_RANGE("lifb_scan_fwd_spec_finish");
     int st = spec_check("lifb_scan_fwd_spec_finish", T, N, L, 0, 0);
     if (st) return st;
     if (T == 0 || N == 0) return LIFB_OK;

@@ -51,6 +51,7 @@ extern "C" {
 int lifb_soft_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                          float theta, void *stream)
 {
+    LIFB_RANGE("lifb_soft_serial_fwd");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_fwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !S) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_fwd: null pointer");
@@ -61,6 +62,7 @@ int lifb_soft_serial_fwd(const float *I, const float *u0, float *U, float *S, in
 int lifb_soft_scan_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                        float theta, int64_t L, int64_t W, void *workspace, size_t workspace_bytes, void *stream)
 {
+    LIFB_RANGE("lifb_soft_scan_fwd");
     if (T < 0 || N < 0 || L <= 0 || W < 0 || (T > 0 && T % L))
         return fail(LIFB_ERR_INVALID_ARGUMENT,
                     "lifb_soft_scan_fwd: T must be a multiple of the segment length L > 0, W >= 0");
@@ -77,6 +79,7 @@ int lifb_soft_scan_fwd(const float *I, const float *u0, float *U, float *S, int6
 int lifb_soft_serial_bwd(const float *I, const float *u0, const float *U, const float *GS, float *Lam, int64_t T,
                          int64_t N, float beta, float theta, float alpha, void *stream)
 {
+    LIFB_RANGE("lifb_soft_serial_bwd");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_bwd: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!I || !u0 || !U || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_serial_bwd: null pointer");
@@ -87,6 +90,7 @@ int lifb_soft_serial_bwd(const float *I, const float *u0, const float *U, const 
 int lifb_soft_adjoint_v(const float *V, const float *GS, float *Lam, int64_t T, int64_t N, float beta, float theta,
                         float alpha, void *stream)
 {
+    LIFB_RANGE("lifb_soft_adjoint_v");
     if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_adjoint_v: negative size");
     if (T == 0 || N == 0) return LIFB_OK;
     if (!V || !GS || !Lam) return fail(LIFB_ERR_INVALID_ARGUMENT, "lifb_soft_adjoint_v: null pointer");

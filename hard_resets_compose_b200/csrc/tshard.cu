@@ -180,6 +180,7 @@ size_t lifb_tshard_workspace_bytes(int64_t T, int64_t N, int C, int G, int K, in
 int lifb_tshard_envelope(const float *I, int64_t T, int64_t N, int C, int G, int K, int K2, float beta, float u_r,
                          float *env, void *ws, size_t bytes, void *stream)
 {
+    LIFB_RANGE("lifb_tshard_envelope");
     int st = ts_args(T, N, C, G, K, K2, ws, bytes);
     if (st) return st;
     TsLayout L = ts_layout(ws, T, N, C, G, K, K2);
@@ -194,6 +195,7 @@ int lifb_tshard_slice_map(const float *I, const float *envs, int rank, const flo
                           float beta, float theta, float u_r, int C, int G, int K, int K2, int K3, float *map, void *ws,
                           size_t bytes, void *stream)
 {
+    LIFB_RANGE("lifb_tshard_slice_map");
     int st = ts_args(T, N, C, G, K, K2, ws, bytes);
     if (st) return st;
     if (K3 < 1 || K3 > 64) return ts_fail(LIFB_ERR_INVALID_ARGUMENT, "time-sharded scan: K3 must be in 1..64");
@@ -225,6 +227,7 @@ int lifb_tshard_apply(const float *I, const float *maps, int rank, int K3, const
                       float *S, float *end, int64_t T, int64_t N, float beta, float theta, float u_r, int C, int G,
                       int K, int K2, void *ws, size_t bytes, void *stream)
 {
+    LIFB_RANGE("lifb_tshard_apply");
     int st = ts_args(T, N, C, G, K, K2, ws, bytes);
     if (st) return st;
     TsLayout L = ts_layout(ws, T, N, C, G, K, K2);
@@ -250,6 +253,7 @@ int lifb_tshard_apply(const float *I, const float *maps, int rank, int K3, const
 int lifb_tshard_repair(const float *I, const float *entry, float *U, float *S, float *end, int32_t *changed,
                        int64_t T, int64_t N, float beta, float theta, float u_r, void *stream)
 {
+    LIFB_RANGE("lifb_tshard_repair");
     if (T <= 0 || N <= 0) return ts_fail(LIFB_ERR_INVALID_ARGUMENT, "time-sharded repair: empty slice");
     lifb::entry_repair(I, entry, U, S, end, changed, T, N, beta, theta, u_r, (cudaStream_t)stream);
     return ts_check("lifb_tshard_repair");
@@ -265,6 +269,7 @@ int lifb_tshard_bwd(const float *I, const float *u_prev, const float *U, const f
                     int64_t T, int64_t N, float beta, float theta, float u_r, float alpha, int C, void *ws,
                     size_t bytes, void *stream)
 {
+    LIFB_RANGE("lifb_tshard_bwd");
     if (T <= 0 || N <= 0 || C <= 0 || T % C)
         return ts_fail(LIFB_ERR_INVALID_ARGUMENT, "time-sharded adjoint: T must be a positive multiple of C");
     if (T / C > 65535) return ts_fail(LIFB_ERR_UNSUPPORTED, "time-sharded adjoint: more than 65535 chunks per slice");
@@ -295,6 +300,7 @@ int lifb_tshard_bwd_fix(const float *I, const float *u_prev, const float *U, con
                         float *Lam, int64_t T, int64_t N, float beta, float theta, float alpha, int C, void *ws,
                         size_t bytes, void *stream)
 {
+    LIFB_RANGE("lifb_tshard_bwd_fix");
     if (T <= 0 || N <= 0 || C <= 0 || T % C)
         return ts_fail(LIFB_ERR_INVALID_ARGUMENT, "time-sharded adjoint: T must be a positive multiple of C");
     if (!ws || (uintptr_t)ws % kAl || bytes < lifb_tshard_bwd_workspace_bytes(T, N, C))

@@ -252,7 +252,11 @@ class CudaSliceOps:
 
 
 def _mark(timeline, name, ref):
-    """Appends (name, CUDA event recorded now on ref's stream) when timing."""
+    """Marks the end of a protocol phase: an NVTX marker for profilers (CUDA
+    tensors only), and, when timing, (name, CUDA event recorded now on ref's
+    stream) appended to the timeline."""
+    if ref.is_cuda:
+        torch.cuda.nvtx.mark(name)
     if timeline is not None:
         e = torch.cuda.Event(enable_timing=True)
         e.record(torch.cuda.current_stream(ref.device))
