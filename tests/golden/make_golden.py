@@ -27,7 +27,12 @@ It imports the reference's own code:
     alif_scan_forward with warm-up predictions, alif_warm_predict and
     alif_backward (serial and scan; interpreted), and ALIFFn's gradients, over
     the neuron classes of tests/test_alif.py -> tests/golden/alif_grid.npz
-    (`--alif-only`).
+    (`--alif-only`);
+  * near-threshold stress inputs (the method of experiments/e2b_stress.py,
+    plus exact fp32 ties v == theta): fast.py's serial forward and its pruned
+    scan with repair, and the Triton scan_forward_v3 / v4 with repair and their
+    stats (interpreted) -> tests/golden/stress_near_threshold.npz
+    (`--stress-only`).
 
 Inputs are drawn on the CPU with torch.Generator (tests/test_fast.py:7-9) and
 stored in the fixture too.  The GPU box never runs this script; the tests read
@@ -258,8 +263,70 @@ def alif_cases():
     np.savez_compressed(os.path.join(HERE, "alif_grid.npz"), **npy(out))
 
 
+def stress_inputs(T, N, beta, eps, p_hit, seed, tie32=False):
+    """Near-threshold stress inputs for theta = 1, u_r = 0, u0 = 0.  The drive
+    is x ~ N(0.15, 0.4^2).  With probability p_hit per (t, n) x_t is replaced:
+      tie32=False (experiments/e2b_stress.py:10-17): in float64, by the value
+        that puts the float64 serial pre-reset potential within +-eps of
+        theta; the fp32 copy then lands within an ulp or two of it;
+      tie32=True: in fp32, by theta - fl(beta*u), so that the fp32 serial
+        potential fl(fl(beta*u) + x) equals theta exactly wherever that
+        difference is exact (a spike decided by >= alone)."""
+    g = torch.Generator().manual_seed(seed)
+    dt = torch.float32 if tie32 else torch.float64
+    I = (0.15 + 0.4 * torch.randn(T, N, dtype=torch.float64, generator=g)).to(dt)
+    hit = torch.rand(T, N, generator=g) < p_hit
+    u = torch.zeros(N, dtype=dt)
+    for t in range(T):
+        if tie32:
+            tgt = torch.ones(N, dtype=dt) - beta * u  # fp32: fl(1 - fl(beta*u))
+        else:
+            tgt = 1.0 + eps * (2 * torch.rand(N, dtype=dt, generator=g) - 1) - beta * u
+        I[t] = torch.where(hit[t], tgt, I[t])
+        v = beta * u + I[t]
+        u = torch.where(v >= 1.0, torch.zeros_like(v), v)
+    return I.to(torch.float32).contiguous()
+
+
+STRESS_CASES = [  # name, T, N, beta, eps, p_hit, seed, tie32
+    ("b09_e1e-6", 512, 32, 0.9, 1e-6, 0.3, 31, False),
+    ("b099_e1e-7", 512, 32, 0.99, 1e-7, 0.3, 32, False),
+    ("b099_tie", 512, 32, 0.99, 0.0, 0.3, 33, True),
+    ("b09_tie", 512, 32, 0.9, 0.0, 0.3, 34, True),
+]
+
+
+def stress_cases():
+    theta, u_r = 1.0, 0.0
+    out = {}
+    for (name, T, N, beta, eps, p_hit, seed, tie32) in STRESS_CASES:
+        I = stress_inputs(T, N, beta, eps, p_hit, seed, tie32)
+        u0 = torch.zeros(N)
+        us, ss, vs = fast.serial_forward_nograd(I, beta, theta, u_r, u0)
+        stp = {}
+        Up, Sp = fast.scan_forward_pruned(I, beta, theta, u_r, u0, C=64, K=64, repair=10 ** 6, stats=stp)[:2]
+        assert torch.equal(Up, us) and torch.equal(Sp, ss), name
+        st3, st4 = {}, {}
+        U3, S3 = L.scan_forward_v3(I, beta, theta, u_r, u0, C=64, K=16, repair=10 ** 6, stats=st3)
+        U4, S4 = L.scan_forward_v4(I, beta, theta, u_r, u0, C=32, G=4, K=16, K2=32, repair=10 ** 6, stats=st4)
+        assert torch.equal(U3, us) and torch.equal(S3, ss) and torch.equal(U4, us) and torch.equal(S4, ss), name
+        ties = int((vs == theta).sum())
+        out.update({f"{name}_I": I, f"{name}_U": us, f"{name}_S": ss,
+                    f"{name}_params": np.array([beta, theta, u_r], np.float64),
+                    f"{name}_v3_keys": np.array(sorted(st3)),
+                    f"{name}_v3_vals": np.array([st3[k] for k in sorted(st3)], np.float64),
+                    f"{name}_v4_keys": np.array(sorted(st4)),
+                    f"{name}_v4_vals": np.array([st4[k] for k in sorted(st4)], np.float64),
+                    f"{name}_ties": np.array(ties)})
+        print(name, "exact ties", ties, "v3", st3, "v4", st4, "pruned repair", stp.get("repair_iters"))
+    np.savez_compressed(os.path.join(HERE, "stress_near_threshold.npz"), **npy(out))
+
+
 def main():
     theta = 1.0
+    if "--stress-only" in sys.argv:
+        stress_cases()
+        return
     if "--alif-only" in sys.argv:
         alif_cases()
         return
@@ -272,6 +339,7 @@ def main():
     soft_cases()
     affine_cases()
     alif_cases()
+    stress_cases()
     for (name, T, N, mu, sd, seed, u0_sd, beta, u_r, C, K) in FWD_CASES:
         I, u0, _ = gen(T, N, mu, sd, seed, u0_sd)
         us, ss, vs = fast.serial_forward_nograd(I, beta, theta, u_r, u0)
