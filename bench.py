@@ -482,6 +482,8 @@ def run_reset_family(args, ws, rank, local, family):
     scan forward at T = 2^18, N = 1024 (x ~ N(0.02, 0.1^2)) beside the serial
     pass it replaces (for ALIF also the two-level adjoint with the parameter
     sums at that length, beside the one reverse sweep)."""
+    if rank != 0:
+        return  # one-GPU workload: under torchrun only rank 0 measures (its line says n_gpus = 1)
     import torch
 
     from hard_resets_compose_b200 import _lib
@@ -635,10 +637,10 @@ def run_reset_family(args, ws, rank, local, family):
     if rank == 0:
         print(json.dumps({
             "metric": metric,
-            "value": units / (ms / 1e3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "value": units / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded CUDA torch.Generator, config 2 shape)",
-            "config": {"workload": workload,
+            "config": {"workload": workload, "gpus": f"one GPU (rank 0 of {ws})" if ws > 1 else "one GPU",
                        "step": "forward + torch.autograd.backward, issued eagerly (host overhead included)",
                        "l2": "flushed before every timed call (256 MiB written, 256 MiB read)"},
             "fwd": {"ms": ms_f, "bytes_per_unit": fwd_bytes, "gbs": fwd_bytes * units / (ms_f / 1e3) / 1e9,
