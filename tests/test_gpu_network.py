@@ -2,8 +2,6 @@
 against the same network with a plain PyTorch fp32 serial LIF loop on the
 same device: identical weights and GEMMs, so spikes must be bit-equal and
 every parameter gradient within 1e-5 relative."""
-import math
-
 import pytest
 import torch
 import torch.nn as nn
