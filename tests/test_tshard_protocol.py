@@ -1,5 +1,5 @@
 """Host protocol of the time-sharded scan on CPU: ranks as gloo processes
-(world size 2 and 4) and as threads, with the oracle standing in for the
+(world size 2 and 4) and as threads (2 to 8 ranks), with the oracle standing in for the
 per-slice GPU phases (tests/tshard_oracle_ops.py).  The slices' U and S must
 equal the serial recurrence over the whole sequence bit for bit, and the
 gradients its adjoint within 1e-5, whatever the entry guesses were; a rank
@@ -65,7 +65,7 @@ def _check(case, world, results):
 
 @pytest.mark.parametrize("mode", ("maps", "corrupt", "speculate"))
 @pytest.mark.parametrize("case", sorted(CASES))
-@pytest.mark.parametrize("world", (2, 3, 4))
+@pytest.mark.parametrize("world", (2, 3, 4, 6, 8))
 def test_protocol_threads(case, mode, world):
     from hard_resets_compose_b200 import tshard
     infos = [dict() for _ in range(world)]
