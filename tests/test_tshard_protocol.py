@@ -7,6 +7,7 @@ that drops out makes the others fail instead of hang."""
 import datetime
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -32,14 +33,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _slice_run(comm, case, mode, info):
+def _slice_run(comm, case, mode, info, K=8, K3=32):
     """mode: "maps" (oracle slice maps), "corrupt" (maps that guess 0.5) or
-    "speculate" (no maps, every later slice starts from u_r)."""
+    "speculate" (no maps, every later slice starts from u_r); K, K3: chunk
+    and slice map capacities."""
     from hard_resets_compose_b200 import tshard
     T_total, N, mu, sd, beta = CASES[case]
     I, u0, GS = gen(T_total, N, mu, sd, seed=3, u0_sd=0.3, grad=True)
     a, b = tshard.slice_rows(T_total, comm.world, comm.rank)
-    ops = OracleSliceOps(b - a, N, beta, 1.0, 0.0, C=64, K=8, K3=32, mode="corrupt" if mode == "corrupt" else "maps")
+    ops = OracleSliceOps(b - a, N, beta, 1.0, 0.0, C=64, K=K, K3=K3, mode="corrupt" if mode == "corrupt" else "maps")
     It, u0t, Gt = (torch.from_numpy(np.ascontiguousarray(x)) for x in (I[a:b], u0, GS[a:b]))
     U, S, entry = tshard.tshard_forward(It, u0t, ops, comm, info=info,
                                         entry_mode="speculate" if mode == "speculate" else "maps")
@@ -136,3 +138,44 @@ def test_thread_rank_failure_propagates():
 
     with pytest.raises(RuntimeError, match="rank 2 failed"):
         tshard.run_local(3, fn)
+
+
+class _LateComm:
+    """A comm whose rank enters every exchange `delay` seconds late (a slow
+    rank, injected on the host)."""
+
+    def __init__(self, comm, delay):
+        self.comm, self.delay = comm, delay
+        self.world, self.rank = comm.world, comm.rank
+
+    def all_gather(self, t):
+        time.sleep(self.delay)
+        return self.comm.all_gather(t)
+
+    def shift(self, t):
+        time.sleep(self.delay)
+        return self.comm.shift(t)
+
+
+@pytest.mark.parametrize("mode", ("maps", "speculate"))
+def test_slow_rank_changes_nothing(mode):
+    """One rank reaches every exchange late: the others wait for it at the
+    collective, and the result is the same bits."""
+    from hard_resets_compose_b200 import tshard
+    world = 4
+    res = tshard.run_local(world, lambda c: _slice_run(_LateComm(c, 0.05 if c.rank == 2 else 0.0), "c4like",
+                                                       mode, {}))
+    _check("c4like", world, res)
+
+
+@pytest.mark.parametrize("world", (2, 4))
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_overflowing_maps_stay_exact(case, world):
+    """Chunk and slice maps of capacity 1 overflow almost everywhere; an
+    overflowed slice map is only a worse entry guess, which the repair rounds
+    correct."""
+    from hard_resets_compose_b200 import tshard
+    infos = [dict() for _ in range(world)]
+    res = tshard.run_local(world, lambda c: _slice_run(c, case, "maps", infos[c.rank], K=1, K3=1))
+    _check(case, world, res)
+    assert infos[0]["repair_rounds"] <= world - 1
