@@ -52,3 +52,23 @@ def test_header_compiles_as_c_and_links(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
     assert r.stdout.startswith("ok ") and lib.lifb_status_string(3).decode() in r.stdout
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc is not installed")
+def test_integration_c_example_compiles_and_links(tmp_path):
+    """The C caller shown in INTEGRATION.md compiles with warnings as errors and
+    links against liblifb.so and the CUDA runtime (running it needs a GPU)."""
+    import re
+    _lib.load()
+    libdir = os.path.dirname(_lib._build.LIB)
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    blocks = re.findall(r"```c\n(.*?)```", text, flags=re.S)
+    assert len(blocks) == 1, "INTEGRATION.md should hold one C example"
+    src = tmp_path / "lif.c"
+    src.write_text(blocks[0])
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cmd = ["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+           "-I", os.path.join(cuda, "include"), str(src), "-o", str(tmp_path / "lif"), "-L", libdir, "-llifb",
+           "-L", os.path.join(cuda, "lib64"), "-lcudart", f"-Wl,-rpath,{libdir}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
