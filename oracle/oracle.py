@@ -65,8 +65,6 @@ def lib():
             build()
         L = ctypes.CDLL(_LIB_PATH)
         L.oracle_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float]
-        L.oracle_serial_fwd_cols.argtypes = [f32p, f32p, f32p, f32p, i64, i64, i64, i64,
-                                             c_float, c_float, c_float]
         L.oracle_soft_serial_fwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float]
         L.oracle_soft_serial_bwd.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, i64, c_float, c_float, c_float,
                                              c_int]
@@ -135,12 +133,6 @@ def serial_forward(I, beta, theta, u_r, u0, want_v=False):
     V = np.empty_like(I) if want_v else None
     lib().oracle_serial_fwd(_p(I), _p(u0), _p(U), _p(S), _p(V), T, N, beta, theta, u_r)
     return (U, S, V) if want_v else (U, S)
-
-
-def serial_forward_cols(I, u0, U, S, n0, n1, beta, theta, u_r):
-    """Serial forward over columns [n0, n1) into preallocated U, S (bench sample)."""
-    T, N = I.shape
-    lib().oracle_serial_fwd_cols(_p(I), _p(u0), _p(U), _p(S), T, N, n0, n1, beta, theta, u_r)
 
 
 def serial_backward(I, u0, U, S, GS, GU, beta, theta, u_r, alpha=4.0, detach=True):
