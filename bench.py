@@ -51,6 +51,9 @@ C4_T, C4_N, C4_MU, C4_SD = 1 << 20, 1024, 0.02, 0.1
 C4_METRIC = "neuron-steps/s, fwd+bwd of one sequence (B*N=1024, T=2^20)"
 C4_WORKLOAD = "c4: T=2^20, B*N=1024, beta=0.99, x~N(0.02,0.1^2), forward + backward"
 L2_FLUSH_BYTES = 256 << 20
+C1_T, C1_N, C1_BETA, C1_MU, C1_SD = 1024, 4096, 0.9, 0.1, 0.3
+C1_METRIC = "neuron-steps/s, scan forward (B*N=4096/GPU, T=1024)"
+C1_WORKLOAD = "c1: scan forward, B*N=4096 per GPU (B=16 x 256), T=1024, beta=0.9, x~N(0.1,0.3^2)"
 
 
 def parse():
@@ -63,9 +66,12 @@ def parse():
                    help="lif_tuned mode (default: the reference's default, scan)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-tshard", action="store_true",
+                   help="under torchrun, skip the config-4 time-sharded parity check and timing of the default run")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--workload", default="c2", choices=("c2", "c3", "c4", "c5", "soft", "affine", "alif"),
-                   help="c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step; "
+    p.add_argument("--workload", default="c2", choices=("c1", "c2", "c3", "c4", "c5", "soft", "affine", "alif"),
+                   help="c1: the scan forward of config 1 (B*N=4096, T=1024); "
+                        "c2: lif_tuned fwd+bwd (the headline); c3: 700-256-256-20 network training step; "
                         "c4: T=2^20, B*N=1024 fwd+bwd, time-sharded over the GPUs; c5: sweep of B*N, T, beta; "
                         "soft: the soft-reset fitting layer (lif_soft) at config 2's shape and a long soft scan; "
                         "affine: the affine-reset layer (lif_affine) at config 2's shape and a long affine scan; "
@@ -265,7 +271,17 @@ def run_reference(args, ws, rank):
     O.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
     wl = args.workload
     scaling = "weak"
-    if wl == "c3":
+    if wl == "c1":
+        T, N = C1_T, C1_N
+        I, u0 = O.gen_inputs(T, N, C1_MU, C1_SD, seed=0)
+
+        def one_step():
+            O.serial_forward(I, C1_BETA, 1.0, 0.0, u0)
+        units = N * T
+        metric, workload = C1_METRIC, C1_WORKLOAD
+        sample = f"full workload per step (T={T}, N={N}), serial forward"
+        path = "CPU oracle port of lifscan/fast.py serial_forward_nograd"
+    elif wl == "c3":
         one_step, units = _reference_network_step(O)
         metric = C3_METRIC
         workload = "c3: 700-256-256-20 training step, B=64, T=1024, beta=0.9, leaky readout, Adam"
@@ -334,6 +350,178 @@ def run_reference(args, ws, rank):
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_c1(args, ws, rank, local):
+    """Config 1: the scan forward (spikes and membrane potentials) of
+    B*N = 4096 neurons per GPU over T = 1024 rows, x ~ N(0.1, 0.3^2),
+    beta = 0.9, u0 = 0.  The step is scan_forward_auto, the library's path
+    for this shape; the map scan (scan_forward_v3 with the reference's C = 64,
+    K = 16: the block-level kernel), the lead-in block scan and the single
+    serial pass are timed beside it.  Batch-sharded under torchrun (weak
+    scaling, no collective).  Every path is checked bit for bit against the
+    serial pass on the device before timing."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200 import lifscan as L
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+    T, N, beta = C1_T, C1_N, C1_BETA
+    g = torch.Generator().manual_seed(100 + rank)
+    I_h = (C1_MU + C1_SD * torch.randn(T, N, generator=g)).float()
+    u0_h = torch.zeros(N)
+    I = I_h.to(dev)
+    u0 = u0_h.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    evict = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if ws == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    paths = {
+        "auto": lambda: L.scan_forward_auto(I, beta, 1.0, 0.0, u0),
+        "map_scan_v3_C64_K16": lambda: L.scan_forward_v3(I, beta, 1.0, 0.0, u0, C=64, K=16),
+        "serial": lambda: L.serial_forward(I, beta, 1.0, 0.0, u0),
+    }
+    Lb, Wb = L.block_leadin(T, N, beta)
+    if Lb:
+        paths[f"leadin_block_L{Lb}_W{Wb}"] = lambda: L.scan_forward_spec(I, beta, 1.0, 0.0, u0, L=Lb, W=Wb)
+    Us, Ss = paths["serial"]()
+    parity = True
+    for name, fn in paths.items():
+        U_, S_ = fn()
+        parity &= bool(torch.equal(U_.view(torch.int32), Us.view(torch.int32)) and
+                       torch.equal(S_.view(torch.int32), Ss.view(torch.int32)))
+    del U_, S_
+
+    def timed(fn, steps, launches_per_call):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        for a, b in evs:
+            flush.fill_(1.0)
+            torch.sum(evict, dim=0, out=sink)
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = sorted(a.elapsed_time(b) for a, b in evs)
+        return sum(ms) / len(ms), launches_per_call * steps
+
+    def graphed(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        n0 = lib.lifb_kernel_launches()
+        with torch.cuda.graph(gr):
+            fn()
+        n1 = lib.lifb_kernel_launches()
+        torch.cuda.synchronize(dev)
+        return gr, n1 - n0
+
+    for _ in range(max(args.warmup, 3)):
+        for fn in paths.values():
+            fn()
+    torch.cuda.synchronize(dev)
+    graphs = {k: graphed(fn) for k, fn in paths.items()}
+    per_path = {}
+    clk_rec = None
+    for k, (gr, nl) in graphs.items():
+        for _ in range(3):
+            gr.replay()
+        if k == "auto":
+            with ClockSampler(local) as clk:
+                ms, launches = timed(gr.replay, args.steps, nl)
+            clk_rec = clk.record()
+        else:
+            ms, _ = timed(gr.replay, args.steps, nl)
+        ms = max_over_ranks(ms)
+        per_path[k] = {"ms": ms, "value": N * T * ws / (ms / 1e3), "launches_per_call": nl,
+                       "gbs": FWD_BYTES * N * T / (ms / 1e3) / 1e9}
+    ms = per_path["auto"]["ms"]
+    units = N * T * ws
+    value = units / (ms / 1e3)
+    hbm, peak_kind = peaks()
+    for v in per_path.values():
+        v["frac"] = v["gbs"] / hbm
+    tpu = traffic_per_unit("c1_auto")
+    roofline = {"bound": "hbm", "kernel": "scan_forward_auto at config 1 (its launches: "
+                f"{per_path['auto']['launches_per_call']})", "achieved": per_path["auto"]["gbs"], "peak": hbm,
+                "peak_source": peak_kind, "unit": "GB/s", "frac": per_path["auto"]["frac"],
+                "traffic": (tpu * N * T) if tpu is not None else None, "algorithmic_bytes": FWD_BYTES * N * T}
+
+    e2e = None
+    if not args.no_e2e:
+        I_pin = I_h.pin_memory()
+        U_pin = torch.empty(T, N).pin_memory()
+        S_pin = torch.empty(T, N).pin_memory()
+
+        def e2e_step():
+            Id = I_pin.to(dev, non_blocking=True)
+            U_, S_ = L.scan_forward_auto(Id, beta, 1.0, 0.0, u0)
+            U_pin.copy_(U_, non_blocking=True)
+            S_pin.copy_(S_, non_blocking=True)
+        for _ in range(3):
+            e2e_step()
+        n_e = max(args.steps // 2, 5)
+        ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_e)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        for a, b in ee:
+            a.record(stream)
+            e2e_step()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms_e = max_over_ranks(sum(a.elapsed_time(b) for a, b in ee) / n_e)
+        e2e = {"value": units / (ms_e / 1e3), "unit": UNIT, "ms_per_step": ms_e,
+               "h2d_bytes_per_step": T * N * 4, "d2h_bytes_per_step": 2 * T * N * 4,
+               "api": "pinned host I -> .to(cuda) -> scan_forward_auto -> U, S copied to pinned host buffers"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        v, threads, sample = cpu_oracle_rate(T, N, args.cpu_seconds, want_bwd=False, mu=C1_MU, sd=C1_SD, beta=beta)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": sample.replace("serial forward + adjoint", "serial forward")}
+    if rank == 0:
+        print(json.dumps({
+            "metric": C1_METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch.Generator, config 1 shape)",
+            "config": {"workload": C1_WORKLOAD, "global_neurons": N * ws, "seq_len": T,
+                       "parallelism": f"batch-sharded x{ws}, no collective",
+                       "step": "scan_forward_auto, captured in a CUDA graph and replayed",
+                       "l2": "flushed between steps outside the events (256 MiB written, then 256 MiB read)"},
+            "parity_bit_exact_vs_serial": parity, "paths": per_path,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clk_rec}), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_sweep(args, ws, rank, local):
@@ -816,6 +1004,128 @@ def run_long(args, ws, rank, local):
         dist.destroy_process_group()
 
 
+def c4_time_sharded(args, ws, rank, dev, lib):
+    """Under torchrun (ws > 1) the default run also runs config 4's
+    time-sharded scan (lif_tshard: rank r owns rows [r*T/ws, (r+1)*T/ws) of
+    the 2^20-row sequence) and checks it against the whole sequence through
+    single-GPU lif_tuned on every rank: U and S of the rank's rows bit for bit,
+    dI within 1e-5 relative over all ranks, du0 within 1e-5.  Returns
+    (tshard_parity, c4_tshard) for the JSON line: the parity verdict (every
+    rank agreeing) and the timings (step max over ranks, per-phase maxima, the
+    1-GPU step and the strong-scaling efficiency against it)."""
+    import torch
+    import torch.distributed as dist
+
+    from hard_resets_compose_b200 import lifscan as L
+    from hard_resets_compose_b200 import tshard
+
+    stream = torch.cuda.current_stream(dev)
+    N, T = C4_N, C4_T
+    Ts = T // ws
+    r0, r1 = rank * Ts, (rank + 1) * Ts
+    g = torch.Generator(device=dev).manual_seed(4000)  # the same sequence on every rank
+    I = (C4_MU + C4_SD * torch.randn(T, N, generator=g, device=dev)).float()
+    GS = torch.randn(T, N, generator=g, device=dev).float()
+    u0 = torch.zeros(N, device=dev)
+
+    def all_max(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_sum(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def event_ms(fn, steps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        for a, b in evs:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+    # the whole sequence on this GPU: lif_tuned's forward potentials and gradients
+    U1, S1 = L.scan_forward_auto(I, BETA, 1.0, 0.0, u0)
+    Iq = I.clone().requires_grad_(True)
+    u0q = u0.clone().requires_grad_(True)
+
+    def step1():
+        Iq.grad = None
+        u0q.grad = None
+        S_ = L.lif_tuned(Iq, u0q, beta=BETA, mode="scan")
+        torch.autograd.backward(S_, GS)
+        return S_
+    S_layer = step1()
+    s_layer_ok = bool(torch.equal(S_layer.detach().view(torch.int32), S1.view(torch.int32)))
+    del S_layer
+    dI1 = Iq.grad[r0:r1].clone()
+    du01 = u0q.grad.clone()
+    for _ in range(2):
+        step1()
+    ms1 = all_max(event_ms(step1, 3))
+    del Iq, u0q
+
+    Is = I[r0:r1].contiguous()
+    GSs = GS[r0:r1].contiguous()
+    U1s = U1[r0:r1].contiguous()
+    S1s = S1[r0:r1].contiguous()
+    del I, GS, U1, S1
+    ops = tshard.CudaSliceOps(Ts, N, dev, BETA, 1.0, 0.0)
+    comm = tshard.TorchComm()
+    info = {}
+    Us, Ss, entry = tshard.tshard_forward(Is, u0, ops, comm, info=info)
+    Lam, du0 = tshard.tshard_backward(Is, entry, Us, GSs, ops, comm, BETA)
+    ok = s_layer_ok and bool(torch.equal(Us.view(torch.int32), U1s.view(torch.int32)) and
+                             torch.equal(Ss.view(torch.int32), S1s.view(torch.int32)))
+    num = all_sum(float(((Lam.double() - dI1.double()) ** 2).sum()))
+    den = all_sum(float((dI1.double() ** 2).sum()))
+    dI_rel = (num / den) ** 0.5 if den > 0 else 0.0
+    du0_rel = float((du0 - du01).norm() / du01.norm()) if rank == 0 else 0.0
+    du0_rel = all_max(du0_rel)
+    ok = ok and dI_rel <= 1e-5 and du0_rel <= 1e-5
+    parity = all_max(0.0 if ok else 1.0) == 0.0
+    del Us, Ss, Lam, U1s, S1s, dI1
+
+    Iqs = Is.clone().requires_grad_(True)
+
+    def step_ts():
+        Iqs.grad = None
+        S_ = tshard.lif_tshard(Iqs, u0, beta=BETA, ops=ops, comm=comm)
+        torch.autograd.backward(S_, GSs)
+    for _ in range(max(args.warmup, 3)):
+        step_ts()
+    ms_ts = all_max(event_ms(step_ts, max(min(args.steps, 20), 5)))
+    # one more step through the protocol with CUDA-event marks per phase
+    tl = []
+    U_, _, entry_ = tshard.tshard_forward(Is, u0, ops, comm, timeline=tl)
+    tshard.tshard_backward(Is, entry_, U_, GSs, ops, comm, BETA, timeline=tl)
+    torch.cuda.synchronize(dev)
+    mine = [(tl[i][0], tl[i - 1][1].elapsed_time(tl[i][1])) for i in range(1, len(tl))]
+    every = [None] * ws
+    dist.all_gather_object(every, mine)
+    per_phase = {}
+    for lst in every:
+        for name, v in lst:
+            per_phase[name] = round(max(per_phase.get(name, 0.0), v), 4)
+    del U_, entry_, Iqs
+    torch.cuda.empty_cache()
+    return parity, {
+        "workload": C4_WORKLOAD, "path": "lif_tshard (entry_mode='speculate') fwd + autograd backward",
+        "ranks": ws, "ms_per_step": ms_ts, "value": T * N / (ms_ts / 1e3), "unit": UNIT,
+        "one_gpu_ms_per_step": ms1, "one_gpu_path": "lif_tuned(mode='scan') over the whole sequence, on each rank",
+        "strong_scaling_efficiency": ms1 / (ws * ms_ts),
+        "parity": {"U_S_bit_exact": ok, "dI_rel": dI_rel, "du0_rel": du0_rel,
+                   "repair_rounds": info.get("repair_rounds")},
+        "phases_ms_max_over_ranks": per_phase,
+        "note": "every rank holds the whole sequence for the check; the timed step moves only its slice"}
+
+
 def run_network(args, ws, rank, local):
     """Config 3: one training step (forward, backward, Adam) of the 700-256-256-20
     LIF network, B = 64 per GPU, T = 1024, beta = 0.9, Kaiming-uniform init,
@@ -920,6 +1230,9 @@ def main():
     ws, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, ws, rank)
+        return
+    if args.workload == "c1":
+        run_c1(args, ws, rank, local)
         return
     if args.workload == "c3":
         run_network(args, ws, rank, local)
@@ -1139,6 +1452,10 @@ def main():
         v, threads, sample = cpu_oracle_rate(T, N, args.cpu_seconds)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
+    tshard_parity, c4_ts = None, None
+    if ws > 1 and not args.no_tshard:
+        tshard_parity, c4_ts = c4_time_sharded(args, ws, rank, dev, lib)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -1162,6 +1479,9 @@ def main():
             "gpu_launches": launches,
             "clocks": clk.record(),
         }
+        if ws > 1 and not args.no_tshard:
+            line["tshard_parity"] = tshard_parity
+            line["c4_tshard"] = c4_ts
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

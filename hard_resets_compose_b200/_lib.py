@@ -32,6 +32,8 @@ SIGNATURES = {
     "lifb_status_string": ([c_int], ctypes.c_char_p),
     "lifb_last_error": ([], ctypes.c_char_p),
     "lifb_device_status": ([c_int], c_int),
+    "lifb_check_device": ([c_int], c_int),
+    "lifb_poll_device": ([], c_int),
     "lifb_serial_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float,
                          c_void_p], c_int),
     "lifb_serial_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
@@ -119,12 +121,37 @@ SIGNATURES = {
 }
 
 
+LIFB_ERR_DEVICE = 5
+
+
 class LifbError(RuntimeError):
-    """A nonzero status returned by liblifb."""
+    """A nonzero status returned by liblifb.  `status` is the library's
+    status code; for a device-side error (LIFB_ERR_DEVICE) `device_code` is
+    the code a kernel recorded (101: a bounded wait for an asynchronous copy
+    expired), else None."""
+
+    def __init__(self, msg, status=None, device_code=None):
+        super().__init__(msg)
+        self.status = status
+        self.device_code = device_code
 
 
 def lib_path() -> str:
     return _build.LIB
+
+
+def bind(path: str):
+    """ctypes handle of a liblifb build at `path` with every declared
+    signature set (the product library, or a test build of it)."""
+    L = ctypes.CDLL(path)
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    v = L.lifb_abi_version()
+    if v != ABI_VERSION:
+        raise RuntimeError(f"liblifb ABI version {v} != expected {ABI_VERSION}")
+    return L
 
 
 def load(build_if_missing: bool = True):
@@ -143,23 +170,39 @@ def load(build_if_missing: bool = True):
                     raise RuntimeError(f"liblifb.so is missing and cannot be built: {e}") from e
         if not os.path.exists(path):
             raise RuntimeError(f"liblifb.so not found at {path}; run python -m hard_resets_compose_b200.build")
-        L = ctypes.CDLL(path)
-        for name, (args, res) in SIGNATURES.items():
-            fn = getattr(L, name)
-            fn.argtypes = args
-            fn.restype = res
-        v = L.lifb_abi_version()
-        if v != ABI_VERSION:
-            raise RuntimeError(f"liblifb ABI version {v} != expected {ABI_VERSION}")
-        _lib = L
-        return L
+        _lib = bind(path)
+        return _lib
 
 
-def check(status: int, what: str) -> None:
+def check(status: int, what: str, lib=None) -> None:
     if status != 0:
-        L = load(False)
+        L = lib or load(False)
         msg = L.lifb_last_error().decode() or L.lifb_status_string(status).decode()
-        raise LifbError(f"{what} failed (status {status}: {L.lifb_status_string(status).decode()}): {msg}")
+        code = None
+        if status == LIFB_ERR_DEVICE:
+            import re
+            m = re.search(r"device status (-?\d+)", msg)
+            code = int(m.group(1)) if m else None
+        raise LifbError(f"{what} failed (status {status}: {L.lifb_status_string(status).decode()}): {msg}",
+                        status=status, device_code=code)
+
+
+def check_device(what: str, reset: bool = False, lib=None) -> None:
+    """Raises LifbError (status LIFB_ERR_DEVICE, device_code = the kernel's
+    code) when a kernel of the library has reported a device-side error on
+    the current device.  Synchronous: call it where the host waits anyway."""
+    L = lib or load(False)
+    check(L.lifb_check_device(int(bool(reset))), what, L)
+
+
+def poll_device(what: str, lib=None) -> None:
+    """The non-blocking form of check_device: raises for a device-side error
+    seen by an earlier poll's asynchronous read, and starts the next read.
+    Does nothing while the current stream is being captured into a graph."""
+    if torch.cuda.is_current_stream_capturing():
+        return
+    L = lib or load(False)
+    check(L.lifb_poll_device(), what, L)
 
 
 def ptr(t):

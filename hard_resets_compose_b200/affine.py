@@ -223,6 +223,7 @@ class LIFAffineFn(torch.autograd.Function):
             lam, pg = aff_adjoint_v(V, u0, gS, b, th, g, dl, alpha, param_grads=want_params)
             if want_params:
                 d_beta, d_gamma, d_delta = pg
+            _lib.poll_device("lif_affine backward")
             return (lam, b * lam[0], d_beta if need[2] else None, d_gamma if need[3] else None,
                     d_delta if need[4] else None, None, None, None, None, None)
         I, u0, U = ctx.saved_tensors
@@ -231,6 +232,7 @@ class LIFAffineFn(torch.autograd.Function):
         if want_params:
             d_beta, d_gamma, d_delta = aff_param_grads(I, u0, U, gS, lam, b, th, alpha)
         # parameters passed as Python numbers get no gradient
+        _lib.poll_device("lif_affine backward")
         return (lam, b * lam[0], d_beta if need[2] else None, d_gamma if need[3] else None,
                 d_delta if need[4] else None, None, None, None, None, None)
 

@@ -242,6 +242,7 @@ class ALIFFn(torch.autograd.Function):
                                       chunked=ctx.bwd == "scan")
         g = sums.sum(dim=(1, 2)).to(torch.float32) if want else None
         pick = lambda i, v: v if need[i] else None  # noqa: E731
+        _lib.poll_device("alif backward")
         return (LV, pick(1, b * LV[0]), pick(2, lwm1), pick(3, g[0] if want else None),
                 pick(4, g[1] if want else None), pick(5, g[2] if want else None), pick(6, g[3] if want else None),
                 None, None, None, None, None, None, None, None)

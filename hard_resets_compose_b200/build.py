@@ -9,6 +9,7 @@ source tree to the GPU machine.  Rebuilds only when a source is newer.
 """
 from __future__ import annotations
 
+import concurrent.futures
 import glob
 import os
 import shutil
@@ -58,14 +59,20 @@ def build(force: bool = False, verbose: bool = False, defines=(), out: str = Non
     objdir = os.path.join(libdir, "obj" if out is None else "obj_" + os.path.basename(target))
     os.makedirs(objdir, exist_ok=True)
     nvcc = _nvcc()
-    objs = []
+    objs, cmds = [], []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc, *ARCH, *NVCC_FLAGS, *[f"-D{d}" for d in defines], "-c", src, "-o", obj]
-        if verbose:
-            print(" ".join(cmd))
-        subprocess.run(cmd, check=True)
+        cmds.append([nvcc, *ARCH, *NVCC_FLAGS, *[f"-D{d}" for d in defines], "-c", src, "-o", obj])
         objs.append(obj)
+    # one nvcc per translation unit, as many at once as there are cores
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for cmd, res in zip(cmds, ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), cmds)):
+            if verbose:
+                print(" ".join(cmd))
+            if res.stdout or res.stderr:
+                print(res.stdout + res.stderr, end="", file=sys.stderr)
+            if res.returncode:
+                raise subprocess.CalledProcessError(res.returncode, cmd, res.stdout, res.stderr)
     tmp = target + ".tmp"
     cmd = [nvcc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"]
     if verbose:

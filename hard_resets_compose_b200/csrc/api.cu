@@ -9,6 +9,7 @@
 #include <string>
 
 #include "lifb_internal.h"
+#include "tma.cuh"
 
 namespace {
 
@@ -141,6 +142,7 @@ const char *lifb_status_string(int status)
     case LIFB_ERR_CUDA: return "CUDA error";
     case LIFB_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case LIFB_ERR_UNSUPPORTED: return "unsupported configuration";
+    case LIFB_ERR_DEVICE: return "device-side error reported by a kernel";
     default: return "unknown status";
     }
 }
@@ -148,6 +150,23 @@ const char *lifb_status_string(int status)
 const char *lifb_last_error(void) { return g_last_error.c_str(); }
 
 int lifb_device_status(int reset) { return lifb::read_device_status(reset != 0); }
+
+static int device_code_status(int code, const char *who)
+{
+    if (code < 0) return fail(LIFB_ERR_CUDA, "%s: the device status could not be read", who);
+    if (code == 0) {
+        g_last_error.clear();
+        return LIFB_OK;
+    }
+    if (code == lifb::kStatusTmaWaitTimeout)
+        return fail(LIFB_ERR_DEVICE, "%s: device status %d: a bounded wait for an asynchronous copy expired; the "
+                    "outputs of the calls before this check may be incomplete", who, code);
+    return fail(LIFB_ERR_DEVICE, "%s: device status %d", who, code);
+}
+
+int lifb_check_device(int reset) { return device_code_status(lifb::read_device_status(reset != 0), "lifb_check_device"); }
+
+int lifb_poll_device(void) { return device_code_status(lifb::poll_device_status(), "lifb_poll_device"); }
 
 int lifb_serial_fwd(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, float beta,
                     float theta, float u_r, void *stream)
@@ -205,6 +224,13 @@ int lifb_scan_fwd_v3(const float *I, const float *u0, float *U, float *S, int64_
     if (stats_dev && cudaMemsetAsync(stats_dev, 0, sizeof(lifb_stats), s) != cudaSuccess)
         return check_launch("lifb_scan_fwd_v3: stats reset");
     if (T == 0 || N == 0) return LIFB_OK;
+    if (!stats_dev && max_repair < 0 && M > 1) {
+        // When the slab of 32 neurons x T rows and its maps fit on chip, one
+        // launch runs every phase (scan_block.cu) and needs no workspace.
+        LIFB_RANGE("block scan");
+        if (lifb::scan_block(I, u0, U, S, T, N, C, K, true, 0, beta, theta, u_r, nullptr, s))
+            return check_launch("lifb_scan_fwd_v3");
+    }
     size_t need = lifb_scan_fwd_v3_workspace_bytes(T, N, C, K);
     if ((st = check_ws(workspace, workspace_bytes, need))) return st;
     // Without stats the last chunk's map is never evaluated: build M-1 maps.

@@ -65,6 +65,9 @@ bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int b
 bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N, int64_t T, int box_x, int box_y);
 int *device_status_ptr();                 // status word of the current device
 int read_device_status(bool reset);       // synchronous read (current device)
+// Non-blocking: the word as of the last completed asynchronous read of the
+// current device (0 before any), or -1 on a CUDA error; starts the next read.
+int poll_device_status();
 
 // chunk_tma.cu: true when N % 4 == 0 and every non-null pointer is 16-byte
 // aligned (the TMA kernels' requirement).
@@ -176,6 +179,18 @@ void replay_any(const float *I, const float *u0, const float *Starts, float *U, 
 void leadin_starts(const float *I, const float *u0, const float *I_halo, int64_t W_halo, float *Starts,
                    float *end_guess, int64_t N, int64_t NS, int64_t L, int64_t W, float beta, float theta, float u_r,
                    cudaStream_t s, Reset rs = {});
+
+// scan_block.cu: the block-level fused forward, one CTA per 32-neuron slab
+// holding all T rows in shared memory (T % C == 0, 2 <= T/C <= 16 with maps
+// and K <= 16, <= 32 without, C <= 256, N % 4 == 0, 16-byte aligned tensors,
+// the slab and its maps within the opt-in shared memory).  maps: the
+// two-level map scan (envelope, build, carry, replay, fix-up) with chunk
+// length C and capacity K, stats accumulated into st when given; otherwise
+// W-row lead-ins guess each chunk's start.  False when it does not apply
+// (nothing launched).
+bool scan_block_applies(int64_t T, int64_t N, int C, int K, bool maps);
+bool scan_block(const float *I, const float *u0, float *U, float *S, int64_t T, int64_t N, int C, int K, bool maps,
+                int64_t W, float beta, float theta, float u_r, lifb_stats *st, cudaStream_t s);
 
 // host_pipeline.cu
 size_t host_pipe_workspace_bytes(int64_t T, int64_t N, int64_t block_n);

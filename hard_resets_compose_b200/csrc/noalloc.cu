@@ -14,6 +14,8 @@
 
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "lifb_internal.h"
 
 namespace {
@@ -23,12 +25,33 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[LIFB_NOALLOC_SC
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void *g_scratch_dev[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
+// Device address of g_noalloc_scratch per device, valid for the context it
+// was looked up in: a context torn down and made again (cudaDeviceReset)
+// reloads the module, and the array may then sit at another address.
+void *g_scratch_dev[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
 int report(int status, const char *msg)
 {
     lifb::set_last_error(msg);
     return status;
+}
+
+// The calling thread's current context, through the driver entry point (no
+// link-time libcuda dependency); nullptr if it cannot be queried.
+CUcontext current_context()
+{
+    static PFN_cuCtxGetCurrent_v4000 get = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return (PFN_cuCtxGetCurrent_v4000)fn;
+    }();
+    CUcontext c = nullptr;
+    if (!get || get(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
 }
 
 }  // namespace
@@ -51,12 +74,22 @@ extern "C" int lifb_scan_fwd_v3_noalloc(const float *I, const float *u0, float *
     // One-time set-up per device, with that device current: the host-side name
     // g_noalloc_scratch is not a device address, so look the address up.
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0)
         return report(LIFB_ERR_CUDA, "lifb_scan_fwd_v3_noalloc: cannot query the current device");
+    if (dev >= kMaxDevices) {
+        char buf[160];
+        snprintf(buf, sizeof(buf), "lifb_scan_fwd_v3_noalloc: device %d is beyond the %d devices this entry point "
+                 "serves", dev, kMaxDevices);
+        return report(LIFB_ERR_UNSUPPORTED, buf);
+    }
+    // The first call on a device (and the first in a new context of it) looks
+    // the address up; it should come before any stream capture.
+    cudaSetDevice(dev);  // binds the device's primary context to this thread if none is
+    const CUcontext ctx = current_context();
     void *scratch = nullptr;
     {
         std::lock_guard<std::mutex> g(g_mu);
-        if (!g_scratch_dev[dev]) {
+        if (!g_scratch_dev[dev] || !ctx || g_scratch_ctx[dev] != ctx) {
             void *p = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
             if (e != cudaSuccess || p == nullptr) {
@@ -66,6 +99,7 @@ extern "C" int lifb_scan_fwd_v3_noalloc(const float *I, const float *u0, float *
                 return report(LIFB_ERR_CUDA, buf);
             }
             g_scratch_dev[dev] = p;
+            g_scratch_ctx[dev] = current_context();  // the context the lookup ran in
         }
         scratch = g_scratch_dev[dev];
     }

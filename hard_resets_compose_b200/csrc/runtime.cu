@@ -79,6 +79,20 @@ int *device_status_ptr()
     return g_status_ptr[dev];
 }
 
+// Asynchronous reads of the status word, per device: a pinned host mirror
+// filled by a copy on a private non-blocking stream, and an event marking
+// when the copy has landed.
+namespace {
+struct StatusPoll {
+    int *mirror = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t landed = nullptr;
+    bool pending = false;
+    int last = 0;  // the word as of the last completed read
+};
+StatusPoll g_poll[kMaxDevices];
+}  // namespace
+
 int read_device_status(bool reset)
 {
     int v = 0;
@@ -86,8 +100,52 @@ int read_device_status(bool reset)
     if (reset && v) {
         int z = 0;
         cudaMemcpyToSymbol(g_status_word, &z, sizeof(int));
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+            // a read still in flight may have seen the old value
+            std::lock_guard<std::mutex> g(g_status_mu);
+            StatusPoll &p = g_poll[dev];
+            if (p.pending) cudaStreamSynchronize(p.stream);
+            p.pending = false;
+            p.last = 0;
+        }
     }
     return v;
+}
+
+int poll_device_status()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    std::lock_guard<std::mutex> g(g_status_mu);
+    StatusPoll &p = g_poll[dev];
+    if (!p.mirror) {
+        if (cudaHostAlloc((void **)&p.mirror, sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
+            p.mirror = nullptr;
+            return -1;
+        }
+        *p.mirror = 0;
+        if (cudaStreamCreateWithFlags(&p.stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&p.landed, cudaEventDisableTiming) != cudaSuccess)
+            return -1;
+    }
+    if (p.pending) {
+        const cudaError_t q = cudaEventQuery(p.landed);
+        if (q == cudaSuccess) {
+            p.last = *(volatile int *)p.mirror;
+            p.pending = false;
+        } else if (q != cudaErrorNotReady) {
+            return -1;
+        }
+    }
+    if (!p.pending) {
+        if (cudaMemcpyFromSymbolAsync(p.mirror, g_status_word, sizeof(int), 0, cudaMemcpyDeviceToHost, p.stream) !=
+                cudaSuccess ||
+            cudaEventRecord(p.landed, p.stream) != cudaSuccess)
+            return -1;
+        p.pending = true;
+    }
+    return p.last;
 }
 
 }  // namespace lifb

@@ -190,6 +190,10 @@ int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S, int6
     const int64_t NS = T / L;
     if (NS == 1 && (!I_halo || W_halo == 0)) {
         lifb::serial_fwd(I, u0, U, S, T, N, beta, theta, u_r, s);
+    } else if (!(I_halo && W_halo > 0) && L <= 256 &&
+               lifb::scan_block(I, u0, U, S, T, N, (int)L, 0, false, W, beta, theta, u_r, nullptr, s)) {
+        // short sequences: lead-ins, replay and fix-up of one 32-neuron slab
+        // per CTA on chip (scan_block.cu), no workspace used
     } else {
         if ((st = spec_ws("lifb_scan_fwd_spec", T, N, L, workspace, workspace_bytes))) return st;
         SpecScratch w = spec_carve(workspace, NS, N);

@@ -11,7 +11,12 @@
 
 namespace lifb {
 
-constexpr long long kWaitCycles = 2000000000LL;  // about 1 s at 1.9-2 GHz
+// About 1 s at 1.9-2 GHz.  A build may shorten it (-DLIFB_WAIT_CYCLES=...),
+// as the test of the timeout path does.
+#ifndef LIFB_WAIT_CYCLES
+#define LIFB_WAIT_CYCLES 2000000000LL
+#endif
+constexpr long long kWaitCycles = LIFB_WAIT_CYCLES;
 
 enum DeviceStatus : int {
     kStatusOk = 0,

@@ -65,6 +65,7 @@ class LIFParamFn(torch.autograd.Function):
         else:
             lam = L.serial_backward_auto(I, u0, U, None, gS, None, b, th, ur, alpha)
         g_beta, g_theta, g_ur = param_grads(I, u0, U, gS, lam, b, th, alpha)
+        _lib.poll_device("fitting layer backward")
         return lam, b * lam[0], g_beta, g_theta, g_ur, None, None, None, None
 
 
@@ -120,6 +121,7 @@ class LIFSoftFn(torch.autograd.Function):
     def backward(ctx, gS):
         b, th, alpha = ctx.cfg
         dI, du0, db = _soft_backward_v(ctx, gS, b, th, alpha, ctx.needs_input_grad[2])
+        _lib.poll_device("fitting layer backward")
         return dI, du0, db, None, None
 
 
@@ -154,12 +156,14 @@ class LIFSoftScanFn(torch.autograd.Function):
         b, th, alpha = ctx.cfg
         if ctx.vpath:
             dI, du0, db = _soft_backward_v(ctx, gS, b, th, alpha, ctx.needs_input_grad[2])
+            _lib.poll_device("fitting layer backward")
             return dI, du0, db, None, None, None, None, None
         I, u0, U = ctx.saved_tensors
         gS = gS.contiguous()
         # both modes: the same adjoint (the reference's scan mode forms V and
         # convolves by FFT, its serial mode sweeps; one sweep from U and I here)
         lam = L.soft_serial_backward_auto(I, u0, U, gS, b, th, alpha)
+        _lib.poll_device("fitting layer backward")
         return lam, b * lam[0], _soft_beta_grad(I, u0, U, gS, lam, b, th, alpha), None, None, None, None, None
 
 

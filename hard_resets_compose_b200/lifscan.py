@@ -38,7 +38,7 @@ __all__ = [
     "LIFAuto", "lif_auto", "serial_fwd_cfg", "serial_bwd_cfg", "scan_chunk_fwd", "scan_chunk_bwd",
     "lif_tuned_host", "scan_forward_spec", "spec_segment", "serial_forward_v", "lif_backward_v",
     "soft_serial_forward", "soft_serial_backward", "soft_serial_backward_pf", "soft_serial_backward_auto",
-    "soft_bwd_cfg",
+    "soft_bwd_cfg", "block_leadin",
 ]
 
 _CONVERGE = -1  # max_repair value meaning "repair until converged"
@@ -161,7 +161,8 @@ def _stats_buffer(dev, want):
 
 
 def _fill_stats(stats, buf, level):
-    st = _lib.read_stats(buf)
+    st = _lib.read_stats(buf)  # the host waits here anyway: fold in the device status
+    _lib.check_device("scan stats")
     stats["repair_iters"] = int(st.repair_iters)
     n = max(int(st.n_maps), 1)
     stats["overflow_frac"] = float(st.n_overflow) / n
@@ -309,6 +310,38 @@ def spec_segment(T, N):
     return L, min(SPEC_LEAD, L)
 
 
+# Block-level lead-in forward for short sequences with few neurons
+# (lifb_scan_fwd_spec with segments of BLOCK_L rows runs csrc/scan_block.cu):
+# one CTA per 32-neuron slab holds all T rows on chip, each warp guesses its
+# chunk's start with a W-row lead-in from u_r and replays it at once, and
+# fix-up rounds replay the rare wrong guesses until they rejoin.  W must
+# outlast the rows two trajectories of one neuron take to become identical,
+# which grows like 1/(-ln beta) (the rows for beta^k to shrink a difference
+# below one ulp: 24 ln 2 / -ln beta); 1.6 times that, in 64-row steps, is
+# 256 rows at beta = 0.9, where the measured p99.9 is about 150 rows
+# (config 1).  It pays while the chain W + L stays under half the single
+# pass's T rows and the neurons alone cannot fill the GPU: measured on B200
+# at T = 1024, beta = 0.9: N = 4096 16.4 us against 24.6 us for the single
+# pass, N = 8192 27.7 against 25.8 us.
+BLOCK_L = 64
+BLOCK_MAX_N = 6144
+BLOCK_MAX_T = 1536
+
+
+def block_leadin(T, N, beta):
+    """(L, W) of the block-level lead-in forward for this shape and beta, or
+    (0, 0) when the single pass (or the long-sequence path) is the choice."""
+    import math
+    if not (0 < N <= BLOCK_MAX_N and N % 4 == 0 and 0 < T <= BLOCK_MAX_T and T % BLOCK_L == 0
+            and T // BLOCK_L >= 2 and 0.0 < beta < 1.0):
+        return 0, 0
+    rows = 1.6 * 24.0 * math.log(2.0) / -math.log(beta)
+    W = BLOCK_L * max(1, math.ceil(rows / BLOCK_L))
+    if W + BLOCK_L > T // 2:
+        return 0, 0
+    return BLOCK_L, W
+
+
 def scan_forward_spec(I, beta, theta, u_r, u0, L=None, W=None, halo=None):
     """Speculative segment forward (lifb_scan_fwd_spec) -> (U, S), identical to
     the serial recurrence; L = segment length (T % L == 0), W = lead-in rows
@@ -341,11 +374,16 @@ def scan_forward_spec(I, beta, theta, u_r, u0, L=None, W=None, halo=None):
 
 def scan_forward_auto(I, beta, theta, u_r, u0, K=16, repair=0):
     """lifscan/triton_lif.py:1228-1232 with a B200 path choice: the single
-    streaming pass, or the speculative segment forward when N is too small to
-    fill the GPU (spec_segment).  Outputs are identical either way (exact)."""
+    streaming pass; the speculative segment forward when N is too small to
+    fill the GPU and T is long (spec_segment); the block-level lead-in
+    forward when T is short and N small (block_leadin).  Outputs are
+    identical whichever runs (exact)."""
     T, N = I.shape
     if T > 0 and N > 0 and spec_segment(T, N)[0] < T:
         return scan_forward_spec(I, beta, theta, u_r, u0)
+    Lb, Wb = block_leadin(T, N, float(beta))
+    if Lb:
+        return scan_forward_spec(I, beta, theta, u_r, u0, L=Lb, W=Wb)
     return scan_forward_v3(I, beta, theta, u_r, u0, C=scan_chunk_fwd(T, N), K=K, repair=repair)
 
 
@@ -517,6 +555,7 @@ class LIFTuned(torch.autograd.Function):
             (V,) = ctx.saved_tensors
             T, N = V.shape
             Lam = lif_backward_v(V, gS, beta, theta, alpha, C=T if mode == "serial" else scan_chunk_bwd(T, N))
+            _lib.poll_device("lif_tuned")
             return Lam, beta * Lam[0], None, None, None, None, None, None, None
         I, u0, U, S = ctx.saved_tensors
         # GU is identically zero on this path: pass None instead of materialising
@@ -526,6 +565,7 @@ class LIFTuned(torch.autograd.Function):
             Lam = serial_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         else:
             Lam = scan_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
+        _lib.poll_device("lif_tuned")
         return Lam, beta * Lam[0], None, None, None, None, None, None, None
 
 
@@ -557,6 +597,7 @@ class LIFFunction(torch.autograd.Function):
             Lam = serial_backward(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         else:
             Lam = scan_backward(I, u0, U, None, gS, None, beta, theta, u_r, alpha, C=C)
+        _lib.poll_device("lif")
         return Lam, beta * Lam[0], None, None, None, None, None, None, None, None
 
 
@@ -606,6 +647,7 @@ class LIFAuto(torch.autograd.Function):
             Lam = scan_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
         else:
             Lam = serial_backward_auto(I, u0, U, None, gS, None, beta, theta, u_r, alpha)
+        _lib.poll_device("lif_auto")
         return Lam, beta * Lam[0], None, None, None, None, None, None, None, None
 
 
@@ -617,14 +659,17 @@ def lif_auto(I, u0, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, K=16, repair=0):
 
 # ----------------------------------------------------------------------------- host-resident tensors
 def lif_tuned_host(I, GS, u0=None, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, block_n=None, device=None,
-                   out=None):
+                   out=None, sync=True):
     """lif_tuned forward + backward for host (CPU) tensors, pipelined over
     neuron blocks so host->device copies, compute and device->host copies
     overlap (lifb_lif_fwd_bwd_host).  Returns (S, dI, du0) as CPU tensors
     (pinned); equivalent to S = lif_tuned(I, u0, ...);
     torch.autograd.backward(S, GS) with dI = I.grad and du0 = u0.grad.
     I and GS should be pinned for full overlap; `out` may pass preallocated
-    pinned (S, dI, du0)."""
+    pinned (S, dI, du0).  sync=True (default) waits for the device's current
+    stream, so the returned tensors are complete, and raises LifbError if a
+    kernel reported a device-side error; sync=False returns at once (the
+    results are valid after the stream has drained)."""
     if I.is_cuda or GS.is_cuda:
         raise ValueError("lif_tuned_host takes host tensors; use lif_tuned for CUDA tensors")
     if I.dtype != torch.float32 or GS.dtype != torch.float32:
@@ -649,4 +694,9 @@ def lif_tuned_host(I, GS, u0=None, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, bloc
         check(L.lifb_lif_fwd_bwd_host(ptr(I), ptr(GS), ptr(u0), ptr(S), ptr(dI), ptr(du0), T, N, _f(beta),
                                       _f(theta), _f(u_r), _f(alpha), int(block_n), ptr(ws), nb, st),
               "lif_tuned_host")
+        if sync:
+            # the host buffers are complete only once the stream has drained;
+            # the device status is read at the same point
+            torch.cuda.current_stream(dev).synchronize()
+            _lib.check_device("lif_tuned_host")
     return S, dI, du0

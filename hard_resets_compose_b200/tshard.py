@@ -314,6 +314,8 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", timeline
             need = r > 0  # every slice end is new: no flags to read (no host sync)
         else:
             flags = g[:, N].tolist()
+            if I.is_cuda:  # the host has just waited: fold in the device status
+                _lib.check_device("time-sharded forward")
             if not any(f != 0.0 for f in flags[:R - 1]):
                 break
             need = r > 0 and flags[r - 1] != 0.0
@@ -368,6 +370,8 @@ class LIFTimeSharded(torch.autograd.Function):
     def backward(ctx, gS):
         I, U, entry = ctx.saved_tensors
         dI, du0 = tshard_backward(I, entry, U, gS.contiguous(), ctx.ops, ctx.comm, ctx.beta)
+        if I.is_cuda:
+            _lib.poll_device("lif_tshard")
         return dI, du0, None, None, None, None, None, None, None
 
 

@@ -40,6 +40,7 @@ extern "C" {
 #define LIFB_ERR_CUDA 2             /* a CUDA runtime call or launch failed */
 #define LIFB_ERR_WORKSPACE 3        /* workspace NULL, too small or misaligned */
 #define LIFB_ERR_UNSUPPORTED 4      /* valid request this build cannot serve */
+#define LIFB_ERR_DEVICE 5           /* a kernel reported a device-side error (lifb_check_device) */
 
 /* Device-resident counters filled by the scan forward when a stats pointer is
  * given; they give the reference's `stats` dict (triton_lif.py:812-816 for v3,
@@ -80,6 +81,24 @@ uint64_t lifb_kernel_launches(void);
  * its outputs are incomplete).  Synchronous (reads device memory); reset != 0
  * clears the word afterwards.  Returns -1 if the read itself failed. */
 int lifb_device_status(int reset);
+
+/* The device-side status folded into a return code: LIFB_OK when no kernel
+ * of this library on the current device has reported a problem since the
+ * word was last cleared, LIFB_ERR_DEVICE when one has (lifb_last_error() then
+ * names the code, e.g. 101: a bounded wait for an asynchronous copy expired,
+ * so the outputs of the calls before this check may be incomplete), or
+ * LIFB_ERR_CUDA when the read failed.  Synchronous, like lifb_device_status;
+ * reset != 0 clears the word after reading it.  No reference counterpart (the
+ * reference's Triton kernels never wait on a copy). */
+int lifb_check_device(int reset);
+
+/* The same check without blocking: returns the status word as of the last
+ * read that has completed (LIFB_OK before any) and starts a new asynchronous
+ * read on a private stream of the library, so a problem shows up at most one
+ * poll late.  The word stays set until lifb_check_device(1) or
+ * lifb_device_status(1) clears it.  Not for use while a stream of the calling
+ * thread is being captured into a CUDA graph. */
+int lifb_poll_device(void);
 
 /* Human-readable text of a status code, and the last error message recorded
  * on the calling host thread (empty string if none). */

@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_status_strings():
     L = _lib.load()
     assert L.lifb_abi_version() == _lib.ABI_VERSION
-    for code in range(5):
+    for code in range(6):
         assert L.lifb_status_string(code)
     assert L.lifb_status_string(99) == b"unknown status"
 

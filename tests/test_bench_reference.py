@@ -15,8 +15,8 @@ def _args(workload):
     return types.SimpleNamespace(workload=workload, steps=1, warmup=0, gpus=1)
 
 
-@pytest.mark.parametrize("workload,metric", [("affine", bench.AFF_METRIC), ("alif", bench.ALIF_METRIC),
-                                             ("c3", bench.C3_METRIC)])
+@pytest.mark.parametrize("workload,metric", [("c1", bench.C1_METRIC), ("affine", bench.AFF_METRIC),
+                                             ("alif", bench.ALIF_METRIC), ("c3", bench.C3_METRIC)])
 def test_reference_line_matches_the_workload(capsys, workload, metric):
     bench.run_reference(_args(workload), 1, 0)
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])

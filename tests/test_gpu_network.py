@@ -62,3 +62,35 @@ def test_network_matches_torch_reference(cuda, readout, init, beta, mode):
     assert rel(logits.detach().cpu().numpy(), rlogits.detach().cpu().numpy()) < 1e-6
     for g, rg in zip(grads, rgrads):
         assert rel(g.cpu().numpy(), rg.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("readout,init,beta,scale", (
+    ("mean", "reference", 0.95, (1.0, 1.0)),   # the reference Net as written (lifscan/shdnet.py:53-66)
+    ("mean", "reference", 0.95, (6.0, 3.0)),   # the same with both layers driven to spike
+    ("leaky", "kaiming", 0.9, (6.0, 3.0)),     # the config-3 benchmark variant
+))
+def test_network_c3_full_shape(cuda, readout, init, beta, scale):
+    """Config 3 at its real shape: B = 64, T = 1024, the 700-channel Bernoulli
+    raster of synthetic_batch.  Spikes of both LIF layers (16384 neurons each)
+    bit-equal to the plain torch fp32 serial loop on the same GEMM outputs;
+    every parameter gradient within 1e-5 relative."""
+    from hard_resets_compose_b200.shdnet import Net, synthetic_batch
+    torch.manual_seed(1)
+    net = Net(mode="scan", beta=beta, init=init, readout=readout).to(cuda)
+    x, y = synthetic_batch(1024, 64, seed=2, device=cuda)
+    with torch.no_grad():
+        net.l1.fc.weight.mul_(scale[0])
+        net.l2.fc.weight.mul_(scale[1])
+    logits, (s1, s2) = net(x)
+    loss = nn.functional.cross_entropy(logits, y)
+    grads = torch.autograd.grad(loss, list(net.parameters()))
+    rlogits, (r1, r2) = _reference_forward(net, x)
+    rloss = nn.functional.cross_entropy(rlogits, y)
+    rgrads = torch.autograd.grad(rloss, list(net.parameters()))
+    assert s1.sum() > 0
+    if scale != (1.0, 1.0):
+        assert s2.sum() > 0
+    assert torch.equal(s1, r1.detach()) and torch.equal(s2, r2.detach())
+    assert rel(logits.detach().cpu().numpy(), rlogits.detach().cpu().numpy()) < 1e-6
+    for g, rg in zip(grads, rgrads):
+        assert rel(g.cpu().numpy(), rg.cpu().numpy()) < 1e-5

@@ -71,3 +71,17 @@ def test_speculative_segments(N, T):
 def test_wide_problems_take_the_single_pass():
     assert L.spec_segment(1 << 20, L.SPEC_FILL) == (1 << 20, 0)
     assert L.scan_chunk_fwd(1024, 16384) == 1024
+
+
+def test_block_leadin_policy():
+    """The block-level lead-in forward is chosen for short sequences with few
+    neurons when its lead-in (grown like 1/(-ln beta)) keeps the chain under
+    half of T; otherwise the single pass or the long-sequence path."""
+    from hard_resets_compose_b200 import lifscan as L
+    assert L.block_leadin(1024, 4096, 0.9) == (64, 256)   # config 1
+    assert L.block_leadin(1024, 4096, 0.5) == (64, 64)
+    assert L.block_leadin(1024, 4096, 0.99) == (0, 0)     # lead-in longer than half of T
+    assert L.block_leadin(1024, 16384, 0.9) == (0, 0)     # the single pass fills the GPU
+    assert L.block_leadin(1024, 4097, 0.9) == (0, 0)      # no TMA path (N % 4)
+    assert L.block_leadin(4096, 4096, 0.9) == (0, 0)      # the slab no longer fits on chip
+    assert L.block_leadin(1024, 4096, 1.0) == (0, 0)
