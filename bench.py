@@ -54,6 +54,8 @@ L2_FLUSH_BYTES = 256 << 20
 C1_T, C1_N, C1_BETA, C1_MU, C1_SD = 1024, 4096, 0.9, 0.1, 0.3
 C1_METRIC = "neuron-steps/s, scan forward (B*N=4096/GPU, T=1024)"
 C1_WORKLOAD = "c1: scan forward, B*N=4096 per GPU (B=16 x 256), T=1024, beta=0.9, x~N(0.1,0.3^2)"
+C1_RING = 6  # input sets cycled by the c1 timing: 6 x 48 MiB > the 126 MB L2
+C2_RING = 3  # input sets cycled by the c2 timing: each step touches 320 MiB
 
 
 def parse():
@@ -174,6 +176,88 @@ class ClockSampler:
                 "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
 
 
+class RingTimer:
+    """Back-to-back timing of a step over a ring of input sets whose joint
+    footprint exceeds L2, so every step reads inputs that are no longer in L2
+    (the contract's "inputs larger than L2", instead of a flush per step).
+
+    One CUDA graph holds one step per set (a full cycle of the ring), so the
+    host launches one graph per cycle and the device runs the steps back to
+    back; K steps are timed by one pair of CUDA events as floor(K / R)
+    replays of the cycle graph plus K mod R replays of single-step graphs.
+    `step_fns[r]()` runs one step on set r (warmed up before capture)."""
+
+    def __init__(self, torch, dev, stream, lib, step_fns, barrier):
+        self.torch, self.dev, self.stream, self.barrier = torch, dev, stream, barrier
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                for fn in step_fns:
+                    fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.single = []
+        n0 = lib.lifb_kernel_launches()
+        for fn in step_fns:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn()
+            self.single.append(gr)
+        self.launches_per_step = (lib.lifb_kernel_launches() - n0) // len(step_fns)
+        self.cycle = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.cycle):
+            for fn in step_fns:
+                fn()
+        torch.cuda.synchronize(dev)
+        self.R = len(step_fns)
+
+    def run(self, steps):
+        q, r = divmod(steps, self.R)
+        for _ in range(q):
+            self.cycle.replay()
+        for i in range(r):
+            self.single[i].replay()
+
+    def ms_per_step(self, steps):
+        torch = self.torch
+        self.run(self.R)
+        self.barrier()
+        torch.cuda.synchronize(self.dev)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        self.run(steps)
+        b.record(self.stream)
+        torch.cuda.synchronize(self.dev)
+        self.barrier()
+        return a.elapsed_time(b) / steps
+
+
+def bind_numa(torch, dev):
+    """Binds this process's CPUs to the NUMA node of its GPU (read from
+    sysfs), so pinned host buffers allocated afterwards are first touched on
+    that node.  Returns the node, or None when the platform does not say."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bdf}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus = set()
+            for part in f.read().strip().split(","):
+                a, _, b = part.partition("-")
+                cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return node
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def cpu_oracle_rate(T, N, seconds, want_bwd=True, mu=MU, sd=SD, beta=BETA):
     """Reference CPU path (C restatement of lifscan/fast.py serial forward +
     adjoint) on all host threads; repeats the full workload until `seconds`
@@ -193,7 +277,8 @@ def cpu_oracle_rate(T, N, seconds, want_bwd=True, mu=MU, sd=SD, beta=BETA):
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return done * T * N / el, threads, f"{done} x T={T}, N={N} (serial forward + adjoint) in {el:.1f} s"
+    what = "serial forward + adjoint" if want_bwd else "serial forward"
+    return done * T * N / el, threads, f"{done} x T={T}, N={N} ({what}) in {el:.1f} s"
 
 
 SOFT_METRIC = "neuron-steps/s, soft-reset fitting layer lif_soft fwd+bwd (B*N=16384/GPU, T=1024)"
@@ -357,10 +442,18 @@ def run_c1(args, ws, rank, local):
     B*N = 4096 neurons per GPU over T = 1024 rows, x ~ N(0.1, 0.3^2),
     beta = 0.9, u0 = 0.  The step is scan_forward_auto, the library's path
     for this shape; the map scan (scan_forward_v3 with the reference's C = 64,
-    K = 16: the block-level kernel), the lead-in block scan and the single
+    K = 16, the block-level kernel), the lead-in block scan and the single
     serial pass are timed beside it.  Batch-sharded under torchrun (weak
     scaling, no collective).  Every path is checked bit for bit against the
-    serial pass on the device before timing."""
+    serial pass on the device before timing.
+
+    A step's working set (48 MiB) fits in L2, so the timed region runs K
+    steps back to back over a ring of C1_RING input sets (their inputs and
+    outputs together exceed L2: each step's input was last touched
+    C1_RING - 1 steps earlier, with more than L2's capacity of other traffic
+    since), one pair of CUDA events around all K.  Each path is also timed as
+    an isolated call after an L2 flush (the event pair then also holds the
+    launch's fixed latency, about 6 us measured for an empty kernel)."""
     import datetime
 
     import torch
@@ -376,9 +469,9 @@ def run_c1(args, ws, rank, local):
     lib = _lib.load()
     T, N, beta = C1_T, C1_N, C1_BETA
     g = torch.Generator().manual_seed(100 + rank)
-    I_h = (C1_MU + C1_SD * torch.randn(T, N, generator=g)).float()
+    I_hs = [(C1_MU + C1_SD * torch.randn(T, N, generator=g)).float() for _ in range(C1_RING)]
     u0_h = torch.zeros(N)
-    I = I_h.to(dev)
+    Is = [x.to(dev) for x in I_hs]
     u0 = u0_h.to(dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     evict = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
@@ -396,23 +489,26 @@ def run_c1(args, ws, rank, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    paths = {
-        "auto": lambda: L.scan_forward_auto(I, beta, 1.0, 0.0, u0),
-        "map_scan_v3_C64_K16": lambda: L.scan_forward_v3(I, beta, 1.0, 0.0, u0, C=64, K=16),
-        "serial": lambda: L.serial_forward(I, beta, 1.0, 0.0, u0),
-    }
     Lb, Wb = L.block_leadin(T, N, beta)
-    if Lb:
-        paths[f"leadin_block_L{Lb}_W{Wb}"] = lambda: L.scan_forward_spec(I, beta, 1.0, 0.0, u0, L=Lb, W=Wb)
-    Us, Ss = paths["serial"]()
-    parity = True
-    for name, fn in paths.items():
-        U_, S_ = fn()
-        parity &= bool(torch.equal(U_.view(torch.int32), Us.view(torch.int32)) and
-                       torch.equal(S_.view(torch.int32), Ss.view(torch.int32)))
-    del U_, S_
 
-    def timed(fn, steps, launches_per_call):
+    def path_fns(I):
+        f = {"auto": lambda: L.scan_forward_auto(I, beta, 1.0, 0.0, u0),
+             "map_scan_v3_C64_K16": lambda: L.scan_forward_v3(I, beta, 1.0, 0.0, u0, C=64, K=16),
+             "serial": lambda: L.serial_forward(I, beta, 1.0, 0.0, u0)}
+        if Lb:
+            f[f"leadin_block_L{Lb}_W{Wb}"] = lambda: L.scan_forward_spec(I, beta, 1.0, 0.0, u0, L=Lb, W=Wb)
+        return f
+    ring = [path_fns(I) for I in Is]
+    parity = True
+    for fns in ring[:2]:
+        Us, Ss = fns["serial"]()
+        for name, fn in fns.items():
+            U_, S_ = fn()
+            parity &= bool(torch.equal(U_.view(torch.int32), Us.view(torch.int32)) and
+                           torch.equal(S_.view(torch.int32), Ss.view(torch.int32)))
+    del U_, S_, Us, Ss
+
+    def isolated_ms(replay, steps):
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         barrier()
         torch.cuda.synchronize(dev)
@@ -420,48 +516,35 @@ def run_c1(args, ws, rank, local):
             flush.fill_(1.0)
             torch.sum(evict, dim=0, out=sink)
             a.record(stream)
-            fn()
+            replay()
             b.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
-        ms = sorted(a.elapsed_time(b) for a, b in evs)
-        return sum(ms) / len(ms), launches_per_call * steps
-
-    def graphed(fn):
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            for _ in range(3):
-                fn()
-        stream.wait_stream(side)
-        torch.cuda.synchronize(dev)
-        gr = torch.cuda.CUDAGraph()
-        n0 = lib.lifb_kernel_launches()
-        with torch.cuda.graph(gr):
-            fn()
-        n1 = lib.lifb_kernel_launches()
-        torch.cuda.synchronize(dev)
-        return gr, n1 - n0
+        return sum(a.elapsed_time(b) for a, b in evs) / steps
 
     for _ in range(max(args.warmup, 3)):
-        for fn in paths.values():
-            fn()
+        for fns in ring:
+            for fn in fns.values():
+                fn()
     torch.cuda.synchronize(dev)
-    graphs = {k: graphed(fn) for k, fn in paths.items()}
     per_path = {}
     clk_rec = None
-    for k, (gr, nl) in graphs.items():
-        for _ in range(3):
-            gr.replay()
+    launches = 0
+    for k in ring[0]:
+        rt = RingTimer(torch, dev, stream, lib, [fns[k] for fns in ring], barrier)
+        nl = rt.launches_per_step
         if k == "auto":
             with ClockSampler(local) as clk:
-                ms, launches = timed(gr.replay, args.steps, nl)
+                ms = rt.ms_per_step(args.steps)
             clk_rec = clk.record()
+            launches = nl * args.steps
         else:
-            ms, _ = timed(gr.replay, args.steps, nl)
+            ms = rt.ms_per_step(args.steps)
         ms = max_over_ranks(ms)
+        ms_iso = max_over_ranks(isolated_ms(rt.single[0].replay, max(args.steps // 2, 5)))
         per_path[k] = {"ms": ms, "value": N * T * ws / (ms / 1e3), "launches_per_call": nl,
-                       "gbs": FWD_BYTES * N * T / (ms / 1e3) / 1e9}
+                       "gbs": FWD_BYTES * N * T / (ms / 1e3) / 1e9, "isolated_call_ms": ms_iso}
+        del rt
     ms = per_path["auto"]["ms"]
     units = N * T * ws
     value = units / (ms / 1e3)
@@ -469,14 +552,14 @@ def run_c1(args, ws, rank, local):
     for v in per_path.values():
         v["frac"] = v["gbs"] / hbm
     tpu = traffic_per_unit("c1_auto")
-    roofline = {"bound": "hbm", "kernel": "scan_forward_auto at config 1 (its launches: "
+    roofline = {"bound": "hbm", "kernel": "scan_forward_auto at config 1 (its launches per call: "
                 f"{per_path['auto']['launches_per_call']})", "achieved": per_path["auto"]["gbs"], "peak": hbm,
                 "peak_source": peak_kind, "unit": "GB/s", "frac": per_path["auto"]["frac"],
                 "traffic": (tpu * N * T) if tpu is not None else None, "algorithmic_bytes": FWD_BYTES * N * T}
 
     e2e = None
     if not args.no_e2e:
-        I_pin = I_h.pin_memory()
+        I_pin = I_hs[0].pin_memory()
         U_pin = torch.empty(T, N).pin_memory()
         S_pin = torch.empty(T, N).pin_memory()
 
@@ -488,25 +571,26 @@ def run_c1(args, ws, rank, local):
         for _ in range(3):
             e2e_step()
         n_e = max(args.steps // 2, 5)
-        ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_e)]
         barrier()
         torch.cuda.synchronize(dev)
-        for a, b in ee:
-            a.record(stream)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n_e):
             e2e_step()
-            b.record(stream)
+        b.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
-        ms_e = max_over_ranks(sum(a.elapsed_time(b) for a, b in ee) / n_e)
+        ms_e = max_over_ranks(a.elapsed_time(b) / n_e)
         e2e = {"value": units / (ms_e / 1e3), "unit": UNIT, "ms_per_step": ms_e,
                "h2d_bytes_per_step": T * N * 4, "d2h_bytes_per_step": 2 * T * N * 4,
-               "api": "pinned host I -> .to(cuda) -> scan_forward_auto -> U, S copied to pinned host buffers"}
+               "api": "pinned host I -> .to(cuda) -> scan_forward_auto -> U, S copied to pinned host buffers, "
+                      "steps back to back"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         v, threads, sample = cpu_oracle_rate(T, N, args.cpu_seconds, want_bwd=False, mu=C1_MU, sd=C1_SD, beta=beta)
-        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": sample.replace("serial forward + adjoint", "serial forward")}
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps({
             "metric": C1_METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -514,8 +598,11 @@ def run_c1(args, ws, rank, local):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded torch.Generator, config 1 shape)",
             "config": {"workload": C1_WORKLOAD, "global_neurons": N * ws, "seq_len": T,
                        "parallelism": f"batch-sharded x{ws}, no collective",
-                       "step": "scan_forward_auto, captured in a CUDA graph and replayed",
-                       "l2": "flushed between steps outside the events (256 MiB written, then 256 MiB read)"},
+                       "step": "scan_forward_auto; one CUDA graph holds one step per input set of the ring",
+                       "l2": f"inputs larger than L2: {args.steps} steps back to back over a ring of {C1_RING} input "
+                             f"sets ({C1_RING} x 48 MiB of I, U, S), one event pair around all of them; "
+                             "isolated_call_ms: one call after an L2 flush, its own event pair (launch latency "
+                             "included)"},
             "parity_bit_exact_vs_serial": parity, "paths": per_path,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clk_rec}), flush=True)
@@ -1271,6 +1358,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    numa_node = bind_numa(torch, dev)
     T, N = T_STEPS, N_PER_GPU
     g = torch.Generator().manual_seed(1000 + rank)
     I_h = (MU + SD * torch.randn(T, N, generator=g)).float()
@@ -1346,12 +1434,31 @@ def main():
     # eager: the autograd call as a training loop issues it, host overhead included
     ms_eager, _ = timed(step, args.steps)
     ms_eager = max_over_ranks(ms_eager)
-    # the same step captured once in a CUDA graph and replayed (device time)
+    # the same step captured once in a CUDA graph, each replay timed alone
+    # after an L2 flush (the event pair also holds the launch's latency)
     replay_step, per_step_launches = graphed(step)
     for _ in range(max(args.warmup, 3)):
         replay_step()
+    ms_isolated, _ = timed(replay_step, args.steps, per_step_launches)
+    ms_isolated = max_over_ranks(ms_isolated)
+    # the headline: steps back to back over a ring of input sets larger than
+    # L2 (each step's I and GS last touched C2_RING - 1 steps earlier, with
+    # more than L2's capacity of other traffic since), one event pair
+    ring_sets = [(I.clone().requires_grad_(True), torch.randn(T, N, generator=torch.Generator(device=dev).manual_seed(
+        2000 + 10 * rank + r), device=dev)) for r in range(C2_RING - 1)]
+    ring_sets.insert(0, (Iq, GS))
+
+    def ring_step(Ir, Gr):
+        def f():
+            Ir.grad = None
+            S_ = L.lif_tuned(Ir, u0, beta=BETA, theta=1.0, u_r=0.0, alpha=4.0, mode=args.mode) \
+                if args.mode != "auto" else L.lif_auto(Ir, u0, beta=BETA)
+            torch.autograd.backward(S_, Gr)
+        return f
+    ring = RingTimer(torch, dev, stream, lib, [ring_step(Ir, Gr) for Ir, Gr in ring_sets], barrier)
     with ClockSampler(local) as clk:
-        ms_local, launches = timed(replay_step, args.steps, per_step_launches)
+        ms_local = ring.ms_per_step(args.steps)
+    launches = ring.launches_per_step * args.steps
     ms = max_over_ranks(ms_local)
     value = units / (ms / 1e3)
 
@@ -1376,12 +1483,34 @@ def main():
     for _ in range(3):
         fwd_call()
         bwd_call()
-    rf, n_fwd = graphed(fwd_call)
-    rb, n_bwd = graphed(bwd_call)
-    ms_fwd, _ = timed(rf, args.steps, n_fwd)
-    ms_bwd, _ = timed(rb, args.steps, n_bwd)
-    ms_fwd = max_over_ranks(ms_fwd)
-    ms_bwd = max_over_ranks(ms_bwd)
+    # per call, back to back over the same ring (forward: I of each set;
+    # backward: that set's forward output and GS)
+    fwd_sets = [(Ir.detach(),) for Ir, _ in ring_sets]
+    bwd_sets = []
+    for (Ir,), (_, Gr) in zip(fwd_sets, ring_sets):
+        V_, _ = (L.serial_forward_v(Ir, BETA, 1.0, 0.0, u0) if vpath else
+                 L.scan_forward_auto(Ir, BETA, 1.0, 0.0, u0))
+        bwd_sets.append((Ir, V_, Gr))
+
+    def fwd_of(Ir):
+        if vpath:
+            return lambda: L.serial_forward_v(Ir, BETA, 1.0, 0.0, u0)
+        return (lambda: L.scan_forward_auto(Ir, BETA, 1.0, 0.0, u0)) if args.mode == "scan" else \
+            (lambda: L.serial_forward_auto(Ir, BETA, 1.0, 0.0, u0))
+
+    def bwd_of(Ir, Ur, Gr):
+        if vpath:
+            return lambda: L.lif_backward_v(Ur, Gr, BETA, 1.0, 4.0, C=T if args.mode == "serial" else
+                                            L.scan_chunk_bwd(T, N))
+        if args.mode == "scan":
+            return lambda: L.scan_backward_auto(Ir, u0, Ur, None, Gr, None, BETA, 1.0, 0.0, 4.0)
+        return lambda: L.serial_backward_auto(Ir, u0, Ur, None, Gr, None, BETA, 1.0, 0.0, 4.0)
+    rf = RingTimer(torch, dev, stream, lib, [fwd_of(*a) for a in fwd_sets], barrier)
+    rb = RingTimer(torch, dev, stream, lib, [bwd_of(*a) for a in bwd_sets], barrier)
+    n_fwd, n_bwd = rf.launches_per_step, rb.launches_per_step
+    ms_fwd = max_over_ranks(rf.ms_per_step(args.steps))
+    ms_bwd = max_over_ranks(rb.ms_per_step(args.steps))
+    del rf, rb, bwd_sets, fwd_sets
     hbm, peak_kind = peaks()
     per_call = {
         "fwd": {"ms": ms_fwd, "bytes": FWD_BYTES * N * T, "launches": n_fwd},
@@ -1441,9 +1570,40 @@ def main():
             e2e_step()
         ms_e2e, _ = timed(e2e_step, max(args.steps // 2, 5))
         ms_e2e = max_over_ranks(ms_e2e)
+        # the copy floor: the same bytes moved with nothing else, on all
+        # ranks at once (H2D of I and GS on one stream while S and dI come
+        # back on another, and the same copies one after the other)
+        dbuf = [torch.empty(T, N, device=dev) for _ in range(4)]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+        def copies(concurrent):
+            s_in.wait_stream(stream)
+            s_out.wait_stream(stream)
+            so = s_out if concurrent else s_in
+            with torch.cuda.stream(s_in):
+                dbuf[0].copy_(I_pin, non_blocking=True)
+                dbuf[1].copy_(GS_pin, non_blocking=True)
+            with torch.cuda.stream(so):
+                host_out[0].copy_(dbuf[2], non_blocking=True)
+                host_out[1].copy_(dbuf[3], non_blocking=True)
+            stream.wait_stream(s_in)
+            stream.wait_stream(s_out)
+        for _ in range(2):
+            copies(True)
+            copies(False)
+        ms_floor, _ = timed(lambda: copies(True), max(args.steps // 2, 5))
+        ms_floor = max_over_ranks(ms_floor)
+        ms_floor_serial, _ = timed(lambda: copies(False), max(args.steps // 2, 5))
+        ms_floor_serial = max_over_ranks(ms_floor_serial)
+        del dbuf
         e2e = {"value": units / (ms_e2e_host / 1e3), "unit": UNIT, "ms_per_step": ms_e2e_host,
                "h2d_bytes_per_step": 2 * N * T * 4 + N * 4, "d2h_bytes_per_step": 2 * N * T * 4 + N * 4,
                "api": "lif_tuned_host (C-ABI lifb_lif_fwd_bwd_host): pinned host I, GS, u0 in; host S, dI, du0 out",
+               "copy_floor_ms": ms_floor, "copy_floor_serial_ms": ms_floor_serial,
+               "copy_floor_note": "the step's H2D (I, GS) and D2H (S, dI) bytes alone between the same pinned host "
+                                  "buffers and the device, every rank at once; concurrent: H2D and D2H on two "
+                                  "streams; serial: one after the other",
+               "numa_node": numa_node,
                "unpipelined": {"value": units / (ms_e2e / 1e3), "ms_per_step": ms_e2e,
                                "api": "tensor.to(cuda) + lif_tuned + autograd.backward + copies back"}}
 
@@ -1464,11 +1624,16 @@ def main():
             "config": {"workload": "c2: lif_tuned fwd+bwd, B*N=16384 per GPU, T=1024, beta=0.99, x~N(0.05,0.2^2)",
                        "mode": args.mode, "global_neurons": N * ws, "seq_len": T,
                        "parallelism": f"batch-sharded x{ws}, no collective",
-                       "step": "lif_tuned forward + torch.autograd.backward, captured in a CUDA graph and replayed",
-                       "l2": "flushed between steps outside the events: 256 MiB written, then another 256 MiB read "
-                             "(cold L2, no dirty lines left from the flush)"},
+                       "step": "lif_tuned forward + torch.autograd.backward; one CUDA graph holds one step per "
+                               "input set of the ring",
+                       "l2": f"inputs larger than L2: the steps run back to back over a ring of {C2_RING} input sets "
+                             f"(I, GS: 128 MiB per set, 320 MiB touched per step), one event pair around all of "
+                             f"them; isolated_step: each graph replay alone after an L2 flush (256 MiB written, "
+                             f"then 256 MiB read), its own event pair"},
+            "isolated_step": {"ms_per_step": ms_isolated, "value": units / (ms_isolated / 1e3)},
             "eager": {"ms_per_step": ms_eager, "value": units / (ms_eager / 1e3),
-                      "note": "same step issued eagerly from Python each time (host overhead included)"},
+                      "note": "same step issued eagerly from Python each time after an L2 flush "
+                              "(host overhead included)"},
             "fwd": {"ms": ms_fwd, "value": units / (ms_fwd / 1e3), "gbs": per_call["fwd"]["gbs"],
                     "frac": per_call["fwd"]["frac"]},
             "bwd": {"ms": ms_bwd, "value": units / (ms_bwd / 1e3), "gbs": per_call["bwd"]["gbs"],

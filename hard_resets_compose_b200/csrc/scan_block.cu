@@ -314,9 +314,13 @@ __global__ void __launch_bounds__(MAPS ? 32 * kMaxChunksMaps : 32 * kMaxChunksSp
                 t0 = 0;
                 u = u0n;
             }
-            bool ok = true;
-            for (int m = t0 / C; m < w && ok; m++) ok = wait_rows(m);
-            if (ok) u = run_rows(u, xs + (size_t)t0 * kSlab + lane, w * C - t0, beta, theta, u_r);
+            // chunk by chunk, each as soon as its rows have landed: the
+            // lead-in overlaps the loads of the later chunks
+            for (int m = t0 / C; m < w; m++) {
+                if (!wait_rows(m)) break;
+                const int r0 = m * C > t0 ? m * C : t0;
+                u = run_rows(u, xs + (size_t)r0 * kSlab + lane, (m + 1) * C - r0, beta, theta, u_r);
+            }
         }
         sts[w * kSlab + lane] = u;
     }
