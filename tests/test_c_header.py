@@ -55,20 +55,16 @@ def test_header_compiles_as_c_and_links(tmp_path):
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc is not installed")
-def test_integration_c_example_compiles_and_links(tmp_path):
-    """The C caller shown in INTEGRATION.md compiles with warnings as errors and
-    links against liblifb.so and the CUDA runtime (running it needs a GPU)."""
-    import re
+def test_c_example_compiles_and_links(tmp_path):
+    """The C caller of the library (tests/c/lif_example.c) compiles with
+    warnings as errors and links against liblifb.so and the CUDA runtime
+    (running it needs a GPU)."""
     _lib.load()
     libdir = os.path.dirname(_lib._build.LIB)
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    blocks = re.findall(r"```c\n(.*?)```", text, flags=re.S)
-    assert len(blocks) == 1, "INTEGRATION.md should hold one C example"
-    src = tmp_path / "lif.c"
-    src.write_text(blocks[0])
+    src = os.path.join(ROOT, "tests", "c", "lif_example.c")
     cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
     cmd = ["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
-           "-I", os.path.join(cuda, "include"), str(src), "-o", str(tmp_path / "lif"), "-L", libdir, "-llifb",
+           "-I", os.path.join(cuda, "include"), src, "-o", str(tmp_path / "lif"), "-L", libdir, "-llifb",
            "-L", os.path.join(cuda, "lib64"), "-lcudart", f"-Wl,-rpath,{libdir}"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
