@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
                                                 float *__restrict__ U, float *__restrict__ Sout,
                                                 float *__restrict__ Ends, int64_t N, int64_t C, float beta,
                                                 float theta, float u_r, int64_t lead, float *__restrict__ LeadStarts,
-                                                float gamma, float delta, int *status)
+                                                float gamma, float delta, int *status, int64_t m0)
 {
     constexpr int NB = 32 * NPL;
     constexpr int kTile = R * NB;  // floats per tile
@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
     __shared__ __align__(8) uint64_t full[S];
     const int lane = threadIdx.x;
     const int64_t n0 = (int64_t)blockIdx.x * NB;
-    const int64_t m = blockIdx.y;
+    const int64_t m = blockIdx.y + m0;  // chunks m0..M-1 (m0 > 0: the caller runs the first ones)
     const int64_t row0 = m * C;
     const int64_t nfull = C / R;
     const int rem = (int)(C - nfull * R);
@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
     Vec<NPL> u;
     if (act) {
         if (leading) {
-            if (lrow0 == 0) {
+            if (lrow0 == 0 && u0) {  // without u0, a lead-in from row 0 starts from u_r too
                 u = ld_vec<NPL>(u0 + nl);
             } else {
 #pragma unroll
@@ -638,30 +638,31 @@ int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm)
 template <int NPL, bool VOUT, bool AFF, bool DEEP>
 static void launch_fwd(const CUtensorMap *maps, const float *u0, const float *Starts, int64_t start_stride, float *U,
                        float *S, float *Ends, int64_t N, int64_t M, int64_t C, float beta, float theta, float u_r,
-                       int64_t lead, float *LeadStarts, float gamma, float delta, int *status, cudaStream_t s)
+                       int64_t lead, float *LeadStarts, float gamma, float delta, int *status, cudaStream_t s,
+                       int64_t m0)
 {
     constexpr int NB = 32 * NPL;
     constexpr int R = FwdTile<NPL, DEEP>::R, ST = FwdTile<NPL, DEEP>::S;
     const size_t smem = (size_t)(ST + 4) * R * NB * 4;
     auto kern = k_fwd_tma<NPL, R, ST, VOUT, AFF>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)M);
+    dim3 g((unsigned)((N + NB - 1) / NB), (unsigned)(M - m0));
     count_launches(1);
     kern<<<g, 32, smem, s>>>(maps[0], maps[1], maps[2], u0, Starts, start_stride, U, S, Ends, N, C, beta, theta, u_r,
-                             lead, LeadStarts, gamma, delta, status);
+                             lead, LeadStarts, gamma, delta, status, m0);
 }
 
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
-                    int64_t start_stride, int64_t lead, float *LeadStarts, bool vout, Reset rs)
+                    int64_t start_stride, int64_t lead, float *LeadStarts, bool vout, Reset rs, int64_t first_chunk)
 {
     const bool aff = rs.aff;
     const float gamma = rs.gamma, delta = rs.delta;
     const void *p[] = {I, u0, Starts, U, S, Ends, LeadStarts};
     if (!tma_ok(p, 7, N) || C <= 0 || T % C) return false;
     const int64_t M = T / C;
-    if (M > 65535) return false;
-    const int npl = pick_npl(N, M, LIFB_FWD_NPL4_MIN_CTAS_PER_SM);
+    if (M > 65535 || first_chunk < 0 || first_chunk >= M) return false;
+    const int npl = pick_npl(N, M - first_chunk, LIFB_FWD_NPL4_MIN_CTAS_PER_SM);
     const int R = npl == 4 ? FwdTile<4>::R : FwdTile<1>::R;
     if (lead > 0) {  // lead-in tiles: whole tiles inside whole chunks
         if (C % R) return false;
@@ -673,16 +674,16 @@ bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float 
         return false;
     int *status = device_status_ptr();
     // one chunk, one neuron per lane: the deeper ring
-    const bool deep = npl == 1 && M == 1 && lead == 0;
+    const bool deep = npl == 1 && M == 1 && lead == 0 && first_chunk == 0;
     auto go = [&](auto npl_c, auto vout_c, auto aff_c) {
         constexpr int kNpl = decltype(npl_c)::value;
         constexpr bool kV = decltype(vout_c)::value, kA = decltype(aff_c)::value;
         if (kNpl == 1 && deep)
             launch_fwd<kNpl, kV, kA, true>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r,
-                                           lead, LeadStarts, gamma, delta, status, s);
+                                           lead, LeadStarts, gamma, delta, status, s, first_chunk);
         else
             launch_fwd<kNpl, kV, kA, false>(maps, u0, Starts, start_stride, U, S, Ends, N, M, C, beta, theta, u_r,
-                                            lead, LeadStarts, gamma, delta, status, s);
+                                            lead, LeadStarts, gamma, delta, status, s, first_chunk);
     };
     using I1 = std::integral_constant<int, 1>;
     using I4 = std::integral_constant<int, 4>;

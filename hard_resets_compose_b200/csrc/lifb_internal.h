@@ -84,10 +84,12 @@ int pick_npl(int64_t N, int64_t M, int min_ctas_per_sm);
 // (from u_r, or from u0 when they reach row 0), streamed through the same
 // ring, and records that start in LeadStarts[m] (Starts is then ignored for
 // m >= 1); requires C % R == 0 (false otherwise), lead is rounded up to R.
+// first_chunk > 0: only chunks first_chunk..M-1 run (the caller runs the
+// earlier ones); a lead-in that reaches row 0 starts from u_r when u0 is NULL.
 bool fwd_replay_tma(const float *I, const float *u0, const float *Starts, float *U, float *S, float *Ends,
                     int64_t T, int64_t N, int64_t C, float beta, float theta, float u_r, cudaStream_t s,
                     int64_t start_stride = 1, int64_t lead = 0, float *LeadStarts = nullptr, bool vout = false,
-                    Reset rs = {});
+                    Reset rs = {}, int64_t first_chunk = 0);
 // Reverse adjoint sweep per chunk: mode 0 writes Lam from LamEnd (NULL: 0)
 // and, when P is given, also the chunk maps; mode 1 writes only P, Q.
 // P[m] = prod of a_t over chunk m, Q[m] = lam at the chunk's first row.

@@ -211,6 +211,63 @@ int lifb_scan_fwd_spec(const float *I, const float *u0, float *U, float *S, int6
     return spec_done("lifb_scan_fwd_spec");
 }
 
+int lifb_tshard_fwd_tail(const float *I, float *U, float *S, int64_t T, int64_t N, float beta, float theta, float u_r,
+                         int64_t L, int64_t W, float *end_guess, void *workspace, size_t workspace_bytes, void *stream)
+{
+    LIFB_RANGE("lifb_tshard_fwd_tail");
+    int st = spec_check("lifb_tshard_fwd_tail", T, N, L, W, 0);
+    if (st) return st;
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (T / L < 2 || W <= 0 || !end_guess) {
+        lifb::set_last_error("lifb_tshard_fwd_tail: needs at least two segments, W > 0 and end_guess");
+        return LIFB_ERR_INVALID_ARGUMENT;
+    }
+    if ((st = spec_ws("lifb_tshard_fwd_tail", T, N, L, workspace, workspace_bytes))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t NS = T / L;
+    SpecScratch w = spec_carve(workspace, NS, N);
+    // segments 1..NS-1, each from its W-row lead-in (from u_r: the slice's
+    // entry is not known yet), streamed through the replay's TMA ring;
+    // segment 0 waits for the entry (_head)
+    if (!lifb::fwd_replay_tma(I, nullptr, nullptr, U, S, w.Ends, T, N, L, beta, theta, u_r, s, 1, W, w.Starts, false,
+                              {}, 1)) {
+        lifb::set_last_error("lifb_tshard_fwd_tail: needs N % 4 == 0, 16-byte aligned tensors and L a multiple of "
+                             "the replay's tile");
+        return LIFB_ERR_UNSUPPORTED;
+    }
+    cudaMemcpyAsync(end_guess, w.Ends + (NS - 1) * N, (size_t)N * 4, cudaMemcpyDeviceToDevice, s);
+    return spec_done("lifb_tshard_fwd_tail");
+}
+
+int lifb_tshard_fwd_head(const float *I, const float *entry, float *U, float *S, float *end, int64_t T, int64_t N,
+                         float beta, float theta, float u_r, int64_t L, void *workspace, size_t workspace_bytes,
+                         void *stream)
+{
+    LIFB_RANGE("lifb_tshard_fwd_head");
+    int st = spec_check("lifb_tshard_fwd_head", T, N, L, 0, 0);
+    if (st) return st;
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (T / L < 2 || !entry || !end) {
+        lifb::set_last_error("lifb_tshard_fwd_head: needs at least two segments, entry and end");
+        return LIFB_ERR_INVALID_ARGUMENT;
+    }
+    if ((st = spec_ws("lifb_tshard_fwd_head", T, N, L, workspace, workspace_bytes))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t NS = T / L;
+    SpecScratch w = spec_carve(workspace, NS, N);
+    // segment 0 from the entry (one chain of L rows: the caller keeps L
+    // short), then every segment whose start differs from the exact end
+    // before it, replayed until its rows rejoin
+    cudaMemcpyAsync(w.Starts, entry, (size_t)N * 4, cudaMemcpyDeviceToDevice, s);
+    if (!lifb::fwd_replay_tma(I, entry, nullptr, U, S, w.Ends, L, N, L, beta, theta, u_r, s)) {
+        lifb::set_last_error("lifb_tshard_fwd_head: needs N % 4 == 0 and 16-byte aligned tensors");
+        return LIFB_ERR_UNSUPPORTED;
+    }
+    lifb::fwd_fixup(I, w.Starts, 1, U, S, w.Ends, w.EndsNew, w.Changed, N, NS, L, beta, theta, u_r, nullptr, s);
+    cudaMemcpyAsync(end, U + (T - 1) * N, (size_t)N * 4, cudaMemcpyDeviceToDevice, s);
+    return spec_done("lifb_tshard_fwd_head");
+}
+
 int lifb_scan_fwd_spec_begin(const float *I, int64_t T, int64_t N, float beta, float theta, float u_r, int64_t L,
                              int64_t W, float *end_guess, void *workspace, size_t workspace_bytes, void *stream)
 {

@@ -195,6 +195,54 @@ class CudaSliceOps:
                                            self.G, self.K, self.K2, *self._ws(), stream_of(I)), "tshard apply")
         return entry, U, S, end
 
+    # Segments of a slice's replay in entry mode "speculate": the first
+    # segment is replayed alone once the entry has arrived (one chain of L
+    # rows on the step's critical path), the others at once from their
+    # lead-ins before that, so L is short: 4096 rows, with 4096-row lead-ins
+    # (config 4's trajectories merge within ~2100 rows at p99).
+    TAIL_L = 4096
+
+    def tail_segment(self):
+        """(L, W) of the tail/head forward of this slice, or None when the
+        slice has fewer than two segments (then the lead-in pass is used)."""
+        from .lifscan import SPEC_LEAD
+        L = self.TAIL_L
+        if self.T % L or self.T // L < 2 or self.N % 4:
+            return None
+        return L, SPEC_LEAD
+
+    def fwd_tail(self, I):
+        """U, S of segments 1.. of the slice from their fused lead-ins, and the
+        guess of the slice's final state (lifb_tshard_fwd_tail)."""
+        L, W = self.tail_segment()
+        ws = self._tail_ws(L)
+        U = torch.empty_like(I)
+        S = torch.empty_like(I)
+        g = torch.empty(self.N, device=self.dev)
+        with torch.cuda.device(self.dev):
+            check(self.L.lifb_tshard_fwd_tail(ptr(I), ptr(U), ptr(S), self.T, self.N, self.beta, self.theta, self.u_r,
+                                              L, W, ptr(g), ptr(ws), ws.numel(), stream_of(I)),
+                  "tshard forward (tail)")
+        return U, S, g
+
+    def fwd_head(self, I, entry, U, S):
+        """Segment 0 from `entry` and the fix-up of the slice
+        (lifb_tshard_fwd_head): U, S exact for entry; returns the end state."""
+        L, _ = self.tail_segment()
+        ws = self._tail_ws(L)
+        end = torch.empty(self.N, device=self.dev)
+        with torch.cuda.device(self.dev):
+            check(self.L.lifb_tshard_fwd_head(ptr(I), ptr(entry), ptr(U), ptr(S), ptr(end), self.T, self.N, self.beta,
+                                              self.theta, self.u_r, L, ptr(ws), ws.numel(), stream_of(I)),
+                  "tshard forward (head)")
+        return end
+
+    def _tail_ws(self, L):
+        if getattr(self, "_tws", None) is None:
+            nb = self.L.lifb_scan_fwd_spec_workspace_bytes(self.T, self.N, L)
+            self._tws = torch.empty(max(nb, 1), dtype=torch.uint8, device=self.dev)
+        return self._tws
+
     def _spec_ws(self):
         if getattr(self, "_sws", None) is None:
             from .lifscan import SPEC_LEAD, spec_segment
@@ -289,6 +337,19 @@ def tshard_forward(I, u0, ops, comm, info=None, entry_mode="speculate", timeline
         m = ops.slice_map(I, envs, r, u0)
         maps = comm.all_gather(m)
         entry, U, S, end = ops.apply(I, maps, r, u0)
+    elif entry_mode == "speculate" and getattr(ops, "tail_segment", lambda: None)():
+        # every segment but the first replays at once from its fused lead-in;
+        # the last one's end guesses this slice's final state, which the next
+        # slice takes as its entry; then the first segment from the entry and
+        # the slice's fix-up
+        _mark(timeline, "start", I)
+        U, S, guess = ops.fwd_tail(I)
+        _mark(timeline, "tail", I)
+        entry = comm.shift(guess)
+        entry = u0.clone() if r == 0 else entry
+        _mark(timeline, "shift", I)
+        end = ops.fwd_head(I, entry, U, S)
+        _mark(timeline, "head", I)
     elif entry_mode == "speculate":
         # the previous slice's last rows lead the guess (u_r before them) to
         # the exact entry state in all but a few neurons

@@ -391,6 +391,26 @@ int lifb_alif_bwd_scan(const float *I, const float *u0, const float *w0, const f
                        float theta0, float alpha, int64_t C, void *workspace, size_t workspace_bytes,
                        void *stream);
 
+/* Time-sharded forward, the two halves of a slice's replay around the hand-over
+ * of its end state (workspace: lifb_scan_fwd_spec_workspace_bytes(T, N, L)).
+ * _tail replays segments 1..T/L-1 of the slice at once, each from a W-row
+ * lead-in from u_r streamed through the replay (no separate lead-in pass),
+ * and writes end_guess = the last segment's end: the slice's final state
+ * whenever that segment's guessed start was right, the next slice's entry
+ * guess.  _head, once this slice's entry is known, replays segment 0 from it,
+ * then every segment whose start differs bit for bit from the exact end
+ * before it until its rows rejoin, and writes end = U[T-1].  U, S are then
+ * exact for `entry`.  The time-sharded scan has no reference counterpart (the
+ * reference scans a whole sequence on one device, lifscan/triton_lif.py:935-983). */
+int lifb_tshard_fwd_tail(const float *I, float *U, float *S, int64_t T, int64_t N,
+                         float beta, float theta, float u_r, int64_t L, int64_t W,
+                         float *end_guess, void *workspace, size_t workspace_bytes,
+                         void *stream);
+int lifb_tshard_fwd_head(const float *I, const float *entry, float *U, float *S,
+                         float *end, int64_t T, int64_t N, float beta, float theta,
+                         float u_r, int64_t L, void *workspace, size_t workspace_bytes,
+                         void *stream);
+
 /* ---- Time-sharded scan (one slice of the time axis per GPU) ----------------
  * The reference scans one sequence on one device (lifscan/triton_lif.py:
  * 944-983, scan_forward_v4; :512-526, scan_backward_tiled).  These phases

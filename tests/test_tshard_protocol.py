@@ -34,17 +34,20 @@ def _free_port():
 
 
 def _slice_run(comm, case, mode, info, K=8, K3=32):
-    """mode: "maps" (oracle slice maps), "corrupt" (maps that guess 0.5) or
-    "speculate" (no maps, every later slice starts from u_r); K, K3: chunk
-    and slice map capacities."""
+    """mode: "maps" (oracle slice maps), "corrupt" (maps that guess 0.5),
+    "speculate" (no maps: segments after the first from lead-ins, the last
+    one's end handed on as the next slice's entry guess) or
+    "speculate_leadin" (the same with a separate lead-in pass for the guess);
+    K, K3: chunk and slice map capacities."""
     from hard_resets_compose_b200 import tshard
     T_total, N, mu, sd, beta = CASES[case]
     I, u0, GS = gen(T_total, N, mu, sd, seed=3, u0_sd=0.3, grad=True)
     a, b = tshard.slice_rows(T_total, comm.world, comm.rank)
-    ops = OracleSliceOps(b - a, N, beta, 1.0, 0.0, C=64, K=K, K3=K3, mode="corrupt" if mode == "corrupt" else "maps")
+    ops_mode = {"corrupt": "corrupt", "speculate_leadin": "no_tail"}.get(mode, "maps")
+    ops = OracleSliceOps(b - a, N, beta, 1.0, 0.0, C=64, K=K, K3=K3, mode=ops_mode)
     It, u0t, Gt = (torch.from_numpy(np.ascontiguousarray(x)) for x in (I[a:b], u0, GS[a:b]))
     U, S, entry = tshard.tshard_forward(It, u0t, ops, comm, info=info,
-                                        entry_mode="speculate" if mode == "speculate" else "maps")
+                                        entry_mode="speculate" if mode.startswith("speculate") else "maps")
     Lam, du0 = tshard.tshard_backward(It, entry, U, Gt, ops, comm, beta)
     return U.numpy(), S.numpy(), Lam.numpy(), du0.numpy()
 
@@ -65,7 +68,7 @@ def _check(case, world, results):
         assert not r[3].any()
 
 
-@pytest.mark.parametrize("mode", ("maps", "corrupt", "speculate"))
+@pytest.mark.parametrize("mode", ("maps", "corrupt", "speculate", "speculate_leadin"))
 @pytest.mark.parametrize("case", sorted(CASES))
 @pytest.mark.parametrize("world", (2, 3, 4, 6, 8))
 def test_protocol_threads(case, mode, world):

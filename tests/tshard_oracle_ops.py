@@ -85,6 +85,38 @@ class OracleSliceOps:
         U, S = O.serial_forward(I.numpy(), float(self.beta), float(self.theta), float(self.u_r), u)
         return (torch.from_numpy(u), torch.from_numpy(U), torch.from_numpy(S), torch.from_numpy(U[-1].copy()))
 
+    def tail_segment(self, L=64, W=48):
+        """(L, W) of the tail/head forward (lifb_tshard_fwd_tail/_head), or
+        None for slices of fewer than two segments."""
+        if self.mode == "no_tail" or self.T % L or self.T // L < 2:
+            return None
+        return L, W
+
+    def fwd_tail(self, I):
+        """Segments 1.. from W-row lead-ins from u_r; returns (U, S, guess of
+        the slice's final state = the last segment's end)."""
+        L, W = self.tail_segment()
+        x = I.numpy()
+        U = np.zeros_like(x)
+        S = np.zeros_like(x)
+        b, th, ur = float(self.beta), float(self.theta), float(self.u_r)
+        for sg in range(1, self.T // L):
+            t0 = max(sg * L - W, 0)
+            u = np.full(self.N, self.u_r, np.float32)
+            if t0 < sg * L:
+                Ul, _ = O.serial_forward(x[t0:sg * L], b, th, ur, u)
+                u = Ul[-1].copy()
+            Us, Ss = O.serial_forward(x[sg * L:(sg + 1) * L], b, th, ur, u)
+            U[sg * L:(sg + 1) * L], S[sg * L:(sg + 1) * L] = Us, Ss
+        return torch.from_numpy(U), torch.from_numpy(S), torch.from_numpy(U[-1].copy())
+
+    def fwd_head(self, I, entry, U, S):
+        """Segment 0 from entry and the fix-up: U, S exact for entry."""
+        U2, S2 = O.serial_forward(I.numpy(), float(self.beta), float(self.theta), float(self.u_r), entry.numpy())
+        U.numpy()[:] = U2
+        S.numpy()[:] = S2
+        return torch.from_numpy(U2[-1].copy())
+
     def spec_begin(self, I, lead=256):
         x = I.numpy()[-min(lead, self.T):]
         Ug, _ = O.serial_forward(x, float(self.beta), float(self.theta), float(self.u_r),
