@@ -1218,7 +1218,11 @@ def run_network(args, ws, rank, local):
     LIF network, B = 64 per GPU, T = 1024, beta = 0.9, Kaiming-uniform init,
     leaky readout, cross-entropy over 20 random labels, synthetic Bernoulli
     raster (rates U(0.5%, 4%)).  Data parallel: one bucketed all-reduce of the
-    weight gradients per step when N > 1."""
+    weight gradients per step when N > 1.  The headline runs both LIF layers
+    through the fused spike-input producer (producer="spike"); the same step
+    with nn.Linear then lif_tuned (producer="linear") is timed beside, and the
+    two forwards' spikes are compared bit for bit.  The raster (183 MB) is
+    larger than L2."""
     import torch
     import torch.distributed as dist
     import torch.nn as nn
@@ -1233,68 +1237,83 @@ def run_network(args, ws, rank, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     lib = _lib.load()
     T, B, H = 1024, 64, 256
-    torch.manual_seed(0)
-    net = Net(mode="scan", beta=0.9, H=H, init="kaiming", readout="leaky").to(dev)
     x, y = synthetic_batch(T, B, seed=1000 + rank, device=dev)
-    opt = torch.optim.Adam(net.parameters(), lr=1e-3, capturable=True)
-    params = list(net.parameters())
     stream = torch.cuda.current_stream(dev)
 
-    def fwd_bwd():
-        loss = nn.functional.cross_entropy(net(x)[0], y)
-        loss.backward()
-        return loss
+    def make(producer):
+        torch.manual_seed(0)
+        net = Net(mode="scan", beta=0.9, H=H, init="kaiming", readout="leaky", producer=producer).to(dev)
+        opt = torch.optim.Adam(net.parameters(), lr=1e-3, capturable=True)
+        params = list(net.parameters())
 
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(stream)
-    with torch.cuda.stream(side):
-        for _ in range(3):
-            opt.zero_grad(set_to_none=True)
+        def fwd_bwd():
+            loss = nn.functional.cross_entropy(net(x)[0], y)
+            loss.backward()
+            return loss
+
+        with torch.no_grad():
+            spikes = [s.clone() for s in net(x)[1]]
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                opt.zero_grad(set_to_none=True)
+                fwd_bwd()
+                opt.step()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        opt.zero_grad(set_to_none=True)
+        g_fb = torch.cuda.CUDAGraph()
+        n0 = lib.lifb_kernel_launches()
+        with torch.cuda.graph(g_fb):
             fwd_bwd()
+        launches = lib.lifb_kernel_launches() - n0
+        g_opt = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_opt):
             opt.step()
-    stream.wait_stream(side)
-    torch.cuda.synchronize(dev)
-    opt.zero_grad(set_to_none=True)
-    g_fb = torch.cuda.CUDAGraph()
-    n0 = lib.lifb_kernel_launches()
-    with torch.cuda.graph(g_fb):
-        fwd_bwd()
-    launches = lib.lifb_kernel_launches() - n0
-    g_opt = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_opt):
-        opt.step()
-    flat = torch.empty(sum(p.numel() for p in params), device=dev)
+        flat = torch.empty(sum(p.numel() for p in params), device=dev)
 
-    def step():
-        g_fb.replay()
-        if ws > 1:  # data parallel: average the weight gradients (about 1 MB)
-            torch.cat([p.grad.reshape(-1) for p in params], out=flat)
-            dist.all_reduce(flat)
-            flat.div_(ws)
-            o = 0
-            for p in params:
-                p.grad.copy_(flat[o:o + p.numel()].view_as(p.grad))
-                o += p.numel()
-        g_opt.replay()
+        def step():
+            g_fb.replay()
+            if ws > 1:  # data parallel: average the weight gradients (about 1 MB)
+                torch.cat([p.grad.reshape(-1) for p in params], out=flat)
+                dist.all_reduce(flat)
+                flat.div_(ws)
+                o = 0
+                for p in params:
+                    p.grad.copy_(flat[o:o + p.numel()].view_as(p.grad))
+                    o += p.numel()
+            g_opt.replay()
+        # the graphs hold raw pointers into the net's parameters and the
+        # optimizer's state: both must live as long as the graphs do
+        return step, launches, spikes, (g_fb, g_opt, net, opt)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clk:
+    def time_steps(step, steps, sampler=None):
+        for _ in range(max(args.warmup, 3)):
+            step()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
         for a, b in evs:
             a.record(stream)
             step()
             b.record(stream)
         torch.cuda.synchronize(dev)
-    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
-    if ws > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+        if ws > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    step_s, launches, spikes_s, keep_s = make("spike")
+    step_l, _, spikes_l, keep_l = make("linear")
+    same_spikes = all(torch.equal(a, b) for a, b in zip(spikes_s, spikes_l))
+    with ClockSampler(local) as clk:
+        ms = time_steps(step_s, args.steps)
+    ms_linear = time_steps(step_l, max(args.steps // 2, 3))
     units = 2 * B * H * T * ws  # LIF neuron-steps per step, both layers, all ranks
     if rank == 0:
         print(json.dumps({
@@ -1305,9 +1324,15 @@ def run_network(args, ws, rank, local):
             "config": {"workload": "c3: network training step (forward, backward, Adam)", "beta": 0.9,
                        "init": "kaiming-uniform", "readout": "leaky (non-spiking integrator, mean over T)",
                        "lif_mode": "scan", "batch_per_gpu": B, "seq_len": T,
+                       "producer": "spike (fused spike-input Linear -> LIF forward, lifb_spike_linear_lif_fwd)",
                        "parallelism": f"data-parallel x{ws}, gradient all-reduce per step",
-                       "step": "forward+backward and Adam each captured in a CUDA graph"},
+                       "step": "forward+backward and Adam each captured in a CUDA graph",
+                       "l2": "the input raster (183 MB) and every layer tensor (64 MB) exceed or fill L2"},
+            "linear_producer": {"ms_per_step": ms_linear, "value": units / (ms_linear / 1e3),
+                                "note": "the same step with nn.Linear then lif_tuned in both LIF layers"},
+            "spikes_bit_equal_between_producers": same_spikes,
             "gpu_launches": launches * args.steps, "clocks": clk.record()}), flush=True)
+    del keep_s, keep_l
     if ws > 1:
         dist.destroy_process_group()
 

@@ -11,6 +11,13 @@ integrator y_t = beta*y_{t-1} + W s_t averaged over time), which runs on the
 same kernels: the serial forward with theta = +inf never spikes, and its
 adjoint with the upstream gradient on U is the integrator's backward.
 
+`producer="spike"` runs each LIF layer's Linear and recurrence as one fused
+kernel (lifb_spike_linear_lif_fwd) for spike inputs: I is never written to
+memory, each of its elements sums the active inputs' weights in the order
+cuBLAS's fp32 GEMM does, so the spikes are the same bits as with
+`producer="linear"` (nn.Linear, then lif_tuned); the backward is the same
+adjoint from V followed by the Linear's gradient GEMMs.
+
 The SHD data loader of the reference (h5py, :12-27) is not part of this
 package; inputs are dense [T, B, 700] spike rasters.
 """
@@ -21,23 +28,83 @@ import math
 import torch
 import torch.nn as nn
 
+from . import _lib
 from . import lifscan as L
+from ._lib import check, ptr, stream_of
+
+
+class SpikeLinearLIF(torch.autograd.Function):
+    """Linear on a spike input then lif_tuned's hard-reset LIF (theta, u_r,
+    sigmoid surrogate alpha, detached reset), forward fused in one kernel
+    (lifb_spike_linear_lif_fwd).  Returns S [T, B, Dout]; the backward is
+    lif_tuned's adjoint from V, then the Linear's gradients."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, beta, theta, u_r, alpha, mode):
+        x = x.contiguous()
+        T, B, din = x.shape
+        dout = weight.shape[0]
+        V = torch.empty(T, B * dout, device=x.device)
+        S = torch.empty(T, B * dout, device=x.device)
+        lib = _lib.load()
+        with torch.cuda.device(x.device):
+            check(lib.lifb_spike_linear_lif_fwd(ptr(x), ptr(weight.contiguous()), ptr(None if bias is None else
+                                                                                   bias.contiguous()),
+                                                None, ptr(V), ptr(S), T, B, din, dout, float(beta), float(theta),
+                                                float(u_r), stream_of(x)), "spike_linear_lif")
+        ctx.save_for_backward(x, weight, V)
+        ctx.cfg = (beta, theta, alpha, mode, bias is not None)
+        return S.view(T, B, dout)
+
+    @staticmethod
+    def backward(ctx, gS):
+        x, weight, V = ctx.saved_tensors
+        beta, theta, alpha, mode, has_bias = ctx.cfg
+        T, N = V.shape
+        B, din, dout = x.shape[1], x.shape[2], weight.shape[0]
+        # lif_tuned's backward for this shape (its forward is the single pass)
+        lam = L.lif_backward_v(V, gS.reshape(T, N), beta, theta, alpha,
+                               C=T if mode == "serial" else L.scan_chunk_bwd(T, N))
+        dI = lam.reshape(T * B, dout)
+        gx = dI.mm(weight).reshape(T, B, din) if ctx.needs_input_grad[0] else None
+        gw = dI.t().mm(x.reshape(T * B, din)) if ctx.needs_input_grad[1] else None
+        gb = dI.sum(0) if has_bias and ctx.needs_input_grad[2] else None
+        _lib.poll_device("spike_linear_lif")
+        return gx, gw, gb, None, None, None, None, None
+
+
+def spike_linear_lif(x, weight, bias, beta, theta=1.0, u_r=0.0, alpha=4.0, mode="scan"):
+    """S = lif_tuned(linear(x, weight, bias).reshape(T, -1), 0, ...) for a
+    spike input x [T, B, Din], forward fused (SpikeLinearLIF)."""
+    return SpikeLinearLIF.apply(x, weight, bias, beta, theta, u_r, alpha, mode)
+
+
+def spike_producer_applies(din, dout):
+    """True when the fused producer serves a Linear(din, dout) layer."""
+    return 0 < din <= 1024 and dout % 32 == 0
 
 
 class LIFLayer(nn.Module):
-    """Linear(din, dout) then a hard-reset LIF over time (lifscan/shdnet.py:30-50)."""
+    """Linear(din, dout) then a hard-reset LIF over time (lifscan/shdnet.py:30-50).
+    producer="spike": the fused spike-input producer (the input must hold
+    0/1 spikes), where it applies; "linear": nn.Linear then lif_tuned."""
 
-    def __init__(self, din, dout, beta, mode="scan", K=16, repair=10 ** 6, init="reference"):
+    def __init__(self, din, dout, beta, mode="scan", K=16, repair=10 ** 6, init="reference", producer="linear"):
         super().__init__()
         self.fc = nn.Linear(din, dout)
         if init == "reference":
             nn.init.uniform_(self.fc.weight, -1.5 / din ** 0.5, 1.5 / din ** 0.5)
         elif init != "kaiming":
             raise ValueError(f"unknown init {init!r}")
-        self.beta, self.mode, self.K, self.repair = beta, mode, K, repair
+        if producer not in ("linear", "spike"):
+            raise ValueError(f"unknown producer {producer!r}")
+        self.beta, self.mode, self.K, self.repair, self.producer = beta, mode, K, repair, producer
 
     def forward(self, x):
         Tn, B, _ = x.shape
+        if (self.producer == "spike" and self.mode in ("scan", "serial") and x.is_cuda
+                and spike_producer_applies(self.fc.in_features, self.fc.out_features)):
+            return spike_linear_lif(x, self.fc.weight, self.fc.bias, self.beta, 1.0, 0.0, 4.0, self.mode)
         I = self.fc(x).reshape(Tn, -1).contiguous()
         u0 = torch.zeros(I.shape[1], device=I.device)
         if self.mode == "auto":
@@ -75,10 +142,11 @@ class _LeakyIntegrator(torch.autograd.Function):
 class Net(nn.Module):
     """700-H-H-n_out network (lifscan/shdnet.py:53-66)."""
 
-    def __init__(self, mode="scan", beta=0.95, H=256, n_out=20, din=700, init="reference", readout="mean"):
+    def __init__(self, mode="scan", beta=0.95, H=256, n_out=20, din=700, init="reference", readout="mean",
+                 producer="linear"):
         super().__init__()
-        self.l1 = LIFLayer(din, H, beta, mode, init=init)
-        self.l2 = LIFLayer(H, H, beta, mode, init=init)
+        self.l1 = LIFLayer(din, H, beta, mode, init=init, producer=producer)
+        self.l2 = LIFLayer(H, H, beta, mode, init=init, producer=producer)
         self.out = nn.Linear(H, n_out)
         if readout not in ("mean", "leaky"):
             raise ValueError(f"unknown readout {readout!r}")

@@ -391,6 +391,24 @@ int lifb_alif_bwd_scan(const float *I, const float *u0, const float *w0, const f
                        float theta0, float alpha, int64_t C, void *workspace, size_t workspace_bytes,
                        void *stream);
 
+/* Fused forward of one layer of a spiking network: a Linear layer on a spike
+ * input followed by the hard-reset LIF.  X [T, B, Din] (0/1 spikes), W [Dout,
+ * Din] and bias [Dout] (NULL: none) as torch.nn.Linear holds them, u0 [B*Dout]
+ * (NULL: zeros); writes V (pre-reset potentials, for the adjoint from V) and S,
+ * both [T, B*Dout] with neuron b*Dout + j, the layout of
+ * fc(x).reshape(T, -1) (lifscan/shdnet.py:39).  I = X W^T + bias is formed in
+ * shared memory and consumed there, never written: each element sums the
+ * active inputs' weights in input order from 0 and adds the bias last, the
+ * order of cuBLAS's fp32 GEMM on such an input, so S equals the unfused
+ * Linear -> lif_tuned (lifscan/shdnet.py:38-45, triton_lif.py:654-687) bit for
+ * bit.  Needs Dout % 32 == 0 and Din <= 1024 (LIFB_ERR_UNSUPPORTED otherwise;
+ * the caller then runs the unfused layer).  Replaces the forward of
+ * shdnet.LIFLayer (lifscan/shdnet.py:30-50). */
+int lifb_spike_linear_lif_fwd(const float *X, const float *W, const float *bias,
+                              const float *u0, float *V, float *S, int64_t T, int64_t B,
+                              int64_t Din, int64_t Dout, float beta, float theta,
+                              float u_r, void *stream);
+
 /* Time-sharded forward, the two halves of a slice's replay around the hand-over
  * of its end state (workspace: lifb_scan_fwd_spec_workspace_bytes(T, N, L)).
  * _tail replays segments 1..T/L-1 of the slice at once, each from a W-row

@@ -94,3 +94,54 @@ def test_network_c3_full_shape(cuda, readout, init, beta, scale):
     assert rel(logits.detach().cpu().numpy(), rlogits.detach().cpu().numpy()) < 1e-6
     for g, rg in zip(grads, rgrads):
         assert rel(g.cpu().numpy(), rg.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("T,B,din,dout,rate,scale", ((1024, 64, 700, 256, 0.0225, 6.0), (1024, 64, 256, 256, 0.05, 3.0),
+                                                   (100, 3, 37, 64, 0.2, 2.0), (257, 5, 1024, 32, 0.01, 10.0)))
+def test_spike_producer_matches_linear_then_lif(cuda, T, B, din, dout, rate, scale):
+    """The fused spike-input producer (lifb_spike_linear_lif_fwd) against
+    nn.Linear then lif_tuned on the same 0/1 raster: S bit-equal (the fused I
+    sums in cuBLAS's order), the gradients of x, W and b within 1e-5."""
+    from hard_resets_compose_b200 import lifscan as Lm
+    from hard_resets_compose_b200.shdnet import spike_linear_lif
+    torch.manual_seed(3)
+    fc = nn.Linear(din, dout).to(cuda)
+    with torch.no_grad():
+        fc.weight.mul_(scale)
+    x = (torch.rand(T, B, din, device=cuda) < rate).float().requires_grad_(True)
+    g = torch.randn(T, B, dout, device=cuda)
+    S = spike_linear_lif(x, fc.weight, fc.bias, 0.9)
+    gx, gw, gb = torch.autograd.grad(S, (x, fc.weight, fc.bias), g)
+    x2 = x.detach().clone().requires_grad_(True)
+    I = fc(x2).reshape(T, -1)
+    S2 = Lm.lif_tuned(I, torch.zeros(I.shape[1], device=cuda), beta=0.9).reshape(T, B, dout)
+    gx2, gw2, gb2 = torch.autograd.grad(S2, (x2, fc.weight, fc.bias), g)
+    assert S.sum() > 0
+    assert torch.equal(S.view(torch.int32), S2.view(torch.int32))
+    for a, r in ((gx, gx2), (gw, gw2), (gb, gb2)):
+        assert rel(a.cpu().numpy(), r.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("readout,init,beta", (("mean", "reference", 0.95), ("leaky", "kaiming", 0.9)))
+def test_network_c3_spike_producer(cuda, readout, init, beta):
+    """Config 3's network with the fused producer in both LIF layers: spikes
+    bit-equal to the plain torch fp32 serial restatement, every parameter
+    gradient within 1e-5 relative (B = 64, T = 1024)."""
+    from hard_resets_compose_b200.shdnet import Net, synthetic_batch
+    torch.manual_seed(1)
+    net = Net(mode="scan", beta=beta, init=init, readout=readout, producer="spike").to(cuda)
+    x, y = synthetic_batch(1024, 64, seed=2, device=cuda)
+    with torch.no_grad():
+        net.l1.fc.weight.mul_(6.0)
+        net.l2.fc.weight.mul_(3.0)
+    logits, (s1, s2) = net(x)
+    loss = nn.functional.cross_entropy(logits, y)
+    grads = torch.autograd.grad(loss, list(net.parameters()))
+    rlogits, (r1, r2) = _reference_forward(net, x)
+    rloss = nn.functional.cross_entropy(rlogits, y)
+    rgrads = torch.autograd.grad(rloss, list(net.parameters()))
+    assert s1.sum() > 0 and s2.sum() > 0
+    assert torch.equal(s1, r1.detach()) and torch.equal(s2, r2.detach())
+    assert rel(logits.detach().cpu().numpy(), rlogits.detach().cpu().numpy()) < 1e-6
+    for g, rg in zip(grads, rgrads):
+        assert rel(g.cpu().numpy(), rg.cpu().numpy()) < 1e-5
