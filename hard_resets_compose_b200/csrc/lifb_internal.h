@@ -63,6 +63,10 @@ inline Reset affine_reset(float gamma, float delta)
 bool make_tmap_2d(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_x, int box_y);
 // 2-D map of a [T, N] array of 4-byte elements (fp32, or int32 when int32 is true).
 bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N, int64_t T, int box_x, int box_y);
+// 3-D map of a [d2, d1, d0] array of 32-bit words (d0 innermost), box
+// (b0, b1, b2); false unless d0 * 4 is a multiple of 16 and base is 16-byte
+// aligned.
+bool make_tmap_3d_u32(CUtensorMap *m, const void *base, int64_t d0, int64_t d1, int64_t d2, int b0, int b1, int b2);
 int *device_status_ptr();                 // status word of the current device
 int read_device_status(bool reset);       // synchronous read (current device)
 // Non-blocking: the word as of the last completed asynchronous read of the

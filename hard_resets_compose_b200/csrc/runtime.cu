@@ -66,6 +66,23 @@ bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N,
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_3d_u32(CUtensorMap *m, const void *base, int64_t d0, int64_t d1, int64_t d2, int b0, int b1, int b2)
+{
+    bind_primary_context();
+    auto enc = encoder();
+    if (!enc || ((uintptr_t)base & 15) || (d0 * 4) % 16 || d0 >= (int64_t(1) << 31) || d1 >= (int64_t(1) << 31) ||
+        d2 >= (int64_t(1) << 31) || b0 > 256 || b1 > 256 || b2 > 256)
+        return false;
+    cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+    cuuint64_t strides[2] = {(cuuint64_t)d0 * 4, (cuuint64_t)(d0 * d1) * 4};
+    cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, (cuuint32_t)b2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, (void *)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 int *device_status_ptr()
 {
     int dev = 0;

@@ -1,172 +1,648 @@
-// Fused spike-input Linear -> hard-reset LIF forward (the producer of I for a
-// layer of a spiking network such as the 700-256-256-20 net of
-// lifscan/shdnet.py:30-66).
+// Spike-input Linear layers of a spiking network (the 700-256-256-20 net of
+// lifscan/shdnet.py:30-66): the bitmask spike format, the fused
+// Linear -> hard-reset LIF forward, and the sparse weight gradient.
 //
-// A layer computes I[t, b, :] = X[t, b, :] W^T + bias and then the LIF
-// recurrence over t for every (b, j).  In a spiking network X is itself a
-// spike raster (0/1, a few percent active), so each I row is a sparse sum of
-// weight columns.  cuBLAS's fp32 GEMM on such an input sums the active terms
-// in input order and adds the bias last (measured bit for bit on B200 for
-// both layer shapes of the network); this kernel forms each I element the
-// same way, acc = fma(x_c, W[j, c], acc) over the nonzero x_c in increasing c
-// from acc = 0, then fl(acc + bias[j]), so I, and with it every spike of the
-// layer, equals the unfused Linear -> lif_tuned bit for bit.  I never goes to
-// memory: it is formed in shared memory tile by tile and consumed there by
-// the recurrence, which writes V (the pre-reset potential the V-path adjoint
-// reads) and S.
+// Spike mask.  A [R, D] fp32 tensor whose rows are mostly zeros (a spike
+// raster, R = T*B rows (t, b)) is described by mask words [R, NWp], NWp =
+// round_up(ceil(D/32) + 1, 4): word k of a row holds bit q set when element
+// 32k + q is nonzero (NaN counts as nonzero, -0 as zero), word ceil(D/32)
+// has bit 0 set when some nonzero element of the row is not exactly 1.0 (an
+// "odd" row: its consumers read the values from the dense tensor), the rest
+// is padding so that a row is a whole number of 16-byte TMA units.  88-96
+// bytes describe a 700-input row of 2800 bytes.  k_spike_mask writes it from
+// the dense tensor; the fused forward writes the mask of its own spikes for
+// the next layer, so only the network input is ever scanned.
 //
-// CTA = one batch element b x 32 outputs j (one per lane), the weight slice
-// W[j0:j0+32, :] transposed into shared memory ([Din][32], read conflict-free).
-// For each tile of R = 64 rows, the CTA's 8 warps form I for 8 rows each
-// (row (t, b) of X read with coalesced loads, a ballot per 32 columns, the
-// active columns taken in order), then warp 0 steps the recurrence over the
-// tile (state in registers across tiles) and writes the 128-byte V and S rows.
-// The tile's I buffer is double-buffered so warps 1-7 form the next tile while
-// warp 0 steps this one.
+// Fused forward (k_spike_linear_lif).  I[t, b, j] = X[t, b, :] W[j, :]^T +
+// bias[j], then the LIF recurrence over t for every (b, j), writing V (the
+// pre-reset potentials the V-path adjoint reads), S and the mask of S.
+// cuBLAS's fp32 GEMM on such an input sums x_c * W[j, c] with fused
+// multiply-adds in input order from 0 and adds the bias last (measured bit
+// for bit on B200 for both layer shapes of the network); terms with x_c = 0
+// leave the sum unchanged, so summing only the active inputs in increasing c
+// gives the same bits, and so do the spikes.  One CTA owns 32*JW outputs j
+// (JW per lane) and `bpc` batch elements: the weight slice sits transposed in
+// shared memory ([Din][32] JW-vectors, a conflict-free broadcast read per
+// active input), the mask rows of each 16-step tile arrive by one 3-D TMA
+// load (double-buffered, bounded mbarrier waits), former warps expand each
+// row's mask into a list of active inputs (a warp prefix sum of the words'
+// popcounts) and sum the listed weight vectors in order, and one warp per
+// batch element steps the recurrence over the previous tile from shared
+// memory.  I never reaches global memory.  Weights that are not finite make
+// the GEMM's zero terms NaN (0 * inf): the lanes of such outputs take the
+// dense sum over every input instead, so the bits still match.
+//
+// Weight gradient (k_spike_wgrad).  gW[j, c] = sum_r dI[r, j] X[r, c] and
+// gb[j] = sum_r dI[r, j] touch only the active (r, c): per 32-row block a
+// CTA stages the dI tile of its outputs and the block's mask rows by TMA;
+// each warp owns 16 input columns and 32*JJ outputs (JJ per lane, an
+// accumulator per column and output in registers), turns the block's mask
+// bits into per-column row sets with ballots and adds the listed dI rows in
+// row order.  Each CTA covers a fixed 2048-row chunk; a second pass adds the
+// chunks in order, so the result is deterministic and independent of the GPU.
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
+#include "tma.cuh"
+
+#include <algorithm>
+#include <string>
 
 namespace lifb {
 
 namespace {
-constexpr int kSLWarps = 8;
-constexpr int kSLRows = 64;                  // rows per tile
-constexpr int kSLRowsPerWarp = kSLRows / kSLWarps;
-constexpr int kSLMaxChunks = 32;             // Din <= 1024
-
-size_t spike_linear_smem(int64_t Din) { return (size_t)Din * 32 * 4 + 2 * (size_t)kSLRows * 32 * 4; }
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kMaskWarps = 8;    // rows (one per warp) in flight per mask CTA
+constexpr int kSLTile = 16;      // time steps per producer tile
+constexpr int kSLWarps = 16;     // producer CTA: bpc recurrence warps, the rest form rows
+constexpr int kWgWarps = 8;      // weight-gradient CTA: 8 warps x 16 columns
+constexpr int kWgCols = 16;
+constexpr int kWgChunk = 2048;   // rows per weight-gradient CTA (fixes the summation order)
+constexpr int kMaxMaskStride = 36;
 }  // namespace
 
+int64_t spike_mask_stride(int64_t D) { return ((D + 31) / 32 + 1 + 3) / 4 * 4; }
+
 template <int NCH>
-__global__ void __launch_bounds__(32 * kSLWarps) k_spike_linear_lif(
-    const float *__restrict__ X, const float *__restrict__ W, const float *__restrict__ bias,
-    const float *__restrict__ u0, float *__restrict__ V, float *__restrict__ S, int64_t T, int64_t B, int Din,
-    int Dout, float beta, float theta, float u_r)
+__global__ void __launch_bounds__(32 * kMaskWarps) k_spike_mask(const float *__restrict__ X, uint32_t *__restrict__ M,
+                                                               int64_t R, int D, int NWp)
 {
-    extern __shared__ __align__(16) float sl_smem[];
-    float *Ws = sl_smem;                          // [Din][32]
-    float *Itile = sl_smem + (size_t)Din * 32;    // [2][kSLRows][32]
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int jg = blockIdx.x % (Dout / 32);
-    const int64_t b = blockIdx.x / (Dout / 32);
-    const int j = jg * 32 + lane;
-    const unsigned full = 0xffffffffu;
-
-    // the weight slice, transposed: Ws[c][l] = W[jg*32 + l, c]
-    for (int64_t e = threadIdx.x; e < (int64_t)Din * 32; e += blockDim.x) {
-        const int l = (int)(e / Din), c = (int)(e % Din);
-        Ws[c * 32 + l] = W[(int64_t)(jg * 32 + l) * Din + c];
-    }
-    const float bj = bias ? bias[j] : 0.0f;
-    const int64_t N = B * Dout;
-    const int64_t n = b * Dout + j;
-    float u = u0 ? u0[n] : 0.0f;
-    __syncthreads();
-
-    // I of row t for this lane's output: the active columns in input order
-    auto form_row = [&](int64_t t) -> float {
-        const float *xr = X + (t * B + b) * Din;
+    const int lane = threadIdx.x & 31;
+    const int NW = (D + 31) >> 5;
+    const int64_t nwarps = (int64_t)gridDim.x * kMaskWarps;
+    for (int64_t row = (int64_t)blockIdx.x * kMaskWarps + (threadIdx.x >> 5); row < R; row += nwarps) {
+        const float *xr = X + row * D;
         float xv[NCH];
 #pragma unroll
         for (int k = 0; k < NCH; k++) {
             const int c = k * 32 + lane;
-            xv[k] = c < Din ? __ldg(xr + c) : 0.0f;
+            xv[k] = c < D ? __ldcs(xr + c) : 0.0f;
         }
-        float acc = 0.0f;
+        uint32_t mine = 0;
+        bool odd = false;
 #pragma unroll
         for (int k = 0; k < NCH; k++) {
-            unsigned m = __ballot_sync(full, xv[k] != 0.0f);
-            while (m) {
-                const int q = __ffs(m) - 1;
-                m &= m - 1;
-                const float xc = __shfl_sync(full, xv[k], q);
-                acc = fmaf(xc, Ws[(k * 32 + q) * 32 + lane], acc);
-            }
+            const uint32_t b = __ballot_sync(kFull, xv[k] != 0.0f);
+            mine = lane == k ? b : mine;
+            odd |= xv[k] != 0.0f && xv[k] != 1.0f;
         }
-        return __fadd_rn(acc, bj);
-    };
-
-    const int64_t ntiles = (T + kSLRows - 1) / kSLRows;
-    // tile 0 by every warp
-    for (int r = w * kSLRowsPerWarp; r < (w + 1) * kSLRowsPerWarp; r++)
-        if (r < T) Itile[r * 32 + lane] = form_row(r);
-    __syncthreads();
-    for (int64_t k = 0; k < ntiles; k++) {
-        const float *cur = Itile + (k & 1) * kSLRows * 32;
-        float *nxt = Itile + ((k + 1) & 1) * kSLRows * 32;
-        const int64_t t0 = k * kSLRows;
-        if (w == 0) {
-            // the recurrence over this tile
-            const int rows = (int)(T - t0 < kSLRows ? T - t0 : kSLRows);
-            for (int r = 0; r < rows; r++) {
-                const float v = __fadd_rn(__fmul_rn(beta, u), cur[r * 32 + lane]);
-                const bool f = v >= theta;
-                u = f ? u_r : v;
-                const int64_t o = (t0 + r) * N + n;
-                V[o] = v;
-                S[o] = f ? 1.0f : 0.0f;
-            }
-        } else if (k + 1 < ntiles) {
-            // warps 1..7 form the next tile meanwhile (its 64 rows over 7 warps)
-            const int64_t t1 = t0 + kSLRows;
-            for (int r = w - 1; r < kSLRows; r += kSLWarps - 1)
-                if (t1 + r < T) nxt[r * 32 + lane] = form_row(t1 + r);
-        }
-        __syncthreads();
+        const bool any_odd = __any_sync(kFull, odd);
+        uint32_t *mr = M + row * NWp;
+        for (int i = lane; i < NWp; i += 32) mr[i] = i < NW ? mine : (i == NW && any_odd ? 1u : 0u);
     }
 }
 
-bool spike_linear_lif_fwd(const float *X, const float *W, const float *bias, const float *u0, float *V, float *S,
-                          int64_t T, int64_t B, int64_t Din, int64_t Dout, float beta, float theta, float u_r,
-                          cudaStream_t s)
+bool spike_mask(const float *X, uint32_t *M, int64_t R, int64_t D, cudaStream_t s)
 {
-    if (Din <= 0 || Din > 32 * kSLMaxChunks || Dout <= 0 || Dout % 32) return false;
-    const size_t smem = spike_linear_smem(Din);
-    int dev = 0, lim = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        smem > (size_t)lim)
+    if (D <= 0 || D > 1024 || ((uintptr_t)M & 15)) return false;
+    int dev = 0, nsm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev))
         return false;
-    const int64_t grid = B * (Dout / 32);
-    if (grid <= 0 || grid > INT32_MAX) return false;
-    const int nch = (int)((Din + 31) / 32);
-    auto go = [&](auto kern) {
+    const int NWp = (int)spike_mask_stride(D);
+    const int64_t want = (R + kMaskWarps - 1) / kMaskWarps;
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)nsm * 8));
+    const int nch = (int)((D + 31) / 32);
+    count_launches(1);
+    if (nch <= 8) k_spike_mask<8><<<grid, 32 * kMaskWarps, 0, s>>>(X, M, R, (int)D, NWp);
+    else if (nch <= 16) k_spike_mask<16><<<grid, 32 * kMaskWarps, 0, s>>>(X, M, R, (int)D, NWp);
+    else if (nch <= 24) k_spike_mask<24><<<grid, 32 * kMaskWarps, 0, s>>>(X, M, R, (int)D, NWp);
+    else k_spike_mask<32><<<grid, 32 * kMaskWarps, 0, s>>>(X, M, R, (int)D, NWp);
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// fused forward
+
+namespace {
+struct SLSmem {
+    size_t it, mk, lst, total;
+};
+__host__ __device__ inline SLSmem sl_layout(int Din, int JW, int bpc, int NWp)
+{
+    SLSmem L;
+    L.it = (size_t)Din * 32 * JW * 4;                                    // weight slice at 0
+    L.mk = (L.it + (size_t)2 * bpc * kSLTile * 32 * JW * 4 + 127) / 128 * 128;  // I tiles, then mask tiles
+    L.lst = L.mk + (size_t)2 * kSLTile * bpc * NWp * 4;
+    L.total = L.lst + (size_t)kSLWarps * 32 * 4;
+    return L;
+}
+}  // namespace
+
+template <int JW>
+__global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
+    const __grid_constant__ CUtensorMap tm, const float *__restrict__ X, const float *__restrict__ W,
+    const float *__restrict__ bias, const float *__restrict__ u0, float *__restrict__ V, float *__restrict__ S,
+    uint32_t *__restrict__ Sm, int64_t T, int64_t B, int Din, int Dout, int bpc, int NWp, int NWop, float beta,
+    float theta, float u_r, int *status)
+{
+    constexpr int OG = 32 * JW;
+    extern __shared__ __align__(128) unsigned char sl_raw[];
+    const SLSmem L = sl_layout(Din, JW, bpc, NWp);
+    float *Ws = reinterpret_cast<float *>(sl_raw);
+    float *It = reinterpret_cast<float *>(sl_raw + L.it);
+    uint32_t *Mk = reinterpret_cast<uint32_t *>(sl_raw + L.mk);
+    __shared__ uint64_t bar[2];
+    __shared__ int s_bad[OG];
+    __shared__ int s_err;
+
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ngroups = Dout / OG;
+    const int jg = (int)(blockIdx.x % ngroups);
+    const int64_t b0 = (int64_t)(blockIdx.x / ngroups) * bpc;
+    const int nb = (int)(B - b0 < bpc ? B - b0 : bpc);
+    const int j0 = jg * OG;
+    const int NW = (Din + 31) >> 5;
+    const int NWo = Dout >> 5;
+    const int64_t ntiles = (T + kSLTile - 1) / kSLTile;
+    const size_t mtile = (size_t)kSLTile * bpc * NWp;  // words per mask tile
+    const uint32_t tile_bytes = (uint32_t)(mtile * 4);
+    int *lst = reinterpret_cast<int *>(sl_raw + L.lst) + w * 32;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_barrier_init();
+        s_err = 0;
+    }
+    for (int i = threadIdx.x; i < OG; i += blockDim.x) s_bad[i] = 0;
+    __syncthreads();
+    int64_t last[2] = {-1, -1};  // (thread 0) the last tile issued into each buffer
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < 2 && k < ntiles; k++) {
+            mbar_arrive_expect_tx(&bar[k], tile_bytes);
+            tma_load_3d(Mk + k * mtile, &tm, 0, (int)b0, k * kSLTile, &bar[k]);
+            last[k] = k;
+        }
+    }
+    // the weight slice, transposed: Ws[(c * 32 + l) * JW + e] = W[j0 + e * 32 + l, c]
+    for (int64_t e = threadIdx.x; e < (int64_t)Din * OG; e += blockDim.x) {
+        const int o = (int)(e % OG), c = (int)(e / OG);
+        const float wv = __ldg(W + (int64_t)(j0 + o) * Din + c);
+        Ws[((size_t)c * 32 + (o & 31)) * JW + (o >> 5)] = wv;
+        if (!isfinite(wv)) s_bad[o] = 1;
+    }
+    __syncthreads();
+    float bj[JW];
+    bool bad[JW];
+    bool any_bad = false;
+#pragma unroll
+    for (int e = 0; e < JW; e++) {
+        bj[e] = bias ? __ldg(bias + j0 + e * 32 + lane) : 0.0f;
+        bad[e] = s_bad[e * 32 + lane] != 0;
+        any_bad |= bad[e];
+    }
+    const bool warp_bad = __any_sync(kFull, any_bad);
+
+    // I of one row for this lane's outputs: the active inputs, in order
+    auto form = [&](const uint32_t *mr, int64_t row, float *dst) {
+        uint32_t m = lane < NW ? mr[lane] : 0u;
+        if (lane == NW - 1 && (Din & 31)) m &= (1u << (Din & 31)) - 1u;  // bits past Din are not inputs
+        const bool odd = (mr[NW] & 1u) != 0;
+        const float *xr = X + row * Din;
+        float a[JW];
+#pragma unroll
+        for (int e = 0; e < JW; e++) a[e] = 0.0f;
+        const int cnt = __popc(m);
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const int total = __shfl_sync(kFull, incl, 31);
+        uint32_t mm = m;
+        int p = incl - cnt;  // list position of this lane's next active input
+        for (int base = 0; base < total; base += 32) {
+            while (mm && p < base + 32) {
+                const int q = __ffs(mm) - 1;
+                mm &= mm - 1;
+                lst[p - base] = lane * 32 + q;
+                p++;
+            }
+            __syncwarp();
+            const int n = total - base < 32 ? total - base : 32;
+            const int myc = lane < n ? lst[lane] : 0;
+            __syncwarp();
+            int i = 0;
+            if (!odd) {
+                for (; i + 4 <= n; i += 4) {
+                    const int c0 = __shfl_sync(kFull, myc, i), c1 = __shfl_sync(kFull, myc, i + 1);
+                    const int c2 = __shfl_sync(kFull, myc, i + 2), c3 = __shfl_sync(kFull, myc, i + 3);
+                    if constexpr (JW == 2) {
+                        const float2 w0 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c0 * 32 + lane) * 2);
+                        const float2 w1 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c1 * 32 + lane) * 2);
+                        const float2 w2 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c2 * 32 + lane) * 2);
+                        const float2 w3 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c3 * 32 + lane) * 2);
+                        a[0] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[0], w0.x), w1.x), w2.x), w3.x);
+                        a[JW - 1] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[JW - 1], w0.y), w1.y), w2.y), w3.y);
+                    } else {
+                        const float w0 = Ws[(size_t)c0 * 32 + lane], w1 = Ws[(size_t)c1 * 32 + lane];
+                        const float w2 = Ws[(size_t)c2 * 32 + lane], w3 = Ws[(size_t)c3 * 32 + lane];
+                        a[0] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[0], w0), w1), w2), w3);
+                    }
+                }
+                for (; i < n; i++) {
+                    const int c = __shfl_sync(kFull, myc, i);
+#pragma unroll
+                    for (int e = 0; e < JW; e++) a[e] = __fadd_rn(a[e], Ws[((size_t)c * 32 + lane) * JW + e]);
+                }
+            } else {
+                const float myx = lane < n ? __ldg(xr + myc) : 0.0f;
+                for (; i < n; i++) {
+                    const int c = __shfl_sync(kFull, myc, i);
+                    const float x = __shfl_sync(kFull, myx, i);
+#pragma unroll
+                    for (int e = 0; e < JW; e++) a[e] = fmaf(x, Ws[((size_t)c * 32 + lane) * JW + e], a[e]);
+                }
+            }
+        }
+        if (warp_bad) {  // non-finite weights: every term, zeros included
+            float d[JW];
+#pragma unroll
+            for (int e = 0; e < JW; e++) d[e] = 0.0f;
+            for (int c = 0; c < Din; c++) {
+                const float x = __ldg(xr + c);
+#pragma unroll
+                for (int e = 0; e < JW; e++) d[e] = fmaf(x, Ws[((size_t)c * 32 + lane) * JW + e], d[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < JW; e++) a[e] = bad[e] ? d[e] : a[e];
+        }
+#pragma unroll
+        for (int e = 0; e < JW; e++) dst[e * 32 + lane] = __fadd_rn(a[e], bj[e]);
+    };
+
+    float u[JW];
+#pragma unroll
+    for (int e = 0; e < JW; e++) u[e] = (w < nb && u0) ? u0[(b0 + w) * Dout + j0 + e * 32 + lane] : 0.0f;
+    const int slots = nb * kSLTile;
+    const int nform = kSLWarps - bpc;
+    for (int64_t k = 0; k <= ntiles; k++) {
+        if (w < nb && k >= 1) {  // the recurrence over tile k - 1
+            const int64_t t0 = (k - 1) * kSLTile;
+            const float *cur = It + ((size_t)((k - 1) & 1) * bpc + w) * kSLTile * OG;
+            const int rows = (int)(T - t0 < kSLTile ? T - t0 : kSLTile);
+            for (int r = 0; r < rows; r++) {
+                const int64_t row = (t0 + r) * B + b0 + w;
+                float *vo = V + row * Dout + j0;
+                float *so = S + row * Dout + j0;
+                uint32_t mw[JW];
+#pragma unroll
+                for (int e = 0; e < JW; e++) {
+                    const float v = __fadd_rn(__fmul_rn(beta, u[e]), cur[r * OG + e * 32 + lane]);
+                    const bool f = v >= theta;
+                    u[e] = f ? u_r : v;
+                    vo[e * 32 + lane] = v;
+                    so[e * 32 + lane] = f ? 1.0f : 0.0f;
+                    mw[e] = __ballot_sync(kFull, f);
+                }
+                if (Sm) {
+                    uint32_t *mo = Sm + row * NWop;
+                    if (lane < JW) mo[jg * JW + lane] = lane == 0 ? mw[0] : mw[JW - 1];
+                    if (jg == 0 && NWo + lane < NWop) mo[NWo + lane] = 0u;  // spikes are 0/1: not odd
+                }
+            }
+        }
+        if (w >= bpc && k < ntiles) {  // form tile k
+            const int buf = (int)(k & 1);
+            if (!s_err && !mbar_wait(&bar[buf], (uint32_t)((k >> 1) & 1)) && lane == 0) atomicExch(&s_err, 1);
+            const uint32_t *mt = Mk + buf * mtile;
+            float *nxt = It + (size_t)buf * bpc * kSLTile * OG;
+            const int64_t t0 = k * kSLTile;
+            for (int f = w - bpc; f < slots; f += nform) {
+                const int bi = f / kSLTile, r = f % kSLTile;
+                if (t0 + r < T)
+                    form(mt + ((size_t)r * bpc + bi) * NWp, (t0 + r) * B + b0 + bi,
+                         nxt + ((size_t)bi * kSLTile + r) * OG);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && k + 2 < ntiles && !s_err) {  // buffer k & 1 is free again
+            mbar_arrive_expect_tx(&bar[k & 1], tile_bytes);
+            tma_load_3d(Mk + (k & 1) * mtile, &tm, 0, (int)b0, (int)((k + 2) * kSLTile), &bar[k & 1]);
+            last[k & 1] = k + 2;
+        }
+    }
+    if (threadIdx.x == 0 && s_err) {
+        // let copies still in flight land before the CTA's shared memory goes away
+        for (int i = 0; i < 2; i++)
+            if (last[i] >= 0) mbar_wait(&bar[i], (uint32_t)((last[i] >> 1) & 1));
+        if (status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
+    }
+}
+
+bool spike_linear_lif_fwd(const float *X, const uint32_t *Xm, const float *W, const float *bias, const float *u0,
+                          float *V, float *S, uint32_t *Sm, int64_t T, int64_t B, int64_t Din, int64_t Dout,
+                          float beta, float theta, float u_r, cudaStream_t s)
+{
+    if (Din <= 0 || Din > 1024 || Dout <= 0 || Dout % 32 || T >= INT32_MAX || B >= INT32_MAX) return false;
+    if (((uintptr_t)Xm & 15) || (Sm && ((uintptr_t)Sm & 15))) return false;
+    const int NWp = (int)spike_mask_stride(Din), NWop = (int)spike_mask_stride(Dout);
+    int dev = 0, nsm = 0, lim = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) ||
+        cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))
+        return false;
+    const int JW = (Dout % 64 == 0 && sl_layout((int)Din, 2, 1, NWp).total <= (size_t)lim) ? 2 : 1;
+    if (sl_layout((int)Din, JW, 1, NWp).total > (size_t)lim) return false;
+    const int64_t groups = Dout / (32 * JW);
+    auto go = [&](auto kern) -> bool {
+        // batch elements per CTA: the fewest that put every CTA on the GPU at once
+        int bpc = 1;
+        for (int cand = 1; cand <= 4; cand++) {
+            const size_t sm = sl_layout((int)Din, JW, cand, NWp).total;
+            if (sm > (size_t)lim) break;
+            int occ = 0;
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 32 * kSLWarps, sm) != cudaSuccess || occ < 1)
+                break;
+            bpc = cand;
+            if (groups * ((B + cand - 1) / cand) <= (int64_t)nsm * occ) break;
+        }
+        const size_t smem = sl_layout((int)Din, JW, bpc, NWp).total;
+        CUtensorMap tm;
+        if (!make_tmap_3d_u32(&tm, Xm, NWp, B, T, NWp, bpc, kSLTile)) return false;
+        const int64_t grid = groups * ((B + bpc - 1) / bpc);
+        if (grid > INT32_MAX) return false;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         count_launches(1);
-        kern<<<(unsigned)grid, 32 * kSLWarps, smem, s>>>(X, W, bias, u0, V, S, T, B, (int)Din, (int)Dout, beta, theta,
-                                                         u_r);
+        kern<<<(unsigned)grid, 32 * kSLWarps, smem, s>>>(tm, X, W, bias, u0, V, S, Sm, T, B, (int)Din, (int)Dout,
+                                                          bpc, NWp, NWop, beta, theta, u_r, device_status_ptr());
+        return true;
     };
-    if (nch <= 8) go(k_spike_linear_lif<8>);
-    else if (nch <= 24) go(k_spike_linear_lif<24>);
-    else go(k_spike_linear_lif<32>);
+    return JW == 2 ? go(k_spike_linear_lif<2>) : go(k_spike_linear_lif<1>);
+}
+
+// ---------------------------------------------------------------------------
+// weight gradient
+
+template <int JJ>
+__global__ void __launch_bounds__(32 * kWgWarps) k_spike_wgrad(const __grid_constant__ CUtensorMap tdi,
+                                                              const __grid_constant__ CUtensorMap tmk,
+                                                              const float *__restrict__ X, float *__restrict__ Pw,
+                                                              float *__restrict__ Pb, int64_t R, int Din, int Dout,
+                                                              int NWp, int Dp, int *status)
+{
+    constexpr int JS = 32 * JJ;
+    __shared__ __align__(128) float s_d[2][32 * JS];
+    __shared__ __align__(128) uint32_t s_m[2][32 * kMaxMaskStride];
+    __shared__ uint64_t bar[2];
+    __shared__ int s_err;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int js = blockIdx.y;
+    const int64_t ck = blockIdx.z;
+    const int c0 = (blockIdx.x * kWgWarps + w) * kWgCols;
+    const int64_t r0 = ck * kWgChunk;
+    const int64_t rend = R < r0 + kWgChunk ? R : r0 + kWgChunk;
+    const int nblk = (int)((rend - r0 + 31) / 32);
+    const uint32_t bytes = (uint32_t)(32 * JS * 4 + 32 * NWp * 4);
+    const int NW = (Din + 31) >> 5;
+    const bool has_cols = c0 < Din;
+    const bool do_bias = Pb && blockIdx.x == 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_barrier_init();
+        s_err = 0;
+    }
+    __syncthreads();
+    int last[2] = {-1, -1};  // (thread 0) the last block issued into each buffer
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2 && b < nblk; b++) {
+            mbar_arrive_expect_tx(&bar[b], bytes);
+            tma_load_2d(s_d[b], &tdi, js * JS, (int)(r0 + 32 * b), &bar[b]);
+            tma_load_2d(s_m[b], &tmk, 0, (int)(r0 + 32 * b), &bar[b]);
+            last[b] = b;
+        }
+    }
+    float acc[kWgCols][JJ];
+    float accb[JJ];
+#pragma unroll
+    for (int q = 0; q < kWgCols; q++)
+#pragma unroll
+        for (int e = 0; e < JJ; e++) acc[q][e] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < JJ; e++) accb[e] = 0.0f;
+
+    for (int b = 0; b < nblk; b++) {
+        const int buf = b & 1;
+        if (!s_err && !mbar_wait(&bar[buf], (uint32_t)((b >> 1) & 1)) && lane == 0) atomicExch(&s_err, 1);
+        const float *dt = s_d[buf] + JJ * lane;
+        const uint32_t *mt = s_m[buf];
+        if (has_cols) {
+            uint32_t wd = (mt[lane * NWp + (c0 >> 5)] >> (c0 & 31)) & 0xffffu;
+            if (Din - c0 < kWgCols) wd &= (1u << (Din - c0)) - 1u;  // bits past Din are not inputs
+            const bool od = (mt[lane * NWp + NW] & 1u) != 0;
+            const uint32_t odd_rows = __ballot_sync(kFull, od && wd != 0);
+            const int64_t rb = r0 + 32 * b;
+#pragma unroll
+            for (int q = 0; q < kWgCols; q++) {
+                uint32_t cw = __ballot_sync(kFull, (wd >> q) & 1u);
+                if (!cw) continue;
+                if (!(cw & odd_rows)) {
+                    while (cw) {
+                        const int r = __ffs(cw) - 1;
+                        cw &= cw - 1;
+                        if constexpr (JJ == 4) {
+                            const float4 d = *reinterpret_cast<const float4 *>(dt + r * JS);
+                            acc[q][0] = __fadd_rn(acc[q][0], d.x);
+                            acc[q][1] = __fadd_rn(acc[q][1], d.y);
+                            acc[q][2] = __fadd_rn(acc[q][2], d.z);
+                            acc[q][3] = __fadd_rn(acc[q][3], d.w);
+                        } else if constexpr (JJ == 2) {
+                            const float2 d = *reinterpret_cast<const float2 *>(dt + r * JS);
+                            acc[q][0] = __fadd_rn(acc[q][0], d.x);
+                            acc[q][1] = __fadd_rn(acc[q][1], d.y);
+                        } else {
+                            acc[q][0] = __fadd_rn(acc[q][0], dt[r * JS]);
+                        }
+                    }
+                } else {
+                    while (cw) {
+                        const int r = __ffs(cw) - 1;
+                        cw &= cw - 1;
+                        const float x = ((odd_rows >> r) & 1u) ? __ldg(X + (rb + r) * Din + c0 + q) : 1.0f;
+#pragma unroll
+                        for (int e = 0; e < JJ; e++) acc[q][e] = fmaf(x, dt[r * JS + e], acc[q][e]);
+                    }
+                }
+            }
+        }
+        if (do_bias) {  // this warp's four rows of the block
+#pragma unroll
+            for (int r = 4 * w; r < 4 * w + 4; r++)
+#pragma unroll
+                for (int e = 0; e < JJ; e++) accb[e] = __fadd_rn(accb[e], dt[r * JS + e]);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && b + 2 < nblk && !s_err) {
+            mbar_arrive_expect_tx(&bar[buf], bytes);
+            tma_load_2d(s_d[buf], &tdi, js * JS, (int)(r0 + 32 * (b + 2)), &bar[buf]);
+            tma_load_2d(s_m[buf], &tmk, 0, (int)(r0 + 32 * (b + 2)), &bar[buf]);
+            last[buf] = b + 2;
+        }
+    }
+    if (threadIdx.x == 0 && s_err) {
+        for (int i = 0; i < 2; i++)
+            if (last[i] >= 0) mbar_wait(&bar[i], (uint32_t)((last[i] >> 1) & 1));
+        if (status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
+    }
+    const int jb = js * JS + JJ * lane;
+    if (has_cols) {
+#pragma unroll
+        for (int e = 0; e < JJ; e++) {
+            float4 *o = reinterpret_cast<float4 *>(Pw + ((size_t)ck * Dout + jb + e) * Dp + c0);
+#pragma unroll
+            for (int q = 0; q < kWgCols; q += 4)
+                o[q / 4] = make_float4(acc[q][e], acc[q + 1][e], acc[q + 2][e], acc[q + 3][e]);
+        }
+    }
+    if (do_bias) {
+#pragma unroll
+        for (int e = 0; e < JJ; e++) Pb[((size_t)ck * kWgWarps + w) * Dout + jb + e] = accb[e];
+    }
+}
+
+// The chunks' partial sums, added in chunk order (and, for the bias, warp order).
+__global__ void k_spike_wgrad_reduce(const float *__restrict__ Pw, const float *__restrict__ Pb,
+                                     float *__restrict__ gW, float *__restrict__ gb, int64_t nck, int Din, int Dout,
+                                     int Dp)
+{
+    const int64_t n = (int64_t)Dout * Din;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / Din, c = i % Din;
+        float acc = 0.0f;
+        for (int64_t k = 0; k < nck; k++) acc = __fadd_rn(acc, Pw[(k * Dout + j) * Dp + c]);
+        gW[i] = acc;
+    }
+    if (gb) {
+        for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < Dout; j += (int64_t)gridDim.x * blockDim.x) {
+            float acc = 0.0f;
+            for (int64_t k = 0; k < nck * kWgWarps; k++) acc = __fadd_rn(acc, Pb[k * Dout + j]);
+            gb[j] = acc;
+        }
+    }
+}
+
+namespace {
+int64_t wgrad_chunks(int64_t R) { return (R + kWgChunk - 1) / kWgChunk; }
+int64_t wgrad_dp(int64_t Din) { return (Din + kWgCols - 1) / kWgCols * kWgCols; }
+}  // namespace
+
+size_t spike_wgrad_workspace_bytes(int64_t R, int64_t Din, int64_t Dout)
+{
+    const int64_t nck = wgrad_chunks(R);
+    return (size_t)(nck * Dout * wgrad_dp(Din) + nck * kWgWarps * Dout) * 4;
+}
+
+bool spike_wgrad(const float *dI, const float *X, const uint32_t *Xm, float *gW, float *gb, int64_t R, int64_t Din,
+                 int64_t Dout, void *ws, size_t ws_bytes, cudaStream_t s)
+{
+    if (Din <= 0 || Din > 1024 || Dout <= 0 || Dout % 32 || R >= INT32_MAX) return false;
+    if (((uintptr_t)dI & 15) || ((uintptr_t)Xm & 15) || ((uintptr_t)ws & 15)) return false;
+    if (!ws || ws_bytes < spike_wgrad_workspace_bytes(R, Din, Dout)) return false;
+    const int NWp = (int)spike_mask_stride(Din);
+    const int64_t nck = wgrad_chunks(R), Dp = wgrad_dp(Din);
+    if (nck > 65535) return false;
+    float *Pw = static_cast<float *>(ws);
+    float *Pb = Pw + nck * Dout * Dp;
+    const int JJ = Dout % 128 == 0 ? 4 : Dout % 64 == 0 ? 2 : 1;
+    CUtensorMap tdi, tmk;
+    if (!make_tmap_2d(&tdi, dI, Dout, R, 32 * JJ, 32) || !make_tmap_2d_typed(&tmk, Xm, true, NWp, R, NWp, 32))
+        return false;
+    const dim3 grid((unsigned)((Dp / kWgCols + kWgWarps - 1) / kWgWarps), (unsigned)(Dout / (32 * JJ)),
+                    (unsigned)nck);
+    float *pb = gb ? Pb : nullptr;
+    int *st = device_status_ptr();
+    count_launches(2);
+    if (JJ == 4) k_spike_wgrad<4><<<grid, 32 * kWgWarps, 0, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)Dp, st);
+    else if (JJ == 2) k_spike_wgrad<2><<<grid, 32 * kWgWarps, 0, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)Dp, st);
+    else k_spike_wgrad<1><<<grid, 32 * kWgWarps, 0, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)Dp, st);
+    int dev = 0, nsm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t n = Dout * Din;
+    const unsigned rgrid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)nsm * 8));
+    k_spike_wgrad_reduce<<<rgrid, 256, 0, s>>>(Pw, pb, gW, gb, nck, (int)Din, (int)Dout, (int)Dp);
     return true;
 }
 
 }  // namespace lifb
 
-extern "C" int lifb_spike_linear_lif_fwd(const float *X, const float *W, const float *bias, const float *u0, float *V,
-                                         float *S, int64_t T, int64_t B, int64_t Din, int64_t Dout, float beta,
-                                         float theta, float u_r, void *stream)
+namespace {
+int sl_fail(const char *msg, int code)
 {
-    LIFB_RANGE("lifb_spike_linear_lif_fwd");
-    if (T < 0 || B < 0 || Din <= 0 || Dout <= 0) {
-        lifb::set_last_error("lifb_spike_linear_lif_fwd: negative shape or empty Din/Dout");
-        return LIFB_ERR_INVALID_ARGUMENT;
-    }
-    if (T == 0 || B == 0) return LIFB_OK;
-    if (!X || !W || !V || !S) {
-        lifb::set_last_error("lifb_spike_linear_lif_fwd: null tensor pointer");
-        return LIFB_ERR_INVALID_ARGUMENT;
-    }
-    if (!lifb::spike_linear_lif_fwd(X, W, bias, u0, V, S, T, B, Din, Dout, beta, theta, u_r, (cudaStream_t)stream)) {
-        lifb::set_last_error("lifb_spike_linear_lif_fwd: needs Dout a multiple of 32 and Din <= 1024 (the weight "
-                             "slice in shared memory)");
-        return LIFB_ERR_UNSUPPORTED;
-    }
+    lifb::set_last_error(msg);
+    return code;
+}
+int sl_done(const char *what)
+{
     if (cudaGetLastError() != cudaSuccess) {
-        lifb::set_last_error("lifb_spike_linear_lif_fwd: launch failed");
+        lifb::set_last_error((std::string(what) + ": launch failed").c_str());
         return LIFB_ERR_CUDA;
     }
     lifb::set_last_error("");
     return LIFB_OK;
+}
+}  // namespace
+
+extern "C" int64_t lifb_spike_mask_stride(int64_t D) { return D > 0 ? lifb::spike_mask_stride(D) : 0; }
+
+extern "C" int lifb_spike_mask(const float *X, uint32_t *mask, int64_t R, int64_t D, void *stream)
+{
+    LIFB_RANGE("lifb_spike_mask");
+    if (R < 0 || D <= 0) return sl_fail("lifb_spike_mask: negative R or empty D", LIFB_ERR_INVALID_ARGUMENT);
+    if (R == 0) return LIFB_OK;
+    if (!X || !mask) return sl_fail("lifb_spike_mask: null tensor pointer", LIFB_ERR_INVALID_ARGUMENT);
+    if (!lifb::spike_mask(X, mask, R, D, (cudaStream_t)stream))
+        return sl_fail("lifb_spike_mask: needs D <= 1024 and a 16-byte aligned mask", LIFB_ERR_UNSUPPORTED);
+    return sl_done("lifb_spike_mask");
+}
+
+extern "C" int lifb_spike_linear_lif_fwd(const float *X, const uint32_t *Xmask, const float *W, const float *bias,
+                                         const float *u0, float *V, float *S, uint32_t *Smask, int64_t T, int64_t B,
+                                         int64_t Din, int64_t Dout, float beta, float theta, float u_r, void *stream)
+{
+    LIFB_RANGE("lifb_spike_linear_lif_fwd");
+    if (T < 0 || B < 0 || Din <= 0 || Dout <= 0)
+        return sl_fail("lifb_spike_linear_lif_fwd: negative shape or empty Din/Dout", LIFB_ERR_INVALID_ARGUMENT);
+    if (T == 0 || B == 0) return LIFB_OK;
+    if (!X || !Xmask || !W || !V || !S)
+        return sl_fail("lifb_spike_linear_lif_fwd: null tensor pointer", LIFB_ERR_INVALID_ARGUMENT);
+    if (!lifb::spike_linear_lif_fwd(X, Xmask, W, bias, u0, V, S, Smask, T, B, Din, Dout, beta, theta, u_r,
+                                    (cudaStream_t)stream))
+        return sl_fail("lifb_spike_linear_lif_fwd: needs Dout a multiple of 32, Din <= 1024 (the weight slice in "
+                       "shared memory) and 16-byte aligned masks",
+                       LIFB_ERR_UNSUPPORTED);
+    return sl_done("lifb_spike_linear_lif_fwd");
+}
+
+extern "C" size_t lifb_spike_linear_wgrad_workspace_bytes(int64_t R, int64_t Din, int64_t Dout)
+{
+    if (R <= 0 || Din <= 0 || Dout <= 0) return 0;
+    return lifb::spike_wgrad_workspace_bytes(R, Din, Dout);
+}
+
+extern "C" int lifb_spike_linear_wgrad(const float *dI, const float *X, const uint32_t *Xmask, float *gW, float *gb,
+                                       int64_t R, int64_t Din, int64_t Dout, void *workspace, size_t workspace_bytes,
+                                       void *stream)
+{
+    LIFB_RANGE("lifb_spike_linear_wgrad");
+    if (R < 0 || Din <= 0 || Dout <= 0)
+        return sl_fail("lifb_spike_linear_wgrad: negative R or empty Din/Dout", LIFB_ERR_INVALID_ARGUMENT);
+    if (!dI || !X || !Xmask || !gW)
+        return sl_fail("lifb_spike_linear_wgrad: null tensor pointer", LIFB_ERR_INVALID_ARGUMENT);
+    if (R == 0) {
+        if (cudaMemsetAsync(gW, 0, (size_t)(Din * Dout) * 4, (cudaStream_t)stream) != cudaSuccess ||
+            (gb && cudaMemsetAsync(gb, 0, (size_t)Dout * 4, (cudaStream_t)stream) != cudaSuccess))
+            return sl_fail("lifb_spike_linear_wgrad: memset failed", LIFB_ERR_CUDA);
+        return LIFB_OK;
+    }
+    if (!workspace || workspace_bytes < lifb::spike_wgrad_workspace_bytes(R, Din, Dout))
+        return sl_fail("lifb_spike_linear_wgrad: workspace missing or smaller than "
+                       "lifb_spike_linear_wgrad_workspace_bytes",
+                       LIFB_ERR_INVALID_ARGUMENT);
+    if (!lifb::spike_wgrad(dI, X, Xmask, gW, gb, R, Din, Dout, workspace, workspace_bytes, (cudaStream_t)stream))
+        return sl_fail("lifb_spike_linear_wgrad: needs Dout a multiple of 32, Din <= 1024 and 16-byte aligned dI, "
+                       "mask and workspace",
+                       LIFB_ERR_UNSUPPORTED);
+    return sl_done("lifb_spike_linear_wgrad");
 }

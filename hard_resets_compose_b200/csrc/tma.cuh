@@ -81,6 +81,18 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+// 3-D tiled TMA load of box (c0 innermost) into shared memory, completing on
+// `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                            uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(smem_dst)),
+        "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 2-D tiled TMA store of a shared-memory box to global memory (bulk-group
 // completion).  Out-of-range parts of the box are clipped by the hardware.
 // The writing threads must execute fence_proxy_async_shared() first.

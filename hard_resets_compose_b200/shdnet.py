@@ -12,11 +12,14 @@ same kernels: the serial forward with theta = +inf never spikes, and its
 adjoint with the upstream gradient on U is the integrator's backward.
 
 `producer="spike"` runs each LIF layer's Linear and recurrence as one fused
-kernel (lifb_spike_linear_lif_fwd) for spike inputs: I is never written to
-memory, each of its elements sums the active inputs' weights in the order
-cuBLAS's fp32 GEMM does, so the spikes are the same bits as with
-`producer="linear"` (nn.Linear, then lif_tuned); the backward is the same
-adjoint from V followed by the Linear's gradient GEMMs.
+kernel (lifb_spike_linear_lif_fwd) for spike inputs: the input is read as a
+bitmask of its active elements (lifb_spike_mask; a fused layer hands the mask
+of its own spikes to the next one), I is never written to memory, and each
+of its elements sums the active inputs' weights in the order cuBLAS's fp32
+GEMM does, so the spikes are the same bits as with `producer="linear"`
+(nn.Linear, then lif_tuned).  The backward is lif_tuned's adjoint from V,
+then the weight and bias gradients over the active inputs only
+(lifb_spike_linear_wgrad) and dI W for the input's gradient.
 
 The SHD data loader of the reference (h5py, :12-27) is not part of this
 package; inputs are dense [T, B, 700] spike rasters.
@@ -33,32 +36,63 @@ from . import lifscan as L
 from ._lib import check, ptr, stream_of
 
 
+_MASK_ATTR = "_lifb_spike_mask"
+
+
+def spike_mask(x2d):
+    """Spike mask [R, lifb_spike_mask_stride(D)] int32 of a [R, D] fp32 tensor
+    (lifb_spike_mask): bit q of word k set where element 32k + q is nonzero,
+    word ceil(D/32) bit 0 set on rows with a nonzero value other than 1."""
+    R, D = x2d.shape
+    lib = _lib.load()
+    m = torch.empty(R, lib.lifb_spike_mask_stride(D), dtype=torch.int32, device=x2d.device)
+    with torch.cuda.device(x2d.device):
+        check(lib.lifb_spike_mask(ptr(x2d), ptr(m), R, D, stream_of(x2d)), "spike_mask")
+    return m
+
+
+def _carried_mask(x):
+    """The mask a fused layer attached to its spike output x, if x is still
+    that tensor, unmodified; else None."""
+    rec = getattr(x, _MASK_ATTR, None)
+    if rec is None:
+        return None
+    m, version = rec
+    return m if version == x._version else None
+
+
 class SpikeLinearLIF(torch.autograd.Function):
     """Linear on a spike input then lif_tuned's hard-reset LIF (theta, u_r,
     sigmoid surrogate alpha, detached reset), forward fused in one kernel
-    (lifb_spike_linear_lif_fwd).  Returns S [T, B, Dout]; the backward is
-    lif_tuned's adjoint from V, then the Linear's gradients."""
+    (lifb_spike_linear_lif_fwd).  Returns S [T, B, Dout] and the spike mask
+    of S (not differentiable).  The backward is lif_tuned's adjoint from V,
+    then the weight and bias gradients over the input's active elements
+    (lifb_spike_linear_wgrad) and, when needed, dI W for the input."""
 
     @staticmethod
-    def forward(ctx, x, weight, bias, beta, theta, u_r, alpha, mode):
+    def forward(ctx, x, xmask, weight, bias, beta, theta, u_r, alpha, mode):
         x = x.contiguous()
         T, B, din = x.shape
         dout = weight.shape[0]
-        V = torch.empty(T, B * dout, device=x.device)
-        S = torch.empty(T, B * dout, device=x.device)
         lib = _lib.load()
+        if xmask is None:
+            xmask = spike_mask(x.view(T * B, din))
+        V = torch.empty(T, B * dout, device=x.device)
+        S = torch.empty(T, B, dout, device=x.device)
+        smask = torch.empty(T * B, lib.lifb_spike_mask_stride(dout), dtype=torch.int32, device=x.device)
         with torch.cuda.device(x.device):
-            check(lib.lifb_spike_linear_lif_fwd(ptr(x), ptr(weight.contiguous()), ptr(None if bias is None else
-                                                                                   bias.contiguous()),
-                                                None, ptr(V), ptr(S), T, B, din, dout, float(beta), float(theta),
+            check(lib.lifb_spike_linear_lif_fwd(ptr(x), ptr(xmask), ptr(weight.contiguous()),
+                                                ptr(None if bias is None else bias.contiguous()), None, ptr(V),
+                                                ptr(S), ptr(smask), T, B, din, dout, float(beta), float(theta),
                                                 float(u_r), stream_of(x)), "spike_linear_lif")
-        ctx.save_for_backward(x, weight, V)
+        ctx.save_for_backward(x, xmask, weight, V)
         ctx.cfg = (beta, theta, alpha, mode, bias is not None)
-        return S.view(T, B, dout)
+        ctx.mark_non_differentiable(smask)
+        return S, smask
 
     @staticmethod
-    def backward(ctx, gS):
-        x, weight, V = ctx.saved_tensors
+    def backward(ctx, gS, _gmask):
+        x, xmask, weight, V = ctx.saved_tensors
         beta, theta, alpha, mode, has_bias = ctx.cfg
         T, N = V.shape
         B, din, dout = x.shape[1], x.shape[2], weight.shape[0]
@@ -67,16 +101,30 @@ class SpikeLinearLIF(torch.autograd.Function):
                                C=T if mode == "serial" else L.scan_chunk_bwd(T, N))
         dI = lam.reshape(T * B, dout)
         gx = dI.mm(weight).reshape(T, B, din) if ctx.needs_input_grad[0] else None
-        gw = dI.t().mm(x.reshape(T * B, din)) if ctx.needs_input_grad[1] else None
-        gb = dI.sum(0) if has_bias and ctx.needs_input_grad[2] else None
+        gw = gb = None
+        want_b = has_bias and ctx.needs_input_grad[3]
+        if ctx.needs_input_grad[2] or want_b:
+            lib = _lib.load()
+            gw = torch.empty(dout, din, device=x.device)
+            gb = torch.empty(dout, device=x.device) if want_b else None
+            ws = torch.empty(max(lib.lifb_spike_linear_wgrad_workspace_bytes(T * B, din, dout), 1),
+                             dtype=torch.uint8, device=x.device)
+            with torch.cuda.device(x.device):
+                check(lib.lifb_spike_linear_wgrad(ptr(dI), ptr(x), ptr(xmask), ptr(gw), ptr(gb), T * B, din, dout,
+                                                  ptr(ws), ws.numel(), stream_of(x)), "spike_linear_wgrad")
+            if not ctx.needs_input_grad[2]:
+                gw = None
         _lib.poll_device("spike_linear_lif")
-        return gx, gw, gb, None, None, None, None, None
+        return gx, None, gw, gb, None, None, None, None, None
 
 
 def spike_linear_lif(x, weight, bias, beta, theta=1.0, u_r=0.0, alpha=4.0, mode="scan"):
     """S = lif_tuned(linear(x, weight, bias).reshape(T, -1), 0, ...) for a
-    spike input x [T, B, Din], forward fused (SpikeLinearLIF)."""
-    return SpikeLinearLIF.apply(x, weight, bias, beta, theta, u_r, alpha, mode)
+    spike input x [T, B, Din], forward fused (SpikeLinearLIF).  S carries
+    its spike mask to a fused layer that consumes it."""
+    S, m = SpikeLinearLIF.apply(x, _carried_mask(x), weight, bias, beta, theta, u_r, alpha, mode)
+    setattr(S, _MASK_ATTR, (m, S._version))
+    return S
 
 
 def spike_producer_applies(din, dout):

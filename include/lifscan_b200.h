@@ -391,23 +391,50 @@ int lifb_alif_bwd_scan(const float *I, const float *u0, const float *w0, const f
                        float theta0, float alpha, int64_t C, void *workspace, size_t workspace_bytes,
                        void *stream);
 
+/* Spike mask of a [R, D] fp32 tensor (a spike raster: R = T*B rows (t, b)),
+ * D <= 1024: mask [R, lifb_spike_mask_stride(D)] 32-bit words, 16-byte
+ * aligned.  Word k of a row has bit q set when element 32k + q is nonzero
+ * (NaN counts, -0 does not); word ceil(D/32) has bit 0 set when a nonzero
+ * element of the row is not exactly 1.0 (consumers then read that row's values
+ * from the dense tensor); the remaining words are padding, so that a row is a
+ * whole number of 16-byte TMA units.  The format is this library's own: the
+ * reference keeps spike rasters dense (lifscan/shdnet.py:12-27). */
+int64_t lifb_spike_mask_stride(int64_t D);
+int lifb_spike_mask(const float *X, uint32_t *mask, int64_t R, int64_t D, void *stream);
+
 /* Fused forward of one layer of a spiking network: a Linear layer on a spike
- * input followed by the hard-reset LIF.  X [T, B, Din] (0/1 spikes), W [Dout,
- * Din] and bias [Dout] (NULL: none) as torch.nn.Linear holds them, u0 [B*Dout]
- * (NULL: zeros); writes V (pre-reset potentials, for the adjoint from V) and S,
- * both [T, B*Dout] with neuron b*Dout + j, the layout of
- * fc(x).reshape(T, -1) (lifscan/shdnet.py:39).  I = X W^T + bias is formed in
- * shared memory and consumed there, never written: each element sums the
- * active inputs' weights in input order from 0 and adds the bias last, the
- * order of cuBLAS's fp32 GEMM on such an input, so S equals the unfused
- * Linear -> lif_tuned (lifscan/shdnet.py:38-45, triton_lif.py:654-687) bit for
- * bit.  Needs Dout % 32 == 0 and Din <= 1024 (LIFB_ERR_UNSUPPORTED otherwise;
- * the caller then runs the unfused layer).  Replaces the forward of
- * shdnet.LIFLayer (lifscan/shdnet.py:30-50). */
-int lifb_spike_linear_lif_fwd(const float *X, const float *W, const float *bias,
-                              const float *u0, float *V, float *S, int64_t T, int64_t B,
-                              int64_t Din, int64_t Dout, float beta, float theta,
-                              float u_r, void *stream);
+ * input followed by the hard-reset LIF.  X [T, B, Din] and its spike mask
+ * Xmask (lifb_spike_mask, or the Smask of the layer before), W [Dout, Din] and
+ * bias [Dout] (NULL: none) as torch.nn.Linear holds them, u0 [B*Dout] (NULL:
+ * zeros); writes V (pre-reset potentials, for the adjoint from V) and S, both
+ * [T, B*Dout] with neuron b*Dout + j, the layout of fc(x).reshape(T, -1)
+ * (lifscan/shdnet.py:39), and, when Smask is not NULL, the spike mask of S
+ * ([T*B, lifb_spike_mask_stride(Dout)]) for the next layer.  I = X W^T + bias
+ * is formed in shared memory and consumed there, never written: each element
+ * sums the active inputs' weights in input order from 0 and adds the bias
+ * last, the order of cuBLAS's fp32 GEMM on such an input, so S equals the
+ * unfused Linear -> lif_tuned (lifscan/shdnet.py:38-45,
+ * triton_lif.py:654-687) bit for bit.  Needs Dout % 32 == 0 and Din <= 1024
+ * (LIFB_ERR_UNSUPPORTED otherwise; the caller then runs the unfused layer).
+ * Replaces the forward of shdnet.LIFLayer (lifscan/shdnet.py:30-50). */
+int lifb_spike_linear_lif_fwd(const float *X, const uint32_t *Xmask, const float *W,
+                              const float *bias, const float *u0, float *V, float *S,
+                              uint32_t *Smask, int64_t T, int64_t B, int64_t Din,
+                              int64_t Dout, float beta, float theta, float u_r, void *stream);
+
+/* Weight and bias gradients of a Linear layer on a spike input: gW [Dout, Din]
+ * = dI^T X and gb [Dout] = sum over rows of dI (gb NULL: skipped), from dI
+ * [R, Dout] and the input X [R, Din] with its spike mask; only the active
+ * (row, input) pairs are visited.  The sums run over rows in a fixed order
+ * (2048-row chunks, then the chunks in order), so the result is deterministic;
+ * it differs from a GEMM's by rounding only.  Workspace:
+ * lifb_spike_linear_wgrad_workspace_bytes(R, Din, Dout).  Replaces the weight
+ * and bias gradients torch's Linear backward computes for shdnet.LIFLayer
+ * (lifscan/shdnet.py:33,39). */
+size_t lifb_spike_linear_wgrad_workspace_bytes(int64_t R, int64_t Din, int64_t Dout);
+int lifb_spike_linear_wgrad(const float *dI, const float *X, const uint32_t *Xmask, float *gW,
+                            float *gb, int64_t R, int64_t Din, int64_t Dout, void *workspace,
+                            size_t workspace_bytes, void *stream);
 
 /* Time-sharded forward, the two halves of a slice's replay around the hand-over
  * of its end state (workspace: lifb_scan_fwd_spec_workspace_bytes(T, N, L)).
