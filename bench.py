@@ -1219,9 +1219,11 @@ def run_network(args, ws, rank, local):
     leaky readout, cross-entropy over 20 random labels, synthetic Bernoulli
     raster (rates U(0.5%, 4%)).  Data parallel: one bucketed all-reduce of the
     weight gradients per step when N > 1.  The headline runs both LIF layers
-    through the fused spike-input producer (producer="spike"); the same step
-    with nn.Linear then lif_tuned (producer="linear") is timed beside, and the
-    two forwards' spikes are compared bit for bit.  The raster (183 MB) is
+    as spike-input layers (producer="spike": the input's spike mask, the fused
+    Linear -> LIF forward over the active inputs, the sparse weight and bias
+    gradients); the same step with nn.Linear then lif_tuned
+    (producer="linear") is timed beside, and the two forwards' spikes are
+    compared bit for bit.  The raster (183 MB) is
     larger than L2."""
     import torch
     import torch.distributed as dist
@@ -1324,7 +1326,9 @@ def run_network(args, ws, rank, local):
             "config": {"workload": "c3: network training step (forward, backward, Adam)", "beta": 0.9,
                        "init": "kaiming-uniform", "readout": "leaky (non-spiking integrator, mean over T)",
                        "lif_mode": "scan", "batch_per_gpu": B, "seq_len": T,
-                       "producer": "spike (fused spike-input Linear -> LIF forward, lifb_spike_linear_lif_fwd)",
+                       "producer": "spike (input spike mask, fused Linear -> LIF forward, sparse weight/bias "
+                                   "gradient: lifb_spike_mask, lifb_spike_linear_lif_fwd, "
+                                   "lifb_spike_linear_wgrad)",
                        "parallelism": f"data-parallel x{ws}, gradient all-reduce per step",
                        "step": "forward+backward and Adam each captured in a CUDA graph",
                        "l2": "the input raster (183 MB) and every layer tensor (64 MB) exceed or fill L2"},

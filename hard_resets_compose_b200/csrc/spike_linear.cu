@@ -24,22 +24,23 @@
 // (JW per lane) and `bpc` batch elements: the weight slice sits transposed in
 // shared memory ([Din][32] JW-vectors, a conflict-free broadcast read per
 // active input), the mask rows of each 16-step tile arrive by one 3-D TMA
-// load (double-buffered, bounded mbarrier waits), former warps expand each
-// row's mask into a list of active inputs (a warp prefix sum of the words'
-// popcounts) and sum the listed weight vectors in order, and one warp per
-// batch element steps the recurrence over the previous tile from shared
-// memory.  I never reaches global memory.  Weights that are not finite make
+// load (four stages in flight, bounded mbarrier waits), and the warps take the
+// tile's rows from a shared counter, expand each row's mask into a list of
+// active inputs (a warp prefix sum of the words' popcounts) and sum the listed
+// weight vectors in order; one warp per batch element first steps the
+// recurrence over the previous tile from shared memory.  I never reaches global memory.  Weights that are not finite make
 // the GEMM's zero terms NaN (0 * inf): the lanes of such outputs take the
 // dense sum over every input instead, so the bits still match.
 //
 // Weight gradient (k_spike_wgrad).  gW[j, c] = sum_r dI[r, j] X[r, c] and
 // gb[j] = sum_r dI[r, j] touch only the active (r, c): per 32-row block a
 // CTA stages the dI tile of its outputs and the block's mask rows by TMA;
-// each warp owns 16 input columns and 32*JJ outputs (JJ per lane, an
+// each warp owns 8 input columns and 32*JJ outputs (JJ per lane, up to 8: an
 // accumulator per column and output in registers), turns the block's mask
-// bits into per-column row sets with ballots and adds the listed dI rows in
-// row order.  Each CTA covers a fixed 2048-row chunk; a second pass adds the
-// chunks in order, so the result is deterministic and independent of the GPU.
+// bits into per-column row sets with ballots (only for columns active in the
+// block) and adds the listed dI rows in row order.  Each CTA covers a chunk of
+// rows whose size follows from the shape alone; a second pass adds the
+// chunks in order, so the result is deterministic and the same on every GPU.
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
 #include "tma.cuh"
@@ -53,11 +54,11 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMaskWarps = 8;    // rows (one per warp) in flight per mask CTA
 constexpr int kSLTile = 16;      // time steps per producer tile
-constexpr int kSLWarps = 16;     // producer CTA: bpc recurrence warps, the rest form rows
-constexpr int kWgWarps = 8;      // weight-gradient CTA: 8 warps x 16 columns
-constexpr int kWgCols = 16;
-constexpr int kWgChunk = 2048;   // rows per weight-gradient CTA (fixes the summation order)
-constexpr int kMaxMaskStride = 36;
+constexpr int kSLStages = 4;     // mask tiles in flight
+constexpr int kSLWarps = 16;     // producer CTA: every warp forms rows; bpc of them also step the LIF
+constexpr int kWgWarps = 16;     // weight-gradient CTA: 16 warps x 8 columns
+constexpr int kWgCols = 8;
+constexpr int kWgTargetCtas = 148;  // row chunks sized for about this many CTAs (from the shape alone)
 }  // namespace
 
 int64_t spike_mask_stride(int64_t D) { return ((D + 31) / 32 + 1 + 3) / 4 * 4; }
@@ -121,11 +122,32 @@ __host__ __device__ inline SLSmem sl_layout(int Din, int JW, int bpc, int NWp)
     SLSmem L;
     L.it = (size_t)Din * 32 * JW * 4;                                    // weight slice at 0
     L.mk = (L.it + (size_t)2 * bpc * kSLTile * 32 * JW * 4 + 127) / 128 * 128;  // I tiles, then mask tiles
-    L.lst = L.mk + (size_t)2 * kSLTile * bpc * NWp * 4;
+    L.lst = L.mk + (size_t)kSLStages * kSLTile * bpc * NWp * 4;
     L.total = L.lst + (size_t)kSLWarps * 32 * 4;
     return L;
 }
 }  // namespace
+
+// Shared-memory loads at 32-bit shared addresses: JW consecutive floats, and
+// four ints (a broadcast read of four list entries).
+template <int JW>
+__device__ __forceinline__ void lds_f32(uint32_t a, float (&w)[JW])
+{
+    if constexpr (JW == 2)
+        asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(w[0]), "=f"(w[1]) : "r"(a));
+    else
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(w[0]) : "r"(a));
+}
+
+__device__ __forceinline__ int4 lds_s32x4(uint32_t a)
+{
+    int4 v;
+    asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(a)
+                 : "memory");
+    return v;
+}
 
 template <int JW>
 __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
@@ -140,9 +162,10 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
     float *Ws = reinterpret_cast<float *>(sl_raw);
     float *It = reinterpret_cast<float *>(sl_raw + L.it);
     uint32_t *Mk = reinterpret_cast<uint32_t *>(sl_raw + L.mk);
-    __shared__ uint64_t bar[2];
+    __shared__ uint64_t bar[kSLStages];
     __shared__ int s_bad[OG];
     __shared__ int s_err;
+    __shared__ int s_next[2];
 
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ngroups = Dout / OG;
@@ -156,24 +179,29 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
     const size_t mtile = (size_t)kSLTile * bpc * NWp;  // words per mask tile
     const uint32_t tile_bytes = (uint32_t)(mtile * 4);
     int *lst = reinterpret_cast<int *>(sl_raw + L.lst) + w * 32;
+    constexpr int kWRow = 128 * JW;  // bytes per input row of the weight slice
+    const uint32_t wbase = smem_u32(Ws) + 4u * JW * lane;
+    const uint32_t lst_s = smem_u32(lst);
 
     if (threadIdx.x == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        for (int i = 0; i < kSLStages; i++) mbar_init(&bar[i], 1);
         fence_barrier_init();
         s_err = 0;
+        s_next[0] = 0;
     }
     for (int i = threadIdx.x; i < OG; i += blockDim.x) s_bad[i] = 0;
     __syncthreads();
-    int64_t last[2] = {-1, -1};  // (thread 0) the last tile issued into each buffer
+    int64_t last[kSLStages];  // (thread 0) the last tile issued into each buffer
+    for (int i = 0; i < kSLStages; i++) last[i] = -1;
     if (threadIdx.x == 0) {
-        for (int k = 0; k < 2 && k < ntiles; k++) {
+        for (int k = 0; k < kSLStages && k < ntiles; k++) {
             mbar_arrive_expect_tx(&bar[k], tile_bytes);
             tma_load_3d(Mk + k * mtile, &tm, 0, (int)b0, k * kSLTile, &bar[k]);
             last[k] = k;
         }
     }
     // the weight slice, transposed: Ws[(c * 32 + l) * JW + e] = W[j0 + e * 32 + l, c]
+#pragma unroll 8
     for (int64_t e = threadIdx.x; e < (int64_t)Din * OG; e += blockDim.x) {
         const int o = (int)(e % OG), c = (int)(e / OG);
         const float wv = __ldg(W + (int64_t)(j0 + o) * Din + c);
@@ -212,48 +240,45 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
         uint32_t mm = m;
         int p = incl - cnt;  // list position of this lane's next active input
         for (int base = 0; base < total; base += 32) {
+            // the list holds the active inputs' byte offsets into the weight slice
             while (mm && p < base + 32) {
                 const int q = __ffs(mm) - 1;
                 mm &= mm - 1;
-                lst[p - base] = lane * 32 + q;
+                lst[p - base] = (lane * 32 + q) * kWRow;
                 p++;
             }
             __syncwarp();
             const int n = total - base < 32 ? total - base : 32;
-            const int myc = lane < n ? lst[lane] : 0;
-            __syncwarp();
             int i = 0;
             if (!odd) {
                 for (; i + 4 <= n; i += 4) {
-                    const int c0 = __shfl_sync(kFull, myc, i), c1 = __shfl_sync(kFull, myc, i + 1);
-                    const int c2 = __shfl_sync(kFull, myc, i + 2), c3 = __shfl_sync(kFull, myc, i + 3);
-                    if constexpr (JW == 2) {
-                        const float2 w0 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c0 * 32 + lane) * 2);
-                        const float2 w1 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c1 * 32 + lane) * 2);
-                        const float2 w2 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c2 * 32 + lane) * 2);
-                        const float2 w3 = *reinterpret_cast<const float2 *>(Ws + ((size_t)c3 * 32 + lane) * 2);
-                        a[0] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[0], w0.x), w1.x), w2.x), w3.x);
-                        a[JW - 1] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[JW - 1], w0.y), w1.y), w2.y), w3.y);
-                    } else {
-                        const float w0 = Ws[(size_t)c0 * 32 + lane], w1 = Ws[(size_t)c1 * 32 + lane];
-                        const float w2 = Ws[(size_t)c2 * 32 + lane], w3 = Ws[(size_t)c3 * 32 + lane];
-                        a[0] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[0], w0), w1), w2), w3);
-                    }
+                    const int4 o = lds_s32x4(lst_s + 4 * i);
+                    float w0[JW], w1[JW], w2[JW], w3[JW];
+                    lds_f32<JW>(wbase + o.x, w0);
+                    lds_f32<JW>(wbase + o.y, w1);
+                    lds_f32<JW>(wbase + o.z, w2);
+                    lds_f32<JW>(wbase + o.w, w3);
+#pragma unroll
+                    for (int e = 0; e < JW; e++)
+                        a[e] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[e], w0[e]), w1[e]), w2[e]), w3[e]);
                 }
                 for (; i < n; i++) {
-                    const int c = __shfl_sync(kFull, myc, i);
+                    float w0[JW];
+                    lds_f32<JW>(wbase + lst[i], w0);
 #pragma unroll
-                    for (int e = 0; e < JW; e++) a[e] = __fadd_rn(a[e], Ws[((size_t)c * 32 + lane) * JW + e]);
+                    for (int e = 0; e < JW; e++) a[e] = __fadd_rn(a[e], w0[e]);
                 }
             } else {
-                const float myx = lane < n ? __ldg(xr + myc) : 0.0f;
                 for (; i < n; i++) {
-                    const int c = __shfl_sync(kFull, myc, i);
-                    const float x = __shfl_sync(kFull, myx, i);
+                    const int o = lst[i];
+                    const float x = __ldg(xr + o / kWRow);
+                    float w0[JW];
+                    lds_f32<JW>(wbase + o, w0);
 #pragma unroll
-                    for (int e = 0; e < JW; e++) a[e] = fmaf(x, Ws[((size_t)c * 32 + lane) * JW + e], a[e]);
+                    for (int e = 0; e < JW; e++) a[e] = fmaf(x, w0[e], a[e]);
                 }
             }
+            __syncwarp();  // the next batch rewrites the list
         }
         if (warp_bad) {  // non-finite weights: every term, zeros included
             float d[JW];
@@ -275,8 +300,8 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
 #pragma unroll
     for (int e = 0; e < JW; e++) u[e] = (w < nb && u0) ? u0[(b0 + w) * Dout + j0 + e * 32 + lane] : 0.0f;
     const int slots = nb * kSLTile;
-    const int nform = kSLWarps - bpc;
     for (int64_t k = 0; k <= ntiles; k++) {
+        if (threadIdx.x == 0) s_next[(k + 1) & 1] = 0;  // the row counter of the next tile
         if (w < nb && k >= 1) {  // the recurrence over tile k - 1
             const int64_t t0 = (k - 1) * kSLTile;
             const float *cur = It + ((size_t)((k - 1) & 1) * bpc + w) * kSLTile * OG;
@@ -302,13 +327,17 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
                 }
             }
         }
-        if (w >= bpc && k < ntiles) {  // form tile k
-            const int buf = (int)(k & 1);
-            if (!s_err && !mbar_wait(&bar[buf], (uint32_t)((k >> 1) & 1)) && lane == 0) atomicExch(&s_err, 1);
-            const uint32_t *mt = Mk + buf * mtile;
-            float *nxt = It + (size_t)buf * bpc * kSLTile * OG;
+        if (k < ntiles) {  // form tile k: every warp takes rows from a shared counter until none are left
+            const int st = (int)(k % kSLStages);
+            if (!s_err && !mbar_wait(&bar[st], (uint32_t)((k / kSLStages) & 1)) && lane == 0) atomicExch(&s_err, 1);
+            const uint32_t *mt = Mk + st * mtile;
+            float *nxt = It + (size_t)(k & 1) * bpc * kSLTile * OG;
             const int64_t t0 = k * kSLTile;
-            for (int f = w - bpc; f < slots; f += nform) {
+            for (;;) {
+                int f = 0;
+                if (lane == 0) f = atomicAdd(&s_next[k & 1], 1);
+                f = __shfl_sync(kFull, f, 0);
+                if (f >= slots) break;
                 const int bi = f / kSLTile, r = f % kSLTile;
                 if (t0 + r < T)
                     form(mt + ((size_t)r * bpc + bi) * NWp, (t0 + r) * B + b0 + bi,
@@ -316,16 +345,17 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
             }
         }
         __syncthreads();
-        if (threadIdx.x == 0 && k + 2 < ntiles && !s_err) {  // buffer k & 1 is free again
-            mbar_arrive_expect_tx(&bar[k & 1], tile_bytes);
-            tma_load_3d(Mk + (k & 1) * mtile, &tm, 0, (int)b0, (int)((k + 2) * kSLTile), &bar[k & 1]);
-            last[k & 1] = k + 2;
+        if (threadIdx.x == 0 && k < ntiles && k + kSLStages < ntiles && !s_err) {  // stage k is free again
+            const int st = (int)(k % kSLStages);
+            mbar_arrive_expect_tx(&bar[st], tile_bytes);
+            tma_load_3d(Mk + st * mtile, &tm, 0, (int)b0, (int)((k + kSLStages) * kSLTile), &bar[st]);
+            last[st] = k + kSLStages;
         }
     }
     if (threadIdx.x == 0 && s_err) {
         // let copies still in flight land before the CTA's shared memory goes away
-        for (int i = 0; i < 2; i++)
-            if (last[i] >= 0) mbar_wait(&bar[i], (uint32_t)((last[i] >> 1) & 1));
+        for (int i = 0; i < kSLStages; i++)
+            if (last[i] >= 0) mbar_wait(&bar[i], (uint32_t)((last[i] / kSLStages) & 1));
         if (status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
     }
 }
@@ -374,24 +404,81 @@ bool spike_linear_lif_fwd(const float *X, const uint32_t *Xm, const float *W, co
 // ---------------------------------------------------------------------------
 // weight gradient
 
+namespace {
+// A lane's JJ outputs: groups of 4 consecutive outputs, 128 apart (JJ >= 4),
+// or JJ consecutive ones; either way a lane's shared-memory reads are
+// conflict-free 16-, 8- or 4-byte vectors.
 template <int JJ>
-__global__ void __launch_bounds__(32 * kWgWarps) k_spike_wgrad(const __grid_constant__ CUtensorMap tdi,
-                                                              const __grid_constant__ CUtensorMap tmk,
-                                                              const float *__restrict__ X, float *__restrict__ Pw,
-                                                              float *__restrict__ Pb, int64_t R, int Din, int Dout,
-                                                              int NWp, int Dp, int *status)
+__device__ __forceinline__ int wg_out(int lane, int e)
+{
+    return JJ >= 4 ? (e >> 2) * 128 + 4 * lane + (e & 3) : JJ * lane + e;
+}
+
+template <int JJ>
+__device__ __forceinline__ void wg_load(const float *row, int lane, float (&d)[JJ])
+{
+    if constexpr (JJ >= 4) {
+#pragma unroll
+        for (int g = 0; g < JJ / 4; g++) {
+            const float4 v = *reinterpret_cast<const float4 *>(row + g * 128 + 4 * lane);
+            d[4 * g] = v.x;
+            d[4 * g + 1] = v.y;
+            d[4 * g + 2] = v.z;
+            d[4 * g + 3] = v.w;
+        }
+    } else if constexpr (JJ == 2) {
+        const float2 v = *reinterpret_cast<const float2 *>(row + 2 * lane);
+        d[0] = v.x;
+        d[1] = v.y;
+    } else {
+        d[0] = row[lane];
+    }
+}
+
+struct WgPlan {
+    int JJ;
+    int64_t nsg, njs, chunk, nck, Dp;
+};
+
+// Work split of the weight gradient: 32*JJ outputs per warp, kWgCols columns
+// per warp, kWgWarps warps per CTA, and the rows in chunks sized so that
+// about kWgTargetCtas CTAs cover the job.  It depends on the shape only, so
+// the summation order (and the result) is the same on every GPU.
+WgPlan wg_plan(int64_t R, int64_t Din, int64_t Dout)
+{
+    WgPlan p;
+    p.JJ = Dout % 256 == 0 ? 8 : Dout % 128 == 0 ? 4 : Dout % 64 == 0 ? 2 : 1;
+    p.Dp = (Din + kWgCols - 1) / kWgCols * kWgCols;
+    p.nsg = (p.Dp / kWgCols + kWgWarps - 1) / kWgWarps;
+    p.njs = Dout / (32 * p.JJ);
+    const int64_t want = std::max<int64_t>(1, kWgTargetCtas / (p.nsg * p.njs));
+    p.chunk = std::max<int64_t>(32, ((R + want - 1) / want + 31) / 32 * 32);
+    p.nck = (R + p.chunk - 1) / p.chunk;
+    return p;
+}
+
+size_t wg_smem(int JJ, int NWp) { return (size_t)2 * 32 * 32 * JJ * 4 + (size_t)2 * 32 * NWp * 4; }
+}  // namespace
+
+template <int JJ>
+__global__ void __launch_bounds__(32 * kWgWarps, 1) k_spike_wgrad(const __grid_constant__ CUtensorMap tdi,
+                                                                 const __grid_constant__ CUtensorMap tmk,
+                                                                 const float *__restrict__ X, float *__restrict__ Pw,
+                                                                 float *__restrict__ Pb, int64_t R, int Din, int Dout,
+                                                                 int NWp, int Dp, int64_t chunk, int *status)
 {
     constexpr int JS = 32 * JJ;
-    __shared__ __align__(128) float s_d[2][32 * JS];
-    __shared__ __align__(128) uint32_t s_m[2][32 * kMaxMaskStride];
+    extern __shared__ __align__(128) unsigned char wg_raw[];
+    float *s_d = reinterpret_cast<float *>(wg_raw);                                 // [2][32][JS]
+    uint32_t *s_m = reinterpret_cast<uint32_t *>(wg_raw + (size_t)2 * 32 * JS * 4);  // [2][32][NWp]
     __shared__ uint64_t bar[2];
     __shared__ int s_err;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int js = blockIdx.y;
     const int64_t ck = blockIdx.z;
     const int c0 = (blockIdx.x * kWgWarps + w) * kWgCols;
-    const int64_t r0 = ck * kWgChunk;
-    const int64_t rend = R < r0 + kWgChunk ? R : r0 + kWgChunk;
+    const int64_t r0 = ck * chunk;
+    const int64_t rend = R < r0 + chunk ? R : r0 + chunk;
     const int nblk = (int)((rend - r0 + 31) / 32);
     const uint32_t bytes = (uint32_t)(32 * JS * 4 + 32 * NWp * 4);
     const int NW = (Din + 31) >> 5;
@@ -409,8 +496,8 @@ __global__ void __launch_bounds__(32 * kWgWarps) k_spike_wgrad(const __grid_cons
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2 && b < nblk; b++) {
             mbar_arrive_expect_tx(&bar[b], bytes);
-            tma_load_2d(s_d[b], &tdi, js * JS, (int)(r0 + 32 * b), &bar[b]);
-            tma_load_2d(s_m[b], &tmk, 0, (int)(r0 + 32 * b), &bar[b]);
+            tma_load_2d(s_d + b * 32 * JS, &tdi, js * JS, (int)(r0 + 32 * b), &bar[b]);
+            tma_load_2d(s_m + b * 32 * NWp, &tmk, 0, (int)(r0 + 32 * b), &bar[b]);
             last[b] = b;
         }
     }
@@ -426,34 +513,36 @@ __global__ void __launch_bounds__(32 * kWgWarps) k_spike_wgrad(const __grid_cons
     for (int b = 0; b < nblk; b++) {
         const int buf = b & 1;
         if (!s_err && !mbar_wait(&bar[buf], (uint32_t)((b >> 1) & 1)) && lane == 0) atomicExch(&s_err, 1);
-        const float *dt = s_d[buf] + JJ * lane;
-        const uint32_t *mt = s_m[buf];
+        const float *dt = s_d + buf * 32 * JS;
+        const uint32_t *mt = s_m + buf * 32 * NWp;
         if (has_cols) {
-            uint32_t wd = (mt[lane * NWp + (c0 >> 5)] >> (c0 & 31)) & 0xffffu;
+            uint32_t wd = (mt[lane * NWp + (c0 >> 5)] >> (c0 & 31)) & ((1u << kWgCols) - 1u);
             if (Din - c0 < kWgCols) wd &= (1u << (Din - c0)) - 1u;  // bits past Din are not inputs
             const bool od = (mt[lane * NWp + NW] & 1u) != 0;
             const uint32_t odd_rows = __ballot_sync(kFull, od && wd != 0);
+            const uint32_t colany = __reduce_or_sync(kFull, wd);
             const int64_t rb = r0 + 32 * b;
 #pragma unroll
             for (int q = 0; q < kWgCols; q++) {
+                if (!((colany >> q) & 1u)) continue;
                 uint32_t cw = __ballot_sync(kFull, (wd >> q) & 1u);
-                if (!cw) continue;
                 if (!(cw & odd_rows)) {
+                    // rows in increasing order, two loads in flight
                     while (cw) {
-                        const int r = __ffs(cw) - 1;
+                        const int r1 = __ffs(cw) - 1;
                         cw &= cw - 1;
-                        if constexpr (JJ == 4) {
-                            const float4 d = *reinterpret_cast<const float4 *>(dt + r * JS);
-                            acc[q][0] = __fadd_rn(acc[q][0], d.x);
-                            acc[q][1] = __fadd_rn(acc[q][1], d.y);
-                            acc[q][2] = __fadd_rn(acc[q][2], d.z);
-                            acc[q][3] = __fadd_rn(acc[q][3], d.w);
-                        } else if constexpr (JJ == 2) {
-                            const float2 d = *reinterpret_cast<const float2 *>(dt + r * JS);
-                            acc[q][0] = __fadd_rn(acc[q][0], d.x);
-                            acc[q][1] = __fadd_rn(acc[q][1], d.y);
+                        float d1[JJ];
+                        wg_load<JJ>(dt + r1 * JS, lane, d1);
+                        if (cw) {
+                            const int r2 = __ffs(cw) - 1;
+                            cw &= cw - 1;
+                            float d2[JJ];
+                            wg_load<JJ>(dt + r2 * JS, lane, d2);
+#pragma unroll
+                            for (int e = 0; e < JJ; e++) acc[q][e] = __fadd_rn(__fadd_rn(acc[q][e], d1[e]), d2[e]);
                         } else {
-                            acc[q][0] = __fadd_rn(acc[q][0], dt[r * JS]);
+#pragma unroll
+                            for (int e = 0; e < JJ; e++) acc[q][e] = __fadd_rn(acc[q][e], d1[e]);
                         }
                     }
                 } else {
@@ -461,23 +550,28 @@ __global__ void __launch_bounds__(32 * kWgWarps) k_spike_wgrad(const __grid_cons
                         const int r = __ffs(cw) - 1;
                         cw &= cw - 1;
                         const float x = ((odd_rows >> r) & 1u) ? __ldg(X + (rb + r) * Din + c0 + q) : 1.0f;
+                        float d[JJ];
+                        wg_load<JJ>(dt + r * JS, lane, d);
 #pragma unroll
-                        for (int e = 0; e < JJ; e++) acc[q][e] = fmaf(x, dt[r * JS + e], acc[q][e]);
+                        for (int e = 0; e < JJ; e++) acc[q][e] = fmaf(x, d[e], acc[q][e]);
                     }
                 }
             }
         }
-        if (do_bias) {  // this warp's four rows of the block
+        if (do_bias) {  // this warp's share of the block's rows
 #pragma unroll
-            for (int r = 4 * w; r < 4 * w + 4; r++)
+            for (int r = (32 / kWgWarps) * w; r < (32 / kWgWarps) * (w + 1); r++) {
+                float d[JJ];
+                wg_load<JJ>(dt + r * JS, lane, d);
 #pragma unroll
-                for (int e = 0; e < JJ; e++) accb[e] = __fadd_rn(accb[e], dt[r * JS + e]);
+                for (int e = 0; e < JJ; e++) accb[e] = __fadd_rn(accb[e], d[e]);
+            }
         }
         __syncthreads();
         if (threadIdx.x == 0 && b + 2 < nblk && !s_err) {
             mbar_arrive_expect_tx(&bar[buf], bytes);
-            tma_load_2d(s_d[buf], &tdi, js * JS, (int)(r0 + 32 * (b + 2)), &bar[buf]);
-            tma_load_2d(s_m[buf], &tmk, 0, (int)(r0 + 32 * (b + 2)), &bar[buf]);
+            tma_load_2d(s_d + buf * 32 * JS, &tdi, js * JS, (int)(r0 + 32 * (b + 2)), &bar[buf]);
+            tma_load_2d(s_m + buf * 32 * NWp, &tmk, 0, (int)(r0 + 32 * (b + 2)), &bar[buf]);
             last[buf] = b + 2;
         }
     }
@@ -486,52 +580,63 @@ __global__ void __launch_bounds__(32 * kWgWarps) k_spike_wgrad(const __grid_cons
             if (last[i] >= 0) mbar_wait(&bar[i], (uint32_t)((last[i] >> 1) & 1));
         if (status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
     }
-    const int jb = js * JS + JJ * lane;
     if (has_cols) {
 #pragma unroll
         for (int e = 0; e < JJ; e++) {
-            float4 *o = reinterpret_cast<float4 *>(Pw + ((size_t)ck * Dout + jb + e) * Dp + c0);
+            const int j = js * JS + wg_out<JJ>(lane, e);
+            float4 *o = reinterpret_cast<float4 *>(Pw + ((size_t)ck * Dout + j) * Dp + c0);
 #pragma unroll
             for (int q = 0; q < kWgCols; q += 4)
                 o[q / 4] = make_float4(acc[q][e], acc[q + 1][e], acc[q + 2][e], acc[q + 3][e]);
         }
     }
-    if (do_bias) {
+    if (do_bias) {  // the warps' bias sums, added in warp order: one partial per chunk
+        float *s_b = s_d;  // the dI tiles are no longer read
 #pragma unroll
-        for (int e = 0; e < JJ; e++) Pb[((size_t)ck * kWgWarps + w) * Dout + jb + e] = accb[e];
-    }
-}
-
-// The chunks' partial sums, added in chunk order (and, for the bias, warp order).
-__global__ void k_spike_wgrad_reduce(const float *__restrict__ Pw, const float *__restrict__ Pb,
-                                     float *__restrict__ gW, float *__restrict__ gb, int64_t nck, int Din, int Dout,
-                                     int Dp)
-{
-    const int64_t n = (int64_t)Dout * Din;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t j = i / Din, c = i % Din;
-        float acc = 0.0f;
-        for (int64_t k = 0; k < nck; k++) acc = __fadd_rn(acc, Pw[(k * Dout + j) * Dp + c]);
-        gW[i] = acc;
-    }
-    if (gb) {
-        for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < Dout; j += (int64_t)gridDim.x * blockDim.x) {
+        for (int e = 0; e < JJ; e++) s_b[w * JS + wg_out<JJ>(lane, e)] = accb[e];
+        __syncthreads();
+        for (int j = threadIdx.x; j < JS; j += blockDim.x) {
             float acc = 0.0f;
-            for (int64_t k = 0; k < nck * kWgWarps; k++) acc = __fadd_rn(acc, Pb[k * Dout + j]);
-            gb[j] = acc;
+            for (int v = 0; v < kWgWarps; v++) acc = __fadd_rn(acc, s_b[v * JS + j]);
+            Pb[(size_t)ck * Dout + js * JS + j] = acc;
         }
     }
 }
 
-namespace {
-int64_t wgrad_chunks(int64_t R) { return (R + kWgChunk - 1) / kWgChunk; }
-int64_t wgrad_dp(int64_t Din) { return (Din + kWgCols - 1) / kWgCols * kWgCols; }
-}  // namespace
+// The chunks' partial sums, added in chunk order.
+__global__ void k_spike_wgrad_reduce(const float *__restrict__ Pw, const float *__restrict__ Pb,
+                                     float *__restrict__ gW, float *__restrict__ gb, int64_t nck, int Din, int Dout,
+                                     int Dp)
+{
+    // a sum over chunks in chunk order, eight loads in flight
+    auto chunk_sum = [&](const float *p, int64_t stride) {
+        float acc = 0.0f;
+        int64_t k = 0;
+        for (; k + 8 <= nck; k += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = p[(k + u) * stride];
+#pragma unroll
+            for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
+        }
+        for (; k < nck; k++) acc = __fadd_rn(acc, p[k * stride]);
+        return acc;
+    };
+    const int64_t n = (int64_t)Dout * Din;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / Din, c = i % Din;
+        gW[i] = chunk_sum(Pw + j * Dp + c, (int64_t)Dout * Dp);
+    }
+    if (gb) {
+        for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < Dout; j += (int64_t)gridDim.x * blockDim.x)
+            gb[j] = chunk_sum(Pb + j, Dout);
+    }
+}
 
 size_t spike_wgrad_workspace_bytes(int64_t R, int64_t Din, int64_t Dout)
 {
-    const int64_t nck = wgrad_chunks(R);
-    return (size_t)(nck * Dout * wgrad_dp(Din) + nck * kWgWarps * Dout) * 4;
+    const WgPlan p = wg_plan(R, Din, Dout);
+    return (size_t)(p.nck * Dout * p.Dp + p.nck * Dout) * 4;
 }
 
 bool spike_wgrad(const float *dI, const float *X, const uint32_t *Xm, float *gW, float *gb, int64_t R, int64_t Din,
@@ -541,27 +646,32 @@ bool spike_wgrad(const float *dI, const float *X, const uint32_t *Xm, float *gW,
     if (((uintptr_t)dI & 15) || ((uintptr_t)Xm & 15) || ((uintptr_t)ws & 15)) return false;
     if (!ws || ws_bytes < spike_wgrad_workspace_bytes(R, Din, Dout)) return false;
     const int NWp = (int)spike_mask_stride(Din);
-    const int64_t nck = wgrad_chunks(R), Dp = wgrad_dp(Din);
-    if (nck > 65535) return false;
+    const WgPlan p = wg_plan(R, Din, Dout);
+    if (p.nck > 65535 || p.njs > 65535) return false;
     float *Pw = static_cast<float *>(ws);
-    float *Pb = Pw + nck * Dout * Dp;
-    const int JJ = Dout % 128 == 0 ? 4 : Dout % 64 == 0 ? 2 : 1;
+    float *Pb = Pw + p.nck * Dout * p.Dp;
     CUtensorMap tdi, tmk;
-    if (!make_tmap_2d(&tdi, dI, Dout, R, 32 * JJ, 32) || !make_tmap_2d_typed(&tmk, Xm, true, NWp, R, NWp, 32))
+    if (!make_tmap_2d(&tdi, dI, Dout, R, 32 * p.JJ, 32) || !make_tmap_2d_typed(&tmk, Xm, true, NWp, R, NWp, 32))
         return false;
-    const dim3 grid((unsigned)((Dp / kWgCols + kWgWarps - 1) / kWgWarps), (unsigned)(Dout / (32 * JJ)),
-                    (unsigned)nck);
+    const dim3 grid((unsigned)p.nsg, (unsigned)p.njs, (unsigned)p.nck);
+    const size_t smem = wg_smem(p.JJ, NWp);
     float *pb = gb ? Pb : nullptr;
     int *st = device_status_ptr();
+    auto go = [&](auto kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, 32 * kWgWarps, smem, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)p.Dp, p.chunk,
+                                                st);
+    };
     count_launches(2);
-    if (JJ == 4) k_spike_wgrad<4><<<grid, 32 * kWgWarps, 0, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)Dp, st);
-    else if (JJ == 2) k_spike_wgrad<2><<<grid, 32 * kWgWarps, 0, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)Dp, st);
-    else k_spike_wgrad<1><<<grid, 32 * kWgWarps, 0, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)Dp, st);
+    if (p.JJ == 8) go(k_spike_wgrad<8>);
+    else if (p.JJ == 4) go(k_spike_wgrad<4>);
+    else if (p.JJ == 2) go(k_spike_wgrad<2>);
+    else go(k_spike_wgrad<1>);
     int dev = 0, nsm = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int64_t n = Dout * Din;
     const unsigned rgrid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)nsm * 8));
-    k_spike_wgrad_reduce<<<rgrid, 256, 0, s>>>(Pw, pb, gW, gb, nck, (int)Din, (int)Dout, (int)Dp);
+    k_spike_wgrad_reduce<<<rgrid, 256, 0, s>>>(Pw, pb, gW, gb, p.nck, (int)Din, (int)Dout, (int)p.Dp);
     return true;
 }
 
