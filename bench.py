@@ -68,6 +68,8 @@ def parse():
                    help="lif_tuned mode (default: the reference's default, scan)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-c3", action="store_true",
+                   help="default run: skip the config-3 network step sub-object")
     p.add_argument("--no-tshard", action="store_true",
                    help="under torchrun, skip the config-4 time-sharded parity check and timing of the default run")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -1213,18 +1215,18 @@ def c4_time_sharded(args, ws, rank, dev, lib):
         "note": "every rank holds the whole sequence for the check; the timed step moves only its slice"}
 
 
-def run_network(args, ws, rank, local):
+def c3_network(args, ws, rank, dev, clock=None):
     """Config 3: one training step (forward, backward, Adam) of the 700-256-256-20
     LIF network, B = 64 per GPU, T = 1024, beta = 0.9, Kaiming-uniform init,
     leaky readout, cross-entropy over 20 random labels, synthetic Bernoulli
     raster (rates U(0.5%, 4%)).  Data parallel: one bucketed all-reduce of the
-    weight gradients per step when N > 1.  The headline runs both LIF layers
-    as spike-input layers (producer="spike": the input's spike mask, the fused
-    Linear -> LIF forward over the active inputs, the sparse weight and bias
-    gradients); the same step with nn.Linear then lif_tuned
-    (producer="linear") is timed beside, and the two forwards' spikes are
-    compared bit for bit.  The raster (183 MB) is
-    larger than L2."""
+    weight gradients per step when ws > 1 (the process group must exist).  The
+    headline runs both LIF layers as spike-input layers (producer="spike": the
+    input's spike mask, the fused Linear -> LIF forward over the active inputs,
+    the sparse weight and bias gradients); the same step with nn.Linear then
+    lif_tuned (producer="linear") is timed beside, and the two forwards'
+    spikes are compared bit for bit.  The raster (183 MB) is larger than L2.
+    Returns the record (rank 0's view; timings are maxima over ranks)."""
     import torch
     import torch.distributed as dist
     import torch.nn as nn
@@ -1232,11 +1234,6 @@ def run_network(args, ws, rank, local):
     from hard_resets_compose_b200 import _lib
     from hard_resets_compose_b200.shdnet import Net, synthetic_batch
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     lib = _lib.load()
     T, B, H = 1024, 64, 256
     x, y = synthetic_batch(T, B, seed=1000 + rank, device=dev)
@@ -1290,7 +1287,7 @@ def run_network(args, ws, rank, local):
         # optimizer's state: both must live as long as the graphs do
         return step, launches, spikes, (g_fb, g_opt, net, opt)
 
-    def time_steps(step, steps, sampler=None):
+    def time_steps(step, steps):
         for _ in range(max(args.warmup, 3)):
             step()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
@@ -1312,31 +1309,58 @@ def run_network(args, ws, rank, local):
 
     step_s, launches, spikes_s, keep_s = make("spike")
     step_l, _, spikes_l, keep_l = make("linear")
-    same_spikes = all(torch.equal(a, b) for a, b in zip(spikes_s, spikes_l))
-    with ClockSampler(local) as clk:
+    same = torch.tensor([float(all(torch.equal(a, b) for a, b in zip(spikes_s, spikes_l)))], device=dev)
+    if ws > 1:
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    if clock is not None:
+        with clock:
+            ms = time_steps(step_s, args.steps)
+    else:
         ms = time_steps(step_s, args.steps)
     ms_linear = time_steps(step_l, max(args.steps // 2, 3))
     units = 2 * B * H * T * ws  # LIF neuron-steps per step, both layers, all ranks
+    del keep_s, keep_l
+    return {
+        "metric": C3_METRIC, "ms_per_step": ms, "value": units / (ms / 1e3), "unit": UNIT,
+        "producer": "spike (input spike mask, fused Linear -> LIF forward, sparse weight/bias gradient: "
+                    "lifb_spike_mask, lifb_spike_linear_lif_fwd, lifb_spike_linear_wgrad)",
+        "linear_producer": {"ms_per_step": ms_linear, "value": units / (ms_linear / 1e3),
+                            "note": "the same step with nn.Linear then lif_tuned in both LIF layers"},
+        "speedup_over_linear_producer": ms_linear / ms,
+        "spikes_bit_equal_between_producers": bool(same.item() == 1.0),
+        "gpu_launches_per_step": launches,
+        "parallelism": f"data-parallel x{ws}, gradient all-reduce per step",
+    }
+
+
+def run_network(args, ws, rank, local):
+    """`--workload c3`: the config-3 network step (c3_network) as its own line."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    clk = ClockSampler(local)
+    rec = c3_network(args, ws, rank, dev, clock=clk)
     if rank == 0:
         print(json.dumps({
             "metric": C3_METRIC,
-            "value": units / (ms / 1e3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic Bernoulli raster, rates U(0.5%, 4%), 20 labels",
+            "value": rec["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic Bernoulli raster, rates U(0.5%, 4%), 20 labels",
             "config": {"workload": "c3: network training step (forward, backward, Adam)", "beta": 0.9,
                        "init": "kaiming-uniform", "readout": "leaky (non-spiking integrator, mean over T)",
-                       "lif_mode": "scan", "batch_per_gpu": B, "seq_len": T,
-                       "producer": "spike (input spike mask, fused Linear -> LIF forward, sparse weight/bias "
-                                   "gradient: lifb_spike_mask, lifb_spike_linear_lif_fwd, "
-                                   "lifb_spike_linear_wgrad)",
-                       "parallelism": f"data-parallel x{ws}, gradient all-reduce per step",
+                       "lif_mode": "scan", "batch_per_gpu": 64, "seq_len": 1024, "producer": rec["producer"],
+                       "parallelism": rec["parallelism"],
                        "step": "forward+backward and Adam each captured in a CUDA graph",
                        "l2": "the input raster (183 MB) and every layer tensor (64 MB) exceed or fill L2"},
-            "linear_producer": {"ms_per_step": ms_linear, "value": units / (ms_linear / 1e3),
-                                "note": "the same step with nn.Linear then lif_tuned in both LIF layers"},
-            "spikes_bit_equal_between_producers": same_spikes,
-            "gpu_launches": launches * args.steps, "clocks": clk.record()}), flush=True)
-    del keep_s, keep_l
+            "linear_producer": rec["linear_producer"],
+            "spikes_bit_equal_between_producers": rec["spikes_bit_equal_between_producers"],
+            "gpu_launches": rec["gpu_launches_per_step"] * args.steps, "clocks": clk.record()}), flush=True)
     if ws > 1:
         dist.destroy_process_group()
 
@@ -1644,6 +1668,11 @@ def main():
     tshard_parity, c4_ts = None, None
     if ws > 1 and not args.no_tshard:
         tshard_parity, c4_ts = c4_time_sharded(args, ws, rank, dev, lib)
+    c3 = None
+    if not args.no_c3:
+        c3_args = argparse.Namespace(**{**vars(args), "steps": 10, "warmup": 3})
+        c3 = c3_network(c3_args, ws, rank, dev)
+        c3["steps"] = c3_args.steps
 
     if rank == 0:
         line = {
@@ -1676,6 +1705,8 @@ def main():
         if ws > 1 and not args.no_tshard:
             line["tshard_parity"] = tshard_parity
             line["c4_tshard"] = c4_ts
+        if c3 is not None:
+            line["c3"] = c3
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

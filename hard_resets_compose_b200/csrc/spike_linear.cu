@@ -21,7 +21,7 @@
 // for bit on B200 for both layer shapes of the network); terms with x_c = 0
 // leave the sum unchanged, so summing only the active inputs in increasing c
 // gives the same bits, and so do the spikes.  One CTA owns 32*JW outputs j
-// (JW per lane) and `bpc` batch elements: the weight slice sits transposed in
+// (JW = 1, 2 or 4 per lane: the widest whose slice fits) and `bpc` batch elements: the weight slice sits transposed in
 // shared memory ([Din][32] JW-vectors, a conflict-free broadcast read per
 // active input), the mask rows of each 16-step tile arrive by one 3-D TMA
 // load (four stages in flight, bounded mbarrier waits), and the warps take the
@@ -34,7 +34,9 @@
 //
 // Weight gradient (k_spike_wgrad).  gW[j, c] = sum_r dI[r, j] X[r, c] and
 // gb[j] = sum_r dI[r, j] touch only the active (r, c): per 32-row block a
-// CTA stages the dI tile of its outputs and the block's mask rows by TMA;
+// producer warp stages the dI tile of the CTA's outputs and the block's mask
+// rows by TMA into a 4-stage ring (full/empty mbarriers, so consumer warps
+// drift apart instead of meeting at a barrier per block);
 // each warp owns 8 input columns and 32*JJ outputs (JJ per lane, up to 8: an
 // accumulator per column and output in registers), turns the block's mask
 // bits into per-column row sets with ballots (only for columns active in the
@@ -56,9 +58,10 @@ constexpr int kMaskWarps = 8;    // rows (one per warp) in flight per mask CTA
 constexpr int kSLTile = 16;      // time steps per producer tile
 constexpr int kSLStages = 4;     // mask tiles in flight
 constexpr int kSLWarps = 16;     // producer CTA: every warp forms rows; bpc of them also step the LIF
-constexpr int kWgWarps = 16;     // weight-gradient CTA: 16 warps x 8 columns
+constexpr int kWgWarps = 16;     // weight-gradient CTA: 16 consumer warps x 8 columns, plus a producer warp
 constexpr int kWgCols = 8;
 constexpr int kWgTargetCtas = 148;  // row chunks sized for about this many CTAs (from the shape alone)
+constexpr int kWgStages = 4;        // dI and mask tiles in flight per CTA
 }  // namespace
 
 int64_t spike_mask_stride(int64_t D) { return ((D + 31) / 32 + 1 + 3) / 4 * 4; }
@@ -133,7 +136,9 @@ __host__ __device__ inline SLSmem sl_layout(int Din, int JW, int bpc, int NWp)
 template <int JW>
 __device__ __forceinline__ void lds_f32(uint32_t a, float (&w)[JW])
 {
-    if constexpr (JW == 2)
+    if constexpr (JW == 4)
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(w[0]), "=f"(w[1]), "=f"(w[2]), "=f"(w[3]) : "r"(a));
+    else if constexpr (JW == 2)
         asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(w[0]), "=f"(w[1]) : "r"(a));
     else
         asm volatile("ld.shared.f32 %0, [%1];" : "=f"(w[0]) : "r"(a));
@@ -322,7 +327,10 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
                 }
                 if (Sm) {
                     uint32_t *mo = Sm + row * NWop;
-                    if (lane < JW) mo[jg * JW + lane] = lane == 0 ? mw[0] : mw[JW - 1];
+                    uint32_t mine = mw[0];
+#pragma unroll
+                    for (int e = 1; e < JW; e++) mine = lane == e ? mw[e] : mine;
+                    if (lane < JW) mo[jg * JW + lane] = mine;
                     if (jg == 0 && NWo + lane < NWop) mo[NWo + lane] = 0u;  // spikes are 0/1: not odd
                 }
             }
@@ -371,7 +379,9 @@ bool spike_linear_lif_fwd(const float *X, const uint32_t *Xm, const float *W, co
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) ||
         cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))
         return false;
-    const int JW = (Dout % 64 == 0 && sl_layout((int)Din, 2, 1, NWp).total <= (size_t)lim) ? 2 : 1;
+    int JW = 1;  // outputs per lane: the widest whose weight slice fits in shared memory
+    for (int cand = 4; cand >= 2; cand /= 2)
+        if (JW == 1 && Dout % (32 * cand) == 0 && sl_layout((int)Din, cand, 1, NWp).total <= (size_t)lim) JW = cand;
     if (sl_layout((int)Din, JW, 1, NWp).total > (size_t)lim) return false;
     const int64_t groups = Dout / (32 * JW);
     auto go = [&](auto kern) -> bool {
@@ -398,7 +408,7 @@ bool spike_linear_lif_fwd(const float *X, const uint32_t *Xm, const float *W, co
                                                           bpc, NWp, NWop, beta, theta, u_r, device_status_ptr());
         return true;
     };
-    return JW == 2 ? go(k_spike_linear_lif<2>) : go(k_spike_linear_lif<1>);
+    return JW == 4 ? go(k_spike_linear_lif<4>) : JW == 2 ? go(k_spike_linear_lif<2>) : go(k_spike_linear_lif<1>);
 }
 
 // ---------------------------------------------------------------------------
@@ -450,57 +460,79 @@ WgPlan wg_plan(int64_t R, int64_t Din, int64_t Dout)
     p.JJ = Dout % 256 == 0 ? 8 : Dout % 128 == 0 ? 4 : Dout % 64 == 0 ? 2 : 1;
     p.Dp = (Din + kWgCols - 1) / kWgCols * kWgCols;
     p.nsg = (p.Dp / kWgCols + kWgWarps - 1) / kWgWarps;
-    p.njs = Dout / (32 * p.JJ);
+    p.njs = (Dout + 32 * p.JJ - 1) / (32 * p.JJ);  // the last slice may be partial (JJ = 1)
     const int64_t want = std::max<int64_t>(1, kWgTargetCtas / (p.nsg * p.njs));
     p.chunk = std::max<int64_t>(32, ((R + want - 1) / want + 31) / 32 * 32);
     p.nck = (R + p.chunk - 1) / p.chunk;
     return p;
 }
 
-size_t wg_smem(int JJ, int NWp) { return (size_t)2 * 32 * 32 * JJ * 4 + (size_t)2 * 32 * NWp * 4; }
+size_t wg_smem(int JJ, int NWp) { return (size_t)kWgStages * 32 * 32 * JJ * 4 + (size_t)kWgStages * 32 * NWp * 4; }
 }  // namespace
 
 template <int JJ>
-__global__ void __launch_bounds__(32 * kWgWarps, 1) k_spike_wgrad(const __grid_constant__ CUtensorMap tdi,
-                                                                 const __grid_constant__ CUtensorMap tmk,
-                                                                 const float *__restrict__ X, float *__restrict__ Pw,
-                                                                 float *__restrict__ Pb, int64_t R, int Din, int Dout,
-                                                                 int NWp, int Dp, int64_t chunk, int *status)
+__global__ void __launch_bounds__(32 * (kWgWarps + 1), 1) k_spike_wgrad(const __grid_constant__ CUtensorMap tdi,
+                                                                       const __grid_constant__ CUtensorMap tmk,
+                                                                       const float *__restrict__ X,
+                                                                       float *__restrict__ Pw, float *__restrict__ Pb,
+                                                                       int64_t R, int Din, int Dout, int NWp, int Dp,
+                                                                       int64_t chunk, int *status)
 {
     constexpr int JS = 32 * JJ;
     extern __shared__ __align__(128) unsigned char wg_raw[];
-    float *s_d = reinterpret_cast<float *>(wg_raw);                                 // [2][32][JS]
-    uint32_t *s_m = reinterpret_cast<uint32_t *>(wg_raw + (size_t)2 * 32 * JS * 4);  // [2][32][NWp]
-    __shared__ uint64_t bar[2];
+    float *s_d = reinterpret_cast<float *>(wg_raw);                                         // [stages][32][JS]
+    uint32_t *s_m = reinterpret_cast<uint32_t *>(wg_raw + (size_t)kWgStages * 32 * JS * 4);  // [stages][32][NWp]
+    __shared__ uint64_t full[kWgStages], empty[kWgStages];
     __shared__ int s_err;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int js = blockIdx.y;
     const int64_t ck = blockIdx.z;
-    const int c0 = (blockIdx.x * kWgWarps + w) * kWgCols;
     const int64_t r0 = ck * chunk;
     const int64_t rend = R < r0 + chunk ? R : r0 + chunk;
     const int nblk = (int)((rend - r0 + 31) / 32);
-    const uint32_t bytes = (uint32_t)(32 * JS * 4 + 32 * NWp * 4);
-    const int NW = (Din + 31) >> 5;
-    const bool has_cols = c0 < Din;
     const bool do_bias = Pb && blockIdx.x == 0;
 
     if (threadIdx.x == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        for (int i = 0; i < kWgStages; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kWgWarps);
+        }
         fence_barrier_init();
         s_err = 0;
     }
     __syncthreads();
-    int last[2] = {-1, -1};  // (thread 0) the last block issued into each buffer
-    if (threadIdx.x == 0) {
-        for (int b = 0; b < 2 && b < nblk; b++) {
-            mbar_arrive_expect_tx(&bar[b], bytes);
-            tma_load_2d(s_d + b * 32 * JS, &tdi, js * JS, (int)(r0 + 32 * b), &bar[b]);
-            tma_load_2d(s_m + b * 32 * NWp, &tmk, 0, (int)(r0 + 32 * b), &bar[b]);
-            last[b] = b;
+
+    if (w == kWgWarps) {
+        // producer warp: one lane streams the dI and mask tiles of the chunk's
+        // blocks, refilling a stage once every consumer warp has released it
+        if (lane == 0) {
+            const uint32_t bytes = (uint32_t)(32 * JS * 4 + 32 * NWp * 4);
+            int last[kWgStages];
+            for (int i = 0; i < kWgStages; i++) last[i] = -1;
+            for (int b = 0; b < nblk && !s_err; b++) {
+                const int st = b % kWgStages;
+                if (b >= kWgStages && !mbar_wait(&empty[st], (uint32_t)((b / kWgStages - 1) & 1))) {
+                    atomicExch(&s_err, 1);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[st], bytes);
+                tma_load_2d(s_d + st * 32 * JS, &tdi, js * JS, (int)(r0 + 32 * b), &full[st]);
+                tma_load_2d(s_m + st * 32 * NWp, &tmk, 0, (int)(r0 + 32 * b), &full[st]);
+                last[st] = b;
+            }
+            if (s_err) {  // let copies in flight land before the CTA's shared memory goes away
+                for (int i = 0; i < kWgStages; i++)
+                    if (last[i] >= 0) mbar_wait(&full[i], (uint32_t)((last[i] / kWgStages) & 1));
+                if (status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
+            }
         }
+        __syncthreads();  // the consumers' closing barrier
+        return;
     }
+
+    const int c0 = (blockIdx.x * kWgWarps + w) * kWgCols;
+    const int NW = (Din + 31) >> 5;
+    const bool has_cols = c0 < Din;
     float acc[kWgCols][JJ];
     float accb[JJ];
 #pragma unroll
@@ -511,10 +543,14 @@ __global__ void __launch_bounds__(32 * kWgWarps, 1) k_spike_wgrad(const __grid_c
     for (int e = 0; e < JJ; e++) accb[e] = 0.0f;
 
     for (int b = 0; b < nblk; b++) {
-        const int buf = b & 1;
-        if (!s_err && !mbar_wait(&bar[buf], (uint32_t)((b >> 1) & 1)) && lane == 0) atomicExch(&s_err, 1);
-        const float *dt = s_d + buf * 32 * JS;
-        const uint32_t *mt = s_m + buf * 32 * NWp;
+        const int st = b % kWgStages;
+        if (s_err) break;
+        if (!mbar_wait(&full[st], (uint32_t)((b / kWgStages) & 1))) {
+            if (lane == 0) atomicExch(&s_err, 1);
+            break;
+        }
+        const float *dt = s_d + st * 32 * JS;
+        const uint32_t *mt = s_m + st * 32 * NWp;
         if (has_cols) {
             uint32_t wd = (mt[lane * NWp + (c0 >> 5)] >> (c0 & 31)) & ((1u << kWgCols) - 1u);
             if (Din - c0 < kWgCols) wd &= (1u << (Din - c0)) - 1u;  // bits past Din are not inputs
@@ -567,38 +603,30 @@ __global__ void __launch_bounds__(32 * kWgWarps, 1) k_spike_wgrad(const __grid_c
                 for (int e = 0; e < JJ; e++) accb[e] = __fadd_rn(accb[e], d[e]);
             }
         }
-        __syncthreads();
-        if (threadIdx.x == 0 && b + 2 < nblk && !s_err) {
-            mbar_arrive_expect_tx(&bar[buf], bytes);
-            tma_load_2d(s_d + buf * 32 * JS, &tdi, js * JS, (int)(r0 + 32 * (b + 2)), &bar[buf]);
-            tma_load_2d(s_m + buf * 32 * NWp, &tmk, 0, (int)(r0 + 32 * (b + 2)), &bar[buf]);
-            last[buf] = b + 2;
-        }
-    }
-    if (threadIdx.x == 0 && s_err) {
-        for (int i = 0; i < 2; i++)
-            if (last[i] >= 0) mbar_wait(&bar[i], (uint32_t)((last[i] >> 1) & 1));
-        if (status) atomicCAS(status, 0, (int)kStatusTmaWaitTimeout);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
     }
     if (has_cols) {
 #pragma unroll
         for (int e = 0; e < JJ; e++) {
             const int j = js * JS + wg_out<JJ>(lane, e);
+            if (j >= Dout) continue;
             float4 *o = reinterpret_cast<float4 *>(Pw + ((size_t)ck * Dout + j) * Dp + c0);
 #pragma unroll
             for (int q = 0; q < kWgCols; q += 4)
                 o[q / 4] = make_float4(acc[q][e], acc[q + 1][e], acc[q + 2][e], acc[q + 3][e]);
         }
     }
+    __syncthreads();  // every consumer is past its last stage (the producer warp joins here)
     if (do_bias) {  // the warps' bias sums, added in warp order: one partial per chunk
-        float *s_b = s_d;  // the dI tiles are no longer read
+        float *s_b = s_d;  // the tiles are no longer read
 #pragma unroll
         for (int e = 0; e < JJ; e++) s_b[w * JS + wg_out<JJ>(lane, e)] = accb[e];
-        __syncthreads();
-        for (int j = threadIdx.x; j < JS; j += blockDim.x) {
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * kWgWarps) : "memory");  // the consumer warps only
+        for (int j = threadIdx.x; j < JS; j += 32 * kWgWarps) {
             float acc = 0.0f;
             for (int v = 0; v < kWgWarps; v++) acc = __fadd_rn(acc, s_b[v * JS + j]);
-            Pb[(size_t)ck * Dout + js * JS + j] = acc;
+            if (js * JS + j < Dout) Pb[(size_t)ck * Dout + js * JS + j] = acc;
         }
     }
 }
@@ -642,7 +670,7 @@ size_t spike_wgrad_workspace_bytes(int64_t R, int64_t Din, int64_t Dout)
 bool spike_wgrad(const float *dI, const float *X, const uint32_t *Xm, float *gW, float *gb, int64_t R, int64_t Din,
                  int64_t Dout, void *ws, size_t ws_bytes, cudaStream_t s)
 {
-    if (Din <= 0 || Din > 1024 || Dout <= 0 || Dout % 32 || R >= INT32_MAX) return false;
+    if (Din <= 0 || Din > 1024 || Dout <= 0 || Dout % 4 || R >= INT32_MAX) return false;
     if (((uintptr_t)dI & 15) || ((uintptr_t)Xm & 15) || ((uintptr_t)ws & 15)) return false;
     if (!ws || ws_bytes < spike_wgrad_workspace_bytes(R, Din, Dout)) return false;
     const int NWp = (int)spike_mask_stride(Din);
@@ -659,8 +687,8 @@ bool spike_wgrad(const float *dI, const float *X, const uint32_t *Xm, float *gW,
     int *st = device_status_ptr();
     auto go = [&](auto kern) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, 32 * kWgWarps, smem, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)p.Dp, p.chunk,
-                                                st);
+        kern<<<grid, 32 * (kWgWarps + 1), smem, s>>>(tdi, tmk, X, Pw, pb, R, (int)Din, (int)Dout, NWp, (int)p.Dp,
+                                                      p.chunk, st);
     };
     count_launches(2);
     if (p.JJ == 8) go(k_spike_wgrad<8>);
@@ -751,7 +779,7 @@ extern "C" int lifb_spike_linear_wgrad(const float *dI, const float *X, const ui
                        "lifb_spike_linear_wgrad_workspace_bytes",
                        LIFB_ERR_INVALID_ARGUMENT);
     if (!lifb::spike_wgrad(dI, X, Xmask, gW, gb, R, Din, Dout, workspace, workspace_bytes, (cudaStream_t)stream))
-        return sl_fail("lifb_spike_linear_wgrad: needs Dout a multiple of 32, Din <= 1024 and 16-byte aligned dI, "
+        return sl_fail("lifb_spike_linear_wgrad: needs Dout a multiple of 4, Din <= 1024 and 16-byte aligned dI, "
                        "mask and workspace",
                        LIFB_ERR_UNSUPPORTED);
     return sl_done("lifb_spike_linear_wgrad");

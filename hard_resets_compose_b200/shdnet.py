@@ -19,7 +19,9 @@ of its elements sums the active inputs' weights in the order cuBLAS's fp32
 GEMM does, so the spikes are the same bits as with `producer="linear"`
 (nn.Linear, then lif_tuned).  The backward is lif_tuned's adjoint from V,
 then the weight and bias gradients over the active inputs only
-(lifb_spike_linear_wgrad) and dI W for the input's gradient.
+(lifb_spike_linear_wgrad) and dI W for the input's gradient.  The readout
+Linear then keeps torch's forward and takes the same sparse weight gradient
+from layer 2's spike mask (`spike_input_linear`).
 
 The SHD data loader of the reference (h5py, :12-27) is not part of this
 package; inputs are dense [T, B, 700] spike rasters.
@@ -101,21 +103,62 @@ class SpikeLinearLIF(torch.autograd.Function):
                                C=T if mode == "serial" else L.scan_chunk_bwd(T, N))
         dI = lam.reshape(T * B, dout)
         gx = dI.mm(weight).reshape(T, B, din) if ctx.needs_input_grad[0] else None
-        gw = gb = None
-        want_b = has_bias and ctx.needs_input_grad[3]
-        if ctx.needs_input_grad[2] or want_b:
-            lib = _lib.load()
-            gw = torch.empty(dout, din, device=x.device)
-            gb = torch.empty(dout, device=x.device) if want_b else None
-            ws = torch.empty(max(lib.lifb_spike_linear_wgrad_workspace_bytes(T * B, din, dout), 1),
-                             dtype=torch.uint8, device=x.device)
-            with torch.cuda.device(x.device):
-                check(lib.lifb_spike_linear_wgrad(ptr(dI), ptr(x), ptr(xmask), ptr(gw), ptr(gb), T * B, din, dout,
-                                                  ptr(ws), ws.numel(), stream_of(x)), "spike_linear_wgrad")
-            if not ctx.needs_input_grad[2]:
-                gw = None
+        gw, gb = _spike_wgrad(dI, x, xmask, ctx.needs_input_grad[2], has_bias and ctx.needs_input_grad[3])
         _lib.poll_device("spike_linear_lif")
         return gx, None, gw, gb, None, None, None, None, None
+
+
+def _spike_wgrad(dI, x, xmask, want_w, want_b):
+    """Weight and bias gradients dI^T x and dI.sum(0) of a Linear layer whose
+    input x [..., Din] has the spike mask xmask, over x's active elements only
+    (lifb_spike_linear_wgrad); (None, None) parts that are not wanted."""
+    if not (want_w or want_b):
+        return None, None
+    R, dout = dI.shape
+    din = x.shape[-1]
+    lib = _lib.load()
+    gw = torch.empty(dout, din, device=x.device)
+    gb = torch.empty(dout, device=x.device) if want_b else None
+    ws = torch.empty(max(lib.lifb_spike_linear_wgrad_workspace_bytes(R, din, dout), 1), dtype=torch.uint8,
+                     device=x.device)
+    with torch.cuda.device(x.device):
+        check(lib.lifb_spike_linear_wgrad(ptr(dI), ptr(x), ptr(xmask), ptr(gw), ptr(gb), R, din, dout, ptr(ws),
+                                          ws.numel(), stream_of(x)), "spike_linear_wgrad")
+    return (gw if want_w else None), gb
+
+
+class SpikeInputLinear(torch.autograd.Function):
+    """torch.nn.Linear on a spike input x [..., Din] with mask xmask: the
+    forward is torch's linear itself (the same bits as nn.Linear); the
+    backward computes dX = dY W as torch does and the weight and bias
+    gradients over x's active elements only (lifb_spike_linear_wgrad)."""
+
+    @staticmethod
+    def forward(ctx, x, xmask, weight, bias):
+        y = nn.functional.linear(x, weight, bias)
+        ctx.save_for_backward(x, xmask, weight)
+        ctx.has_bias = bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, xmask, weight = ctx.saved_tensors
+        g2 = gy.reshape(-1, weight.shape[0]).contiguous()
+        gx = g2.mm(weight).reshape(x.shape) if ctx.needs_input_grad[0] else None
+        gw, gb = _spike_wgrad(g2, x, xmask, ctx.needs_input_grad[2], ctx.has_bias and ctx.needs_input_grad[3])
+        _lib.poll_device("spike_input_linear")
+        return gx, None, gw, gb
+
+
+def spike_input_linear(x, weight, bias=None):
+    """nn.functional.linear(x, weight, bias) for a spike input x [..., Din]
+    (Din <= 1024, Dout % 4 == 0), with the sparse weight gradient; x's carried
+    spike mask is used when it has one."""
+    x = x.contiguous()
+    m = _carried_mask(x)
+    if m is None:
+        m = spike_mask(x.reshape(-1, x.shape[-1]))
+    return SpikeInputLinear.apply(x, m, weight, bias)
 
 
 def spike_linear_lif(x, weight, bias, beta, theta=1.0, u_r=0.0, alpha=4.0, mode="scan"):
@@ -206,7 +249,11 @@ class Net(nn.Module):
     def forward(self, x):
         s1 = self.l1(x)
         s2 = self.l2(s1)
-        z = self.out(s2)  # [T, B, n_out]
+        if (self.l2.producer == "spike" and s2.is_cuda and self.out.in_features <= 1024
+                and self.out.out_features % 4 == 0):
+            z = spike_input_linear(s2, self.out.weight, self.out.bias)  # nn.Linear's bits, sparse dW
+        else:
+            z = self.out(s2)  # [T, B, n_out]
         if self.readout == "mean":
             return z.mean(0) * 10, (s1, s2)
         Tn, B, C = z.shape

@@ -424,7 +424,7 @@ int lifb_spike_linear_lif_fwd(const float *X, const uint32_t *Xmask, const float
 
 /* Weight and bias gradients of a Linear layer on a spike input: gW [Dout, Din]
  * = dI^T X and gb [Dout] = sum over rows of dI (gb NULL: skipped), from dI
- * [R, Dout] and the input X [R, Din] with its spike mask; only the active
+ * [R, Dout] (Dout % 4 == 0) and the input X [R, Din] with its spike mask; only the active
  * (row, input) pairs are visited.  The sums run over rows in a fixed order
  * (2048-row chunks, then the chunks in order), so the result is deterministic;
  * it differs from a GEMM's by rounding only.  Workspace:

@@ -142,7 +142,8 @@ def test_fused_forward_odd_values_and_nonfinite_weights(cuda):
 
 
 @pytest.mark.parametrize("R,din,dout,rate", ((65536, 700, 256, 0.0225), (4100, 256, 256, 0.1), (2049, 37, 64, 0.3),
-                                            (31, 1024, 32, 0.05), (5000, 100, 96, 0.0)))
+                                            (31, 1024, 32, 0.05), (5000, 100, 96, 0.0), (65536, 256, 20, 0.12),
+                                            (700, 50, 4, 0.2)))
 def test_wgrad_matches_torch(cuda, R, din, dout, rate):
     """gW = dI^T X and gb = dI.sum(0) over the active inputs only, within 1e-5
     of torch's fp32 GEMM and sum; bit-identical from run to run."""
@@ -203,3 +204,23 @@ def test_layer_gradients_and_mask_chain(cuda):
         s1.mul_(1.0)
     assert shdnet._carried_mask(s1) is None
     assert not math.isnan(float(s2.sum()))
+
+
+def test_spike_input_linear_readout(cuda):
+    """The readout on a spike input: output bit-equal to nn.functional.linear,
+    the gradients of x, W and b within 1e-5 of torch's, with and without a
+    carried mask."""
+    from hard_resets_compose_b200 import shdnet
+    T, B, din, dout = 256, 16, 256, 20
+    torch.manual_seed(4)
+    fc = nn.Linear(din, dout).to(cuda)
+    x = raster((T, B, din), 0.15, cuda, seed=11).requires_grad_(True)
+    g = torch.randn(T, B, dout, device=cuda)
+    y = shdnet.spike_input_linear(x, fc.weight, fc.bias)
+    grads = torch.autograd.grad(y, (x, fc.weight, fc.bias), g)
+    x2 = x.detach().clone().requires_grad_(True)
+    y2 = nn.functional.linear(x2, fc.weight, fc.bias)
+    rgrads = torch.autograd.grad(y2, (x2, fc.weight, fc.bias), g)
+    assert torch.equal(y.detach(), y2.detach())
+    for a, r in zip(grads, rgrads):
+        assert rel(a.cpu().numpy(), r.cpu().numpy()) < 1e-5
