@@ -205,13 +205,29 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
             last[k] = k;
         }
     }
-    // the weight slice, transposed: Ws[(c * 32 + l) * JW + e] = W[j0 + e * 32 + l, c]
+    // the weight slice, transposed: Ws[(c * 32 + l) * JW + e] = W[j0 + e * 32 + l, c]; a lane
+    // reads 16 contiguous bytes of one output's row (whole rows aligned to 16 bytes), else 4
+    if (Din % 4 == 0 && ((uintptr_t)W & 15) == 0) {
+        const int nq = Din / 4;
+#pragma unroll 4
+        for (int e = threadIdx.x; e < OG * nq; e += blockDim.x) {
+            const int o = e % OG, q = e / OG;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(W + (int64_t)(j0 + o) * Din) + q);
+            float *wd = Ws + ((size_t)(4 * q) * 32 + (o & 31)) * JW + (o >> 5);
+            wd[0] = v.x;
+            wd[32 * JW] = v.y;
+            wd[64 * JW] = v.z;
+            wd[96 * JW] = v.w;
+            if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) s_bad[o] = 1;
+        }
+    } else {
 #pragma unroll 8
-    for (int64_t e = threadIdx.x; e < (int64_t)Din * OG; e += blockDim.x) {
-        const int o = (int)(e % OG), c = (int)(e / OG);
-        const float wv = __ldg(W + (int64_t)(j0 + o) * Din + c);
-        Ws[((size_t)c * 32 + (o & 31)) * JW + (o >> 5)] = wv;
-        if (!isfinite(wv)) s_bad[o] = 1;
+        for (int64_t e = threadIdx.x; e < (int64_t)Din * OG; e += blockDim.x) {
+            const int o = (int)(e % OG), c = (int)(e / OG);
+            const float wv = __ldg(W + (int64_t)(j0 + o) * Din + c);
+            Ws[((size_t)c * 32 + (o & 31)) * JW + (o >> 5)] = wv;
+            if (!isfinite(wv)) s_bad[o] = 1;
+        }
     }
     __syncthreads();
     float bj[JW];
@@ -311,7 +327,7 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
             const int64_t t0 = (k - 1) * kSLTile;
             const float *cur = It + ((size_t)((k - 1) & 1) * bpc + w) * kSLTile * OG;
             const int rows = (int)(T - t0 < kSLTile ? T - t0 : kSLTile);
-            for (int r = 0; r < rows; r++) {
+            auto step_row = [&](int r) {
                 const int64_t row = (t0 + r) * B + b0 + w;
                 float *vo = V + row * Dout + j0;
                 float *so = S + row * Dout + j0;
@@ -333,6 +349,12 @@ __global__ void __launch_bounds__(32 * kSLWarps, 1) k_spike_linear_lif(
                     if (lane < JW) mo[jg * JW + lane] = mine;
                     if (jg == 0 && NWo + lane < NWop) mo[NWo + lane] = 0u;  // spikes are 0/1: not odd
                 }
+            };
+            if (rows == kSLTile) {  // unrolled: the tile's I loads go ahead of the chain through u
+#pragma unroll
+                for (int r = 0; r < kSLTile; r++) step_row(r);
+            } else {
+                for (int r = 0; r < rows; r++) step_row(r);
             }
         }
         if (k < ntiles) {  // form tile k: every warp takes rows from a shared counter until none are left
