@@ -70,7 +70,7 @@ def _linear_then_lif(x, fc, beta):
 
 @pytest.mark.parametrize("T,B,din,dout,rate,scale", ((64, 5, 700, 256, 0.03, 6.0), (33, 7, 37, 64, 0.2, 2.0),
                                                    (50, 3, 1024, 96, 0.02, 8.0), (17, 2, 256, 32, 0.3, 1.5),
-                                                   (40, 6, 256, 256, 0.1, 3.0)))
+                                                   (40, 6, 256, 256, 0.1, 3.0), (35, 73, 700, 256, 0.03, 6.0)))
 def test_fused_forward_v_s_and_mask(cuda, T, B, din, dout, rate, scale):
     """V and S equal the LIF over I summed in input order (the sequential
     GEMM order), bit for bit, and so over cuBLAS's I for the network's layer
@@ -224,3 +224,29 @@ def test_spike_input_linear_readout(cuda):
     assert torch.equal(y.detach(), y2.detach())
     for a, r in zip(grads, rgrads):
         assert rel(a.cpu().numpy(), r.cpu().numpy()) < 1e-5
+
+
+def test_spike_kernels_empty_and_errors(cuda):
+    """Empty T or B is a no-op; a bad shape is refused with a status, not run."""
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200._lib import ptr, stream_of
+    lib = _lib.load()
+    x = torch.zeros(4, 3, 64, device=cuda)
+    m = torch.zeros(12, lib.lifb_spike_mask_stride(64), dtype=torch.int32, device=cuda)
+    W = torch.zeros(32, 64, device=cuda)
+    V = torch.zeros(4, 3 * 32, device=cuda)
+    S = torch.zeros_like(V)
+    s = stream_of(x)
+    assert lib.lifb_spike_linear_lif_fwd(ptr(x), ptr(m), ptr(W), None, None, ptr(V), ptr(S), None, 0, 3, 64, 32,
+                                         0.9, 1.0, 0.0, s) == 0
+    assert lib.lifb_spike_linear_lif_fwd(ptr(x), ptr(m), ptr(W), None, None, ptr(V), ptr(S), None, 4, 0, 64, 32,
+                                         0.9, 1.0, 0.0, s) == 0
+    assert lib.lifb_spike_mask(ptr(x), ptr(m), 0, 64, s) == 0
+    # Dout not a multiple of 32: unsupported (the caller runs the unfused layer)
+    assert lib.lifb_spike_linear_lif_fwd(ptr(x), ptr(m), ptr(W), None, None, ptr(V), ptr(S), None, 4, 3, 64, 20,
+                                         0.9, 1.0, 0.0, s) == 4
+    # Din past 1024: unsupported mask
+    assert lib.lifb_spike_mask(ptr(x), ptr(m), 12, 2000, s) == 4
+    # null pointers: invalid argument
+    assert lib.lifb_spike_linear_wgrad(None, ptr(x), ptr(m), ptr(W), None, 12, 64, 32, None, 0, s) == 1
+    torch.cuda.synchronize()
