@@ -86,10 +86,17 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
         fence_barrier_init();
     }
     __syncwarp();
+    // V path: the adjoint reads V next, so V's lines are kept in L2 ahead of I's and S's, which nothing
+    // in the layer reads again
+    const uint64_t pol_first = VOUT ? l2_evict_first() : 0, pol_last = VOUT ? l2_evict_last() : 0;
+    auto load_i = [&](int s, int64_t k) {
+        if constexpr (VOUT) tma_load_2d_hint(ring + s * kTile, &tI, (int)n0, (int)tile_row(k), &full[s], pol_first);
+        else tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)tile_row(k), &full[s]);
+    };
     if (lane == 0) {
         for (int s = 0; s < S && s < ntot; s++) {
             mbar_arrive_expect_tx(&full[s], kStageBytes);
-            tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)tile_row(s), &full[s]);
+            load_i(s, s);
         }
     }
     const int64_t nl = n0 + NPL * lane;
@@ -129,7 +136,7 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
         __syncwarp();
         if (lane == 0 && k + S < ntot) {
             mbar_arrive_expect_tx(&full[s], kStageBytes);
-            tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)tile_row(k + S), &full[s]);
+            load_i(s, k + S);
         }
     }
     if (leading && ok && LeadStarts && act) st_vec<NPL>(LeadStarts + m * N + nl, u);
@@ -165,12 +172,17 @@ __global__ void __launch_bounds__(32) k_fwd_tma(const __grid_constant__ CUtensor
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) {
-            tma_store_2d(&tU, (int)n0, (int)(row0 + kk * R), ou);
-            tma_store_2d(&tS, (int)n0, (int)(row0 + kk * R), os);
+            if constexpr (VOUT) {
+                tma_store_2d_hint(&tU, (int)n0, (int)(row0 + kk * R), ou, pol_last);
+                tma_store_2d_hint(&tS, (int)n0, (int)(row0 + kk * R), os, pol_first);
+            } else {
+                tma_store_2d(&tU, (int)n0, (int)(row0 + kk * R), ou);
+                tma_store_2d(&tS, (int)n0, (int)(row0 + kk * R), os);
+            }
             bulk_commit();
             if (k + S < ntot) {
                 mbar_arrive_expect_tx(&full[s], kStageBytes);
-                tma_load_2d(ring + s * kTile, &tI, (int)n0, (int)tile_row(k + S), &full[s]);
+                load_i(s, k + S);
             }
         }
     }
@@ -344,10 +356,18 @@ __global__ void __launch_bounds__(32) k_bwd_tma(const __grid_constant__ CUtensor
     const int rem = (int)(C - nfull * R);
     const int64_t ntiles = nfull + (rem ? 1 : 0);
 
+    const uint64_t pol_first = FROM_V ? l2_evict_first() : 0;  // V and GS are read once
     auto issue = [&](int s, int64_t k) {
         const int row = (int)(cend - (k + 1) * R);  // may be negative: zero-filled
         float *b = ring + (size_t)s * NT * kTile;
         mbar_arrive_expect_tx(&full[s], kStageBytes);
+        if constexpr (FROM_V) {
+            tma_load_2d_hint(b + Ly::kI * kTile, &tI, (int)n0, row, &full[s], pol_first);
+            if (READ_S) tma_load_2d_hint(b + Ly::kS * kTile, &tS, (int)n0, row, &full[s], pol_first);
+            tma_load_2d_hint(b + Ly::kGS * kTile, &tGS, (int)n0, row, &full[s], pol_first);
+            if (HAS_GU) tma_load_2d_hint(b + Ly::kGU * kTile, &tGU, (int)n0, row, &full[s], pol_first);
+            return;
+        }
         tma_load_2d(b + Ly::kI * kTile, &tI, (int)n0, row, &full[s]);
         if (!FROM_V) tma_load_2d(b + Ly::kU * kTile, &tU, (int)n0, row - 1, &full[s]);
         if (READ_S) tma_load_2d(b + Ly::kS * kTile, &tS, (int)n0, row, &full[s]);

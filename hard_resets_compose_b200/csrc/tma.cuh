@@ -99,6 +99,41 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+// L2 eviction-priority policies for the cache-hinted copies below.
+__device__ __forceinline__ uint64_t l2_evict_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// tma_load_2d with an L2 eviction-priority hint (no multicast).
+__device__ __forceinline__ void tma_load_2d_hint(void *smem_dst, const CUtensorMap *map, int c0, int c1,
+                                                 uint64_t *bar, uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+        "[%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// tma_store_2d with an L2 eviction-priority hint.
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap *map, int c0, int c1, const void *smem_src,
+                                                  uint64_t policy)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
+                     (uint64_t)map),
+                 "r"(c0), "r"(c1), "r"(smem_u32(smem_src)), "l"(policy)
+                 : "memory");
+}
+
 // 2-D tiled TMA store of a shared-memory box to global memory (bulk-group
 // completion).  Out-of-range parts of the box are clipped by the hardware.
 // The writing threads must execute fence_proxy_async_shared() first.
