@@ -1179,7 +1179,22 @@ def c4_time_sharded(args, ws, rank, dev, lib):
     du0_rel = all_max(du0_rel)
     ok = ok and dI_rel <= 1e-5 and du0_rel <= 1e-5
     parity = all_max(0.0 if ok else 1.0) == 0.0
-    del Us, Ss, Lam, U1s, S1s, dI1
+    del Us, Ss, Lam
+    # entry mode "maps" (slice maps all-gathered, the survey's design): the same bits, and its time
+    Um, Sm_, _ = tshard.tshard_forward(Is, u0, ops, comm, entry_mode="maps")
+    maps_ok = all_max(0.0 if (torch.equal(Um.view(torch.int32), U1s.view(torch.int32)) and
+                              torch.equal(Sm_.view(torch.int32), S1s.view(torch.int32))) else 1.0) == 0.0
+    del Um, Sm_, U1s, S1s, dI1
+    Iqm = Is.clone().requires_grad_(True)
+
+    def step_maps():
+        Iqm.grad = None
+        S_ = tshard.lif_tshard(Iqm, u0, beta=BETA, ops=ops, comm=comm, entry_mode="maps")
+        torch.autograd.backward(S_, GSs)
+    for _ in range(2):
+        step_maps()
+    ms_maps = all_max(event_ms(step_maps, 5))
+    del Iqm
 
     Iqs = Is.clone().requires_grad_(True)
 
@@ -1212,6 +1227,9 @@ def c4_time_sharded(args, ws, rank, dev, lib):
         "parity": {"U_S_bit_exact": ok, "dI_rel": dI_rel, "du0_rel": du0_rel,
                    "repair_rounds": info.get("repair_rounds")},
         "phases_ms_max_over_ranks": per_phase,
+        "entry_mode_maps": {"ms_per_step": ms_maps, "strong_scaling_efficiency": ms1 / (ws * ms_maps),
+                            "U_S_bit_exact": maps_ok,
+                            "note": "slice envelopes and slice maps all-gathered, entry from the maps"},
         "note": "every rank holds the whole sequence for the check; the timed step moves only its slice"}
 
 
