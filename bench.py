@@ -1180,7 +1180,7 @@ def c4_time_sharded(args, ws, rank, dev, lib):
     ok = ok and dI_rel <= 1e-5 and du0_rel <= 1e-5
     parity = all_max(0.0 if ok else 1.0) == 0.0
     del Us, Ss, Lam
-    # entry mode "maps" (slice maps all-gathered, the survey's design): the same bits, and its time
+    # entry mode "maps" (slice envelopes and slice maps all-gathered): the same bits, and its time
     Um, Sm_, _ = tshard.tshard_forward(Is, u0, ops, comm, entry_mode="maps")
     maps_ok = all_max(0.0 if (torch.equal(Um.view(torch.int32), U1s.view(torch.int32)) and
                               torch.equal(Sm_.view(torch.int32), S1s.view(torch.int32))) else 1.0) == 0.0
