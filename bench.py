@@ -16,6 +16,13 @@ Multi-GPU: one process per GPU (torchrun); every rank owns its own batch
 shard of 16384 neurons (weak scaling, no data-path collective); the step time
 is the max over ranks; value = all ranks' neuron-steps / that time.
 
+The default line also carries `c3` (config 3's network training step with
+spike-input layers, the nn.Linear + lif_tuned step beside it and their spikes
+compared bit for bit; data parallel under torchrun; --no-c3 skips it) and,
+under torchrun, `tshard_parity` and `c4_tshard` (config 4 time-sharded over
+the ranks, checked against single-GPU lif_tuned, with per-phase maxima and
+the "maps" entry mode beside; --no-tshard skips them).
+
 --impl reference times the reference's CPU path for the same workload: the
 CPU oracle (oracle/, a C restatement of lifscan/fast.py's serial forward and
 adjoint) on all host threads.  Under torchrun only rank 0 runs it.
