@@ -103,6 +103,8 @@ SIGNATURES = {
     "lifb_alif_bwd_scan": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float, c_float, c_float, c_float, c_float,
                             c_i64, c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_leaky_fwd": ([c_void_p, c_void_p, c_i64, c_i64, c_float, c_void_p], c_int),
+    "lifb_leaky_bwd": ([c_void_p, c_void_p, c_i64, c_i64, c_float, c_void_p], c_int),
     "lifb_spike_mask_stride": ([c_i64], c_i64),
     "lifb_spike_mask": ([c_void_p, c_void_p, c_i64, c_i64, c_void_p], c_int),
     "lifb_spike_linear_lif_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -7,9 +7,9 @@ over time and scaled by 10; LIF weights drawn from U(+-1.5/sqrt(din))
 (:34); default beta 0.95 (:54).  Options reproduce the benchmark network
 described for config 3 instead: `init="kaiming"` (PyTorch's default
 Kaiming-uniform Linear init) and `readout="leaky"` (a non-spiking leaky
-integrator y_t = beta*y_{t-1} + W s_t averaged over time), which runs on the
-same kernels: the serial forward with theta = +inf never spikes, and its
-adjoint with the upstream gradient on U is the integrator's backward.
+integrator y_t = beta*y_{t-1} + W s_t averaged over time), a linear
+recurrence run as 64-row chunks with one carried value each
+(lifb_leaky_fwd / lifb_leaky_bwd).
 
 `producer="spike"` runs each LIF layer's Linear and recurrence as one fused
 kernel (lifb_spike_linear_lif_fwd) for spike inputs: the input is read as a
@@ -209,24 +209,43 @@ class LIFLayer(nn.Module):
 
 
 class _LeakyIntegrator(torch.autograd.Function):
-    """y_t = beta*y_{t-1} + z_t, y_0 = 0, over [T, M]: the serial forward with
+    """y_t = beta*y_{t-1} + z_t, y_0 = 0, over [T, M], and its adjoint
+    lam_t = g_t + beta*lam_{t+1}: the chunked linear recurrences of
+    lifb_leaky_fwd / lifb_leaky_bwd (T <= 1024), else the serial forward with
     theta = +inf (no spike can occur) and its adjoint with the upstream
-    gradient on the state (lam_t = g_t + beta*lam_{t+1})."""
+    gradient on the state."""
 
     @staticmethod
     def forward(ctx, z, beta):
         z = z.contiguous()
-        y0 = torch.zeros(z.shape[1], device=z.device)
+        T, M = z.shape
+        lib = _lib.load()
+        ctx.beta = beta
+        if T <= 1024:
+            Y = torch.empty_like(z)
+            with torch.cuda.device(z.device):
+                check(lib.lifb_leaky_fwd(ptr(z), ptr(Y), T, M, float(beta), stream_of(z)), "leaky integrator")
+            ctx.chunked = True
+            return Y
+        y0 = torch.zeros(M, device=z.device)
         Y, _ = L.serial_forward(z, beta, math.inf, 0.0, y0)
         ctx.save_for_backward(z, y0, Y)
-        ctx.beta = beta
+        ctx.chunked = False
         return Y
 
     @staticmethod
     def backward(ctx, gY):
+        gY = gY.contiguous()
+        if ctx.chunked:
+            T, M = gY.shape
+            lam = torch.empty_like(gY)
+            with torch.cuda.device(gY.device):
+                check(_lib.load().lifb_leaky_bwd(ptr(gY), ptr(lam), T, M, float(ctx.beta), stream_of(gY)),
+                      "leaky integrator adjoint")
+            return lam, None
         z, y0, Y = ctx.saved_tensors
         zeros = torch.zeros_like(Y)  # no gradient reaches the (absent) spikes
-        lam = L.serial_backward(z, y0, Y, None, zeros, gY.contiguous(), ctx.beta, math.inf, 0.0, 4.0, True)
+        lam = L.serial_backward(z, y0, Y, None, zeros, gY, ctx.beta, math.inf, 0.0, 4.0, True)
         return lam, None
 
 

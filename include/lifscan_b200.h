@@ -436,6 +436,17 @@ int lifb_spike_linear_wgrad(const float *dI, const float *X, const uint32_t *Xma
                             float *gb, int64_t R, int64_t Din, int64_t Dout, void *workspace,
                             size_t workspace_bytes, void *stream);
 
+/* Leaky (non-spiking) integrator over time, [T, M] row-major fp32: _fwd
+ * writes Y with y_t = beta * y_{t-1} + z_t (y_{-1} = 0); _bwd writes
+ * GZ = the adjoint lam_t = gy_t + beta * lam_{t+1} (lam_T = 0).  Time is split
+ * into 64-row chunks with one carried value between them, so the result equals
+ * the sequential recurrence up to fp32 rounding.  Needs T <= 1024
+ * (LIFB_ERR_UNSUPPORTED otherwise).  The leaky readout of the network in
+ * config 3 (a deviation from lifscan/shdnet.py:66's mean readout that the
+ * benchmark configuration names). */
+int lifb_leaky_fwd(const float *Z, float *Y, int64_t T, int64_t M, float beta, void *stream);
+int lifb_leaky_bwd(const float *GY, float *GZ, int64_t T, int64_t M, float beta, void *stream);
+
 /* Time-sharded forward, the two halves of a slice's replay around the hand-over
  * of its end state (workspace: lifb_scan_fwd_spec_workspace_bytes(T, N, L)).
  * _tail replays segments 1..T/L-1 of the slice at once, each from a W-row

@@ -145,3 +145,36 @@ def test_network_c3_spike_producer(cuda, readout, init, beta):
     assert rel(logits.detach().cpu().numpy(), rlogits.detach().cpu().numpy()) < 1e-6
     for g, rg in zip(grads, rgrads):
         assert rel(g.cpu().numpy(), rg.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("T,M,beta", ((1024, 1280, 0.9), (1000, 33, 0.99), (17, 5, 0.5), (64, 32, 0.95)))
+def test_leaky_integrator_matches_sequential(cuda, T, M, beta):
+    """The chunked leaky integrator (lifb_leaky_fwd / lifb_leaky_bwd) against
+    the sequential recurrences in fp64: y_t = beta*y_{t-1} + z_t and
+    lam_t = g_t + beta*lam_{t+1}, within 1e-6 relative."""
+    from hard_resets_compose_b200 import _lib
+    from hard_resets_compose_b200._lib import check, ptr, stream_of
+    lib = _lib.load()
+    g = torch.Generator(device="cpu").manual_seed(T + M)
+    z = torch.randn(T, M, generator=g).to(cuda)
+    gy = torch.randn(T, M, generator=g).to(cuda)
+    Y = torch.empty_like(z)
+    lam = torch.empty_like(z)
+    check(lib.lifb_leaky_fwd(ptr(z), ptr(Y), T, M, beta, stream_of(z)), "leaky fwd")
+    check(lib.lifb_leaky_bwd(ptr(gy), ptr(lam), T, M, beta, stream_of(z)), "leaky bwd")
+    torch.cuda.synchronize()
+    zd, gd = z.double().cpu(), gy.double().cpu()
+    yr = torch.zeros(T, M, dtype=torch.float64)
+    lr = torch.zeros(T, M, dtype=torch.float64)
+    y = torch.zeros(M, dtype=torch.float64)
+    for t in range(T):
+        y = beta * y + zd[t]
+        yr[t] = y
+    l = torch.zeros(M, dtype=torch.float64)
+    for t in range(T - 1, -1, -1):
+        l = gd[t] + beta * l
+        lr[t] = l
+    assert float((Y.cpu().double() - yr).abs().max() / yr.abs().max()) < 1e-6
+    assert float((lam.cpu().double() - lr).abs().max() / lr.abs().max()) < 1e-6
+    # past the one-launch form: refused, so the layer takes the serial path
+    assert lib.lifb_leaky_fwd(ptr(z), ptr(Y), 1025, 1, beta, stream_of(z)) == 4
