@@ -156,8 +156,6 @@ __device__ __forceinline__ void bulk_wait_read()
 // Wait until all committed bulk groups have completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Approximate reciprocal (hardware MUFU, ~1 ulp); used where the result
-// enters a gradient checked to 1e-5 relative.
 // 2^x (PTX ex2.approx, flush-to-zero).
 __device__ __forceinline__ float ex2_approx(float x)
 {
@@ -166,6 +164,8 @@ __device__ __forceinline__ float ex2_approx(float x)
     return r;
 }
 
+// Approximate reciprocal (PTX rcp.approx, flush-to-zero); used where the result
+// enters a gradient checked to 1e-5 relative.
 __device__ __forceinline__ float rcp_approx(float x)
 {
     float r;
