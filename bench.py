@@ -1612,7 +1612,7 @@ def main():
     }
 
     # end to end through the public API with host buffers: lif_tuned_host
-    # (C-ABI lifb_lif_fwd_bwd_host) takes pinned host I, GS, u0 and returns
+    # (C-ABI lifb_lif_fwd_bwd_host_rows) takes pinned host I, GS, u0 and returns
     # host S, dI, du0; its H2D copies, kernels and D2H copies are all inside
     # the timed region.  The unpipelined eager equivalent is reported beside.
     e2e = None
@@ -1677,7 +1677,8 @@ def main():
         del dbuf
         e2e = {"value": units / (ms_e2e_host / 1e3), "unit": UNIT, "ms_per_step": ms_e2e_host,
                "h2d_bytes_per_step": 2 * N * T * 4 + N * 4, "d2h_bytes_per_step": 2 * N * T * 4 + N * 4,
-               "api": "lif_tuned_host (C-ABI lifb_lif_fwd_bwd_host): pinned host I, GS, u0 in; host S, dI, du0 out",
+               "api": "lif_tuned_host (C-ABI lifb_lif_fwd_bwd_host_rows, blocks of time rows): pinned host I, GS, "
+                      "u0 in; host S, dI, du0 out",
                "copy_floor_ms": ms_floor, "copy_floor_serial_ms": ms_floor_serial,
                "copy_floor_note": "the step's H2D (I, GS) and D2H (S, dI) bytes alone between the same pinned host "
                                   "buffers and the device, every rank at once; concurrent: H2D and D2H on two "

@@ -438,4 +438,36 @@ int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float
     return check_launch("lifb_lif_fwd_bwd_host");
 }
 
+int64_t lifb_lif_fwd_bwd_host_rows_block(int64_t T, int64_t N)
+{
+    return lifb::host_pipe_rows_default_block(T, N);
+}
+
+size_t lifb_lif_fwd_bwd_host_rows_workspace_bytes(int64_t T, int64_t N, int64_t block_t)
+{
+    return lifb::host_pipe_rows_workspace_bytes(T, N, block_t);
+}
+
+int lifb_lif_fwd_bwd_host_rows(const float *I_host, const float *GS_host, const float *u0_host, float *S_host,
+                               float *dI_host, float *du0_host, int64_t T, int64_t N, float beta, float theta,
+                               float u_r, float alpha, int64_t block_t, void *workspace, size_t workspace_bytes,
+                               void *stream)
+{
+    LIFB_RANGE("lifb_lif_fwd_bwd_host_rows");
+    if (T < 0 || N < 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "negative shape T=%lld N=%lld", (long long)T, (long long)N);
+    if (T == 0 || N == 0) return LIFB_OK;
+    if (!I_host || !GS_host || !u0_host || !S_host || !dI_host || !du0_host)
+        return fail(LIFB_ERR_INVALID_ARGUMENT, "null host pointer");
+    if (block_t <= 0) return fail(LIFB_ERR_INVALID_ARGUMENT, "block_t=%lld must be positive", (long long)block_t);
+    if (N % 4) return fail(LIFB_ERR_UNSUPPORTED, "lifb_lif_fwd_bwd_host_rows needs N %% 4 == 0 (N=%lld)", (long long)N);
+    int st;
+    size_t need = lifb::host_pipe_rows_workspace_bytes(T, N, block_t);
+    if ((st = check_ws(workspace, workspace_bytes, need))) return st;
+    const char *err = nullptr;
+    st = lifb::host_pipe_run_rows(I_host, GS_host, u0_host, S_host, dI_host, du0_host, T, N, beta, theta, u_r,
+                                  alpha, block_t, workspace, (cudaStream_t)stream, &err);
+    if (st) return fail(st, "lifb_lif_fwd_bwd_host_rows: %s", err ? err : "error");
+    return check_launch("lifb_lif_fwd_bwd_host_rows");
+}
+
 }  // extern "C"

@@ -751,10 +751,10 @@ static void launch_bwd_v(bool read_s, bool has_gu, const CUtensorMap *maps, cons
 // Adjoint from V (the forward's pre-reset potentials), GS: detached reset,
 // S recomputed as [v >= theta], no GU.  Same outputs as bwd_tma mode 0.
 bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, int32_t *D, int64_t T, int64_t N,
-               int64_t C, float beta, float theta, float alpha, cudaStream_t s)
+               int64_t C, float beta, float theta, float alpha, cudaStream_t s, const float *LamEnd)
 {
-    const void *p[] = {V, GS, Lam, P, Q, D};
-    if (!tma_ok(p, 6, N) || C <= 0 || T % C) return false;
+    const void *p[] = {V, GS, Lam, P, Q, D, LamEnd};
+    if (!tma_ok(p, 7, N) || C <= 0 || T % C) return false;
     const int64_t M = T / C;
     if (M > 65535) return false;
     const int npl = pick_npl(N, M, LIFB_BWD_NPL4_MIN_CTAS_PER_SM);
@@ -767,11 +767,11 @@ bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, 
     maps[1] = maps[2] = maps[4] = maps[0];
     int *status = device_status_ptr();
     if (P) {
-        if (npl == 4) launch_bwd<4, false, false, kReplay, true, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
-        else launch_bwd<1, false, false, kReplay, true, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+        if (npl == 4) launch_bwd<4, false, false, kReplay, true, true>(maps, nullptr, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+        else launch_bwd<1, false, false, kReplay, true, true>(maps, nullptr, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
     } else {
-        if (npl == 4) launch_bwd<4, false, false, kReplay, false, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
-        else launch_bwd<1, false, false, kReplay, false, true>(maps, nullptr, nullptr, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+        if (npl == 4) launch_bwd<4, false, false, kReplay, false, true>(maps, nullptr, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
+        else launch_bwd<1, false, false, kReplay, false, true>(maps, nullptr, LamEnd, Lam, P, Q, D, N, M, C, beta, theta, 0.f, alpha, true, status, s);
     }
     return true;
 }

@@ -11,6 +11,18 @@
 // staging slots in the caller's device workspace keep both PCIe directions
 // busy at once (B200: ~55 GB/s each way alone, ~95 GB/s both ways together),
 // so the call is bound by their joint rate instead of the sum of both.
+//
+// lifb_lif_fwd_bwd_host_rows: the same over blocks of time rows.  A block of
+// rows of a row-major [T, N] array is one contiguous range of host memory, so
+// every copy is a single linear transfer, and the first output can leave as
+// soon as the first (small) input block has arrived.  The forward runs block
+// after block in time order, each from the state the previous one ended in
+// (the replay kernel's end states); the adjoint runs the blocks in reverse
+// order, each from the lam its successor left in its first row.  V of all
+// rows stays on the device between the two sweeps; I, S, GS and Lam pass
+// through four staging slots.  The input stream copies I in time order, then
+// GS in reverse order; the output stream returns S in time order, then dI in
+// reverse order, each one block behind.
 #include <mutex>
 
 #include "lifb_common.cuh"
@@ -21,12 +33,19 @@ namespace lifb {
 namespace {
 
 constexpr int kMaxDev = 64;
-constexpr int kSlots = 3;
+constexpr int kSlots = 3;     // column blocks
+constexpr int kRowSlots = 4;  // row blocks
+constexpr int kEv = kRowSlots;
+
+// Rows per block of the row form: blocks of about this many bytes per array.
+#ifndef LIFB_HOST_BLOCK_BYTES
+#define LIFB_HOST_BLOCK_BYTES (16 << 20)
+#endif
 
 struct HostPipe {
     cudaStream_t in = nullptr, out = nullptr;
-    cudaEvent_t ev_in[kSlots] = {}, ev_gs[kSlots] = {}, ev_fwd[kSlots] = {}, ev_done[kSlots] = {},
-                ev_free[kSlots] = {}, ev_start = nullptr, ev_last = nullptr;
+    cudaEvent_t ev_in[kEv] = {}, ev_gs[kEv] = {}, ev_fwd[kEv] = {}, ev_done[kEv] = {}, ev_free[kEv] = {},
+                ev_sout[kEv] = {}, ev_start = nullptr, ev_last = nullptr;
     bool ready = false;
 };
 HostPipe g_pipe[kMaxDev];
@@ -37,9 +56,9 @@ void destroy_pipe(HostPipe &q)
 {
     if (q.in) cudaStreamDestroy(q.in);
     if (q.out) cudaStreamDestroy(q.out);
-    cudaEvent_t *sets[] = {q.ev_in, q.ev_gs, q.ev_fwd, q.ev_done, q.ev_free};
+    cudaEvent_t *sets[] = {q.ev_in, q.ev_gs, q.ev_fwd, q.ev_done, q.ev_free, q.ev_sout};
     for (cudaEvent_t *set : sets)
-        for (int i = 0; i < kSlots; i++)
+        for (int i = 0; i < kEv; i++)
             if (set[i]) cudaEventDestroy(set[i]);
     if (q.ev_start) cudaEventDestroy(q.ev_start);
     if (q.ev_last) cudaEventDestroy(q.ev_last);
@@ -59,12 +78,13 @@ HostPipe *pipe_for_current_device()
         HostPipe q;
         bool ok = cudaStreamCreateWithFlags(&q.in, cudaStreamNonBlocking) == cudaSuccess &&
                   cudaStreamCreateWithFlags(&q.out, cudaStreamNonBlocking) == cudaSuccess;
-        for (int i = 0; ok && i < kSlots; i++)
+        for (int i = 0; ok && i < kEv; i++)
             ok = cudaEventCreateWithFlags(&q.ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
                  cudaEventCreateWithFlags(&q.ev_gs[i], cudaEventDisableTiming) == cudaSuccess &&
                  cudaEventCreateWithFlags(&q.ev_fwd[i], cudaEventDisableTiming) == cudaSuccess &&
                  cudaEventCreateWithFlags(&q.ev_done[i], cudaEventDisableTiming) == cudaSuccess &&
-                 cudaEventCreateWithFlags(&q.ev_free[i], cudaEventDisableTiming) == cudaSuccess;
+                 cudaEventCreateWithFlags(&q.ev_free[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&q.ev_sout[i], cudaEventDisableTiming) == cudaSuccess;
         ok = ok && cudaEventCreateWithFlags(&q.ev_last, cudaEventDisableTiming) == cudaSuccess &&
              cudaEventCreateWithFlags(&q.ev_start, cudaEventDisableTiming) == cudaSuccess;
         if (!ok) {
@@ -167,6 +187,128 @@ int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float 
         n0 += nb;
     }
     // the caller's stream completes only after the last output copy
+    cudaEventRecord(p->ev_last, p->out);
+    cudaStreamWaitEvent(cs, p->ev_last, 0);
+    return LIFB_OK;
+}
+
+namespace {
+
+size_t al256(size_t b) { return (b + 255) / 256 * 256; }
+
+// Workspace of the row form: V [T, N], then per slot I, S, GS, Lam blocks
+// [block_t, N], then u0, two end-state buffers and du0 [N].
+struct RowWs {
+    float *V, *I[kRowSlots], *S[kRowSlots], *GS[kRowSlots], *Lam[kRowSlots], *u0, *ust[2], *du0;
+};
+
+size_t row_ws_layout(int64_t T, int64_t N, int64_t bt, void *base, RowWs *w)
+{
+    const size_t full = al256((size_t)T * N * 4), blk = al256((size_t)bt * N * 4), vec = al256((size_t)N * 4);
+    if (w) {
+        char *c = (char *)base;
+        w->V = (float *)c; c += full;
+        for (int j = 0; j < kRowSlots; j++) {
+            w->I[j] = (float *)c; c += blk;
+            w->S[j] = (float *)c; c += blk;
+            w->GS[j] = (float *)c; c += blk;
+            w->Lam[j] = (float *)c; c += blk;
+        }
+        w->u0 = (float *)c; c += vec;
+        w->ust[0] = (float *)c; c += vec;
+        w->ust[1] = (float *)c; c += vec;
+        w->du0 = (float *)c;
+    }
+    return full + (size_t)kRowSlots * 4 * blk + 4 * vec;
+}
+
+}  // namespace
+
+int64_t host_pipe_rows_default_block(int64_t T, int64_t N)
+{
+    if (T <= 0 || N <= 0) return 0;
+    int64_t bt = (int64_t)LIFB_HOST_BLOCK_BYTES / (N * 4);
+    if (bt < 1) bt = 1;
+    return bt < T ? bt : T;
+}
+
+size_t host_pipe_rows_workspace_bytes(int64_t T, int64_t N, int64_t block_t)
+{
+    if (T <= 0 || N <= 0 || block_t <= 0) return 0;
+    return row_ws_layout(T, N, block_t < T ? block_t : T, nullptr, nullptr);
+}
+
+int host_pipe_run_rows(const float *I_h, const float *GS_h, const float *u0_h, float *S_h, float *dI_h,
+                       float *du0_h, int64_t T, int64_t N, float beta, float theta, float u_r, float alpha,
+                       int64_t block_t, void *workspace, cudaStream_t cs, const char **err)
+{
+    if (N % 4) {
+        *err = "the row-block pipeline needs N % 4 == 0";
+        return LIFB_ERR_UNSUPPORTED;
+    }
+    HostPipe *p = pipe_for_current_device();
+    if (!p) {
+        *err = "could not create the copy streams/events of the current device";
+        return LIFB_ERR_CUDA;
+    }
+    const int64_t bt = block_t < T ? block_t : T;
+    const int64_t nblk = (T + bt - 1) / bt;
+    RowWs w;
+    row_ws_layout(T, N, bt, workspace, &w);
+    const size_t row_bytes = (size_t)N * 4;
+    auto rows_of = [&](int64_t k) { return (k + 1) * bt <= T ? bt : T - k * bt; };
+
+    cudaEventRecord(p->ev_start, cs);
+    cudaStreamWaitEvent(p->in, p->ev_start, 0);
+    cudaStreamWaitEvent(p->out, p->ev_start, 0);
+    cudaMemcpyAsync(w.u0, u0_h, row_bytes, cudaMemcpyHostToDevice, p->in);
+    // forward, blocks in time order
+    for (int64_t k = 0; k < nblk; k++) {
+        const int j = (int)(k % kRowSlots);
+        const int64_t r = rows_of(k), off = k * bt * N;
+        if (k >= kRowSlots) cudaStreamWaitEvent(p->in, p->ev_fwd[j], 0);  // I slot j consumed
+        cudaMemcpyAsync(w.I[j], I_h + off, (size_t)r * row_bytes, cudaMemcpyHostToDevice, p->in);
+        cudaEventRecord(p->ev_in[j], p->in);
+        cudaStreamWaitEvent(cs, p->ev_in[j], 0);
+        if (k >= kRowSlots) cudaStreamWaitEvent(cs, p->ev_sout[j], 0);  // S slot j copied out
+        const float *uin = k == 0 ? w.u0 : w.ust[(k - 1) & 1];
+        if (!fwd_replay_tma(w.I[j], uin, nullptr, w.V + off, w.S[j], w.ust[k & 1], r, N, r, beta, theta, u_r, cs,
+                            1, 0, nullptr, true)) {
+            *err = "the TMA forward refused a row block";
+            return LIFB_ERR_CUDA;
+        }
+        cudaEventRecord(p->ev_fwd[j], cs);
+        cudaStreamWaitEvent(p->out, p->ev_fwd[j], 0);
+        cudaMemcpyAsync(S_h + off, w.S[j], (size_t)r * row_bytes, cudaMemcpyDeviceToHost, p->out);
+        cudaEventRecord(p->ev_sout[j], p->out);
+    }
+    // adjoint, blocks in reverse order; q counts the blocks processed
+    for (int64_t q = 0; q < nblk; q++) {
+        const int64_t k = nblk - 1 - q;
+        const int j = (int)(q % kRowSlots);
+        const int64_t r = rows_of(k), off = k * bt * N;
+        if (q >= kRowSlots) cudaStreamWaitEvent(p->in, p->ev_done[j], 0);  // GS slot j consumed
+        cudaMemcpyAsync(w.GS[j], GS_h + off, (size_t)r * row_bytes, cudaMemcpyHostToDevice, p->in);
+        cudaEventRecord(p->ev_gs[j], p->in);
+        cudaStreamWaitEvent(cs, p->ev_gs[j], 0);
+        if (q >= kRowSlots) cudaStreamWaitEvent(cs, p->ev_free[j], 0);  // Lam slot j copied out
+        // lam entering from the row after the block: row 0 of the block processed before
+        const float *lam_end = q == 0 ? nullptr : w.Lam[(q - 1) % kRowSlots];
+        if (!bwd_tma_v(w.V + off, w.GS[j], w.Lam[j], nullptr, nullptr, nullptr, r, N, r, beta, theta, alpha, cs,
+                       lam_end)) {
+            *err = "the TMA adjoint refused a row block";
+            return LIFB_ERR_CUDA;
+        }
+        if (k == 0) {
+            count_launches(1);
+            k_scale_row<<<(unsigned)((N + 255) / 256), 256, 0, cs>>>(w.Lam[j], beta, w.du0, N);
+        }
+        cudaEventRecord(p->ev_done[j], cs);
+        cudaStreamWaitEvent(p->out, p->ev_done[j], 0);
+        cudaMemcpyAsync(dI_h + off, w.Lam[j], (size_t)r * row_bytes, cudaMemcpyDeviceToHost, p->out);
+        if (k == 0) cudaMemcpyAsync(du0_h, w.du0, row_bytes, cudaMemcpyDeviceToHost, p->out);
+        cudaEventRecord(p->ev_free[j], p->out);
+    }
     cudaEventRecord(p->ev_last, p->out);
     cudaStreamWaitEvent(cs, p->ev_last, 0);
     return LIFB_OK;

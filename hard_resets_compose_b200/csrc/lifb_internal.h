@@ -107,8 +107,10 @@ bool bwd_tma(int mode, const float *I, const float *u0, const float *U, const fl
 // chunk_tma.cu: the adjoint from V (the forward's pre-reset potentials v_t)
 // and GS only: detached reset, s recomputed as [v >= theta], no GU.  P, Q, D
 // as bwd_tma when P is given; false when the TMA path does not apply.
+// LamEnd (optional, [T/C, N]): the lam entering chunk m from the row after
+// it (lam_{(m+1)C}); NULL: 0.
 bool bwd_tma_v(const float *V, const float *GS, float *Lam, float *P, float *Q, int32_t *D, int64_t T, int64_t N,
-               int64_t C, float beta, float theta, float alpha, cudaStream_t s);
+               int64_t C, float beta, float theta, float alpha, cudaStream_t s, const float *LamEnd = nullptr);
 
 // chunk_tma.cu: the affine-reset adjoint (detached reset: a = beta*gamma at a
 // spike, beta elsewhere) over one chunk of T rows, v from U and I (u0 for row
@@ -203,6 +205,12 @@ size_t host_pipe_workspace_bytes(int64_t T, int64_t N, int64_t block_n);
 int host_pipe_run(const float *I_h, const float *GS_h, const float *u0_h, float *S_h, float *dI_h, float *du0_h,
                   int64_t T, int64_t N, float beta, float theta, float u_r, float alpha, int64_t block_n,
                   void *workspace, cudaStream_t cs, const char **err);
+// The same over blocks of block_t time rows (contiguous copies; N % 4 == 0).
+int64_t host_pipe_rows_default_block(int64_t T, int64_t N);
+size_t host_pipe_rows_workspace_bytes(int64_t T, int64_t N, int64_t block_t);
+int host_pipe_run_rows(const float *I_h, const float *GS_h, const float *u0_h, float *S_h, float *dI_h,
+                       float *du0_h, int64_t T, int64_t N, float beta, float theta, float u_r, float alpha,
+                       int64_t block_t, void *workspace, cudaStream_t cs, const char **err);
 
 // carry_tma.cu: sequential map carry with TMA-staged map windows; false when
 // it does not apply (N % 4 != 0, K > 64).  Writes Starts[m] for m < M.

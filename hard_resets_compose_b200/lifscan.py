@@ -659,12 +659,15 @@ def lif_auto(I, u0, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, K=16, repair=0):
 
 # ----------------------------------------------------------------------------- host-resident tensors
 def lif_tuned_host(I, GS, u0=None, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, block_n=None, device=None,
-                   out=None, sync=True):
-    """lif_tuned forward + backward for host (CPU) tensors, pipelined over
-    neuron blocks so host->device copies, compute and device->host copies
-    overlap (lifb_lif_fwd_bwd_host).  Returns (S, dI, du0) as CPU tensors
-    (pinned); equivalent to S = lif_tuned(I, u0, ...);
-    torch.autograd.backward(S, GS) with dI = I.grad and du0 = u0.grad.
+                   out=None, sync=True, block_t=None):
+    """lif_tuned forward + backward for host (CPU) tensors, pipelined so
+    host->device copies, compute and device->host copies overlap.  Returns
+    (S, dI, du0) as CPU tensors (pinned); equivalent to S = lif_tuned(I, u0,
+    ...); torch.autograd.backward(S, GS) with dI = I.grad and du0 = u0.grad.
+    The pipeline runs over blocks of time rows (lifb_lif_fwd_bwd_host_rows:
+    contiguous copies, block_t rows, default about 16 MiB per block) when N %
+    4 == 0 and block_n is not given, else over blocks of block_n neurons
+    (lifb_lif_fwd_bwd_host); both give the same bits.
     I and GS should be pinned for full overlap; `out` may pass preallocated
     pinned (S, dI, du0).  sync=True (default) waits for the device's current
     stream, so the returned tensors are complete, and raises LifbError if a
@@ -681,19 +684,32 @@ def lif_tuned_host(I, GS, u0=None, beta=0.9, theta=1.0, u_r=0.0, alpha=4.0, bloc
         raise ValueError("GS must have the shape of I")
     u0 = torch.zeros(N, dtype=torch.float32) if u0 is None else u0.contiguous()
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    if block_n is None:  # about 4 blocks, 128-neuron aligned (B200: 3.3 ms at config 2, PCIe floor ~2.8)
+    rows = block_n is None and N % 4 == 0
+    if rows and block_t is not None and block_t <= 0:
+        raise ValueError("block_t must be positive")
+    if not rows and block_t is not None:
+        raise ValueError("block_t applies to the row-block pipeline (N % 4 == 0, block_n not given)")
+    if block_n is None and not rows:  # about 4 blocks, 128-neuron aligned
         block_n = max(128, ((N + 3) // 4 + 127) // 128 * 128)
     if out is None:
         out = (torch.empty(T, N).pin_memory(), torch.empty(T, N).pin_memory(), torch.empty(N).pin_memory())
     S, dI, du0 = out
     L = _lib.load()
     with torch.cuda.device(dev):
-        nb = L.lifb_lif_fwd_bwd_host_workspace_bytes(T, N, block_n)
-        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
         st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        check(L.lifb_lif_fwd_bwd_host(ptr(I), ptr(GS), ptr(u0), ptr(S), ptr(dI), ptr(du0), T, N, _f(beta),
-                                      _f(theta), _f(u_r), _f(alpha), int(block_n), ptr(ws), nb, st),
-              "lif_tuned_host")
+        if rows:
+            bt = int(block_t) if block_t is not None else L.lifb_lif_fwd_bwd_host_rows_block(T, N)
+            nb = L.lifb_lif_fwd_bwd_host_rows_workspace_bytes(T, N, bt)
+            ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+            check(L.lifb_lif_fwd_bwd_host_rows(ptr(I), ptr(GS), ptr(u0), ptr(S), ptr(dI), ptr(du0), T, N,
+                                               _f(beta), _f(theta), _f(u_r), _f(alpha), bt, ptr(ws), nb, st),
+                  "lif_tuned_host")
+        else:
+            nb = L.lifb_lif_fwd_bwd_host_workspace_bytes(T, N, block_n)
+            ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+            check(L.lifb_lif_fwd_bwd_host(ptr(I), ptr(GS), ptr(u0), ptr(S), ptr(dI), ptr(du0), T, N, _f(beta),
+                                          _f(theta), _f(u_r), _f(alpha), int(block_n), ptr(ws), nb, st),
+                  "lif_tuned_host")
         if sync:
             # the host buffers are complete only once the stream has drained;
             # the device status is read at the same point

@@ -196,6 +196,23 @@ int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float
                           int64_t T, int64_t N, float beta, float theta, float u_r, float alpha,
                           int64_t block_n, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The same call pipelined over blocks of block_t time rows instead of neuron
+ * columns (N % 4 == 0; LIFB_ERR_UNSUPPORTED otherwise).  A block of rows is one
+ * contiguous range of each host array, so every copy is one linear transfer.
+ * The forward runs the blocks in time order, each from the state the previous
+ * block ended in; the adjoint runs them in reverse order, each from the lam
+ * the block after it left.  Results equal lifb_lif_fwd_bwd_host's bit for bit.
+ * V of all rows stays in the workspace between the two sweeps, so the
+ * workspace (lifb_lif_fwd_bwd_host_rows_workspace_bytes) is T*N*4 bytes plus
+ * four staging slots of 4*block_t*N*4 bytes.  lifb_lif_fwd_bwd_host_rows_block
+ * gives the default block_t (blocks of about 16 MiB per array). */
+int64_t lifb_lif_fwd_bwd_host_rows_block(int64_t T, int64_t N);
+size_t lifb_lif_fwd_bwd_host_rows_workspace_bytes(int64_t T, int64_t N, int64_t block_t);
+int lifb_lif_fwd_bwd_host_rows(const float *I_host, const float *GS_host, const float *u0_host,
+                               float *S_host, float *dI_host, float *du0_host,
+                               int64_t T, int64_t N, float beta, float theta, float u_r, float alpha,
+                               int64_t block_t, void *workspace, size_t workspace_bytes, void *stream);
+
 /* No-allocation variant of lifb_scan_fwd_v3 (no counterpart in the
  * reference, which only runs inside PyTorch and always allocates).
  * For callers that cannot allocate device memory when they call in: a plain

@@ -138,6 +138,46 @@ def test_lif_tuned_host_pipeline(cuda, N, block_n):
     assert np.array_equal(dI2.numpy(), dI.numpy())
 
 
+@pytest.mark.parametrize("N,T,block_t", ((16384, 1024, None), (1000, 1000, 96), (1024, 1024, 1024),
+                                         (4096, 1024, 16), (512, 37, 5), (8, 64, 1)))
+def test_lif_tuned_host_row_blocks(cuda, N, T, block_t):
+    """Host-buffer forward+backward over blocks of time rows
+    (lifb_lif_fwd_bwd_host_rows): spikes bit-exact, dI and du0 within 1e-5 of
+    the oracle and bit-equal to the neuron-block pipeline, for a ragged last
+    block, a single block, many blocks through four slots, and one-row blocks."""
+    beta = 0.99
+    I, u0, GS = gen(T, N, 0.05, 0.2, seed=11, u0_sd=0.3, grad=True)
+    Us, Ss = O.serial_forward(I, beta, 1.0, 0.0, u0)
+    dI_ref = O.serial_backward(I, u0, Us, Ss, GS, None, beta, 1.0, 0.0, 4.0, True)
+    It = torch.from_numpy(I).pin_memory()
+    Gt = torch.from_numpy(GS).pin_memory()
+    S, dI, du0 = L().lif_tuned_host(It, Gt, torch.from_numpy(u0), beta=beta, block_t=block_t)
+    assert_bit_equal(S.numpy(), Ss, "S")
+    assert rel(dI.numpy(), dI_ref) < TOL
+    assert rel(du0.numpy(), beta * dI_ref[0]) < TOL
+    Sc, dIc, du0c = L().lif_tuned_host(It, Gt, torch.from_numpy(u0), beta=beta, block_n=max(4, N // 2 // 4 * 4))
+    assert np.array_equal(dIc.numpy(), dI.numpy())
+    assert np.array_equal(du0c.numpy(), du0.numpy())
+    # a second call reuses the copy streams and the slots
+    S2, dI2, _ = L().lif_tuned_host(It, Gt, torch.from_numpy(u0), beta=beta, block_t=block_t)
+    assert_bit_equal(S2.numpy(), Ss, "S (second call)")
+    assert np.array_equal(dI2.numpy(), dI.numpy())
+
+
+def test_lif_tuned_host_row_blocks_refusals(cuda):
+    from hard_resets_compose_b200 import _lib
+    lib = _lib.load()
+    z = torch.zeros(4, 6).pin_memory()
+    with pytest.raises(ValueError):
+        L().lif_tuned_host(z, z, block_t=2)  # N % 4 != 0: the neuron-block form only
+    z4 = torch.zeros(4, 8).pin_memory()
+    with pytest.raises(ValueError):
+        L().lif_tuned_host(z4, z4, block_t=0)
+    assert lib.lifb_lif_fwd_bwd_host_rows_block(1024, 16384) == 256
+    assert lib.lifb_lif_fwd_bwd_host_rows_block(10, 16384) == 10
+    assert lib.lifb_lif_fwd_bwd_host_rows_block(1024, 1 << 24) == 1
+
+
 @pytest.mark.parametrize("beta", (0.5, 0.9, 0.99, 1.0))
 @pytest.mark.parametrize("N,T,C", ((1000, 4096, 64), (1024, 1 << 16, 1024), (777, 2048, 128), (64, 4096, 4096)))
 def test_scan_backward_fast_path(cuda, beta, N, T, C):
