@@ -49,6 +49,8 @@ SIGNATURES = {
     "lifb_lif_fwd_bwd_host_workspace_bytes": ([c_i64, c_i64, c_i64], c_size_t),
     "lifb_lif_fwd_bwd_host": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_float,
                                c_float, c_float, c_float, c_i64, c_void_p, c_size_t, c_void_p], c_int),
+    "lifb_dense_dgrad_workspace_bytes": ([c_i64, c_i64], c_size_t),
+    "lifb_dense_dgrad": ([c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_void_p, c_size_t, c_void_p], c_int),
     "lifb_lif_fwd_bwd_host_rows_block": ([c_i64, c_i64], c_i64),
     "lifb_lif_fwd_bwd_host_rows_workspace_bytes": ([c_i64, c_i64, c_i64], c_size_t),
     "lifb_lif_fwd_bwd_host_rows": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,

@@ -196,6 +196,20 @@ int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float
                           int64_t T, int64_t N, float beta, float theta, float u_r, float alpha,
                           int64_t block_n, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Input gradient of a dense layer, dX [R, Din] = dY [R, Dout] . W [Dout, Din]
+ * (row-major fp32; W is the Linear layer's weight), on the tensor cores as
+ * three TF32 products (the operands split into TF32 high and low parts, the
+ * product of the low parts dropped) accumulated in fp32: within about 1e-6
+ * relative of an fp32 GEMM, not bit-equal to one.  This is the backward of
+ * the Linear feeding a LIF layer in the consumer network (lifscan/shdnet.py:
+ * 30-50, where torch computes it as an fp32 GEMM).  Needs Dout % 32 == 0 and
+ * Din in {64, 128, 256} (LIFB_ERR_UNSUPPORTED otherwise) and 16-byte aligned
+ * pointers; the workspace (lifb_dense_dgrad_workspace_bytes) holds W's
+ * transposed high and low parts. */
+size_t lifb_dense_dgrad_workspace_bytes(int64_t Din, int64_t Dout);
+int lifb_dense_dgrad(const float *dY, const float *W, float *dX, int64_t R, int64_t Din, int64_t Dout,
+                     void *workspace, size_t workspace_bytes, void *stream);
+
 /* The same call pipelined over blocks of block_t time rows instead of neuron
  * columns (N % 4 == 0; LIFB_ERR_UNSUPPORTED otherwise).  A block of rows is one
  * contiguous range of each host array, so every copy is one linear transfer.
