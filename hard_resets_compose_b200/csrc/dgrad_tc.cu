@@ -12,15 +12,19 @@
 //
 // Layout: one CTA per 128 rows of dY (the MMA's M), all Din columns (N <= 256)
 // in one TMEM accumulator of 128 lanes x N fp32 columns.  K = Dout runs in
-// chunks of 32 (one 128-byte swizzle row): TMA brings the dY chunk and the
+// chunks of 16 (one 64-byte swizzle row): TMA brings the dY chunk and the
 // chunks of W^T's high and low parts (prepared once per call by k_split_wt)
-// into a 2-stage ring in the 128-byte swizzled K-major layout; the CTA's 128
-// threads split the dY chunk in place (high part) and beside it (low part);
-// one thread issues the 12 MMAs of the chunk (3 products x 4 MMAs of K = 8)
-// and commits them to the stage's barrier, after which the stage is refilled.
-// The epilogue reads the accumulator with tcgen05.ld (one row per thread),
-// writes it to shared memory in the same swizzled layout and stores it with
-// TMA, 32 columns at a time.  Every barrier wait is bounded (status 101).
+// into a 2-stage ring in the 64-byte swizzled K-major layout; the CTA's 128
+// worker threads split the dY chunk in place (high part) and beside it (low
+// part); one of them issues the 6 MMAs of the chunk (3 products x 2 MMAs of
+// K = 8) and commits them to the stage's barrier, on which a producer warp
+// waits to refill the stage while the workers go on to the next one.
+// The 48-KB stages let two CTAs share an SM (and its 512 TMEM columns), so
+// one CTA's epilogue and waits overlap the other's MMAs.  The epilogue reads
+// the accumulator with tcgen05.ld (one row per thread), writes it to shared
+// memory in the 128-byte swizzled layout and stores it with TMA, 32 columns
+// at a time, four column groups per round.  Every barrier wait is bounded
+// (status 101).
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
 #include "tma.cuh"
@@ -30,18 +34,20 @@ namespace lifb {
 namespace {
 
 constexpr int kDgM = 128;        // rows of dY per CTA (the MMA's M)
-constexpr int kDgK = 32;         // K per stage: one 128-byte swizzle row of fp32
+constexpr int kDgK = 16;         // K per stage: one 64-byte swizzle row of fp32
+constexpr int kDgOutCols = 32;   // columns per output tile: one 128-byte swizzle row
+constexpr int kDgOutRound = 4;   // output tiles staged per round (64 KB)
 constexpr int kDgStages = 2;
-constexpr int kDgThreads = 128;  // 4 warps: one TMEM lane quarter each
+constexpr int kDgThreads = 128;  // worker warps: one TMEM lane quarter each (plus a producer warp)
 
-// Shared-memory matrix descriptor of a K-major operand in the 128-byte
-// swizzled layout: rows of 128 bytes, groups of 8 rows 1024 bytes apart
-// (stride byte offset), leading byte offset unused (1), descriptor version 1,
-// layout type 2 (128-byte swizzle).  The tile base must be 1024-byte aligned;
-// the K steps inside the swizzle row advance the start address by 32 bytes.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr)
+// Shared-memory matrix descriptor of a K-major operand in the 64-byte
+// swizzled layout: rows of 64 bytes, groups of 8 rows 512 bytes apart (stride
+// byte offset), leading byte offset unused (1), descriptor version 1, layout
+// type 4 (64-byte swizzle).  The tile base must be 512-byte aligned; the K
+// steps inside the swizzle row advance the start address by 32 bytes.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr)
 {
-    return (uint64_t)((saddr & 0x3FFFF) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+    return (uint64_t)((saddr & 0x3FFFF) >> 4) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
 }
 
 // Instruction descriptor of kind::tf32: D fp32 (bits 4-5 = 1), A and B TF32
@@ -120,20 +126,21 @@ __global__ void k_split_wt(const float *__restrict__ W, float *__restrict__ hi, 
 }
 
 // dX = dY . W for one 128-row tile per CTA; N = Din (a multiple of 16, <= 256),
-// K = Dout (a multiple of 32); tmem_cols: N rounded up to a power of two >= 32.
+// K = Dout (a multiple of 16); tmem_cols: N rounded up to a power of two >= 32.
 template <int N>
-__global__ void __launch_bounds__(kDgThreads, 1)
+__global__ void __launch_bounds__(kDgThreads + 32, 2)
     k_dgrad_3xtf32(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tBh,
                    const __grid_constant__ CUtensorMap tBl, const __grid_constant__ CUtensorMap tC, int K,
                    int *status)
 {
-    constexpr uint32_t kABytes = kDgM * kDgK * 4;  // 16 KB
+    constexpr uint32_t kABytes = kDgM * kDgK * 4;  // 8 KB
+    constexpr uint32_t kOutBytes = kDgM * kDgOutCols * 4;  // 16 KB
     constexpr uint32_t kBBytes = N * kDgK * 4;
     constexpr uint32_t kStage = 2 * kABytes + 2 * kBBytes;
     constexpr int kTmemCols = N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
     constexpr uint32_t kIdesc = umma_idesc_tf32(kDgM, N);
     extern __shared__ unsigned char dg_raw[];
-    // 1024-byte alignment of every tile (the swizzle atom)
+    // 1024-byte alignment of every tile (the largest swizzle atom)
     unsigned char *base = (unsigned char *)(((uintptr_t)dg_raw + 1023) & ~(uintptr_t)1023);
     __shared__ __align__(8) uint64_t full[kDgStages], done[kDgStages];
     __shared__ uint32_t tmem_slot;
@@ -141,17 +148,14 @@ __global__ void __launch_bounds__(kDgThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5;
     const int nk = K / kDgK;
     const int m0 = blockIdx.x * kDgM;
+    // warps 0-3: split, MMA issue (thread 0), epilogue (TMEM lane quarter = warp);
+    // warp 4: the producer, which refills a stage as soon as the MMAs that read it retire
+    auto workers_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(kDgThreads) : "memory"); };
 
     auto A = [&](int s) { return base + (size_t)s * kStage; };
     auto Alo = [&](int s) { return base + (size_t)s * kStage + kABytes; };
     auto Bh = [&](int s) { return base + (size_t)s * kStage + 2 * kABytes; };
     auto Bl = [&](int s) { return base + (size_t)s * kStage + 2 * kABytes + kBBytes; };
-    auto issue = [&](int s, int c) {
-        mbar_arrive_expect_tx(&full[s], kStage - kABytes);  // A, Bh, Bl (Alo is written by the threads)
-        tma_load_2d(A(s), &tA, c * kDgK, m0, &full[s]);
-        tma_load_2d(Bh(s), &tBh, c * kDgK, 0, &full[s]);
-        tma_load_2d(Bl(s), &tBl, c * kDgK, 0, &full[s]);
-    };
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -160,10 +164,6 @@ __global__ void __launch_bounds__(kDgThreads, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        prefetch_tmap(&tA);
-        prefetch_tmap(&tBh);
-        prefetch_tmap(&tBl);
-        prefetch_tmap(&tC);
         for (int s = 0; s < kDgStages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&done[s], 1);
@@ -175,79 +175,98 @@ __global__ void __launch_bounds__(kDgThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    if (tid == 0)
-        for (int c = 0; c < kDgStages && c < nk; c++) issue(c, c);
 
-    int issued_commits = 0;
-    for (int c = 0; c < nk; c++) {
-        const int s = c % kDgStages;
-        const uint32_t ph = (uint32_t)(c / kDgStages) & 1;
-        if (!mbar_wait(&full[s], ph)) atomicExch(&abort_flag, 1);
-        __syncthreads();
-        if (abort_flag) break;
-        // split the dY chunk: high part in place, low part beside it (same layout)
-        float4 *a4 = reinterpret_cast<float4 *>(A(s));
-        float4 *l4 = reinterpret_cast<float4 *>(Alo(s));
-#pragma unroll
-        for (int i = tid; i < (int)(kABytes / 16); i += kDgThreads) {
-            float4 v = a4[i], h, l;
-            h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
-            l.x = tf32_hi(v.x - h.x); l.y = tf32_hi(v.y - h.y); l.z = tf32_hi(v.z - h.z); l.w = tf32_hi(v.w - h.w);
-            a4[i] = h;
-            l4[i] = l;
-        }
-        fence_proxy_async_shared();  // the threads' writes, seen by the tensor cores
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t sa = smem_u32(A(s)), sl = smem_u32(Alo(s)), sh = smem_u32(Bh(s)), sb = smem_u32(Bl(s));
-#pragma unroll
-            for (int kk = 0; kk < kDgK / 8; kk++) {
-                const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
-                const uint64_t da = umma_desc_sw128(sa + off), dl = umma_desc_sw128(sl + off);
-                const uint64_t dh = umma_desc_sw128(sh + off), db = umma_desc_sw128(sb + off);
-                umma_tf32(tmem, da, dh, kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
-                umma_tf32(tmem, da, db, kIdesc, 1u);
-                umma_tf32(tmem, dl, dh, kIdesc, 1u);
-            }
-            umma_commit(&done[s]);
-            if (c + kDgStages < nk) {
-                // the stage is refilled once this chunk's MMAs have read it
-                if (mbar_wait(&done[s], ph)) issue(s, c + kDgStages);
-                else atomicExch(&abort_flag, 1);
+    if (warp == kDgThreads / 32) {
+        if ((tid & 31) == 0) {
+            prefetch_tmap(&tA);
+            prefetch_tmap(&tBh);
+            prefetch_tmap(&tBl);
+            for (int c = 0; c < nk; c++) {
+                const int s = c % kDgStages;
+                // chunk c - kDgStages's MMAs have read the stage
+                if (c >= kDgStages && !mbar_wait(&done[s], (uint32_t)((c - kDgStages) / kDgStages) & 1)) {
+                    atomicExch(&abort_flag, 1);
+                    break;
+                }
+                if (abort_flag) break;
+                mbar_arrive_expect_tx(&full[s], kStage - kABytes);  // A, Bh, Bl (Alo is written by the workers)
+                tma_load_2d(A(s), &tA, c * kDgK, m0, &full[s]);
+                tma_load_2d(Bh(s), &tBh, c * kDgK, 0, &full[s]);
+                tma_load_2d(Bl(s), &tBl, c * kDgK, 0, &full[s]);
             }
         }
-        issued_commits = c + 1;
-    }
-    __syncthreads();
-    // the last commit tracks every MMA issued before it
-    if (issued_commits > 0) {
-        const int c = issued_commits - 1;
-        if (!mbar_wait(&done[c % kDgStages], (uint32_t)(c / kDgStages) & 1)) atomicExch(&abort_flag, 1);
-    }
-    __syncthreads();  // one decision for the whole CTA
-    const bool ok = !abort_flag && issued_commits == nk;
-    if (!ok && tid == 0) atomicExch(status, kStatusTmaWaitTimeout);
-    tc_fence_after();
-    if (ok) {
-        // epilogue: 32 columns at a time, TMEM -> registers -> swizzled smem -> TMA store
-        const int row = warp * 32 + (tid & 31);
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    } else {
+        int issued = 0;
+        for (int c = 0; c < nk; c++) {
+            const int s = c % kDgStages;
+            const uint32_t ph = (uint32_t)(c / kDgStages) & 1;
+            if (!mbar_wait(&full[s], ph)) atomicExch(&abort_flag, 1);
+            workers_sync();
+            if (abort_flag) break;
+            // split the dY chunk: high part in place, low part beside it (same layout)
+            float4 *a4 = reinterpret_cast<float4 *>(A(s));
+            float4 *l4 = reinterpret_cast<float4 *>(Alo(s));
+#pragma unroll
+            for (int i = tid; i < (int)(kABytes / 16); i += kDgThreads) {
+                float4 v = a4[i], h, l;
+                h.x = tf32_hi(v.x); h.y = tf32_hi(v.y); h.z = tf32_hi(v.z); h.w = tf32_hi(v.w);
+                l.x = tf32_hi(v.x - h.x); l.y = tf32_hi(v.y - h.y); l.z = tf32_hi(v.z - h.z); l.w = tf32_hi(v.w - h.w);
+                a4[i] = h;
+                l4[i] = l;
+            }
+            fence_proxy_async_shared();  // the workers' writes, seen by the tensor cores
+            workers_sync();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t sa = smem_u32(A(s)), sl = smem_u32(Alo(s)), sh = smem_u32(Bh(s)), sb = smem_u32(Bl(s));
+#pragma unroll
+                for (int kk = 0; kk < kDgK / 8; kk++) {
+                    const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
+                    const uint64_t da = umma_desc_sw64(sa + off), dl = umma_desc_sw64(sl + off);
+                    const uint64_t dh = umma_desc_sw64(sh + off), db = umma_desc_sw64(sb + off);
+                    umma_tf32(tmem, da, dh, kIdesc, (c > 0 || kk > 0) ? 1u : 0u);
+                    umma_tf32(tmem, da, db, kIdesc, 1u);
+                    umma_tf32(tmem, dl, dh, kIdesc, 1u);
+                }
+                umma_commit(&done[s]);
+            }
+            issued = c + 1;
+        }
+        workers_sync();
+        // the last commit tracks every MMA issued before it
+        if (issued > 0 && !mbar_wait(&done[(issued - 1) % kDgStages], (uint32_t)((issued - 1) / kDgStages) & 1))
+            atomicExch(&abort_flag, 1);
+        workers_sync();  // one decision for all workers
+        const bool ok = !abort_flag && issued == nk;
+        if (!ok && tid == 0) atomicExch(status, kStatusTmaWaitTimeout);
+        tc_fence_after();
+        if (ok) {
+            // epilogue: TMEM -> registers -> swizzled smem -> TMA store, 32 columns
+            // per tile, kDgOutRound tiles per round
+            const int row = warp * 32 + (tid & 31);
+            const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
 #pragma unroll 1
-        for (int g = 0; g < N / 32; g++) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_base + (uint32_t)(g * 32), r);
-            unsigned char *tile = base + (size_t)g * kABytes;  // [128 rows][128 bytes], swizzled
-            uint4 *rowp = reinterpret_cast<uint4 *>(tile + row * 128);
+            for (int g0 = 0; g0 < N / kDgOutCols; g0 += kDgOutRound) {
+#pragma unroll 1
+                for (int g = g0; g < g0 + kDgOutRound && g < N / kDgOutCols; g++) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lane_base + (uint32_t)(g * kDgOutCols), r);
+                    unsigned char *tile = base + (size_t)(g - g0) * kOutBytes;  // [128 rows][128 bytes], swizzled
+                    uint4 *rowp = reinterpret_cast<uint4 *>(tile + row * 128);
 #pragma unroll
-            for (int j = 0; j < 8; j++) rowp[j ^ (row & 7)] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-        }
-        fence_proxy_async_shared();
-        __syncthreads();
-        if (tid == 0) {
-            for (int g = 0; g < N / 32; g++) tma_store_2d(&tC, g * 32, m0, base + (size_t)g * kABytes);
-            bulk_commit();
-            bulk_wait_all();
+                    for (int j = 0; j < 8; j++)
+                        rowp[j ^ (row & 7)] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                }
+                fence_proxy_async_shared();
+                workers_sync();
+                if (tid == 0) {
+                    for (int g = g0; g < g0 + kDgOutRound && g < N / kDgOutCols; g++)
+                        tma_store_2d(&tC, g * kDgOutCols, m0, base + (size_t)(g - g0) * kOutBytes);
+                    bulk_commit();
+                    bulk_wait_all();  // the staging tiles are reused by the next round
+                }
+                workers_sync();
+            }
         }
     }
     tc_fence_before();
@@ -271,17 +290,19 @@ static bool launch_dgrad(const float *dY, const float *Wt_hi, const float *Wt_lo
                          cudaStream_t s)
 {
     CUtensorMap mA, mBh, mBl, mC;
-    if (!make_tmap_2d_sw128(&mA, dY, K, R, kDgM) || !make_tmap_2d_sw128(&mBh, Wt_hi, K, N, N) ||
-        !make_tmap_2d_sw128(&mBl, Wt_lo, K, N, N) || !make_tmap_2d_sw128(&mC, dX, N, R, kDgM))
+    if (!make_tmap_2d_swz(&mA, dY, K, R, kDgM, kDgK * 4) || !make_tmap_2d_swz(&mBh, Wt_hi, K, N, N, kDgK * 4) ||
+        !make_tmap_2d_swz(&mBl, Wt_lo, K, N, N, kDgK * 4) || !make_tmap_2d_swz(&mC, dX, N, R, kDgM, kDgOutCols * 4))
         return false;
     constexpr size_t stage = (size_t)2 * kDgM * kDgK * 4 + (size_t)2 * N * kDgK * 4;
-    const size_t epi = (size_t)N / 32 * kDgM * kDgK * 4;
+    constexpr int rounds_tiles = N / kDgOutCols < kDgOutRound ? N / kDgOutCols : kDgOutRound;
+    const size_t epi = (size_t)rounds_tiles * kDgM * kDgOutCols * 4;
     const size_t smem = (kDgStages * stage > epi ? kDgStages * stage : epi) + 1024;
     auto kern = k_dgrad_3xtf32<N>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return false;
     count_launches(1);
-    kern<<<(unsigned)((R + kDgM - 1) / kDgM), kDgThreads, smem, s>>>(mA, mBh, mBl, mC, (int)K, device_status_ptr());
+    kern<<<(unsigned)((R + kDgM - 1) / kDgM), kDgThreads + 32, smem, s>>>(mA, mBh, mBl, mC, (int)K,
+                                                                        device_status_ptr());
     return true;
 }
 
@@ -326,7 +347,7 @@ extern "C" int lifb_dense_dgrad(const float *dY, const float *W, float *dX, int6
         return LIFB_ERR_INVALID_ARGUMENT;
     }
     if (!lifb::dgrad_tc_applies(R, Din, Dout)) {
-        lifb::set_last_error("lifb_dense_dgrad: needs Dout % 32 == 0 and Din in {64, 128, 256}");
+        lifb::set_last_error("lifb_dense_dgrad: needs Dout % 16 == 0 and Din in {64, 128, 256}");
         return LIFB_ERR_UNSUPPORTED;
     }
     if (!lifb::dgrad_tc(dY, W, dX, R, Din, Dout, workspace, (cudaStream_t)stream)) {

@@ -66,10 +66,10 @@ bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N,
 // 3-D map of a [d2, d1, d0] array of 32-bit words (d0 innermost), box
 // (b0, b1, b2); false unless d0 * 4 is a multiple of 16 and base is 16-byte
 // aligned.
-// 2-D float map [T rows, N columns] with boxes of 32 columns (128 bytes) x
-// box_y rows in the 128-byte swizzled shared-memory layout of the tensor cores'
-// K-major operands.
-bool make_tmap_2d_sw128(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_y);
+// 2-D float map [T rows, N columns] with boxes of one swizzle row (swz_bytes
+// = 64 or 128 bytes of columns) x box_y rows, in the swizzled shared-memory
+// layout of the tensor cores' K-major operands.
+bool make_tmap_2d_swz(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_y, int swz_bytes);
 bool make_tmap_3d_u32(CUtensorMap *m, const void *base, int64_t d0, int64_t d1, int64_t d2, int b0, int b1, int b2);
 int *device_status_ptr();                 // status word of the current device
 int read_device_status(bool reset);       // synchronous read (current device)

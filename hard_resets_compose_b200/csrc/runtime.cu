@@ -66,20 +66,21 @@ bool make_tmap_2d_typed(CUtensorMap *m, const void *base, bool int32, int64_t N,
     return r == CUDA_SUCCESS;
 }
 
-bool make_tmap_2d_sw128(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_y)
+bool make_tmap_2d_swz(CUtensorMap *m, const float *base, int64_t N, int64_t T, int box_y, int swz_bytes)
 {
     bind_primary_context();
     auto enc = encoder();
     if (!enc || ((uintptr_t)base & 15) || (N * 4) % 16 || T >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) ||
-        box_y < 1 || box_y > 256)
+        box_y < 1 || box_y > 256 || (swz_bytes != 64 && swz_bytes != 128))
         return false;
     cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)T};
     cuuint64_t strides[1] = {(cuuint64_t)N * 4};
-    cuuint32_t box[2] = {32, (cuuint32_t)box_y};  // 32 floats = one 128-byte swizzle row
+    cuuint32_t box[2] = {(cuuint32_t)(swz_bytes / 4), (cuuint32_t)box_y};  // one swizzle row of floats
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swz_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 

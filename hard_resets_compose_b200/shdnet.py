@@ -110,7 +110,7 @@ class SpikeLinearLIF(torch.autograd.Function):
 
 def dense_dgrad_applies(din, dout):
     """Whether lifb_dense_dgrad takes a layer of this shape."""
-    return dout % 32 == 0 and din in (64, 128, 256)
+    return dout % 16 == 0 and din in (64, 128, 256)
 
 
 def dense_dgrad(dY, weight):

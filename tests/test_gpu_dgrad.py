@@ -35,7 +35,7 @@ def rel(a, b):
 
 
 @pytest.mark.parametrize("R,Din,Dout", ((65536, 256, 256), (1000, 128, 64), (37, 64, 32), (384, 256, 512),
-                                        (129, 256, 32), (4096, 64, 256)))
+                                        (129, 256, 32), (4096, 64, 256), (300, 128, 48)))
 def test_dense_dgrad_matches_fp64(cuda, R, Din, Dout):
     g = torch.Generator(device="cuda").manual_seed(R + Din + Dout)
     dY = torch.randn(R, Dout, device="cuda", generator=g) * 1e-3
@@ -68,7 +68,7 @@ def test_dense_dgrad_refusals(cuda):
     dY = torch.zeros(8, 20, device="cuda")
     W = torch.zeros(20, 256, device="cuda")
     rc, _ = dgrad(dY, W)
-    assert rc == 4  # LIFB_ERR_UNSUPPORTED: Dout % 32 != 0
+    assert rc == 4  # LIFB_ERR_UNSUPPORTED: Dout % 16 != 0
     dY = torch.zeros(8, 32, device="cuda")
     W = torch.zeros(32, 96, device="cuda")
     rc, _ = dgrad(dY, W)
