@@ -104,8 +104,11 @@ __device__ __forceinline__ float tf32_hi(float a)
 }  // namespace
 
 // Wt_hi[n][k], Wt_lo[n][k] from W[k][n] (k < K = Dout, n < N = Din): the
-// transposed weight split into its TF32 high part and the TF32 part of the rest.
-__global__ void k_split_wt(const float *__restrict__ W, float *__restrict__ hi, float *__restrict__ lo, int K, int N)
+// transposed weight split into its TF32 high part and the TF32 part of the rest,
+// rows of Kp >= K (zeros past K, so a last K chunk that reaches past Dout adds
+// nothing).
+__global__ void k_split_wt(const float *__restrict__ W, float *__restrict__ hi, float *__restrict__ lo, int K, int Kp,
+                           int N)
 {
     __shared__ float t[32][33];
     const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
@@ -116,17 +119,18 @@ __global__ void k_split_wt(const float *__restrict__ W, float *__restrict__ hi, 
     __syncthreads();
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         const int n = n0 + r, k = k0 + threadIdx.x;
-        if (n < N && k < K) {
-            const float a = t[threadIdx.x][r];
+        if (n < N && k < Kp) {
+            const float a = t[threadIdx.x][r];  // 0 past K
             const float h = tf32_hi(a);
-            hi[(int64_t)n * K + k] = h;
-            lo[(int64_t)n * K + k] = tf32_hi(a - h);
+            hi[(int64_t)n * Kp + k] = h;
+            lo[(int64_t)n * Kp + k] = tf32_hi(a - h);
         }
     }
 }
 
-// dX = dY . W for one 128-row tile per CTA; N = Din (a multiple of 16, <= 256),
-// K = Dout (a multiple of 16); tmem_cols: N rounded up to a power of two >= 32.
+// dX = dY . W for one 128-row tile per CTA; N = Din (64, 128 or 256), K = Dout
+// rounded up to a multiple of 16 (the dY columns past Dout load as zeros);
+// tmem_cols: N rounded up to a power of two >= 32.
 template <int N>
 __global__ void __launch_bounds__(kDgThreads + 32, 2)
     k_dgrad_3xtf32(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tBh,
@@ -277,21 +281,23 @@ __global__ void __launch_bounds__(kDgThreads + 32, 2)
     }
 }
 
-size_t dgrad_tc_workspace_bytes(int64_t Din, int64_t Dout) { return (size_t)2 * Din * Dout * 4; }
+static int64_t padded_k(int64_t Dout) { return (Dout + kDgK - 1) / kDgK * kDgK; }
+
+size_t dgrad_tc_workspace_bytes(int64_t Din, int64_t Dout) { return (size_t)2 * Din * padded_k(Dout) * 4; }
 
 bool dgrad_tc_applies(int64_t R, int64_t Din, int64_t Dout)
 {
-    return R > 0 && Dout > 0 && Dout % kDgK == 0 && (Din == 64 || Din == 128 || Din == 256) &&
+    return R > 0 && Dout > 0 && Dout % 4 == 0 && (Din == 64 || Din == 128 || Din == 256) &&
            R < (int64_t(1) << 31);
 }
 
 template <int N>
 static bool launch_dgrad(const float *dY, const float *Wt_hi, const float *Wt_lo, float *dX, int64_t R, int64_t K,
-                         cudaStream_t s)
+                         int64_t Kp, cudaStream_t s)
 {
     CUtensorMap mA, mBh, mBl, mC;
-    if (!make_tmap_2d_swz(&mA, dY, K, R, kDgM, kDgK * 4) || !make_tmap_2d_swz(&mBh, Wt_hi, K, N, N, kDgK * 4) ||
-        !make_tmap_2d_swz(&mBl, Wt_lo, K, N, N, kDgK * 4) || !make_tmap_2d_swz(&mC, dX, N, R, kDgM, kDgOutCols * 4))
+    if (!make_tmap_2d_swz(&mA, dY, K, R, kDgM, kDgK * 4) || !make_tmap_2d_swz(&mBh, Wt_hi, Kp, N, N, kDgK * 4) ||
+        !make_tmap_2d_swz(&mBl, Wt_lo, Kp, N, N, kDgK * 4) || !make_tmap_2d_swz(&mC, dX, N, R, kDgM, kDgOutCols * 4))
         return false;
     constexpr size_t stage = (size_t)2 * kDgM * kDgK * 4 + (size_t)2 * N * kDgK * 4;
     constexpr int rounds_tiles = N / kDgOutCols < kDgOutRound ? N / kDgOutCols : kDgOutRound;
@@ -301,7 +307,7 @@ static bool launch_dgrad(const float *dY, const float *Wt_hi, const float *Wt_lo
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return false;
     count_launches(1);
-    kern<<<(unsigned)((R + kDgM - 1) / kDgM), kDgThreads + 32, smem, s>>>(mA, mBh, mBl, mC, (int)K,
+    kern<<<(unsigned)((R + kDgM - 1) / kDgM), kDgThreads + 32, smem, s>>>(mA, mBh, mBl, mC, (int)Kp,
                                                                         device_status_ptr());
     return true;
 }
@@ -313,13 +319,14 @@ bool dgrad_tc(const float *dY, const float *W, float *dX, int64_t R, int64_t Din
     const void *p[] = {dY, W, dX, ws};
     for (const void *q : p)
         if (((uintptr_t)q & 15)) return false;
-    float *hi = (float *)ws, *lo = hi + Din * Dout;
+    const int64_t Kp = padded_k(Dout);
+    float *hi = (float *)ws, *lo = hi + Din * Kp;
     count_launches(1);
-    k_split_wt<<<dim3((unsigned)((Din + 31) / 32), (unsigned)((Dout + 31) / 32)), dim3(32, 8), 0, s>>>(
-        W, hi, lo, (int)Dout, (int)Din);
-    if (Din == 256) return launch_dgrad<256>(dY, hi, lo, dX, R, Dout, s);
-    if (Din == 128) return launch_dgrad<128>(dY, hi, lo, dX, R, Dout, s);
-    return launch_dgrad<64>(dY, hi, lo, dX, R, Dout, s);
+    k_split_wt<<<dim3((unsigned)((Din + 31) / 32), (unsigned)((Kp + 31) / 32)), dim3(32, 8), 0, s>>>(
+        W, hi, lo, (int)Dout, (int)Kp, (int)Din);
+    if (Din == 256) return launch_dgrad<256>(dY, hi, lo, dX, R, Dout, Kp, s);
+    if (Din == 128) return launch_dgrad<128>(dY, hi, lo, dX, R, Dout, Kp, s);
+    return launch_dgrad<64>(dY, hi, lo, dX, R, Dout, Kp, s);
 }
 
 }  // namespace lifb
@@ -347,7 +354,7 @@ extern "C" int lifb_dense_dgrad(const float *dY, const float *W, float *dX, int6
         return LIFB_ERR_INVALID_ARGUMENT;
     }
     if (!lifb::dgrad_tc_applies(R, Din, Dout)) {
-        lifb::set_last_error("lifb_dense_dgrad: needs Dout % 16 == 0 and Din in {64, 128, 256}");
+        lifb::set_last_error("lifb_dense_dgrad: needs Dout % 4 == 0 and Din in {64, 128, 256}");
         return LIFB_ERR_UNSUPPORTED;
     }
     if (!lifb::dgrad_tc(dY, W, dX, R, Din, Dout, workspace, (cudaStream_t)stream)) {

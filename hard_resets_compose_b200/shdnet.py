@@ -110,7 +110,7 @@ class SpikeLinearLIF(torch.autograd.Function):
 
 def dense_dgrad_applies(din, dout):
     """Whether lifb_dense_dgrad takes a layer of this shape."""
-    return dout % 16 == 0 and din in (64, 128, 256)
+    return dout % 4 == 0 and din in (64, 128, 256)
 
 
 def dense_dgrad(dY, weight):
@@ -170,7 +170,7 @@ class SpikeInputLinear(torch.autograd.Function):
     def backward(ctx, gy):
         x, xmask, weight = ctx.saved_tensors
         g2 = gy.reshape(-1, weight.shape[0]).contiguous()
-        gx = g2.mm(weight).reshape(x.shape) if ctx.needs_input_grad[0] else None
+        gx = dense_dgrad(g2, weight).reshape(x.shape) if ctx.needs_input_grad[0] else None
         gw, gb = _spike_wgrad(g2, x, xmask, ctx.needs_input_grad[2], ctx.has_bias and ctx.needs_input_grad[3])
         _lib.poll_device("spike_input_linear")
         return gx, None, gw, gb

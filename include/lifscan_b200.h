@@ -202,7 +202,7 @@ int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float
  * product of the low parts dropped) accumulated in fp32: within about 1e-6
  * relative of an fp32 GEMM, not bit-equal to one.  This is the backward of
  * the Linear feeding a LIF layer in the consumer network (lifscan/shdnet.py:
- * 30-50, where torch computes it as an fp32 GEMM).  Needs Dout % 16 == 0 and
+ * 30-50, where torch computes it as an fp32 GEMM).  Needs Dout % 4 == 0 and
  * Din in {64, 128, 256} (LIFB_ERR_UNSUPPORTED otherwise) and 16-byte aligned
  * pointers; the workspace (lifb_dense_dgrad_workspace_bytes) holds W's
  * transposed high and low parts. */

@@ -35,7 +35,8 @@ def rel(a, b):
 
 
 @pytest.mark.parametrize("R,Din,Dout", ((65536, 256, 256), (1000, 128, 64), (37, 64, 32), (384, 256, 512),
-                                        (129, 256, 32), (4096, 64, 256), (300, 128, 48)))
+                                        (129, 256, 32), (4096, 64, 256), (300, 128, 48),
+                                        (65536, 256, 20), (1000, 256, 4), (513, 64, 36)))
 def test_dense_dgrad_matches_fp64(cuda, R, Din, Dout):
     g = torch.Generator(device="cuda").manual_seed(R + Din + Dout)
     dY = torch.randn(R, Dout, device="cuda", generator=g) * 1e-3
@@ -65,10 +66,10 @@ def test_dense_dgrad_spike_gradient_shape(cuda):
 
 def test_dense_dgrad_refusals(cuda):
     L = _lib()
-    dY = torch.zeros(8, 20, device="cuda")
-    W = torch.zeros(20, 256, device="cuda")
+    dY = torch.zeros(8, 18, device="cuda")
+    W = torch.zeros(18, 256, device="cuda")
     rc, _ = dgrad(dY, W)
-    assert rc == 4  # LIFB_ERR_UNSUPPORTED: Dout % 16 != 0
+    assert rc == 4  # LIFB_ERR_UNSUPPORTED: Dout % 4 != 0
     dY = torch.zeros(8, 32, device="cuda")
     W = torch.zeros(32, 96, device="cuda")
     rc, _ = dgrad(dY, W)
