@@ -205,7 +205,8 @@ int lifb_lif_fwd_bwd_host(const float *I_host, const float *GS_host, const float
  * 30-50, where torch computes it as an fp32 GEMM).  Needs Dout % 4 == 0 and
  * Din in {64, 128, 256} (LIFB_ERR_UNSUPPORTED otherwise) and 16-byte aligned
  * pointers; the workspace (lifb_dense_dgrad_workspace_bytes) holds W's
- * transposed high and low parts. */
+ * transposed high and low parts.  A non-finite element of dY or W makes the
+ * outputs it reaches non-finite (NaN where an fp32 GEMM may give +-inf). */
 size_t lifb_dense_dgrad_workspace_bytes(int64_t Din, int64_t Dout);
 int lifb_dense_dgrad(const float *dY, const float *W, float *dX, int64_t R, int64_t Din, int64_t Dout,
                      void *workspace, size_t workspace_bytes, void *stream);

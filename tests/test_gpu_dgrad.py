@@ -64,6 +64,24 @@ def test_dense_dgrad_spike_gradient_shape(cuda):
     assert rel(dX, dY.double() @ W.double()) < TOL
 
 
+def test_dense_dgrad_non_finite_stays_in_its_rows(cuda):
+    """An inf or NaN in dY makes its own output row non-finite and leaves the
+    other rows exact to the bound; nothing non-finite turns finite."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    dY = torch.randn(300, 64, device="cuda", generator=g)
+    W = (torch.rand(64, 128, device="cuda", generator=g) * 2 - 1) / 8
+    dY[5, 3] = float("inf")
+    dY[200, 0] = float("nan")
+    rc, dX = dgrad(dY, W)
+    torch.cuda.synchronize()
+    assert rc == 0
+    bad = torch.zeros(300, dtype=torch.bool, device="cuda")
+    bad[5] = bad[200] = True
+    assert not torch.isfinite(dX[bad]).any()
+    assert torch.isfinite(dX[~bad]).all()
+    assert rel(dX[~bad], dY[~bad].double() @ W.double()) < TOL
+
+
 def test_dense_dgrad_refusals(cuda):
     L = _lib()
     dY = torch.zeros(8, 18, device="cuda")
