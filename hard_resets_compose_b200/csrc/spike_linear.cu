@@ -42,7 +42,8 @@
 // bits into per-column row sets with ballots (only for columns active in the
 // block) and adds the listed dI rows in row order.  Each CTA covers a chunk of
 // rows whose size follows from the shape alone; a second pass adds the
-// chunks in order, so the result is deterministic and the same on every GPU.
+// chunks in a fixed order (eight contiguous groups in chunk order, then the
+// groups in order), so the result is deterministic and the same on every GPU.
 #include "lifb_common.cuh"
 #include "lifb_internal.h"
 #include "tma.cuh"
@@ -653,33 +654,69 @@ __global__ void __launch_bounds__(32 * (kWgWarps + 1), 1) k_spike_wgrad(const __
     }
 }
 
-// The chunks' partial sums, added in chunk order.
-__global__ void k_spike_wgrad_reduce(const float *__restrict__ Pw, const float *__restrict__ Pb,
-                                     float *__restrict__ gW, float *__restrict__ gb, int64_t nck, int Din, int Dout,
-                                     int Dp)
+// The chunks' partial sums.  A block takes 32 outputs (one per lane) and G
+// warps (G = blockDim.x / 32, at most kWgRedGroups): warp g adds the chunks of
+// its contiguous range [g*nck/G, (g+1)*nck/G) in chunk order (the 32 lanes
+// read 32 consecutive floats), then lane l of warp 0 adds the G group sums in
+// group order.  G follows from the shape alone (wg_red_groups), and so does
+// the order: the result is deterministic and the same on every GPU.  Blocks
+// past the weight's go to the bias.
+constexpr int kWgRedGroups = 8;
+
+// The fewest groups that leave at most 16 chunks to each thread.
+static int wg_red_groups(int64_t nck)
 {
-    // a sum over chunks in chunk order, eight loads in flight
-    auto chunk_sum = [&](const float *p, int64_t stride) {
-        float acc = 0.0f;
-        int64_t k = 0;
-        for (; k + 8 <= nck; k += 8) {
+    int G = 1;
+    while (G < kWgRedGroups && (nck + G - 1) / G > 16) G *= 2;
+    return G;
+}
+
+__global__ void __launch_bounds__(32 * kWgRedGroups) k_spike_wgrad_reduce(const float *__restrict__ Pw,
+                                                                          const float *__restrict__ Pb,
+                                                                          float *__restrict__ gW,
+                                                                          float *__restrict__ gb, int64_t nck, int Din,
+                                                                          int Dout, int Dp)
+{
+    __shared__ float part[kWgRedGroups][32];
+    const int lane = threadIdx.x & 31, g = threadIdx.x >> 5, G = blockDim.x >> 5;
+    const int64_t nW = (int64_t)Dout * Din, nWb = (nW + 31) / 32;
+    const int64_t k0 = nck * g / G, k1 = nck * (g + 1) / G;
+    const float *p = nullptr;
+    float *out = nullptr;
+    int64_t stride = 0;
+    if ((int64_t)blockIdx.x < nWb) {
+        const int64_t i = (int64_t)blockIdx.x * 32 + lane;
+        if (i < nW) {
+            p = Pw + (i / Din) * Dp + i % Din;
+            stride = (int64_t)Dout * Dp;
+            out = gW + i;
+        }
+    } else {
+        const int64_t j = ((int64_t)blockIdx.x - nWb) * 32 + lane;
+        if (gb && j < Dout) {
+            p = Pb + j;
+            stride = Dout;
+            out = gb + j;
+        }
+    }
+    float acc = 0.0f;
+    if (p) {
+        int64_t k = k0;
+        for (; k + 8 <= k1; k += 8) {  // eight loads in flight
             float v[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) v[u] = p[(k + u) * stride];
 #pragma unroll
             for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
         }
-        for (; k < nck; k++) acc = __fadd_rn(acc, p[k * stride]);
-        return acc;
-    };
-    const int64_t n = (int64_t)Dout * Din;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t j = i / Din, c = i % Din;
-        gW[i] = chunk_sum(Pw + j * Dp + c, (int64_t)Dout * Dp);
+        for (; k < k1; k++) acc = __fadd_rn(acc, p[k * stride]);
     }
-    if (gb) {
-        for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < Dout; j += (int64_t)gridDim.x * blockDim.x)
-            gb[j] = chunk_sum(Pb + j, Dout);
+    part[g][lane] = acc;
+    __syncthreads();
+    if (g == 0 && out) {
+        float t = part[0][lane];
+        for (int q = 1; q < G; q++) t = __fadd_rn(t, part[q][lane]);
+        *out = t;
     }
 }
 
@@ -717,11 +754,9 @@ bool spike_wgrad(const float *dI, const float *X, const uint32_t *Xm, float *gW,
     else if (p.JJ == 4) go(k_spike_wgrad<4>);
     else if (p.JJ == 2) go(k_spike_wgrad<2>);
     else go(k_spike_wgrad<1>);
-    int dev = 0, nsm = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t n = Dout * Din;
-    const unsigned rgrid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)nsm * 8));
-    k_spike_wgrad_reduce<<<rgrid, 256, 0, s>>>(Pw, pb, gW, gb, p.nck, (int)Din, (int)Dout, (int)p.Dp);
+    const int64_t nWb = (Dout * Din + 31) / 32, nbb = gb ? (Dout + 31) / 32 : 0;
+    k_spike_wgrad_reduce<<<(unsigned)(nWb + nbb), 32 * wg_red_groups(p.nck), 0, s>>>(Pw, pb, gW, gb, p.nck,
+                                                                                    (int)Din, (int)Dout, (int)p.Dp);
     return true;
 }
 

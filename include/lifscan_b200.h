@@ -458,7 +458,8 @@ int lifb_spike_linear_lif_fwd(const float *X, const uint32_t *Xmask, const float
  * = dI^T X and gb [Dout] = sum over rows of dI (gb NULL: skipped), from dI
  * [R, Dout] (Dout % 4 == 0) and the input X [R, Din] with its spike mask; only the active
  * (row, input) pairs are visited.  The sums run over rows in a fixed order
- * (2048-row chunks, then the chunks in order), so the result is deterministic;
+ * that follows from the shape alone (row chunks sized for about one CTA per
+ * SM, then the chunks' sums in a fixed grouping), so the result is deterministic;
  * it differs from a GEMM's by rounding only.  Workspace:
  * lifb_spike_linear_wgrad_workspace_bytes(R, Din, Dout).  Replaces the weight
  * and bias gradients torch's Linear backward computes for shdnet.LIFLayer
