@@ -16,8 +16,8 @@
 namespace lifb {
 
 namespace {
-constexpr int kLkChunk = 64;   // rows per warp
-constexpr int kLkMaxWarps = 16;  // T <= 1024 in one launch (the chunk lives in registers)
+constexpr int kLkChunk = 32;   // rows per warp
+constexpr int kLkMaxWarps = 32;  // T <= 1024 in one launch (the chunk lives in registers)
 }  // namespace
 
 // REV = false: the forward (chunks in time order, carry from the chunks before);
@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(32 * kLkMaxWarps) k_leaky(const float *__restr
     }
 }
 
-// False when T is past the one-launch form (16 chunks of 64 rows).
+// False when T is past the one-launch form (32 chunks of 32 rows).
 bool leaky(const float *in, float *out, int64_t T, int64_t M, float beta, bool rev, cudaStream_t s)
 {
     if (T <= 0 || M <= 0) return true;
